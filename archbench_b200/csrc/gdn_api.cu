@@ -1,0 +1,147 @@
+// C-ABI entry points (include/gdn_b200.h): argument validation and kernel selection.
+// Nothing here allocates device memory or synchronises the stream.
+#include <string.h>
+
+#include "gdn_common.cuh"
+
+namespace {
+
+int dtype_size(int dt) {
+  switch (dt) {
+    case GDN_DTYPE_F32: return 4;
+    case GDN_DTYPE_BF16: return 2;
+    default: return 0;
+  }
+}
+
+// The current device must be an sm_100 part: the library carries sm_100a code only.
+int check_device() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return GDN_ERR_DEVICE;
+  static int cached[64] = {0};  // 0 unknown, 1 ok, -1 bad
+  if (dev >= 0 && dev < 64 && cached[dev] != 0) return cached[dev] > 0 ? GDN_OK : GDN_ERR_DEVICE;
+  int major = 0, minor = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess)
+    return GDN_ERR_DEVICE;
+  const bool ok = (major == 10 && minor == 0);
+  if (dev >= 0 && dev < 64) cached[dev] = ok ? 1 : -1;
+  return ok ? GDN_OK : GDN_ERR_DEVICE;
+}
+
+bool aligned(const void* p, int bytes) { return ((uintptr_t)p % (uintptr_t)bytes) == 0; }
+
+bool strides_ok(const gdn_strides& s, int64_t elem, int vec_bytes) {
+  auto ok = [&](int64_t x) { return x >= 0 && (x * elem) % vec_bytes == 0; };
+  return ok(s.b) && ok(s.t) && ok(s.h);
+}
+
+// Validation shared by prefill and decode.  `T` may be 0.
+int validate(const gdn_prefill_args* a) {
+  if (!a) return GDN_ERR_NULL;
+  if (!a->q || !a->k || !a->v || !a->la || !a->y) return GDN_ERR_NULL;
+  if (!a->u && !a->beta) return GDN_ERR_NULL;
+  if (a->B <= 0 || a->H <= 0 || a->T < 0) return GDN_ERR_SHAPE;
+  if (!(a->DK == 32 || a->DK == 64 || a->DK == 128 || a->DK == 256)) return GDN_ERR_UNSUPPORTED;
+  if (a->DV < 1 || a->DV > 1024) return GDN_ERR_UNSUPPORTED;
+  if (a->B > (1 << 20) || a->H > (1 << 16) || a->T > (1LL << 31) - 1) return GDN_ERR_SHAPE;
+  if (a->B * a->H * a->DV > (1LL << 31)) return GDN_ERR_SHAPE;
+  const int es = dtype_size(a->in_dtype);
+  if (!es || !dtype_size(a->out_dtype)) return GDN_ERR_DTYPE;
+  if (a->impl < GDN_IMPL_AUTO || a->impl > GDN_IMPL_RECURRENT) return GDN_ERR_UNSUPPORTED;
+  // The recurrent kernel reads DK/32 consecutive elements per lane as one vector.
+  const int vec = (int)(a->DK / 32) * es;
+  const int vb = vec >= 16 ? 16 : vec;
+  if (!aligned(a->q, vb) || !aligned(a->k, vb) || (a->u && !aligned(a->u, vb))) return GDN_ERR_ALIGN;
+  if (!strides_ok(a->sq, es, vb) || !strides_ok(a->sk, es, vb) || (a->u && !strides_ok(a->su, es, vb)))
+    return GDN_ERR_ALIGN;
+  if (!aligned(a->v, es) || !aligned(a->y, dtype_size(a->out_dtype))) return GDN_ERR_ALIGN;
+  if (!strides_ok(a->sv, es, es) || !strides_ok(a->sy, dtype_size(a->out_dtype), dtype_size(a->out_dtype)))
+    return GDN_ERR_ALIGN;
+  const int svec = (int)(a->DK / 32) * 4 >= 16 ? 16 : (int)(a->DK / 32) * 4;
+  if ((a->s0 && !aligned(a->s0, svec)) || (a->s_out && !aligned(a->s_out, svec))) return GDN_ERR_ALIGN;
+  return GDN_OK;
+}
+
+int select_impl(const gdn_prefill_args* a) {
+  const bool chunk_ok = gdn_chunk_supported(a);
+  if (a->impl == GDN_IMPL_CHUNK) return chunk_ok ? (int)GDN_IMPL_CHUNK : (int)GDN_ERR_UNSUPPORTED;
+  if (a->impl == GDN_IMPL_RECURRENT) return (int)GDN_IMPL_RECURRENT;
+  return chunk_ok ? (int)GDN_IMPL_CHUNK : (int)GDN_IMPL_RECURRENT;
+}
+
+}  // namespace
+
+extern "C" {
+
+int gdn_abi_version(void) { return GDN_B200_ABI_VERSION; }
+
+const char* gdn_status_string(int s) {
+  switch (s) {
+    case GDN_OK: return "ok";
+    case GDN_ERR_NULL: return "a required pointer is NULL";
+    case GDN_ERR_SHAPE: return "a size is out of range or inconsistent";
+    case GDN_ERR_DTYPE: return "unsupported dtype";
+    case GDN_ERR_ALIGN: return "pointer or stride misaligned for the kernel's vector accesses";
+    case GDN_ERR_UNSUPPORTED: return "no kernel of this build implements this request";
+    case GDN_ERR_DEVICE: return "the current device is not an sm_100 (B200) GPU";
+    case GDN_ERR_LAUNCH: return "CUDA kernel launch failed";
+    case GDN_ERR_TIMEOUT: return "a bounded device-side wait gave up";
+    default: return "unknown gdn_status";
+  }
+}
+
+int gdn_prefill_workspace_bytes(const gdn_prefill_args* a, size_t* bytes) {
+  if (!bytes) return GDN_ERR_NULL;
+  int st = validate(a);
+  if (st != GDN_OK) return st;
+  *bytes = 0;
+  return GDN_OK;
+}
+
+int gdn_prefill_select_impl(const gdn_prefill_args* a) {
+  int st = validate(a);
+  if (st != GDN_OK) return st;
+  return select_impl(a);
+}
+
+int gdn_prefill_fwd(const gdn_prefill_args* a, void* stream) {
+  int st = validate(a);
+  if (st != GDN_OK) return st;
+  st = check_device();
+  if (st != GDN_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (a->T == 0) {  // nothing to scan: S_T = S_0
+    if (a->s_out && a->s_out != a->s0) {
+      const size_t n = (size_t)(a->B * a->H * a->DV * a->DK) * sizeof(float);
+      cudaError_t e = a->s0 ? cudaMemcpyAsync(a->s_out, a->s0, n, cudaMemcpyDeviceToDevice, s)
+                            : cudaMemsetAsync(a->s_out, 0, n, s);
+      if (e != cudaSuccess) return GDN_ERR_LAUNCH;
+    }
+    return GDN_OK;
+  }
+  const int impl = select_impl(a);
+  if (impl < 0) return impl;
+  if (impl == GDN_IMPL_CHUNK) return gdn_launch_chunk_sm100(a, s);
+  return gdn_launch_recurrent(a, a->s0, a->s_out, s);
+}
+
+int gdn_decode_step(const gdn_decode_args* d, void* stream) {
+  if (!d) return GDN_ERR_NULL;
+  if (!d->state) return GDN_ERR_NULL;
+  gdn_prefill_args a;
+  memset(&a, 0, sizeof(a));
+  a.q = d->q; a.k = d->k; a.u = d->u; a.v = d->v;
+  a.beta = d->beta; a.la = d->la; a.s0 = d->state; a.s_out = d->state; a.y = d->y;
+  a.sq = d->sq; a.sk = d->sk; a.su = d->su; a.sv = d->sv; a.sy = d->sy;
+  a.sq.t = a.sk.t = a.su.t = a.sv.t = a.sy.t = 0;  // one token: the t stride is never used
+  a.B = d->B; a.T = 1; a.H = d->H; a.DK = d->DK; a.DV = d->DV;
+  a.in_dtype = d->in_dtype; a.out_dtype = d->out_dtype; a.impl = GDN_IMPL_RECURRENT;
+  int st = validate(&a);
+  if (st != GDN_OK) return st;
+  st = check_device();
+  if (st != GDN_OK) return st;
+  return gdn_launch_recurrent(&a, d->state, d->state, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

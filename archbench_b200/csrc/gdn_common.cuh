@@ -1,0 +1,61 @@
+// Shared helpers of the gated-DeltaNet kernels (sm_100a).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "gdn_b200.h"
+
+namespace gdn {
+
+// Element loads/stores for the two I/O dtypes.
+__device__ __forceinline__ float to_f32(float x) { return x; }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 x) { return __bfloat162float(x); }
+__device__ __forceinline__ void store_as(float* p, float x) { *p = x; }
+__device__ __forceinline__ void store_as(__nv_bfloat16* p, float x) { *p = __float2bfloat16_rn(x); }
+
+// Load N consecutive elements (N * sizeof(T) bytes, naturally aligned) as floats.
+template <int N, typename T>
+__device__ __forceinline__ void load_vec(const T* __restrict__ p, float (&out)[N]) {
+  if constexpr (sizeof(T) * N == 16) {
+    uint4 raw = *reinterpret_cast<const uint4*>(p);
+    const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+    for (int i = 0; i < N; ++i) out[i] = to_f32(e[i]);
+  } else if constexpr (sizeof(T) * N == 8) {
+    uint2 raw = *reinterpret_cast<const uint2*>(p);
+    const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+    for (int i = 0; i < N; ++i) out[i] = to_f32(e[i]);
+  } else if constexpr (sizeof(T) * N == 4) {
+    uint32_t raw = *reinterpret_cast<const uint32_t*>(p);
+    const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+    for (int i = 0; i < N; ++i) out[i] = to_f32(e[i]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < N; ++i) out[i] = to_f32(p[i]);
+  }
+}
+
+template <typename T>
+struct DtypeOf;
+template <>
+struct DtypeOf<float> {
+  static constexpr int value = GDN_DTYPE_F32;
+};
+template <>
+struct DtypeOf<__nv_bfloat16> {
+  static constexpr int value = GDN_DTYPE_BF16;
+};
+
+}  // namespace gdn
+
+// Host-side entry points of the individual kernels (defined in their .cu files).  They
+// assume validated arguments and return a gdn_status.
+int gdn_launch_recurrent(const gdn_prefill_args* a, const float* s_in, float* s_out,
+                         cudaStream_t stream);
+int gdn_launch_chunk_sm100(const gdn_prefill_args* a, cudaStream_t stream);
+bool gdn_chunk_supported(const gdn_prefill_args* a);

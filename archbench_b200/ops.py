@@ -1,0 +1,303 @@
+"""Python/PyTorch side of the gated-DeltaNet kernels: a thin ctypes layer over the C ABI of
+``include/gdn_b200.h`` (``libgdn_b200.so``) plus ``torch.library`` custom ops.
+
+There is no CPU path and no other backend: every function here requires CUDA tensors and the
+native library, and raises if either is missing.
+
+Public functions
+  gdn_prefill(q, k, v, la, beta=None, u=None, initial_state=None, output_final_state=False,
+              out_dtype=None, impl="auto") -> (y, S_T | None)
+  gdn_decode_step(q, k, v, la, state, beta=None, u=None, out_dtype=None) -> y   (state in place)
+  nsgdn_scan(q, k, u, v, la) -> y      # same signature and meaning as the scan functions of
+                                       # archbench/layers/nsgdn.py:219,400,408
+Custom ops (for torch.compile, mirroring archbench/layers/nsgdn.py:162-216,352-367)
+  torch.ops.archbench_b200.prefill, torch.ops.archbench_b200.decode_step
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import Optional
+
+import torch
+
+_PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_PKG, "libgdn_b200.so")
+
+GDN_DTYPE_F32, GDN_DTYPE_BF16 = 0, 1
+IMPLS = {"auto": 0, "chunk": 1, "recurrent": 2}
+_DT = {torch.float32: GDN_DTYPE_F32, torch.bfloat16: GDN_DTYPE_BF16}
+
+
+class GdnError(RuntimeError):
+    """A gdn_status error returned by the native library."""
+
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"gdn_b200 error {status}: {msg}")
+        self.status = status
+
+
+class Strides(ctypes.Structure):
+    _fields_ = [("b", ctypes.c_int64), ("t", ctypes.c_int64), ("h", ctypes.c_int64)]
+
+
+class PrefillArgs(ctypes.Structure):
+    """Mirror of gdn_prefill_args (include/gdn_b200.h)."""
+
+    _fields_ = [
+        ("q", ctypes.c_void_p), ("k", ctypes.c_void_p), ("u", ctypes.c_void_p), ("v", ctypes.c_void_p),
+        ("beta", ctypes.c_void_p), ("la", ctypes.c_void_p), ("s0", ctypes.c_void_p), ("y", ctypes.c_void_p),
+        ("s_out", ctypes.c_void_p),
+        ("sq", Strides), ("sk", Strides), ("su", Strides), ("sv", Strides), ("sy", Strides),
+        ("B", ctypes.c_int64), ("T", ctypes.c_int64), ("H", ctypes.c_int64), ("DK", ctypes.c_int64), ("DV", ctypes.c_int64),
+        ("in_dtype", ctypes.c_int32), ("out_dtype", ctypes.c_int32), ("impl", ctypes.c_int32), ("reserved", ctypes.c_int32),
+    ]
+
+
+class DecodeArgs(ctypes.Structure):
+    """Mirror of gdn_decode_args (include/gdn_b200.h)."""
+
+    _fields_ = [
+        ("q", ctypes.c_void_p), ("k", ctypes.c_void_p), ("u", ctypes.c_void_p), ("v", ctypes.c_void_p),
+        ("beta", ctypes.c_void_p), ("la", ctypes.c_void_p), ("state", ctypes.c_void_p), ("y", ctypes.c_void_p),
+        ("sq", Strides), ("sk", Strides), ("su", Strides), ("sv", Strides), ("sy", Strides),
+        ("B", ctypes.c_int64), ("H", ctypes.c_int64), ("DK", ctypes.c_int64), ("DV", ctypes.c_int64),
+        ("in_dtype", ctypes.c_int32), ("out_dtype", ctypes.c_int32),
+    ]
+
+
+# Every symbol include/gdn_b200.h declares, with its ctypes signature.
+SYMBOLS = {
+    "gdn_prefill_fwd": ([ctypes.POINTER(PrefillArgs), ctypes.c_void_p], ctypes.c_int),
+    "gdn_decode_step": ([ctypes.POINTER(DecodeArgs), ctypes.c_void_p], ctypes.c_int),
+    "gdn_prefill_workspace_bytes": ([ctypes.POINTER(PrefillArgs), ctypes.POINTER(ctypes.c_size_t)], ctypes.c_int),
+    "gdn_prefill_select_impl": ([ctypes.POINTER(PrefillArgs)], ctypes.c_int),
+    "gdn_status_string": ([ctypes.c_int], ctypes.c_char_p),
+    "gdn_abi_version": ([], ctypes.c_int),
+}
+
+_LIB = None
+
+
+def load_library(path: str = LIB_PATH):
+    """Load libgdn_b200.so (built by ``python -m archbench_b200.build``); raises if absent."""
+    global _LIB
+    if _LIB is not None and path == LIB_PATH:
+        return _LIB
+    if not os.path.exists(path):
+        raise FileNotFoundError(f"{path} is missing: build it with `python -m archbench_b200.build`")
+    lib = ctypes.CDLL(path)
+    for name, (argtypes, restype) in SYMBOLS.items():
+        fn = getattr(lib, name)
+        fn.argtypes = argtypes
+        fn.restype = restype
+    if path == LIB_PATH:
+        _LIB = lib
+    return lib
+
+
+def _check(status: int):
+    if status != 0:
+        msg = load_library().gdn_status_string(status)
+        raise GdnError(status, msg.decode() if msg else "?")
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return None if t is None else t.data_ptr()
+
+
+def _tok_strides(t: torch.Tensor) -> Strides:
+    """(b, t, h) element strides of a [B][T][H][D] view."""
+    return Strides(t.stride(0), t.stride(1), t.stride(2))
+
+
+def _aligned16(t: torch.Tensor) -> bool:
+    es = t.element_size()
+    return t.data_ptr() % 16 == 0 and all((s * es) % 16 == 0 for s in t.stride()[:-1])
+
+
+def _prep_token(t: torch.Tensor, name: str, dtype: torch.dtype) -> torch.Tensor:
+    """A [B,T,H,D] tensor in ``dtype`` with unit last stride and 16-byte aligned rows."""
+    if t.dim() != 4:
+        raise ValueError(f"{name} must be (B, T, H, D), got {tuple(t.shape)}")
+    if t.dtype != dtype:
+        t = t.to(dtype)
+    if t.stride(-1) != 1 or not _aligned16(t):
+        t = t.contiguous()
+    return t
+
+
+def _check_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("archbench_b200 ops run on CUDA tensors only (no CPU path)")
+
+
+def _prefill_impl(q, k, u, v, la, beta, s0, output_final_state: bool, out_dtype: torch.dtype, impl: str):
+    _check_cuda(q, k, u, v, la, beta, s0)
+    in_dtype = torch.bfloat16 if q.dtype == torch.bfloat16 else torch.float32
+    q, k, v = (_prep_token(t, n, in_dtype) for t, n in ((q, "q"), (k, "k"), (v, "v")))
+    if u is not None:
+        u = _prep_token(u, "u", in_dtype)
+    B, T, H, DK = q.shape
+    DV = v.shape[-1]
+    if k.shape != q.shape or v.shape[:3] != q.shape[:3] or (u is not None and u.shape != q.shape):
+        raise ValueError("q, k, u must be (B, T, H, DK) and v (B, T, H, DV)")
+    la = la.float().contiguous()
+    if la.shape != (B, T, H):
+        raise ValueError(f"la must be (B, T, H) = {(B, T, H)}, got {tuple(la.shape)}")
+    if u is None:
+        if beta is None:
+            raise ValueError("give beta (u = beta * k) or u")
+        beta = beta.float().contiguous()
+        if beta.shape != (B, T, H):
+            raise ValueError("beta must be (B, T, H)")
+    else:
+        beta = None
+    if s0 is not None:
+        s0 = s0.float().contiguous()
+        if s0.shape != (B, H, DV, DK):
+            raise ValueError(f"initial_state must be (B, H, DV, DK) = {(B, H, DV, DK)}")
+    y = torch.empty(B, T, H, DV, device=q.device, dtype=out_dtype)
+    s_out = torch.empty(B, H, DV, DK, device=q.device, dtype=torch.float32) if output_final_state else None
+    a = PrefillArgs(
+        _ptr(q), _ptr(k), _ptr(u), _ptr(v), _ptr(beta), _ptr(la), _ptr(s0), _ptr(y), _ptr(s_out),
+        _tok_strides(q), _tok_strides(k), _tok_strides(u) if u is not None else Strides(0, 0, 0), _tok_strides(v), _tok_strides(y),
+        B, T, H, DK, DV, _DT[in_dtype], _DT[out_dtype], IMPLS[impl], 0,
+    )
+    lib = load_library()
+    with torch.cuda.device(q.device):
+        _check(lib.gdn_prefill_fwd(ctypes.byref(a), ctypes.c_void_p(torch.cuda.current_stream(q.device).cuda_stream)))
+    return y, s_out
+
+
+def _dec_strides(t: torch.Tensor) -> Strides:
+    return Strides(t.stride(0), 0, t.stride(1))
+
+
+def _decode_impl(q, k, u, v, la, beta, state, out_dtype):
+    _check_cuda(q, k, u, v, la, beta, state)
+    if q.dim() == 4:  # (B, 1, H, D) accepted as well as (B, H, D)
+        q, k, v = q[:, 0], k[:, 0], v[:, 0]
+        u = None if u is None else u[:, 0]
+        la = la[:, 0] if la.dim() == 3 else la
+        beta = None if beta is None else (beta[:, 0] if beta.dim() == 3 else beta)
+    in_dtype = torch.bfloat16 if q.dtype == torch.bfloat16 else torch.float32
+    fix = lambda t: None if t is None else (t.to(in_dtype) if t.dtype != in_dtype else t).contiguous()
+    q, k, v, u = fix(q), fix(k), fix(v), fix(u)
+    B, H, DK = q.shape
+    DV = v.shape[-1]
+    if state.dtype != torch.float32 or not state.is_contiguous() or state.shape != (B, H, DV, DK):
+        raise ValueError(f"state must be a contiguous fp32 (B, H, DV, DK) = {(B, H, DV, DK)} tensor")
+    la = la.float().contiguous()
+    beta = None if (u is not None or beta is None) else beta.float().contiguous()
+    if u is None and beta is None:
+        raise ValueError("give beta (u = beta * k) or u")
+    y = torch.empty(B, H, DV, device=q.device, dtype=out_dtype)
+    a = DecodeArgs(
+        _ptr(q), _ptr(k), _ptr(u), _ptr(v), _ptr(beta), _ptr(la), _ptr(state), _ptr(y),
+        _dec_strides(q), _dec_strides(k), _dec_strides(u) if u is not None else Strides(0, 0, 0), _dec_strides(v), _dec_strides(y),
+        B, H, DK, DV, _DT[in_dtype], _DT[out_dtype],
+    )
+    lib = load_library()
+    with torch.cuda.device(q.device):
+        _check(lib.gdn_decode_step(ctypes.byref(a), ctypes.c_void_p(torch.cuda.current_stream(q.device).cuda_stream)))
+    return y
+
+
+# ------------------------------------------------------------------------------------------------
+# torch.library custom ops (opaque to torch.compile; fake impls give output metadata)
+# ------------------------------------------------------------------------------------------------
+
+_DTYPE_CODE = {0: torch.float32, 1: torch.bfloat16}
+
+
+@torch.library.custom_op("archbench_b200::prefill", mutates_args=())
+def _prefill_op(
+    q: torch.Tensor, k: torch.Tensor, u: Optional[torch.Tensor], v: torch.Tensor, la: torch.Tensor,
+    beta: Optional[torch.Tensor], s0: Optional[torch.Tensor], output_final_state: bool, out_dtype_code: int, impl: str,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    y, s = _prefill_impl(q, k, u, v, la, beta, s0, output_final_state, _DTYPE_CODE[out_dtype_code], impl)
+    return y, (s if s is not None else q.new_empty(0, dtype=torch.float32))
+
+
+@_prefill_op.register_fake
+def _(q, k, u, v, la, beta, s0, output_final_state, out_dtype_code, impl):
+    B, T, H, DK = q.shape
+    DV = v.shape[-1]
+    y = q.new_empty(B, T, H, DV, dtype=_DTYPE_CODE[out_dtype_code])
+    s = q.new_empty(B, H, DV, DK, dtype=torch.float32) if output_final_state else q.new_empty(0, dtype=torch.float32)
+    return y, s
+
+
+@torch.library.custom_op("archbench_b200::decode_step", mutates_args=("state",))
+def _decode_op(
+    q: torch.Tensor, k: torch.Tensor, u: Optional[torch.Tensor], v: torch.Tensor, la: torch.Tensor,
+    beta: Optional[torch.Tensor], state: torch.Tensor, out_dtype_code: int,
+) -> torch.Tensor:
+    return _decode_impl(q, k, u, v, la, beta, state, _DTYPE_CODE[out_dtype_code])
+
+
+@_decode_op.register_fake
+def _(q, k, u, v, la, beta, state, out_dtype_code):
+    B, H, DV = state.shape[0], state.shape[1], state.shape[2]
+    return q.new_empty(B, H, DV, dtype=_DTYPE_CODE[out_dtype_code])
+
+
+def _code(dt: Optional[torch.dtype], default: torch.dtype) -> int:
+    dt = default if dt is None else dt
+    if dt not in _DT:
+        raise ValueError(f"out_dtype must be float32 or bfloat16, got {dt}")
+    return _DT[dt]
+
+
+def gdn_prefill(q, k, v, la, beta=None, u=None, initial_state=None, output_final_state=False, out_dtype=None, impl="auto"):
+    """Gated delta rule over a whole sequence block.
+
+    q, k, u: (B, T, H, DK); v: (B, T, H, DV); la, beta: (B, T, H) fp32; initial_state:
+    (B, H, DV, DK) fp32.  q/k/u/v in bf16 run the chunked tcgen05 kernel (DK = DV = 128) or
+    the recurrent kernel; fp32 inputs run the recurrent kernel.  Returns (y, S_T or None);
+    y defaults to the input dtype.
+    """
+    if impl not in IMPLS:
+        raise ValueError(f"impl must be one of {sorted(IMPLS)}")
+    y, s = _prefill_op(q, k, u, v, la, beta, initial_state, bool(output_final_state), _code(out_dtype, q.dtype if q.dtype in _DT else torch.float32), impl)
+    return y, (s if output_final_state else None)
+
+
+def gdn_decode_step(q, k, v, la, state, beta=None, u=None, out_dtype=None):
+    """One token per sequence: q, k, u (B, H, DK), v (B, H, DV), la/beta (B, H); ``state``
+    (B, H, DV, DK) fp32 is updated in place.  Returns y (B, H, DV)."""
+    return _decode_op(q, k, u, v, la, beta, state, _code(out_dtype, q.dtype if q.dtype in _DT else torch.float32))
+
+
+def nsgdn_scan(q, k, u, v, la) -> torch.Tensor:
+    """Drop-in for archbench's scan ops (archbench/layers/nsgdn.py:219 nsgdn_scan, :400
+    nsgdn_scan_chunk, :408 nsgdn_ref): y (B, T, H, DV) for q, k, u (B, T, H, DK), v, la.
+
+    Like nsgdn_scan_chunk, q/k/u/v are cast to bf16 and y is bf16 (fp32 inputs with
+    DK != 128 or DV != 128 keep fp32 and run the recurrent kernel)."""
+    if q.shape[-1] == 128 and v.shape[-1] == 128:
+        dt = torch.bfloat16
+        q, k, u, v = (t.to(dt) for t in (q, k, u, v))
+    return gdn_prefill(q, k, v, la, u=u)[0]
+
+
+def selected_impl(q, k, v, la, beta=None, u=None, impl="auto") -> str:
+    """Name of the kernel ``gdn_prefill`` runs for these arguments ("chunk" or "recurrent")."""
+    _check_cuda(q, k, u, v, la, beta)
+    in_dtype = torch.bfloat16 if q.dtype == torch.bfloat16 else torch.float32
+    q, k, v = (_prep_token(t, n, in_dtype) for t, n in ((q, "q"), (k, "k"), (v, "v")))
+    u = None if u is None else _prep_token(u, "u", in_dtype)
+    B, T, H, DK = q.shape
+    DV = v.shape[-1]
+    a = PrefillArgs(
+        _ptr(q), _ptr(k), _ptr(u), _ptr(v), _ptr(beta), _ptr(la), None, 0x100, None,
+        _tok_strides(q), _tok_strides(k), _tok_strides(u) if u is not None else Strides(0, 0, 0), _tok_strides(v),
+        Strides(T * H * DV, H * DV, DV), B, T, H, DK, DV, _DT[in_dtype], _DT[in_dtype], IMPLS[impl], 0,
+    )
+    r = load_library().gdn_prefill_select_impl(ctypes.byref(a))
+    if r < 0:
+        _check(r)
+    return {1: "chunk", 2: "recurrent"}[r]

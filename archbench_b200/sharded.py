@@ -1,0 +1,55 @@
+"""Head-sharded multi-GPU execution of the gated delta rule.
+
+Every (b, h) recurrence is independent (archbench/layers/nsgdn.py:408-417 never mixes heads),
+so heads are partitioned over ranks and each rank runs the prefill kernel on its own heads
+with no inter-GPU traffic inside the recurrence.  The one collective is an NCCL all-gather of
+the outputs, issued only when a caller needs all heads on every rank.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from . import ops
+
+
+def head_slice(H: int, rank: int, world: int) -> slice:
+    """Heads owned by ``rank``: a contiguous block of H / world heads."""
+    if H % world:
+        raise ValueError(f"H={H} heads do not split over {world} ranks")
+    n = H // world
+    return slice(rank * n, (rank + 1) * n)
+
+
+def gather_heads(y_local: torch.Tensor, world: int, group=None) -> torch.Tensor:
+    """All-gather head shards (B, T, H/world, DV) into a contiguous (B, T, H, DV) tensor.
+
+    NCCL gathers rank-major blocks; one permute-copy then interleaves them into the
+    (B, T, H, DV) layout the caller expects."""
+    if world == 1:
+        return y_local
+    y_local = y_local.contiguous()
+    B, T, hl, DV = y_local.shape
+    buf = torch.empty((world, B, T, hl, DV), dtype=y_local.dtype, device=y_local.device)
+    dist.all_gather_into_tensor(buf, y_local, group=group)
+    return buf.permute(1, 2, 0, 3, 4).reshape(B, T, world * hl, DV)
+
+
+def sharded_prefill(q, k, v, la, beta=None, u=None, initial_state=None, output_final_state=False, gather=True, group=None, impl="auto"):
+    """Run this rank's heads of a full-head problem and optionally all-gather y.
+
+    q, k, v, la, beta, u, initial_state hold ALL heads (every rank passes the same logical
+    tensors, e.g. views of a replicated activation); each rank computes heads
+    ``head_slice(H, rank, world)``.  Returns (y, S_T_local): y is the gathered (B, T, H, DV)
+    when ``gather`` else this rank's (B, T, H/world, DV); S_T_local covers this rank's heads."""
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    rank = dist.get_rank(group) if dist.is_initialized() else 0
+    hs = head_slice(q.shape[2], rank, world)
+    sel = lambda t: None if t is None else t[:, :, hs]
+    s0 = None if initial_state is None else initial_state[:, hs]
+    y, S = ops.gdn_prefill(sel(q), sel(k), sel(v), sel(la), beta=sel(beta), u=sel(u), initial_state=s0,
+                           output_final_state=output_final_state, impl=impl)
+    if gather:
+        y = gather_heads(y, world, group)
+    return y, S

@@ -1,0 +1,398 @@
+"""Benchmark of the gated-DeltaNet hot path on B200 (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--skip-extra]
+    torchrun --nproc-per-node N bench.py --gpus N ...
+
+Headline (``value``): chunkwise prefill of configuration 1 -- B=8, T=4096, H=8, DK=DV=128,
+bf16 q/k/v, fp32 beta/la/state, chunk 64 -- as whole-job tokens/s.  Each rank runs its own
+configuration-1 batch (batch x heads partitioned over ranks, no data-path collective), so
+scaling is weak.  Inputs are 201 MB of q/k/v per rank, larger than the 126 MB L2, so no
+flush is needed between steps.
+
+Extra objects on the same line:
+  decode       configuration 2: B=256, H=16 single-token steps on a state built by a 1024-token
+               prefill; state streamed from HBM once per step (per rank: its own batch).
+  long_context configuration 3: B=1, T=65536, H=32, heads sharded over the N ranks (strong
+               scaling), outputs all-gathered over NCCL into (B, T, H, DV) on every rank.
+  e2e          the headline prefill through the public API with host buffers: pinned-host ->
+               device copies of q/k/v/beta/la and the device -> host copy of y inside the timed
+               region.
+  roofline     the prefill kernel against measured HBM bandwidth (MEASURED_PEAKS.json), with
+               its tensor-pipe FLOP rate beside it.
+  cpu_baseline archbench's recurrence (restated in torch, oracle/cpu_reference.py) on the host
+               cores, on a bounded sample of configuration 1.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from archbench_b200.workloads import (  # noqa: E402
+    CONFIGS,
+    decode_bytes_per_token_head,
+    make_inputs,
+    prefill_bytes_per_token_head,
+    prefill_flops_per_token_head,
+)
+
+METRIC = "GDN prefill tok/s/GPU (T=4096,d=128), decode tok/s; % roofline at 1/2/4/8 GPU"
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+# ------------------------------------------------------------------------------------------
+# distributed plumbing
+# ------------------------------------------------------------------------------------------
+
+
+def dist_init(n_gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms while active."""
+
+    FIELDS = "clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200", "-i", str(self.gpu)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True,
+            )
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        rows = []
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) != 7:
+                continue
+            try:
+                rows.append((float(parts[0]), float(parts[1]), float(parts[2]), parts[3:]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i, v in enumerate(r[3]) if v.lower() == "active"})
+        loaded = [r[0] for r in rows if r[2] > 200.0] or [r[0] for r in rows]
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(r[1] for r in rows), "reasons": reasons,
+                "samples": len(rows), "power_w_max": max(r[2] for r in rows)}
+
+
+def timed(fn, steps, warmup, world, stream=None):
+    """Warm up, then time exactly ``steps`` calls with CUDA events on the launching stream,
+    bracketed by a barrier and a device synchronize; returns max-over-ranks seconds."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    stream = stream or torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    return max_over_ranks(e0.elapsed_time(e1) / 1e3, world)
+
+
+# ------------------------------------------------------------------------------------------
+# our arm
+# ------------------------------------------------------------------------------------------
+
+
+def bench_prefill(args, rank, world):
+    from archbench_b200 import ops
+
+    c = CONFIGS["cfg1"]
+    x = make_inputs(c.B, c.T, c.H, c.DK, c.DV, seed=1000 + rank, dtype=c.dtype, device="cuda")
+    impl = args.prefill_impl
+    out = {}
+
+    def step():
+        out["y"], _ = ops.gdn_prefill(x["q"], x["k"], x["v"], x["la"], beta=x["beta"], impl=impl)
+
+    sel = ops.selected_impl(x["q"], x["k"], x["v"], x["la"], beta=x["beta"], impl=impl)
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        secs = timed(step, args.steps, args.warmup, world)
+    tokens_per_step = c.B * c.T
+    th = c.B * c.T * c.H
+    per_launch = secs / args.steps
+    hbm, tflops, src = peaks()
+    alg_bytes = th * prefill_bytes_per_token_head(c.DK, c.DV)
+    alg_flops = th * prefill_flops_per_token_head(c.DK, c.DV)
+    achieved_gbs = alg_bytes / per_launch / 1e9
+    res = {
+        "value": world * tokens_per_step / secs * args.steps,
+        "ms_per_step": per_launch * 1e3,
+        "kernel": sel,
+        "roofline": {
+            "bound": "hbm", "achieved": achieved_gbs, "peak": hbm, "unit": "GB/s", "frac": achieved_gbs / hbm,
+            "traffic": None, "peak_source": src, "algorithmic_bytes_per_launch": alg_bytes,
+            "tensor": {"achieved_tflops": alg_flops / per_launch / 1e12, "peak_tflops": tflops,
+                       "frac": alg_flops / per_launch / 1e12 / tflops, "algorithmic_flops_per_launch": alg_flops},
+        },
+        "clocks": clk.summary(),
+        "gpu_launches": args.steps,
+    }
+    del x, out
+    return res
+
+
+def bench_prefill_e2e(args, rank, world):
+    """Same workload through the public API from pinned host buffers; copies timed."""
+    from archbench_b200 import ops
+
+    c = CONFIGS["cfg1"]
+    xh = make_inputs(c.B, c.T, c.H, c.DK, c.DV, seed=2000 + rank, dtype=c.dtype, device="cpu")
+    xh = {k: v.pin_memory() for k, v in xh.items()}
+    y_host = torch.empty(c.B, c.T, c.H, c.DV, dtype=torch.bfloat16).pin_memory()
+    h2d = sum(v.numel() * v.element_size() for v in xh.values())
+    d2h = y_host.numel() * y_host.element_size()
+
+    def step():
+        g = {k: v.to("cuda", non_blocking=True) for k, v in xh.items()}
+        y, _ = ops.gdn_prefill(g["q"], g["k"], g["v"], g["la"], beta=g["beta"], impl=args.prefill_impl)
+        y_host.copy_(y, non_blocking=True)
+
+    steps = max(1, min(args.steps, 5))
+    secs = timed(step, steps, min(args.warmup, 2), world)
+    return {"value": world * c.B * c.T * steps / secs, "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "steps": steps, "ms_per_step": secs / steps * 1e3}
+
+
+def bench_decode(args, rank, world):
+    from archbench_b200 import ops
+    from archbench_b200.workloads import DECODE_PREFILL_T
+
+    c = CONFIGS["cfg2"]
+    B, H, D = c.B, c.H, c.DK
+    pre = make_inputs(B, DECODE_PREFILL_T, H, D, D, seed=3000 + rank, dtype=torch.bfloat16, device="cuda")
+    _, state = ops.gdn_prefill(pre["q"], pre["k"], pre["v"], pre["la"], beta=pre["beta"], output_final_state=True)
+    del pre
+    n = args.warmup + args.steps
+    tok = make_inputs(B, n, H, D, D, seed=4000 + rank, dtype=torch.bfloat16, device="cuda")
+    tok = {k: v.transpose(0, 1).contiguous() for k, v in tok.items()}  # (steps, B, H, ...)
+    it = {"i": 0}
+
+    def step():
+        i = it["i"] % n
+        it["i"] += 1
+        ops.gdn_decode_step(tok["q"][i], tok["k"][i], tok["v"][i], tok["la"][i], state, beta=tok["beta"][i])
+
+    secs = timed(step, args.steps, args.warmup, world)
+    per = secs / args.steps
+    hbm, _, src = peaks()
+    alg = B * H * decode_bytes_per_token_head(D, D)
+    return {"value": world * B / per, "unit": "tok/s", "ms_per_step": per * 1e3, "config": "cfg2 B256 H16 d128, state from a 1024-token prefill",
+            "roofline": {"bound": "hbm", "achieved": alg / per / 1e9, "peak": hbm, "unit": "GB/s", "frac": alg / per / 1e9 / hbm,
+                         "peak_source": src, "algorithmic_bytes_per_launch": alg},
+            "gpu_launches": args.steps}
+
+
+def bench_long_context(args, rank, world):
+    """cfg3 heads sharded over ranks; NCCL all-gather of y (strong scaling)."""
+    from archbench_b200 import ops
+    from archbench_b200.sharded import gather_heads
+
+    c = CONFIGS["cfg3"]
+    if c.H % world:
+        return {"skipped": f"H={c.H} not divisible by {world} ranks"}
+    h_loc = c.H // world
+    x = make_inputs(c.B, c.T, h_loc, c.DK, c.DV, seed=5000 + rank, dtype=c.dtype, device="cuda")
+    out = {}
+
+    def step_compute():
+        out["y"], _ = ops.gdn_prefill(x["q"], x["k"], x["v"], x["la"], beta=x["beta"])
+
+    def step_gather():
+        step_compute()
+        out["full"] = gather_heads(out["y"], world)
+
+    steps = max(1, min(args.steps, 10))
+    t_c = timed(step_compute, steps, min(args.warmup, 3), world)
+    t_g = timed(step_gather, steps, min(args.warmup, 3), world)
+    tokens = c.B * c.T
+    return {"value": tokens * steps / t_g, "unit": "tok/s", "value_without_gather": tokens * steps / t_c,
+            "ms_per_step": t_g / steps * 1e3, "ms_compute": t_c / steps * 1e3, "heads_per_rank": h_loc, "scaling": "strong",
+            "gpu_launches": steps}
+
+
+def cpu_baseline(budget_s=12.0):
+    """archbench's recurrence (torch restatement) on the host cores, configuration-1 shapes,
+    run for ~budget_s over growing T-slices; tok/s at B=8, H=8, d=128."""
+    from oracle.cpu_reference import nsgdn_ref_torch
+
+    c = CONFIGS["cfg1"]
+    x = make_inputs(c.B, 64, c.H, c.DK, c.DV, seed=7, dtype=torch.float32, device="cpu")
+    u = x["beta"][..., None] * x["k"]
+    nsgdn_ref_torch(x["q"][:, :4], x["k"][:, :4], u[:, :4], x["v"][:, :4], x["la"][:, :4])  # warm-up
+    tokens, t0, S = 0, time.perf_counter(), None
+    while time.perf_counter() - t0 < budget_s and tokens < c.B * c.T:
+        _, S = nsgdn_ref_torch(x["q"], x["k"], u, x["v"], x["la"], s0=S)
+        tokens += c.B * 64
+    dt = time.perf_counter() - t0
+    return {"value": tokens / dt, "unit": "tok/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"cfg1 shapes B8 H8 d128 fp32, {tokens // c.B} tokens per sequence in 64-token slices ({dt:.1f} s)"}
+
+
+def run_ours(args):
+    rank, world, local = dist_init(args.gpus)
+    res = bench_prefill(args, rank, world)
+    line = {
+        "metric": METRIC, "value": res["value"], "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": res["ms_per_step"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (seeded; BASELINE distributions)",
+        "config": {"workload": "cfg1 chunkwise prefill B=8 T=4096 H=8 DK=DV=128 chunk=64 (per rank)", "global_batch": 8 * world,
+                   "seq_len": 4096, "heads": 8, "head_dim": 128, "parallelism": f"batch-heads sharded x{world}",
+                   "l2": "inputs 201 MB/rank > 126 MB L2 (no flush)", "kernel": res["kernel"]},
+        "roofline": res["roofline"], "clocks": res["clocks"], "gpu_launches": res["gpu_launches"],
+    }
+    if not args.skip_extra:
+        line["e2e"] = bench_prefill_e2e(args, rank, world)
+        torch.cuda.empty_cache()
+        line["decode"] = bench_decode(args, rank, world)
+        torch.cuda.empty_cache()
+        line["long_context"] = bench_long_context(args, rank, world)
+        line["gpu_launches"] += line["decode"]["gpu_launches"] + line["long_context"].get("gpu_launches", 0) * 2
+    if rank == 0 and world == 1 and not args.skip_cpu:
+        line["cpu_baseline"] = cpu_baseline()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    finish(world)
+
+
+def run_reference(args):
+    """The reference's CPU implementation of this path on the host cores (rank 0 only)."""
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    from oracle.cpu_reference import nsgdn_ref_torch
+
+    c = CONFIGS["cfg1"]
+    T_slice = 128
+    x = make_inputs(c.B, T_slice, c.H, c.DK, c.DV, seed=7, dtype=torch.float32, device="cpu")
+    u = x["beta"][..., None] * x["k"]
+    S = None
+    for _ in range(args.warmup):
+        _, S = nsgdn_ref_torch(x["q"], x["k"], u, x["v"], x["la"], s0=S)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        _, S = nsgdn_ref_torch(x["q"], x["k"], u, x["v"], x["la"], s0=S)
+    dt = time.perf_counter() - t0
+    v = c.B * T_slice * args.steps / dt
+    sample = f"cfg1 shapes B8 H8 d128 fp32, {T_slice}-token slice per step (state carried)"
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded; BASELINE distributions)",
+        "config": {"workload": "cfg1 chunkwise prefill B=8 T=4096 H=8 DK=DV=128 chunk=64 (per rank)", "sample": sample},
+        "cpu_baseline": {"value": v, "unit": "tok/s", "cores": torch.get_num_threads(), "kind": "port", "sample": sample},
+        "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def finish(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--prefill-impl", choices=["auto", "chunk", "recurrent"], default="auto")
+    ap.add_argument("--skip-extra", action="store_true", help="headline prefill only")
+    ap.add_argument("--skip-cpu", action="store_true", help="omit the cpu_baseline leg")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,141 @@
+/*
+ * gdn_b200.h -- C ABI of the B200 (sm_100a) gated-DeltaNet token-mixing library.
+ *
+ * The library implements the gated delta rule used by archbench's `gdn` and `nsgdn`
+ * mixers.  Per (batch b, head h), with a DV x DK fp32 state S:
+ *
+ *     S_t = alpha_t * S_{t-1}                       (alpha_t = exp(la_t))
+ *     r_t = v_t - S_t k_t
+ *     S_t = S_t + r_t u_t^T                         (u_t = beta_t k_t unless u is given)
+ *     y_t = S_t q_t
+ *
+ * which is the per-token loop of archbench/layers/nsgdn.py:408-417 (nsgdn_ref) with the
+ * write vector u of nsgdn.py:61-75 (write_direction).  q is used as given: the caller
+ * pre-scales it by DK^-1/2 exactly as archbench/layers/nsgdn.py:527 does.
+ *
+ * Conventions
+ *   - Tensors are dense with a unit-stride last dimension.  Token tensors (q, k, u, v, y)
+ *     are indexed [b][t][h][d] through explicit element strides (stride_b, stride_t,
+ *     stride_h); gate tensors (la, beta) are contiguous (B, T, H) fp32.
+ *   - The state is (B, H, DV, DK) fp32 row-major: row i of S (a DV index) holds DK
+ *     contiguous values, the layout of nsgdn_ref's S (nsgdn.py:410).
+ *   - Every pointer is a device pointer; `stream` is a cudaStream_t (NULL = legacy stream).
+ *   - All calls are asynchronous on `stream`, allocate nothing, keep no state between
+ *     calls and are re-entrant.  Errors are returned as negative gdn_status codes before
+ *     anything is launched; no C++ exception crosses this boundary.
+ */
+#ifndef GDN_B200_H
+#define GDN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GDN_B200_ABI_VERSION 1
+
+typedef enum {
+  GDN_OK = 0,
+  GDN_ERR_NULL = -1,         /* a required pointer is NULL */
+  GDN_ERR_SHAPE = -2,        /* a size is out of range or inconsistent */
+  GDN_ERR_DTYPE = -3,        /* unsupported dtype combination */
+  GDN_ERR_ALIGN = -4,        /* pointer or stride not aligned as the kernel needs */
+  GDN_ERR_UNSUPPORTED = -5,  /* valid request that no kernel of this build implements */
+  GDN_ERR_DEVICE = -6,       /* current device is not an sm_100 GPU */
+  GDN_ERR_LAUNCH = -7,       /* the CUDA launch itself failed */
+  GDN_ERR_TIMEOUT = -8       /* a bounded device-side wait gave up (kernel reported it) */
+} gdn_status;
+
+typedef enum { GDN_DTYPE_F32 = 0, GDN_DTYPE_BF16 = 1 } gdn_dtype;
+
+typedef enum {
+  GDN_IMPL_AUTO = 0,       /* chunked tensor-core kernel where it applies, else recurrent */
+  GDN_IMPL_CHUNK = 1,      /* chunkwise-parallel tcgen05/TMEM kernel (bf16 I/O, DK = DV = 128) */
+  GDN_IMPL_RECURRENT = 2   /* token-serial fp32 kernel (any supported dtype and head size) */
+} gdn_impl;
+
+/* Strides of one token tensor, in elements.  The last (feature) dimension has stride 1. */
+typedef struct {
+  int64_t b, t, h;
+} gdn_strides;
+
+/*
+ * Prefill: the whole (B, T) block in one call.
+ *
+ * Replaces the scan ops archbench dispatches to from NStepGDN.forward
+ * (archbench/layers/nsgdn.py:537-538): nsgdn_scan_chunk (nsgdn.py:400-405, which runs the
+ * custom op archbench::nsgdn_chunk_fwd, nsgdn.py:352-363), nsgdn_scan (nsgdn.py:219-221)
+ * and nsgdn_ref (nsgdn.py:408-417); and fla's chunk_gated_delta_rule as called by the
+ * `gdn` mixer (fla/layers/gated_deltanet.py:266-279, via archbench/layers/fla.py:36-38).
+ * Unlike those it also takes an initial state and returns the final state.
+ */
+typedef struct {
+  const void* q;      /* [B][T][H][DK], dtype `in_dtype` */
+  const void* k;      /* [B][T][H][DK], read vector */
+  const void* u;      /* [B][T][H][DK] write vector, or NULL: u_t = beta_t * k_t */
+  const void* v;      /* [B][T][H][DV] */
+  const float* beta;  /* (B, T, H) fp32; required when u == NULL, ignored otherwise */
+  const float* la;    /* (B, T, H) fp32 natural-log retention, la <= 0 */
+  const float* s0;    /* (B, H, DV, DK) fp32 initial state, or NULL for S_0 = 0 */
+  void* y;            /* [B][T][H][DV], dtype `out_dtype` */
+  float* s_out;       /* (B, H, DV, DK) fp32 final state, or NULL; may equal s0 */
+  gdn_strides sq, sk, su, sv, sy;
+  int64_t B, T, H, DK, DV;
+  int32_t in_dtype;   /* gdn_dtype of q, k, u, v */
+  int32_t out_dtype;  /* gdn_dtype of y */
+  int32_t impl;       /* gdn_impl */
+  int32_t reserved;
+} gdn_prefill_args;
+
+int gdn_prefill_fwd(const gdn_prefill_args* args, void* stream);
+
+/*
+ * Decode: one new token per sequence, state updated in place.
+ *
+ * Replaces fla's fused_recurrent_gated_delta_rule as the `gdn` layer calls it for
+ * q_len <= 64 at inference (fla/layers/gated_deltanet.py:219,281-294), with the state in
+ * the nsgdn (B, H, DV, DK) layout instead of fla's [N, H, K, V].  archbench itself has no
+ * single-step path (archbench/model.py:122, archbench/core_eval.py:136-142 re-run the
+ * prefix); this is the step its recurrence (nsgdn.py:413-416) takes for one token.
+ */
+typedef struct {
+  const void* q;      /* [B][H][DK] (token tensors with T = 1; stride_t unused) */
+  const void* k;      /* [B][H][DK] */
+  const void* u;      /* [B][H][DK] or NULL: u = beta * k */
+  const void* v;      /* [B][H][DV] */
+  const float* beta;  /* (B, H) fp32 when u == NULL */
+  const float* la;    /* (B, H) fp32 */
+  float* state;       /* (B, H, DV, DK) fp32, read and written in place */
+  void* y;            /* [B][H][DV], dtype `out_dtype` */
+  gdn_strides sq, sk, su, sv, sy;
+  int64_t B, H, DK, DV;
+  int32_t in_dtype;
+  int32_t out_dtype;
+} gdn_decode_args;
+
+int gdn_decode_step(const gdn_decode_args* args, void* stream);
+
+/*
+ * Bytes of device workspace a prefill call with these arguments needs.  Every kernel in
+ * this build keeps its working set on chip, so the answer is 0; the query exists so a
+ * caller can size buffers without knowing which kernel runs.
+ */
+int gdn_prefill_workspace_bytes(const gdn_prefill_args* args, size_t* bytes);
+
+/* Which kernel a prefill with these arguments runs (GDN_IMPL_CHUNK or _RECURRENT), or a
+ * negative gdn_status if the arguments are invalid.  Launches nothing. */
+int gdn_prefill_select_impl(const gdn_prefill_args* args);
+
+/* Static description of a status code. */
+const char* gdn_status_string(int status);
+
+/* GDN_B200_ABI_VERSION of the loaded library. */
+int gdn_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GDN_B200_H */

@@ -1,0 +1,99 @@
+"""The C-ABI library: it loads, exports every symbol include/gdn_b200.h declares, and its
+host-side argument checks answer without a GPU (no compute call is made here)."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from archbench_b200 import ops
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "gdn_b200.h")
+
+
+def declared_functions():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\**\s+\**(gdn_\w+)\s*\(", src, flags=re.M)))
+
+
+def test_header_declares_the_expected_api():
+    assert declared_functions() == sorted(ops.SYMBOLS), declared_functions()
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ops.load_library()
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+    assert lib.gdn_abi_version() == 1
+
+
+def test_struct_layout_matches_header():
+    # pointers 9*8, strides 5*24, sizes 5*8, ints 4*4
+    assert ctypes.sizeof(ops.PrefillArgs) == 9 * 8 + 5 * 24 + 5 * 8 + 4 * 4
+    assert ctypes.sizeof(ops.DecodeArgs) == 8 * 8 + 5 * 24 + 4 * 8 + 2 * 4
+
+
+def fake_args(**kw):
+    """Valid-looking prefill args with fake (never dereferenced) 256-aligned pointers."""
+    B, T, H, DK, DV = kw.pop("shape", (2, 128, 4, 128, 128))
+    st = ops.Strides(T * H * DK, H * DK, DK)
+    a = ops.PrefillArgs(
+        0x10000, 0x20000, None, 0x30000, 0x40000, 0x50000, None, 0x60000, None,
+        st, st, ops.Strides(0, 0, 0), ops.Strides(T * H * DV, H * DV, DV), ops.Strides(T * H * DV, H * DV, DV),
+        B, T, H, DK, DV, ops.GDN_DTYPE_BF16, ops.GDN_DTYPE_BF16, 0, 0,
+    )
+    for k, v in kw.items():
+        setattr(a, k, v)
+    return a
+
+
+def status(a):
+    return ops.load_library().gdn_prefill_select_impl(ctypes.byref(a))
+
+
+def test_validation_codes():
+    assert status(fake_args()) in (1, 2)
+    assert status(fake_args(q=None)) == -1
+    assert status(fake_args(beta=None)) == -1  # no u and no beta
+    assert status(fake_args(B=0)) == -2
+    assert status(fake_args(T=-1)) == -2
+    assert status(fake_args(DK=96)) == -5
+    assert status(fake_args(DV=0)) == -5
+    assert status(fake_args(in_dtype=7)) == -3
+    assert status(fake_args(impl=9)) == -5
+    assert status(fake_args(q=0x10002)) == -4  # misaligned vector loads
+
+
+def test_recurrent_selected_for_fp32_and_small_heads():
+    assert status(fake_args(in_dtype=ops.GDN_DTYPE_F32, out_dtype=ops.GDN_DTYPE_F32)) == 2
+    assert status(fake_args(shape=(2, 64, 4, 64, 64))) == 2
+    assert status(fake_args(shape=(2, 64, 4, 64, 64), impl=1)) == -5  # chunk forced, not covered
+
+
+def test_workspace_query_is_zero():
+    n = ctypes.c_size_t(123)
+    assert ops.load_library().gdn_prefill_workspace_bytes(ctypes.byref(fake_args()), ctypes.byref(n)) == 0
+    assert n.value == 0
+
+
+def test_status_strings():
+    lib = ops.load_library()
+    for s in range(-8, 1):
+        assert lib.gdn_status_string(s) and b"unknown" not in lib.gdn_status_string(s)
+
+
+def test_null_args_rejected_before_device_use():
+    lib = ops.load_library()
+    assert lib.gdn_prefill_fwd(None, None) == -1
+    assert lib.gdn_decode_step(None, None) == -1
+
+
+def test_ops_refuse_cpu_tensors():
+    import torch
+
+    x = torch.zeros(1, 4, 1, 32)
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.gdn_prefill(x, x, x, torch.zeros(1, 4, 1), beta=torch.zeros(1, 4, 1))
