@@ -39,9 +39,12 @@ bool strides_ok(const gdn_strides& s, int64_t elem, int vec_bytes) {
 // Validation shared by prefill and decode.  `T` may be 0.
 int validate(const gdn_prefill_args* a) {
   if (!a) return GDN_ERR_NULL;
-  if (!a->q || !a->k || !a->v || !a->la || !a->y) return GDN_ERR_NULL;
-  if (!a->u && !a->beta) return GDN_ERR_NULL;
   if (a->B <= 0 || a->H <= 0 || a->T < 0) return GDN_ERR_SHAPE;
+  // With T == 0 no token tensor is read or written (empty tensors may have NULL data).
+  if (a->T > 0) {
+    if (!a->q || !a->k || !a->v || !a->la || !a->y) return GDN_ERR_NULL;
+    if (!a->u && !a->beta) return GDN_ERR_NULL;
+  }
   if (!(a->DK == 32 || a->DK == 64 || a->DK == 128 || a->DK == 256)) return GDN_ERR_UNSUPPORTED;
   if (a->DV < 1 || a->DV > 1024) return GDN_ERR_UNSUPPORTED;
   if (a->B > (1 << 20) || a->H > (1 << 16) || a->T > (1LL << 31) - 1) return GDN_ERR_SHAPE;
@@ -89,6 +92,13 @@ const char* gdn_status_string(int s) {
     case GDN_ERR_TIMEOUT: return "a bounded device-side wait gave up";
     default: return "unknown gdn_status";
   }
+}
+
+int gdn_device_status(int* status, int reset) {
+  if (!status) return GDN_ERR_NULL;
+  int st = check_device();
+  if (st != GDN_OK) return st;
+  return gdn_chunk_read_status(status, reset);
 }
 
 int gdn_prefill_workspace_bytes(const gdn_prefill_args* a, size_t* bytes) {

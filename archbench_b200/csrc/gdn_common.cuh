@@ -59,3 +59,4 @@ int gdn_launch_recurrent(const gdn_prefill_args* a, const float* s_in, float* s_
                          cudaStream_t stream);
 int gdn_launch_chunk_sm100(const gdn_prefill_args* a, cudaStream_t stream);
 bool gdn_chunk_supported(const gdn_prefill_args* a);
+int gdn_chunk_read_status(int* out, int reset);

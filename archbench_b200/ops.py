@@ -73,6 +73,7 @@ SYMBOLS = {
     "gdn_decode_step": ([ctypes.POINTER(DecodeArgs), ctypes.c_void_p], ctypes.c_int),
     "gdn_prefill_workspace_bytes": ([ctypes.POINTER(PrefillArgs), ctypes.POINTER(ctypes.c_size_t)], ctypes.c_int),
     "gdn_prefill_select_impl": ([ctypes.POINTER(PrefillArgs)], ctypes.c_int),
+    "gdn_device_status": ([ctypes.POINTER(ctypes.c_int), ctypes.c_int], ctypes.c_int),
     "gdn_status_string": ([ctypes.c_int], ctypes.c_char_p),
     "gdn_abi_version": ([], ctypes.c_int),
 }
@@ -301,3 +302,10 @@ def selected_impl(q, k, v, la, beta=None, u=None, impl="auto") -> str:
     if r < 0:
         _check(r)
     return {1: "chunk", 2: "recurrent"}[r]
+
+
+def device_status(reset: bool = False) -> int:
+    """The sticky device-side status word (0 = no kernel reported a bounded-wait timeout)."""
+    out = ctypes.c_int(0)
+    _check(load_library().gdn_device_status(ctypes.byref(out), int(bool(reset))))
+    return out.value

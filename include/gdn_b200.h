@@ -128,6 +128,15 @@ int gdn_prefill_workspace_bytes(const gdn_prefill_args* args, size_t* bytes);
  * negative gdn_status if the arguments are invalid.  Launches nothing. */
 int gdn_prefill_select_impl(const gdn_prefill_args* args);
 
+/*
+ * Read (and, if `reset` is non-zero, clear) the library's sticky device-side status word.
+ * A kernel whose bounded wait on an mbarrier gave up stores GDN_ERR_TIMEOUT there, skips the
+ * rest of its work, releases its tensor memory and returns, so the context stays usable.
+ * Synchronises the current device (cudaMemcpyFromSymbol).  `*status` is GDN_OK when no kernel
+ * reported a problem.
+ */
+int gdn_device_status(int* status, int reset);
+
 /* Static description of a status code. */
 const char* gdn_status_string(int status);
 

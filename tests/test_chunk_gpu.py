@@ -1,0 +1,147 @@
+"""Parity of the chunked tcgen05/TMEM prefill kernel with the CPU oracle.
+
+Tolerance (north-star, bf16 I/O with fp32 state): max-abs <= 2e-3 and rel-L2 <= 1e-3 on y and
+on the final state, measured on fp32 outputs against the float64 oracle run on the same
+bf16-rounded inputs.  A bf16 output adds its own rounding (rel-L2 ~1.7e-3 for a perfect
+result), so bf16 outputs are held to max-abs <= 2e-3 and rel-L2 <= 3e-3."""
+
+import numpy as np
+import pytest
+import torch
+
+from archbench_b200 import ops
+from archbench_b200.workloads import make_inputs
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+TOL_MAX, TOL_REL = 2e-3, 1e-3
+TOL_REL_BF16_OUT = 3e-3
+
+
+def np32(t):
+    return t.detach().float().cpu().numpy()
+
+
+def check(got, want, what, tol_max=TOL_MAX, tol_rel=TOL_REL):
+    mx, rel = O.errors(np32(got), want)
+    assert mx <= tol_max and rel <= tol_rel, f"{what}: max-abs {mx:.3e} rel-L2 {rel:.3e}"
+    return mx, rel
+
+
+def run_case(B, T, H, seed=0, s0=False, with_u=False, out_dtype=torch.float32):
+    x = make_inputs(B, T, H, 128, 128, seed=seed, dtype=torch.bfloat16)
+    S0 = (torch.randn(B, H, 128, 128, generator=torch.Generator().manual_seed(seed + 1)) * 0.3) if s0 else None
+    u = (x["beta"][..., None] * x["k"].float()).to(torch.bfloat16) if with_u else None
+    y_o, S_o = O.recurrence_c(*(np32(x[n]) for n in ("q", "k", "v", "la")),
+                              beta=None if with_u else np32(x["beta"]), u=None if u is None else np32(u),
+                              s0=None if S0 is None else S0.numpy())
+    g = {k: v.cuda() for k, v in x.items()}
+    y, S = ops.gdn_prefill(g["q"], g["k"], g["v"], g["la"], beta=None if with_u else g["beta"],
+                           u=None if u is None else u.cuda(), initial_state=None if S0 is None else S0.cuda(),
+                           output_final_state=True, out_dtype=out_dtype, impl="chunk")
+    torch.cuda.synchronize()
+    return y, S, y_o, S_o
+
+
+def test_chunk_kernel_is_selected():
+    x = make_inputs(1, 64, 1, 128, 128, dtype=torch.bfloat16)
+    g = {k: v.cuda() for k, v in x.items()}
+    assert ops.selected_impl(g["q"], g["k"], g["v"], g["la"], beta=g["beta"]) == "chunk"
+
+
+@pytest.mark.parametrize("T", [64, 192, 1, 63, 65, 100, 130])
+def test_lengths(T):
+    y, S, y_o, S_o = run_case(2, T, 2, seed=T)
+    check(y, y_o, f"y T={T}")
+    check(S, S_o, f"S_T T={T}")
+    assert ops.device_status() == 0
+
+
+def test_initial_state():
+    y, S, y_o, S_o = run_case(1, 256, 3, seed=5, s0=True)
+    check(y, y_o, "y")
+    check(S, S_o, "S_T")
+
+
+def test_write_vector_given():
+    y, S, y_o, S_o = run_case(2, 160, 2, seed=6, with_u=True)
+    check(y, y_o, "y (u given)")
+    check(S, S_o, "S_T (u given)")
+
+
+def test_nstep_write_vectors():
+    """n_steps = 2 write vectors (archbench/layers/nsgdn.py:61-75): u is not parallel to k."""
+    B, T, H = 1, 128, 2
+    x = make_inputs(B, T, H, 128, 128, seed=17, dtype=torch.bfloat16)
+    k = np32(x["k"]).astype(np.float64)
+    p = np.pad(k[:, :-1], ((0, 0), (1, 0), (0, 0), (0, 0)))
+    u = O.write_direction(k, p, np32(x["beta"]).astype(np.float64), np.array([1.0, 0.7]), 2)
+    u_bf = torch.from_numpy(u.astype(np.float32)).to(torch.bfloat16)
+    y_o, S_o = O.recurrence_c(*(np32(x[n]) for n in ("q", "k", "v", "la")), u=np32(u_bf))
+    g = {k_: v.cuda() for k_, v in x.items()}
+    y, S = ops.gdn_prefill(g["q"], g["k"], g["v"], g["la"], u=u_bf.cuda(), output_final_state=True, out_dtype=torch.float32, impl="chunk")
+    check(y, y_o, "y")
+    check(S, S_o, "S_T")
+
+
+def test_bf16_output():
+    y, S, y_o, S_o = run_case(2, 128, 2, seed=7, out_dtype=torch.bfloat16)
+    assert y.dtype == torch.bfloat16
+    check(y, y_o, "y bf16", tol_rel=TOL_REL_BF16_OUT)
+    check(S, S_o, "S_T")
+
+
+def test_strided_views():
+    B, T, H, D = 2, 128, 2, 128
+    x = make_inputs(B, T, H, D, D, seed=9, dtype=torch.bfloat16)
+    fused = torch.cat([x["q"].reshape(B, T, -1), x["k"].reshape(B, T, -1), x["v"].reshape(B, T, -1)], -1).cuda()
+    q, k, v = (fused[..., i * H * D : (i + 1) * H * D].view(B, T, H, D) for i in range(3))
+    assert not q.is_contiguous()
+    assert ops.selected_impl(q, k, v, x["la"].cuda(), beta=x["beta"].cuda()) == "chunk"
+    y, S = ops.gdn_prefill(q, k, v, x["la"].cuda(), beta=x["beta"].cuda(), output_final_state=True, out_dtype=torch.float32)
+    y_o, S_o = O.recurrence_c(*(np32(x[n]) for n in ("q", "k", "v", "la")), beta=np32(x["beta"]))
+    check(y, y_o, "y")
+    check(S, S_o, "S_T")
+
+
+def test_cfg1_heads_against_oracle():
+    """Configuration-1 sequence length and heads (T=4096, H=8) for one batch row."""
+    x = make_inputs(1, 4096, 8, 128, 128, seed=41, dtype=torch.bfloat16)
+    y_o, S_o = O.recurrence_c(*(np32(x[n]) for n in ("q", "k", "v", "la")), beta=np32(x["beta"]))
+    g = {k: v.cuda() for k, v in x.items()}
+    y, S = ops.gdn_prefill(g["q"], g["k"], g["v"], g["la"], beta=g["beta"], output_final_state=True, out_dtype=torch.float32, impl="chunk")
+    check(y, y_o, "y cfg1 row")
+    check(S, S_o, "S_T cfg1 row")
+
+
+def test_cfg1_full_size_against_recurrent_kernel():
+    """Full configuration 1 (B=8, T=4096, H=8): the chunk kernel against the fp32 recurrent
+    kernel (itself pinned to the oracle at 1e-5), same tolerance."""
+    g = make_inputs(8, 4096, 8, 128, 128, seed=1000, dtype=torch.bfloat16, device="cuda")
+    y_c, S_c = ops.gdn_prefill(g["q"], g["k"], g["v"], g["la"], beta=g["beta"], output_final_state=True, out_dtype=torch.float32, impl="chunk")
+    y_r, S_r = ops.gdn_prefill(g["q"], g["k"], g["v"], g["la"], beta=g["beta"], output_final_state=True, out_dtype=torch.float32, impl="recurrent")
+    for a, b_, what in ((y_c, y_r, "y"), (S_c, S_r, "S_T")):
+        d = (a - b_).double()
+        mx = d.abs().max().item()
+        rel = (d.norm() / b_.double().norm()).item()
+        assert mx <= TOL_MAX and rel <= TOL_REL, f"{what}: max-abs {mx:.3e} rel-L2 {rel:.3e}"
+    assert ops.device_status() == 0
+
+
+def test_deterministic():
+    g = make_inputs(2, 256, 4, 128, 128, seed=3, dtype=torch.bfloat16, device="cuda")
+    y1, S1 = ops.gdn_prefill(g["q"], g["k"], g["v"], g["la"], beta=g["beta"], output_final_state=True)
+    y2, S2 = ops.gdn_prefill(g["q"], g["k"], g["v"], g["la"], beta=g["beta"], output_final_state=True)
+    assert torch.equal(y1, y2) and torch.equal(S1, S2)
+
+
+def test_state_in_place_and_chaining():
+    """Two prefill calls chained through the state equal one call over the concatenation."""
+    g = make_inputs(2, 320, 2, 128, 128, seed=12, dtype=torch.bfloat16, device="cuda")
+    cut = 192
+    sl = lambda n, s: g[n][:, s]
+    y_a, S = ops.gdn_prefill(*(sl(n, slice(0, cut)) for n in ("q", "k", "v", "la")), beta=sl("beta", slice(0, cut)), output_final_state=True, out_dtype=torch.float32)
+    y_b, S2 = ops.gdn_prefill(*(sl(n, slice(cut, None)) for n in ("q", "k", "v", "la")), beta=sl("beta", slice(cut, None)), initial_state=S, output_final_state=True, out_dtype=torch.float32)
+    y_f, S_f = ops.gdn_prefill(g["q"], g["k"], g["v"], g["la"], beta=g["beta"], output_final_state=True, out_dtype=torch.float32)
+    torch.testing.assert_close(torch.cat([y_a, y_b], 1), y_f, rtol=0, atol=2e-3)
+    torch.testing.assert_close(S2, S_f, rtol=0, atol=2e-3)
