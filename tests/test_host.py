@@ -1,0 +1,115 @@
+"""Host-side logic that needs no GPU: layer construction and parameter names against the
+reference's layers, the registry boundary, the custom-op fake implementations, sharding maths
+and the bench's roofline arithmetic."""
+
+import os
+import sys
+
+import pytest
+import torch
+
+from archbench_b200 import ops, registry, workloads
+from archbench_b200.layers import GatedDeltaNet, NStepGDN
+from archbench_b200.sharded import head_slice
+
+REF = "/root/reference"
+
+
+def reference_nsgdn():
+    if not os.path.isdir(REF):
+        pytest.skip("reference tree not present on this host")
+    if REF not in sys.path:
+        sys.path.insert(0, REF)
+    from archbench.layers.nsgdn import NStepGDN as RefNStepGDN
+
+    return RefNStepGDN
+
+
+@pytest.mark.parametrize("kw", [dict(), dict(expand_v=1.0, n_steps=1), dict(use_gate=False, conv_size=2), dict(num_heads=4, head_dim=64)])
+def test_nsgdn_parameters_match_reference(kw):
+    Ref = reference_nsgdn()
+    torch.manual_seed(0)
+    ours = NStepGDN(256, **kw)
+    ref = Ref(256, **kw)
+    a = {k: tuple(v.shape) for k, v in ours.state_dict().items()}
+    b = {k: tuple(v.shape) for k, v in ref.state_dict().items()}
+    assert a == b
+    ours.load_state_dict(ref.state_dict())  # interchangeable checkpoints
+
+
+def test_nsgdn_constructor_validation_matches_reference():
+    for bad in (dict(head_dim=96), dict(n_steps=0), dict(lam=0.0), dict(scan_impl="nope")):
+        with pytest.raises(ValueError):
+            NStepGDN(128, **bad)
+
+
+def test_gdn_parameter_names_match_fla():
+    m = GatedDeltaNet(hidden_size=256, expand_v=2, head_dim=128, num_heads=2)
+    names = set(m.state_dict())
+    for n in ("q_proj.weight", "k_proj.weight", "v_proj.weight", "a_proj.weight", "b_proj.weight", "A_log", "dt_bias",
+              "q_conv1d.weight", "k_conv1d.weight", "v_conv1d.weight", "g_proj.weight", "o_norm.weight", "o_proj.weight"):
+        assert n in names, n
+    assert tuple(m.q_conv1d.weight.shape) == (256, 1, 4)
+    assert tuple(m.v_proj.weight.shape) == (512, 256)
+
+
+def test_registry_builders_and_wrapper():
+    m = registry.build_mixer("gdn", d_model=256, layer_idx=0, n_layer=2, head_dim=128, expand_v=1.0, num_heads=2)
+    assert hasattr(m, "layer") and isinstance(m.layer, GatedDeltaNet)
+    n = registry.build_mixer("nsgdn", d_model=256, layer_idx=0, n_layer=2, head_dim=128, expand_v=1.0, num_heads=2, n_steps=1)
+    assert isinstance(n, NStepGDN)
+    with pytest.raises(KeyError):
+        registry.build_mixer("mamba", 256, 0, 1)
+
+
+def test_registry_installs_into_archbench():
+    reference_nsgdn()
+    from archbench import layers as L
+
+    saved = dict(L._REGISTRY)
+    try:
+        registry.install()
+        m = L.build_mixer("nsgdn", 256, 0, 2, head_dim=128, expand_v=1.0, num_heads=2)
+        assert isinstance(m, NStepGDN)
+        g = L.build_mixer("gdn", 256, 0, 2, head_dim=128, expand_v=1.0, num_heads=2)
+        assert isinstance(g.layer, GatedDeltaNet)
+    finally:
+        L._REGISTRY.clear()
+        L._REGISTRY.update(saved)
+
+
+def test_fake_impls_give_output_metadata():
+    from torch._subclasses.fake_tensor import FakeTensorMode
+
+    with FakeTensorMode():
+        q = torch.empty(2, 64, 4, 128, dtype=torch.bfloat16)
+        la = torch.empty(2, 64, 4)
+        y, s = torch.ops.archbench_b200.prefill(q, q, None, q, la, la, None, True, 1, "auto")
+        assert y.shape == (2, 64, 4, 128) and y.dtype == torch.bfloat16 and s.shape == (2, 4, 128, 128)
+        st = torch.empty(2, 4, 128, 128)
+        yd = torch.ops.archbench_b200.decode_step(q[:, 0], q[:, 0], None, q[:, 0], la[:, 0], la[:, 0], st, 0)
+        assert yd.shape == (2, 4, 128) and yd.dtype == torch.float32
+
+
+def test_head_slices_partition_heads():
+    H, world = 32, 8
+    seen = []
+    for r in range(world):
+        s = head_slice(H, r, world)
+        seen += list(range(H))[s]
+    assert seen == list(range(H))
+    with pytest.raises(ValueError):
+        head_slice(30, 0, 8)
+
+
+def test_algorithmic_counts():
+    assert workloads.prefill_flops_per_token_head(128, 128, 64) == 180224
+    assert workloads.prefill_bytes_per_token_head(128, 128) == 1032
+    assert workloads.decode_bytes_per_token_head(128, 128) == 132104
+
+
+def test_config_table_matches_baseline():
+    c = workloads.CONFIGS
+    assert (c["cfg1"].B, c["cfg1"].T, c["cfg1"].H, c["cfg1"].DK) == (8, 4096, 8, 128)
+    assert (c["cfg2"].B, c["cfg2"].H) == (256, 16)
+    assert (c["cfg3"].B, c["cfg3"].T, c["cfg3"].H) == (1, 65536, 32)
