@@ -101,6 +101,12 @@ int gdn_device_status(int* status, int reset) {
   return gdn_chunk_read_status(status, reset);
 }
 
+int gdn_selftest_bounded_wait(long long max_cycles, void* stream) {
+  int st = check_device();
+  if (st != GDN_OK) return st;
+  return gdn_launch_selftest_wait(max_cycles, static_cast<cudaStream_t>(stream));
+}
+
 int gdn_prefill_workspace_bytes(const gdn_prefill_args* a, size_t* bytes) {
   if (!bytes) return GDN_ERR_NULL;
   int st = validate(a);

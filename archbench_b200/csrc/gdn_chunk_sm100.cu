@@ -559,29 +559,35 @@ bool tma_ok(const void* ptr, const gdn_strides& s) {
 }  // namespace chunk
 }  // namespace gdn
 
+// The chunked path: the warp-specialised kernel (gdn_chunk_ws_sm100.cu) for u = beta k with
+// DV any multiple of 128, and this single-warp-group kernel for an explicit write vector u
+// (nsgdn n_steps > 1) with DV = 128.  Both need 16-byte-aligned rows for TMA.
 bool gdn_chunk_supported(const gdn_prefill_args* a) {
   using namespace gdn::chunk;
-  if (a->in_dtype != GDN_DTYPE_BF16 || a->DK != D || a->DV != D || a->T < 1) return false;
+  if (a->in_dtype != GDN_DTYPE_BF16 || a->DK != D || a->T < 1) return false;
   if (!tma_ok(a->q, a->sq) || !tma_ok(a->k, a->sk) || !tma_ok(a->v, a->sv)) return false;
   if (a->u && !tma_ok(a->u, a->su)) return false;
   if ((a->s0 && (uintptr_t)a->s0 % 16) || (a->s_out && (uintptr_t)a->s_out % 16)) return false;
-  return true;
+  if (a->u) return a->DV == D;
+  return gdn_chunk_ws_supported(a);
 }
 
 int gdn_launch_chunk_sm100(const gdn_prefill_args* a, cudaStream_t stream) {
   using namespace gdn::chunk;
-  using bf = __nv_bfloat16;
-  if (a->u) return a->out_dtype == GDN_DTYPE_BF16 ? launch<true, 1, bf>(a, stream) : launch<true, 1, float>(a, stream);
-  return a->out_dtype == GDN_DTYPE_BF16 ? launch<false, 2, bf>(a, stream) : launch<false, 2, float>(a, stream);
+  if (a->u == nullptr) return gdn_launch_chunk_ws(a, stream);
+  return a->out_dtype == GDN_DTYPE_BF16 ? launch<true, 1, __nv_bfloat16>(a, stream) : launch<true, 1, float>(a, stream);
 }
 
 int gdn_chunk_read_status(int* out, int reset) {
+  int ws = 0;
+  int st = gdn_chunk_ws_read_status(&ws, reset);
+  if (st != GDN_OK) return st;
   int v = 0;
   if (cudaMemcpyFromSymbol(&v, gdn::chunk::g_status, sizeof(int)) != cudaSuccess) return GDN_ERR_LAUNCH;
   if (reset) {
     int z = 0;
     if (cudaMemcpyToSymbol(gdn::chunk::g_status, &z, sizeof(int)) != cudaSuccess) return GDN_ERR_LAUNCH;
   }
-  *out = v;
+  *out = v != 0 ? v : ws;
   return GDN_OK;
 }

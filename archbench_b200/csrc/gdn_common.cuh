@@ -60,3 +60,7 @@ int gdn_launch_recurrent(const gdn_prefill_args* a, const float* s_in, float* s_
 int gdn_launch_chunk_sm100(const gdn_prefill_args* a, cudaStream_t stream);
 bool gdn_chunk_supported(const gdn_prefill_args* a);
 int gdn_chunk_read_status(int* out, int reset);
+bool gdn_chunk_ws_supported(const gdn_prefill_args* a);
+int gdn_launch_chunk_ws(const gdn_prefill_args* a, cudaStream_t stream);
+int gdn_chunk_ws_read_status(int* out, int reset);
+int gdn_launch_selftest_wait(long long max_cycles, cudaStream_t stream);

@@ -74,6 +74,7 @@ SYMBOLS = {
     "gdn_prefill_workspace_bytes": ([ctypes.POINTER(PrefillArgs), ctypes.POINTER(ctypes.c_size_t)], ctypes.c_int),
     "gdn_prefill_select_impl": ([ctypes.POINTER(PrefillArgs)], ctypes.c_int),
     "gdn_device_status": ([ctypes.POINTER(ctypes.c_int), ctypes.c_int], ctypes.c_int),
+    "gdn_selftest_bounded_wait": ([ctypes.c_longlong, ctypes.c_void_p], ctypes.c_int),
     "gdn_status_string": ([ctypes.c_int], ctypes.c_char_p),
     "gdn_abi_version": ([], ctypes.c_int),
 }
@@ -309,3 +310,14 @@ def device_status(reset: bool = False) -> int:
     out = ctypes.c_int(0)
     _check(load_library().gdn_device_status(ctypes.byref(out), int(bool(reset))))
     return out.value
+
+
+def selftest_bounded_wait(max_cycles: int = 2_000_000) -> int:
+    """Run the device-side bounded-wait self test and return the status word it leaves
+    (GDN_ERR_TIMEOUT = -8 when the wait gave up as designed).  Clears the word first."""
+    device_status(reset=True)
+    lib = load_library()
+    _check(lib.gdn_selftest_bounded_wait(int(max_cycles), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
+    torch.cuda.synchronize()
+    st = device_status(reset=True)
+    return st

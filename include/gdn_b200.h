@@ -137,6 +137,14 @@ int gdn_prefill_select_impl(const gdn_prefill_args* args);
  */
 int gdn_device_status(int* status, int reset);
 
+/*
+ * Failure-detection self test: launches one CTA that waits on an mbarrier nothing arrives on,
+ * gives up after `max_cycles` SM clocks (0 < max_cycles <= 4e9), stores GDN_ERR_TIMEOUT in the
+ * device status word and exits normally -- the same bounded-wait path every kernel uses.  Read
+ * the outcome with gdn_device_status.  The context stays usable.
+ */
+int gdn_selftest_bounded_wait(long long max_cycles, void* stream);
+
 /* Static description of a status code. */
 const char* gdn_status_string(int status);
 

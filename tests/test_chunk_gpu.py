@@ -145,3 +145,25 @@ def test_state_in_place_and_chaining():
     y_f, S_f = ops.gdn_prefill(g["q"], g["k"], g["v"], g["la"], beta=g["beta"], output_final_state=True, out_dtype=torch.float32)
     torch.testing.assert_close(torch.cat([y_a, y_b], 1), y_f, rtol=0, atol=2e-3)
     torch.testing.assert_close(S2, S_f, rtol=0, atol=2e-3)
+
+
+def test_bounded_wait_times_out_and_context_survives():
+    """Failure detection on the device: a wait on a barrier nothing arrives on gives up after its
+    cycle limit, the status word reports GDN_ERR_TIMEOUT, and the GPU keeps working."""
+    assert ops.selftest_bounded_wait(2_000_000) == ops.GdnError(-8, "").status
+    assert ops.device_status() == 0  # the read above cleared it
+    y, S, y_o, S_o = run_case(1, 64, 1, seed=99)
+    check(y, y_o, "y after timeout self test")
+
+
+@pytest.mark.parametrize("DV", [256, 384])
+def test_value_dim_multiple_of_128(DV):
+    """expand_v > 1 (configs/arch/nsgdn.yaml uses DV = 2 DK): one CTA per 128-row state slice."""
+    x = make_inputs(2, 130, 2, 128, DV, seed=DV, dtype=torch.bfloat16)
+    S0 = torch.randn(2, 2, DV, 128, generator=torch.Generator().manual_seed(3)) * 0.2
+    y_o, S_o = O.recurrence_c(*(np32(x[n]) for n in ("q", "k", "v", "la")), beta=np32(x["beta"]), s0=S0.numpy())
+    g = {k: v.cuda() for k, v in x.items()}
+    assert ops.selected_impl(g["q"], g["k"], g["v"], g["la"], beta=g["beta"]) == "chunk"
+    y, S = ops.gdn_prefill(g["q"], g["k"], g["v"], g["la"], beta=g["beta"], initial_state=S0.cuda(), output_final_state=True, out_dtype=torch.float32)
+    check(y, y_o, f"y DV={DV}")
+    check(S, S_o, f"S_T DV={DV}")

@@ -19,6 +19,12 @@ from oracle import oracle as O
 pytestmark = pytest.mark.gpu
 
 
+@pytest.fixture(autouse=True)
+def _inference_mode():
+    with torch.no_grad():
+        yield
+
+
 def conv_silu(x, w, bias=None):
     T = x.shape[1]
     y = F.conv1d(x.transpose(1, 2), w, bias, padding=w.shape[-1] - 1, groups=x.shape[2])
@@ -27,8 +33,8 @@ def conv_silu(x, w, bias=None):
 
 def scan64(q, k, v, la, beta=None, u=None):
     """Oracle token mixing on inputs rounded to bf16 exactly as the layer hands them to the kernel."""
-    r = lambda t: t.to(torch.bfloat16).double().numpy()
-    y, _ = O.recurrence(r(q), r(k), r(v), la.double().numpy(), beta=None if beta is None else beta.double().numpy(),
+    r = lambda t: t.detach().to(torch.bfloat16).double().numpy()
+    y, _ = O.recurrence(r(q), r(k), r(v), la.detach().double().numpy(), beta=None if beta is None else beta.detach().double().numpy(),
                         u=None if u is None else r(u))
     return torch.from_numpy(y)
 
