@@ -32,7 +32,8 @@ namespace ws {
 
 constexpr int C = 64;
 constexpr int D = 128;
-constexpr int NT = 384;
+constexpr int NT = 384;     // warps 0-3: state chain; warps 4-11: workers (prep + output)
+constexpr int NWORK = 256;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t COL_S = 0, COL_G = 128, COL_W = 192, COL_U = 256, COL_Y = 384;  // U, Y: +64 per buffer
 constexpr uint32_t TILE = 8192;
@@ -46,20 +47,22 @@ constexpr uint32_t KQ_BYTES = 4 * TILE;
 constexpr uint32_t VB = KQ + 3 * KQ_BYTES;        // 2 x [V0][V1]
 constexpr uint32_t V_BYTES = 2 * TILE;
 constexpr uint32_t SR = VB + 2 * V_BYTES;         // S16 (2 x 16 KB) | R16 (16 KB) + R'16 (16 KB)
-constexpr uint32_t TW = SR + 4 * TILE;            // T16 (8 KB) + TG16 (8 KB) | W16 (16 KB)
+constexpr uint32_t TW = SR + 4 * TILE;            // T_hi (bf16, 8 KB) + TG16 (8 KB) | W16 (16 KB)
 constexpr uint32_t AB = TW + 2 * TILE;            // 2 x A16 (8 KB)
-constexpr uint32_t L16 = AB + 2 * TILE;           // 64 rows x 144 B (diagonal blocks hold D_b)
+constexpr uint32_t TLO = AB + 2 * TILE;           // T_lo (bf16, 8 KB): T = T_hi + T_lo to ~2^-16
+constexpr uint32_t L16 = TLO + TILE;              // 64 rows x 144 B (diagonal blocks hold D_b)
 constexpr uint32_t LDIAG = L16 + 64 * LD16;       // 4 x 16 x LDG floats
-constexpr uint32_t SMALL = LDIAG + 4 * 16 * LDG * 4;
+constexpr uint32_t EXPT = LDIAG + 4 * 16 * LDG * 4;  // decay tables: 64 + 4x64 + 4x16x17 floats
+constexpr uint32_t SMALL = EXPT + (64 + 4 * 64 + 4 * 16 * 20) * 4;
 constexpr uint32_t SLOT = 6 * C;                  // floats per gate slot: la, beta, g, gam, w, misc
 constexpr uint32_t BARS = SMALL + 3 * SLOT * 4;
-constexpr uint32_t NBARS = 16;
+constexpr uint32_t NBARS = 18;
 constexpr uint32_t TOTAL = BARS + NBARS * 8 + 16;
 constexpr uint32_t DYN = TOTAL + 1024;
 static_assert(DYN <= 232448, "shared memory budget");
-static_assert(SR % 1024 == 0 && TW % 1024 == 0 && AB % 1024 == 0, "swizzled tiles need 1 KB alignment");
+static_assert(SR % 1024 == 0 && TW % 1024 == 0 && AB % 1024 == 0 && TLO % 1024 == 0, "swizzled tiles need 1 KB alignment");
 
-enum Bar { B_KQ = 0, B_V = 3, B_G = 5, B_WU = 6, B_PREP = 7, B_R = 8, B_S = 9, B_YF = 10, B_YE = 12, B_DRAIN = 14 };
+enum Bar { B_KQ = 0, B_V = 3, B_G = 5, B_WU = 6, B_PREP = 7, B_R = 8, B_S = 9, B_YF = 10, B_YE = 12, B_DRAIN = 14, B_UU = 16 };
 
 struct Params {
   const float* beta;
@@ -110,32 +113,55 @@ __device__ __forceinline__ uint32_t frag_addr_sw(uint32_t base, int row0, int co
   return base + sw128(row, chunk);
 }
 
+__device__ __forceinline__ uint32_t pack_bf2(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
 // Block column J of T = (I + L)^-1, computed transposed so that C fragments chain into A
 // fragments: T^T_{J,i} = -(sum_{k=J}^{i-1} T^T_{J,k} L^T_{k,i}) D_i^T, with D_i = (I + L_ii)^-1 in
-// the diagonal blocks of L16.  Writes T (to T16) and T diag(gamma) (to TG16), block column J,
-// including the zero blocks above the diagonal.
+// the diagonal blocks of L16.  Writes block column J (including the zero blocks above the
+// diagonal) of T as a bf16 pair (T_hi + T_lo: the B operand of U^T = V^T T^T, whose A operand is
+// the bf16 V tile as loaded) and of T Gamma in fp16 (for W^T = K^T (T Gamma)^T).
 template <int J>
-__device__ __forceinline__ void merge_column(uint32_t l16, uint32_t t16, uint32_t tg16, const float* gam, int lane) {
+__device__ __forceinline__ void merge_column(uint32_t l16, uint32_t thi, uint32_t tlo, uint32_t tg16, const float* gam,
+                                             int lane) {
   const int g = lane >> 2;
   const float g0 = gam[16 * J + g], g8 = gam[16 * J + g + 8];
   uint32_t X[4][4];
   ptx::ldsm_x4_t(frag_addr_plain(l16, LD16, 16 * J, 16 * J, lane), X[J]);
-  auto emit = [&](int i, const uint32_t (&a)[4]) {
-    ptx::stsm_x4_t(frag_addr_sw(t16, 16 * i, 16 * J, lane), a);
-    uint32_t s[4];
+  // fp32 fragment (8 values in A-fragment order) -> T_hi, T_lo, T Gamma tiles, block (i, J).
+  auto emit = [&](int i, const float (&f)[8]) {
+    uint32_t hi[4], lo[4], gs[4];
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
-      const float2 f = unpack_h2(a[r]);
+      const float a = f[2 * r], b = f[2 * r + 1];
+      const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+      const float2 hf = __bfloat1622float2(h);
+      hi[r] = *reinterpret_cast<const uint32_t*>(&h);
+      lo[r] = pack_bf2(a - hf.x, b - hf.y);
       const float sc = (r & 1) ? g8 : g0;
-      s[r] = pack_h2(f.x * sc, f.y * sc);
+      gs[r] = pack_h2(a * sc, b * sc);
     }
-    ptx::stsm_x4_t(frag_addr_sw(tg16, 16 * i, 16 * J, lane), s);
+    ptx::stsm_x4_t(frag_addr_sw(thi, 16 * i, 16 * J, lane), hi);
+    ptx::stsm_x4_t(frag_addr_sw(tlo, 16 * i, 16 * J, lane), lo);
+    ptx::stsm_x4_t(frag_addr_sw(tg16, 16 * i, 16 * J, lane), gs);
   };
-  emit(J, X[J]);
+  {
+    float f[8];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const float2 v = unpack_h2(X[J][r]);
+      f[2 * r] = v.x;
+      f[2 * r + 1] = v.y;
+    }
+    emit(J, f);
+  }
   const uint32_t z[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
   for (int i = 0; i < J; ++i) {
-    ptx::stsm_x4_t(frag_addr_sw(t16, 16 * i, 16 * J, lane), z);
+    ptx::stsm_x4_t(frag_addr_sw(thi, 16 * i, 16 * J, lane), z);
+    ptx::stsm_x4_t(frag_addr_sw(tlo, 16 * i, 16 * J, lane), z);
     ptx::stsm_x4_t(frag_addr_sw(tg16, 16 * i, 16 * J, lane), z);
   }
 #pragma unroll
@@ -158,17 +184,14 @@ __device__ __forceinline__ void merge_column(uint32_t l16, uint32_t t16, uint32_
     X[i][1] = pack_h2(Tt[2], Tt[3]);
     X[i][2] = pack_h2(Tt[4], Tt[5]);
     X[i][3] = pack_h2(Tt[6], Tt[7]);
-    ptx::stsm_x4_t(frag_addr_sw(t16, 16 * i, 16 * J, lane), X[i]);
-    const uint32_t s[4] = {pack_h2(Tt[0] * g0, Tt[1] * g0), pack_h2(Tt[2] * g8, Tt[3] * g8),
-                           pack_h2(Tt[4] * g0, Tt[5] * g0), pack_h2(Tt[6] * g8, Tt[7] * g8)};
-    ptx::stsm_x4_t(frag_addr_sw(tg16, 16 * i, 16 * J, lane), s);
+    emit(i, Tt);
   }
 }
 
 template <typename TOut>
 __global__ void __launch_bounds__(NT, 1)
     ws_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-              const __grid_constant__ CUtensorMap tm_v, const Params p) {
+              const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_y, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sb = ptx::smem_u32(sm);
@@ -182,6 +205,9 @@ __global__ void __launch_bounds__(NT, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + NBARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* small = reinterpret_cast<float*>(sm + SMALL);
+  float* eT = reinterpret_cast<float*>(sm + EXPT);      // [64]      exp(g_t - g_{16 floor(t/16)})
+  float* eJ = eT + C;                                    // [4][64]   beta_j exp(g_{16b} - g_j), j < 16b
+  float* Ed = eJ + 4 * C;                                // [4][16][20] beta_{16b+c} exp(g_{16b+r} - g_{16b+c}), c <= r
 
   if (warp == 0) {
     ptx::tmem_alloc(tmem_slot, TMEM_COLS);
@@ -192,31 +218,33 @@ __global__ void __launch_bounds__(NT, 1)
     for (int i = 0; i < 2; ++i) ptx::mbar_init(&bars[B_V + i], 1);
     ptx::mbar_init(&bars[B_G], 1);
     ptx::mbar_init(&bars[B_WU], 1);
+    ptx::mbar_init(&bars[B_UU], 1);
     ptx::mbar_init(&bars[B_PREP], 1);
     ptx::mbar_init(&bars[B_R], 1);
     ptx::mbar_init(&bars[B_S], 1);
     for (int i = 0; i < 2; ++i) ptx::mbar_init(&bars[B_YF + i], 1);
-    for (int i = 0; i < 2; ++i) ptx::mbar_init(&bars[B_YE + i], 128);
+    for (int i = 0; i < 2; ++i) ptx::mbar_init(&bars[B_YE + i], 4);  // one arrival per output warp
     for (int i = 0; i < 2; ++i) ptx::mbar_init(&bars[B_DRAIN + i], 1);
     *abort_flag = 0;
     ptx::fence_mbar_init();
     ptx::prefetch_tensormap(&tm_q);
     ptx::prefetch_tensormap(&tm_k);
     ptx::prefetch_tensormap(&tm_v);
+    ptx::prefetch_tensormap(&tm_y);
   }
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t my = tmem + ((uint32_t)((warp & 3) * 32) << 16);  // this warp's TMEM lane quarter
-  const int row = tid & 127;                                         // = TMEM lane of this thread
+  const int row = tid & 127;                                         // TMEM lane of this thread
 
-  // One elected thread of a 128-thread group waits on the mbarrier; a reducing named barrier
-  // hands the outcome to the whole group, so all of its threads take the same branch.
-  auto gwait = [&](int bar, uint32_t parity, bool leader, int group) -> bool {
+  // One elected thread of a group waits on the mbarrier; a reducing named barrier hands the
+  // outcome to the whole group, so all of its threads take the same branch.
+  auto gwait = [&](int bar, uint32_t parity, bool leader, int group, int n) -> bool {
     bool fail = false;
     if (leader) fail = !ptx::mbar_wait_abortable(&bars[bar], parity, WAIT_LIMIT, abort_flag);
-    return !ptx::named_bar_or(group, 128, fail);
+    return !ptx::named_bar_or(group, n, fail);
   };
   auto issue_kq = [&](int c) {
     uint8_t* dst = sm + KQ + (c % 3) * KQ_BYTES;
@@ -237,55 +265,102 @@ __global__ void __launch_bounds__(NT, 1)
   };
 
   constexpr uint32_t ID_G = ptx::idesc_bf16_f32(128, 64);
+  constexpr uint32_t ID_U_BF16 = ptx::idesc_bf16_f32(128, 64, true, false);  // V^T (bf16, MN-major) x T^T
   constexpr uint32_t ID_N64 = ptx::idesc_f16_f32(128, 64, false, false, false);
   constexpr uint32_t ID_N64_AMN = ptx::idesc_f16_f32(128, 64, true, false, false);
   constexpr uint32_t ID_N64_BMN_NEG = ptx::idesc_f16_f32(128, 64, false, true, true);
   constexpr uint32_t ID_N128_BMN = ptx::idesc_f16_f32(128, 128, false, true, false);
+  // Descriptor templates: an operand at byte offset `o` from the shared base is tmpl + (o >> 4).
+  const uint64_t D_K = ptx::sdesc_sw128(sb, 16, 1024);           // K-major operands
+  const uint64_t D_MN16K = ptx::sdesc_sw128(sb, 2 * TILE, 1024); // MN-major, 64-blocks 16 KB apart
+  const uint64_t D_MN8K = ptx::sdesc_sw128(sb, TILE, 1024);      // MN-major, 64-blocks 8 KB apart
+  auto at = [](uint64_t tmpl, uint32_t off) { return tmpl + (uint64_t)(off >> 4); };
 
-  if (warp < 4) {
-    // =============================== prep ===============================
-    const int pt = tid;
-    bool issued = false;  // MMAs issued by this thread since the last completed wait
-    int v_issued = 0;     // V loads issued (chunks [0, v_issued))
-    if (pt == 0) {
+  if (warp >= 4) {
+    // ============================ workers: prep of chunk c, y of chunk c-1 ============================
+    const int wt = tid - 128;            // 0..255
+    const int ww = wt >> 5;              // worker warp 0..7
+    const int hf = ww >> 2;              // column half (0: 0-31, 1: 32-63) of every 64-column tile
+    const bool leader = wt == 0;
+    bool issued = false;
+    int v_issued = 0;
+    float ga0 = 0.f, ga1 = 0.f, gb0 = 0.f, gb1 = 0.f;  // prefetched gates of the next chunk (worker warp 1)
+    auto load_gates = [&](int c) {
+      ga0 = ga1 = gb0 = gb1 = 0.f;
+      const int t0 = c * C;
+      const int64_t gi = ((int64_t)b * p.T + t0) * p.H + h;
+      if (t0 + lane < p.T) { ga0 = p.la[gi + (int64_t)lane * p.H]; gb0 = p.beta[gi + (int64_t)lane * p.H]; }
+      if (t0 + lane + 32 < p.T) { ga1 = p.la[gi + (int64_t)(lane + 32) * p.H]; gb1 = p.beta[gi + (int64_t)(lane + 32) * p.H]; }
+    };
+    if (ww == 1) load_gates(0);
+    if (leader) {
       issue_v(0);
       v_issued = 1;
       if (nch > 1) { issue_v(1); v_issued = 2; }
     }
+    // y of chunk c: TMEM -> shared staging -> HBM by TMA tile stores, done by the output warps
+    // (worker warps 4-7 = warps 8-11).  The staging buffer is A16 of chunk c, whose reader Yi(c)
+    // has completed once Y(c) is ready; the next writer of that buffer is prep(c+2), after this
+    // group's final wait for its stores to be read.  Y[c & 1] is released with one mbarrier
+    // arrival per warp.
+    auto epilogue = [&](int c) -> bool {
+      const int pp = c & 1;
+      if (!gwait(B_YF + pp, (uint32_t)(c >> 1) & 1u, wt == 128, 3, 128)) return false;
+      ptx::tc_fence_after();
+      float yv[64];
+      ptx::tmem_ld32(my + COL_Y + 64 * pp, *reinterpret_cast<float(*)[32]>(yv));
+      ptx::tmem_ld32(my + COL_Y + 64 * pp + 32, *reinterpret_cast<float(*)[32]>(yv + 32));
+      ptx::tc_wait_ld();
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&bars[B_YE + pp]);
+      constexpr int ROWS = (int)(TILE / (D * sizeof(TOut)));  // tokens per 8 KB staging piece
+      TOut* stage = reinterpret_cast<TOut*>(sm + AB + pp * TILE);
+#pragma unroll
+      for (int piece = 0; piece < C / ROWS; ++piece) {
+        if (piece > 0) {  // the previous piece's bytes must have been read out first
+          if (wt == 128) ptx::bulk_wait_read0();
+          ptx::named_bar(3, 128);
+        }
+#pragma unroll
+        for (int j = 0; j < ROWS; ++j) store_as(stage + j * D + row, yv[piece * ROWS + j]);
+        ptx::fence_proxy_async_smem();
+        ptx::named_bar(3, 128);
+        if (wt == 128) {
+          ptx::tma_store_4d(&tm_y, stage, dv0, h, c * C + piece * ROWS, b);
+          ptx::bulk_commit();
+        }
+      }
+      if (wt == 128) ptx::bulk_wait_read0();
+      return true;
+    };
+    int c = 0;
 #pragma unroll 1
-    for (int c = 0; c < nch; ++c) {
+    for (; c < nch; ++c) {
       const int pb = c & 1;
-      const uint32_t kq_a = sb + KQ + (c % 3) * KQ_BYTES;
-      uint8_t* kq = sm + KQ + (c % 3) * KQ_BYTES;
-      uint8_t* vv = sm + VB + pb * V_BYTES;
-      const uint32_t v_a = sb + VB + pb * V_BYTES;
+      const uint32_t kq_o = KQ + (c % 3) * KQ_BYTES;
+      uint8_t* kq = sm + kq_o;
+      const uint32_t v_o = VB + pb * V_BYTES;
       float* la_s = small + (c % 3) * SLOT;
       float* beta_s = la_s + C;
       float* g_s = beta_s + C;
       float* gam_s = g_s + C;
       float* w_s = gam_s + C;
       float* misc_s = w_s + C;
-      const int t0 = c * C;
 
-      if (!gwait(B_KQ + c % 3, (uint32_t)(c / 3) & 1u, pt == 0, 1)) break;
-      if (pt == 0) {  // G = [K;Q] K^T from the bf16 tiles as loaded
+      if (!gwait(B_KQ + c % 3, (uint32_t)(c / 3) & 1u, leader, 1, NWORK)) break;
+      if (leader) {  // G = [K;Q] K^T from the bf16 tiles as loaded
         ptx::tc_fence_after();
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
-          const uint32_t kb = k >> 2, kk = k & 3;
-          const uint64_t a = ptx::sdesc_sw128(kq_a + kb * 2 * TILE + kk * 32, 16, 1024);
+          const uint64_t a = at(D_K, kq_o + (k >> 2) * 2 * TILE + (k & 3) * 32);
           ptx::mma_f16_ss(tmem + COL_G, a, a, ID_G, k > 0);
         }
         ptx::mma_commit(&bars[B_G]);
         issued = true;
       }
-      if (warp == 0) {  // gates and chunk-local cumulative log-decay (log-space, fp32)
-        float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
-        const int64_t gi = ((int64_t)b * p.T + t0) * p.H + h;
-        if (t0 + lane < p.T) { a0 = p.la[gi + (int64_t)lane * p.H]; b0 = p.beta[gi + (int64_t)lane * p.H]; }
-        if (t0 + lane + 32 < p.T) { a1 = p.la[gi + (int64_t)(lane + 32) * p.H]; b1 = p.beta[gi + (int64_t)(lane + 32) * p.H]; }
-        beta_s[lane] = b0;
-        beta_s[lane + 32] = b1;
+      if (ww == 1) {  // chunk-local cumulative log-decay (not on the MMA-issuing warp)
+        float a0 = ga0, a1 = ga1;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
           const float n0 = __shfl_up_sync(0xffffffffu, a0, o);
@@ -294,25 +369,45 @@ __global__ void __launch_bounds__(NT, 1)
         }
         a1 += __shfl_sync(0xffffffffu, a0, 31);
         const float gC = __shfl_sync(0xffffffffu, a1, 31);
+        beta_s[lane] = gb0;
+        beta_s[lane + 32] = gb1;
         g_s[lane] = a0;
         g_s[lane + 32] = a1;
         gam_s[lane] = expf(a0);
         gam_s[lane + 32] = expf(a1);
-        w_s[lane] = b0 * expf(gC - a0);
-        w_s[lane + 32] = b1 * expf(gC - a1);
+        w_s[lane] = gb0 * expf(gC - a0);
+        w_s[lane + 32] = gb1 * expf(gC - a1);
         if (lane == 0) misc_s[0] = expf(gC);
       }
-      // V(c) must have landed too (issued two chunks ahead by this group's leader).
-      if (!gwait(B_V + pb, (uint32_t)(c >> 1) & 1u, pt == 0, 1)) break;
-      if (!gwait(B_G, (uint32_t)c & 1u, pt == 0, 1)) break;
-      if (pt == 0) issued = false;
+      ptx::named_bar(1, NWORK);
+      // Decay tables: 1,280 exponentials per chunk instead of one per (t, j) pair.  Every factor
+      // is exp of a non-positive number, so none overflows whatever the decay.
+#pragma unroll
+      for (int n = 0; n < 2; ++n) {  // 64 + 256 entries
+        const int e = wt + NWORK * n;
+        if (e < C) {
+          eT[e] = __expf(g_s[e] - g_s[e & ~15]);
+        } else if (e < 5 * C) {
+          const int bb = (e - C) >> 6, j = (e - C) & 63;
+          eJ[bb * C + j] = (bb > 0 && j < 16 * bb) ? beta_s[j] * __expf(g_s[16 * bb] - g_s[j]) : 0.f;
+        }
+      }
+#pragma unroll
+      for (int n = 0; n < 4; ++n) {
+        const int e = wt + NWORK * n;  // 1024 diagonal-block entries
+        const int bb = e >> 8, r = (e >> 4) & 15, cc = e & 15;
+        Ed[(bb * 16 + r) * 20 + cc] = cc <= r ? beta_s[16 * bb + cc] * __expf(g_s[16 * bb + r] - g_s[16 * bb + cc]) : 0.f;
+      }
+      if (!gwait(B_V + pb, (uint32_t)(c >> 1) & 1u, leader, 1, NWORK)) break;
+      if (!gwait(B_G, (uint32_t)c & 1u, leader, 1, NWORK)) break;
+      if (leader) issued = false;
       ptx::tc_fence_after();
 
-      // bf16 -> fp16 in place: K (tiles 0, 2), gamma-scaled Q (tiles 1, 3), V (2 tiles).
+      // bf16 -> fp16 in place: K (tiles 0, 2) and gamma-scaled Q (tiles 1, 3).  V stays bf16.
 #pragma unroll 4
-      for (int i = pt; i < 6 * 512; i += 128) {
+      for (int i = wt; i < 4 * 512; i += NWORK) {
         const int tile = i >> 9;
-        uint8_t* base = tile < 4 ? kq + tile * TILE : vv + (tile - 4) * TILE;
+        uint8_t* base = kq + tile * TILE;
         const int off = (i & 511) * 16;
         const float sc = (tile == 1 || tile == 3) ? gam_s[off >> 7] : 1.f;
         uint4 r = *reinterpret_cast<uint4*>(base + off);
@@ -326,32 +421,38 @@ __global__ void __launch_bounds__(NT, 1)
         }
         *reinterpret_cast<uint4*>(base + off) = o;
       }
-      // Rows of L (threads 0-63, TMEM lanes 0-63) and A (threads 64-127) from G.
-      float gv[64];
-      ptx::tmem_ld32(my + COL_G, *reinterpret_cast<float(*)[32]>(gv));
-      ptx::tmem_ld32(my + COL_G + 32, *reinterpret_cast<float(*)[32]>(gv + 32));
+      // Half-rows of L (TMEM lanes 0-63) and A (lanes 64-127) from G: columns 32 hf .. 32 hf + 31.
+      float gv[32];
+      ptx::tmem_ld32(my + COL_G + 32 * hf, gv);
       ptx::tc_wait_ld();
-      const int t = pt & 63;
-      const float gt = g_s[t];
-      const int jmax_blk = (warp & 1) ? 4 : 2;  // 16-column blocks that can hold j <= t in this warp
+      const int t = row & 63, tb = t >> 4;
+      const bool is_l = row < 64;
+      const float et = eT[t];
 #pragma unroll
-      for (int jb = 0; jb < 4; ++jb) {
-        if (jb < jmax_blk) {
+      for (int q2 = 0; q2 < 2; ++q2) {
+        const int jb = 2 * hf + q2;
+        // This thread's decay factors for the 16 columns of block jb (vector loads; the block's
+        // case -- below, on or above the diagonal block -- is fixed per thread).
+        float e[16];
+        const float4* src4 = jb < tb ? reinterpret_cast<const float4*>(eJ + tb * C + 16 * jb)
+                                     : reinterpret_cast<const float4*>(Ed + (tb * 16 + (t & 15)) * 20);
 #pragma unroll
-          for (int jj = 0; jj < 16; ++jj) {
-            const int j = jb * 16 + jj;
-            const bool keep = (pt < 64) ? (j < t) : (j <= t);
-            gv[j] = keep ? gv[j] * beta_s[j] * expf(gt - g_s[j]) : 0.f;
-          }
-        } else {
+        for (int v = 0; v < 4; ++v) {
+          const float4 f = src4[v];
+          e[4 * v] = f.x; e[4 * v + 1] = f.y; e[4 * v + 2] = f.z; e[4 * v + 3] = f.w;
+        }
+        const float sc = jb < tb ? et : (jb == tb ? 1.f : 0.f);
 #pragma unroll
-          for (int jj = 0; jj < 16; ++jj) gv[jb * 16 + jj] = 0.f;
+        for (int jj = 0; jj < 16; ++jj) {
+          float ej = e[jj] * sc;
+          if (is_l && 16 * jb + jj == t) ej = 0.f;
+          gv[16 * q2 + jj] *= ej;
         }
       }
-      if (pt < 64) {
-        uint8_t* lrow = sm + L16 + t * LD16;
+      if (is_l) {
+        uint8_t* lrow = sm + L16 + t * LD16 + hf * 64;
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
+        for (int q = 0; q < 4; ++q) {
           uint4 v4;
           v4.x = pack_h2(gv[q * 8 + 0], gv[q * 8 + 1]);
           v4.y = pack_h2(gv[q * 8 + 2], gv[q * 8 + 3]);
@@ -359,96 +460,123 @@ __global__ void __launch_bounds__(NT, 1)
           v4.w = pack_h2(gv[q * 8 + 6], gv[q * 8 + 7]);
           *reinterpret_cast<uint4*>(lrow + q * 16) = v4;
         }
-        float* drow = reinterpret_cast<float*>(sm + LDIAG) + ((t >> 4) * 16 + (t & 15)) * LDG;
-        const int bt = t >> 4;
-        float dv[16];  // gv[16 bt + q] with static register indices
+        if ((tb >> 1) == hf) {  // this half holds the row's diagonal block: keep it in fp32
+          float* drow = reinterpret_cast<float*>(sm + LDIAG) + (tb * 16 + (t & 15)) * LDG;
+          const bool second = (tb & 1) != 0;
 #pragma unroll
-        for (int q = 0; q < 16; ++q) dv[q] = bt == 0 ? gv[q] : bt == 1 ? gv[16 + q] : bt == 2 ? gv[32 + q] : gv[48 + q];
-#pragma unroll
-        for (int q = 0; q < 16; q += 4)
-          *reinterpret_cast<float4*>(drow + q) = make_float4(dv[q], dv[q + 1], dv[q + 2], dv[q + 3]);
+          for (int q = 0; q < 16; q += 4)
+            *reinterpret_cast<float4*>(drow + q) =
+                second ? make_float4(gv[16 + q], gv[17 + q], gv[18 + q], gv[19 + q]) : make_float4(gv[q], gv[q + 1], gv[q + 2], gv[q + 3]);
+        }
       }
-      ptx::named_bar(1, 128);
-      // W16(c-1), which shares T16/TG16's space, must have been consumed by R(c-1), and A16[p]
-      // by Yi(c-2).
-      if (c > 0 && !gwait(B_R, (uint32_t)(c - 1) & 1u, pt == 0, 1)) break;
-      if (c >= 2 && !gwait(B_YF + pb, (uint32_t)((c - 2) >> 1) & 1u, pt == 0, 1)) break;
-      if (pt >= 64) {
-        store_row_f16(sm + AB + pb * TILE, t, gv);
-      } else {
-        // D_b = (I + L_bb)^-1, one column per thread, fp32 forward substitution.
-        const int bb = pt >> 4, j = pt & 15;
+      ptx::named_bar(1, NWORK);
+      // W16(c-1) shares T16/TG16's space (needs R(c-1) done); A16[pb] was read by Yi(c-2).
+      if (c > 0 && !gwait(B_R, (uint32_t)(c - 1) & 1u, leader, 1, NWORK)) break;
+      if (c >= 2 && !gwait(B_YF + pb, (uint32_t)((c - 2) >> 1) & 1u, leader, 1, NWORK)) break;
+      if (!is_l) {
+        uint8_t* arow = sm + AB + pb * TILE;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint4 v4;
+          v4.x = pack_h2(gv[q * 8 + 0], gv[q * 8 + 1]);
+          v4.y = pack_h2(gv[q * 8 + 2], gv[q * 8 + 3]);
+          v4.z = pack_h2(gv[q * 8 + 4], gv[q * 8 + 5]);
+          v4.w = pack_h2(gv[q * 8 + 6], gv[q * 8 + 7]);
+          *reinterpret_cast<uint4*>(arow + sw128(t, 4 * hf + q)) = v4;
+        }
+      } else if (wt < 64) {
+        // D_b = (I + L_bb)^-1, one column per thread; right-looking fp32 forward substitution
+        // (after x_m is known, every later row's sum takes its term at once: 15 independent FMAs).
+        const int bb = wt >> 4, j = wt & 15;
         const float* Lb = reinterpret_cast<const float*>(sm + LDIAG) + bb * 16 * LDG;
-        float x[16];
+        float x[16], acc[16];
 #pragma unroll
-        for (int r = 0; r < 16; ++r) {
-          float s = 0.f;
+        for (int r = 0; r < 16; ++r) acc[r] = 0.f;
 #pragma unroll
-          for (int m = 0; m < r; ++m) s = fmaf(Lb[r * LDG + m], x[m], s);
-          x[r] = (r == j) ? 1.f : (r > j ? -s : 0.f);
+        for (int m = 0; m < 16; ++m) {
+          x[m] = (m == j) ? 1.f : (m > j ? -acc[m] : 0.f);
+#pragma unroll
+          for (int r = m + 1; r < 16; ++r) acc[r] = fmaf(Lb[r * LDG + m], x[m], acc[r]);
         }
         __half* l16 = reinterpret_cast<__half*>(sm + L16);
 #pragma unroll
         for (int r = 0; r < 16; ++r) l16[(bb * 16 + r) * (LD16 / 2) + bb * 16 + j] = __float2half_rn(x[r]);
       }
-      ptx::named_bar(1, 128);
-      {
-        const uint32_t l16a = sb + L16, t16a = sb + TW, tg16a = sb + TW + TILE;
-        switch (warp) {
-          case 0: merge_column<0>(l16a, t16a, tg16a, gam_s, lane); break;
-          case 1: merge_column<1>(l16a, t16a, tg16a, gam_s, lane); break;
-          case 2: merge_column<2>(l16a, t16a, tg16a, gam_s, lane); break;
-          default: merge_column<3>(l16a, t16a, tg16a, gam_s, lane); break;
+      bool epi_ok = true;
+      if (ww >= 4) {
+        if (c >= 1) epi_ok = epilogue(c - 1);  // overlaps the diagonal blocks and the merges
+      } else {
+        ptx::named_bar(4, 128);  // D_b in L16 before the merges read it (warps 4-7 only)
+        const uint32_t l16a = sb + L16, thi = sb + TW, tlo = sb + TLO, tg16a = sb + TW + TILE;
+        switch (ww) {
+          case 0: merge_column<0>(l16a, thi, tlo, tg16a, gam_s, lane); break;
+          case 1: merge_column<1>(l16a, thi, tlo, tg16a, gam_s, lane); break;
+          case 2: merge_column<2>(l16a, thi, tlo, tg16a, gam_s, lane); break;
+          default: merge_column<3>(l16a, thi, tlo, tg16a, gam_s, lane); break;
         }
       }
       ptx::fence_proxy_async_smem();
-      ptx::named_bar(1, 128);
-      if (pt == 0) {  // W^T = K^T (T Gamma)^T, U^T = V^T T^T
+      if (ptx::named_bar_or(1, NWORK, !epi_ok)) break;
+      if (leader) {  // W^T = K^T (T Gamma)^T (waited for below), then U^T = V^T T^T (checked at ready)
         ptx::tc_fence_after();
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const uint64_t ak = ptx::sdesc_sw128(kq_a + k * 2048, 2 * TILE, 1024);
-          const uint64_t bt = ptx::sdesc_sw128(sb + TW + TILE + k * 32, 16, 1024);
-          ptx::mma_f16_ss(tmem + COL_W, ak, bt, ID_N64_AMN, k > 0);
-        }
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const uint64_t av = ptx::sdesc_sw128(v_a + k * 2048, TILE, 1024);
-          const uint64_t bt = ptx::sdesc_sw128(sb + TW + k * 32, 16, 1024);
-          ptx::mma_f16_ss(tmem + COL_U + 64 * pb, av, bt, ID_N64_AMN, k > 0);
-        }
+        for (int k = 0; k < 4; ++k)
+          ptx::mma_f16_ss(tmem + COL_W, at(D_MN16K, kq_o + k * 2048), at(D_K, TW + TILE + k * 32), ID_N64_AMN, k > 0);
         ptx::mma_commit(&bars[B_WU]);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          ptx::mma_f16_ss(tmem + COL_U + 64 * pb, at(D_MN8K, v_o + k * 2048), at(D_K, TW + k * 32), ID_U_BF16, k > 0);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          ptx::mma_f16_ss(tmem + COL_U + 64 * pb, at(D_MN8K, v_o + k * 2048), at(D_K, TLO + k * 32), ID_U_BF16, 1);
+        ptx::mma_commit(&bars[B_UU]);
         issued = true;
       }
-      if (!gwait(B_WU, (uint32_t)c & 1u, pt == 0, 1)) break;
-      if (pt == 0) {
-        issued = false;
-        if (c + 2 < nch) { issue_v(c + 2); v_issued = c + 3; }  // V(c) consumed by U^T(c)
-      }
+      if (ww == 1 && c + 1 < nch) load_gates(c + 1);  // latency hidden behind the MMAs below
+      if (!gwait(B_WU, (uint32_t)c & 1u, leader, 1, NWORK)) break;
       ptx::tc_fence_after();
       {
-        float wv[64];
-        ptx::tmem_ld32(my + COL_W, *reinterpret_cast<float(*)[32]>(wv));
-        ptx::tmem_ld32(my + COL_W + 32, *reinterpret_cast<float(*)[32]>(wv + 32));
+        float wv[32];
+        ptx::tmem_ld32(my + COL_W + 32 * hf, wv);
         ptx::tc_wait_ld();
-        store_row_f16(sm + TW, pt, wv);  // W16: row d = TMEM lane, 64 tokens
+        uint8_t* wrow = sm + TW;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint4 v4;
+          v4.x = pack_h2(wv[q * 8 + 0], wv[q * 8 + 1]);
+          v4.y = pack_h2(wv[q * 8 + 2], wv[q * 8 + 3]);
+          v4.z = pack_h2(wv[q * 8 + 4], wv[q * 8 + 5]);
+          v4.w = pack_h2(wv[q * 8 + 6], wv[q * 8 + 7]);
+          *reinterpret_cast<uint4*>(wrow + sw128(row, 4 * hf + q)) = v4;  // W16: row d, 64 tokens
+        }
       }
       ptx::fence_proxy_async_smem();
       ptx::tc_fence_before();
-      ptx::named_bar(1, 128);
-      if (pt == 0) ptx::mbar_arrive(&bars[B_PREP]);
+      {
+        bool fail = false;
+        if (leader) fail = !ptx::mbar_wait_abortable(&bars[B_UU], (uint32_t)c & 1u, WAIT_LIMIT, abort_flag);
+        if (ptx::named_bar_or(1, NWORK, fail)) break;
+      }
+      if (leader) {
+        issued = false;
+        ptx::mbar_arrive(&bars[B_PREP]);
+        if (c + 2 < nch) { issue_v(c + 2); v_issued = c + 3; }  // V(c) consumed by U^T(c)
+      }
     }
-    if (*abort_flag && pt == 0) {  // drain this thread's MMAs and V loads before the CTA exits
+    if (c == nch && nch > 0 && ww >= 4) epilogue(nch - 1);
+    if (wt == 128) ptx::bulk_wait0();
+    if (*abort_flag && leader) {  // drain this thread's MMAs and V loads before the CTA exits
       if (issued) {
         ptx::mma_commit(&bars[B_DRAIN]);
         ptx::mbar_wait_bounded(&bars[B_DRAIN], 0, WAIT_LIMIT);
       }
-      for (int c = v_issued - 2 < 0 ? 0 : v_issued - 2; c < v_issued; ++c)
-        ptx::mbar_wait_bounded(&bars[B_V + (c & 1)], (uint32_t)(c >> 1) & 1u, WAIT_LIMIT);
+      for (int cc = v_issued - 2 < 0 ? 0 : v_issued - 2; cc < v_issued; ++cc)
+        ptx::mbar_wait_bounded(&bars[B_V + (cc & 1)], (uint32_t)(cc >> 1) & 1u, WAIT_LIMIT);
     }
-  } else if (warp < 8) {
-    // =============================== chain ===============================
-    const int ct = tid - 128;
+  } else {
+    // ==================================== state chain ====================================
+    const int ct = tid;
+    const bool leader = ct == 0;
     bool issued = false;
     {
       const float* src = p.s0 ? p.s0 + ((int64_t)bh * p.DV + dv0 + ct) * D : nullptr;
@@ -464,81 +592,73 @@ __global__ void __launch_bounds__(NT, 1)
       }
       ptx::tc_wait_st();
     }
-    int kq_issued = 0;  // q/k loads issued (chunks [0, kq_issued))
-    if (ct == 0) {
+    int kq_issued = 0;
+    if (leader) {
       issue_kq(0);
       kq_issued = 1;
       if (nch > 1) { issue_kq(1); kq_issued = 2; }
     }
-    int c = 0;
 #pragma unroll 1
-    for (; c < nch; ++c) {
+    for (int c = 0; c < nch; ++c) {
       const int pb = c & 1;
-      const uint32_t kq_a = sb + KQ + (c % 3) * KQ_BYTES;
+      const uint32_t kq_o = KQ + (c % 3) * KQ_BYTES;
       const float* slot = small + (c % 3) * SLOT;
       const float* w_s = slot + 4 * C;
-      if (!gwait(B_PREP, (uint32_t)c & 1u, ct == 0, 2)) break;
+      if (!gwait(B_PREP, (uint32_t)c & 1u, leader, 2, 128)) break;
       const float gC = slot[5 * C];  // written by prep(c): read only after its ready barrier
       if (c > 0) {
-        if (!gwait(B_S, (uint32_t)(c - 1) & 1u, ct == 0, 2)) break;
-        if (ct == 0) issued = false;
+        if (!gwait(B_S, (uint32_t)(c - 1) & 1u, leader, 2, 128)) break;
+        if (leader) issued = false;
       }
       ptx::tc_fence_after();
-      if (ct == 0 && c + 2 < nch) { issue_kq(c + 2); kq_issued = c + 3; }  // buffer of chunk c-1, freed by S(c-1)
-      // S16 <- fp16(S); S <- gamma_C S
-#pragma unroll 1
-      for (int c4 = 0; c4 < 4; ++c4) {
-        float v[32];
-        ptx::tmem_ld32(my + COL_S + c4 * 32, v);
-        ptx::tc_wait_ld();
-        uint8_t* half = sm + SR + (c4 >> 1) * 2 * TILE;
+      if (leader && c + 2 < nch) { issue_kq(c + 2); kq_issued = c + 3; }  // buffer of chunk c-1, freed by S(c-1)
+      // S16 <- fp16(S): four loads, one wait.
+      float sv[128];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          uint4 pk;
-          pk.x = pack_h2(v[q * 8 + 0], v[q * 8 + 1]);
-          pk.y = pack_h2(v[q * 8 + 2], v[q * 8 + 3]);
-          pk.z = pack_h2(v[q * 8 + 4], v[q * 8 + 5]);
-          pk.w = pack_h2(v[q * 8 + 6], v[q * 8 + 7]);
-          *reinterpret_cast<uint4*>(half + sw128(ct, (c4 & 1) * 4 + q)) = pk;
-        }
+      for (int c4 = 0; c4 < 4; ++c4) ptx::tmem_ld32(my + COL_S + c4 * 32, *reinterpret_cast<float(*)[32]>(sv + 32 * c4));
+      ptx::tc_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] *= gC;
-        ptx::tmem_st32(my + COL_S + c4 * 32, v);
+      for (int q = 0; q < 16; ++q) {
+        uint4 pk;
+        pk.x = pack_h2(sv[q * 8 + 0], sv[q * 8 + 1]);
+        pk.y = pack_h2(sv[q * 8 + 2], sv[q * 8 + 3]);
+        pk.z = pack_h2(sv[q * 8 + 4], sv[q * 8 + 5]);
+        pk.w = pack_h2(sv[q * 8 + 6], sv[q * 8 + 7]);
+        *reinterpret_cast<uint4*>(sm + SR + (q >> 3) * 2 * TILE + sw128(ct, q & 7)) = pk;
       }
-      ptx::tc_wait_st();
       ptx::fence_proxy_async_smem();
       ptx::tc_fence_before();
       ptx::named_bar(2, 128);
       bool r_ok = true;
-      if (ct == 0) {  // R^T = U^T - S W^T ; Y = S (Gamma Q)^T
+      if (leader) {  // R^T = U^T - S W^T ; Y = S (Gamma Q)^T
         ptx::tc_fence_after();
-        if (c >= 2)  // Y[p] drained by the epilogue
+        if (c >= 2)  // Y[pb] drained by the workers
           r_ok = ptx::mbar_wait_abortable(&bars[B_YE + pb], (uint32_t)((c - 2) >> 1) & 1u, WAIT_LIMIT, abort_flag);
         if (r_ok) {
 #pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const uint32_t kb = k >> 2, kk = k & 3;
-            const uint64_t as = ptx::sdesc_sw128(sb + SR + kb * 2 * TILE + kk * 32, 16, 1024);
-            const uint64_t bw = ptx::sdesc_sw128(sb + TW + k * 2048, 16, 1024);
-            ptx::mma_f16_ss(tmem + COL_U + 64 * pb, as, bw, ID_N64_BMN_NEG, 1);
-          }
+          for (int k = 0; k < 8; ++k)
+            ptx::mma_f16_ss(tmem + COL_U + 64 * pb, at(D_K, SR + (k >> 2) * 2 * TILE + (k & 3) * 32),
+                            at(D_K, TW + k * 2048), ID_N64_BMN_NEG, 1);
 #pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const uint32_t kb = k >> 2, kk = k & 3;
-            const uint64_t as = ptx::sdesc_sw128(sb + SR + kb * 2 * TILE + kk * 32, 16, 1024);
-            const uint64_t bq = ptx::sdesc_sw128(kq_a + TILE + kb * 2 * TILE + kk * 32, 16, 1024);
-            ptx::mma_f16_ss(tmem + COL_Y + 64 * pb, as, bq, ID_N64, k > 0);
-          }
+          for (int k = 0; k < 8; ++k)
+            ptx::mma_f16_ss(tmem + COL_Y + 64 * pb, at(D_K, SR + (k >> 2) * 2 * TILE + (k & 3) * 32),
+                            at(D_K, kq_o + TILE + (k >> 2) * 2 * TILE + (k & 3) * 32), ID_N64, k > 0);
           ptx::mma_commit(&bars[B_R]);
           issued = true;
         }
       }
+      // S <- gamma_C S while the MMAs run (they do not touch the S columns).
+#pragma unroll
+      for (int i = 0; i < 128; ++i) sv[i] *= gC;
+#pragma unroll
+      for (int c4 = 0; c4 < 4; ++c4) ptx::tmem_st32(my + COL_S + c4 * 32, *reinterpret_cast<float(*)[32]>(sv + 32 * c4));
+      ptx::tc_wait_st();
       {
         bool fail = false;
-        if (ct == 0) fail = !r_ok || !ptx::mbar_wait_abortable(&bars[B_R], (uint32_t)c & 1u, WAIT_LIMIT, abort_flag);
+        if (leader) fail = !r_ok || !ptx::mbar_wait_abortable(&bars[B_R], (uint32_t)c & 1u, WAIT_LIMIT, abort_flag);
         if (ptx::named_bar_or(2, 128, fail)) break;
       }
-      if (ct == 0) issued = false;
+      if (leader) issued = false;
       ptx::tc_fence_after();
       {
         float rv[64];
@@ -553,27 +673,21 @@ __global__ void __launch_bounds__(NT, 1)
       ptx::fence_proxy_async_smem();
       ptx::tc_fence_before();
       ptx::named_bar(2, 128);
-      if (ct == 0) {  // S += (R diag w)^T K ; Y += R^T A^T
+      if (leader) {  // S += (R diag w)^T K ; Y += R^T A^T
         ptx::tc_fence_after();
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const uint64_t ap = ptx::sdesc_sw128(sb + SR + 2 * TILE + k * 32, 16, 1024);
-          const uint64_t bk = ptx::sdesc_sw128(kq_a + k * 2048, 2 * TILE, 1024);
-          ptx::mma_f16_ss(tmem + COL_S, ap, bk, ID_N128_BMN, 1);
-        }
+        for (int k = 0; k < 4; ++k)
+          ptx::mma_f16_ss(tmem + COL_S, at(D_K, SR + 2 * TILE + k * 32), at(D_MN16K, kq_o + k * 2048), ID_N128_BMN, 1);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const uint64_t ar = ptx::sdesc_sw128(sb + SR + k * 32, 16, 1024);
-          const uint64_t ba = ptx::sdesc_sw128(sb + AB + pb * TILE + k * 32, 16, 1024);
-          ptx::mma_f16_ss(tmem + COL_Y + 64 * pb, ar, ba, ID_N64, 1);
-        }
+        for (int k = 0; k < 4; ++k)
+          ptx::mma_f16_ss(tmem + COL_Y + 64 * pb, at(D_K, SR + k * 32), at(D_K, AB + pb * TILE + k * 32), ID_N64, 1);
         ptx::mma_commit(&bars[B_S]);
         ptx::mma_commit(&bars[B_YF + pb]);
         issued = true;
       }
     }
-    if (!*abort_flag && nch > 0 && gwait(B_S, (uint32_t)(nch - 1) & 1u, ct == 0, 2)) {
-      if (ct == 0) issued = false;
+    if (!*abort_flag && nch > 0 && gwait(B_S, (uint32_t)(nch - 1) & 1u, leader, 2, 128)) {
+      if (leader) issued = false;
       ptx::tc_fence_after();
       if (p.s_out != nullptr) {
         float* dst = p.s_out + ((int64_t)bh * p.DV + dv0 + ct) * D;
@@ -588,36 +702,13 @@ __global__ void __launch_bounds__(NT, 1)
         }
       }
     }
-    if (*abort_flag && ct == 0) {  // drain this thread's MMAs and q/k loads before the CTA exits
+    if (*abort_flag && leader) {  // drain this thread's MMAs and q/k loads before the CTA exits
       if (issued) {
         ptx::mma_commit(&bars[B_DRAIN + 1]);
         ptx::mbar_wait_bounded(&bars[B_DRAIN + 1], 0, WAIT_LIMIT);
       }
       for (int c = kq_issued - 3 < 0 ? 0 : kq_issued - 3; c < kq_issued; ++c)
         ptx::mbar_wait_bounded(&bars[B_KQ + c % 3], (uint32_t)(c / 3) & 1u, WAIT_LIMIT);
-    }
-  } else {
-    // =============================== epilogue ===============================
-    const int et = tid - 256;
-    TOut* yb = static_cast<TOut*>(p.y) + (int64_t)b * p.sy.b + (int64_t)h * p.sy.h + dv0 + et;
-#pragma unroll 1
-    for (int c = 0; c < nch; ++c) {
-      const int pp = c & 1;
-      if (!gwait(B_YF + pp, (uint32_t)(c >> 1) & 1u, et == 0, 3)) break;
-      ptx::tc_fence_after();
-      float y0[32], y1[32];
-      ptx::tmem_ld32(my + COL_Y + 64 * pp, y0);
-      ptx::tmem_ld32(my + COL_Y + 64 * pp + 32, y1);
-      ptx::tc_wait_ld();
-      ptx::tc_fence_before();
-      ptx::mbar_arrive(&bars[B_YE + pp]);
-      const int t0 = c * C, nvalid = min(C, p.T - t0);
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (j < nvalid) store_as(yb + (int64_t)(t0 + j) * p.sy.t, y0[j]);
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (32 + j < nvalid) store_as(yb + (int64_t)(t0 + 32 + j) * p.sy.t, y1[j]);
     }
   }
 
@@ -653,11 +744,26 @@ bool make_map(CUtensorMap* m, const void* base, int64_t F, const gdn_prefill_arg
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// y [B][T][H][DV] -> 4-D store map (f, h, t, b), box 128 features x 1 x (8 KB / 256 B) tokens, no swizzle.
+template <typename TOut>
+bool make_store_map(CUtensorMap* m, void* base, int64_t F, const gdn_prefill_args* a, const gdn_strides& s) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  constexpr int es = (int)sizeof(TOut);
+  cuuint64_t dims[4] = {(cuuint64_t)F, (cuuint64_t)a->H, (cuuint64_t)a->T, (cuuint64_t)a->B};
+  cuuint64_t strides[3] = {(cuuint64_t)s.h * es, (cuuint64_t)s.t * es, (cuuint64_t)s.b * es};
+  cuuint32_t box[4] = {(cuuint32_t)D, 1, (cuuint32_t)(TILE / (D * es)), 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  return fn(m, es == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <typename TOut>
 int launch(const gdn_prefill_args* a, cudaStream_t stream) {
-  CUtensorMap mq, mk, mv;
+  CUtensorMap mq, mk, mv, my;
   if (!make_map(&mq, a->q, a->DK, a, a->sq) || !make_map(&mk, a->k, a->DK, a, a->sk) ||
-      !make_map(&mv, a->v, a->DV, a, a->sv))
+      !make_map(&mv, a->v, a->DV, a, a->sv) || !make_store_map<TOut>(&my, a->y, a->DV, a, a->sy))
     return GDN_ERR_LAUNCH;
   auto kern = ws_kernel<TOut>;
   static bool attr_set = false;
@@ -670,7 +776,7 @@ int launch(const gdn_prefill_args* a, cudaStream_t stream) {
   p.beta = a->beta; p.la = a->la; p.s0 = a->s0; p.s_out = a->s_out; p.y = a->y; p.sy = a->sy;
   p.B = (int)a->B; p.T = (int)a->T; p.H = (int)a->H; p.DV = (int)a->DV;
   const int64_t grid = a->B * a->H * (a->DV / D);
-  kern<<<(unsigned)grid, NT, DYN, stream>>>(mq, mk, mv, p);
+  kern<<<(unsigned)grid, NT, DYN, stream>>>(mq, mk, mv, my, p);
   return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
 }
 
@@ -679,7 +785,10 @@ int launch(const gdn_prefill_args* a, cudaStream_t stream) {
 
 // DK = 128, DV a multiple of 128, u = beta k (no explicit write vector).
 bool gdn_chunk_ws_supported(const gdn_prefill_args* a) {
-  return a->u == nullptr && a->DK == 128 && a->DV % 128 == 0 && a->DV >= 128;
+  if (a->u != nullptr || a->DK != 128 || a->DV % 128 != 0 || a->DV < 128) return false;
+  const int64_t es = a->out_dtype == GDN_DTYPE_BF16 ? 2 : 4;
+  auto ok = [&](int64_t x) { return x > 0 && (x * es) % 16 == 0; };
+  return a->y && (uintptr_t)a->y % 16 == 0 && ok(a->sy.h) && ok(a->sy.t) && ok(a->sy.b);
 }
 
 int gdn_launch_chunk_ws(const gdn_prefill_args* a, cudaStream_t stream) {

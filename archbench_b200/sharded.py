@@ -31,9 +31,9 @@ def gather_heads(y_local: torch.Tensor, world: int, group=None) -> torch.Tensor:
         return y_local
     y_local = y_local.contiguous()
     B, T, hl, DV = y_local.shape
-    buf = torch.empty((world, B, T, hl, DV), dtype=y_local.dtype, device=y_local.device)
-    dist.all_gather_into_tensor(buf, y_local, group=group)
-    return buf.permute(1, 2, 0, 3, 4).reshape(B, T, world * hl, DV)
+    buf = torch.empty((world * B, T, hl, DV), dtype=y_local.dtype, device=y_local.device)
+    dist.all_gather_into_tensor(buf, y_local, group=group)  # rank-major blocks along dim 0
+    return buf.view(world, B, T, hl, DV).permute(1, 2, 0, 3, 4).reshape(B, T, world * hl, DV)
 
 
 def sharded_prefill(q, k, v, la, beta=None, u=None, initial_state=None, output_final_state=False, gather=True, group=None, impl="auto"):
