@@ -51,7 +51,7 @@ int validate(const gdn_prefill_args* a) {
   if (a->B * a->H * a->DV > (1LL << 31)) return GDN_ERR_SHAPE;
   const int es = dtype_size(a->in_dtype);
   if (!es || !dtype_size(a->out_dtype)) return GDN_ERR_DTYPE;
-  if (a->impl < GDN_IMPL_AUTO || a->impl > GDN_IMPL_RECURRENT) return GDN_ERR_UNSUPPORTED;
+  if (a->impl < GDN_IMPL_AUTO || a->impl > GDN_IMPL_SEGMENTED) return GDN_ERR_UNSUPPORTED;
   // The recurrent kernel reads DK/32 consecutive elements per lane as one vector.
   const int vec = (int)(a->DK / 32) * es;
   const int vb = vec >= 16 ? 16 : vec;
@@ -66,11 +66,29 @@ int validate(const gdn_prefill_args* a) {
   return GDN_OK;
 }
 
+// SM count used for planning: the current device's when a CUDA device is present, else the
+// B200's 148 (host-only queries on machines without a GPU).
+int plan_sms() {
+  const int n = gdn_segmented_sms();
+  return n > 0 ? n : 148;
+}
+
 int select_impl(const gdn_prefill_args* a) {
   const bool chunk_ok = gdn_chunk_supported(a);
-  if (a->impl == GDN_IMPL_CHUNK) return chunk_ok ? (int)GDN_IMPL_CHUNK : (int)GDN_ERR_UNSUPPORTED;
-  if (a->impl == GDN_IMPL_RECURRENT) return (int)GDN_IMPL_RECURRENT;
-  return chunk_ok ? (int)GDN_IMPL_CHUNK : (int)GDN_IMPL_RECURRENT;
+  int P = 0, L = 0;
+  size_t need = 0;
+  const bool seg_ok = chunk_ok && gdn_segmented_plan(a, plan_sms(), &P, &L, &need);
+  const bool ws_ok = seg_ok && a->workspace != nullptr && a->workspace_bytes >= need;
+  switch (a->impl) {
+    case GDN_IMPL_CHUNK: return chunk_ok ? (int)GDN_IMPL_CHUNK : (int)GDN_ERR_UNSUPPORTED;
+    case GDN_IMPL_RECURRENT: return (int)GDN_IMPL_RECURRENT;
+    case GDN_IMPL_SEGMENTED:
+      if (!seg_ok) return (int)GDN_ERR_UNSUPPORTED;
+      return ws_ok ? (int)GDN_IMPL_SEGMENTED : (int)GDN_ERR_SHAPE;
+    default:
+      if (ws_ok) return (int)GDN_IMPL_SEGMENTED;
+      return chunk_ok ? (int)GDN_IMPL_CHUNK : (int)GDN_IMPL_RECURRENT;
+  }
 }
 
 }  // namespace
@@ -112,6 +130,11 @@ int gdn_prefill_workspace_bytes(const gdn_prefill_args* a, size_t* bytes) {
   int st = validate(a);
   if (st != GDN_OK) return st;
   *bytes = 0;
+  int P = 0, L = 0;
+  size_t need = 0;
+  if (a->impl != GDN_IMPL_CHUNK && a->impl != GDN_IMPL_RECURRENT && a->T > 0 &&
+      gdn_segmented_plan(a, plan_sms(), &P, &L, &need))
+    *bytes = need;
   return GDN_OK;
 }
 
@@ -138,6 +161,8 @@ int gdn_prefill_fwd(const gdn_prefill_args* a, void* stream) {
   }
   const int impl = select_impl(a);
   if (impl < 0) return impl;
+  if (impl == GDN_IMPL_SEGMENTED)
+    return gdn_launch_segmented(a, static_cast<float*>(a->workspace), (size_t)a->workspace_bytes, plan_sms(), s);
   if (impl == GDN_IMPL_CHUNK) return gdn_launch_chunk_sm100(a, s);
   return gdn_launch_recurrent(a, a->s0, a->s_out, s);
 }

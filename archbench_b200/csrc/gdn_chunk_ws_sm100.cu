@@ -72,6 +72,14 @@ struct Params {
   void* y;
   gdn_strides sy;
   int B, T, H, DV;
+  // Segments: CTA (b, h, seg, tile) runs chunks [seg * seg_len, (seg + 1) * seg_len).
+  int nseg, seg_len;
+  int nv;      // real 128-row state tiles (DV / 128)
+  int ntiles;  // tiles per (b, h, seg): nv, or nv + 1 in state mode (the transition block)
+  int mode;    // 0: outputs y (and S_T of the last segment); 1: segment states only, no y
+  const float* seg_s0;  // mode 0: initial state of segment s >= 1 at slot (bh, s - 1)
+  float* seg_out;       // mode 1: [N_s; M_s] of each segment at slot (bh, s)
+  int ws_stride;        // slots per (b, h) in the segment workspace
 };
 
 __device__ int g_status = 0;
@@ -196,10 +204,14 @@ __global__ void __launch_bounds__(NT, 1)
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sb = ptx::smem_u32(sm);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int dv_tiles = p.DV / D;
-  const int bh = blockIdx.x / dv_tiles, dv0 = (blockIdx.x % dv_tiles) * D;
+  const int tile = blockIdx.x % p.ntiles, rest = blockIdx.x / p.ntiles;
+  const int seg = rest % p.nseg, bh = rest / p.nseg;
+  const int dv0 = tile * D;
   const int b = bh / p.H, h = bh % p.H;
-  const int nch = (p.T + C - 1) / C;
+  const bool virt = tile >= p.nv;   // state mode: the transition block (v = 0, S_0 = I)
+  const bool want_y = p.mode == 0;
+  const int cb = seg * p.seg_len;    // first chunk of this CTA's segment
+  const int nch = max(0, min((p.T + C - 1) / C - cb, p.seg_len));
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + BARS);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + NBARS);
@@ -250,7 +262,7 @@ __global__ void __launch_bounds__(NT, 1)
     uint8_t* dst = sm + KQ + (c % 3) * KQ_BYTES;
     uint64_t* bar = &bars[B_KQ + c % 3];
     ptx::mbar_arrive_expect_tx(bar, KQ_BYTES);
-    const int t0 = c * C;
+    const int t0 = (cb + c) * C;
     ptx::tma_load_4d(dst + 0 * TILE, &tm_k, bar, 0, h, t0, b);
     ptx::tma_load_4d(dst + 1 * TILE, &tm_q, bar, 0, h, t0, b);
     ptx::tma_load_4d(dst + 2 * TILE, &tm_k, bar, 64, h, t0, b);
@@ -260,8 +272,8 @@ __global__ void __launch_bounds__(NT, 1)
     uint8_t* dst = sm + VB + (c & 1) * V_BYTES;
     uint64_t* bar = &bars[B_V + (c & 1)];
     ptx::mbar_arrive_expect_tx(bar, V_BYTES);
-    ptx::tma_load_4d(dst + 0 * TILE, &tm_v, bar, dv0, h, c * C, b);
-    ptx::tma_load_4d(dst + 1 * TILE, &tm_v, bar, dv0 + 64, h, c * C, b);
+    ptx::tma_load_4d(dst + 0 * TILE, &tm_v, bar, dv0, h, (cb + c) * C, b);
+    ptx::tma_load_4d(dst + 1 * TILE, &tm_v, bar, dv0 + 64, h, (cb + c) * C, b);
   };
 
   constexpr uint32_t ID_G = ptx::idesc_bf16_f32(128, 64);
@@ -287,13 +299,13 @@ __global__ void __launch_bounds__(NT, 1)
     float ga0 = 0.f, ga1 = 0.f, gb0 = 0.f, gb1 = 0.f;  // prefetched gates of the next chunk (worker warp 1)
     auto load_gates = [&](int c) {
       ga0 = ga1 = gb0 = gb1 = 0.f;
-      const int t0 = c * C;
+      const int t0 = (cb + c) * C;
       const int64_t gi = ((int64_t)b * p.T + t0) * p.H + h;
       if (t0 + lane < p.T) { ga0 = p.la[gi + (int64_t)lane * p.H]; gb0 = p.beta[gi + (int64_t)lane * p.H]; }
       if (t0 + lane + 32 < p.T) { ga1 = p.la[gi + (int64_t)(lane + 32) * p.H]; gb1 = p.beta[gi + (int64_t)(lane + 32) * p.H]; }
     };
     if (ww == 1) load_gates(0);
-    if (leader) {
+    if (leader && !virt && nch > 0) {
       issue_v(0);
       v_issued = 1;
       if (nch > 1) { issue_v(1); v_issued = 2; }
@@ -327,7 +339,7 @@ __global__ void __launch_bounds__(NT, 1)
         ptx::fence_proxy_async_smem();
         ptx::named_bar(3, 128);
         if (wt == 128) {
-          ptx::tma_store_4d(&tm_y, stage, dv0, h, c * C + piece * ROWS, b);
+          ptx::tma_store_4d(&tm_y, stage, dv0, h, (cb + c) * C + piece * ROWS, b);
           ptx::bulk_commit();
         }
       }
@@ -398,7 +410,7 @@ __global__ void __launch_bounds__(NT, 1)
         const int bb = e >> 8, r = (e >> 4) & 15, cc = e & 15;
         Ed[(bb * 16 + r) * 20 + cc] = cc <= r ? beta_s[16 * bb + cc] * __expf(g_s[16 * bb + r] - g_s[16 * bb + cc]) : 0.f;
       }
-      if (!gwait(B_V + pb, (uint32_t)(c >> 1) & 1u, leader, 1, NWORK)) break;
+      if (!virt && !gwait(B_V + pb, (uint32_t)(c >> 1) & 1u, leader, 1, NWORK)) break;
       if (!gwait(B_G, (uint32_t)c & 1u, leader, 1, NWORK)) break;
       if (leader) issued = false;
       ptx::tc_fence_after();
@@ -472,7 +484,7 @@ __global__ void __launch_bounds__(NT, 1)
       ptx::named_bar(1, NWORK);
       // W16(c-1) shares T16/TG16's space (needs R(c-1) done); A16[pb] was read by Yi(c-2).
       if (c > 0 && !gwait(B_R, (uint32_t)(c - 1) & 1u, leader, 1, NWORK)) break;
-      if (c >= 2 && !gwait(B_YF + pb, (uint32_t)((c - 2) >> 1) & 1u, leader, 1, NWORK)) break;
+      if (want_y && c >= 2 && !gwait(B_YF + pb, (uint32_t)((c - 2) >> 1) & 1u, leader, 1, NWORK)) break;
       if (!is_l) {
         uint8_t* arow = sm + AB + pb * TILE;
 #pragma unroll
@@ -504,7 +516,7 @@ __global__ void __launch_bounds__(NT, 1)
       }
       bool epi_ok = true;
       if (ww >= 4) {
-        if (c >= 1) epi_ok = epilogue(c - 1);  // overlaps the diagonal blocks and the merges
+        if (want_y && c >= 1) epi_ok = epilogue(c - 1);  // overlaps the diagonal blocks and the merges
       } else {
         ptx::named_bar(4, 128);  // D_b in L16 before the merges read it (warps 4-7 only)
         const uint32_t l16a = sb + L16, thi = sb + TW, tlo = sb + TLO, tg16a = sb + TW + TILE;
@@ -523,12 +535,14 @@ __global__ void __launch_bounds__(NT, 1)
         for (int k = 0; k < 4; ++k)
           ptx::mma_f16_ss(tmem + COL_W, at(D_MN16K, kq_o + k * 2048), at(D_K, TW + TILE + k * 32), ID_N64_AMN, k > 0);
         ptx::mma_commit(&bars[B_WU]);
+        if (!virt) {  // the transition block has v = 0, hence U = 0
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
-          ptx::mma_f16_ss(tmem + COL_U + 64 * pb, at(D_MN8K, v_o + k * 2048), at(D_K, TW + k * 32), ID_U_BF16, k > 0);
+          for (int k = 0; k < 4; ++k)
+            ptx::mma_f16_ss(tmem + COL_U + 64 * pb, at(D_MN8K, v_o + k * 2048), at(D_K, TW + k * 32), ID_U_BF16, k > 0);
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
-          ptx::mma_f16_ss(tmem + COL_U + 64 * pb, at(D_MN8K, v_o + k * 2048), at(D_K, TLO + k * 32), ID_U_BF16, 1);
+          for (int k = 0; k < 4; ++k)
+            ptx::mma_f16_ss(tmem + COL_U + 64 * pb, at(D_MN8K, v_o + k * 2048), at(D_K, TLO + k * 32), ID_U_BF16, 1);
+        }
         ptx::mma_commit(&bars[B_UU]);
         issued = true;
       }
@@ -560,10 +574,10 @@ __global__ void __launch_bounds__(NT, 1)
       if (leader) {
         issued = false;
         ptx::mbar_arrive(&bars[B_PREP]);
-        if (c + 2 < nch) { issue_v(c + 2); v_issued = c + 3; }  // V(c) consumed by U^T(c)
+        if (!virt && c + 2 < nch) { issue_v(c + 2); v_issued = c + 3; }  // V(c) consumed by U^T(c)
       }
     }
-    if (c == nch && nch > 0 && ww >= 4) epilogue(nch - 1);
+    if (want_y && c == nch && nch > 0 && ww >= 4) epilogue(nch - 1);
     if (wt == 128) ptx::bulk_wait0();
     if (*abort_flag && leader) {  // drain this thread's MMAs and V loads before the CTA exits
       if (issued) {
@@ -579,7 +593,16 @@ __global__ void __launch_bounds__(NT, 1)
     const bool leader = ct == 0;
     bool issued = false;
     {
-      const float* src = p.s0 ? p.s0 + ((int64_t)bh * p.DV + dv0 + ct) * D : nullptr;
+      // Initial state: the caller's S_0 (first segment), the combined state of the previous
+      // segments (later segments), or in state mode 0 (v block) / the identity (transition block).
+      const float* src = nullptr;
+      if (want_y) {
+        if (seg == 0) {
+          if (p.s0) src = p.s0 + ((int64_t)bh * p.DV + dv0 + ct) * D;
+        } else {
+          src = p.seg_s0 + ((int64_t)(bh * p.ws_stride + seg - 1) * (p.DV + D) + dv0 + ct) * D;
+        }
+      }
 #pragma unroll 1
       for (int c4 = 0; c4 < 4; ++c4) {
         float v[32];
@@ -587,6 +610,10 @@ __global__ void __launch_bounds__(NT, 1)
         for (int i = 0; i < 32; i += 4) {
           const float4 t4 = src ? *reinterpret_cast<const float4*>(src + c4 * 32 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
           v[i] = t4.x; v[i + 1] = t4.y; v[i + 2] = t4.z; v[i + 3] = t4.w;
+        }
+        if (virt) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = (c4 * 32 + i == ct) ? 1.f : 0.f;
         }
         ptx::tmem_st32(my + COL_S + c4 * 32, v);
       }
@@ -632,17 +659,19 @@ __global__ void __launch_bounds__(NT, 1)
       bool r_ok = true;
       if (leader) {  // R^T = U^T - S W^T ; Y = S (Gamma Q)^T
         ptx::tc_fence_after();
-        if (c >= 2)  // Y[pb] drained by the workers
+        if (want_y && c >= 2)  // Y[pb] drained by the workers
           r_ok = ptx::mbar_wait_abortable(&bars[B_YE + pb], (uint32_t)((c - 2) >> 1) & 1u, WAIT_LIMIT, abort_flag);
         if (r_ok) {
 #pragma unroll
-          for (int k = 0; k < 8; ++k)
+          for (int k = 0; k < 8; ++k)  // onto U^T; the transition block starts from U = 0
             ptx::mma_f16_ss(tmem + COL_U + 64 * pb, at(D_K, SR + (k >> 2) * 2 * TILE + (k & 3) * 32),
-                            at(D_K, TW + k * 2048), ID_N64_BMN_NEG, 1);
+                            at(D_K, TW + k * 2048), ID_N64_BMN_NEG, virt ? (k > 0) : 1);
+          if (want_y) {
 #pragma unroll
-          for (int k = 0; k < 8; ++k)
-            ptx::mma_f16_ss(tmem + COL_Y + 64 * pb, at(D_K, SR + (k >> 2) * 2 * TILE + (k & 3) * 32),
-                            at(D_K, kq_o + TILE + (k >> 2) * 2 * TILE + (k & 3) * 32), ID_N64, k > 0);
+            for (int k = 0; k < 8; ++k)
+              ptx::mma_f16_ss(tmem + COL_Y + 64 * pb, at(D_K, SR + (k >> 2) * 2 * TILE + (k & 3) * 32),
+                              at(D_K, kq_o + TILE + (k >> 2) * 2 * TILE + (k & 3) * 32), ID_N64, k > 0);
+          }
           ptx::mma_commit(&bars[B_R]);
           issued = true;
         }
@@ -678,19 +707,23 @@ __global__ void __launch_bounds__(NT, 1)
 #pragma unroll
         for (int k = 0; k < 4; ++k)
           ptx::mma_f16_ss(tmem + COL_S, at(D_K, SR + 2 * TILE + k * 32), at(D_MN16K, kq_o + k * 2048), ID_N128_BMN, 1);
+        if (want_y) {
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
-          ptx::mma_f16_ss(tmem + COL_Y + 64 * pb, at(D_K, SR + k * 32), at(D_K, AB + pb * TILE + k * 32), ID_N64, 1);
+          for (int k = 0; k < 4; ++k)
+            ptx::mma_f16_ss(tmem + COL_Y + 64 * pb, at(D_K, SR + k * 32), at(D_K, AB + pb * TILE + k * 32), ID_N64, 1);
+        }
         ptx::mma_commit(&bars[B_S]);
-        ptx::mma_commit(&bars[B_YF + pb]);
+        if (want_y) ptx::mma_commit(&bars[B_YF + pb]);
         issued = true;
       }
     }
     if (!*abort_flag && nch > 0 && gwait(B_S, (uint32_t)(nch - 1) & 1u, leader, 2, 128)) {
       if (leader) issued = false;
       ptx::tc_fence_after();
-      if (p.s_out != nullptr) {
-        float* dst = p.s_out + ((int64_t)bh * p.DV + dv0 + ct) * D;
+      float* dst = nullptr;
+      if (want_y && seg == p.nseg - 1 && p.s_out != nullptr) dst = p.s_out + ((int64_t)bh * p.DV + dv0 + ct) * D;
+      if (!want_y) dst = p.seg_out + ((int64_t)(bh * p.ws_stride + seg) * (p.DV + D) + dv0 + ct) * D;
+      if (dst != nullptr) {
 #pragma unroll 1
         for (int c4 = 0; c4 < 4; ++c4) {
           float v[32];
@@ -759,8 +792,14 @@ bool make_store_map(CUtensorMap* m, void* base, int64_t F, const gdn_prefill_arg
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+struct Segmentation {
+  int mode = 0, nseg = 1, seg_len = 0, ws_stride = 0;
+  const float* seg_s0 = nullptr;
+  float* seg_out = nullptr;
+};
+
 template <typename TOut>
-int launch(const gdn_prefill_args* a, cudaStream_t stream) {
+int launch(const gdn_prefill_args* a, const Segmentation& sg, cudaStream_t stream) {
   CUtensorMap mq, mk, mv, my;
   if (!make_map(&mq, a->q, a->DK, a, a->sq) || !make_map(&mk, a->k, a->DK, a, a->sk) ||
       !make_map(&mv, a->v, a->DV, a, a->sv) || !make_store_map<TOut>(&my, a->y, a->DV, a, a->sy))
@@ -772,12 +811,27 @@ int launch(const gdn_prefill_args* a, cudaStream_t stream) {
       return GDN_ERR_LAUNCH;
     attr_set = true;
   }
+  const int nch = (int)((a->T + C - 1) / C);
   Params p;
   p.beta = a->beta; p.la = a->la; p.s0 = a->s0; p.s_out = a->s_out; p.y = a->y; p.sy = a->sy;
   p.B = (int)a->B; p.T = (int)a->T; p.H = (int)a->H; p.DV = (int)a->DV;
-  const int64_t grid = a->B * a->H * (a->DV / D);
+  p.nv = (int)(a->DV / D);
+  p.mode = sg.mode;
+  p.ntiles = p.nv + (sg.mode == 1 ? 1 : 0);
+  p.nseg = sg.nseg;
+  p.seg_len = sg.seg_len > 0 ? sg.seg_len : nch;
+  p.seg_s0 = sg.seg_s0;
+  p.seg_out = sg.seg_out;
+  p.ws_stride = sg.ws_stride;
+  const int64_t grid = a->B * a->H * (int64_t)p.nseg * p.ntiles;
+  if (grid <= 0 || grid > 0x7fffffff) return GDN_ERR_SHAPE;
   kern<<<(unsigned)grid, NT, DYN, stream>>>(mq, mk, mv, my, p);
   return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+}
+
+template <typename TOut>
+int launch(const gdn_prefill_args* a, cudaStream_t stream) {
+  return launch<TOut>(a, Segmentation(), stream);
 }
 
 }  // namespace ws
@@ -793,6 +847,22 @@ bool gdn_chunk_ws_supported(const gdn_prefill_args* a) {
 
 int gdn_launch_chunk_ws(const gdn_prefill_args* a, cudaStream_t stream) {
   return a->out_dtype == GDN_DTYPE_BF16 ? gdn::ws::launch<__nv_bfloat16>(a, stream) : gdn::ws::launch<float>(a, stream);
+}
+
+// One pass of the segmented prefill.  mode 1: segments [0, nseg) write [N_s; M_s] to `ws`
+// (slots of `ws_stride` per (b, h)); mode 0: segment s >= 1 starts from the state stored at slot
+// s - 1 of `ws`, the last segment writes S_T.
+int gdn_launch_chunk_ws_segments(const gdn_prefill_args* a, int mode, int nseg, int seg_len, float* ws, int ws_stride,
+                                 cudaStream_t stream) {
+  gdn::ws::Segmentation sg;
+  sg.mode = mode;
+  sg.nseg = nseg;
+  sg.seg_len = seg_len;
+  sg.ws_stride = ws_stride;
+  sg.seg_s0 = ws;
+  sg.seg_out = ws;
+  return a->out_dtype == GDN_DTYPE_BF16 ? gdn::ws::launch<__nv_bfloat16>(a, sg, stream)
+                                        : gdn::ws::launch<float>(a, sg, stream);
 }
 
 namespace gdn {

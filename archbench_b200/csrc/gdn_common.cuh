@@ -64,3 +64,8 @@ bool gdn_chunk_ws_supported(const gdn_prefill_args* a);
 int gdn_launch_chunk_ws(const gdn_prefill_args* a, cudaStream_t stream);
 int gdn_chunk_ws_read_status(int* out, int reset);
 int gdn_launch_selftest_wait(long long max_cycles, cudaStream_t stream);
+int gdn_launch_chunk_ws_segments(const gdn_prefill_args* a, int mode, int nseg, int seg_len, float* ws, int ws_stride,
+                                 cudaStream_t stream);
+bool gdn_segmented_plan(const gdn_prefill_args* a, int sms, int* nseg, int* seg_len, size_t* bytes);
+int gdn_segmented_sms();
+int gdn_launch_segmented(const gdn_prefill_args* a, float* ws, size_t ws_bytes, int sms, cudaStream_t stream);

@@ -26,7 +26,8 @@ _PKG = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_PKG, "libgdn_b200.so")
 
 GDN_DTYPE_F32, GDN_DTYPE_BF16 = 0, 1
-IMPLS = {"auto": 0, "chunk": 1, "recurrent": 2}
+IMPLS = {"auto": 0, "chunk": 1, "recurrent": 2, "segmented": 3}
+IMPL_NAMES = {1: "chunk", 2: "recurrent", 3: "segmented"}
 _DT = {torch.float32: GDN_DTYPE_F32, torch.bfloat16: GDN_DTYPE_BF16}
 
 
@@ -52,6 +53,7 @@ class PrefillArgs(ctypes.Structure):
         ("sq", Strides), ("sk", Strides), ("su", Strides), ("sv", Strides), ("sy", Strides),
         ("B", ctypes.c_int64), ("T", ctypes.c_int64), ("H", ctypes.c_int64), ("DK", ctypes.c_int64), ("DV", ctypes.c_int64),
         ("in_dtype", ctypes.c_int32), ("out_dtype", ctypes.c_int32), ("impl", ctypes.c_int32), ("reserved", ctypes.c_int32),
+        ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_uint64),
     ]
 
 
@@ -169,7 +171,14 @@ def _prefill_impl(q, k, u, v, la, beta, s0, output_final_state: bool, out_dtype:
         B, T, H, DK, DV, _DT[in_dtype], _DT[out_dtype], IMPLS[impl], 0,
     )
     lib = load_library()
+    ws = None
     with torch.cuda.device(q.device):
+        if impl in ("auto", "segmented"):
+            need = ctypes.c_size_t(0)
+            _check(lib.gdn_prefill_workspace_bytes(ctypes.byref(a), ctypes.byref(need)))
+            if need.value > 0:  # scratch through torch's caching allocator; the library allocates nothing
+                ws = torch.empty(need.value, dtype=torch.uint8, device=q.device)
+                a.workspace, a.workspace_bytes = ws.data_ptr(), need.value
         _check(lib.gdn_prefill_fwd(ctypes.byref(a), ctypes.c_void_p(torch.cuda.current_stream(q.device).cuda_stream)))
     return y, s_out
 
@@ -264,6 +273,7 @@ def gdn_prefill(q, k, v, la, beta=None, u=None, initial_state=None, output_final
     """
     if impl not in IMPLS:
         raise ValueError(f"impl must be one of {sorted(IMPLS)}")
+    # (workspace for the segmented path is sized and allocated per call by _prefill_impl)
     y, s = _prefill_op(q, k, u, v, la, beta, initial_state, bool(output_final_state), _code(out_dtype, q.dtype if q.dtype in _DT else torch.float32), impl)
     return y, (s if output_final_state else None)
 
@@ -299,10 +309,16 @@ def selected_impl(q, k, v, la, beta=None, u=None, impl="auto") -> str:
         _tok_strides(q), _tok_strides(k), _tok_strides(u) if u is not None else Strides(0, 0, 0), _tok_strides(v),
         Strides(T * H * DV, H * DV, DV), B, T, H, DK, DV, _DT[in_dtype], _DT[in_dtype], IMPLS[impl], 0,
     )
-    r = load_library().gdn_prefill_select_impl(ctypes.byref(a))
+    lib = load_library()
+    if impl in ("auto", "segmented"):
+        need = ctypes.c_size_t(0)
+        _check(lib.gdn_prefill_workspace_bytes(ctypes.byref(a), ctypes.byref(need)))
+        if need.value > 0:  # the caller of gdn_prefill always supplies it
+            a.workspace, a.workspace_bytes = 0x100, need.value
+    r = lib.gdn_prefill_select_impl(ctypes.byref(a))
     if r < 0:
         _check(r)
-    return {1: "chunk", 2: "recurrent"}[r]
+    return IMPL_NAMES[r]
 
 
 def device_status(reset: bool = False) -> int:

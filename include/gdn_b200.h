@@ -34,7 +34,7 @@
 extern "C" {
 #endif
 
-#define GDN_B200_ABI_VERSION 1
+#define GDN_B200_ABI_VERSION 2
 
 typedef enum {
   GDN_OK = 0,
@@ -51,9 +51,11 @@ typedef enum {
 typedef enum { GDN_DTYPE_F32 = 0, GDN_DTYPE_BF16 = 1 } gdn_dtype;
 
 typedef enum {
-  GDN_IMPL_AUTO = 0,       /* chunked tensor-core kernel where it applies, else recurrent */
-  GDN_IMPL_CHUNK = 1,      /* chunkwise-parallel tcgen05/TMEM kernel (bf16 I/O, DK = DV = 128) */
-  GDN_IMPL_RECURRENT = 2   /* token-serial fp32 kernel (any supported dtype and head size) */
+  GDN_IMPL_AUTO = 0,       /* the fastest kernel that applies (see gdn_prefill_select_impl) */
+  GDN_IMPL_CHUNK = 1,      /* chunkwise tcgen05/TMEM kernel (bf16 I/O, DK = 128, DV a multiple of 128) */
+  GDN_IMPL_RECURRENT = 2,  /* token-serial fp32 kernel (any supported dtype and head size) */
+  GDN_IMPL_SEGMENTED = 3   /* chunk kernel split into sequence segments for few long sequences;
+                              needs the workspace gdn_prefill_workspace_bytes reports */
 } gdn_impl;
 
 /* Strides of one token tensor, in elements.  The last (feature) dimension has stride 1. */
@@ -87,6 +89,8 @@ typedef struct {
   int32_t out_dtype;  /* gdn_dtype of y */
   int32_t impl;       /* gdn_impl */
   int32_t reserved;
+  void* workspace;    /* device scratch for GDN_IMPL_SEGMENTED (16-byte aligned), or NULL */
+  uint64_t workspace_bytes;
 } gdn_prefill_args;
 
 int gdn_prefill_fwd(const gdn_prefill_args* args, void* stream);
@@ -118,9 +122,11 @@ typedef struct {
 int gdn_decode_step(const gdn_decode_args* args, void* stream);
 
 /*
- * Bytes of device workspace a prefill call with these arguments needs.  Every kernel in
- * this build keeps its working set on chip, so the answer is 0; the query exists so a
- * caller can size buffers without knowing which kernel runs.
+ * Bytes of device workspace the segmented path needs for these arguments (0 when it does not
+ * apply).  The segmented path is chosen for few (b, h) sequences with long T: phase A writes a
+ * (DV + 128) x 128 fp32 pair of segment states per (b, h, segment), phase B combines them, phase
+ * C reads them back.  Under GDN_IMPL_AUTO a call without enough workspace runs the single-pass
+ * chunk kernel instead; GDN_IMPL_SEGMENTED without it fails with GDN_ERR_SHAPE.
  */
 int gdn_prefill_workspace_bytes(const gdn_prefill_args* args, size_t* bytes);
 

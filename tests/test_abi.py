@@ -27,12 +27,12 @@ def test_library_exports_every_declared_symbol():
     lib = ops.load_library()
     for name in declared_functions():
         assert hasattr(lib, name), name
-    assert lib.gdn_abi_version() == 1
+    assert lib.gdn_abi_version() == 2
 
 
 def test_struct_layout_matches_header():
     # pointers 9*8, strides 5*24, sizes 5*8, ints 4*4
-    assert ctypes.sizeof(ops.PrefillArgs) == 9 * 8 + 5 * 24 + 5 * 8 + 4 * 4
+    assert ctypes.sizeof(ops.PrefillArgs) == 9 * 8 + 5 * 24 + 5 * 8 + 4 * 4 + 8 + 8
     assert ctypes.sizeof(ops.DecodeArgs) == 8 * 8 + 5 * 24 + 4 * 8 + 2 * 4
 
 
@@ -43,7 +43,7 @@ def fake_args(**kw):
     a = ops.PrefillArgs(
         0x10000, 0x20000, None, 0x30000, 0x40000, 0x50000, None, 0x60000, None,
         st, st, ops.Strides(0, 0, 0), ops.Strides(T * H * DV, H * DV, DV), ops.Strides(T * H * DV, H * DV, DV),
-        B, T, H, DK, DV, ops.GDN_DTYPE_BF16, ops.GDN_DTYPE_BF16, 0, 0,
+        B, T, H, DK, DV, ops.GDN_DTYPE_BF16, ops.GDN_DTYPE_BF16, 0, 0, None, 0,
     )
     for k, v in kw.items():
         setattr(a, k, v)
@@ -71,12 +71,25 @@ def test_recurrent_selected_for_fp32_and_small_heads():
     assert status(fake_args(in_dtype=ops.GDN_DTYPE_F32, out_dtype=ops.GDN_DTYPE_F32)) == 2
     assert status(fake_args(shape=(2, 64, 4, 64, 64))) == 2
     assert status(fake_args(shape=(2, 64, 4, 64, 64), impl=1)) == -5  # chunk forced, not covered
+    assert status(fake_args(impl=3)) == -5  # segmented forced where it does not apply
 
 
-def test_workspace_query_is_zero():
+def test_workspace_query():
+    lib = ops.load_library()
     n = ctypes.c_size_t(123)
-    assert ops.load_library().gdn_prefill_workspace_bytes(ctypes.byref(fake_args()), ctypes.byref(n)) == 0
+    # 64 (b, h) units on a 148-SM part: the single-pass kernel, no workspace
+    assert lib.gdn_prefill_workspace_bytes(ctypes.byref(fake_args()), ctypes.byref(n)) == 0
     assert n.value == 0
+    # one long sequence: segmented, (P - 1) slots of (DV + 128) x 128 fp32
+    a = fake_args(shape=(1, 4096, 2, 128, 128))
+    assert lib.gdn_prefill_workspace_bytes(ctypes.byref(a), ctypes.byref(n)) == 0
+    assert n.value > 0 and n.value % (256 * 128 * 4 * 2) == 0
+    assert status(a) == 1  # no workspace supplied: the single-pass chunk kernel
+    a.workspace, a.workspace_bytes = 0x100000, n.value
+    assert status(a) == 3
+    a.impl = 3
+    a.workspace_bytes = n.value - 1
+    assert status(a) == -2
 
 
 def test_status_strings():
