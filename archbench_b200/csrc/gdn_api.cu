@@ -108,6 +108,7 @@ const char* gdn_status_string(int s) {
     case GDN_ERR_DEVICE: return "the current device is not an sm_100 (B200) GPU";
     case GDN_ERR_LAUNCH: return "CUDA kernel launch failed";
     case GDN_ERR_TIMEOUT: return "a bounded device-side wait gave up";
+    case GDN_ERR_WORKSPACE: return "the problem needs more segment scratch than GDN_STATIC_WORKSPACE_BYTES";
     default: return "unknown gdn_status";
   }
 }
@@ -165,6 +166,15 @@ int gdn_prefill_fwd(const gdn_prefill_args* a, void* stream) {
     return gdn_launch_segmented(a, static_cast<float*>(a->workspace), (size_t)a->workspace_bytes, plan_sms(), s);
   if (impl == GDN_IMPL_CHUNK) return gdn_launch_chunk_sm100(a, s);
   return gdn_launch_recurrent(a, a->s0, a->s_out, s);
+}
+
+int gdn_prefill_fwd_static_workspace(const gdn_prefill_args* a, void* stream) {
+  int st = validate(a);
+  if (st != GDN_OK) return st;
+  st = check_device();
+  if (st != GDN_OK) return st;
+  if (a->T == 0) return GDN_ERR_UNSUPPORTED;
+  return gdn_launch_segmented_static(a, plan_sms(), static_cast<cudaStream_t>(stream));
 }
 
 int gdn_decode_step(const gdn_decode_args* d, void* stream) {

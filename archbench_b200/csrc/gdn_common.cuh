@@ -69,3 +69,4 @@ int gdn_launch_chunk_ws_segments(const gdn_prefill_args* a, int mode, int nseg, 
 bool gdn_segmented_plan(const gdn_prefill_args* a, int sms, int* nseg, int* seg_len, size_t* bytes);
 int gdn_segmented_sms();
 int gdn_launch_segmented(const gdn_prefill_args* a, float* ws, size_t ws_bytes, int sms, cudaStream_t stream);
+int gdn_launch_segmented_static(const gdn_prefill_args* a, int sms, cudaStream_t stream);

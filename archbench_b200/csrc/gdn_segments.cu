@@ -11,6 +11,8 @@
 // Workspace (caller-allocated): B*H*(P-1) slots of (DV + 128) x 128 fp32.
 // The reference computes the same recurrence sequentially (archbench/layers/nsgdn.py:408-417,
 // fla's chunk_gated_delta_rule_fwd_h walks chunks in order); this split is this build's own.
+#include <mutex>
+
 #include "gdn_common.cuh"
 
 namespace gdn {
@@ -67,29 +69,34 @@ int sm_count() {
 }  // namespace gdn
 
 // Segment plan for these arguments; false when the single-pass kernel is the better choice.
-bool gdn_segmented_plan(const gdn_prefill_args* a, int sms, int* nseg, int* seg_len, size_t* bytes) {
+// `max_bytes` (0 = no limit) caps the workspace by using fewer, longer segments.
+static bool plan(const gdn_prefill_args* a, int sms, size_t max_bytes, int* nseg, int* seg_len, size_t* bytes) {
   if (!gdn_chunk_supported(a) || a->u != nullptr) return false;
   const int64_t nch = (a->T + 63) / 64;
   const int64_t units = a->B * a->H * (a->DV / 128);
   if (sms <= 0 || units * 4 > sms || nch < 8) return false;
   int64_t P = sms / units;
   if (P > nch / 2) P = nch / 2;
+  const size_t slot = (size_t)(a->B * a->H) * (size_t)(a->DV + 128) * 128 * sizeof(float);
+  if (max_bytes > 0 && P > 1 && (size_t)(P - 1) * slot > max_bytes) P = (int64_t)(max_bytes / slot) + 1;
   if (P < 2) return false;
   const int64_t L = (nch + P - 1) / P;
   P = (nch + L - 1) / L;
   if (P < 2) return false;
   *nseg = (int)P;
   *seg_len = (int)L;
-  *bytes = (size_t)(a->B * a->H * (P - 1)) * (size_t)(a->DV + 128) * 128 * sizeof(float);
+  *bytes = (size_t)(P - 1) * slot;
   return true;
+}
+
+bool gdn_segmented_plan(const gdn_prefill_args* a, int sms, int* nseg, int* seg_len, size_t* bytes) {
+  return plan(a, sms, 0, nseg, seg_len, bytes);
 }
 
 int gdn_segmented_sms() { return gdn::seg::sm_count(); }
 
-int gdn_launch_segmented(const gdn_prefill_args* a, float* ws, size_t ws_bytes, int sms, cudaStream_t stream) {
-  int P = 0, L = 0;
-  size_t need = 0;
-  if (!gdn_segmented_plan(a, sms, &P, &L, &need)) return GDN_ERR_UNSUPPORTED;
+static int launch_plan(const gdn_prefill_args* a, float* ws, size_t ws_bytes, int P, int L, size_t need,
+                       cudaStream_t stream) {
   if (ws == nullptr || ws_bytes < need) return GDN_ERR_SHAPE;
   if ((uintptr_t)ws % 16) return GDN_ERR_ALIGN;
   int st = gdn_launch_chunk_ws_segments(a, 1, P - 1, L, ws, P - 1, stream);
@@ -99,4 +106,61 @@ int gdn_launch_segmented(const gdn_prefill_args* a, float* ws, size_t ws_bytes, 
   gdn::seg::combine_kernel<<<(unsigned)grid, gdn::seg::D, 0, stream>>>(ws, a->s0, (int)a->DV, P - 1, rblocks);
   if (cudaGetLastError() != cudaSuccess) return GDN_ERR_LAUNCH;
   return gdn_launch_chunk_ws_segments(a, 0, P, L, ws, P - 1, stream);
+}
+
+int gdn_launch_segmented(const gdn_prefill_args* a, float* ws, size_t ws_bytes, int sms, cudaStream_t stream) {
+  int P = 0, L = 0;
+  size_t need = 0;
+  if (!plan(a, sms, 0, &P, &L, &need)) return GDN_ERR_UNSUPPORTED;
+  return launch_plan(a, ws, ws_bytes, P, L, need, stream);
+}
+
+// ---- the same prefill without any allocation --------------------------------------------------
+// Callers that cannot allocate device memory when they call us -- a plugin whose host framework
+// owns all device memory and hands over only input and output pointers, or a serving loop that
+// forbids cudaMalloc after start-up because it synchronises the device and breaks a pre-planned
+// memory pool -- get the segment workspace from this fixed array instead.  It is reserved on every
+// GPU that loads the library and held until the process exits.  In host code `g_static_ws` only
+// names the symbol; its device address comes from cudaGetSymbolAddress, looked up once per device
+// with that device current, on the first call there.
+static __device__ __align__(256) float g_static_ws[GDN_STATIC_WORKSPACE_BYTES / sizeof(float)];
+
+namespace {
+std::mutex g_static_ws_mu;
+float* g_static_ws_ptr[64] = {};
+}  // namespace
+
+static float* static_ws_address(int* status) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    *status = GDN_ERR_DEVICE;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(g_static_ws_mu);
+  if (g_static_ws_ptr[dev] == nullptr) {
+    void* ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_static_ws);
+    if (e != cudaSuccess || ptr == nullptr) {
+      *status = GDN_ERR_LAUNCH;
+      return nullptr;
+    }
+    g_static_ws_ptr[dev] = static_cast<float*>(ptr);
+  }
+  return g_static_ws_ptr[dev];
+}
+
+// Segmented prefill with the workspace in g_static_ws: the plan uses fewer, longer segments when
+// the usual one would need more than GDN_STATIC_WORKSPACE_BYTES.  Nothing in the workspace has
+// to start at zero (phase A writes every slot before phase B reads it).
+int gdn_launch_segmented_static(const gdn_prefill_args* a, int sms, cudaStream_t stream) {
+  int P = 0, L = 0;
+  size_t need = 0;
+  if (!plan(a, sms, 0, &P, &L, &need)) return GDN_ERR_UNSUPPORTED;
+  if (need > GDN_STATIC_WORKSPACE_BYTES &&
+      (!plan(a, sms, GDN_STATIC_WORKSPACE_BYTES, &P, &L, &need) || need > GDN_STATIC_WORKSPACE_BYTES))
+    return GDN_ERR_WORKSPACE;
+  int st = GDN_OK;
+  float* ws = static_ws_address(&st);
+  if (ws == nullptr) return st;
+  return launch_plan(a, ws, GDN_STATIC_WORKSPACE_BYTES, P, L, need, stream);
 }

@@ -77,6 +77,7 @@ SYMBOLS = {
     "gdn_prefill_select_impl": ([ctypes.POINTER(PrefillArgs)], ctypes.c_int),
     "gdn_device_status": ([ctypes.POINTER(ctypes.c_int), ctypes.c_int], ctypes.c_int),
     "gdn_selftest_bounded_wait": ([ctypes.c_longlong, ctypes.c_void_p], ctypes.c_int),
+    "gdn_prefill_fwd_static_workspace": ([ctypes.POINTER(PrefillArgs), ctypes.c_void_p], ctypes.c_int),
     "gdn_status_string": ([ctypes.c_int], ctypes.c_char_p),
     "gdn_abi_version": ([], ctypes.c_int),
 }
@@ -138,7 +139,15 @@ def _check_cuda(*ts):
             raise ValueError("archbench_b200 ops run on CUDA tensors only (no CPU path)")
 
 
-def _prefill_impl(q, k, u, v, la, beta, s0, output_final_state: bool, out_dtype: torch.dtype, impl: str):
+def prefill_args(q, k, v, la, beta=None, u=None, initial_state=None, output_final_state=False, out_dtype=None, impl="auto"):
+    """Build the C-ABI argument block for a prefill: returns (PrefillArgs, y, S_T or None, keep),
+    with y and S_T freshly allocated and `keep` holding the (possibly converted) inputs alive for
+    as long as the block is used.  For callers that drive the C entry points directly."""
+    out_dtype = q.dtype if out_dtype is None else out_dtype
+    return _prepare(q, k, u, v, la, beta, initial_state, bool(output_final_state), out_dtype, impl)
+
+
+def _prepare(q, k, u, v, la, beta, s0, output_final_state: bool, out_dtype: torch.dtype, impl: str):
     _check_cuda(q, k, u, v, la, beta, s0)
     in_dtype = torch.bfloat16 if q.dtype == torch.bfloat16 else torch.float32
     q, k, v = (_prep_token(t, n, in_dtype) for t, n in ((q, "q"), (k, "k"), (v, "v")))
@@ -170,6 +179,11 @@ def _prefill_impl(q, k, u, v, la, beta, s0, output_final_state: bool, out_dtype:
         _tok_strides(q), _tok_strides(k), _tok_strides(u) if u is not None else Strides(0, 0, 0), _tok_strides(v), _tok_strides(y),
         B, T, H, DK, DV, _DT[in_dtype], _DT[out_dtype], IMPLS[impl], 0,
     )
+    return a, y, s_out, (q, k, u, v, la, beta, s0)
+
+
+def _prefill_impl(q, k, u, v, la, beta, s0, output_final_state: bool, out_dtype: torch.dtype, impl: str):
+    a, y, s_out, _keep = _prepare(q, k, u, v, la, beta, s0, output_final_state, out_dtype, impl)
     lib = load_library()
     ws = None
     with torch.cuda.device(q.device):

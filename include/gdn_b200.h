@@ -45,7 +45,8 @@ typedef enum {
   GDN_ERR_UNSUPPORTED = -5,  /* valid request that no kernel of this build implements */
   GDN_ERR_DEVICE = -6,       /* current device is not an sm_100 GPU */
   GDN_ERR_LAUNCH = -7,       /* the CUDA launch itself failed */
-  GDN_ERR_TIMEOUT = -8       /* a bounded device-side wait gave up (kernel reported it) */
+  GDN_ERR_TIMEOUT = -8,      /* a bounded device-side wait gave up (kernel reported it) */
+  GDN_ERR_WORKSPACE = -9     /* the problem needs more scratch than GDN_STATIC_WORKSPACE_BYTES */
 } gdn_status;
 
 typedef enum { GDN_DTYPE_F32 = 0, GDN_DTYPE_BF16 = 1 } gdn_dtype;
@@ -129,6 +130,26 @@ int gdn_decode_step(const gdn_decode_args* args, void* stream);
  * chunk kernel instead; GDN_IMPL_SEGMENTED without it fails with GDN_ERR_SHAPE.
  */
 int gdn_prefill_workspace_bytes(const gdn_prefill_args* args, size_t* bytes);
+
+/*
+ * Segmented prefill that allocates nothing.  It has no counterpart in the reference.
+ *
+ * For callers that cannot allocate device memory when they call: a plugin whose host framework
+ * owns all device memory and passes only input and output pointers, or a serving loop that
+ * forbids cudaMalloc after start-up (it synchronises the device and breaks a pre-planned pool).
+ * Same computation as gdn_prefill_fwd's segmented path (few, long sequences), with the segment
+ * workspace taken from an array of GDN_STATIC_WORKSPACE_BYTES that the library reserves on every
+ * GPU that loads it and holds until the process exits; args->impl, args->workspace and
+ * args->workspace_bytes are ignored.  When the usual segmentation would need more, fewer and
+ * longer segments are used; if none fits, the call fails with GDN_ERR_WORKSPACE.  Arguments the
+ * segmented path does not serve (many sequences, short T, u given) fail with GDN_ERR_UNSUPPORTED.
+ * Calls no cudaMalloc, cudaFree or allocating routine.  The first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress); make that first call before any stream capture.
+ * Every call shares the one array and leaves its contents behind: calls that overlap on the GPU
+ * (other streams, other threads) race on it and must be serialised by the caller.
+ */
+#define GDN_STATIC_WORKSPACE_BYTES (16u << 20)
+int gdn_prefill_fwd_static_workspace(const gdn_prefill_args* args, void* stream);
 
 /* Which kernel a prefill with these arguments runs (GDN_IMPL_CHUNK or _RECURRENT), or a
  * negative gdn_status if the arguments are invalid.  Launches nothing. */
