@@ -28,6 +28,7 @@ from __future__ import annotations
 import argparse
 import json
 import os
+import re
 import statistics
 import subprocess
 import sys
@@ -48,6 +49,16 @@ from archbench_b200.workloads import (  # noqa: E402
 )
 
 METRIC = "GDN prefill tok/s/GPU (T=4096,d=128), decode tok/s; % roofline at 1/2/4/8 GPU"
+
+
+def profiled_traffic(summary):
+    """DRAM bytes (read + write) per launch from one committed ncu capture of the kernel."""
+    try:
+        with open(os.path.join(ROOT, "profiles", summary)) as f:
+            m = re.search(r"^traffic_bytes_per_launch:\s*(\d+)", f.read(), re.M)
+        return int(m.group(1)) if m else None
+    except OSError:
+        return None
 
 
 def peaks():
@@ -203,7 +214,9 @@ def bench_prefill(args, rank, world):
         "kernel": sel,
         "roofline": {
             "bound": "hbm", "achieved": achieved_gbs, "peak": hbm, "unit": "GB/s", "frac": achieved_gbs / hbm,
-            "traffic": None, "peak_source": src, "algorithmic_bytes_per_launch": alg_bytes,
+            "traffic": profiled_traffic("ws_kernel_cfg1.md") if sel == "chunk" else None,
+            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, profiles/ws_kernel_cfg1.md",
+            "peak_source": src, "algorithmic_bytes_per_launch": alg_bytes,
             "tensor": {"achieved_tflops": alg_flops / per_launch / 1e12, "peak_tflops": tflops,
                        "frac": alg_flops / per_launch / 1e12 / tflops, "algorithmic_flops_per_launch": alg_flops},
         },
