@@ -51,7 +51,7 @@ int validate(const gdn_prefill_args* a) {
   if (a->B * a->H * a->DV > (1LL << 31)) return GDN_ERR_SHAPE;
   const int es = dtype_size(a->in_dtype);
   if (!es || !dtype_size(a->out_dtype)) return GDN_ERR_DTYPE;
-  if (a->impl < GDN_IMPL_AUTO || a->impl > GDN_IMPL_SEGMENTED) return GDN_ERR_UNSUPPORTED;
+  if (a->impl < GDN_IMPL_AUTO || a->impl > GDN_IMPL_CHUNK_SINGLE) return GDN_ERR_UNSUPPORTED;
   // The recurrent kernel reads DK/32 consecutive elements per lane as one vector.
   const int vec = (int)(a->DK / 32) * es;
   const int vb = vec >= 16 ? 16 : vec;
@@ -73,6 +73,12 @@ int plan_sms() {
   return n > 0 ? n : 148;
 }
 
+// The chunk variant for these arguments: the two-CTA cluster kernel where it applies (DV = 128,
+// u = beta k), else the single-CTA kernel.
+int chunk_variant(const gdn_prefill_args* a) {
+  return (a->u == nullptr && gdn_chunk_pair_supported(a)) ? (int)GDN_IMPL_CHUNK_CLUSTER : (int)GDN_IMPL_CHUNK_SINGLE;
+}
+
 int select_impl(const gdn_prefill_args* a) {
   const bool chunk_ok = gdn_chunk_supported(a);
   int P = 0, L = 0;
@@ -80,14 +86,18 @@ int select_impl(const gdn_prefill_args* a) {
   const bool seg_ok = chunk_ok && gdn_segmented_plan(a, plan_sms(), &P, &L, &need);
   const bool ws_ok = seg_ok && a->workspace != nullptr && a->workspace_bytes >= need;
   switch (a->impl) {
-    case GDN_IMPL_CHUNK: return chunk_ok ? (int)GDN_IMPL_CHUNK : (int)GDN_ERR_UNSUPPORTED;
+    case GDN_IMPL_CHUNK: return chunk_ok ? chunk_variant(a) : (int)GDN_ERR_UNSUPPORTED;
+    case GDN_IMPL_CHUNK_CLUSTER:
+      return chunk_ok && chunk_variant(a) == GDN_IMPL_CHUNK_CLUSTER ? (int)GDN_IMPL_CHUNK_CLUSTER
+                                                                     : (int)GDN_ERR_UNSUPPORTED;
+    case GDN_IMPL_CHUNK_SINGLE: return chunk_ok ? (int)GDN_IMPL_CHUNK_SINGLE : (int)GDN_ERR_UNSUPPORTED;
     case GDN_IMPL_RECURRENT: return (int)GDN_IMPL_RECURRENT;
     case GDN_IMPL_SEGMENTED:
       if (!seg_ok) return (int)GDN_ERR_UNSUPPORTED;
       return ws_ok ? (int)GDN_IMPL_SEGMENTED : (int)GDN_ERR_SHAPE;
     default:
       if (ws_ok) return (int)GDN_IMPL_SEGMENTED;
-      return chunk_ok ? (int)GDN_IMPL_CHUNK : (int)GDN_IMPL_RECURRENT;
+      return chunk_ok ? chunk_variant(a) : (int)GDN_IMPL_RECURRENT;
   }
 }
 
@@ -117,7 +127,13 @@ int gdn_device_status(int* status, int reset) {
   if (!status) return GDN_ERR_NULL;
   int st = check_device();
   if (st != GDN_OK) return st;
-  return gdn_chunk_read_status(status, reset);
+  int single = 0, pair = 0;
+  st = gdn_chunk_read_status(&single, reset);
+  if (st != GDN_OK) return st;
+  st = gdn_chunk_pair_read_status(&pair, reset);
+  if (st != GDN_OK) return st;
+  *status = single != 0 ? single : pair;
+  return GDN_OK;
 }
 
 int gdn_selftest_bounded_wait(long long max_cycles, void* stream) {
@@ -133,7 +149,7 @@ int gdn_prefill_workspace_bytes(const gdn_prefill_args* a, size_t* bytes) {
   *bytes = 0;
   int P = 0, L = 0;
   size_t need = 0;
-  if (a->impl != GDN_IMPL_CHUNK && a->impl != GDN_IMPL_RECURRENT && a->T > 0 &&
+  if ((a->impl == GDN_IMPL_AUTO || a->impl == GDN_IMPL_SEGMENTED) && a->T > 0 &&
       gdn_segmented_plan(a, plan_sms(), &P, &L, &need))
     *bytes = need;
   return GDN_OK;
@@ -164,7 +180,8 @@ int gdn_prefill_fwd(const gdn_prefill_args* a, void* stream) {
   if (impl < 0) return impl;
   if (impl == GDN_IMPL_SEGMENTED)
     return gdn_launch_segmented(a, static_cast<float*>(a->workspace), (size_t)a->workspace_bytes, plan_sms(), s);
-  if (impl == GDN_IMPL_CHUNK) return gdn_launch_chunk_sm100(a, s);
+  if (impl == GDN_IMPL_CHUNK_CLUSTER) return gdn_launch_chunk_pair(a, 1, 0, nullptr, 0, s);
+  if (impl == GDN_IMPL_CHUNK_SINGLE) return gdn_launch_chunk_sm100(a, s);
   return gdn_launch_recurrent(a, a->s0, a->s_out, s);
 }
 

@@ -1,0 +1,784 @@
+// Cluster-pair chunkwise gated delta rule (u = beta k) on tcgen05 / TMEM, sm_100a.
+//
+// Same mathematics as gdn_chunk_ws_sm100.cu (the WY form of archbench/layers/nsgdn.py:408-417,
+// derivation as in nsgdn.py:240-249).  One cluster of two CTAs per (b, h) sequence, on two SMs,
+// so that a batch of few sequences still covers most of the GPU and the state recurrence does
+// not share its SM with the state-independent work:
+//
+//   prep CTA (rank 1)   two chunks in flight (warps 0-3: even chunks, warps 4-7: odd chunks):
+//                       G = [K;Q] K^T (bf16 operands as loaded), gates and decay tables, the rows
+//                       of L and A, T = (I + L)^-1 (fp32 16x16 diagonal blocks, fp16 mma.sync
+//                       block columns) and T Gamma.  A, T and T Gamma (fp16, 24 KB per chunk) go
+//                       straight into a product slot in the state CTA's shared memory.
+//   state CTA (rank 0)  chain (warps 0-3): U^T = V^T T^T, S -> fp16, R^T = U^T - S W^T,
+//                       Y = S (Gamma Q)^T, S <- gamma_C S + (R diag w)^T K, Y += R^T A^T.  The
+//                       fp16 copies of S, R and R diag(w) stay in tensor memory as the A operands
+//                       of their MMAs; the commits that the chain waits on cover only the MMAs on
+//                       its critical path (R before Y, S before the intra-chunk part of Y).
+//                       convert (warps 4-7): gates, K / Gamma Q / V -> fp16 in place,
+//                       W^T = K^T (T Gamma)^T and W -> fp16.
+//                       output (warps 8-11): Y -> y through a staging tile and TMA stores.
+//
+// Handoff: prep pipeline p writes its chunk into slot p with st.shared::cluster, fences the
+// writes for the async proxy and arrives (release, cluster scope) on the slot's full barrier in
+// the state CTA; the state CTA's chain hands the slot back by arriving on the pipeline's empty
+// barrier once the last MMA reading it has completed.  The prep CTA loads each chunk's k and q
+// tiles with TMA and pulls its v tile into L2, so the state CTA's own tile loads (issued as soon
+// as the chunk two back has released their buffers) are L2 hits.
+//
+// Every mbarrier wait is bounded and abortable.  An abort raised in either CTA is copied into the
+// other; both drain their own MMAs and tile loads, and the two CTAs leave through one cluster
+// barrier, so neither exits while the other may still write into its shared memory.
+#include "gdn_tiles.cuh"
+
+namespace gdn {
+namespace pair {
+
+using namespace gdn::tiles;
+
+constexpr int NT = 384;
+constexpr long long WAIT_LIMIT = 4000000000LL;  // ~2 s of SM clocks
+
+constexpr uint32_t KQ_BYTES = 4 * TILE;  // [K0][Q0][K1][Q1]: features 0-63 and 64-127 of k and q
+constexpr uint32_t V_BYTES = 2 * TILE;   // [V0][V1]
+constexpr uint32_t PS_BYTES = 3 * TILE;  // product slot: [A16][T16][TG16]
+
+// State CTA shared-memory map (bytes from a 1024-aligned base).
+constexpr uint32_t S_KQ = 0;                       // 2 x KQ: bf16 as loaded -> fp16 K, Gamma Q in place
+constexpr uint32_t S_V = S_KQ + 2 * KQ_BYTES;      // 2 x V: bf16 -> fp16 in place
+constexpr uint32_t S_W = S_V + 2 * V_BYTES;        // W16: DK rows x 64 tokens
+constexpr uint32_t S_PS = S_W + 2 * TILE;          // 2 product slots, written by the prep CTA
+constexpr uint32_t S_YS = S_PS + 2 * PS_BYTES;     // y staging tile
+constexpr uint32_t S_GS = S_YS + TILE;             // 2 gate slots: gamma[64], w[64], gamma_C
+constexpr uint32_t GSLOT = 3 * C;                  // floats per gate slot
+constexpr uint32_t S_BARS = S_GS + 2 * GSLOT * 4;
+constexpr uint32_t S_NBARS = 16;
+
+// Prep CTA shared-memory map: pipeline p at p * P_STRIDE.
+constexpr uint32_t P_KQ = 0;                                  // KQ tile set, bf16 as loaded
+constexpr uint32_t P_ST = P_KQ + KQ_BYTES;                    // staging [A16][T16][TG16]
+constexpr uint32_t P_L16 = P_ST + PS_BYTES;                   // 64 rows x LD16 bytes (diagonal blocks hold D_b)
+constexpr uint32_t P_LDIAG = P_L16 + 64 * LD16;               // 4 x 16 x LDG floats
+constexpr uint32_t P_EXPT = P_LDIAG + 4 * 16 * LDG * 4;       // decay tables: 64 + 4x64 + 4x16x20 floats
+constexpr uint32_t P_GS = P_EXPT + (64 + 4 * 64 + 4 * 16 * 20) * 4;  // beta[64], g[64], gamma[64]
+constexpr uint32_t P_STRIDE = ((P_GS + 3 * C * 4) + 1023) / 1024 * 1024;
+constexpr uint32_t P_BARS = 2 * P_STRIDE;
+constexpr uint32_t P_NBARS = 8;
+
+constexpr uint32_t cmax(uint32_t a, uint32_t b) { return a > b ? a : b; }
+constexpr uint32_t CTRL = (cmax(S_BARS + S_NBARS * 8, P_BARS + P_NBARS * 8) + 15) / 16 * 16;  // tmem, abort, loads
+constexpr uint32_t TOTAL = CTRL + 16;
+constexpr uint32_t DYN = TOTAL + 1024;
+static_assert(DYN <= 232448, "shared memory budget");
+static_assert(S_V % 1024 == 0 && S_W % 1024 == 0 && S_PS % 1024 == 0, "swizzled tiles need 1 KB alignment");
+static_assert(P_STRIDE % 1024 == 0 && P_ST % 1024 == 0, "swizzled tiles need 1 KB alignment");
+
+// TMEM columns of the state CTA (all 512) and of the prep CTA (128: G of each pipeline).  S16, R16
+// and RW16 hold two fp16 values per column.
+constexpr uint32_t COL_S = 0, COL_S16 = 128, COL_U = 192, COL_R16 = 256, COL_RW16 = 288, COL_Y = 320, COL_W = 448;
+
+enum SBar { SB_PF = 0, SB_KQR = 2, SB_KQF = 4, SB_WM = 6, SB_W16R = 7, SB_R = 8, SB_S = 9, SB_YF = 10, SB_YE = 12, SB_DRAIN = 14 };
+enum PBar { PB_KQF = 0, PB_G = 2, PB_PE = 4, PB_DRAIN = 6 };
+
+struct Params {
+  const float* beta;
+  const float* la;
+  const float* s0;
+  float* s_out;
+  int B, T, H;
+  // Segments: cluster (b, h, seg) runs chunks [seg * seg_len, (seg + 1) * seg_len); segment s >= 1
+  // starts from the state at slot (bh, s - 1) of seg_s0 ((DV + 128) x 128 floats per slot).
+  int nseg, seg_len;
+  const float* seg_s0;
+  int ws_stride;
+};
+
+__device__ int g_status = 0;
+
+__device__ __forceinline__ void cumsum_gates(float la0, float la1, float& g0, float& g1, float& gC) {
+  const int lane = threadIdx.x & 31;
+  float a0 = la0, a1 = la1;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float n0 = __shfl_up_sync(0xffffffffu, a0, o);
+    const float n1 = __shfl_up_sync(0xffffffffu, a1, o);
+    if (lane >= o) {
+      a0 += n0;
+      a1 += n1;
+    }
+  }
+  a1 += __shfl_sync(0xffffffffu, a0, 31);
+  gC = __shfl_sync(0xffffffffu, a1, 31);
+  g0 = a0;
+  g1 = a1;
+}
+
+template <typename TOut>
+__global__ void __launch_bounds__(NT, 1)
+    pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_y, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sb = ptx::smem_u32(sm);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t rank = ptx::cluster_ctarank();
+  const int rest = blockIdx.x >> 1;
+  const int seg = rest % p.nseg, bh = rest / p.nseg;
+  const int b = bh / p.H, h = bh % p.H;
+  const int cb = seg * p.seg_len;  // first chunk of this cluster's segment
+  const int nch = max(0, min((p.T + C - 1) / C - cb, p.seg_len));
+
+  uint64_t* sbar = reinterpret_cast<uint64_t*>(sm + S_BARS);
+  uint64_t* pbar = reinterpret_cast<uint64_t*>(sm + P_BARS);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + CTRL);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + CTRL + 4);
+  volatile int* loads_issued = reinterpret_cast<volatile int*>(sm + CTRL + 8);
+  const uint32_t peer_abort = ptx::mapa_shared(sb + CTRL + 4, rank ^ 1u);
+  // Abort here and in the other CTA of the cluster (idempotent).
+  auto raise_abort = [&]() {
+    *abort_flag = 1;
+    ptx::st_cluster_u32(peer_abort, 1u);
+  };
+
+  const uint32_t tmem_cols = rank == 0 ? 512u : 128u;
+  if (warp == 0) {
+    ptx::tmem_alloc(tmem_slot, tmem_cols);
+    ptx::tmem_relinquish();
+  }
+  if (tid == 32) {
+    if (rank == 0) {
+      for (int i = 0; i < (int)S_NBARS; ++i) ptx::mbar_init(&sbar[i], (i == SB_YE || i == SB_YE + 1) ? 4 : 1);
+      ptx::prefetch_tensormap(&tm_y);
+    } else {
+      for (int i = 0; i < (int)P_NBARS; ++i) ptx::mbar_init(&pbar[i], 1);
+    }
+    ptx::prefetch_tensormap(&tm_q);
+    ptx::prefetch_tensormap(&tm_k);
+    ptx::prefetch_tensormap(&tm_v);
+    *abort_flag = 0;
+    *loads_issued = 0;
+    ptx::fence_mbar_init();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::cluster_sync();  // both CTAs' barriers exist before any remote arrive
+  ptx::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t my = tmem + ((uint32_t)((warp & 3) * 32) << 16);  // this warp's TMEM lane quarter
+  const int row = tid & 127;                                         // TMEM lane of this thread
+
+  const uint64_t D_K = ptx::sdesc_sw128(sb, 16, 1024);            // K-major operands
+  const uint64_t D_MN16K = ptx::sdesc_sw128(sb, 2 * TILE, 1024);  // MN-major, 64-blocks 16 KB apart
+  const uint64_t D_MN8K = ptx::sdesc_sw128(sb, TILE, 1024);       // MN-major, 64-blocks 8 KB apart
+  auto at = [](uint64_t tmpl, uint32_t off) { return tmpl + (uint64_t)(off >> 4); };
+  constexpr uint32_t ID_G = ptx::idesc_bf16_f32(128, 64);
+  constexpr uint32_t ID_N64 = ptx::idesc_f16_f32(128, 64, false, false, false);
+  constexpr uint32_t ID_N64_AMN = ptx::idesc_f16_f32(128, 64, true, false, false);
+  constexpr uint32_t ID_N64_BMN_NEG = ptx::idesc_f16_f32(128, 64, false, true, true);
+  constexpr uint32_t ID_N128_BMN = ptx::idesc_f16_f32(128, 128, false, true, false);
+
+  // la and beta of 64 tokens, two per lane (zero past the end of the sequence).
+  auto load_gates = [&](int c, float& la0, float& la1, float& be0, float& be1) {
+    la0 = la1 = be0 = be1 = 0.f;
+    const int t0 = (cb + c) * C;
+    const int64_t gi = ((int64_t)b * p.T + t0) * p.H + h;
+    if (t0 + lane < p.T) { la0 = p.la[gi + (int64_t)lane * p.H]; be0 = p.beta[gi + (int64_t)lane * p.H]; }
+    if (t0 + lane + 32 < p.T) { la1 = p.la[gi + (int64_t)(lane + 32) * p.H]; be1 = p.beta[gi + (int64_t)(lane + 32) * p.H]; }
+  };
+  auto issue_kq = [&](uint8_t* dst, uint64_t* bar, int c) {  // the caller has set the barrier's byte count
+    const int t0 = (cb + c) * C;
+    ptx::tma_load_4d(dst + 0 * TILE, &tm_k, bar, 0, h, t0, b);
+    ptx::tma_load_4d(dst + 1 * TILE, &tm_q, bar, 0, h, t0, b);
+    ptx::tma_load_4d(dst + 2 * TILE, &tm_k, bar, 64, h, t0, b);
+    ptx::tma_load_4d(dst + 3 * TILE, &tm_q, bar, 64, h, t0, b);
+  };
+
+  if (rank == 0) {
+    // ======================================= state CTA =======================================
+    // One elected thread of a group waits; a reducing named barrier hands the outcome to the group.
+    auto gwait = [&](int bar, uint32_t parity, bool leader, int group, bool cluster_scope) -> bool {
+      bool fail = false;
+      if (leader) {
+        fail = cluster_scope ? !ptx::mbar_wait_abortable_cluster(&sbar[bar], parity, WAIT_LIMIT, abort_flag)
+                             : !ptx::mbar_wait_abortable(&sbar[bar], parity, WAIT_LIMIT, abort_flag);
+        if (fail) raise_abort();
+      }
+      return !ptx::named_bar_or(group, 128, fail);
+    };
+    // k, q and v tiles of chunk c into buffer c & 1 (one thread; the buffer's previous chunk, c - 2,
+    // has completed).  One barrier per buffer, expecting both tile sets.
+    auto issue_loads = [&](int c) {
+      const int s = c & 1;
+      uint64_t* bar = &sbar[SB_KQF + s];
+      ptx::mbar_arrive_expect_tx(bar, KQ_BYTES + V_BYTES);
+      issue_kq(sm + S_KQ + s * KQ_BYTES, bar, c);
+      uint8_t* dst = sm + S_V + s * V_BYTES;
+      ptx::tma_load_4d(dst, &tm_v, bar, 0, h, (cb + c) * C, b);
+      ptx::tma_load_4d(dst + TILE, &tm_v, bar, 64, h, (cb + c) * C, b);
+      *loads_issued = c + 1;
+    };
+    float* gslots = reinterpret_cast<float*>(sm + S_GS);
+
+    if (warp < 4) {
+      // ----------------------------------- state chain -----------------------------------
+      const bool leader = tid == 0;
+      bool issued = false;
+      const uint32_t peer_pe0 = ptx::mapa_shared(ptx::smem_u32(&pbar[PB_PE]), 1u);
+      {
+        // Initial state: the caller's S_0 (first segment) or the combined state of the segments before.
+        const float* src = nullptr;
+        if (seg == 0) {
+          if (p.s0) src = p.s0 + ((int64_t)bh * D + row) * D;
+        } else {
+          src = p.seg_s0 + ((int64_t)(bh * p.ws_stride + seg - 1) * (2 * D) + row) * D;
+        }
+#pragma unroll 1
+        for (int c4 = 0; c4 < 4; ++c4) {
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 32; i += 4) {
+            const float4 t4 = src ? *reinterpret_cast<const float4*>(src + c4 * 32 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+            v[i] = t4.x; v[i + 1] = t4.y; v[i + 2] = t4.z; v[i + 3] = t4.w;
+          }
+          ptx::tmem_st32(my + COL_S + c4 * 32, v);
+        }
+        ptx::tc_wait_st();
+      }
+      if (leader && nch > 0) {
+        issue_loads(0);
+        if (nch > 1) issue_loads(1);
+      }
+#pragma unroll 1
+      for (int c = 0; c < nch; ++c) {
+        const int s = c & 1;
+        const uint32_t ph = (uint32_t)(c >> 1) & 1u;
+        const uint32_t kq_o = S_KQ + s * KQ_BYTES, v_o = S_V + s * V_BYTES, ps_o = S_PS + s * PS_BYTES;
+        const float* gs = gslots + s * GSLOT;
+        if (c > 0) {  // chunk c-1 done: its tile buffers and product slot are free
+          if (!gwait(SB_S, (uint32_t)(c - 1) & 1u, leader, 1, false)) break;
+          if (leader) {
+            issued = false;
+            if (c + 1 < nch) issue_loads(c + 1);
+            ptx::mbar_arrive_remote(peer_pe0 + 8u * (uint32_t)((c - 1) & 1));
+          }
+        }
+        if (!gwait(SB_KQR + s, ph, leader, 1, false)) break;  // fp16 K, Gamma Q, V and the gates of chunk c
+        if (!gwait(SB_PF + s, ph, leader, 1, true)) break;    // A, T, T Gamma of chunk c from the prep CTA
+        const float gC = gs[2 * C];
+        ptx::tc_fence_after();
+        if (leader) {  // U^T = V^T T^T while the state is converted
+          ptx::fence_proxy_async_smem();
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            ptx::mma_f16_ss(tmem + COL_U, at(D_MN8K, v_o + k * 2048), at(D_K, ps_o + TILE + k * 32), ID_N64_AMN, k > 0);
+          issued = true;
+        }
+        // S -> S16 (fp16, tensor memory: the A operand of R and Y) and S <- gamma_C S, 32 columns at
+        // a time; no MMA in flight touches these columns.
+#pragma unroll 1
+        for (int c4 = 0; c4 < 4; ++c4) {
+          float v[32];
+          ptx::tmem_ld32(my + COL_S + c4 * 32, v);
+          ptx::tc_wait_ld();
+          uint32_t hv[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) hv[i] = pack_h2(v[2 * i], v[2 * i + 1]);
+          ptx::tmem_st16(my + COL_S16 + c4 * 16, hv);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] *= gC;
+          ptx::tmem_st32(my + COL_S + c4 * 32, v);
+        }
+        ptx::tc_wait_st();
+        ptx::tc_fence_before();
+        if (!gwait(SB_W16R, (uint32_t)c & 1u, leader, 1, false)) break;  // W16 of chunk c (also orders the stores)
+        bool r_ok = true;
+        if (leader) {  // R^T = U^T - S W^T (committed alone), then Y = S (Gamma Q)^T
+          ptx::tc_fence_after();
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            ptx::mma_f16_ts(tmem + COL_U, tmem + COL_S16 + 8 * k, at(D_K, S_W + k * 2048), ID_N64_BMN_NEG, 1);
+          ptx::mma_commit(&sbar[SB_R]);
+          if (c >= 2) {  // Y[s] drained by the output warps
+            r_ok = ptx::mbar_wait_abortable(&sbar[SB_YE + s], (uint32_t)((c - 2) >> 1) & 1u, WAIT_LIMIT, abort_flag);
+            if (!r_ok) raise_abort();
+          }
+          if (r_ok) {
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+              ptx::mma_f16_ts(tmem + COL_Y + 64 * s, tmem + COL_S16 + 8 * k,
+                              at(D_K, kq_o + TILE + (k >> 2) * 2 * TILE + (k & 3) * 32), ID_N64, k > 0);
+          }
+        }
+        {
+          bool fail = false;
+          if (leader) {
+            fail = !r_ok || !ptx::mbar_wait_abortable(&sbar[SB_R], (uint32_t)c & 1u, WAIT_LIMIT, abort_flag);
+            if (fail) raise_abort();
+          }
+          if (ptx::named_bar_or(1, 128, fail)) break;
+        }
+        if (leader) issued = false;
+        ptx::tc_fence_after();
+        {
+          // R -> R16 and R diag(w) -> RW16 (fp16, tensor memory), 32 tokens at a time.
+          const float* w_s = gs + C;
+#pragma unroll 1
+          for (int h2 = 0; h2 < 2; ++h2) {
+            float rv[32];
+            ptx::tmem_ld32(my + COL_U + 32 * h2, rv);
+            ptx::tc_wait_ld();
+            uint32_t hv[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) hv[i] = pack_h2(rv[2 * i], rv[2 * i + 1]);
+            ptx::tmem_st16(my + COL_R16 + 16 * h2, hv);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) hv[i] = pack_h2(rv[2 * i] * w_s[32 * h2 + 2 * i], rv[2 * i + 1] * w_s[32 * h2 + 2 * i + 1]);
+            ptx::tmem_st16(my + COL_RW16 + 16 * h2, hv);
+          }
+          ptx::tc_wait_st();
+        }
+        ptx::tc_fence_before();
+        ptx::named_bar(1, 128);
+        if (leader) {  // S += (R diag w)^T K (committed alone), then Y += R^T A^T
+          ptx::tc_fence_after();
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            ptx::mma_f16_ts(tmem + COL_S, tmem + COL_RW16 + 8 * k, at(D_MN16K, kq_o + k * 2048), ID_N128_BMN, 1);
+          ptx::mma_commit(&sbar[SB_S]);
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            ptx::mma_f16_ts(tmem + COL_Y + 64 * s, tmem + COL_R16 + 8 * k, at(D_K, ps_o + k * 32), ID_N64, 1);
+          ptx::mma_commit(&sbar[SB_YF + s]);
+          issued = true;
+        }
+      }
+      if (!*abort_flag && nch > 0 && gwait(SB_S, (uint32_t)(nch - 1) & 1u, leader, 1, false)) {
+        if (leader) issued = false;
+        ptx::tc_fence_after();
+        if (seg == p.nseg - 1 && p.s_out != nullptr) {
+          float* dst = p.s_out + ((int64_t)bh * D + row) * D;
+#pragma unroll 1
+          for (int c4 = 0; c4 < 4; ++c4) {
+            float v[32];
+            ptx::tmem_ld32(my + COL_S + c4 * 32, v);
+            ptx::tc_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; i += 4)
+              *reinterpret_cast<float4*>(dst + c4 * 32 + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+          }
+        }
+      }
+      if (*abort_flag && leader && issued) {  // drain this thread's MMAs
+        ptx::mma_commit(&sbar[SB_DRAIN]);
+        ptx::mbar_wait_bounded(&sbar[SB_DRAIN], 0, WAIT_LIMIT);
+      }
+    } else if (warp < 8) {
+      // ------------------------- convert: gates, fp16 tiles, W ----------------------------
+      const int wt = tid - 128, ww = wt >> 5;
+      const bool leader = wt == 0;
+      bool issued = false;
+      float la0 = 0.f, la1 = 0.f, be0 = 0.f, be1 = 0.f;
+      if (ww == 1 && nch > 0) load_gates(0, la0, la1, be0, be1);
+#pragma unroll 1
+      for (int c = 0; c < nch; ++c) {
+        const int s = c & 1;
+        const uint32_t ph = (uint32_t)(c >> 1) & 1u;
+        const uint32_t kq_o = S_KQ + s * KQ_BYTES, v_o = S_V + s * V_BYTES, ps_o = S_PS + s * PS_BYTES;
+        float* gs = gslots + s * GSLOT;
+        float g0 = 0.f, g1 = 0.f, gC = 0.f;
+        if (ww == 1) cumsum_gates(la0, la1, g0, g1, gC);
+        if (!gwait(SB_KQF + s, ph, leader, 2, false)) break;  // k, q, v tiles of chunk c
+        if (ww == 1) {  // the gate slot of chunk c-2 was last read before S(c-2), which preceded these loads
+          gs[lane] = expf(g0);
+          gs[lane + 32] = expf(g1);
+          gs[C + lane] = be0 * expf(gC - g0);
+          gs[C + lane + 32] = be1 * expf(gC - g1);
+          if (lane == 0) gs[2 * C] = expf(gC);
+          if (c + 1 < nch) load_gates(c + 1, la0, la1, be0, be1);
+        }
+        ptx::named_bar(2, 128);
+        // bf16 -> fp16 in place: K (tiles 0, 2 of the k/q set), gamma-scaled Q (tiles 1, 3), V (two
+        // tiles).  Unrolled by four only: the kernel's instruction working set, not latency, is
+        // what limits it when many clusters share a GPC.
+#pragma unroll 4
+        for (int j = 0; j < 24; ++j) {
+          const int i = wt + 128 * j;
+          const int tile = i >> 9;
+          uint8_t* base = tile < 4 ? sm + kq_o + tile * TILE : sm + v_o + (tile - 4) * TILE;
+          const int off = (i & 511) * 16;
+          const float sc = (tile == 1 || tile == 3) ? gs[off >> 7] : 1.f;
+          uint4 r = *reinterpret_cast<uint4*>(base + off);
+          __nv_bfloat162* b2 = reinterpret_cast<__nv_bfloat162*>(&r);
+          uint4 o;
+          uint32_t* o32 = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float2 f = __bfloat1622float2(b2[k]);
+            o32[k] = pack_h2(f.x * sc, f.y * sc);
+          }
+          *reinterpret_cast<uint4*>(base + off) = o;
+        }
+        ptx::fence_proxy_async_smem();
+        ptx::named_bar(2, 128);
+        if (leader) ptx::mbar_arrive(&sbar[SB_KQR + s]);
+        // W^T = K^T (T Gamma)^T, after T Gamma has arrived and R(c-1) has read W16(c-1).
+        if (!gwait(SB_PF + s, ph, leader, 2, true)) break;
+        if (c > 0 && !gwait(SB_R, (uint32_t)(c - 1) & 1u, leader, 2, false)) break;
+        if (leader) {
+          ptx::fence_proxy_async_smem();
+          ptx::tc_fence_after();
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            ptx::mma_f16_ss(tmem + COL_W, at(D_MN16K, kq_o + k * 2048), at(D_K, ps_o + 2 * TILE + k * 32), ID_N64_AMN,
+                            k > 0);
+          ptx::mma_commit(&sbar[SB_WM]);
+          issued = true;
+        }
+        if (!gwait(SB_WM, (uint32_t)c & 1u, leader, 2, false)) break;
+        if (leader) issued = false;
+        ptx::tc_fence_after();
+        {
+          float wv[64];
+          ptx::tmem_ld32(my + COL_W, *reinterpret_cast<float(*)[32]>(wv));
+          ptx::tmem_ld32(my + COL_W + 32, *reinterpret_cast<float(*)[32]>(wv + 32));
+          ptx::tc_wait_ld();
+          store_row_f16(sm + S_W, row, wv);  // W16: row d, 64 tokens
+        }
+        ptx::fence_proxy_async_smem();
+        ptx::tc_fence_before();
+        ptx::named_bar(2, 128);
+        if (leader) ptx::mbar_arrive(&sbar[SB_W16R]);
+      }
+      if (*abort_flag && leader && issued) {
+        ptx::mma_commit(&sbar[SB_DRAIN + 1]);
+        ptx::mbar_wait_bounded(&sbar[SB_DRAIN + 1], 0, WAIT_LIMIT);
+      }
+    } else {
+      // ------------------------------ output: Y -> y ---------------------------------------
+      const bool leader = tid == 256;
+      constexpr int ROWS = (int)(TILE / (D * sizeof(TOut)));  // tokens per staging piece
+      TOut* stage = reinterpret_cast<TOut*>(sm + S_YS);
+#pragma unroll 1
+      for (int c = 0; c < nch; ++c) {
+        const int s = c & 1;
+        if (!gwait(SB_YF + s, (uint32_t)(c >> 1) & 1u, leader, 3, false)) break;
+        ptx::tc_fence_after();
+        float yv[64];
+        ptx::tmem_ld32(my + COL_Y + 64 * s, *reinterpret_cast<float(*)[32]>(yv));
+        ptx::tmem_ld32(my + COL_Y + 64 * s + 32, *reinterpret_cast<float(*)[32]>(yv + 32));
+        ptx::tc_wait_ld();
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&sbar[SB_YE + s]);
+#pragma unroll
+        for (int piece = 0; piece < C / ROWS; ++piece) {  // unrolled: yv stays in registers
+          if (piece > 0) {  // the previous piece's bytes must have been read out first
+            if (leader) ptx::bulk_wait_read0();
+            ptx::named_bar(3, 128);
+          }
+#pragma unroll
+          for (int j = 0; j < ROWS; ++j) store_as(stage + j * D + row, yv[piece * ROWS + j]);
+          ptx::fence_proxy_async_smem();
+          ptx::named_bar(3, 128);
+          if (leader) {
+            ptx::tma_store_4d(&tm_y, stage, 0, h, (cb + c) * C + piece * ROWS, b);
+            ptx::bulk_commit();
+          }
+        }
+        if (leader) ptx::bulk_wait_read0();  // before the next chunk's first piece (ordered by the next gwait)
+      }
+      if (leader) ptx::bulk_wait0();
+    }
+  } else {
+    // ======================================== prep CTA ========================================
+    if (warp < 8) {
+      const int pp = warp >> 2;  // pipeline: chunks pp, pp + 2, ...
+      const int pt = tid & 127, pw = pt >> 5;
+      const bool leader = pt == 0;
+      const uint32_t base = pp * P_STRIDE;
+      uint8_t* kq = sm + base + P_KQ;
+      uint8_t* st = sm + base + P_ST;
+      float* eT = reinterpret_cast<float*>(sm + base + P_EXPT);  // [64]      exp(g_t - g_{16 floor(t/16)})
+      float* eJ = eT + C;                                         // [4][64]   beta_j exp(g_{16b} - g_j), j < 16b
+      float* Ed = eJ + 4 * C;                                     // [4][16][20] beta_{16b+c} exp(g_{16b+r} - g_{16b+c}), c <= r
+      float* beta_s = reinterpret_cast<float*>(sm + base + P_GS);
+      float* g_s = beta_s + C;
+      float* gam_s = g_s + C;
+      const uint32_t remote_slot = ptx::mapa_shared(sb + S_PS + pp * PS_BYTES, 0u);
+      const uint32_t remote_pf = ptx::mapa_shared(ptx::smem_u32(&sbar[SB_PF + pp]), 0u);
+      auto gwait = [&](int bar, uint32_t parity, bool cluster_scope) -> bool {
+        bool fail = false;
+        if (leader) {
+          fail = cluster_scope ? !ptx::mbar_wait_abortable_cluster(&pbar[bar], parity, WAIT_LIMIT, abort_flag)
+                               : !ptx::mbar_wait_abortable(&pbar[bar], parity, WAIT_LIMIT, abort_flag);
+          if (fail) raise_abort();
+        }
+        return !ptx::named_bar_or(1 + pp, 128, fail);
+      };
+      auto issue = [&](int c) {
+        ptx::mbar_arrive_expect_tx(&pbar[PB_KQF + pp], KQ_BYTES);
+        issue_kq(kq, &pbar[PB_KQF + pp], c);
+        ptx::tma_prefetch_4d(&tm_v, 0, h, (cb + c) * C, b);  // the state CTA's v tile, into L2
+        ptx::tma_prefetch_4d(&tm_v, 64, h, (cb + c) * C, b);
+      };
+      bool issued = false;
+      int last_load = -1;  // index k of the last tile set requested
+      float la0 = 0.f, la1 = 0.f, be0 = 0.f, be1 = 0.f;
+      if (leader && pp < nch) { issue(pp); last_load = 0; }
+      if (pw == 1 && pp < nch) load_gates(pp, la0, la1, be0, be1);
+      int k = 0;
+#pragma unroll 1
+      for (int c = pp; c < nch; c += 2, ++k) {
+        const uint32_t ph = (uint32_t)k & 1u;
+        if (!gwait(PB_KQF + pp, ph, false)) break;
+        if (leader) {  // G = [K;Q] K^T from the bf16 tiles as loaded
+          ptx::tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint64_t a = at(D_K, base + P_KQ + (kk >> 2) * 2 * TILE + (kk & 3) * 32);
+            ptx::mma_f16_ss(tmem + 64 * pp, a, a, ID_G, kk > 0);
+          }
+          ptx::mma_commit(&pbar[PB_G + pp]);
+          issued = true;
+        }
+        if (pw == 1) {  // chunk-local cumulative log-decay
+          float g0, g1, gC;
+          cumsum_gates(la0, la1, g0, g1, gC);
+          beta_s[lane] = be0;
+          beta_s[lane + 32] = be1;
+          g_s[lane] = g0;
+          g_s[lane + 32] = g1;
+          gam_s[lane] = expf(g0);
+          gam_s[lane + 32] = expf(g1);
+        }
+        ptx::named_bar(1 + pp, 128);
+        // Decay tables: 1,344 exponentials per chunk instead of one per (t, j) pair; every factor is
+        // exp of a non-positive number, so none overflows whatever the decay.
+#pragma unroll 1
+        for (int e = pt; e < 5 * C; e += 128) {
+          if (e < C) {
+            eT[e] = __expf(g_s[e] - g_s[e & ~15]);
+          } else {
+            const int bb = (e - C) >> 6, j = (e - C) & 63;
+            eJ[bb * C + j] = (bb > 0 && j < 16 * bb) ? beta_s[j] * __expf(g_s[16 * bb] - g_s[j]) : 0.f;
+          }
+        }
+#pragma unroll 1
+        for (int n = 0; n < 8; ++n) {
+          const int e = pt + 128 * n;  // 1024 diagonal-block entries
+          const int bb = e >> 8, r = (e >> 4) & 15, cc = e & 15;
+          Ed[(bb * 16 + r) * 20 + cc] = cc <= r ? beta_s[16 * bb + cc] * __expf(g_s[16 * bb + r] - g_s[16 * bb + cc]) : 0.f;
+        }
+        if (!gwait(PB_G + pp, ph, false)) break;  // also orders the tables
+        if (leader) {  // the tile set is free once G has been formed: fetch chunk c + 2
+          issued = false;
+          if (c + 2 < nch) { issue(c + 2); last_load = k + 1; }
+        }
+        if (pw == 1 && c + 2 < nch) load_gates(c + 2, la0, la1, be0, be1);
+        ptx::tc_fence_after();
+        // Row pt of G: rows 0-63 give L (strictly lower), rows 64-127 give A (lower with diagonal).
+        {
+          float gv[64];
+          ptx::tmem_ld32(my + 64 * pp, *reinterpret_cast<float(*)[32]>(gv));
+          ptx::tmem_ld32(my + 64 * pp + 32, *reinterpret_cast<float(*)[32]>(gv + 32));
+          ptx::tc_wait_ld();
+          const int t = pt & 63, tb = t >> 4;
+          const bool is_l = pt < 64;
+          const float et = eT[t];
+#pragma unroll
+          for (int jb = 0; jb < 4; ++jb) {
+            float e[16];
+            const float4* src4 = jb < tb ? reinterpret_cast<const float4*>(eJ + tb * C + 16 * jb)
+                                         : reinterpret_cast<const float4*>(Ed + (tb * 16 + (t & 15)) * 20);
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              const float4 f = src4[v];
+              e[4 * v] = f.x; e[4 * v + 1] = f.y; e[4 * v + 2] = f.z; e[4 * v + 3] = f.w;
+            }
+            const float sc = jb < tb ? et : (jb == tb ? 1.f : 0.f);
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) {
+              float ej = e[jj] * sc;
+              if (is_l && 16 * jb + jj == t) ej = 0.f;
+              gv[16 * jb + jj] *= ej;
+            }
+          }
+          if (is_l) {
+            uint8_t* lrow = sm + base + P_L16 + t * LD16;
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              uint4 v4;
+              v4.x = pack_h2(gv[q * 8 + 0], gv[q * 8 + 1]);
+              v4.y = pack_h2(gv[q * 8 + 2], gv[q * 8 + 3]);
+              v4.z = pack_h2(gv[q * 8 + 4], gv[q * 8 + 5]);
+              v4.w = pack_h2(gv[q * 8 + 6], gv[q * 8 + 7]);
+              *reinterpret_cast<uint4*>(lrow + q * 16) = v4;
+            }
+            float* drow = reinterpret_cast<float*>(sm + base + P_LDIAG) + (tb * 16 + (t & 15)) * LDG;
+#pragma unroll
+            for (int q = 0; q < 16; q += 4) {
+              float4 f4;
+              switch (tb) {  // static register selection
+                case 0: f4 = make_float4(gv[q], gv[q + 1], gv[q + 2], gv[q + 3]); break;
+                case 1: f4 = make_float4(gv[16 + q], gv[17 + q], gv[18 + q], gv[19 + q]); break;
+                case 2: f4 = make_float4(gv[32 + q], gv[33 + q], gv[34 + q], gv[35 + q]); break;
+                default: f4 = make_float4(gv[48 + q], gv[49 + q], gv[50 + q], gv[51 + q]); break;
+              }
+              *reinterpret_cast<float4*>(drow + q) = f4;
+            }
+          } else {
+            store_row_f16(st, (uint32_t)t, gv);  // A16 row t
+          }
+        }
+        ptx::named_bar(1 + pp, 128);
+        if (pt < 64) {
+          // D_b = (I + L_bb)^-1, one column per thread; right-looking fp32 forward substitution.
+          const int bb = pt >> 4, j = pt & 15;
+          const float* Lb = reinterpret_cast<const float*>(sm + base + P_LDIAG) + bb * 16 * LDG;
+          float x[16], acc[16];
+#pragma unroll
+          for (int r = 0; r < 16; ++r) acc[r] = 0.f;
+#pragma unroll
+          for (int m = 0; m < 16; ++m) {
+            x[m] = (m == j) ? 1.f : (m > j ? -acc[m] : 0.f);
+#pragma unroll
+            for (int r = m + 1; r < 16; ++r) acc[r] = fmaf(Lb[r * LDG + m], x[m], acc[r]);
+          }
+          __half* l16 = reinterpret_cast<__half*>(sm + base + P_L16);
+#pragma unroll
+          for (int r = 0; r < 16; ++r) l16[(bb * 16 + r) * (LD16 / 2) + bb * 16 + j] = __float2half_rn(x[r]);
+        }
+        ptx::named_bar(1 + pp, 128);
+        merge_column_any<false>(pw, sb + base + P_L16, sb + base + P_ST + TILE, 0u, sb + base + P_ST + 2 * TILE, gam_s,
+                               lane);
+        // The slot this pipeline used two chunks ago must have been given back; the group wait
+        // (or the barrier) also orders the merges' and the rows' stores before the copy.
+        if (k > 0) {
+          if (!gwait(PB_PE + pp, (uint32_t)(k - 1) & 1u, true)) break;
+        } else {
+          ptx::named_bar(1 + pp, 128);
+        }
+#pragma unroll 4
+        for (int i = pt; i < (int)(PS_BYTES / 16); i += 128)
+          ptx::st_cluster_v4(remote_slot + (uint32_t)i * 16u, *reinterpret_cast<const uint4*>(st + i * 16));
+        ptx::fence_proxy_async_cluster();
+        ptx::named_bar(1 + pp, 128);
+        if (leader) ptx::mbar_arrive_remote(remote_pf);
+      }
+      if (*abort_flag && leader) {  // drain this pipeline's MMA and tile loads
+        if (issued) {
+          ptx::mma_commit(&pbar[PB_DRAIN + pp]);
+          ptx::mbar_wait_bounded(&pbar[PB_DRAIN + pp], 0, WAIT_LIMIT);
+        }
+        if (last_load >= 0) ptx::mbar_wait_bounded(&pbar[PB_KQF + pp], (uint32_t)last_load & 1u, WAIT_LIMIT);
+      }
+    }
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (rank == 0 && tid == 0 && *abort_flag) {  // tile loads still in flight: the last one per buffer
+    const int n = *loads_issued;
+    for (int c = n - 2 < 0 ? 0 : n - 2; c < n; ++c)
+      ptx::mbar_wait_bounded(&sbar[SB_KQF + (c & 1)], (uint32_t)(c >> 1) & 1u, WAIT_LIMIT);
+  }
+  __syncwarp();
+  ptx::cluster_sync();  // neither CTA leaves while the other may still write into it
+  ptx::tc_fence_after();
+  if (tid == 0 && *abort_flag) atomicExch(&g_status, GDN_ERR_TIMEOUT);
+  if (warp == 0) ptx::tmem_dealloc(tmem, tmem_cols);
+}
+
+template <typename TOut>
+int launch(const gdn_prefill_args* a, int nseg, int seg_len, const float* seg_s0, int ws_stride, cudaStream_t stream) {
+  CUtensorMap mq, mk, mv, my;
+  if (!make_map(&mq, a->q, a->DK, a, a->sq) || !make_map(&mk, a->k, a->DK, a, a->sk) ||
+      !make_map(&mv, a->v, a->DV, a, a->sv) || !make_store_map<TOut>(&my, a->y, a->DV, a, a->sy))
+    return GDN_ERR_LAUNCH;
+  auto kern = pair_kernel<TOut>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, DYN) != cudaSuccess)
+      return GDN_ERR_LAUNCH;
+    attr_set = true;
+  }
+  const int nch = (int)((a->T + C - 1) / C);
+  Params p;
+  p.beta = a->beta; p.la = a->la; p.s0 = a->s0; p.s_out = a->s_out;
+  p.B = (int)a->B; p.T = (int)a->T; p.H = (int)a->H;
+  p.nseg = nseg;
+  p.seg_len = seg_len > 0 ? seg_len : nch;
+  p.seg_s0 = seg_s0;
+  p.ws_stride = ws_stride;
+  const int64_t grid = 2 * a->B * a->H * (int64_t)nseg;
+  if (grid <= 0 || grid > 0x7fffffff) return GDN_ERR_SHAPE;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid, 1, 1);
+  cfg.blockDim = dim3(NT, 1, 1);
+  cfg.dynamicSmemBytes = DYN;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, mq, mk, mv, my, p) != cudaSuccess) return GDN_ERR_LAUNCH;
+  return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+}
+
+// Clusters of this kernel that fit on the device at once (0 if the query fails).
+int max_active_clusters() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  if (cached[dev] > 0) return cached[dev];
+  auto kern = pair_kernel<__nv_bfloat16>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, DYN) != cudaSuccess) return 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2, 1, 1);
+  cfg.blockDim = dim3(NT, 1, 1);
+  cfg.dynamicSmemBytes = DYN;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  cached[dev] = n;
+  return n;
+}
+
+}  // namespace pair
+}  // namespace gdn
+
+// DK = DV = 128, u = beta k; the rest as the single-CTA kernel (bf16 inputs, TMA-aligned y).
+bool gdn_chunk_pair_supported(const gdn_prefill_args* a) {
+  return a->DV == 128 && a->in_dtype == GDN_DTYPE_BF16 && gdn_chunk_ws_supported(a);
+}
+
+int gdn_chunk_pair_max_clusters() { return gdn::pair::max_active_clusters(); }
+
+int gdn_launch_chunk_pair(const gdn_prefill_args* a, int nseg, int seg_len, const float* seg_s0, int ws_stride,
+                          cudaStream_t stream) {
+  return a->out_dtype == GDN_DTYPE_BF16 ? gdn::pair::launch<__nv_bfloat16>(a, nseg, seg_len, seg_s0, ws_stride, stream)
+                                        : gdn::pair::launch<float>(a, nseg, seg_len, seg_s0, ws_stride, stream);
+}
+
+int gdn_chunk_pair_read_status(int* out, int reset) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, gdn::pair::g_status, sizeof(int)) != cudaSuccess) return GDN_ERR_LAUNCH;
+  if (reset) {
+    int z = 0;
+    if (cudaMemcpyToSymbol(gdn::pair::g_status, &z, sizeof(int)) != cudaSuccess) return GDN_ERR_LAUNCH;
+  }
+  *out = v;
+  return GDN_OK;
+}

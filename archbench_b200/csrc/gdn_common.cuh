@@ -70,3 +70,8 @@ bool gdn_segmented_plan(const gdn_prefill_args* a, int sms, int* nseg, int* seg_
 int gdn_segmented_sms();
 int gdn_launch_segmented(const gdn_prefill_args* a, float* ws, size_t ws_bytes, int sms, cudaStream_t stream);
 int gdn_launch_segmented_static(const gdn_prefill_args* a, int sms, cudaStream_t stream);
+bool gdn_chunk_pair_supported(const gdn_prefill_args* a);
+int gdn_chunk_pair_max_clusters();
+int gdn_launch_chunk_pair(const gdn_prefill_args* a, int nseg, int seg_len, const float* seg_s0, int ws_stride,
+                          cudaStream_t stream);
+int gdn_chunk_pair_read_status(int* out, int reset);

@@ -26,8 +26,8 @@ _PKG = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_PKG, "libgdn_b200.so")
 
 GDN_DTYPE_F32, GDN_DTYPE_BF16 = 0, 1
-IMPLS = {"auto": 0, "chunk": 1, "recurrent": 2, "segmented": 3}
-IMPL_NAMES = {1: "chunk", 2: "recurrent", 3: "segmented"}
+IMPLS = {"auto": 0, "chunk": 1, "recurrent": 2, "segmented": 3, "chunk_cluster": 4, "chunk_single": 5}
+IMPL_NAMES = {1: "chunk", 2: "recurrent", 3: "segmented", 4: "chunk_cluster", 5: "chunk_single"}
 _DT = {torch.float32: GDN_DTYPE_F32, torch.bfloat16: GDN_DTYPE_BF16}
 
 
@@ -311,7 +311,8 @@ def nsgdn_scan(q, k, u, v, la) -> torch.Tensor:
 
 
 def selected_impl(q, k, v, la, beta=None, u=None, impl="auto") -> str:
-    """Name of the kernel ``gdn_prefill`` runs for these arguments ("chunk" or "recurrent")."""
+    """Name of the kernel ``gdn_prefill`` runs for these arguments ("chunk_cluster", "chunk_single",
+    "segmented" or "recurrent")."""
     _check_cuda(q, k, u, v, la, beta)
     in_dtype = torch.bfloat16 if q.dtype == torch.bfloat16 else torch.float32
     q, k, v = (_prep_token(t, n, in_dtype) for t, n in ((q, "q"), (k, "k"), (v, "v")))

@@ -51,6 +51,10 @@ from archbench_b200.workloads import (  # noqa: E402
 METRIC = "GDN prefill tok/s/GPU (T=4096,d=128), decode tok/s; % roofline at 1/2/4/8 GPU"
 
 
+# Committed ncu capture of each prefill kernel on the headline workload.
+PROFILE_OF = {"chunk_single": "ws_kernel_cfg1.md", "chunk_cluster": "pair_kernel_cfg1.md"}
+
+
 def profiled_traffic(summary):
     """DRAM bytes (read + write) per launch from one committed ncu capture of the kernel."""
     try:
@@ -214,8 +218,8 @@ def bench_prefill(args, rank, world):
         "kernel": sel,
         "roofline": {
             "bound": "hbm", "achieved": achieved_gbs, "peak": hbm, "unit": "GB/s", "frac": achieved_gbs / hbm,
-            "traffic": profiled_traffic("ws_kernel_cfg1.md") if sel == "chunk" else None,
-            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, profiles/ws_kernel_cfg1.md",
+            "traffic": profiled_traffic(PROFILE_OF.get(sel, "")),
+            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, profiles/" + PROFILE_OF.get(sel, "(none)"),
             "peak_source": src, "algorithmic_bytes_per_launch": alg_bytes,
             "tensor": {"achieved_tflops": alg_flops / per_launch / 1e12, "peak_tflops": tflops,
                        "frac": alg_flops / per_launch / 1e12 / tflops, "algorithmic_flops_per_launch": alg_flops},
@@ -395,7 +399,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--prefill-impl", choices=["auto", "chunk", "recurrent"], default="auto")
+    ap.add_argument("--prefill-impl", choices=["auto", "chunk", "chunk_cluster", "chunk_single", "recurrent", "segmented"], default="auto")
     ap.add_argument("--skip-extra", action="store_true", help="headline prefill only")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the cpu_baseline leg")
     args = ap.parse_args()

@@ -55,8 +55,10 @@ typedef enum {
   GDN_IMPL_AUTO = 0,       /* the fastest kernel that applies (see gdn_prefill_select_impl) */
   GDN_IMPL_CHUNK = 1,      /* chunkwise tcgen05/TMEM kernel (bf16 I/O, DK = 128, DV a multiple of 128) */
   GDN_IMPL_RECURRENT = 2,  /* token-serial fp32 kernel (any supported dtype and head size) */
-  GDN_IMPL_SEGMENTED = 3   /* chunk kernel split into sequence segments for few long sequences;
+  GDN_IMPL_SEGMENTED = 3,  /* chunk kernel split into sequence segments for few long sequences;
                               needs the workspace gdn_prefill_workspace_bytes reports */
+  GDN_IMPL_CHUNK_CLUSTER = 4, /* chunk kernel on a two-CTA cluster per sequence (DV = 128, u = NULL) */
+  GDN_IMPL_CHUNK_SINGLE = 5   /* chunk kernel on one CTA per sequence and 128-row state tile */
 } gdn_impl;
 
 /* Strides of one token tensor, in elements.  The last (feature) dimension has stride 1. */
@@ -151,7 +153,8 @@ int gdn_prefill_workspace_bytes(const gdn_prefill_args* args, size_t* bytes);
 #define GDN_STATIC_WORKSPACE_BYTES (16u << 20)
 int gdn_prefill_fwd_static_workspace(const gdn_prefill_args* args, void* stream);
 
-/* Which kernel a prefill with these arguments runs (GDN_IMPL_CHUNK or _RECURRENT), or a
+/* Which kernel a prefill with these arguments runs (GDN_IMPL_CHUNK_CLUSTER, _CHUNK_SINGLE,
+ * _SEGMENTED or _RECURRENT; GDN_IMPL_CHUNK resolves to one of the two chunk variants), or a
  * negative gdn_status if the arguments are invalid.  Launches nothing. */
 int gdn_prefill_select_impl(const gdn_prefill_args* args);
 

@@ -55,7 +55,7 @@ def status(a):
 
 
 def test_validation_codes():
-    assert status(fake_args()) in (1, 2)
+    assert status(fake_args()) in (2, 4, 5)
     assert status(fake_args(q=None)) == -1
     assert status(fake_args(beta=None)) == -1  # no u and no beta
     assert status(fake_args(B=0)) == -2
@@ -64,6 +64,7 @@ def test_validation_codes():
     assert status(fake_args(DV=0)) == -5
     assert status(fake_args(in_dtype=7)) == -3
     assert status(fake_args(impl=9)) == -5
+    assert status(fake_args(impl=6)) == -5
     assert status(fake_args(q=0x10002)) == -4  # misaligned vector loads
 
 
@@ -72,6 +73,21 @@ def test_recurrent_selected_for_fp32_and_small_heads():
     assert status(fake_args(shape=(2, 64, 4, 64, 64))) == 2
     assert status(fake_args(shape=(2, 64, 4, 64, 64), impl=1)) == -5  # chunk forced, not covered
     assert status(fake_args(impl=3)) == -5  # segmented forced where it does not apply
+
+
+def test_chunk_variant_selection():
+    # DV = 128, u = beta k: the two-CTA cluster kernel; "chunk" resolves to it
+    assert status(fake_args()) == 4
+    assert status(fake_args(impl=1)) == 4
+    assert status(fake_args(impl=4)) == 4
+    assert status(fake_args(impl=5)) == 5
+    # DV = 256 or an explicit write vector: only the single-CTA kernel
+    wide = (2, 128, 4, 128, 256)
+    assert status(fake_args(shape=wide)) == 5
+    assert status(fake_args(shape=wide, impl=4)) == -5
+    st = ops.Strides(128 * 4 * 128, 4 * 128, 128)
+    assert status(fake_args(u=0x70000, su=st)) == 5
+    assert status(fake_args(u=0x70000, su=st, impl=4)) == -5
 
 
 def test_workspace_query():
@@ -84,7 +100,7 @@ def test_workspace_query():
     a = fake_args(shape=(1, 4096, 2, 128, 128))
     assert lib.gdn_prefill_workspace_bytes(ctypes.byref(a), ctypes.byref(n)) == 0
     assert n.value > 0 and n.value % (256 * 128 * 4 * 2) == 0
-    assert status(a) == 1  # no workspace supplied: the single-pass chunk kernel
+    assert status(a) == 4  # no workspace supplied: the single-pass (cluster) chunk kernel
     a.workspace, a.workspace_bytes = 0x100000, n.value
     assert status(a) == 3
     a.impl = 3

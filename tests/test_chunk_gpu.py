@@ -16,6 +16,9 @@ from oracle import oracle as O
 pytestmark = pytest.mark.gpu
 TOL_MAX, TOL_REL = 2e-3, 1e-3
 TOL_REL_BF16_OUT = 3e-3
+# The two chunk kernels: a two-CTA cluster per sequence (DV = 128, u = beta k) and one CTA per
+# sequence and 128-row state slice.
+VARIANTS = ["chunk_cluster", "chunk_single"]
 
 
 def np32(t):
@@ -28,7 +31,7 @@ def check(got, want, what, tol_max=TOL_MAX, tol_rel=TOL_REL):
     return mx, rel
 
 
-def run_case(B, T, H, seed=0, s0=False, with_u=False, out_dtype=torch.float32):
+def run_case(B, T, H, seed=0, s0=False, with_u=False, out_dtype=torch.float32, impl="chunk"):
     x = make_inputs(B, T, H, 128, 128, seed=seed, dtype=torch.bfloat16)
     S0 = (torch.randn(B, H, 128, 128, generator=torch.Generator().manual_seed(seed + 1)) * 0.3) if s0 else None
     u = (x["beta"][..., None] * x["k"].float()).to(torch.bfloat16) if with_u else None
@@ -38,7 +41,7 @@ def run_case(B, T, H, seed=0, s0=False, with_u=False, out_dtype=torch.float32):
     g = {k: v.cuda() for k, v in x.items()}
     y, S = ops.gdn_prefill(g["q"], g["k"], g["v"], g["la"], beta=None if with_u else g["beta"],
                            u=None if u is None else u.cuda(), initial_state=None if S0 is None else S0.cuda(),
-                           output_final_state=True, out_dtype=out_dtype, impl="chunk")
+                           output_final_state=True, out_dtype=out_dtype, impl=impl)
     torch.cuda.synchronize()
     return y, S, y_o, S_o
 
@@ -46,19 +49,22 @@ def run_case(B, T, H, seed=0, s0=False, with_u=False, out_dtype=torch.float32):
 def test_chunk_kernel_is_selected():
     x = make_inputs(1, 64, 1, 128, 128, dtype=torch.bfloat16)
     g = {k: v.cuda() for k, v in x.items()}
-    assert ops.selected_impl(g["q"], g["k"], g["v"], g["la"], beta=g["beta"]) == "chunk"
+    assert ops.selected_impl(g["q"], g["k"], g["v"], g["la"], beta=g["beta"]) == "chunk_cluster"
+    assert ops.selected_impl(g["q"], g["k"], g["v"], g["la"], beta=g["beta"], impl="chunk_single") == "chunk_single"
 
 
+@pytest.mark.parametrize("impl", VARIANTS)
 @pytest.mark.parametrize("T", [64, 192, 1, 63, 65, 100, 130])
-def test_lengths(T):
-    y, S, y_o, S_o = run_case(2, T, 2, seed=T)
+def test_lengths(T, impl):
+    y, S, y_o, S_o = run_case(2, T, 2, seed=T, impl=impl)
     check(y, y_o, f"y T={T}")
     check(S, S_o, f"S_T T={T}")
     assert ops.device_status() == 0
 
 
-def test_initial_state():
-    y, S, y_o, S_o = run_case(1, 256, 3, seed=5, s0=True)
+@pytest.mark.parametrize("impl", VARIANTS)
+def test_initial_state(impl):
+    y, S, y_o, S_o = run_case(1, 256, 3, seed=5, s0=True, impl=impl)
     check(y, y_o, "y")
     check(S, S_o, "S_T")
 
@@ -84,41 +90,45 @@ def test_nstep_write_vectors():
     check(S, S_o, "S_T")
 
 
-def test_bf16_output():
-    y, S, y_o, S_o = run_case(2, 128, 2, seed=7, out_dtype=torch.bfloat16)
+@pytest.mark.parametrize("impl", VARIANTS)
+def test_bf16_output(impl):
+    y, S, y_o, S_o = run_case(2, 128, 2, seed=7, out_dtype=torch.bfloat16, impl=impl)
     assert y.dtype == torch.bfloat16
     check(y, y_o, "y bf16", tol_rel=TOL_REL_BF16_OUT)
     check(S, S_o, "S_T")
 
 
-def test_strided_views():
+@pytest.mark.parametrize("impl", VARIANTS)
+def test_strided_views(impl):
     B, T, H, D = 2, 128, 2, 128
     x = make_inputs(B, T, H, D, D, seed=9, dtype=torch.bfloat16)
     fused = torch.cat([x["q"].reshape(B, T, -1), x["k"].reshape(B, T, -1), x["v"].reshape(B, T, -1)], -1).cuda()
     q, k, v = (fused[..., i * H * D : (i + 1) * H * D].view(B, T, H, D) for i in range(3))
     assert not q.is_contiguous()
-    assert ops.selected_impl(q, k, v, x["la"].cuda(), beta=x["beta"].cuda()) == "chunk"
-    y, S = ops.gdn_prefill(q, k, v, x["la"].cuda(), beta=x["beta"].cuda(), output_final_state=True, out_dtype=torch.float32)
+    assert ops.selected_impl(q, k, v, x["la"].cuda(), beta=x["beta"].cuda(), impl=impl) == impl
+    y, S = ops.gdn_prefill(q, k, v, x["la"].cuda(), beta=x["beta"].cuda(), output_final_state=True, out_dtype=torch.float32, impl=impl)
     y_o, S_o = O.recurrence_c(*(np32(x[n]) for n in ("q", "k", "v", "la")), beta=np32(x["beta"]))
     check(y, y_o, "y")
     check(S, S_o, "S_T")
 
 
-def test_cfg1_heads_against_oracle():
+@pytest.mark.parametrize("impl", VARIANTS)
+def test_cfg1_heads_against_oracle(impl):
     """Configuration-1 sequence length and heads (T=4096, H=8) for one batch row."""
     x = make_inputs(1, 4096, 8, 128, 128, seed=41, dtype=torch.bfloat16)
     y_o, S_o = O.recurrence_c(*(np32(x[n]) for n in ("q", "k", "v", "la")), beta=np32(x["beta"]))
     g = {k: v.cuda() for k, v in x.items()}
-    y, S = ops.gdn_prefill(g["q"], g["k"], g["v"], g["la"], beta=g["beta"], output_final_state=True, out_dtype=torch.float32, impl="chunk")
+    y, S = ops.gdn_prefill(g["q"], g["k"], g["v"], g["la"], beta=g["beta"], output_final_state=True, out_dtype=torch.float32, impl=impl)
     check(y, y_o, "y cfg1 row")
     check(S, S_o, "S_T cfg1 row")
 
 
-def test_cfg1_full_size_against_recurrent_kernel():
+@pytest.mark.parametrize("impl", VARIANTS)
+def test_cfg1_full_size_against_recurrent_kernel(impl):
     """Full configuration 1 (B=8, T=4096, H=8): the chunk kernel against the fp32 recurrent
     kernel (itself pinned to the oracle at 1e-5), same tolerance."""
     g = make_inputs(8, 4096, 8, 128, 128, seed=1000, dtype=torch.bfloat16, device="cuda")
-    y_c, S_c = ops.gdn_prefill(g["q"], g["k"], g["v"], g["la"], beta=g["beta"], output_final_state=True, out_dtype=torch.float32, impl="chunk")
+    y_c, S_c = ops.gdn_prefill(g["q"], g["k"], g["v"], g["la"], beta=g["beta"], output_final_state=True, out_dtype=torch.float32, impl=impl)
     y_r, S_r = ops.gdn_prefill(g["q"], g["k"], g["v"], g["la"], beta=g["beta"], output_final_state=True, out_dtype=torch.float32, impl="recurrent")
     for a, b_, what in ((y_c, y_r, "y"), (S_c, S_r, "S_T")):
         d = (a - b_).double()
@@ -128,10 +138,11 @@ def test_cfg1_full_size_against_recurrent_kernel():
     assert ops.device_status() == 0
 
 
-def test_deterministic():
+@pytest.mark.parametrize("impl", VARIANTS)
+def test_deterministic(impl):
     g = make_inputs(2, 256, 4, 128, 128, seed=3, dtype=torch.bfloat16, device="cuda")
-    y1, S1 = ops.gdn_prefill(g["q"], g["k"], g["v"], g["la"], beta=g["beta"], output_final_state=True)
-    y2, S2 = ops.gdn_prefill(g["q"], g["k"], g["v"], g["la"], beta=g["beta"], output_final_state=True)
+    y1, S1 = ops.gdn_prefill(g["q"], g["k"], g["v"], g["la"], beta=g["beta"], output_final_state=True, impl=impl)
+    y2, S2 = ops.gdn_prefill(g["q"], g["k"], g["v"], g["la"], beta=g["beta"], output_final_state=True, impl=impl)
     assert torch.equal(y1, y2) and torch.equal(S1, S2)
 
 
@@ -163,7 +174,7 @@ def test_value_dim_multiple_of_128(DV):
     S0 = torch.randn(2, 2, DV, 128, generator=torch.Generator().manual_seed(3)) * 0.2
     y_o, S_o = O.recurrence_c(*(np32(x[n]) for n in ("q", "k", "v", "la")), beta=np32(x["beta"]), s0=S0.numpy())
     g = {k: v.cuda() for k, v in x.items()}
-    assert ops.selected_impl(g["q"], g["k"], g["v"], g["la"], beta=g["beta"]) == "chunk"
+    assert ops.selected_impl(g["q"], g["k"], g["v"], g["la"], beta=g["beta"]) == "chunk_single"
     y, S = ops.gdn_prefill(g["q"], g["k"], g["v"], g["la"], beta=g["beta"], initial_state=S0.cuda(), output_final_state=True, out_dtype=torch.float32)
     check(y, y_o, f"y DV={DV}")
     check(S, S_o, f"S_T DV={DV}")
