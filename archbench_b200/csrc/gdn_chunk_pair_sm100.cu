@@ -15,14 +15,14 @@
 //                       fp16 copies of S, R and R diag(w) stay in tensor memory as the A operands
 //                       of their MMAs; the commits that the chain waits on cover only the MMAs on
 //                       its critical path (R before Y, S before the intra-chunk part of Y).
-//                       convert (warps 4-7): gates, K / Gamma Q / V -> fp16 in place,
-//                       W^T = K^T (T Gamma)^T and W -> fp16.
+//                       convert (warps 4-7): tile loads, gates, W^T = K^T (T Gamma)^T, W -> fp16.
 //                       output (warps 8-11): Y -> y through a staging tile and TMA stores.
+//                       Warps 4-11 together convert each chunk's k, q, v tiles to fp16 in place.
 //
 // Handoff: prep pipeline p writes its chunk into slot p with st.shared::cluster, fences the
 // writes for the async proxy and arrives (release, cluster scope) on the slot's full barrier in
-// the state CTA; the state CTA's chain hands the slot back by arriving on the pipeline's empty
-// barrier once the last MMA reading it has completed.  The prep CTA loads each chunk's k and q
+// the state CTA; the output warps hand the slot back by arriving on the pipeline's empty barrier
+// once the chunk's last MMA (the one that reads A) has completed.  The prep CTA loads each chunk's k and q
 // tiles with TMA and pulls its v tile into L2, so the state CTA's own tile loads (issued as soon
 // as the chunk two back has released their buffers) are L2 hits.
 //
@@ -52,7 +52,7 @@ constexpr uint32_t S_YS = S_PS + 2 * PS_BYTES;     // y staging tile
 constexpr uint32_t S_GS = S_YS + TILE;             // 2 gate slots: gamma[64], w[64], gamma_C
 constexpr uint32_t GSLOT = 3 * C;                  // floats per gate slot
 constexpr uint32_t S_BARS = S_GS + 2 * GSLOT * 4;
-constexpr uint32_t S_NBARS = 16;
+constexpr uint32_t S_NBARS = 22;
 
 // Prep CTA shared-memory map: pipeline p at p * P_STRIDE.
 constexpr uint32_t P_KQ = 0;                                  // KQ tile set, bf16 as loaded
@@ -77,7 +77,10 @@ static_assert(P_STRIDE % 1024 == 0 && P_ST % 1024 == 0, "swizzled tiles need 1 K
 // and RW16 hold two fp16 values per column.
 constexpr uint32_t COL_S = 0, COL_S16 = 128, COL_U = 192, COL_R16 = 256, COL_RW16 = 288, COL_Y = 320, COL_W = 448;
 
-enum SBar { SB_PF = 0, SB_KQR = 2, SB_KQF = 4, SB_WM = 6, SB_W16R = 7, SB_R = 8, SB_S = 9, SB_YF = 10, SB_YE = 12, SB_DRAIN = 14 };
+enum SBar {
+  SB_PF = 0, SB_KQR = 2, SB_KQF = 4, SB_KQE = 6, SB_CVS = 8, SB_CVD = 10,  // two buffers each
+  SB_WM = 12, SB_W16R = 13, SB_R = 14, SB_S = 15, SB_YF = 16, SB_YE = 18, SB_DRAIN = 20
+};
 enum PBar { PB_KQF = 0, PB_G = 2, PB_PE = 4, PB_DRAIN = 6 };
 
 struct Params {
@@ -147,7 +150,8 @@ __global__ void __launch_bounds__(NT, 1)
   }
   if (tid == 32) {
     if (rank == 0) {
-      for (int i = 0; i < (int)S_NBARS; ++i) ptx::mbar_init(&sbar[i], (i == SB_YE || i == SB_YE + 1) ? 4 : 1);
+      for (int i = 0; i < (int)S_NBARS; ++i)
+        ptx::mbar_init(&sbar[i], (i == SB_YE || i == SB_YE + 1) ? 4 : (i == SB_CVD || i == SB_CVD + 1) ? 8 : 1);
       ptx::prefetch_tensormap(&tm_y);
     } else {
       for (int i = 0; i < (int)P_NBARS; ++i) ptx::mbar_init(&pbar[i], 1);
@@ -218,12 +222,41 @@ __global__ void __launch_bounds__(NT, 1)
       *loads_issued = c + 1;
     };
     float* gslots = reinterpret_cast<float*>(sm + S_GS);
+    // This thread's share of the bf16 -> fp16 conversion in place, done by warps 4-11 together
+    // (`ht` = 0..255) between the convert-start and convert-done barriers of buffer c & 1: K (tiles
+    // 0, 2 of the k/q set), gamma-scaled Q (tiles 1, 3), V (two tiles).  Each warp then fences the
+    // tiles for the tensor core and arrives on convert-done.  Unrolled by four only: the kernel's
+    // instruction working set, not latency, is what limits it when many clusters share a GPC.
+    auto convert_tiles = [&](int c, int ht) {
+      const uint32_t kq_o = S_KQ + (c & 1) * KQ_BYTES, v_o = S_V + (c & 1) * V_BYTES;
+      const float* gs = gslots + (c & 1) * GSLOT;
+#pragma unroll 4
+      for (int j = 0; j < 12; ++j) {
+        const int i = ht + 256 * j;
+        const int tile = i >> 9;
+        uint8_t* base = tile < 4 ? sm + kq_o + tile * TILE : sm + v_o + (tile - 4) * TILE;
+        const int off = (i & 511) * 16;
+        const float sc = (tile == 1 || tile == 3) ? gs[off >> 7] : 1.f;
+        uint4 r = *reinterpret_cast<uint4*>(base + off);
+        __nv_bfloat162* b2 = reinterpret_cast<__nv_bfloat162*>(&r);
+        uint4 o;
+        uint32_t* o32 = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 f = __bfloat1622float2(b2[k]);
+          o32[k] = pack_h2(f.x * sc, f.y * sc);
+        }
+        *reinterpret_cast<uint4*>(base + off) = o;
+      }
+      ptx::fence_proxy_async_smem();
+      __syncwarp();
+      if ((threadIdx.x & 31) == 0) ptx::mbar_arrive(&sbar[SB_CVD + (c & 1)]);
+    };
 
     if (warp < 4) {
       // ----------------------------------- state chain -----------------------------------
       const bool leader = tid == 0;
       bool issued = false;
-      const uint32_t peer_pe0 = ptx::mapa_shared(ptx::smem_u32(&pbar[PB_PE]), 1u);
       {
         // Initial state: the caller's S_0 (first segment) or the combined state of the segments before.
         const float* src = nullptr;
@@ -244,22 +277,17 @@ __global__ void __launch_bounds__(NT, 1)
         }
         ptx::tc_wait_st();
       }
-      if (leader && nch > 0) {
-        issue_loads(0);
-        if (nch > 1) issue_loads(1);
-      }
 #pragma unroll 1
       for (int c = 0; c < nch; ++c) {
         const int s = c & 1;
         const uint32_t ph = (uint32_t)(c >> 1) & 1u;
         const uint32_t kq_o = S_KQ + s * KQ_BYTES, v_o = S_V + s * V_BYTES, ps_o = S_PS + s * PS_BYTES;
         const float* gs = gslots + s * GSLOT;
-        if (c > 0) {  // chunk c-1 done: its tile buffers and product slot are free
+        if (c > 0) {  // S(c-1) done: the tile buffers of chunk c-1 are free
           if (!gwait(SB_S, (uint32_t)(c - 1) & 1u, leader, 1, false)) break;
           if (leader) {
             issued = false;
-            if (c + 1 < nch) issue_loads(c + 1);
-            ptx::mbar_arrive_remote(peer_pe0 + 8u * (uint32_t)((c - 1) & 1));
+            ptx::mbar_arrive(&sbar[SB_KQE + ((c - 1) & 1)]);
           }
         }
         if (!gwait(SB_KQR + s, ph, leader, 1, false)) break;  // fp16 K, Gamma Q, V and the gates of chunk c
@@ -273,20 +301,25 @@ __global__ void __launch_bounds__(NT, 1)
             ptx::mma_f16_ss(tmem + COL_U, at(D_MN8K, v_o + k * 2048), at(D_K, ps_o + TILE + k * 32), ID_N64_AMN, k > 0);
           issued = true;
         }
-        // S -> S16 (fp16, tensor memory: the A operand of R and Y) and S <- gamma_C S, 32 columns at
-        // a time; no MMA in flight touches these columns.
-#pragma unroll 1
-        for (int c4 = 0; c4 < 4; ++c4) {
-          float v[32];
-          ptx::tmem_ld32(my + COL_S + c4 * 32, v);
+        // S -> S16 (fp16, tensor memory: the A operand of R and Y) and S <- gamma_C S, in two halves of
+        // 64 columns (two loads in flight per wait).  No MMA in flight touches these columns.
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          float sv[64];
+          ptx::tmem_ld32(my + COL_S + 64 * hf, *reinterpret_cast<float(*)[32]>(sv));
+          ptx::tmem_ld32(my + COL_S + 64 * hf + 32, *reinterpret_cast<float(*)[32]>(sv + 32));
           ptx::tc_wait_ld();
-          uint32_t hv[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) hv[i] = pack_h2(v[2 * i], v[2 * i + 1]);
-          ptx::tmem_st16(my + COL_S16 + c4 * 16, hv);
+          for (int c2 = 0; c2 < 2; ++c2) {
+            uint32_t hv[16];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] *= gC;
-          ptx::tmem_st32(my + COL_S + c4 * 32, v);
+            for (int i = 0; i < 16; ++i) hv[i] = pack_h2(sv[32 * c2 + 2 * i], sv[32 * c2 + 2 * i + 1]);
+            ptx::tmem_st16(my + COL_S16 + 32 * hf + 16 * c2, hv);
+          }
+#pragma unroll
+          for (int i = 0; i < 64; ++i) sv[i] *= gC;
+          ptx::tmem_st32(my + COL_S + 64 * hf, *reinterpret_cast<float(*)[32]>(sv));
+          ptx::tmem_st32(my + COL_S + 64 * hf + 32, *reinterpret_cast<float(*)[32]>(sv + 32));
         }
         ptx::tc_wait_st();
         ptx::tc_fence_before();
@@ -320,19 +353,25 @@ __global__ void __launch_bounds__(NT, 1)
         if (leader) issued = false;
         ptx::tc_fence_after();
         {
-          // R -> R16 and R diag(w) -> RW16 (fp16, tensor memory), 32 tokens at a time.
+          // R -> R16 and R diag(w) -> RW16 (fp16, tensor memory); both loads before the one wait.
           const float* w_s = gs + C;
-#pragma unroll 1
+          float rv[64];
+          ptx::tmem_ld32(my + COL_U, *reinterpret_cast<float(*)[32]>(rv));
+          ptx::tmem_ld32(my + COL_U + 32, *reinterpret_cast<float(*)[32]>(rv + 32));
+          ptx::tc_wait_ld();
+#pragma unroll
           for (int h2 = 0; h2 < 2; ++h2) {
-            float rv[32];
-            ptx::tmem_ld32(my + COL_U + 32 * h2, rv);
-            ptx::tc_wait_ld();
             uint32_t hv[16];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) hv[i] = pack_h2(rv[2 * i], rv[2 * i + 1]);
+            for (int i = 0; i < 16; ++i) hv[i] = pack_h2(rv[32 * h2 + 2 * i], rv[32 * h2 + 2 * i + 1]);
             ptx::tmem_st16(my + COL_R16 + 16 * h2, hv);
+          }
 #pragma unroll
-            for (int i = 0; i < 16; ++i) hv[i] = pack_h2(rv[2 * i] * w_s[32 * h2 + 2 * i], rv[2 * i + 1] * w_s[32 * h2 + 2 * i + 1]);
+          for (int h2 = 0; h2 < 2; ++h2) {
+            uint32_t hv[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              hv[i] = pack_h2(rv[32 * h2 + 2 * i] * w_s[32 * h2 + 2 * i], rv[32 * h2 + 2 * i + 1] * w_s[32 * h2 + 2 * i + 1]);
             ptx::tmem_st16(my + COL_RW16 + 16 * h2, hv);
           }
           ptx::tc_wait_st();
@@ -379,16 +418,24 @@ __global__ void __launch_bounds__(NT, 1)
       bool issued = false;
       float la0 = 0.f, la1 = 0.f, be0 = 0.f, be1 = 0.f;
       if (ww == 1 && nch > 0) load_gates(0, la0, la1, be0, be1);
+      if (leader && nch > 0) {
+        issue_loads(0);
+        if (nch > 1) issue_loads(1);
+      }
 #pragma unroll 1
       for (int c = 0; c < nch; ++c) {
         const int s = c & 1;
         const uint32_t ph = (uint32_t)(c >> 1) & 1u;
-        const uint32_t kq_o = S_KQ + s * KQ_BYTES, v_o = S_V + s * V_BYTES, ps_o = S_PS + s * PS_BYTES;
+        const uint32_t kq_o = S_KQ + s * KQ_BYTES, ps_o = S_PS + s * PS_BYTES;
         float* gs = gslots + s * GSLOT;
         float g0 = 0.f, g1 = 0.f, gC = 0.f;
         if (ww == 1) cumsum_gates(la0, la1, g0, g1, gC);
+        if (c >= 2) {  // S(c-2) done: buffers s (tiles and gate slot) are free for chunk c
+          if (!gwait(SB_KQE + s, (uint32_t)((c - 2) >> 1) & 1u, leader, 2, false)) break;
+          if (leader) issue_loads(c);
+        }
         if (!gwait(SB_KQF + s, ph, leader, 2, false)) break;  // k, q, v tiles of chunk c
-        if (ww == 1) {  // the gate slot of chunk c-2 was last read before S(c-2), which preceded these loads
+        if (ww == 1) {
           gs[lane] = expf(g0);
           gs[lane + 32] = expf(g1);
           gs[C + lane] = be0 * expf(gC - g0);
@@ -396,30 +443,10 @@ __global__ void __launch_bounds__(NT, 1)
           if (lane == 0) gs[2 * C] = expf(gC);
           if (c + 1 < nch) load_gates(c + 1, la0, la1, be0, be1);
         }
-        ptx::named_bar(2, 128);
-        // bf16 -> fp16 in place: K (tiles 0, 2 of the k/q set), gamma-scaled Q (tiles 1, 3), V (two
-        // tiles).  Unrolled by four only: the kernel's instruction working set, not latency, is
-        // what limits it when many clusters share a GPC.
-#pragma unroll 4
-        for (int j = 0; j < 24; ++j) {
-          const int i = wt + 128 * j;
-          const int tile = i >> 9;
-          uint8_t* base = tile < 4 ? sm + kq_o + tile * TILE : sm + v_o + (tile - 4) * TILE;
-          const int off = (i & 511) * 16;
-          const float sc = (tile == 1 || tile == 3) ? gs[off >> 7] : 1.f;
-          uint4 r = *reinterpret_cast<uint4*>(base + off);
-          __nv_bfloat162* b2 = reinterpret_cast<__nv_bfloat162*>(&r);
-          uint4 o;
-          uint32_t* o32 = reinterpret_cast<uint32_t*>(&o);
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const float2 f = __bfloat1622float2(b2[k]);
-            o32[k] = pack_h2(f.x * sc, f.y * sc);
-          }
-          *reinterpret_cast<uint4*>(base + off) = o;
-        }
-        ptx::fence_proxy_async_smem();
-        ptx::named_bar(2, 128);
+        ptx::named_bar(2, 128);                            // gate slot written
+        if (leader) ptx::mbar_arrive(&sbar[SB_CVS + s]);  // the output warps join the conversion
+        convert_tiles(c, wt);
+        if (!gwait(SB_CVD + s, ph, leader, 2, false)) break;
         if (leader) ptx::mbar_arrive(&sbar[SB_KQR + s]);
         // W^T = K^T (T Gamma)^T, after T Gamma has arrived and R(c-1) has read W16(c-1).
         if (!gwait(SB_PF + s, ph, leader, 2, true)) break;
@@ -455,13 +482,16 @@ __global__ void __launch_bounds__(NT, 1)
       }
     } else {
       // ------------------------------ output: Y -> y ---------------------------------------
+      // Iteration c: the output of chunk c-2, then the conversion of chunk c with the convert warps.
       const bool leader = tid == 256;
+      const uint32_t peer_pe0 = ptx::mapa_shared(ptx::smem_u32(&pbar[PB_PE]), 1u);
       constexpr int ROWS = (int)(TILE / (D * sizeof(TOut)));  // tokens per staging piece
       TOut* stage = reinterpret_cast<TOut*>(sm + S_YS);
-#pragma unroll 1
-      for (int c = 0; c < nch; ++c) {
+      auto epilogue = [&](int c) -> bool {
         const int s = c & 1;
-        if (!gwait(SB_YF + s, (uint32_t)(c >> 1) & 1u, leader, 3, false)) break;
+        if (!gwait(SB_YF + s, (uint32_t)(c >> 1) & 1u, leader, 3, false)) return false;
+        // Every MMA of chunk c is complete: its product slot goes back to the prep CTA.
+        if (leader) ptx::mbar_arrive_remote(peer_pe0 + 8u * (uint32_t)s);
         ptx::tc_fence_after();
         float yv[64];
         ptx::tmem_ld32(my + COL_Y + 64 * s, *reinterpret_cast<float(*)[32]>(yv));
@@ -485,7 +515,20 @@ __global__ void __launch_bounds__(NT, 1)
             ptx::bulk_commit();
           }
         }
-        if (leader) ptx::bulk_wait_read0();  // before the next chunk's first piece (ordered by the next gwait)
+        if (leader) ptx::bulk_wait_read0();  // before the next chunk's first piece
+        ptx::named_bar(3, 128);
+        return true;
+      };
+      bool ok = true;
+      int c = 0;
+#pragma unroll 1
+      for (; c < nch && ok; ++c) {
+        if (c >= 2) ok = epilogue(c - 2);
+        if (!ok || !gwait(SB_CVS + (c & 1), (uint32_t)(c >> 1) & 1u, leader, 3, false)) break;
+        convert_tiles(c, tid - 128);
+      }
+      if (ok && c == nch && !*abort_flag) {
+        for (int e = nch - 2 < 0 ? 0 : nch - 2; e < nch && ok; ++e) ok = epilogue(e);
       }
       if (leader) ptx::bulk_wait0();
     }
