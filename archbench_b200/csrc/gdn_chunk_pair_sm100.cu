@@ -116,6 +116,38 @@ __device__ __forceinline__ void cumsum_gates(float la0, float la1, float& g0, fl
   g1 = a1;
 }
 
+// This thread's share of the bf16 -> fp16 conversion in place of chunk c's tiles (buffer c & 1),
+// done by the state CTA's warps 4-11 together (`ht` = 0..255) between the convert-start and
+// convert-done barriers: K (tiles 0, 2 of the k/q set), gamma-scaled Q (tiles 1, 3), V (two
+// tiles).  Each warp then fences the tiles for the tensor core and arrives on convert-done
+// (`done`).  Not inlined, and unrolled by four only: the kernel's instruction working set, not
+// latency, is what limits it when many clusters share a GPC.
+__device__ __noinline__ void convert_share(uint8_t* sm, const float* gslots, uint64_t* done, int c, int ht) {
+  const uint32_t kq_o = S_KQ + (c & 1) * KQ_BYTES, v_o = S_V + (c & 1) * V_BYTES;
+  const float* gs = gslots + (c & 1) * GSLOT;
+#pragma unroll 4
+  for (int j = 0; j < 12; ++j) {
+    const int i = ht + 256 * j;
+    const int tile = i >> 9;
+    uint8_t* base = tile < 4 ? sm + kq_o + tile * TILE : sm + v_o + (tile - 4) * TILE;
+    const int off = (i & 511) * 16;
+    const float sc = (tile == 1 || tile == 3) ? gs[off >> 7] : 1.f;
+    uint4 r = *reinterpret_cast<uint4*>(base + off);
+    __nv_bfloat162* b2 = reinterpret_cast<__nv_bfloat162*>(&r);
+    uint4 o;
+    uint32_t* o32 = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 f = __bfloat1622float2(b2[k]);
+      o32[k] = pack_h2(f.x * sc, f.y * sc);
+    }
+    *reinterpret_cast<uint4*>(base + off) = o;
+  }
+  ptx::fence_proxy_async_smem();
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) ptx::mbar_arrive(done);
+}
+
 template <typename TOut>
 __global__ void __launch_bounds__(NT, 1)
     pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -222,36 +254,7 @@ __global__ void __launch_bounds__(NT, 1)
       *loads_issued = c + 1;
     };
     float* gslots = reinterpret_cast<float*>(sm + S_GS);
-    // This thread's share of the bf16 -> fp16 conversion in place, done by warps 4-11 together
-    // (`ht` = 0..255) between the convert-start and convert-done barriers of buffer c & 1: K (tiles
-    // 0, 2 of the k/q set), gamma-scaled Q (tiles 1, 3), V (two tiles).  Each warp then fences the
-    // tiles for the tensor core and arrives on convert-done.  Unrolled by four only: the kernel's
-    // instruction working set, not latency, is what limits it when many clusters share a GPC.
-    auto convert_tiles = [&](int c, int ht) {
-      const uint32_t kq_o = S_KQ + (c & 1) * KQ_BYTES, v_o = S_V + (c & 1) * V_BYTES;
-      const float* gs = gslots + (c & 1) * GSLOT;
-#pragma unroll 4
-      for (int j = 0; j < 12; ++j) {
-        const int i = ht + 256 * j;
-        const int tile = i >> 9;
-        uint8_t* base = tile < 4 ? sm + kq_o + tile * TILE : sm + v_o + (tile - 4) * TILE;
-        const int off = (i & 511) * 16;
-        const float sc = (tile == 1 || tile == 3) ? gs[off >> 7] : 1.f;
-        uint4 r = *reinterpret_cast<uint4*>(base + off);
-        __nv_bfloat162* b2 = reinterpret_cast<__nv_bfloat162*>(&r);
-        uint4 o;
-        uint32_t* o32 = reinterpret_cast<uint32_t*>(&o);
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const float2 f = __bfloat1622float2(b2[k]);
-          o32[k] = pack_h2(f.x * sc, f.y * sc);
-        }
-        *reinterpret_cast<uint4*>(base + off) = o;
-      }
-      ptx::fence_proxy_async_smem();
-      __syncwarp();
-      if ((threadIdx.x & 31) == 0) ptx::mbar_arrive(&sbar[SB_CVD + (c & 1)]);
-    };
+    auto convert_tiles = [&](int c, int ht) { convert_share(sm, gslots, &sbar[SB_CVD + (c & 1)], c, ht); };
 
     if (warp < 4) {
       // ----------------------------------- state chain -----------------------------------
@@ -296,14 +299,14 @@ __global__ void __launch_bounds__(NT, 1)
         ptx::tc_fence_after();
         if (leader) {  // U^T = V^T T^T while the state is converted
           ptx::fence_proxy_async_smem();
-#pragma unroll
+#pragma unroll 1
           for (int k = 0; k < 4; ++k)
             ptx::mma_f16_ss(tmem + COL_U, at(D_MN8K, v_o + k * 2048), at(D_K, ps_o + TILE + k * 32), ID_N64_AMN, k > 0);
           issued = true;
         }
         // S -> S16 (fp16, tensor memory: the A operand of R and Y) and S <- gamma_C S, in two halves of
         // 64 columns (two loads in flight per wait).  No MMA in flight touches these columns.
-#pragma unroll
+#pragma unroll 1
         for (int hf = 0; hf < 2; ++hf) {
           float sv[64];
           ptx::tmem_ld32(my + COL_S + 64 * hf, *reinterpret_cast<float(*)[32]>(sv));
@@ -327,7 +330,7 @@ __global__ void __launch_bounds__(NT, 1)
         bool r_ok = true;
         if (leader) {  // R^T = U^T - S W^T (committed alone), then Y = S (Gamma Q)^T
           ptx::tc_fence_after();
-#pragma unroll
+#pragma unroll 1
           for (int k = 0; k < 8; ++k)
             ptx::mma_f16_ts(tmem + COL_U, tmem + COL_S16 + 8 * k, at(D_K, S_W + k * 2048), ID_N64_BMN_NEG, 1);
           ptx::mma_commit(&sbar[SB_R]);
@@ -336,7 +339,7 @@ __global__ void __launch_bounds__(NT, 1)
             if (!r_ok) raise_abort();
           }
           if (r_ok) {
-#pragma unroll
+#pragma unroll 1
             for (int k = 0; k < 8; ++k)
               ptx::mma_f16_ts(tmem + COL_Y + 64 * s, tmem + COL_S16 + 8 * k,
                               at(D_K, kq_o + TILE + (k >> 2) * 2 * TILE + (k & 3) * 32), ID_N64, k > 0);
@@ -380,11 +383,11 @@ __global__ void __launch_bounds__(NT, 1)
         ptx::named_bar(1, 128);
         if (leader) {  // S += (R diag w)^T K (committed alone), then Y += R^T A^T
           ptx::tc_fence_after();
-#pragma unroll
+#pragma unroll 1
           for (int k = 0; k < 4; ++k)
             ptx::mma_f16_ts(tmem + COL_S, tmem + COL_RW16 + 8 * k, at(D_MN16K, kq_o + k * 2048), ID_N128_BMN, 1);
           ptx::mma_commit(&sbar[SB_S]);
-#pragma unroll
+#pragma unroll 1
           for (int k = 0; k < 4; ++k)
             ptx::mma_f16_ts(tmem + COL_Y + 64 * s, tmem + COL_R16 + 8 * k, at(D_K, ps_o + k * 32), ID_N64, 1);
           ptx::mma_commit(&sbar[SB_YF + s]);
@@ -454,7 +457,7 @@ __global__ void __launch_bounds__(NT, 1)
         if (leader) {
           ptx::fence_proxy_async_smem();
           ptx::tc_fence_after();
-#pragma unroll
+#pragma unroll 1
           for (int k = 0; k < 4; ++k)
             ptx::mma_f16_ss(tmem + COL_W, at(D_MN16K, kq_o + k * 2048), at(D_K, ps_o + 2 * TILE + k * 32), ID_N64_AMN,
                             k > 0);
@@ -519,16 +522,15 @@ __global__ void __launch_bounds__(NT, 1)
         ptx::named_bar(3, 128);
         return true;
       };
-      bool ok = true;
-      int c = 0;
+      // One call site each (a smaller instruction working set): iterations nch and nch + 1 only
+      // drain the last two outputs.
 #pragma unroll 1
-      for (; c < nch && ok; ++c) {
-        if (c >= 2) ok = epilogue(c - 2);
-        if (!ok || !gwait(SB_CVS + (c & 1), (uint32_t)(c >> 1) & 1u, leader, 3, false)) break;
-        convert_tiles(c, tid - 128);
-      }
-      if (ok && c == nch && !*abort_flag) {
-        for (int e = nch - 2 < 0 ? 0 : nch - 2; e < nch && ok; ++e) ok = epilogue(e);
+      for (int c = 0; c < nch + 2; ++c) {
+        if (c >= 2 && !epilogue(c - 2)) break;
+        if (c < nch) {
+          if (!gwait(SB_CVS + (c & 1), (uint32_t)(c >> 1) & 1u, leader, 3, false)) break;
+          convert_tiles(c, tid - 128);
+        }
       }
       if (leader) ptx::bulk_wait0();
     }
@@ -576,7 +578,7 @@ __global__ void __launch_bounds__(NT, 1)
         if (!gwait(PB_KQF + pp, ph, false)) break;
         if (leader) {  // G = [K;Q] K^T from the bf16 tiles as loaded
           ptx::tc_fence_after();
-#pragma unroll
+#pragma unroll 1
           for (int kk = 0; kk < 8; ++kk) {
             const uint64_t a = at(D_K, base + P_KQ + (kk >> 2) * 2 * TILE + (kk & 3) * 32);
             ptx::mma_f16_ss(tmem + 64 * pp, a, a, ID_G, kk > 0);
