@@ -621,18 +621,17 @@ __global__ void __launch_bounds__(NT, 1)
         }
         if (pw == 1 && c + 2 < nch) load_gates(c + 2, la0, la1, be0, be1);
         ptx::tc_fence_after();
-        // Row pt of G: rows 0-63 give L (strictly lower), rows 64-127 give A (lower with diagonal).
+        // Row pt of G: rows 0-63 give L (strictly lower), rows 64-127 give A (lower with diagonal),
+        // one 16-column block at a time (a rolled loop: the prep's instruction working set matters
+        // more than the three extra tensor-memory round trips).
         {
-          float gv[64];
-          ptx::tmem_ld32(my + 64 * pp, *reinterpret_cast<float(*)[32]>(gv));
-          ptx::tmem_ld32(my + 64 * pp + 32, *reinterpret_cast<float(*)[32]>(gv + 32));
-          ptx::tc_wait_ld();
           const int t = pt & 63, tb = t >> 4;
           const bool is_l = pt < 64;
           const float et = eT[t];
-#pragma unroll
+#pragma unroll 1
           for (int jb = 0; jb < 4; ++jb) {
-            float e[16];
+            float gv[16], e[16];
+            ptx::tmem_ld16(my + 64 * pp + 16 * jb, gv);
             const float4* src4 = jb < tb ? reinterpret_cast<const float4*>(eJ + tb * C + 16 * jb)
                                          : reinterpret_cast<const float4*>(Ed + (tb * 16 + (t & 15)) * 20);
 #pragma unroll
@@ -641,38 +640,32 @@ __global__ void __launch_bounds__(NT, 1)
               e[4 * v] = f.x; e[4 * v + 1] = f.y; e[4 * v + 2] = f.z; e[4 * v + 3] = f.w;
             }
             const float sc = jb < tb ? et : (jb == tb ? 1.f : 0.f);
+            ptx::tc_wait_ld();
 #pragma unroll
             for (int jj = 0; jj < 16; ++jj) {
               float ej = e[jj] * sc;
               if (is_l && 16 * jb + jj == t) ej = 0.f;
-              gv[16 * jb + jj] *= ej;
+              gv[jj] *= ej;
             }
-          }
-          if (is_l) {
-            uint8_t* lrow = sm + base + P_L16 + t * LD16;
+            uint4 h0, h1;
+            h0.x = pack_h2(gv[0], gv[1]);   h0.y = pack_h2(gv[2], gv[3]);
+            h0.z = pack_h2(gv[4], gv[5]);   h0.w = pack_h2(gv[6], gv[7]);
+            h1.x = pack_h2(gv[8], gv[9]);   h1.y = pack_h2(gv[10], gv[11]);
+            h1.z = pack_h2(gv[12], gv[13]); h1.w = pack_h2(gv[14], gv[15]);
+            if (is_l) {
+              uint8_t* lrow = sm + base + P_L16 + t * LD16 + jb * 32;
+              *reinterpret_cast<uint4*>(lrow) = h0;
+              *reinterpret_cast<uint4*>(lrow + 16) = h1;
+              if (jb == tb) {  // the diagonal block also in fp32, for the substitution
+                float* drow = reinterpret_cast<float*>(sm + base + P_LDIAG) + (tb * 16 + (t & 15)) * LDG;
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              uint4 v4;
-              v4.x = pack_h2(gv[q * 8 + 0], gv[q * 8 + 1]);
-              v4.y = pack_h2(gv[q * 8 + 2], gv[q * 8 + 3]);
-              v4.z = pack_h2(gv[q * 8 + 4], gv[q * 8 + 5]);
-              v4.w = pack_h2(gv[q * 8 + 6], gv[q * 8 + 7]);
-              *reinterpret_cast<uint4*>(lrow + q * 16) = v4;
-            }
-            float* drow = reinterpret_cast<float*>(sm + base + P_LDIAG) + (tb * 16 + (t & 15)) * LDG;
-#pragma unroll
-            for (int q = 0; q < 16; q += 4) {
-              float4 f4;
-              switch (tb) {  // static register selection
-                case 0: f4 = make_float4(gv[q], gv[q + 1], gv[q + 2], gv[q + 3]); break;
-                case 1: f4 = make_float4(gv[16 + q], gv[17 + q], gv[18 + q], gv[19 + q]); break;
-                case 2: f4 = make_float4(gv[32 + q], gv[33 + q], gv[34 + q], gv[35 + q]); break;
-                default: f4 = make_float4(gv[48 + q], gv[49 + q], gv[50 + q], gv[51 + q]); break;
+                for (int q = 0; q < 16; q += 4)
+                  *reinterpret_cast<float4*>(drow + q) = make_float4(gv[q], gv[q + 1], gv[q + 2], gv[q + 3]);
               }
-              *reinterpret_cast<float4*>(drow + q) = f4;
+            } else {  // A16 row t, columns 16 jb .. 16 jb + 15
+              *reinterpret_cast<uint4*>(st + sw128((uint32_t)t, 2 * jb)) = h0;
+              *reinterpret_cast<uint4*>(st + sw128((uint32_t)t, 2 * jb + 1)) = h1;
             }
-          } else {
-            store_row_f16(st, (uint32_t)t, gv);  // A16 row t
           }
         }
         ptx::named_bar(1 + pp, 128);
