@@ -15,8 +15,9 @@
 //                       fp16 copies of S, R and R diag(w) stay in tensor memory as the A operands
 //                       of their MMAs; the commits that the chain waits on cover only the MMAs on
 //                       its critical path (R before Y, S before the intra-chunk part of Y).
-//                       convert (warps 4-7): tile loads, gates, W^T = K^T (T Gamma)^T, W -> fp16.
-//                       output (warps 8-11): Y -> y through a staging tile and TMA stores.
+//                       convert (warps 4-7): gates, W^T = K^T (T Gamma)^T, W -> fp16.
+//                       output (warps 8-11): Y -> y through a staging tile and TMA stores; issues
+//                       the tile loads a chunk ahead (three tile buffers).
 //                       Warps 4-11 together convert each chunk's k, q, v tiles to fp16 in place.
 //
 // Handoff: prep pipeline p writes its chunk into slot p with st.shared::cluster, fences the
@@ -42,17 +43,18 @@ constexpr long long WAIT_LIMIT = 4000000000LL;  // ~2 s of SM clocks
 constexpr uint32_t KQ_BYTES = 4 * TILE;  // [K0][Q0][K1][Q1]: features 0-63 and 64-127 of k and q
 constexpr uint32_t V_BYTES = 2 * TILE;   // [V0][V1]
 constexpr uint32_t PS_BYTES = 3 * TILE;  // product slot: [A16][T16][TG16]
+constexpr int NB = 3;                    // tile buffers of the state CTA: chunk c uses buffer c % NB
 
 // State CTA shared-memory map (bytes from a 1024-aligned base).
-constexpr uint32_t S_KQ = 0;                       // 2 x KQ: bf16 as loaded -> fp16 K, Gamma Q in place
-constexpr uint32_t S_V = S_KQ + 2 * KQ_BYTES;      // 2 x V: bf16 -> fp16 in place
-constexpr uint32_t S_W = S_V + 2 * V_BYTES;        // W16: DK rows x 64 tokens
+constexpr uint32_t S_KQ = 0;                       // NB x KQ: bf16 as loaded -> fp16 K, Gamma Q in place
+constexpr uint32_t S_V = S_KQ + NB * KQ_BYTES;     // NB x V: bf16 -> fp16 in place
+constexpr uint32_t S_W = S_V + NB * V_BYTES;       // W16: DK rows x 64 tokens
 constexpr uint32_t S_PS = S_W + 2 * TILE;          // 2 product slots, written by the prep CTA
 constexpr uint32_t S_YS = S_PS + 2 * PS_BYTES;     // y staging tile
-constexpr uint32_t S_GS = S_YS + TILE;             // 2 gate slots: gamma[64], w[64], gamma_C
+constexpr uint32_t S_GS = S_YS + TILE;             // NB gate slots: gamma[64], w[64], gamma_C
 constexpr uint32_t GSLOT = 3 * C;                  // floats per gate slot
-constexpr uint32_t S_BARS = S_GS + 2 * GSLOT * 4;
-constexpr uint32_t S_NBARS = 22;
+constexpr uint32_t S_BARS = S_GS + NB * GSLOT * 4;
+constexpr uint32_t S_NBARS = 24;
 
 // Prep CTA shared-memory map: pipeline p at p * P_STRIDE.
 constexpr uint32_t P_KQ = 0;                                  // KQ tile set, bf16 as loaded
@@ -78,8 +80,9 @@ static_assert(P_STRIDE % 1024 == 0 && P_ST % 1024 == 0, "swizzled tiles need 1 K
 constexpr uint32_t COL_S = 0, COL_S16 = 128, COL_U = 192, COL_R16 = 256, COL_RW16 = 288, COL_Y = 320, COL_W = 448;
 
 enum SBar {
-  SB_PF = 0, SB_KQR = 2, SB_KQF = 4, SB_KQE = 6, SB_CVS = 8, SB_CVD = 10,  // two buffers each
-  SB_WM = 12, SB_W16R = 13, SB_R = 14, SB_S = 15, SB_YF = 16, SB_YE = 18, SB_DRAIN = 20
+  SB_PF = 0,                                                       // per product slot (2)
+  SB_KQR = 2, SB_KQF = 5, SB_CVS = 8, SB_CVD = 11,                 // per tile buffer (NB)
+  SB_WM = 14, SB_W16R = 15, SB_R = 16, SB_S = 17, SB_YF = 18, SB_YE = 20, SB_DRAIN = 22  // YF, YE, DRAIN: 2
 };
 enum PBar { PB_KQF = 0, PB_G = 2, PB_PE = 4, PB_DRAIN = 6 };
 
@@ -116,15 +119,15 @@ __device__ __forceinline__ void cumsum_gates(float la0, float la1, float& g0, fl
   g1 = a1;
 }
 
-// This thread's share of the bf16 -> fp16 conversion in place of chunk c's tiles (buffer c & 1),
+// This thread's share of the bf16 -> fp16 conversion in place of chunk c's tiles (buffer c % NB),
 // done by the state CTA's warps 4-11 together (`ht` = 0..255) between the convert-start and
 // convert-done barriers: K (tiles 0, 2 of the k/q set), gamma-scaled Q (tiles 1, 3), V (two
 // tiles).  Each warp then fences the tiles for the tensor core and arrives on convert-done
 // (`done`).  Not inlined, and unrolled by four only: the kernel's instruction working set, not
 // latency, is what limits it when many clusters share a GPC.
 __device__ __noinline__ void convert_share(uint8_t* sm, const float* gslots, uint64_t* done, int c, int ht) {
-  const uint32_t kq_o = S_KQ + (c & 1) * KQ_BYTES, v_o = S_V + (c & 1) * V_BYTES;
-  const float* gs = gslots + (c & 1) * GSLOT;
+  const uint32_t kq_o = S_KQ + (c % NB) * KQ_BYTES, v_o = S_V + (c % NB) * V_BYTES;
+  const float* gs = gslots + (c % NB) * GSLOT;
 #pragma unroll 4
   for (int j = 0; j < 12; ++j) {
     const int i = ht + 256 * j;
@@ -183,7 +186,7 @@ __global__ void __launch_bounds__(NT, 1)
   if (tid == 32) {
     if (rank == 0) {
       for (int i = 0; i < (int)S_NBARS; ++i)
-        ptx::mbar_init(&sbar[i], (i == SB_YE || i == SB_YE + 1) ? 4 : (i == SB_CVD || i == SB_CVD + 1) ? 8 : 1);
+        ptx::mbar_init(&sbar[i], (i == SB_YE || i == SB_YE + 1) ? 4 : (i >= SB_CVD && i < SB_CVD + NB) ? 8 : 1);
       ptx::prefetch_tensormap(&tm_y);
     } else {
       for (int i = 0; i < (int)P_NBARS; ++i) ptx::mbar_init(&pbar[i], 1);
@@ -241,10 +244,11 @@ __global__ void __launch_bounds__(NT, 1)
       }
       return !ptx::named_bar_or(group, 128, fail);
     };
-    // k, q and v tiles of chunk c into buffer c & 1 (one thread; the buffer's previous chunk, c - 2,
-    // has completed).  One barrier per buffer, expecting both tile sets.
+    // k, q and v tiles of chunk c into buffer c % NB (one thread of the output warps; every MMA of
+    // the buffer's previous chunk, c - NB, has completed).  One barrier per buffer, expecting both
+    // tile sets.
     auto issue_loads = [&](int c) {
-      const int s = c & 1;
+      const int s = c % NB;
       uint64_t* bar = &sbar[SB_KQF + s];
       ptx::mbar_arrive_expect_tx(bar, KQ_BYTES + V_BYTES);
       issue_kq(sm + S_KQ + s * KQ_BYTES, bar, c);
@@ -254,7 +258,7 @@ __global__ void __launch_bounds__(NT, 1)
       *loads_issued = c + 1;
     };
     float* gslots = reinterpret_cast<float*>(sm + S_GS);
-    auto convert_tiles = [&](int c, int ht) { convert_share(sm, gslots, &sbar[SB_CVD + (c & 1)], c, ht); };
+    auto convert_tiles = [&](int c, int ht) { convert_share(sm, gslots, &sbar[SB_CVD + c % NB], c, ht); };
 
     if (warp < 4) {
       // ----------------------------------- state chain -----------------------------------
@@ -282,19 +286,16 @@ __global__ void __launch_bounds__(NT, 1)
       }
 #pragma unroll 1
       for (int c = 0; c < nch; ++c) {
-        const int s = c & 1;
-        const uint32_t ph = (uint32_t)(c >> 1) & 1u;
-        const uint32_t kq_o = S_KQ + s * KQ_BYTES, v_o = S_V + s * V_BYTES, ps_o = S_PS + s * PS_BYTES;
-        const float* gs = gslots + s * GSLOT;
-        if (c > 0) {  // S(c-1) done: the tile buffers of chunk c-1 are free
+        const int s = c & 1, tb = c % NB;  // product slot and Y buffer; tile buffer
+        const uint32_t ph = (uint32_t)(c >> 1) & 1u, tph = (uint32_t)(c / NB) & 1u;
+        const uint32_t kq_o = S_KQ + tb * KQ_BYTES, v_o = S_V + tb * V_BYTES, ps_o = S_PS + s * PS_BYTES;
+        const float* gs = gslots + tb * GSLOT;
+        if (c > 0) {  // S(c-1) done
           if (!gwait(SB_S, (uint32_t)(c - 1) & 1u, leader, 1, false)) break;
-          if (leader) {
-            issued = false;
-            ptx::mbar_arrive(&sbar[SB_KQE + ((c - 1) & 1)]);
-          }
+          if (leader) issued = false;
         }
-        if (!gwait(SB_KQR + s, ph, leader, 1, false)) break;  // fp16 K, Gamma Q, V and the gates of chunk c
-        if (!gwait(SB_PF + s, ph, leader, 1, true)) break;    // A, T, T Gamma of chunk c from the prep CTA
+        if (!gwait(SB_KQR + tb, tph, leader, 1, false)) break;  // fp16 K, Gamma Q, V and the gates of chunk c
+        if (!gwait(SB_PF + s, ph, leader, 1, true)) break;      // A, T, T Gamma of chunk c from the prep CTA
         const float gC = gs[2 * C];
         ptx::tc_fence_after();
         if (leader) {  // U^T = V^T T^T while the state is converted
@@ -421,23 +422,15 @@ __global__ void __launch_bounds__(NT, 1)
       bool issued = false;
       float la0 = 0.f, la1 = 0.f, be0 = 0.f, be1 = 0.f;
       if (ww == 1 && nch > 0) load_gates(0, la0, la1, be0, be1);
-      if (leader && nch > 0) {
-        issue_loads(0);
-        if (nch > 1) issue_loads(1);
-      }
 #pragma unroll 1
       for (int c = 0; c < nch; ++c) {
-        const int s = c & 1;
-        const uint32_t ph = (uint32_t)(c >> 1) & 1u;
-        const uint32_t kq_o = S_KQ + s * KQ_BYTES, ps_o = S_PS + s * PS_BYTES;
-        float* gs = gslots + s * GSLOT;
+        const int s = c & 1, tb = c % NB;  // product slot; tile buffer
+        const uint32_t ph = (uint32_t)(c >> 1) & 1u, tph = (uint32_t)(c / NB) & 1u;
+        const uint32_t kq_o = S_KQ + tb * KQ_BYTES, ps_o = S_PS + s * PS_BYTES;
+        float* gs = gslots + tb * GSLOT;
         float g0 = 0.f, g1 = 0.f, gC = 0.f;
         if (ww == 1) cumsum_gates(la0, la1, g0, g1, gC);
-        if (c >= 2) {  // S(c-2) done: buffers s (tiles and gate slot) are free for chunk c
-          if (!gwait(SB_KQE + s, (uint32_t)((c - 2) >> 1) & 1u, leader, 2, false)) break;
-          if (leader) issue_loads(c);
-        }
-        if (!gwait(SB_KQF + s, ph, leader, 2, false)) break;  // k, q, v tiles of chunk c
+        if (!gwait(SB_KQF + tb, tph, leader, 2, false)) break;  // k, q, v tiles of chunk c
         if (ww == 1) {
           gs[lane] = expf(g0);
           gs[lane + 32] = expf(g1);
@@ -447,13 +440,13 @@ __global__ void __launch_bounds__(NT, 1)
           if (c + 1 < nch) load_gates(c + 1, la0, la1, be0, be1);
         }
         ptx::named_bar(2, 128);                            // gate slot written
-        if (leader) ptx::mbar_arrive(&sbar[SB_CVS + s]);  // the output warps join the conversion
+        if (leader) ptx::mbar_arrive(&sbar[SB_CVS + tb]);  // the output warps join the conversion
         convert_tiles(c, wt);
-        if (!gwait(SB_CVD + s, ph, leader, 2, false)) break;
-        if (leader) ptx::mbar_arrive(&sbar[SB_KQR + s]);
-        // W^T = K^T (T Gamma)^T, after T Gamma has arrived and R(c-1) has read W16(c-1).
+        if (!gwait(SB_CVD + tb, tph, leader, 2, false)) break;
+        if (leader) ptx::mbar_arrive(&sbar[SB_KQR + tb]);
+        // W^T = K^T (T Gamma)^T once T Gamma has arrived (the W columns were read out by this group
+        // for chunk c-1); W16 is rewritten only after R(c-1) has read it.
         if (!gwait(SB_PF + s, ph, leader, 2, true)) break;
-        if (c > 0 && !gwait(SB_R, (uint32_t)(c - 1) & 1u, leader, 2, false)) break;
         if (leader) {
           ptx::fence_proxy_async_smem();
           ptx::tc_fence_after();
@@ -464,6 +457,7 @@ __global__ void __launch_bounds__(NT, 1)
           ptx::mma_commit(&sbar[SB_WM]);
           issued = true;
         }
+        if (c > 0 && !gwait(SB_R, (uint32_t)(c - 1) & 1u, leader, 2, false)) break;
         if (!gwait(SB_WM, (uint32_t)c & 1u, leader, 2, false)) break;
         if (leader) issued = false;
         ptx::tc_fence_after();
@@ -493,8 +487,12 @@ __global__ void __launch_bounds__(NT, 1)
       auto epilogue = [&](int c) -> bool {
         const int s = c & 1;
         if (!gwait(SB_YF + s, (uint32_t)(c >> 1) & 1u, leader, 3, false)) return false;
-        // Every MMA of chunk c is complete: its product slot goes back to the prep CTA.
-        if (leader) ptx::mbar_arrive_remote(peer_pe0 + 8u * (uint32_t)s);
+        // Every MMA of chunk c is complete: its product slot goes back to the prep CTA and its tile
+        // buffer takes the loads of chunk c + NB.
+        if (leader) {
+          ptx::mbar_arrive_remote(peer_pe0 + 8u * (uint32_t)s);
+          if (c + NB < nch) issue_loads(c + NB);
+        }
         ptx::tc_fence_after();
         float yv[64];
         ptx::tmem_ld32(my + COL_Y + 64 * s, *reinterpret_cast<float(*)[32]>(yv));
@@ -524,11 +522,13 @@ __global__ void __launch_bounds__(NT, 1)
       };
       // One call site each (a smaller instruction working set): iterations nch and nch + 1 only
       // drain the last two outputs.
+      if (leader)
+        for (int c = 0; c < NB && c < nch; ++c) issue_loads(c);
 #pragma unroll 1
       for (int c = 0; c < nch + 2; ++c) {
         if (c >= 2 && !epilogue(c - 2)) break;
         if (c < nch) {
-          if (!gwait(SB_CVS + (c & 1), (uint32_t)(c >> 1) & 1u, leader, 3, false)) break;
+          if (!gwait(SB_CVS + c % NB, (uint32_t)(c / NB) & 1u, leader, 3, false)) break;
           convert_tiles(c, tid - 128);
         }
       }
@@ -717,8 +717,8 @@ __global__ void __launch_bounds__(NT, 1)
   __syncthreads();
   if (rank == 0 && tid == 0 && *abort_flag) {  // tile loads still in flight: the last one per buffer
     const int n = *loads_issued;
-    for (int c = n - 2 < 0 ? 0 : n - 2; c < n; ++c)
-      ptx::mbar_wait_bounded(&sbar[SB_KQF + (c & 1)], (uint32_t)(c >> 1) & 1u, WAIT_LIMIT);
+    for (int c = n - NB < 0 ? 0 : n - NB; c < n; ++c)
+      ptx::mbar_wait_bounded(&sbar[SB_KQF + c % NB], (uint32_t)(c / NB) & 1u, WAIT_LIMIT);
   }
   __syncwarp();
   ptx::cluster_sync();  // neither CTA leaves while the other may still write into it
