@@ -20,10 +20,12 @@
 //                       the tile loads a chunk ahead (three tile buffers).
 //                       Warps 4-11 together convert each chunk's k, q, v tiles to fp16 in place.
 //
-// Handoff: prep pipeline p writes its chunk into slot p with st.shared::cluster, fences the
-// writes for the async proxy and arrives (release, cluster scope) on the slot's full barrier in
-// the state CTA; the output warps hand the slot back by arriving on the pipeline's empty barrier
-// once the chunk's last MMA (the one that reads A) has completed.  The prep CTA loads each chunk's k and q
+// Handoff: prep pipeline p stages its chunk's products locally (two staging buffers per pipeline)
+// and sends them into slot p of the state CTA with one asynchronous bulk copy that completes on
+// the slot's full barrier there; the output warps hand the slot back by arriving on the
+// pipeline's empty barrier once the chunk's last MMA (the one that reads A) has completed.  A
+// staging buffer is rewritten two pipeline chunks later, after the pipeline has seen the slot of
+// the chunk in between given back, so its copy has long completed.  The prep CTA loads each chunk's k and q
 // tiles with TMA and pulls its v tile into L2, so the state CTA's own tile loads (issued as soon
 // as the chunk two back has released their buffers) are L2 hits.
 //
@@ -58,8 +60,8 @@ constexpr uint32_t S_NBARS = 24;
 
 // Prep CTA shared-memory map: pipeline p at p * P_STRIDE.
 constexpr uint32_t P_KQ = 0;                                  // KQ tile set, bf16 as loaded
-constexpr uint32_t P_ST = P_KQ + KQ_BYTES;                    // staging [A16][T16][TG16]
-constexpr uint32_t P_L16 = P_ST + PS_BYTES;                   // 64 rows x LD16 bytes (diagonal blocks hold D_b)
+constexpr uint32_t P_ST = P_KQ + KQ_BYTES;                    // 2 staging buffers [A16][T16][TG16]
+constexpr uint32_t P_L16 = P_ST + 2 * PS_BYTES;               // 64 rows x LD16 bytes (diagonal blocks hold D_b)
 constexpr uint32_t P_LDIAG = P_L16 + 64 * LD16;               // 4 x 16 x LDG floats
 constexpr uint32_t P_EXPT = P_LDIAG + 4 * 16 * LDG * 4;       // decay tables: 64 + 4x64 + 4x16x20 floats
 constexpr uint32_t P_GS = P_EXPT + (64 + 4 * 64 + 4 * 16 * 20) * 4;  // beta[64], g[64], gamma[64]
@@ -68,8 +70,10 @@ constexpr uint32_t P_BARS = 2 * P_STRIDE;
 constexpr uint32_t P_NBARS = 8;
 
 constexpr uint32_t cmax(uint32_t a, uint32_t b) { return a > b ? a : b; }
-constexpr uint32_t CTRL = (cmax(S_BARS + S_NBARS * 8, P_BARS + P_NBARS * 8) + 15) / 16 * 16;  // tmem, abort, loads
-constexpr uint32_t TOTAL = CTRL + 16;
+// Control words: TMEM base, abort flag, tile loads issued (state), product slots seen by the chain
+// (state, per slot), product copies issued (written into the state CTA by the prep, per slot).
+constexpr uint32_t CTRL = (cmax(S_BARS + S_NBARS * 8, P_BARS + P_NBARS * 8) + 15) / 16 * 16;
+constexpr uint32_t TOTAL = CTRL + 32;
 constexpr uint32_t DYN = TOTAL + 1024;
 static_assert(DYN <= 232448, "shared memory budget");
 static_assert(S_V % 1024 == 0 && S_W % 1024 == 0 && S_PS % 1024 == 0, "swizzled tiles need 1 KB alignment");
@@ -196,6 +200,7 @@ __global__ void __launch_bounds__(NT, 1)
     ptx::prefetch_tensormap(&tm_v);
     *abort_flag = 0;
     *loads_issued = 0;
+    for (int i = 4; i < 8; ++i) reinterpret_cast<volatile int*>(sm + CTRL)[i] = 0;
     ptx::fence_mbar_init();
   }
   ptx::tc_fence_before();
@@ -296,6 +301,7 @@ __global__ void __launch_bounds__(NT, 1)
         }
         if (!gwait(SB_KQR + tb, tph, leader, 1, false)) break;  // fp16 K, Gamma Q, V and the gates of chunk c
         if (!gwait(SB_PF + s, ph, leader, 1, true)) break;      // A, T, T Gamma of chunk c from the prep CTA
+        if (leader) *reinterpret_cast<volatile int*>(sm + CTRL + 16 + 4 * s) = (c >> 1) + 1;
         const float gC = gs[2 * C];
         ptx::tc_fence_after();
         if (leader) {  // U^T = V^T T^T while the state is converted
@@ -542,7 +548,6 @@ __global__ void __launch_bounds__(NT, 1)
       const bool leader = pt == 0;
       const uint32_t base = pp * P_STRIDE;
       uint8_t* kq = sm + base + P_KQ;
-      uint8_t* st = sm + base + P_ST;
       float* eT = reinterpret_cast<float*>(sm + base + P_EXPT);  // [64]      exp(g_t - g_{16 floor(t/16)})
       float* eJ = eT + C;                                         // [4][64]   beta_j exp(g_{16b} - g_j), j < 16b
       float* Ed = eJ + 4 * C;                                     // [4][16][20] beta_{16b+c} exp(g_{16b+r} - g_{16b+c}), c <= r
@@ -550,6 +555,8 @@ __global__ void __launch_bounds__(NT, 1)
       float* g_s = beta_s + C;
       float* gam_s = g_s + C;
       const uint32_t remote_slot = ptx::mapa_shared(sb + S_PS + pp * PS_BYTES, 0u);
+      const uint32_t remote_copies = ptx::mapa_shared(sb + CTRL + 24 + 4 * pp, 0u);
+      int copies = 0;
       const uint32_t remote_pf = ptx::mapa_shared(ptx::smem_u32(&sbar[SB_PF + pp]), 0u);
       auto gwait = [&](int bar, uint32_t parity, bool cluster_scope) -> bool {
         bool fail = false;
@@ -575,6 +582,8 @@ __global__ void __launch_bounds__(NT, 1)
 #pragma unroll 1
       for (int c = pp; c < nch; c += 2, ++k) {
         const uint32_t ph = (uint32_t)k & 1u;
+        const uint32_t st_o = base + P_ST + (uint32_t)(k & 1) * PS_BYTES;
+        uint8_t* st = sm + st_o;
         if (!gwait(PB_KQF + pp, ph, false)) break;
         if (leader) {  // G = [K;Q] K^T from the bf16 tiles as loaded
           ptx::tc_fence_after();
@@ -687,21 +696,20 @@ __global__ void __launch_bounds__(NT, 1)
           for (int r = 0; r < 16; ++r) l16[(bb * 16 + r) * (LD16 / 2) + bb * 16 + j] = __float2half_rn(x[r]);
         }
         ptx::named_bar(1 + pp, 128);
-        merge_column_any<false>(pw, sb + base + P_L16, sb + base + P_ST + TILE, 0u, sb + base + P_ST + 2 * TILE, gam_s,
-                               lane);
+        merge_column_any<false>(pw, sb + base + P_L16, sb + st_o + TILE, 0u, sb + st_o + 2 * TILE, gam_s, lane);
+        ptx::fence_proxy_async_smem();  // the staged products, for the bulk copy
         // The slot this pipeline used two chunks ago must have been given back; the group wait
-        // (or the barrier) also orders the merges' and the rows' stores before the copy.
+        // (or the barrier) also orders every thread's staging stores before the copy.
         if (k > 0) {
           if (!gwait(PB_PE + pp, (uint32_t)(k - 1) & 1u, true)) break;
         } else {
           ptx::named_bar(1 + pp, 128);
         }
-#pragma unroll 4
-        for (int i = pt; i < (int)(PS_BYTES / 16); i += 128)
-          ptx::st_cluster_v4(remote_slot + (uint32_t)i * 16u, *reinterpret_cast<const uint4*>(st + i * 16));
-        ptx::fence_proxy_async_cluster();
-        ptx::named_bar(1 + pp, 128);
-        if (leader) ptx::mbar_arrive_remote(remote_pf);
+        if (leader) {
+          ptx::mbar_arrive_expect_tx_remote(remote_pf, PS_BYTES);
+          ptx::bulk_copy_to_cluster(remote_slot, st, PS_BYTES, remote_pf);
+          ptx::st_cluster_u32(remote_copies, (uint32_t)++copies);
+        }
       }
       if (*abort_flag && leader) {  // drain this pipeline's MMA and tile loads
         if (issued) {
@@ -721,7 +729,16 @@ __global__ void __launch_bounds__(NT, 1)
       ptx::mbar_wait_bounded(&sbar[SB_KQF + c % NB], (uint32_t)(c / NB) & 1u, WAIT_LIMIT);
   }
   __syncwarp();
-  ptx::cluster_sync();  // neither CTA leaves while the other may still write into it
+  ptx::cluster_sync();  // every remote store, arrive and copy of both CTAs has been issued
+  if (rank == 0 && tid == 0 && *abort_flag) {  // product copies still in flight into this CTA
+    for (int sl = 0; sl < 2; ++sl) {
+      const int issued_n = *reinterpret_cast<volatile int*>(sm + CTRL + 24 + 4 * sl);
+      for (int k = *reinterpret_cast<volatile int*>(sm + CTRL + 16 + 4 * sl); k < issued_n; ++k)
+        ptx::mbar_wait_bounded(&sbar[SB_PF + sl], (uint32_t)k & 1u, WAIT_LIMIT);
+    }
+  }
+  __syncwarp();
+  ptx::cluster_sync();  // neither CTA leaves while the other may still read from or write into it
   ptx::tc_fence_after();
   if (tid == 0 && *abort_flag) atomicExch(&g_status, GDN_ERR_TIMEOUT);
   if (warp == 0) ptx::tmem_dealloc(tmem, tmem_cols);

@@ -369,3 +369,25 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
 }
 }  // namespace ptx
 }  // namespace gdn
+
+namespace gdn {
+namespace ptx {
+// Arrive (release, cluster scope) on another CTA's mbarrier and raise its expected byte count.
+__device__ __forceinline__ void mbar_arrive_expect_tx_remote(uint32_t cluster_addr, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.release.cluster.shared::cluster.b64 _, [%0], %1;" ::"r"(cluster_addr),
+               "r"(bytes)
+               : "memory");
+}
+// Bulk copy (no tensor map, no multicast) from this CTA's shared memory into another CTA's shared
+// memory of the cluster; completes `bytes` on the destination CTA's mbarrier.  Addresses 16-byte
+// aligned, size a multiple of 16.
+__device__ __forceinline__ void bulk_copy_to_cluster(uint32_t dst_cluster, const void* src, uint32_t bytes,
+                                                     uint32_t mbar_cluster) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          dst_cluster),
+      "r"(smem_u32(src)), "r"(bytes), "r"(mbar_cluster)
+      : "memory");
+}
+}  // namespace ptx
+}  // namespace gdn
