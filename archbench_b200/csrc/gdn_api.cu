@@ -79,11 +79,20 @@ int chunk_variant(const gdn_prefill_args* a) {
   return (a->u == nullptr && gdn_chunk_pair_supported(a)) ? (int)GDN_IMPL_CHUNK_CLUSTER : (int)GDN_IMPL_CHUNK_SINGLE;
 }
 
+// The segmented path pays for a state pass over all but the last segment; it beats the cluster
+// kernel only when the sequences are so few that the cluster kernel leaves most SMs idle (fewer
+// than one (b, h) unit per 8 SMs).  Where the cluster kernel does not apply, the plan decides.
+bool segmented_preferred(const gdn_prefill_args* a, int sms) {
+  if (chunk_variant(a) != GDN_IMPL_CHUNK_CLUSTER) return true;
+  return a->B * a->H * 8 <= (int64_t)sms;
+}
+
 int select_impl(const gdn_prefill_args* a) {
   const bool chunk_ok = gdn_chunk_supported(a);
   int P = 0, L = 0;
   size_t need = 0;
   const bool seg_ok = chunk_ok && gdn_segmented_plan(a, plan_sms(), &P, &L, &need);
+  const bool seg_auto = seg_ok && segmented_preferred(a, plan_sms());
   const bool ws_ok = seg_ok && a->workspace != nullptr && a->workspace_bytes >= need;
   switch (a->impl) {
     case GDN_IMPL_CHUNK: return chunk_ok ? chunk_variant(a) : (int)GDN_ERR_UNSUPPORTED;
@@ -96,7 +105,7 @@ int select_impl(const gdn_prefill_args* a) {
       if (!seg_ok) return (int)GDN_ERR_UNSUPPORTED;
       return ws_ok ? (int)GDN_IMPL_SEGMENTED : (int)GDN_ERR_SHAPE;
     default:
-      if (ws_ok) return (int)GDN_IMPL_SEGMENTED;
+      if (ws_ok && seg_auto) return (int)GDN_IMPL_SEGMENTED;
       return chunk_ok ? chunk_variant(a) : (int)GDN_IMPL_RECURRENT;
   }
 }
@@ -149,8 +158,9 @@ int gdn_prefill_workspace_bytes(const gdn_prefill_args* a, size_t* bytes) {
   *bytes = 0;
   int P = 0, L = 0;
   size_t need = 0;
-  if ((a->impl == GDN_IMPL_AUTO || a->impl == GDN_IMPL_SEGMENTED) && a->T > 0 &&
-      gdn_segmented_plan(a, plan_sms(), &P, &L, &need))
+  if ((a->impl == GDN_IMPL_SEGMENTED || (a->impl == GDN_IMPL_AUTO && gdn_chunk_supported(a) &&
+                                           segmented_preferred(a, plan_sms()))) &&
+      a->T > 0 && gdn_segmented_plan(a, plan_sms(), &P, &L, &need))
     *bytes = need;
   return GDN_OK;
 }

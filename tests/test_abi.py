@@ -108,6 +108,20 @@ def test_workspace_query():
     assert status(a) == -2
 
 
+def test_cluster_kernel_preferred_over_segments_for_enough_sequences():
+    lib = ops.load_library()
+    n = ctypes.c_size_t(123)
+    # 32 (b, h) units on 148 SMs (configuration 3 on one GPU): the cluster kernel, no workspace
+    a = fake_args(shape=(1, 65536, 32, 128, 128))
+    assert lib.gdn_prefill_workspace_bytes(ctypes.byref(a), ctypes.byref(n)) == 0
+    assert n.value == 0
+    assert status(a) == 4
+    # the segmented path still plans when asked for explicitly
+    a.impl = 3
+    assert lib.gdn_prefill_workspace_bytes(ctypes.byref(a), ctypes.byref(n)) == 0
+    assert n.value > 0
+
+
 def test_status_strings():
     lib = ops.load_library()
     for s in range(-8, 1):
