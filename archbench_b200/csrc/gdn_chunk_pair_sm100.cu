@@ -52,9 +52,10 @@ constexpr uint32_t S_KQ = 0;                       // NB x KQ: bf16 as loaded ->
 constexpr uint32_t S_V = S_KQ + NB * KQ_BYTES;     // NB x V: bf16 -> fp16 in place
 constexpr uint32_t S_W = S_V + NB * V_BYTES;       // W16: DK rows x 64 tokens
 constexpr uint32_t S_PS = S_W + 2 * TILE;          // 2 product slots, written by the prep CTA
-constexpr uint32_t S_YS = S_PS + 2 * PS_BYTES;     // y staging tile
-constexpr uint32_t S_GS = S_YS + TILE;             // NB gate slots: gamma[64], w[64], gamma_C
-constexpr uint32_t GSLOT = 3 * C;                  // floats per gate slot
+constexpr uint32_t S_YS = S_PS + 2 * PS_BYTES;     // y staging: one bf16 chunk (or half an fp32 one)
+constexpr uint32_t YS_BYTES = 2 * TILE;
+constexpr uint32_t S_GS = S_YS + YS_BYTES;         // NB gate slots: gamma[64], w[64], gamma_C
+constexpr uint32_t GSLOT = 2 * C + 4;              // floats per gate slot
 constexpr uint32_t S_BARS = S_GS + NB * GSLOT * 4;
 constexpr uint32_t S_NBARS = 24;
 
@@ -80,7 +81,7 @@ static_assert(S_V % 1024 == 0 && S_W % 1024 == 0 && S_PS % 1024 == 0, "swizzled 
 static_assert(P_STRIDE % 1024 == 0 && P_ST % 1024 == 0, "swizzled tiles need 1 KB alignment");
 
 // TMEM columns of the state CTA (all 512) and of the prep CTA (128: G of each pipeline).  S16, R16
-// and RW16 hold two fp16 values per column.
+// and RW16 hold two fp16 values per column; Y has two buffers of 64.
 constexpr uint32_t COL_S = 0, COL_S16 = 128, COL_U = 192, COL_R16 = 256, COL_RW16 = 288, COL_Y = 320, COL_W = 448;
 
 enum SBar {
@@ -488,7 +489,7 @@ __global__ void __launch_bounds__(NT, 1)
       // Iteration c: the output of chunk c-2, then the conversion of chunk c with the convert warps.
       const bool leader = tid == 256;
       const uint32_t peer_pe0 = ptx::mapa_shared(ptx::smem_u32(&pbar[PB_PE]), 1u);
-      constexpr int ROWS = (int)(TILE / (D * sizeof(TOut)));  // tokens per staging piece
+      constexpr int ROWS = (int)(YS_BYTES / (D * sizeof(TOut)));  // tokens per staging piece
       TOut* stage = reinterpret_cast<TOut*>(sm + S_YS);
       auto epilogue = [&](int c) -> bool {
         const int s = c & 1;
@@ -509,10 +510,10 @@ __global__ void __launch_bounds__(NT, 1)
         if (lane == 0) ptx::mbar_arrive(&sbar[SB_YE + s]);
 #pragma unroll
         for (int piece = 0; piece < C / ROWS; ++piece) {  // unrolled: yv stays in registers
-          if (piece > 0) {  // the previous piece's bytes must have been read out first
-            if (leader) ptx::bulk_wait_read0();
-            ptx::named_bar(3, 128);
-          }
+          // The staging tile's previous store (the last chunk's, or the previous piece) must have
+          // been read out first.
+          if (leader) ptx::bulk_wait_read0();
+          ptx::named_bar(3, 128);
 #pragma unroll
           for (int j = 0; j < ROWS; ++j) store_as(stage + j * D + row, yv[piece * ROWS + j]);
           ptx::fence_proxy_async_smem();
@@ -522,8 +523,6 @@ __global__ void __launch_bounds__(NT, 1)
             ptx::bulk_commit();
           }
         }
-        if (leader) ptx::bulk_wait_read0();  // before the next chunk's first piece
-        ptx::named_bar(3, 128);
         return true;
       };
       // One call site each (a smaller instruction working set): iterations nch and nch + 1 only
@@ -748,7 +747,7 @@ template <typename TOut>
 int launch(const gdn_prefill_args* a, int nseg, int seg_len, const float* seg_s0, int ws_stride, cudaStream_t stream) {
   CUtensorMap mq, mk, mv, my;
   if (!make_map(&mq, a->q, a->DK, a, a->sq) || !make_map(&mk, a->k, a->DK, a, a->sk) ||
-      !make_map(&mv, a->v, a->DV, a, a->sv) || !make_store_map<TOut>(&my, a->y, a->DV, a, a->sy))
+      !make_map(&mv, a->v, a->DV, a, a->sv) || !make_store_map<TOut>(&my, a->y, a->DV, a, a->sy, YS_BYTES))
     return GDN_ERR_LAUNCH;
   auto kern = pair_kernel<TOut>;
   static bool attr_set = false;

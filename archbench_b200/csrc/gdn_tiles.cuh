@@ -251,16 +251,17 @@ inline bool make_map(CUtensorMap* m, const void* base, int64_t F, const gdn_pref
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// y [B][T][H][DV] -> 4-D store map (f, h, t, b), box 128 features x 1 x (8 KB / row bytes) tokens,
-// no swizzle.
+// y [B][T][H][DV] -> 4-D store map (f, h, t, b), box 128 features x 1 x (box_bytes / row bytes)
+// tokens, no swizzle.
 template <typename TOut>
-bool make_store_map(CUtensorMap* m, void* base, int64_t F, const gdn_prefill_args* a, const gdn_strides& s) {
+bool make_store_map(CUtensorMap* m, void* base, int64_t F, const gdn_prefill_args* a, const gdn_strides& s,
+                    uint32_t box_bytes = TILE) {
   auto fn = encode_fn();
   if (!fn) return false;
   constexpr int es = (int)sizeof(TOut);
   cuuint64_t dims[4] = {(cuuint64_t)F, (cuuint64_t)a->H, (cuuint64_t)a->T, (cuuint64_t)a->B};
   cuuint64_t strides[3] = {(cuuint64_t)s.h * es, (cuuint64_t)s.t * es, (cuuint64_t)s.b * es};
-  cuuint32_t box[4] = {(cuuint32_t)D, 1, (cuuint32_t)(TILE / (D * es)), 1};
+  cuuint32_t box[4] = {(cuuint32_t)D, 1, (cuuint32_t)(box_bytes / (D * es)), 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   return fn(m, es == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, dims, strides, box,
             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
