@@ -5,8 +5,9 @@
 // maps its entry state to S_out = S_in M_s + N_s.  Three passes, all on the stream:
 //   A. gdn_chunk_ws_sm100.cu in state mode over segments 0..P-2: N_s from S = 0 with the real
 //      v, M_s from S = I with v = 0 (one extra 128-row tile per (b, h, segment)); no y.
-//   B. combine_kernel: S_{s+1} = S_s M_s + N_s, s = 0..P-2, fp32 on CUDA cores, the 128 state
-//      rows split over CTAs (rows evolve independently), result written over N_s.
+//   B. combine_kernel: S_{s+1} = S_s M_s + N_s, s = 0..P-2, fp32 on CUDA cores, the state rows
+//      split over CTAs (rows evolve independently), M_s double-buffered in shared memory, result
+//      written over N_s.
 //   C. the chunk kernel in output mode over all P segments, segment s starting from S_s.
 // Workspace (caller-allocated): B*H*(P-1) slots of (DV + 128) x 128 fp32.
 // The reference computes the same recurrence sequentially (archbench/layers/nsgdn.py:408-417,
@@ -19,29 +20,59 @@ namespace gdn {
 namespace seg {
 
 constexpr int D = 128;
-constexpr int RB = 4;  // state rows per combine CTA
+constexpr int RB = 4;                                 // state rows per combine CTA
+constexpr uint32_t COMB_SMEM = 2u * D * D * 4u;       // two transition matrices M_s (64 KB each)
 
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(smem))),
+               "l"(gmem)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// S_{s+1} = S_s M_s + N_s for s = 0..nslots-1, RB state rows per CTA (rows evolve independently),
+// one thread per state column.  M_s is staged in shared memory by cp.async, the next step's copy
+// in flight while the current step computes: the chain of steps is bound by the step's own
+// arithmetic instead of by L2 latency.
 __global__ void __launch_bounds__(D) combine_kernel(float* __restrict__ ws, const float* __restrict__ s0, int DV,
                                                     int nslots, int rblocks) {
+  extern __shared__ __align__(16) float msm[];  // [2][D][D]
+  __shared__ float srow[RB][D];
   const int bh = blockIdx.x / rblocks, r0 = (blockIdx.x % rblocks) * RB;
   const int j = threadIdx.x;
-  __shared__ float srow[RB][D];
   float s[RB];
 #pragma unroll
   for (int r = 0; r < RB; ++r) s[r] = s0 ? s0[((int64_t)bh * DV + r0 + r) * D + j] : 0.f;
+  auto slot = [&](int t) { return ws + (int64_t)(bh * nslots + t) * (DV + D) * D; };
+  auto prefetch = [&](int t) {
+    const float* M = slot(t) + (int64_t)DV * D;
+    float* dst = msm + (t & 1) * D * D;
+#pragma unroll 4
+    for (int i = j; i < D * D / 4; i += D) cp_async16(dst + 4 * i, M + 4 * i);
+    cp_async_commit();
+  };
+  if (nslots > 0) prefetch(0);
 #pragma unroll 1
   for (int t = 0; t < nslots; ++t) {
-    float* mat = ws + (int64_t)(bh * nslots + t) * (DV + D) * D;
+    float* mat = slot(t);
 #pragma unroll
     for (int r = 0; r < RB; ++r) srow[r][j] = s[r];
-    __syncthreads();
     float acc[RB];
 #pragma unroll
     for (int r = 0; r < RB; ++r) acc[r] = mat[(int64_t)(r0 + r) * D + j];
-    const float* M = mat + (int64_t)DV * D;
+    if (t + 1 < nslots) {  // the buffer it fills was last read at step t - 1 (barrier below)
+      prefetch(t + 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();  // srow written; M_t copied by every thread
+    const float* M = msm + (t & 1) * D * D;
 #pragma unroll 8
     for (int k = 0; k < D; ++k) {
-      const float m = M[(int64_t)k * D + j];
+      const float m = M[k * D + j];
 #pragma unroll
       for (int r = 0; r < RB; ++r) acc[r] = fmaf(srow[r][k], m, acc[r]);
     }
@@ -103,7 +134,15 @@ static int launch_plan(const gdn_prefill_args* a, float* ws, size_t ws_bytes, in
   if (st != GDN_OK) return st;
   const int rblocks = (int)(a->DV / gdn::seg::RB);
   const int64_t grid = a->B * a->H * rblocks;
-  gdn::seg::combine_kernel<<<(unsigned)grid, gdn::seg::D, 0, stream>>>(ws, a->s0, (int)a->DV, P - 1, rblocks);
+  static bool attr_set = false;
+  if (!attr_set) {
+    if (cudaFuncSetAttribute(gdn::seg::combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)gdn::seg::COMB_SMEM) != cudaSuccess)
+      return GDN_ERR_LAUNCH;
+    attr_set = true;
+  }
+  gdn::seg::combine_kernel<<<(unsigned)grid, gdn::seg::D, gdn::seg::COMB_SMEM, stream>>>(ws, a->s0, (int)a->DV, P - 1,
+                                                                                          rblocks);
   if (cudaGetLastError() != cudaSuccess) return GDN_ERR_LAUNCH;
   return gdn_launch_chunk_ws_segments(a, 0, P, L, ws, P - 1, stream);
 }
