@@ -10,15 +10,17 @@
 //                       of L and A, T = (I + L)^-1 (fp32 16x16 diagonal blocks, fp16 mma.sync
 //                       block columns) and T Gamma.  A, T and T Gamma (fp16, 24 KB per chunk) go
 //                       straight into a product slot in the state CTA's shared memory.
-//   state CTA (rank 0)  chain (warps 0-3): U^T = V^T T^T, S -> fp16, R^T = U^T - S W^T,
-//                       Y = S (Gamma Q)^T, S <- gamma_C S + (R diag w)^T K, Y += R^T A^T.  The
-//                       fp16 copies of S, R and R diag(w) stay in tensor memory as the A operands
-//                       of their MMAs; the commits that the chain waits on cover only the MMAs on
-//                       its critical path (R before Y, S before the intra-chunk part of Y).
-//                       convert (warps 4-7): gates, W^T = K^T (T Gamma)^T, W -> fp16.
-//                       output (warps 8-11): Y -> y through a staging tile and TMA stores; issues
-//                       the tile loads a chunk ahead (three tile buffers).
-//                       Warps 4-11 together convert each chunk's k, q, v tiles to fp16 in place.
+//   state CTA (rank 0)  chain (warps 0-3): U^T = V^T T^T, S -> fp16, then one N = 128 MMA for
+//                       [R^T | Y] = [U^T | 0] - S [W | -Gamma Q]^T, S <- gamma_C S + (R diag w)^T K,
+//                       Y += R^T A^T.  The fp16 copies of S, R and R diag(w) stay in tensor memory
+//                       as the A operands of their MMAs; R and S are each committed alone.
+//                       convert (warps 4-7): gates, W^T = K^T (T Gamma)^T -> W16; issues the v tile
+//                       loads.
+//                       output (warps 8-11): Y -> y through a staging tile and TMA stores (and Y
+//                       zeroed for the next chunk), QT16 = (-Gamma Q)^T of the next chunk; issues
+//                       the k/q tile loads.  W16 and QT16, both with DK rows, sit side by side as
+//                       the B operand of the fused MMA.
+//                       Warps 4-11 together convert each chunk's k and v tiles to fp16 in place.
 //
 // Handoff: prep pipeline p stages its chunk's products locally (two staging buffers per pipeline)
 // and sends them into slot p of the state CTA with one asynchronous bulk copy that completes on
@@ -45,13 +47,14 @@ constexpr long long WAIT_LIMIT = 4000000000LL;  // ~2 s of SM clocks
 constexpr uint32_t KQ_BYTES = 4 * TILE;  // [K0][Q0][K1][Q1]: features 0-63 and 64-127 of k and q
 constexpr uint32_t V_BYTES = 2 * TILE;   // [V0][V1]
 constexpr uint32_t PS_BYTES = 3 * TILE;  // product slot: [A16][T16][TG16]
-constexpr int NB = 3;                    // tile buffers of the state CTA: chunk c uses buffer c % NB
+constexpr int NB = 3;                    // k/q tile buffers of the state CTA: chunk c uses buffer c % NB
+constexpr int NBV = 2;                   // v tile buffers: chunk c uses buffer c % NBV
 
 // State CTA shared-memory map (bytes from a 1024-aligned base).
-constexpr uint32_t S_KQ = 0;                       // NB x KQ: bf16 as loaded -> fp16 K, Gamma Q in place
-constexpr uint32_t S_V = S_KQ + NB * KQ_BYTES;     // NB x V: bf16 -> fp16 in place
-constexpr uint32_t S_W = S_V + NB * V_BYTES;       // W16: DK rows x 64 tokens
-constexpr uint32_t S_PS = S_W + 2 * TILE;          // 2 product slots, written by the prep CTA
+constexpr uint32_t S_KQ = 0;                       // NB x KQ: bf16 as loaded -> fp16 K in place (q stays bf16)
+constexpr uint32_t S_V = S_KQ + NB * KQ_BYTES;     // NBV x V: bf16 -> fp16 in place
+constexpr uint32_t S_WQ = S_V + NBV * V_BYTES;     // [W16 | QT16]: DK rows x 64 tokens each, 16 KB apart
+constexpr uint32_t S_PS = S_WQ + 4 * TILE;         // 2 product slots, written by the prep CTA
 constexpr uint32_t S_YS = S_PS + 2 * PS_BYTES;     // y staging: one bf16 chunk (or half an fp32 one)
 constexpr uint32_t YS_BYTES = 2 * TILE;
 constexpr uint32_t S_GS = S_YS + YS_BYTES;         // NB gate slots: gamma[64], w[64], gamma_C
@@ -71,23 +74,25 @@ constexpr uint32_t P_BARS = 2 * P_STRIDE;
 constexpr uint32_t P_NBARS = 8;
 
 constexpr uint32_t cmax(uint32_t a, uint32_t b) { return a > b ? a : b; }
-// Control words: TMEM base, abort flag, tile loads issued (state), product slots seen by the chain
-// (state, per slot), product copies issued (written into the state CTA by the prep, per slot).
+// Control words: TMEM base, abort flag, k/q and v tile loads issued (state), product slots seen by
+// the chain (state, per slot), product copies issued (written into the state CTA by the prep, per
+// slot).
 constexpr uint32_t CTRL = (cmax(S_BARS + S_NBARS * 8, P_BARS + P_NBARS * 8) + 15) / 16 * 16;
 constexpr uint32_t TOTAL = CTRL + 32;
 constexpr uint32_t DYN = TOTAL + 1024;
 static_assert(DYN <= 232448, "shared memory budget");
-static_assert(S_V % 1024 == 0 && S_W % 1024 == 0 && S_PS % 1024 == 0, "swizzled tiles need 1 KB alignment");
+static_assert(S_V % 1024 == 0 && S_WQ % 1024 == 0 && S_PS % 1024 == 0, "swizzled tiles need 1 KB alignment");
 static_assert(P_STRIDE % 1024 == 0 && P_ST % 1024 == 0, "swizzled tiles need 1 KB alignment");
 
 // TMEM columns of the state CTA (all 512) and of the prep CTA (128: G of each pipeline).  S16, R16
-// and RW16 hold two fp16 values per column; Y has two buffers of 64.
-constexpr uint32_t COL_S = 0, COL_S16 = 128, COL_U = 192, COL_R16 = 256, COL_RW16 = 288, COL_Y = 320, COL_W = 448;
+// and RW16 hold two fp16 values per column; Y follows U (the fused MMA's 128 output columns).
+constexpr uint32_t COL_S = 0, COL_S16 = 128, COL_U = 192, COL_Y = 256, COL_R16 = 320, COL_RW16 = 352, COL_W = 384;
 
 enum SBar {
   SB_PF = 0,                                                       // per product slot (2)
-  SB_KQR = 2, SB_KQF = 5, SB_CVS = 8, SB_CVD = 11,                 // per tile buffer (NB)
-  SB_WM = 14, SB_W16R = 15, SB_R = 16, SB_S = 17, SB_YF = 18, SB_YE = 20, SB_DRAIN = 22  // YF, YE, DRAIN: 2
+  SB_KQR = 2, SB_KQF = 5, SB_CVS = 8, SB_CVD = 11,                 // per k/q tile buffer (NB)
+  SB_VF = 14,                                                      // per v tile buffer (NBV)
+  SB_WM = 16, SB_W16R = 17, SB_R = 18, SB_S = 19, SB_YF = 20, SB_YE = 21, SB_DRAIN = 22  // DRAIN: 2
 };
 enum PBar { PB_KQF = 0, PB_G = 2, PB_PE = 4, PB_DRAIN = 6 };
 
@@ -124,22 +129,19 @@ __device__ __forceinline__ void cumsum_gates(float la0, float la1, float& g0, fl
   g1 = a1;
 }
 
-// This thread's share of the bf16 -> fp16 conversion in place of chunk c's tiles (buffer c % NB),
-// done by the state CTA's warps 4-11 together (`ht` = 0..255) between the convert-start and
-// convert-done barriers: K (tiles 0, 2 of the k/q set), gamma-scaled Q (tiles 1, 3), V (two
-// tiles).  Each warp then fences the tiles for the tensor core and arrives on convert-done
-// (`done`).  Not inlined, and unrolled by four only: the kernel's instruction working set, not
-// latency, is what limits it when many clusters share a GPC.
-__device__ __noinline__ void convert_share(uint8_t* sm, const float* gslots, uint64_t* done, int c, int ht) {
-  const uint32_t kq_o = S_KQ + (c % NB) * KQ_BYTES, v_o = S_V + (c % NB) * V_BYTES;
-  const float* gs = gslots + (c % NB) * GSLOT;
+// This thread's share of the bf16 -> fp16 conversion in place of chunk c's k tiles (buffer c % NB)
+// and v tiles (buffer c % NBV), done by the state CTA's warps 4-11 together (`ht` = 0..255)
+// between the convert-start and convert-done barriers.  Each warp then fences the tiles for the
+// tensor core and arrives on convert-done (`done`).  Not inlined, and unrolled by four only: the
+// kernel's instruction working set, not latency, is what limits it when many clusters share a GPC.
+__device__ __noinline__ void convert_share(uint8_t* sm, uint64_t* done, int c, int ht) {
+  const uint32_t kq_o = S_KQ + (c % NB) * KQ_BYTES, v_o = S_V + (c % NBV) * V_BYTES;
 #pragma unroll 4
-  for (int j = 0; j < 12; ++j) {
+  for (int j = 0; j < 8; ++j) {
     const int i = ht + 256 * j;
-    const int tile = i >> 9;
-    uint8_t* base = tile < 4 ? sm + kq_o + tile * TILE : sm + v_o + (tile - 4) * TILE;
+    const int tile = i >> 9;  // 0, 1: k features 0-63 / 64-127; 2, 3: v
+    uint8_t* base = tile < 2 ? sm + kq_o + tile * 2 * TILE : sm + v_o + (tile - 2) * TILE;
     const int off = (i & 511) * 16;
-    const float sc = (tile == 1 || tile == 3) ? gs[off >> 7] : 1.f;
     uint4 r = *reinterpret_cast<uint4*>(base + off);
     __nv_bfloat162* b2 = reinterpret_cast<__nv_bfloat162*>(&r);
     uint4 o;
@@ -147,7 +149,7 @@ __device__ __noinline__ void convert_share(uint8_t* sm, const float* gslots, uin
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const float2 f = __bfloat1622float2(b2[k]);
-      o32[k] = pack_h2(f.x * sc, f.y * sc);
+      o32[k] = pack_h2(f.x, f.y);
     }
     *reinterpret_cast<uint4*>(base + off) = o;
   }
@@ -176,6 +178,7 @@ __global__ void __launch_bounds__(NT, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + CTRL);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + CTRL + 4);
   volatile int* loads_issued = reinterpret_cast<volatile int*>(sm + CTRL + 8);
+  volatile int* v_loads_issued = reinterpret_cast<volatile int*>(sm + CTRL + 12);
   const uint32_t peer_abort = ptx::mapa_shared(sb + CTRL + 4, rank ^ 1u);
   // Abort here and in the other CTA of the cluster (idempotent).
   auto raise_abort = [&]() {
@@ -191,7 +194,7 @@ __global__ void __launch_bounds__(NT, 1)
   if (tid == 32) {
     if (rank == 0) {
       for (int i = 0; i < (int)S_NBARS; ++i)
-        ptx::mbar_init(&sbar[i], (i == SB_YE || i == SB_YE + 1) ? 4 : (i >= SB_CVD && i < SB_CVD + NB) ? 8 : 1);
+        ptx::mbar_init(&sbar[i], i == SB_YE ? 4 : i == SB_W16R ? 2 : (i >= SB_CVD && i < SB_CVD + NB) ? 8 : 1);
       ptx::prefetch_tensormap(&tm_y);
     } else {
       for (int i = 0; i < (int)P_NBARS; ++i) ptx::mbar_init(&pbar[i], 1);
@@ -201,6 +204,7 @@ __global__ void __launch_bounds__(NT, 1)
     ptx::prefetch_tensormap(&tm_v);
     *abort_flag = 0;
     *loads_issued = 0;
+    *v_loads_issued = 0;
     for (int i = 4; i < 8; ++i) reinterpret_cast<volatile int*>(sm + CTRL)[i] = 0;
     ptx::fence_mbar_init();
   }
@@ -219,7 +223,7 @@ __global__ void __launch_bounds__(NT, 1)
   constexpr uint32_t ID_G = ptx::idesc_bf16_f32(128, 64);
   constexpr uint32_t ID_N64 = ptx::idesc_f16_f32(128, 64, false, false, false);
   constexpr uint32_t ID_N64_AMN = ptx::idesc_f16_f32(128, 64, true, false, false);
-  constexpr uint32_t ID_N64_BMN_NEG = ptx::idesc_f16_f32(128, 64, false, true, true);
+  constexpr uint32_t ID_N128_BMN_NEG = ptx::idesc_f16_f32(128, 128, false, true, true);
   constexpr uint32_t ID_N128_BMN = ptx::idesc_f16_f32(128, 128, false, true, false);
 
   // la and beta of 64 tokens, two per lane (zero past the end of the sequence).
@@ -250,21 +254,36 @@ __global__ void __launch_bounds__(NT, 1)
       }
       return !ptx::named_bar_or(group, 128, fail);
     };
-    // k, q and v tiles of chunk c into buffer c % NB (one thread of the output warps; every MMA of
-    // the buffer's previous chunk, c - NB, has completed).  One barrier per buffer, expecting both
-    // tile sets.
+    // Several waits of one elected thread handed to its group with one reducing barrier: `fail`
+    // accumulates the waits (each a no-op once one has failed); agree() raises the abort and
+    // returns whether the whole group goes on.
+    auto lwait = [&](bool& fail, int bar, uint32_t parity) {
+      if (!fail) fail = !ptx::mbar_wait_abortable(&sbar[bar], parity, WAIT_LIMIT, abort_flag);
+    };
+    auto agree = [&](bool fail, bool leader, int group) -> bool {
+      if (leader && fail) raise_abort();
+      return !ptx::named_bar_or(group, 128, leader && fail);
+    };
+    // k and q tiles of chunk c into buffer c % NB (one thread of the output warps; every MMA of the
+    // buffer's previous chunk, c - NB, has completed).
     auto issue_loads = [&](int c) {
-      const int s = c % NB;
-      uint64_t* bar = &sbar[SB_KQF + s];
-      ptx::mbar_arrive_expect_tx(bar, KQ_BYTES + V_BYTES);
-      issue_kq(sm + S_KQ + s * KQ_BYTES, bar, c);
-      uint8_t* dst = sm + S_V + s * V_BYTES;
-      ptx::tma_load_4d(dst, &tm_v, bar, 0, h, (cb + c) * C, b);
-      ptx::tma_load_4d(dst + TILE, &tm_v, bar, 64, h, (cb + c) * C, b);
+      uint64_t* bar = &sbar[SB_KQF + c % NB];
+      ptx::mbar_arrive_expect_tx(bar, KQ_BYTES);
+      issue_kq(sm + S_KQ + (c % NB) * KQ_BYTES, bar, c);
       *loads_issued = c + 1;
     };
+    // v tiles of chunk c into buffer c % NBV (convert warps; the buffer's previous chunk's U MMA,
+    // covered by that chunk's R commit, has completed).
+    auto issue_v_loads = [&](int c) {
+      uint64_t* bar = &sbar[SB_VF + c % NBV];
+      uint8_t* dst = sm + S_V + (c % NBV) * V_BYTES;
+      ptx::mbar_arrive_expect_tx(bar, V_BYTES);
+      ptx::tma_load_4d(dst, &tm_v, bar, 0, h, (cb + c) * C, b);
+      ptx::tma_load_4d(dst + TILE, &tm_v, bar, 64, h, (cb + c) * C, b);
+      *v_loads_issued = c + 1;
+    };
     float* gslots = reinterpret_cast<float*>(sm + S_GS);
-    auto convert_tiles = [&](int c, int ht) { convert_share(sm, gslots, &sbar[SB_CVD + c % NB], c, ht); };
+    auto convert_tiles = [&](int c, int ht) { convert_share(sm, &sbar[SB_CVD + c % NB], c, ht); };
 
     if (warp < 4) {
       // ----------------------------------- state chain -----------------------------------
@@ -288,20 +307,30 @@ __global__ void __launch_bounds__(NT, 1)
           }
           ptx::tmem_st32(my + COL_S + c4 * 32, v);
         }
+        float z[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) z[i] = 0.f;
+        ptx::tmem_st32(my + COL_Y, z);  // the fused MMA accumulates Y onto zeros
+        ptx::tmem_st32(my + COL_Y + 32, z);
         ptx::tc_wait_st();
       }
 #pragma unroll 1
       for (int c = 0; c < nch; ++c) {
-        const int s = c & 1, tb = c % NB;  // product slot and Y buffer; tile buffer
+        const int s = c & 1, tb = c % NB;  // product slot; k/q tile buffer
         const uint32_t ph = (uint32_t)(c >> 1) & 1u, tph = (uint32_t)(c / NB) & 1u;
-        const uint32_t kq_o = S_KQ + tb * KQ_BYTES, v_o = S_V + tb * V_BYTES, ps_o = S_PS + s * PS_BYTES;
+        const uint32_t kq_o = S_KQ + tb * KQ_BYTES, v_o = S_V + (c % NBV) * V_BYTES, ps_o = S_PS + s * PS_BYTES;
         const float* gs = gslots + tb * GSLOT;
-        if (c > 0) {  // S(c-1) done
-          if (!gwait(SB_S, (uint32_t)(c - 1) & 1u, leader, 1, false)) break;
-          if (leader) issued = false;
+        {
+          // S(c-1) done; fp16 K and V and the gates of chunk c; A, T, T Gamma of chunk c from the
+          // prep CTA.
+          bool fail = false;
+          if (leader) {
+            if (c > 0) lwait(fail, SB_S, (uint32_t)(c - 1) & 1u);
+            lwait(fail, SB_KQR + tb, tph);
+            if (!fail) fail = !ptx::mbar_wait_abortable_cluster(&sbar[SB_PF + s], ph, WAIT_LIMIT, abort_flag);
+          }
+          if (!agree(fail, leader, 1)) break;
         }
-        if (!gwait(SB_KQR + tb, tph, leader, 1, false)) break;  // fp16 K, Gamma Q, V and the gates of chunk c
-        if (!gwait(SB_PF + s, ph, leader, 1, true)) break;      // A, T, T Gamma of chunk c from the prep CTA
         if (leader) *reinterpret_cast<volatile int*>(sm + CTRL + 16 + 4 * s) = (c >> 1) + 1;
         const float gC = gs[2 * C];
         ptx::tc_fence_after();
@@ -312,77 +341,59 @@ __global__ void __launch_bounds__(NT, 1)
             ptx::mma_f16_ss(tmem + COL_U, at(D_MN8K, v_o + k * 2048), at(D_K, ps_o + TILE + k * 32), ID_N64_AMN, k > 0);
           issued = true;
         }
-        // S -> S16 (fp16, tensor memory: the A operand of R and Y) and S <- gamma_C S, in two halves of
-        // 64 columns (two loads in flight per wait).  No MMA in flight touches these columns.
+        // S -> S16 (fp16, tensor memory: the A operand of the fused MMA) and S <- gamma_C S, in
+        // quarters of 32 columns (a short loop body: instruction fetch, not latency, limits this
+        // kernel when many clusters share a GPC).  No MMA in flight touches these columns.
 #pragma unroll 1
-        for (int hf = 0; hf < 2; ++hf) {
-          float sv[64];
-          ptx::tmem_ld32(my + COL_S + 64 * hf, *reinterpret_cast<float(*)[32]>(sv));
-          ptx::tmem_ld32(my + COL_S + 64 * hf + 32, *reinterpret_cast<float(*)[32]>(sv + 32));
+        for (int q4 = 0; q4 < 4; ++q4) {
+          float sv[32];
+          ptx::tmem_ld32(my + COL_S + 32 * q4, sv);
           ptx::tc_wait_ld();
+          uint32_t hv[16];
 #pragma unroll
-          for (int c2 = 0; c2 < 2; ++c2) {
-            uint32_t hv[16];
+          for (int i = 0; i < 16; ++i) hv[i] = pack_h2(sv[2 * i], sv[2 * i + 1]);
+          ptx::tmem_st16(my + COL_S16 + 16 * q4, hv);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) hv[i] = pack_h2(sv[32 * c2 + 2 * i], sv[32 * c2 + 2 * i + 1]);
-            ptx::tmem_st16(my + COL_S16 + 32 * hf + 16 * c2, hv);
-          }
-#pragma unroll
-          for (int i = 0; i < 64; ++i) sv[i] *= gC;
-          ptx::tmem_st32(my + COL_S + 64 * hf, *reinterpret_cast<float(*)[32]>(sv));
-          ptx::tmem_st32(my + COL_S + 64 * hf + 32, *reinterpret_cast<float(*)[32]>(sv + 32));
+          for (int i = 0; i < 32; ++i) sv[i] *= gC;
+          ptx::tmem_st32(my + COL_S + 32 * q4, sv);
         }
         ptx::tc_wait_st();
         ptx::tc_fence_before();
-        if (!gwait(SB_W16R, (uint32_t)c & 1u, leader, 1, false)) break;  // W16 of chunk c (also orders the stores)
-        bool r_ok = true;
-        if (leader) {  // R^T = U^T - S W^T (committed alone), then Y = S (Gamma Q)^T
-          ptx::tc_fence_after();
-#pragma unroll 1
-          for (int k = 0; k < 8; ++k)
-            ptx::mma_f16_ts(tmem + COL_U, tmem + COL_S16 + 8 * k, at(D_K, S_W + k * 2048), ID_N64_BMN_NEG, 1);
-          ptx::mma_commit(&sbar[SB_R]);
-          if (c >= 2) {  // Y[s] drained by the output warps
-            r_ok = ptx::mbar_wait_abortable(&sbar[SB_YE + s], (uint32_t)((c - 2) >> 1) & 1u, WAIT_LIMIT, abort_flag);
-            if (!r_ok) raise_abort();
-          }
-          if (r_ok) {
-#pragma unroll 1
-            for (int k = 0; k < 8; ++k)
-              ptx::mma_f16_ts(tmem + COL_Y + 64 * s, tmem + COL_S16 + 8 * k,
-                              at(D_K, kq_o + TILE + (k >> 2) * 2 * TILE + (k & 3) * 32), ID_N64, k > 0);
-          }
-        }
+        ptx::named_bar(1, 128);  // every chain warp's S16 stores are complete
         {
+          // [R^T | Y] = [U^T | 0] - S [W | -Gamma Q]^T, committed as R, once W16 and QT16 of chunk c
+          // are written and Y has been read out (and zeroed) by the output warps for chunk c-1.
           bool fail = false;
           if (leader) {
-            fail = !r_ok || !ptx::mbar_wait_abortable(&sbar[SB_R], (uint32_t)c & 1u, WAIT_LIMIT, abort_flag);
-            if (fail) raise_abort();
+            lwait(fail, SB_W16R, (uint32_t)c & 1u);
+            if (c >= 1) lwait(fail, SB_YE, (uint32_t)(c - 1) & 1u);
+            ptx::tc_fence_after();
+            if (!fail) {
+#pragma unroll 1
+              for (int k = 0; k < 8; ++k)
+                ptx::mma_f16_ts(tmem + COL_U, tmem + COL_S16 + 8 * k, at(D_MN16K, S_WQ + k * 2048), ID_N128_BMN_NEG, 1);
+              ptx::mma_commit(&sbar[SB_R]);
+              lwait(fail, SB_R, (uint32_t)c & 1u);
+            }
           }
-          if (ptx::named_bar_or(1, 128, fail)) break;
+          if (!agree(fail, leader, 1)) break;
         }
         if (leader) issued = false;
         ptx::tc_fence_after();
         {
-          // R -> R16 and R diag(w) -> RW16 (fp16, tensor memory); both loads before the one wait.
-          const float* w_s = gs + C;
-          float rv[64];
-          ptx::tmem_ld32(my + COL_U, *reinterpret_cast<float(*)[32]>(rv));
-          ptx::tmem_ld32(my + COL_U + 32, *reinterpret_cast<float(*)[32]>(rv + 32));
-          ptx::tc_wait_ld();
-#pragma unroll
+          // R -> R16 and R diag(w) -> RW16 (fp16, tensor memory), in halves of 32 tokens.
+#pragma unroll 1
           for (int h2 = 0; h2 < 2; ++h2) {
+            const float* w_s = gs + C + 32 * h2;
+            float rv[32];
+            ptx::tmem_ld32(my + COL_U + 32 * h2, rv);
+            ptx::tc_wait_ld();
             uint32_t hv[16];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) hv[i] = pack_h2(rv[32 * h2 + 2 * i], rv[32 * h2 + 2 * i + 1]);
+            for (int i = 0; i < 16; ++i) hv[i] = pack_h2(rv[2 * i], rv[2 * i + 1]);
             ptx::tmem_st16(my + COL_R16 + 16 * h2, hv);
-          }
 #pragma unroll
-          for (int h2 = 0; h2 < 2; ++h2) {
-            uint32_t hv[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i)
-              hv[i] = pack_h2(rv[32 * h2 + 2 * i] * w_s[32 * h2 + 2 * i], rv[32 * h2 + 2 * i + 1] * w_s[32 * h2 + 2 * i + 1]);
+            for (int i = 0; i < 16; ++i) hv[i] = pack_h2(rv[2 * i] * w_s[2 * i], rv[2 * i + 1] * w_s[2 * i + 1]);
             ptx::tmem_st16(my + COL_RW16 + 16 * h2, hv);
           }
           ptx::tc_wait_st();
@@ -397,13 +408,13 @@ __global__ void __launch_bounds__(NT, 1)
           ptx::mma_commit(&sbar[SB_S]);
 #pragma unroll 1
           for (int k = 0; k < 4; ++k)
-            ptx::mma_f16_ts(tmem + COL_Y + 64 * s, tmem + COL_R16 + 8 * k, at(D_K, ps_o + k * 32), ID_N64, 1);
-          ptx::mma_commit(&sbar[SB_YF + s]);
+            ptx::mma_f16_ts(tmem + COL_Y, tmem + COL_R16 + 8 * k, at(D_K, ps_o + k * 32), ID_N64, 1);
+          ptx::mma_commit(&sbar[SB_YF]);
           issued = true;
         }
       }
+      // The last Y MMA may still run after this wait: `issued` stays set for the abort drain.
       if (!*abort_flag && nch > 0 && gwait(SB_S, (uint32_t)(nch - 1) & 1u, leader, 1, false)) {
-        if (leader) issued = false;
         ptx::tc_fence_after();
         if (seg == p.nseg - 1 && p.s_out != nullptr) {
           float* dst = p.s_out + ((int64_t)bh * D + row) * D;
@@ -429,21 +440,30 @@ __global__ void __launch_bounds__(NT, 1)
       bool issued = false;
       float la0 = 0.f, la1 = 0.f, be0 = 0.f, be1 = 0.f;
       if (ww == 1 && nch > 0) load_gates(0, la0, la1, be0, be1);
+      if (leader)
+        for (int c = 0; c < NBV && c < nch; ++c) issue_v_loads(c);
 #pragma unroll 1
       for (int c = 0; c < nch; ++c) {
-        const int s = c & 1, tb = c % NB;  // product slot; tile buffer
+        const int s = c & 1, tb = c % NB;  // product slot; k/q tile buffer
         const uint32_t ph = (uint32_t)(c >> 1) & 1u, tph = (uint32_t)(c / NB) & 1u;
         const uint32_t kq_o = S_KQ + tb * KQ_BYTES, ps_o = S_PS + s * PS_BYTES;
         float* gs = gslots + tb * GSLOT;
         float g0 = 0.f, g1 = 0.f, gC = 0.f;
         if (ww == 1) cumsum_gates(la0, la1, g0, g1, gC);
-        if (!gwait(SB_KQF + tb, tph, leader, 2, false)) break;  // k, q, v tiles of chunk c
+        {
+          bool fail = false;  // k, q and v tiles of chunk c
+          if (leader) {
+            lwait(fail, SB_KQF + tb, tph);
+            lwait(fail, SB_VF + c % NBV, (uint32_t)(c / NBV) & 1u);
+          }
+          if (!agree(fail, leader, 2)) break;
+        }
         if (ww == 1) {
-          gs[lane] = expf(g0);
-          gs[lane + 32] = expf(g1);
-          gs[C + lane] = be0 * expf(gC - g0);
-          gs[C + lane + 32] = be1 * expf(gC - g1);
-          if (lane == 0) gs[2 * C] = expf(gC);
+          gs[lane] = __expf(g0);  // arguments are sums of log decays (<= 0)
+          gs[lane + 32] = __expf(g1);
+          gs[C + lane] = be0 * __expf(gC - g0);
+          gs[C + lane + 32] = be1 * __expf(gC - g1);
+          if (lane == 0) gs[2 * C] = __expf(gC);
           if (c + 1 < nch) load_gates(c + 1, la0, la1, be0, be1);
         }
         ptx::named_bar(2, 128);                            // gate slot written
@@ -452,7 +472,8 @@ __global__ void __launch_bounds__(NT, 1)
         if (!gwait(SB_CVD + tb, tph, leader, 2, false)) break;
         if (leader) ptx::mbar_arrive(&sbar[SB_KQR + tb]);
         // W^T = K^T (T Gamma)^T once T Gamma has arrived (the W columns were read out by this group
-        // for chunk c-1); W16 is rewritten only after R(c-1) has read it.
+        // for chunk c-1); W16 is rewritten only after the fused MMA of chunk c-1 has read it, which
+        // also frees the v buffer of chunk c-1 (its U MMA came first) for chunk c+1.
         if (!gwait(SB_PF + s, ph, leader, 2, true)) break;
         if (leader) {
           ptx::fence_proxy_async_smem();
@@ -464,16 +485,29 @@ __global__ void __launch_bounds__(NT, 1)
           ptx::mma_commit(&sbar[SB_WM]);
           issued = true;
         }
-        if (c > 0 && !gwait(SB_R, (uint32_t)(c - 1) & 1u, leader, 2, false)) break;
-        if (!gwait(SB_WM, (uint32_t)c & 1u, leader, 2, false)) break;
-        if (leader) issued = false;
-        ptx::tc_fence_after();
         {
-          float wv[64];
-          ptx::tmem_ld32(my + COL_W, *reinterpret_cast<float(*)[32]>(wv));
-          ptx::tmem_ld32(my + COL_W + 32, *reinterpret_cast<float(*)[32]>(wv + 32));
+          bool fail = false;  // the fused MMA of chunk c-1 (reader of W16 and of v buffer c+1) and W
+          if (leader) {
+            if (c > 0) {
+              lwait(fail, SB_R, (uint32_t)(c - 1) & 1u);
+              if (!fail && c + 1 < nch) issue_v_loads(c + 1);
+            }
+            lwait(fail, SB_WM, (uint32_t)c & 1u);
+            issued = false;
+          }
+          if (!agree(fail, leader, 2)) break;
+        }
+        ptx::tc_fence_after();
+#pragma unroll 1
+        for (int h2 = 0; h2 < 2; ++h2) {  // W16: row d, 64 tokens, in halves of 32
+          float wv[32];
+          ptx::tmem_ld32(my + COL_W + 32 * h2, wv);
           ptx::tc_wait_ld();
-          store_row_f16(sm + S_W, row, wv);  // W16: row d, 64 tokens
+#pragma unroll
+          for (int c4 = 0; c4 < 4; ++c4)
+            *reinterpret_cast<uint4*>(sm + S_WQ + sw128((uint32_t)row, (uint32_t)(4 * h2 + c4))) =
+                make_uint4(pack_h2(wv[8 * c4], wv[8 * c4 + 1]), pack_h2(wv[8 * c4 + 2], wv[8 * c4 + 3]),
+                           pack_h2(wv[8 * c4 + 4], wv[8 * c4 + 5]), pack_h2(wv[8 * c4 + 6], wv[8 * c4 + 7]));
         }
         ptx::fence_proxy_async_smem();
         ptx::tc_fence_before();
@@ -486,55 +520,88 @@ __global__ void __launch_bounds__(NT, 1)
       }
     } else {
       // ------------------------------ output: Y -> y ---------------------------------------
-      // Iteration c: the output of chunk c-2, then the conversion of chunk c with the convert warps.
+      // Iteration c: the conversion of chunk c + 1 (with the convert warps); Y of chunk c read out
+      // and zeroed for the fused MMA of chunk c + 1; that MMA's QT16 half; then chunk c's y stores,
+      // product slot and tile loads.  Iteration -1 only prepares chunk 0.
       const bool leader = tid == 256;
+      const int ow = (tid - 256) >> 5;
       const uint32_t peer_pe0 = ptx::mapa_shared(ptx::smem_u32(&pbar[PB_PE]), 1u);
       constexpr int ROWS = (int)(YS_BYTES / (D * sizeof(TOut)));  // tokens per staging piece
       TOut* stage = reinterpret_cast<TOut*>(sm + S_YS);
-      auto epilogue = [&](int c) -> bool {
-        const int s = c & 1;
-        if (!gwait(SB_YF + s, (uint32_t)(c >> 1) & 1u, leader, 3, false)) return false;
-        // Every MMA of chunk c is complete: its product slot goes back to the prep CTA and its tile
-        // buffer takes the loads of chunk c + NB.
-        if (leader) {
-          ptx::mbar_arrive_remote(peer_pe0 + 8u * (uint32_t)s);
-          if (c + NB < nch) issue_loads(c + NB);
-        }
-        ptx::tc_fence_after();
-        float yv[64];
-        ptx::tmem_ld32(my + COL_Y + 64 * s, *reinterpret_cast<float(*)[32]>(yv));
-        ptx::tmem_ld32(my + COL_Y + 64 * s + 32, *reinterpret_cast<float(*)[32]>(yv + 32));
-        ptx::tc_wait_ld();
-        ptx::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(&sbar[SB_YE + s]);
-#pragma unroll
-        for (int piece = 0; piece < C / ROWS; ++piece) {  // unrolled: yv stays in registers
-          // The staging tile's previous store (the last chunk's, or the previous piece) must have
-          // been read out first.
-          if (leader) ptx::bulk_wait_read0();
-          ptx::named_bar(3, 128);
-#pragma unroll
-          for (int j = 0; j < ROWS; ++j) store_as(stage + j * D + row, yv[piece * ROWS + j]);
-          ptx::fence_proxy_async_smem();
-          ptx::named_bar(3, 128);
-          if (leader) {
-            ptx::tma_store_4d(&tm_y, stage, 0, h, (cb + c) * C + piece * ROWS, b);
-            ptx::bulk_commit();
-          }
-        }
-        return true;
-      };
-      // One call site each (a smaller instruction working set): iterations nch and nch + 1 only
-      // drain the last two outputs.
       if (leader)
         for (int c = 0; c < NB && c < nch; ++c) issue_loads(c);
 #pragma unroll 1
-      for (int c = 0; c < nch + 2; ++c) {
-        if (c >= 2 && !epilogue(c - 2)) break;
-        if (c < nch) {
-          if (!gwait(SB_CVS + c % NB, (uint32_t)(c / NB) & 1u, leader, 3, false)) break;
-          convert_tiles(c, tid - 128);
+      for (int c = -1; c < nch; ++c) {
+        const int cn = c + 1;
+        if (cn < nch) {
+          if (!gwait(SB_CVS + cn % NB, (uint32_t)(cn / NB) & 1u, leader, 3, false)) break;
+          convert_tiles(cn, tid - 128);
+        }
+        float yv[64];
+        if (c >= 0) {
+          if (!gwait(SB_YF, (uint32_t)c & 1u, leader, 3, false)) break;  // every MMA of chunk c
+          ptx::tc_fence_after();
+          ptx::tmem_ld32(my + COL_Y, *reinterpret_cast<float(*)[32]>(yv));
+          ptx::tmem_ld32(my + COL_Y + 32, *reinterpret_cast<float(*)[32]>(yv + 32));
+          ptx::tc_wait_ld();
+          float z[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) z[j] = 0.f;
+          ptx::tmem_st32(my + COL_Y, z);
+          ptx::tmem_st32(my + COL_Y + 32, z);
+          ptx::tc_wait_st();
+          ptx::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) ptx::mbar_arrive(&sbar[SB_YE]);
+        }
+        if (cn < nch) {
+          // QT16 = (-Gamma Q)^T of chunk c + 1, DK rows x 64 tokens (the Y half of the fused MMA's B
+          // operand; its A-negation restores the sign), from the bf16 q tiles as loaded: each 8x8
+          // block is read by ldmatrix (a token per row), scaled, and written transposed by
+          // stmatrix.  Warp ow covers features 32 ow .. 32 ow + 31.  The fused MMA of chunk c, the
+          // last reader of QT16, has completed (YF of chunk c).
+          const float* gs = gslots + (cn % NB) * GSLOT;
+          const uint32_t qs = sb + S_KQ + (cn % NB) * KQ_BYTES + TILE, qd = sb + S_WQ + 2 * TILE;
+          const int m = lane >> 3, r8 = lane & 7;
+#pragma unroll 1
+          for (int it = 0; it < 8; ++it) {
+            const int fb = 4 * ow + (it >> 1), tb0 = 4 * (it & 1);  // feature block, first token block
+            uint32_t x[4];
+            ptx::ldsm_x4(qs + (uint32_t)(fb >> 3) * 2 * TILE + sw128((uint32_t)(8 * (tb0 + m) + r8), (uint32_t)(fb & 7)), x);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float ng = -gs[8 * (tb0 + i) + (lane >> 2)];
+              const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&x[i]));
+              x[i] = pack_h2(f.x * ng, f.y * ng);
+            }
+            ptx::stsm_x4_t(qd + sw128((uint32_t)(8 * fb + r8), (uint32_t)(tb0 + m)), x);
+          }
+          ptx::fence_proxy_async_smem();
+          ptx::named_bar(3, 128);
+          if (leader) ptx::mbar_arrive(&sbar[SB_W16R]);
+        }
+        if (c >= 0) {
+          // Chunk c's product slot goes back to the prep CTA and its tile buffer takes the loads of
+          // chunk c + NB.
+          if (leader) {
+            ptx::mbar_arrive_remote_relaxed(peer_pe0 + 8u * (uint32_t)(c & 1));
+            if (c + NB < nch) issue_loads(c + NB);
+          }
+#pragma unroll
+          for (int piece = 0; piece < C / ROWS; ++piece) {  // unrolled: yv stays in registers
+            // The staging tile's previous store (the last chunk's, or the previous piece) must have
+            // been read out first.
+            if (leader) ptx::bulk_wait_read0();
+            ptx::named_bar(3, 128);
+#pragma unroll
+            for (int j = 0; j < ROWS; ++j) store_as(stage + j * D + row, yv[piece * ROWS + j]);
+            ptx::fence_proxy_async_smem();
+            ptx::named_bar(3, 128);
+            if (leader) {
+              ptx::tma_store_4d(&tm_y, stage, 0, h, (cb + c) * C + piece * ROWS, b);
+              ptx::bulk_commit();
+            }
+          }
         }
       }
       if (leader) ptx::bulk_wait0();
@@ -723,9 +790,11 @@ __global__ void __launch_bounds__(NT, 1)
   ptx::tc_fence_before();
   __syncthreads();
   if (rank == 0 && tid == 0 && *abort_flag) {  // tile loads still in flight: the last one per buffer
-    const int n = *loads_issued;
+    const int n = *loads_issued, nv = *v_loads_issued;
     for (int c = n - NB < 0 ? 0 : n - NB; c < n; ++c)
       ptx::mbar_wait_bounded(&sbar[SB_KQF + c % NB], (uint32_t)(c / NB) & 1u, WAIT_LIMIT);
+    for (int c = nv - NBV < 0 ? 0 : nv - NBV; c < nv; ++c)
+      ptx::mbar_wait_bounded(&sbar[SB_VF + c % NBV], (uint32_t)(c / NBV) & 1u, WAIT_LIMIT);
   }
   __syncwarp();
   ptx::cluster_sync();  // every remote store, arrive and copy of both CTAs has been issued

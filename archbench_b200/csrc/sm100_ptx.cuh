@@ -282,6 +282,12 @@ __device__ __forceinline__ void st_cluster_u32(uint32_t addr, uint32_t v) {
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
+// Relaxed remote arrive: orders none of this thread's memory operations (a few cycles instead of a
+// few hundred).  For signals whose data was produced and consumed elsewhere, e.g. "every MMA that
+// read this buffer has completed", already established through another barrier.
+__device__ __forceinline__ void mbar_arrive_remote_relaxed(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
 // Phase test with acquire at cluster scope: for barriers that another CTA's writes complete.
 __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
