@@ -520,8 +520,8 @@ __global__ void __launch_bounds__(NT, 1)
       }
     } else {
       // ------------------------------ output: Y -> y ---------------------------------------
-      // Iteration c: the conversion of chunk c + 1 (with the convert warps); Y of chunk c read out
-      // and zeroed for the fused MMA of chunk c + 1; that MMA's QT16 half; then chunk c's y stores,
+      // Iteration c: the conversion of chunk c + 1 (with the convert warps); the QT16 half of chunk
+      // c + 1's fused MMA; Y of chunk c read out and zeroed for that MMA; then chunk c's y stores,
       // product slot and tile loads.  Iteration -1 only prepares chunk 0.
       const bool leader = tid == 256;
       const int ow = (tid - 256) >> 5;
@@ -536,6 +536,44 @@ __global__ void __launch_bounds__(NT, 1)
         if (cn < nch) {
           if (!gwait(SB_CVS + cn % NB, (uint32_t)(cn / NB) & 1u, leader, 3, false)) break;
           convert_tiles(cn, tid - 128);
+        }
+        if (cn < nch) {
+          // QT16 = (-Gamma Q)^T of chunk c + 1, DK rows x 64 tokens (the Y half of the fused MMA's B
+          // operand; its A-negation restores the sign), from the bf16 q tiles as loaded: each 8x8
+          // block is read by ldmatrix (a token per row), scaled, and written transposed by
+          // stmatrix.  Warp ow covers features 32 ow .. 32 ow + 31.  Built as soon as the fused MMA
+          // of chunk c, the last reader of QT16, has completed, before chunk c's Y is read out.
+          bool fail = false;
+          if (leader && c >= 0)
+            fail = !ptx::mbar_wait_abortable(&sbar[SB_R], (uint32_t)c & 1u, WAIT_LIMIT, abort_flag);
+          if (!agree(fail, leader, 3)) break;
+          const float* gs = gslots + (cn % NB) * GSLOT;
+          float ng[8];  // -gamma of the 8 tokens this lane scales: 8 j + lane / 4
+#pragma unroll
+          for (int j = 0; j < 8; ++j) ng[j] = -gs[8 * j + (lane >> 2)];
+          const uint32_t qs = sb + S_KQ + (cn % NB) * KQ_BYTES + TILE, qd = sb + S_WQ + 2 * TILE;
+          const int m = lane >> 3, r8 = lane & 7;
+#pragma unroll 1
+          for (int fq = 0; fq < 4; ++fq) {
+            const int fb = 4 * ow + fq;  // feature block
+            const uint32_t src = qs + (uint32_t)(fb >> 3) * 2 * TILE;
+            uint32_t x[2][4];
+#pragma unroll
+            for (int hb = 0; hb < 2; ++hb)  // token blocks 4 hb .. 4 hb + 3
+              ptx::ldsm_x4(src + sw128((uint32_t)(8 * (4 * hb + m) + r8), (uint32_t)(fb & 7)), x[hb]);
+#pragma unroll
+            for (int hb = 0; hb < 2; ++hb) {
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&x[hb][i]));
+                x[hb][i] = pack_h2(f.x * ng[4 * hb + i], f.y * ng[4 * hb + i]);
+              }
+              ptx::stsm_x4_t(qd + sw128((uint32_t)(8 * fb + r8), (uint32_t)(4 * hb + m)), x[hb]);
+            }
+          }
+          ptx::fence_proxy_async_smem();
+          ptx::named_bar(3, 128);
+          if (leader) ptx::mbar_arrive(&sbar[SB_W16R]);
         }
         float yv[64];
         if (c >= 0) {
@@ -553,32 +591,6 @@ __global__ void __launch_bounds__(NT, 1)
           ptx::tc_fence_before();
           __syncwarp();
           if (lane == 0) ptx::mbar_arrive(&sbar[SB_YE]);
-        }
-        if (cn < nch) {
-          // QT16 = (-Gamma Q)^T of chunk c + 1, DK rows x 64 tokens (the Y half of the fused MMA's B
-          // operand; its A-negation restores the sign), from the bf16 q tiles as loaded: each 8x8
-          // block is read by ldmatrix (a token per row), scaled, and written transposed by
-          // stmatrix.  Warp ow covers features 32 ow .. 32 ow + 31.  The fused MMA of chunk c, the
-          // last reader of QT16, has completed (YF of chunk c).
-          const float* gs = gslots + (cn % NB) * GSLOT;
-          const uint32_t qs = sb + S_KQ + (cn % NB) * KQ_BYTES + TILE, qd = sb + S_WQ + 2 * TILE;
-          const int m = lane >> 3, r8 = lane & 7;
-#pragma unroll 1
-          for (int it = 0; it < 8; ++it) {
-            const int fb = 4 * ow + (it >> 1), tb0 = 4 * (it & 1);  // feature block, first token block
-            uint32_t x[4];
-            ptx::ldsm_x4(qs + (uint32_t)(fb >> 3) * 2 * TILE + sw128((uint32_t)(8 * (tb0 + m) + r8), (uint32_t)(fb & 7)), x);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const float ng = -gs[8 * (tb0 + i) + (lane >> 2)];
-              const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&x[i]));
-              x[i] = pack_h2(f.x * ng, f.y * ng);
-            }
-            ptx::stsm_x4_t(qd + sw128((uint32_t)(8 * fb + r8), (uint32_t)(tb0 + m)), x);
-          }
-          ptx::fence_proxy_async_smem();
-          ptx::named_bar(3, 128);
-          if (leader) ptx::mbar_arrive(&sbar[SB_W16R]);
         }
         if (c >= 0) {
           // Chunk c's product slot goes back to the prep CTA and its tile buffer takes the loads of
