@@ -20,7 +20,8 @@
 //                       zeroed for the next chunk), QT16 = (-Gamma Q)^T of the next chunk; issues
 //                       the k/q tile loads.  W16 and QT16, both with DK rows, sit side by side as
 //                       the B operand of the fused MMA.
-//                       Warps 4-11 together convert each chunk's k and v tiles to fp16 in place.
+//                       The convert warps turn each chunk's k tiles, the output warps its v tiles, to
+//                       fp16 in place.
 //
 // Handoff: prep pipeline p stages its chunk's products locally (two staging buffers per pipeline)
 // and sends them into slot p of the state CTA with one asynchronous bulk copy that completes on
@@ -60,7 +61,7 @@ constexpr uint32_t YS_BYTES = 2 * TILE;
 constexpr uint32_t S_GS = S_YS + YS_BYTES;         // NB gate slots: gamma[64], w[64], gamma_C
 constexpr uint32_t GSLOT = 2 * C + 4;              // floats per gate slot
 constexpr uint32_t S_BARS = S_GS + NB * GSLOT * 4;
-constexpr uint32_t S_NBARS = 24;
+constexpr uint32_t S_NBARS = 18;
 
 // Prep CTA shared-memory map: pipeline p at p * P_STRIDE.
 constexpr uint32_t P_KQ = 0;                                  // KQ tile set, bf16 as loaded
@@ -90,9 +91,9 @@ constexpr uint32_t COL_S = 0, COL_S16 = 128, COL_U = 192, COL_Y = 256, COL_R16 =
 
 enum SBar {
   SB_PF = 0,                                                       // per product slot (2)
-  SB_KQR = 2, SB_KQF = 5, SB_CVS = 8, SB_CVD = 11,                 // per k/q tile buffer (NB)
-  SB_VF = 14,                                                      // per v tile buffer (NBV)
-  SB_WM = 16, SB_W16R = 17, SB_R = 18, SB_S = 19, SB_YF = 20, SB_YE = 21, SB_DRAIN = 22  // DRAIN: 2
+  SB_KQR = 2, SB_KQF = 5,                                          // per k/q tile buffer (NB)
+  SB_VF = 8,                                                       // per v tile buffer (NBV)
+  SB_WM = 10, SB_W16R = 11, SB_R = 12, SB_S = 13, SB_YF = 14, SB_YE = 15, SB_DRAIN = 16  // DRAIN: 2
 };
 enum PBar { PB_KQF = 0, PB_G = 2, PB_PE = 4, PB_DRAIN = 6 };
 
@@ -129,21 +130,22 @@ __device__ __forceinline__ void cumsum_gates(float la0, float la1, float& g0, fl
   g1 = a1;
 }
 
-// This thread's share of the bf16 -> fp16 conversion in place of chunk c's k tiles (buffer c % NB)
-// and v tiles (buffer c % NBV), done by the state CTA's warps 4-11 together (`ht` = 0..255)
-// between the convert-start and convert-done barriers.  Each warp then fences the tiles for the
-// tensor core and arrives on convert-done (`done`).  Not inlined, and unrolled by four only: the
-// kernel's instruction working set, not latency, is what limits it when many clusters share a GPC.
-__device__ __noinline__ void convert_share(uint8_t* sm, uint64_t* done, int c, int ht) {
-  const uint32_t kq_o = S_KQ + (c % NB) * KQ_BYTES, v_o = S_V + (c % NBV) * V_BYTES;
-#pragma unroll 4
+// This thread's share (`ht` = 0..127 of a warp group) of the bf16 -> fp16 conversion in place of
+// two 64x64 tiles: the k tiles of a chunk (convert warps) or its v tiles (output warps).  All eight
+// loads are in flight before the first store; the writes are then fenced for the tensor core.  Not
+// inlined: one copy serves both groups (the kernel's instruction working set, not latency, is what
+// limits it when many clusters share a GPC).
+__device__ __noinline__ void convert_pair(uint8_t* t0, uint8_t* t1, int ht) {
+  uint4 r[8];
+#pragma unroll
   for (int j = 0; j < 8; ++j) {
-    const int i = ht + 256 * j;
-    const int tile = i >> 9;  // 0, 1: k features 0-63 / 64-127; 2, 3: v
-    uint8_t* base = tile < 2 ? sm + kq_o + tile * 2 * TILE : sm + v_o + (tile - 2) * TILE;
-    const int off = (i & 511) * 16;
-    uint4 r = *reinterpret_cast<uint4*>(base + off);
-    __nv_bfloat162* b2 = reinterpret_cast<__nv_bfloat162*>(&r);
+    const int i = ht + 128 * j;
+    r[j] = *reinterpret_cast<const uint4*>(((i >> 9) ? t1 : t0) + (i & 511) * 16);
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int i = ht + 128 * j;
+    const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&r[j]);
     uint4 o;
     uint32_t* o32 = reinterpret_cast<uint32_t*>(&o);
 #pragma unroll
@@ -151,11 +153,9 @@ __device__ __noinline__ void convert_share(uint8_t* sm, uint64_t* done, int c, i
       const float2 f = __bfloat1622float2(b2[k]);
       o32[k] = pack_h2(f.x, f.y);
     }
-    *reinterpret_cast<uint4*>(base + off) = o;
+    *reinterpret_cast<uint4*>(((i >> 9) ? t1 : t0) + (i & 511) * 16) = o;
   }
   ptx::fence_proxy_async_smem();
-  __syncwarp();
-  if ((threadIdx.x & 31) == 0) ptx::mbar_arrive(done);
 }
 
 template <typename TOut>
@@ -194,7 +194,7 @@ __global__ void __launch_bounds__(NT, 1)
   if (tid == 32) {
     if (rank == 0) {
       for (int i = 0; i < (int)S_NBARS; ++i)
-        ptx::mbar_init(&sbar[i], i == SB_YE ? 4 : i == SB_W16R ? 2 : (i >= SB_CVD && i < SB_CVD + NB) ? 8 : 1);
+        ptx::mbar_init(&sbar[i], i == SB_YE ? 4 : (i == SB_W16R || (i >= SB_KQR && i < SB_KQR + NB)) ? 2 : 1);
       ptx::prefetch_tensormap(&tm_y);
     } else {
       for (int i = 0; i < (int)P_NBARS; ++i) ptx::mbar_init(&pbar[i], 1);
@@ -283,7 +283,6 @@ __global__ void __launch_bounds__(NT, 1)
       *v_loads_issued = c + 1;
     };
     float* gslots = reinterpret_cast<float*>(sm + S_GS);
-    auto convert_tiles = [&](int c, int ht) { convert_share(sm, &sbar[SB_CVD + c % NB], c, ht); };
 
     if (warp < 4) {
       // ----------------------------------- state chain -----------------------------------
@@ -452,10 +451,7 @@ __global__ void __launch_bounds__(NT, 1)
         if (ww == 1) cumsum_gates(la0, la1, g0, g1, gC);
         {
           bool fail = false;  // k, q and v tiles of chunk c
-          if (leader) {
-            lwait(fail, SB_KQF + tb, tph);
-            lwait(fail, SB_VF + c % NBV, (uint32_t)(c / NBV) & 1u);
-          }
+          if (leader) lwait(fail, SB_KQF + tb, tph);
           if (!agree(fail, leader, 2)) break;
         }
         if (ww == 1) {
@@ -466,10 +462,8 @@ __global__ void __launch_bounds__(NT, 1)
           if (lane == 0) gs[2 * C] = __expf(gC);
           if (c + 1 < nch) load_gates(c + 1, la0, la1, be0, be1);
         }
-        ptx::named_bar(2, 128);                            // gate slot written
-        if (leader) ptx::mbar_arrive(&sbar[SB_CVS + tb]);  // the output warps join the conversion
-        convert_tiles(c, wt);
-        if (!gwait(SB_CVD + tb, tph, leader, 2, false)) break;
+        convert_pair(sm + kq_o, sm + kq_o + 2 * TILE, wt);  // K -> fp16 (the output warps take V)
+        ptx::named_bar(2, 128);                              // gate slot and fp16 K written
         if (leader) ptx::mbar_arrive(&sbar[SB_KQR + tb]);
         // W^T = K^T (T Gamma)^T once T Gamma has arrived (the W columns were read out by this group
         // for chunk c-1); W16 is rewritten only after the fused MMA of chunk c-1 has read it, which
@@ -520,22 +514,30 @@ __global__ void __launch_bounds__(NT, 1)
       }
     } else {
       // ------------------------------ output: Y -> y ---------------------------------------
-      // Iteration c: the conversion of chunk c + 1 (with the convert warps); the QT16 half of chunk
-      // c + 1's fused MMA; Y of chunk c read out and zeroed for that MMA; then chunk c's y stores,
-      // product slot and tile loads.  Iteration -1 only prepares chunk 0.
+      // Iteration c: the k/q tile loads of chunk c + 2; V of chunk c + 1 to fp16; the QT16 half of
+      // chunk c + 1's fused MMA; chunk c's y stored from tensor memory, then its Y zeroed for that
+      // MMA.  Iteration -1 only prepares chunk 0.
       const bool leader = tid == 256;
       const int ow = (tid - 256) >> 5;
       const uint32_t peer_pe0 = ptx::mapa_shared(ptx::smem_u32(&pbar[PB_PE]), 1u);
       constexpr int ROWS = (int)(YS_BYTES / (D * sizeof(TOut)));  // tokens per staging piece
       TOut* stage = reinterpret_cast<TOut*>(sm + S_YS);
-      if (leader)
-        for (int c = 0; c < NB && c < nch; ++c) issue_loads(c);
 #pragma unroll 1
       for (int c = -1; c < nch; ++c) {
         const int cn = c + 1;
-        if (cn < nch) {
-          if (!gwait(SB_CVS + cn % NB, (uint32_t)(cn / NB) & 1u, leader, 3, false)) break;
-          convert_tiles(cn, tid - 128);
+        if (leader) {
+          // Every MMA of chunk c-1 has completed (its Y was read out last iteration): its product
+          // slot goes back to the prep CTA and its tile buffer takes the loads of chunk c + 2.
+          // Iteration -1 issues those of chunks 0 and 1.  One call site.
+          if (c >= 1) ptx::mbar_arrive_remote_relaxed(peer_pe0 + 8u * (uint32_t)((c - 1) & 1));
+          for (int l = c < 0 ? 0 : c + 2; l <= c + 2 && l < nch; ++l) issue_loads(l);
+        }
+        if (cn < nch) {  // V of chunk c + 1 -> fp16 (the convert warps take K and the gates)
+          if (!gwait(SB_VF + cn % NBV, (uint32_t)(cn / NBV) & 1u, leader, 3, false)) break;
+          const uint32_t v_o = S_V + (cn % NBV) * V_BYTES;
+          convert_pair(sm + v_o, sm + v_o + TILE, tid - 256);
+          ptx::named_bar(3, 128);
+          if (leader) ptx::mbar_arrive(&sbar[SB_KQR + cn % NB]);
         }
         if (cn < nch) {
           // QT16 = (-Gamma Q)^T of chunk c + 1, DK rows x 64 tokens (the Y half of the fused MMA's B
@@ -543,9 +545,11 @@ __global__ void __launch_bounds__(NT, 1)
           // block is read by ldmatrix (a token per row), scaled, and written transposed by
           // stmatrix.  Warp ow covers features 32 ow .. 32 ow + 31.  Built as soon as the fused MMA
           // of chunk c, the last reader of QT16, has completed, before chunk c's Y is read out.
-          bool fail = false;
-          if (leader && c >= 0)
-            fail = !ptx::mbar_wait_abortable(&sbar[SB_R], (uint32_t)c & 1u, WAIT_LIMIT, abort_flag);
+          bool fail = false;  // the fused MMA of chunk c; q tiles and gates of chunk c + 1
+          if (leader) {
+            if (c >= 0) lwait(fail, SB_R, (uint32_t)c & 1u);
+            lwait(fail, SB_KQR + cn % NB, (uint32_t)(cn / NB) & 1u);
+          }
           if (!agree(fail, leader, 3)) break;
           const float* gs = gslots + (cn % NB) * GSLOT;
           float ng[8];  // -gamma of the 8 tokens this lane scales: 8 j + lane / 4
@@ -575,13 +579,33 @@ __global__ void __launch_bounds__(NT, 1)
           ptx::named_bar(3, 128);
           if (leader) ptx::mbar_arrive(&sbar[SB_W16R]);
         }
-        float yv[64];
         if (c >= 0) {
           if (!gwait(SB_YF, (uint32_t)c & 1u, leader, 3, false)) break;  // every MMA of chunk c
           ptx::tc_fence_after();
-          ptx::tmem_ld32(my + COL_Y, *reinterpret_cast<float(*)[32]>(yv));
-          ptx::tmem_ld32(my + COL_Y + 32, *reinterpret_cast<float(*)[32]>(yv + 32));
-          ptx::tc_wait_ld();
+          // y of chunk c straight from tensor memory, 16 tokens at a time (a short loop body), through
+          // the staging tile: one TMA store per piece.
+#pragma unroll 1
+          for (int piece = 0; piece < C / ROWS; ++piece) {
+            // The staging tile's previous store (the last chunk's, or the previous piece) must have
+            // been read out first.
+            if (leader) ptx::bulk_wait_read0();
+            ptx::named_bar(3, 128);
+#pragma unroll 1
+            for (int g = 0; g < ROWS / 16; ++g) {
+              float yv[16];
+              ptx::tmem_ld16(my + COL_Y + piece * ROWS + 16 * g, yv);
+              ptx::tc_wait_ld();
+#pragma unroll
+              for (int j = 0; j < 16; ++j) store_as(stage + (16 * g + j) * D + row, yv[j]);
+            }
+            ptx::fence_proxy_async_smem();
+            ptx::named_bar(3, 128);
+            if (leader) {
+              ptx::tma_store_4d(&tm_y, stage, 0, h, (cb + c) * C + piece * ROWS, b);
+              ptx::bulk_commit();
+            }
+          }
+          // Y is accumulated afresh by the fused MMA of chunk c + 1: zero it, then hand it back.
           float z[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) z[j] = 0.f;
@@ -591,29 +615,6 @@ __global__ void __launch_bounds__(NT, 1)
           ptx::tc_fence_before();
           __syncwarp();
           if (lane == 0) ptx::mbar_arrive(&sbar[SB_YE]);
-        }
-        if (c >= 0) {
-          // Chunk c's product slot goes back to the prep CTA and its tile buffer takes the loads of
-          // chunk c + NB.
-          if (leader) {
-            ptx::mbar_arrive_remote_relaxed(peer_pe0 + 8u * (uint32_t)(c & 1));
-            if (c + NB < nch) issue_loads(c + NB);
-          }
-#pragma unroll
-          for (int piece = 0; piece < C / ROWS; ++piece) {  // unrolled: yv stays in registers
-            // The staging tile's previous store (the last chunk's, or the previous piece) must have
-            // been read out first.
-            if (leader) ptx::bulk_wait_read0();
-            ptx::named_bar(3, 128);
-#pragma unroll
-            for (int j = 0; j < ROWS; ++j) store_as(stage + j * D + row, yv[piece * ROWS + j]);
-            ptx::fence_proxy_async_smem();
-            ptx::named_bar(3, 128);
-            if (leader) {
-              ptx::tma_store_4d(&tm_y, stage, 0, h, (cb + c) * C + piece * ROWS, b);
-              ptx::bulk_commit();
-            }
-          }
         }
       }
       if (leader) ptx::bulk_wait0();

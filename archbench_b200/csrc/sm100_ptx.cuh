@@ -171,18 +171,18 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 // Bounded wait that also gives up as soon as another thread has raised `*abort` (shared flag).
 __device__ __forceinline__ bool mbar_wait_abortable(uint64_t* bar, uint32_t parity, long long max_cycles,
                                                  volatile int* abort) {
+  // One short loop (try_wait suspends in hardware between polls): every inlined copy is small.
+  // The clock is read only once the first poll has failed.
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
-  while (true) {
-#pragma unroll 1
-    for (int i = 0; i < 32; ++i)
-      if (mbar_try_wait(bar, parity)) return true;
+  while (!mbar_try_wait(bar, parity)) {
     if (*abort) return false;
     if (clock64() - t0 > max_cycles) {
       *abort = 1;
       return false;
     }
   }
+  return true;
 }
 
 // ---- legacy warp-level tensor-core helpers for small 16x16 blocks ------------------------
@@ -305,16 +305,14 @@ __device__ __forceinline__ bool mbar_wait_abortable_cluster(uint64_t* bar, uint3
                                                             volatile int* abort) {
   if (mbar_try_wait_cluster(bar, parity)) return true;
   const long long t0 = clock64();
-  while (true) {
-#pragma unroll 1
-    for (int i = 0; i < 32; ++i)
-      if (mbar_try_wait_cluster(bar, parity)) return true;
+  while (!mbar_try_wait_cluster(bar, parity)) {
     if (*abort) return false;
     if (clock64() - t0 > max_cycles) {
       *abort = 1;
       return false;
     }
   }
+  return true;
 }
 // Generic-proxy writes to shared memory anywhere in the cluster -> visible to the async proxy.
 __device__ __forceinline__ void fence_proxy_async_cluster() {
