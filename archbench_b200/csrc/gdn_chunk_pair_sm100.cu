@@ -333,11 +333,11 @@ __global__ void __launch_bounds__(NT, 1)
         if (leader) *reinterpret_cast<volatile int*>(sm + CTRL + 16 + 4 * s) = (c >> 1) + 1;
         const float gC = gs[2 * C];
         ptx::tc_fence_after();
-        if (leader) {  // U^T = V^T T^T while the state is converted
-          ptx::fence_proxy_async_smem();
+        if (warp == 0) {  // U^T = V^T T^T while the state is converted (issued from the converged warp)
 #pragma unroll 1
           for (int k = 0; k < 4; ++k)
-            ptx::mma_f16_ss(tmem + COL_U, at(D_MN8K, v_o + k * 2048), at(D_K, ps_o + TILE + k * 32), ID_N64_AMN, k > 0);
+            ptx::mma_f16_ss_elect(tmem + COL_U, at(D_MN8K, v_o + k * 2048), at(D_K, ps_o + TILE + k * 32), ID_N64_AMN,
+                                  k > 0);
           issued = true;
         }
         // S -> S16 (fp16, tensor memory: the A operand of the fused MMA) and S <- gamma_C S, in
@@ -363,21 +363,25 @@ __global__ void __launch_bounds__(NT, 1)
           // [R^T | Y] = [U^T | 0] - S [W | -Gamma Q]^T, committed as R, once W16 and QT16 of chunk c
           // are written and Y has been read out (and zeroed) by the output warps for chunk c-1.
           bool fail = false;
-          if (leader) {
-            lwait(fail, SB_W16R, (uint32_t)c & 1u);
-            if (c >= 1) lwait(fail, SB_YE, (uint32_t)(c - 1) & 1u);
+          if (warp == 0) {
+            if (leader) {
+              lwait(fail, SB_W16R, (uint32_t)c & 1u);
+              if (c >= 1) lwait(fail, SB_YE, (uint32_t)(c - 1) & 1u);
+            }
+            fail = __shfl_sync(0xffffffffu, fail, 0);
             ptx::tc_fence_after();
             if (!fail) {
 #pragma unroll 1
               for (int k = 0; k < 8; ++k)
-                ptx::mma_f16_ts(tmem + COL_U, tmem + COL_S16 + 8 * k, at(D_MN16K, S_WQ + k * 2048), ID_N128_BMN_NEG, 1);
-              ptx::mma_commit(&sbar[SB_R]);
-              lwait(fail, SB_R, (uint32_t)c & 1u);
+                ptx::mma_f16_ts_elect(tmem + COL_U, tmem + COL_S16 + 8 * k, at(D_MN16K, S_WQ + k * 2048), ID_N128_BMN_NEG,
+                                      1);
+              ptx::mma_commit_elect(&sbar[SB_R]);
+              if (leader) lwait(fail, SB_R, (uint32_t)c & 1u);
             }
           }
           if (!agree(fail, leader, 1)) break;
         }
-        if (leader) issued = false;
+        if (warp == 0) issued = false;
         ptx::tc_fence_after();
         {
           // R -> R16 and R diag(w) -> RW16 (fp16, tensor memory), in halves of 32 tokens.
@@ -399,16 +403,16 @@ __global__ void __launch_bounds__(NT, 1)
         }
         ptx::tc_fence_before();
         ptx::named_bar(1, 128);
-        if (leader) {  // S += (R diag w)^T K (committed alone), then Y += R^T A^T
+        if (warp == 0) {  // S += (R diag w)^T K (committed alone), then Y += R^T A^T
           ptx::tc_fence_after();
 #pragma unroll 1
           for (int k = 0; k < 4; ++k)
-            ptx::mma_f16_ts(tmem + COL_S, tmem + COL_RW16 + 8 * k, at(D_MN16K, kq_o + k * 2048), ID_N128_BMN, 1);
-          ptx::mma_commit(&sbar[SB_S]);
+            ptx::mma_f16_ts_elect(tmem + COL_S, tmem + COL_RW16 + 8 * k, at(D_MN16K, kq_o + k * 2048), ID_N128_BMN, 1);
+          ptx::mma_commit_elect(&sbar[SB_S]);
 #pragma unroll 1
           for (int k = 0; k < 4; ++k)
-            ptx::mma_f16_ts(tmem + COL_Y, tmem + COL_R16 + 8 * k, at(D_K, ps_o + k * 32), ID_N64, 1);
-          ptx::mma_commit(&sbar[SB_YF]);
+            ptx::mma_f16_ts_elect(tmem + COL_Y, tmem + COL_R16 + 8 * k, at(D_K, ps_o + k * 32), ID_N64, 1);
+          ptx::mma_commit_elect(&sbar[SB_YF]);
           issued = true;
         }
       }
@@ -428,9 +432,10 @@ __global__ void __launch_bounds__(NT, 1)
           }
         }
       }
-      if (*abort_flag && leader && issued) {  // drain this thread's MMAs
-        ptx::mma_commit(&sbar[SB_DRAIN]);
-        ptx::mbar_wait_bounded(&sbar[SB_DRAIN], 0, WAIT_LIMIT);
+      if (*abort_flag && warp == 0 && issued) {  // drain this warp's MMAs
+        ptx::mma_commit_elect(&sbar[SB_DRAIN]);
+        if (leader) ptx::mbar_wait_bounded(&sbar[SB_DRAIN], 0, WAIT_LIMIT);
+        __syncwarp();
       }
     } else if (warp < 8) {
       // ------------------------- convert: gates, fp16 tiles, W ----------------------------
@@ -469,14 +474,13 @@ __global__ void __launch_bounds__(NT, 1)
         // for chunk c-1); W16 is rewritten only after the fused MMA of chunk c-1 has read it, which
         // also frees the v buffer of chunk c-1 (its U MMA came first) for chunk c+1.
         if (!gwait(SB_PF + s, ph, leader, 2, true)) break;
-        if (leader) {
-          ptx::fence_proxy_async_smem();
+        if (ww == 0) {  // issued from the converged warp
           ptx::tc_fence_after();
 #pragma unroll 1
           for (int k = 0; k < 4; ++k)
-            ptx::mma_f16_ss(tmem + COL_W, at(D_MN16K, kq_o + k * 2048), at(D_K, ps_o + 2 * TILE + k * 32), ID_N64_AMN,
-                            k > 0);
-          ptx::mma_commit(&sbar[SB_WM]);
+            ptx::mma_f16_ss_elect(tmem + COL_W, at(D_MN16K, kq_o + k * 2048), at(D_K, ps_o + 2 * TILE + k * 32),
+                                  ID_N64_AMN, k > 0);
+          ptx::mma_commit_elect(&sbar[SB_WM]);
           issued = true;
         }
         {
@@ -487,9 +491,9 @@ __global__ void __launch_bounds__(NT, 1)
               if (!fail && c + 1 < nch) issue_v_loads(c + 1);
             }
             lwait(fail, SB_WM, (uint32_t)c & 1u);
-            issued = false;
           }
           if (!agree(fail, leader, 2)) break;
+          if (ww == 0) issued = false;
         }
         ptx::tc_fence_after();
 #pragma unroll 1
@@ -508,9 +512,10 @@ __global__ void __launch_bounds__(NT, 1)
         ptx::named_bar(2, 128);
         if (leader) ptx::mbar_arrive(&sbar[SB_W16R]);
       }
-      if (*abort_flag && leader && issued) {
-        ptx::mma_commit(&sbar[SB_DRAIN + 1]);
-        ptx::mbar_wait_bounded(&sbar[SB_DRAIN + 1], 0, WAIT_LIMIT);
+      if (*abort_flag && ww == 0 && issued) {
+        ptx::mma_commit_elect(&sbar[SB_DRAIN + 1]);
+        if (leader) ptx::mbar_wait_bounded(&sbar[SB_DRAIN + 1], 0, WAIT_LIMIT);
+        __syncwarp();
       }
     } else {
       // ------------------------------ output: Y -> y ---------------------------------------
@@ -526,10 +531,9 @@ __global__ void __launch_bounds__(NT, 1)
       for (int c = -1; c < nch; ++c) {
         const int cn = c + 1;
         if (leader) {
-          // Every MMA of chunk c-1 has completed (its Y was read out last iteration): its product
-          // slot goes back to the prep CTA and its tile buffer takes the loads of chunk c + 2.
-          // Iteration -1 issues those of chunks 0 and 1.  One call site.
-          if (c >= 1) ptx::mbar_arrive_remote_relaxed(peer_pe0 + 8u * (uint32_t)((c - 1) & 1));
+          // Every MMA of chunk c-1 has completed (its Y was read out last iteration): its tile
+          // buffer takes the loads of chunk c + 2.  Iteration -1 issues those of chunks 0 and 1.
+          // One call site.
           for (int l = c < 0 ? 0 : c + 2; l <= c + 2 && l < nch; ++l) issue_loads(l);
         }
         if (cn < nch) {  // V of chunk c + 1 -> fp16 (the convert warps take K and the gates)
@@ -581,6 +585,8 @@ __global__ void __launch_bounds__(NT, 1)
         }
         if (c >= 0) {
           if (!gwait(SB_YF, (uint32_t)c & 1u, leader, 3, false)) break;  // every MMA of chunk c
+          // Chunk c's product slot goes back to the prep CTA at once (its copy of chunk c + 2 waits).
+          if (leader) ptx::mbar_arrive_remote_relaxed(peer_pe0 + 8u * (uint32_t)(c & 1));
           ptx::tc_fence_after();
           // y of chunk c straight from tensor memory, 16 tokens at a time (a short loop body), through
           // the staging tile: one TMA store per piece.
@@ -664,14 +670,14 @@ __global__ void __launch_bounds__(NT, 1)
         const uint32_t st_o = base + P_ST + (uint32_t)(k & 1) * PS_BYTES;
         uint8_t* st = sm + st_o;
         if (!gwait(PB_KQF + pp, ph, false)) break;
-        if (leader) {  // G = [K;Q] K^T from the bf16 tiles as loaded
+        if (pw == 0) {  // G = [K;Q] K^T from the bf16 tiles as loaded (issued from the converged warp)
           ptx::tc_fence_after();
 #pragma unroll 1
           for (int kk = 0; kk < 8; ++kk) {
             const uint64_t a = at(D_K, base + P_KQ + (kk >> 2) * 2 * TILE + (kk & 3) * 32);
-            ptx::mma_f16_ss(tmem + 64 * pp, a, a, ID_G, kk > 0);
+            ptx::mma_f16_ss_elect(tmem + 64 * pp, a, a, ID_G, kk > 0);
           }
-          ptx::mma_commit(&pbar[PB_G + pp]);
+          ptx::mma_commit_elect(&pbar[PB_G + pp]);
           issued = true;
         }
         if (pw == 1) {  // chunk-local cumulative log-decay
@@ -703,9 +709,10 @@ __global__ void __launch_bounds__(NT, 1)
           Ed[(bb * 16 + r) * 20 + cc] = cc <= r ? beta_s[16 * bb + cc] * __expf(g_s[16 * bb + r] - g_s[16 * bb + cc]) : 0.f;
         }
         if (!gwait(PB_G + pp, ph, false)) break;  // also orders the tables
-        if (leader) {  // the tile set is free once G has been formed: fetch chunk c + 2
-          issued = false;
-          if (c + 2 < nch) { issue(c + 2); last_load = k + 1; }
+        if (pw == 0) issued = false;
+        if (leader && c + 2 < nch) {  // the tile set is free once G has been formed: fetch chunk c + 2
+          issue(c + 2);
+          last_load = k + 1;
         }
         if (pw == 1 && c + 2 < nch) load_gates(c + 2, la0, la1, be0, be1);
         ptx::tc_fence_after();
@@ -790,12 +797,13 @@ __global__ void __launch_bounds__(NT, 1)
           ptx::st_cluster_u32(remote_copies, (uint32_t)++copies);
         }
       }
-      if (*abort_flag && leader) {  // drain this pipeline's MMA and tile loads
+      if (*abort_flag && pw == 0) {  // drain this pipeline's MMA and tile loads
         if (issued) {
-          ptx::mma_commit(&pbar[PB_DRAIN + pp]);
-          ptx::mbar_wait_bounded(&pbar[PB_DRAIN + pp], 0, WAIT_LIMIT);
+          ptx::mma_commit_elect(&pbar[PB_DRAIN + pp]);
+          if (leader) ptx::mbar_wait_bounded(&pbar[PB_DRAIN + pp], 0, WAIT_LIMIT);
         }
-        if (last_load >= 0) ptx::mbar_wait_bounded(&pbar[PB_KQF + pp], (uint32_t)last_load & 1u, WAIT_LIMIT);
+        if (leader && last_load >= 0) ptx::mbar_wait_bounded(&pbar[PB_KQF + pp], (uint32_t)last_load & 1u, WAIT_LIMIT);
+        __syncwarp();
       }
     }
   }
