@@ -89,6 +89,8 @@ def dist_init(n_gpus):
         import torch.distributed as dist
 
         torch.cuda.set_device(local)
+        # Keep rank 0's stdout to the one JSON line: NCCL's version banner goes only where asked for.
+        os.environ.setdefault("NCCL_DEBUG", "WARN")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
     elif torch.cuda.is_available():
         torch.cuda.set_device(0)
