@@ -1,0 +1,375 @@
+// Layer prologue and epilogue of the gated-DeltaNet mixers, each one bandwidth-bound kernel.
+//
+// Prologue: from the layer's projections to the token-mixing inputs.  Per (b, t, h):
+//   q, k, v  <- SiLU(depthwise causal conv over conv_size taps of the projection), computed in the
+//               projection's dtype as archbench/layers/nsgdn.py:457-470 does (F.conv1d then F.silu);
+//   q        <- q / max(|q|, eps) * q_scale,  k <- k / max(|k|, eps)          (nsgdn.py:526-527)
+//   la       <- -softplus(a + dt_bias) * exp(A_log), optionally clamped below  (nsgdn.py:530-532)
+//   beta     <- sigmoid(b + b_bias) * beta_scale                                (nsgdn.py:533)
+// and the last conv_size - 1 projection rows of every channel as the next call's conv state.
+// fla's gdn mixer (fla/layers/gated_deltanet.py:240-279) is the same computation with three
+// separately projected inputs, eps = 1e-6 and no b_bias.
+//
+// Epilogue: o = y / sqrt(mean(y^2) + eps) * weight * SiLU(g) over each head's DV values
+// (nsgdn.py:539-541; fla's FusedRMSNormGated), in fp32, rounded once to the output dtype.
+//
+// One warp per (b, t, h) in both kernels: a lane owns DK/32 channels of q and k and DV/32 of v.
+// The prologue reads the conv_size rows a token needs directly (the neighbouring tokens' warps
+// of the block find them in L1), so no warp waits on a chain of loads.
+#include <math.h>
+#include <string.h>
+
+#include "gdn_common.cuh"
+
+namespace gdn {
+namespace layer_io {
+
+constexpr int MAX_TAPS = 4;   // largest conv_size served (the reference uses 4)
+constexpr int TOKS = 4;       // tokens per prologue block (one warp each; neighbours share rows in L1)
+
+template <typename T>
+__device__ __forceinline__ float round_to(float x) {
+  if constexpr (sizeof(T) == 2) return __bfloat162float(__float2bfloat16_rn(x));
+  return x;
+}
+// SiLU with the fast exponential and division (a few ulps of fp32, far below the bf16 rounding of
+// the projections; for fp32 projections within 1e-6 relative of torch's): the prologue is
+// otherwise bound by the instruction cost of the precise forms.
+__device__ __forceinline__ float silu(float x) { return __fdividef(x, 1.f + __expf(-x)); }
+__device__ __forceinline__ float softplus(float x) { return x > 20.f ? x : log1pf(expf(x)); }  // torch's threshold
+
+// N consecutive outputs with vector stores of up to 16 bytes (the address is aligned to them).
+template <typename TO, int N>
+__device__ __forceinline__ void store_vec(TO* p, const float (&v)[N]) {
+  if constexpr (sizeof(TO) == 2) {
+    static_assert(N % 2 == 0, "pairs of bf16");
+    uint32_t w[N / 2];
+#pragma unroll
+    for (int i = 0; i < N / 2; ++i) {
+      const __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+      w[i] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+#pragma unroll
+    for (int i = 0; i < N / 2; i += 4) {
+      if (N / 2 - i >= 4) *reinterpret_cast<uint4*>(p + 2 * i) = make_uint4(w[i], w[i + 1], w[i + 2], w[i + 3]);
+      else if (N / 2 - i >= 2) *reinterpret_cast<uint2*>(p + 2 * i) = make_uint2(w[i], w[i + 1]);
+      else *reinterpret_cast<uint32_t*>(p + 2 * i) = w[i];
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < N; i += 4) {
+      if (N - i >= 4) *reinterpret_cast<float4*>(p + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+      else if (N - i >= 2) *reinterpret_cast<float2*>(p + i) = make_float2(v[i], v[i + 1]);
+      else p[i] = v[i];
+    }
+  }
+}
+
+// N consecutive fp32 values with 16-byte loads (the address is 16-byte aligned).
+template <int N>
+__device__ __forceinline__ void load_f32(const float* p, float (&v)[N]) {
+  if constexpr (N % 4 == 0) {
+#pragma unroll
+    for (int i = 0; i < N; i += 4) {
+      const float4 f = __ldg(reinterpret_cast<const float4*>(p + i));
+      v[i] = f.x; v[i + 1] = f.y; v[i + 2] = f.z; v[i + 3] = f.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < N; ++i) v[i] = __ldg(p + i);
+  }
+}
+
+struct Comp {            // one of q, k, v
+  const void* x;         // projection [B][T][channels] with strides
+  int64_t sb, st;
+  const float* w;        // (taps, channels) fp32, tap-major, or NULL: no convolution (SiLU only)
+  int64_t wch;           // channels (the row length of w)
+  const void* cin;       // conv state in (B, channels, taps - 1) with batch stride, or NULL
+  void* cout;            // conv state out, or NULL
+  int64_t csb;
+  void* out;             // [B][T][H][D] contiguous
+};
+
+struct PrologueParams {
+  Comp q, k, v;
+  const void* xa;
+  const void* xb;
+  int64_t sa_b, sa_t, sb_b, sb_t;
+  const float* A_log;
+  const float* dt_bias;
+  const float* b_bias;
+  float* la;
+  float* beta;
+  int B, T, H, DK, DV, taps, clamp;
+  float q_scale, eps, la_min, beta_scale;
+};
+
+// Row `t` (t < 0: the incoming conv state, or zeros) of channels [c0, c0 + NPL) of a component.
+template <typename TX, int NPL>
+__device__ __forceinline__ void load_row(const Comp& cp, int b, int t, int taps, int c0, float (&r)[NPL]) {
+  if (t >= 0) {
+    load_vec<NPL>(reinterpret_cast<const TX*>(cp.x) + (int64_t)b * cp.sb + (int64_t)t * cp.st + c0, r);
+  } else {
+#pragma unroll
+    for (int n = 0; n < NPL; ++n) r[n] = 0.f;
+    if (cp.cin) {
+      const TX* pc = reinterpret_cast<const TX*>(cp.cin) + (int64_t)b * cp.csb;
+#pragma unroll
+      for (int n = 0; n < NPL; ++n) r[n] = to_f32(pc[(int64_t)(c0 + n) * (taps - 1) + (taps - 1) + t]);
+    }
+  }
+}
+
+// SiLU(conv) of one component at token t for this lane's channels, in the projection dtype (the
+// weights rounded to it, as F.conv1d(x, weight.to(x.dtype)) uses them), accumulated tap by tap.
+template <typename TX, int NPL>
+__device__ __forceinline__ void conv_silu(const Comp& cp, int b, int t, int taps, int c0, float (&out)[NPL]) {
+  float acc[NPL];
+#pragma unroll
+  for (int n = 0; n < NPL; ++n) acc[n] = 0.f;
+#pragma unroll
+  for (int j = 0; j < MAX_TAPS; ++j) {
+    if (j >= taps) continue;
+    float row[NPL];
+    load_row<TX, NPL>(cp, b, t - (taps - 1) + j, taps, c0, row);
+    if (cp.w) {
+      float wt[NPL];
+      load_f32<NPL>(cp.w + (int64_t)j * cp.wch + c0, wt);  // coalesced: lanes own consecutive channels
+#pragma unroll
+      for (int n = 0; n < NPL; ++n) acc[n] = fmaf(round_to<TX>(wt[n]), row[n], acc[n]);
+    } else {
+#pragma unroll
+      for (int n = 0; n < NPL; ++n) acc[n] = row[n];
+    }
+  }
+#pragma unroll
+  for (int n = 0; n < NPL; ++n) out[n] = round_to<TX>(silu(cp.w ? round_to<TX>(acc[n]) : acc[n]));
+}
+
+// The next call's conv state of one component: rows T - (taps - 1) .. T - 1 of this lane's
+// channels (earlier rows from the incoming state when T is short).
+template <typename TX, int NPL>
+__device__ __forceinline__ void save_state(const Comp& cp, int b, int T, int taps, int c0) {
+  if (!cp.cout) return;
+  TX* pc = reinterpret_cast<TX*>(cp.cout) + (int64_t)b * cp.csb;
+#pragma unroll 1
+  for (int j = 1; j < taps; ++j) {
+    float row[NPL];
+    load_row<TX, NPL>(cp, b, T - taps + j, taps, c0, row);
+#pragma unroll
+    for (int n = 0; n < NPL; ++n) store_as(pc + (int64_t)(c0 + n) * (taps - 1) + (j - 1), row[n]);
+  }
+}
+
+// One warp per (b, t, h): every load of the token is independent (conv rows re-read from L1 by
+// the neighbouring tokens' warps), so a launch keeps many loads in flight.
+template <typename TX, typename TO, int NK, int NV>
+__global__ void __launch_bounds__(32 * TOKS, NV >= 16 ? 4 : (NV >= 8 ? 6 : 8)) prologue_kernel(const PrologueParams p) {
+  const int lane = threadIdx.x & 31;
+  const int groups = (p.T + TOKS - 1) / TOKS;
+  const int blk = blockIdx.x;
+  const int tg = blk % groups, bh = blk / groups, h = bh % p.H, b = bh / p.H;
+  const int t = tg * TOKS + (threadIdx.x >> 5);
+  if (t >= p.T) return;
+  const int ck = h * p.DK + lane * NK, cv = h * p.DV + lane * NV;  // first channel of this lane
+  float q[NK], k[NK], v[NV];
+  conv_silu<TX, NK>(p.q, b, t, p.taps, ck, q);
+  conv_silu<TX, NK>(p.k, b, t, p.taps, ck, k);
+  conv_silu<TX, NV>(p.v, b, t, p.taps, cv, v);
+  float sq = 0.f, sk = 0.f;
+#pragma unroll
+  for (int n = 0; n < NK; ++n) {
+    sq = fmaf(q[n], q[n], sq);
+    sk = fmaf(k[n], k[n], sk);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    sq += __shfl_xor_sync(0xffffffffu, sq, o);
+    sk += __shfl_xor_sync(0xffffffffu, sk, o);
+  }
+  const float iq = p.q_scale / fmaxf(sqrtf(sq), p.eps), ik = 1.f / fmaxf(sqrtf(sk), p.eps);
+  const int64_t tok = ((int64_t)b * p.T + t) * p.H + h;
+  TO* oq = reinterpret_cast<TO*>(p.q.out) + tok * p.DK + lane * NK;
+  TO* ok = reinterpret_cast<TO*>(p.k.out) + tok * p.DK + lane * NK;
+  TO* ov = reinterpret_cast<TO*>(p.v.out) + tok * p.DV + lane * NV;
+#pragma unroll
+  for (int n = 0; n < NK; ++n) {
+    q[n] *= iq;
+    k[n] *= ik;
+  }
+  store_vec<TO, NK>(oq, q);
+  store_vec<TO, NK>(ok, k);
+  store_vec<TO, NV>(ov, v);
+  if (lane == 0) {
+    const float a = to_f32(reinterpret_cast<const TX*>(p.xa)[(int64_t)b * p.sa_b + (int64_t)t * p.sa_t + h]);
+    const float bb = to_f32(reinterpret_cast<const TX*>(p.xb)[(int64_t)b * p.sb_b + (int64_t)t * p.sb_t + h]);
+    float la = -softplus(a + p.dt_bias[h]) * expf(p.A_log[h]);
+    if (p.clamp) la = fmaxf(la, p.la_min);
+    p.la[tok] = la;
+    p.beta[tok] = p.beta_scale / (1.f + expf(-(bb + (p.b_bias ? p.b_bias[h] : 0.f))));
+  }
+  // The next call's conv state: the last taps - 1 rows of every channel, from the sequence's last
+  // token (earlier rows come from the incoming state when T is short).
+  if (t == p.T - 1 && p.taps > 1) {
+    save_state<TX, NK>(p.q, b, p.T, p.taps, ck);
+    save_state<TX, NK>(p.k, b, p.T, p.taps, ck);
+    save_state<TX, NV>(p.v, b, p.T, p.taps, cv);
+  }
+}
+
+struct EpilogueParams {
+  const void* y;
+  gdn_strides sy;
+  const void* g;
+  int64_t sg_b, sg_t;
+  const float* weight;
+  void* o;
+  int64_t so_b, so_t;
+  int B, T, H, DV;
+  float eps;
+};
+
+template <typename TY, typename TG, typename TO, int NPL>
+__global__ void __launch_bounds__(128) epilogue_kernel(const EpilogueParams p) {
+  const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= (int64_t)p.B * p.T * p.H) return;
+  const int h = (int)(row % p.H);
+  const int64_t bt = row / p.H;
+  const int t = (int)(bt % p.T), b = (int)(bt / p.T);
+  const int c0 = lane * NPL;
+  float y[NPL];
+  load_vec<NPL>(reinterpret_cast<const TY*>(p.y) + b * p.sy.b + t * p.sy.t + h * p.sy.h + c0, y);
+  float ss = 0.f;
+#pragma unroll
+  for (int n = 0; n < NPL; ++n) ss = fmaf(y[n], y[n], ss);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float r = rsqrtf(ss / (float)p.DV + p.eps);
+  float g[NPL];
+  if (p.g) load_vec<NPL>(reinterpret_cast<const TG*>(p.g) + b * p.sg_b + t * p.sg_t + (int64_t)h * p.DV + c0, g);
+  TO* po = reinterpret_cast<TO*>(p.o) + b * p.so_b + t * p.so_t + (int64_t)h * p.DV + c0;
+  float wv[NPL];
+  load_vec<NPL>(p.weight + c0, wv);
+#pragma unroll
+  for (int n = 0; n < NPL; ++n) {
+    y[n] *= r * wv[n];
+    if (p.g) y[n] *= silu(g[n]);
+  }
+  store_vec<TO, NPL>(po, y);
+}
+
+bool device_ok() {
+  int dev = 0, major = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return false;
+  return major == 10;
+}
+
+bool a16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+template <typename TX, typename TO>
+int launch_prologue(const PrologueParams& p, cudaStream_t s) {
+  const int64_t blocks = (int64_t)p.B * p.H * ((p.T + TOKS - 1) / TOKS);
+  if (blocks > 0x7fffffff) return GDN_ERR_SHAPE;
+  const int nk = p.DK / 32, nv = p.DV / 32;
+#define GDN_PRO(NK, NV)                                                                     \
+  if (nk == NK && nv == NV) {                                                               \
+    prologue_kernel<TX, TO, NK, NV><<<(unsigned)blocks, 32 * TOKS, 0, s>>>(p);              \
+    return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;                     \
+  }
+  GDN_PRO(2, 2) GDN_PRO(2, 4) GDN_PRO(4, 4) GDN_PRO(4, 8) GDN_PRO(8, 8) GDN_PRO(8, 16)
+#undef GDN_PRO
+  return GDN_ERR_UNSUPPORTED;
+}
+
+template <typename TY, typename TG, typename TO>
+int launch_epilogue(const EpilogueParams& p, cudaStream_t s) {
+  const int64_t rows = (int64_t)p.B * p.T * p.H;
+  const int blocks = (int)((rows * 32 + 127) / 128);
+  switch (p.DV / 32) {
+    case 2: epilogue_kernel<TY, TG, TO, 2><<<blocks, 128, 0, s>>>(p); break;
+    case 4: epilogue_kernel<TY, TG, TO, 4><<<blocks, 128, 0, s>>>(p); break;
+    case 8: epilogue_kernel<TY, TG, TO, 8><<<blocks, 128, 0, s>>>(p); break;
+    case 16: epilogue_kernel<TY, TG, TO, 16><<<blocks, 128, 0, s>>>(p); break;
+    default: return GDN_ERR_UNSUPPORTED;
+  }
+  return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+}
+
+}  // namespace layer_io
+}  // namespace gdn
+
+using namespace gdn::layer_io;
+
+extern "C" {
+
+int gdn_layer_prologue(const gdn_prologue_args* a, void* stream) {
+  if (!a) return GDN_ERR_NULL;
+  if (!a->xq || !a->xk || !a->xv || !a->xa || !a->xb || !a->A_log || !a->dt_bias || !a->q || !a->k || !a->v ||
+      !a->la || !a->beta)
+    return GDN_ERR_NULL;
+  if (a->B < 1 || a->T < 1 || a->H < 1 || a->B * a->T * a->H > (int64_t)1 << 31) return GDN_ERR_SHAPE;
+  const bool dk_ok = a->DK == 64 || a->DK == 128 || a->DK == 256, dv_ok = a->DV == 64 || a->DV == 128 || a->DV == 256 || a->DV == 512;
+  if (!dk_ok || !dv_ok || a->DV < a->DK || a->DV > 2 * a->DK) return GDN_ERR_SHAPE;
+  if (a->conv_size < 1 || a->conv_size > MAX_TAPS) return GDN_ERR_SHAPE;
+  if (a->in_dtype != GDN_DTYPE_BF16 && a->in_dtype != GDN_DTYPE_F32) return GDN_ERR_DTYPE;
+  if (a->out_dtype != GDN_DTYPE_BF16 && a->out_dtype != GDN_DTYPE_F32) return GDN_ERR_DTYPE;
+  // Lanes load DK/32 or DV/32 consecutive channels with one vector load: 16-byte aligned rows.
+  const int64_t es = a->in_dtype == GDN_DTYPE_BF16 ? 2 : 4;
+  const int64_t sts[] = {a->sxq_b, a->sxq_t, a->sxk_b, a->sxk_t, a->sxv_b, a->sxv_t};
+  for (int64_t st : sts)
+    if ((st * es) % 16) return GDN_ERR_ALIGN;
+  if (!a16(a->xq) || !a16(a->xk) || !a16(a->xv)) return GDN_ERR_ALIGN;
+  const int64_t out_es = a->out_dtype == GDN_DTYPE_BF16 ? 2 : 4;
+  if (!a16(a->q) || !a16(a->k) || !a16(a->v) || (a->DK / 32 * out_es) % 4) return GDN_ERR_ALIGN;
+  if (!device_ok()) return GDN_ERR_DEVICE;
+  PrologueParams p;
+  memset(&p, 0, sizeof(p));
+  p.q = {a->xq, a->sxq_b, a->sxq_t, a->wq, a->H * a->DK, a->cq_in, a->cq_out, a->scq_b, a->q};
+  p.k = {a->xk, a->sxk_b, a->sxk_t, a->wk, a->H * a->DK, a->ck_in, a->ck_out, a->sck_b, a->k};
+  p.v = {a->xv, a->sxv_b, a->sxv_t, a->wv, a->H * a->DV, a->cv_in, a->cv_out, a->scv_b, a->v};
+  if ((a->wq && !a16(a->wq)) || (a->wk && !a16(a->wk)) || (a->wv && !a16(a->wv))) return GDN_ERR_ALIGN;
+  p.xa = a->xa; p.xb = a->xb;
+  p.sa_b = a->sxa_b; p.sa_t = a->sxa_t; p.sb_b = a->sxb_b; p.sb_t = a->sxb_t;
+  p.A_log = a->A_log; p.dt_bias = a->dt_bias; p.b_bias = a->b_bias;
+  p.la = a->la; p.beta = a->beta;
+  p.B = (int)a->B; p.T = (int)a->T; p.H = (int)a->H; p.DK = (int)a->DK; p.DV = (int)a->DV;
+  p.taps = a->conv_size; p.clamp = (a->flags & GDN_PROLOGUE_CLAMP_LA) != 0;
+  p.q_scale = a->q_scale; p.eps = a->l2_eps; p.la_min = a->la_min; p.beta_scale = a->beta_scale;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (a->in_dtype == GDN_DTYPE_BF16)
+    return a->out_dtype == GDN_DTYPE_BF16 ? launch_prologue<__nv_bfloat16, __nv_bfloat16>(p, s)
+                                          : launch_prologue<__nv_bfloat16, float>(p, s);
+  return a->out_dtype == GDN_DTYPE_BF16 ? launch_prologue<float, __nv_bfloat16>(p, s) : launch_prologue<float, float>(p, s);
+}
+
+int gdn_layer_epilogue(const gdn_epilogue_args* a, void* stream) {
+  if (!a) return GDN_ERR_NULL;
+  if (!a->y || !a->weight || !a->o) return GDN_ERR_NULL;
+  if (a->B < 1 || a->T < 1 || a->H < 1 || (a->DV != 64 && a->DV != 128 && a->DV != 256 && a->DV != 512)) return GDN_ERR_SHAPE;
+  for (int32_t dt : {a->y_dtype, a->g_dtype, a->o_dtype})
+    if (dt != GDN_DTYPE_BF16 && dt != GDN_DTYPE_F32) return GDN_ERR_DTYPE;
+  if (!a16(a->y) || (a->g && !a16(a->g)) || !a16(a->o)) return GDN_ERR_ALIGN;
+  if (!device_ok()) return GDN_ERR_DEVICE;
+  EpilogueParams p;
+  p.y = a->y; p.sy = a->sy; p.g = a->g; p.sg_b = a->sg_b; p.sg_t = a->sg_t; p.weight = a->weight;
+  p.o = a->o; p.so_b = a->so_b; p.so_t = a->so_t;
+  p.B = (int)a->B; p.T = (int)a->T; p.H = (int)a->H; p.DV = (int)a->DV; p.eps = a->eps;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  using bf = __nv_bfloat16;
+  const int key = a->y_dtype * 4 + a->g_dtype * 2 + a->o_dtype;  // F32 = 0, BF16 = 1
+  switch (key) {
+    case 7: return launch_epilogue<bf, bf, bf>(p, s);
+    case 6: return launch_epilogue<bf, bf, float>(p, s);
+    case 3: return launch_epilogue<float, bf, bf>(p, s);
+    case 2: return launch_epilogue<float, bf, float>(p, s);
+    case 5: return launch_epilogue<bf, float, bf>(p, s);
+    case 4: return launch_epilogue<bf, float, float>(p, s);
+    case 1: return launch_epilogue<float, float, bf>(p, s);
+    default: return launch_epilogue<float, float, float>(p, s);
+  }
+}
+
+}  // extern "C"

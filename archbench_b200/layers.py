@@ -9,8 +9,12 @@
 Both keep ``forward(x) -> y`` (B, T, D) and add an optional ``cache`` argument (a
 ``GDNCache``) that carries the recurrent state and the short-convolution state between calls:
 a call with a cache continues from it (prefill of any length, or one-token decode) and leaves
-the updated state in it.  Projections, the short convolution and the norms are PyTorch; the
-token mixing is ``ops.gdn_prefill`` / ``ops.gdn_decode_step``.  There is no CPU path.
+the updated state in it.  The projections are PyTorch GEMMs; the short convolution, the q/k
+norms and the gates run as one CUDA kernel (``ops.layer_prologue``), the token mixing is
+``ops.gdn_prefill`` / ``ops.gdn_decode_step``, and the output norm and gate one more kernel
+(``ops.layer_epilogue``).  ``fused_io = False`` on a module (or a configuration the kernels do
+not serve: N-step write vectors, conv bias, odd head sizes) keeps those parts in PyTorch.  There
+is no CPU path.
 """
 
 from __future__ import annotations
@@ -69,6 +73,11 @@ def _scan_impl(name: str) -> str:
     raise ValueError(f"unknown scan_impl {name!r}")
 
 
+def _fused_ok(DK: int, DV: int) -> bool:
+    """Head sizes the layer prologue/epilogue kernels serve."""
+    return DK in (64, 128, 256) and DV in (64, 128, 256, 512) and DK <= DV <= 2 * DK
+
+
 def _mix(q, k, v, la, beta, u, cache: Optional[GDNCache], impl: str):
     """Token mixing with an optional cache: prefill (T > 1 or no state) or one decode step."""
     B, T, H, DK = q.shape
@@ -116,12 +125,42 @@ class NStepGDN(nn.Module):
         self.la_min = la_min
         self.o_proj = nn.Linear(self.v_dim, d_model, bias=False)
         self.layer_idx = layer_idx
+        self.fused_io = True
+
+    def _forward_fused(self, x: torch.Tensor, proj: torch.Tensor, cache: Optional[GDNCache]) -> torch.Tensor:
+        B, T, _ = x.shape
+        H, DK, DV = self.H, self.DK, self.DV
+        qd, n_qkv = self.qk_dim, 2 * self.qk_dim + self.v_dim
+        ab0 = n_qkv + self.n_gate
+        conv = state = None
+        if self.conv is not None:
+            w = self.conv.weight.reshape(n_qkv, -1)
+            conv = (w[:qd], w[qd:2 * qd], w[2 * qd:])
+            st = cache.conv.get("qkv") if cache is not None else None
+            if st is not None:
+                state = (st[:, :qd], st[:, qd:2 * qd], st[:, 2 * qd:])
+        dt = torch.bfloat16 if (DK == 128 and self._impl != "recurrent") else torch.float32
+        q, k, v, la, beta, new_state = ops.layer_prologue(
+            proj[..., :qd], proj[..., qd:2 * qd], proj[..., 2 * qd:n_qkv], proj[..., ab0:ab0 + H], proj[..., ab0 + H:ab0 + 2 * H],
+            self.A_log, self.dt_bias, H=H, DK=DK, DV=DV, b_bias=self.b_bias, conv=conv, conv_state=state,
+            want_state=cache is not None, q_scale=DK**-0.5, la_min=self.la_min, out_dtype=dt)
+        if cache is not None and new_state is not None:
+            cache.conv["qkv"] = torch.cat(new_state, 1)
+        y = _mix(q, k, v, la, beta, None, cache, self._impl)
+        if cache is not None:
+            cache.seen += T
+        g = proj[..., n_qkv:n_qkv + self.n_gate] if self.use_gate else None
+        o = ops.layer_epilogue(y, self.norm.weight, g, eps=self.norm.eps, out_dtype=x.dtype)
+        return self.o_proj(o)
 
     def forward(self, x: torch.Tensor, cache: Optional[GDNCache] = None) -> torch.Tensor:
         B, T, _ = x.shape
         H, DK, DV = self.H, self.DK, self.DV
         n_qkv = 2 * self.qk_dim + self.v_dim
         proj = self.in_proj(x)
+        if (self.fused_io and self.n_steps == 1 and _fused_ok(DK, DV) and proj.dtype in (torch.bfloat16, torch.float32)
+                and (self.conv is None or (self.conv.bias is None and self.conv.size <= 4))):
+            return self._forward_fused(x, proj, cache)
         qkv, g, ab = proj[..., :n_qkv], proj[..., n_qkv:n_qkv + self.n_gate], proj[..., n_qkv + self.n_gate:n_qkv + self.n_gate + 2 * H]
         if self.conv is not None:
             qkv, st = self.conv(qkv, None if cache is None else cache.conv.get("qkv"), want_state=cache is not None)
@@ -216,11 +255,38 @@ class GatedDeltaNet(nn.Module):
             self.g_proj = nn.Linear(hidden_size, self.value_dim, bias=False)
         self.o_norm = FusedRMSNormGated(self.head_v_dim, eps=norm_eps)
         self.o_proj = nn.Linear(self.value_dim, hidden_size, bias=False)
+        self.fused_io = True
+
+    def _forward_fused(self, x: torch.Tensor, cache: Optional[GDNCache]) -> torch.Tensor:
+        B, T, _ = x.shape
+        H, DK, DV = self.num_heads, self.head_k_dim, self.head_v_dim
+        conv = state = None
+        if self.use_short_conv:
+            conv = (self.q_conv1d.weight, self.k_conv1d.weight, self.v_conv1d.weight)
+            if cache is not None and cache.conv.get("q") is not None:
+                state = (cache.conv["q"], cache.conv["k"], cache.conv["v"])
+        xq, xk, xv, xa, xb = self.q_proj(x), self.k_proj(x), self.v_proj(x), self.a_proj(x), self.b_proj(x)
+        dt = torch.bfloat16 if DK == 128 else torch.float32
+        q, k, v, la, beta, new_state = ops.layer_prologue(
+            xq, xk, xv, xa.to(xq.dtype), xb.to(xq.dtype), self.A_log, self.dt_bias, H=H, DK=DK, DV=DV, conv=conv,
+            conv_state=state, want_state=cache is not None, q_scale=DK**-0.5, l2_eps=1e-6,
+            beta_scale=2.0 if self.allow_neg_eigval else 1.0, out_dtype=dt)
+        if cache is not None and new_state is not None:
+            cache.conv.update(q=new_state[0], k=new_state[1], v=new_state[2])
+        o = _mix(q, k, v, la, beta, None, cache, "auto")
+        if cache is not None:
+            cache.seen += T
+        g = self.g_proj(x) if self.use_gate else None
+        o = ops.layer_epilogue(o, self.o_norm.weight, g, eps=self.o_norm.eps, out_dtype=x.dtype)
+        return self.o_proj(o)
 
     def forward(self, hidden_states: torch.Tensor, cache: Optional[GDNCache] = None, **kwargs) -> torch.Tensor:
         x = hidden_states
         B, T, _ = x.shape
         want = cache is not None
+        if (self.fused_io and _fused_ok(self.head_k_dim, self.head_v_dim) and not self.conv_bias and self.conv_size <= 4
+                and self.q_proj.weight.dtype in (torch.bfloat16, torch.float32)):
+            return self._forward_fused(x, cache)
         if self.use_short_conv:
             q, sq = self.q_conv1d(self.q_proj(x), None if cache is None else cache.conv.get("q"), want)
             k, sk = self.k_conv1d(self.k_proj(x), None if cache is None else cache.conv.get("k"), want)

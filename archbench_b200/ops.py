@@ -69,6 +69,33 @@ class DecodeArgs(ctypes.Structure):
     ]
 
 
+class PrologueArgs(ctypes.Structure):
+    """Mirror of gdn_prologue_args (include/gdn_b200.h)."""
+
+    _fields_ = [(n, ctypes.c_void_p) for n in ("xq", "xk", "xv")] + \
+               [(n, ctypes.c_int64) for n in ("sxq_b", "sxq_t", "sxk_b", "sxk_t", "sxv_b", "sxv_t")] + \
+               [(n, ctypes.c_void_p) for n in ("xa", "xb")] + \
+               [(n, ctypes.c_int64) for n in ("sxa_b", "sxa_t", "sxb_b", "sxb_t")] + \
+               [(n, ctypes.c_void_p) for n in ("wq", "wk", "wv", "cq_in", "ck_in", "cv_in", "cq_out", "ck_out", "cv_out")] + \
+               [(n, ctypes.c_int64) for n in ("scq_b", "sck_b", "scv_b")] + \
+               [(n, ctypes.c_void_p) for n in ("A_log", "dt_bias", "b_bias", "q", "k", "v", "la", "beta")] + \
+               [(n, ctypes.c_int64) for n in ("B", "T", "H", "DK", "DV")] + \
+               [(n, ctypes.c_int32) for n in ("conv_size", "flags", "in_dtype", "out_dtype")] + \
+               [(n, ctypes.c_float) for n in ("q_scale", "l2_eps", "la_min", "beta_scale")]
+
+
+class EpilogueArgs(ctypes.Structure):
+    """Mirror of gdn_epilogue_args (include/gdn_b200.h)."""
+
+    _fields_ = [("y", ctypes.c_void_p), ("sy", Strides), ("g", ctypes.c_void_p), ("sg_b", ctypes.c_int64),
+                ("sg_t", ctypes.c_int64), ("weight", ctypes.c_void_p), ("o", ctypes.c_void_p), ("so_b", ctypes.c_int64),
+                ("so_t", ctypes.c_int64)] + \
+               [(n, ctypes.c_int64) for n in ("B", "T", "H", "DV")] + \
+               [(n, ctypes.c_int32) for n in ("y_dtype", "g_dtype", "o_dtype")] + [("eps", ctypes.c_float)]
+
+
+GDN_PROLOGUE_CLAMP_LA = 1
+
 # Every symbol include/gdn_b200.h declares, with its ctypes signature.
 SYMBOLS = {
     "gdn_prefill_fwd": ([ctypes.POINTER(PrefillArgs), ctypes.c_void_p], ctypes.c_int),
@@ -80,6 +107,8 @@ SYMBOLS = {
     "gdn_prefill_fwd_static_workspace": ([ctypes.POINTER(PrefillArgs), ctypes.c_void_p], ctypes.c_int),
     "gdn_status_string": ([ctypes.c_int], ctypes.c_char_p),
     "gdn_abi_version": ([], ctypes.c_int),
+    "gdn_layer_prologue": ([ctypes.POINTER(PrologueArgs), ctypes.c_void_p], ctypes.c_int),
+    "gdn_layer_epilogue": ([ctypes.POINTER(EpilogueArgs), ctypes.c_void_p], ctypes.c_int),
 }
 
 _LIB = None
@@ -352,3 +381,82 @@ def selftest_bounded_wait(max_cycles: int = 2_000_000) -> int:
     torch.cuda.synchronize()
     st = device_status(reset=True)
     return st
+
+
+# ------------------------------------------------------------------------------------------------
+# Layer prologue / epilogue (the torch ops around the scan in NStepGDN / GatedDeltaNet.forward)
+
+_DTC = {torch.bfloat16: GDN_DTYPE_BF16, torch.float32: GDN_DTYPE_F32}
+
+
+def _rows16(t: torch.Tensor) -> torch.Tensor:
+    """A (B, T, C) view with unit channel stride and 16-byte aligned (b, t) strides, else a copy."""
+    es = t.element_size()
+    if t.stride(-1) != 1 or t.data_ptr() % 16 or (t.stride(0) * es) % 16 or (t.stride(1) * es) % 16:
+        t = t.contiguous()
+    return t
+
+
+def layer_prologue(xq, xk, xv, xa, xb, A_log, dt_bias, *, H, DK, DV, b_bias=None, conv=None, conv_state=None,
+                   want_state=False, q_scale=1.0, l2_eps=1e-12, la_min=None, beta_scale=1.0, out_dtype=torch.bfloat16):
+    """q, k, v (B, T, H, D) in ``out_dtype`` and la, beta (B, T, H) fp32 from the layer's
+    projections, in one CUDA kernel: SiLU(short causal conv) of each projection, l2-normalised q
+    (times ``q_scale``) and k, la = -softplus(a + dt_bias) exp(A_log) (clamped at ``la_min``),
+    beta = sigmoid(b + b_bias) * beta_scale.  ``conv`` = (wq, wk, wv) weights of shape
+    (channels, conv_size) (or the layer's (channels, 1, conv_size)) or None (SiLU only); ``conv_state`` = (cq, ck, cv) of shape
+    (B, channels, conv_size - 1) continues a previous call.  Returns (q, k, v, la, beta, new_state)
+    with new_state None unless ``want_state``."""
+    _check_cuda(xq, xk, xv, xa, xb)
+    dt = xq.dtype
+    if dt not in _DTC or any(t.dtype != dt for t in (xk, xv, xa, xb)):
+        raise ValueError("projections must share one dtype, bf16 or fp32")
+    xq, xk, xv = _rows16(xq), _rows16(xk), _rows16(xv)
+    B, T, _ = xq.shape
+    dev = xq.device
+    q = torch.empty(B, T, H, DK, device=dev, dtype=out_dtype)
+    k = torch.empty(B, T, H, DK, device=dev, dtype=out_dtype)
+    v = torch.empty(B, T, H, DV, device=dev, dtype=out_dtype)
+    la = torch.empty(B, T, H, device=dev, dtype=torch.float32)
+    beta = torch.empty(B, T, H, device=dev, dtype=torch.float32)
+    taps = 1 if conv is None else conv[0].shape[-1]
+    ws = [None, None, None] if conv is None else [w.reshape(w.shape[0], taps).float().t().contiguous() for w in conv]
+    cin = [None, None, None] if conv_state is None else [c.to(dt).contiguous() for c in conv_state]
+    cout = [None, None, None]
+    if want_state and taps > 1:
+        cout = [torch.empty(B, ch, taps - 1, device=dev, dtype=dt) for ch in (H * DK, H * DK, H * DV)]
+    A_log, dt_bias = A_log.float().contiguous(), dt_bias.float().contiguous()
+    b_bias = None if b_bias is None else b_bias.float().contiguous()
+    st = lambda c: 0 if c is None else c.stride(0)
+    a = PrologueArgs(
+        _ptr(xq), _ptr(xk), _ptr(xv), xq.stride(0), xq.stride(1), xk.stride(0), xk.stride(1), xv.stride(0), xv.stride(1),
+        _ptr(xa), _ptr(xb), xa.stride(0), xa.stride(1), xb.stride(0), xb.stride(1),
+        *[_ptr(w) for w in ws], *[_ptr(c) for c in cin], *[_ptr(c) for c in cout],
+        st(cout[0] if cout[0] is not None else cin[0]), st(cout[1] if cout[1] is not None else cin[1]),
+        st(cout[2] if cout[2] is not None else cin[2]),
+        _ptr(A_log), _ptr(dt_bias), _ptr(b_bias), _ptr(q), _ptr(k), _ptr(v), _ptr(la), _ptr(beta),
+        B, T, H, DK, DV, taps, GDN_PROLOGUE_CLAMP_LA if la_min is not None else 0, _DTC[dt], _DTC[out_dtype],
+        float(q_scale), float(l2_eps), float(la_min if la_min is not None else 0.0), float(beta_scale))
+    for t in (xa, xb):
+        if t.stride(-1) != 1:
+            raise ValueError("gate projections need a unit last stride")
+    _check(load_library().gdn_layer_prologue(ctypes.byref(a), ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)))
+    return q, k, v, la, beta, (tuple(cout) if want_state and taps > 1 else None)
+
+
+def layer_epilogue(y, weight, g=None, eps=1e-5, out_dtype=torch.bfloat16):
+    """o (B, T, H*DV) = RMSNorm over each head's DV values of y (B, T, H, DV) times ``weight``,
+    times SiLU(g) when g (B, T, H*DV) is given; fp32 arithmetic, one rounding to ``out_dtype``."""
+    _check_cuda(y, g)
+    if y.dtype not in _DTC or (g is not None and g.dtype not in _DTC):
+        raise ValueError("y and g must be bf16 or fp32")
+    B, T, H, DV = y.shape
+    y = _prep_token(y, "y", y.dtype)
+    if g is not None:
+        g = _rows16(g.reshape(B, T, H * DV))
+    o = torch.empty(B, T, H * DV, device=y.device, dtype=out_dtype)
+    w = weight.float().contiguous()
+    a = EpilogueArgs(_ptr(y), _tok_strides(y), _ptr(g), 0 if g is None else g.stride(0), 0 if g is None else g.stride(1),
+                     _ptr(w), _ptr(o), o.stride(0), o.stride(1), B, T, H, DV, _DTC[y.dtype],
+                     _DTC[g.dtype] if g is not None else GDN_DTYPE_F32, _DTC[out_dtype], float(eps))
+    _check(load_library().gdn_layer_epilogue(ctypes.byref(a), ctypes.c_void_p(torch.cuda.current_stream(y.device).cuda_stream)))
+    return o

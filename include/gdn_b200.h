@@ -153,6 +153,80 @@ int gdn_prefill_workspace_bytes(const gdn_prefill_args* args, size_t* bytes);
 #define GDN_STATIC_WORKSPACE_BYTES (16u << 20)
 int gdn_prefill_fwd_static_workspace(const gdn_prefill_args* args, void* stream);
 
+/*
+ * Layer prologue: the token-mixing inputs of one gated-DeltaNet layer, from its projections, in one
+ * bandwidth-bound kernel.  Per (b, t, h): q, k, v = SiLU(depthwise causal conv of conv_size taps)
+ * of their projections (computed in the projection dtype, as F.conv1d and F.silu do); then
+ * q = q / max(|q|, l2_eps) * q_scale, k = k / max(|k|, l2_eps); la = -softplus(a + dt_bias) *
+ * exp(A_log), clamped below at la_min when flags has GDN_PROLOGUE_CLAMP_LA; beta =
+ * sigmoid(b + b_bias) * beta_scale.  The last conv_size - 1 projection rows of every channel
+ * (with the incoming state before t = 0) are written as the next call's conv state.
+ *
+ * Replaces the torch ops between the projections and the scan in archbench's NStepGDN.forward
+ * (archbench/layers/nsgdn.py:520-536: ShortConv nsgdn.py:457-470, F.normalize, the gate and
+ * beta; n_steps = 1) and in fla's GatedDeltaNet.forward (fla/layers/gated_deltanet.py:240-279:
+ * q/k/v_conv1d, the kernel-side l2norm with eps 1e-6, the gate and beta).
+ */
+#define GDN_PROLOGUE_CLAMP_LA 1
+typedef struct {
+  const void* xq;     /* q projection [B][T][H*DK] before the conv, dtype in_dtype */
+  const void* xk;     /* k projection [B][T][H*DK] */
+  const void* xv;     /* v projection [B][T][H*DV] */
+  int64_t sxq_b, sxq_t, sxk_b, sxk_t, sxv_b, sxv_t;  /* element strides of b and t (16-byte multiples) */
+  const void* xa;     /* gate pre-activation a [B][T][H], dtype in_dtype */
+  const void* xb;     /* beta pre-activation b [B][T][H] */
+  int64_t sxa_b, sxa_t, sxb_b, sxb_t;
+  const float* wq;    /* conv weights (conv_size, H*DK) fp32, tap-major (the transpose of the
+                         layer's (channels, 1, conv_size) parameter), 16-byte aligned, or NULL:
+                         no conv, SiLU only */
+  const float* wk;
+  const float* wv;    /* (conv_size, H*DV) */
+  const void* cq_in;  /* conv states (B, channels, conv_size - 1), dtype in_dtype, or NULL: zero history */
+  const void* ck_in;
+  const void* cv_in;
+  void* cq_out;       /* next conv states, same layout, or NULL; must not overlap the _in states */
+  void* ck_out;
+  void* cv_out;
+  int64_t scq_b, sck_b, scv_b;  /* batch strides of the conv states, in elements */
+  const float* A_log; /* (H) fp32 */
+  const float* dt_bias; /* (H) fp32 */
+  const float* b_bias;  /* (H) fp32, or NULL */
+  void* q;            /* [B][T][H][DK] contiguous, dtype out_dtype */
+  void* k;
+  void* v;            /* [B][T][H][DV] contiguous */
+  float* la;          /* (B, T, H) fp32 */
+  float* beta;        /* (B, T, H) fp32 */
+  int64_t B, T, H, DK, DV;  /* DK in {64, 128, 256}, DK <= DV <= 2 DK, DV a power of two */
+  int32_t conv_size;  /* 1 .. 4 taps */
+  int32_t flags;      /* GDN_PROLOGUE_CLAMP_LA */
+  int32_t in_dtype;   /* gdn_dtype of the projections and conv states */
+  int32_t out_dtype;  /* gdn_dtype of q, k, v */
+  float q_scale, l2_eps, la_min, beta_scale;
+} gdn_prologue_args;
+
+int gdn_layer_prologue(const gdn_prologue_args* args, void* stream);
+
+/*
+ * Layer epilogue: o = y / sqrt(mean(y^2) + eps) * weight * SiLU(g) over each head's DV values, in
+ * fp32 and rounded once to o_dtype (g == NULL: no gate).  Replaces the RMSNorm and gate of
+ * archbench's NStepGDN.forward (archbench/layers/nsgdn.py:539-541) and fla's FusedRMSNormGated
+ * in GatedDeltaNet.forward (fla/layers/gated_deltanet.py:307-313).
+ */
+typedef struct {
+  const void* y;      /* [B][T][H][DV] token-mixing output, 16-byte aligned */
+  gdn_strides sy;
+  const void* g;      /* gate [B][T][H*DV], or NULL */
+  int64_t sg_b, sg_t;
+  const float* weight;  /* (DV) fp32 */
+  void* o;            /* [B][T][H*DV] */
+  int64_t so_b, so_t;
+  int64_t B, T, H, DV;  /* DV in {64, 128, 256, 512} */
+  int32_t y_dtype, g_dtype, o_dtype;
+  float eps;
+} gdn_epilogue_args;
+
+int gdn_layer_epilogue(const gdn_epilogue_args* args, void* stream);
+
 /* Which kernel a prefill with these arguments runs (GDN_IMPL_CHUNK_CLUSTER, _CHUNK_SINGLE,
  * _SEGMENTED or _RECURRENT; GDN_IMPL_CHUNK resolves to one of the two chunk variants), or a
  * negative gdn_status if the arguments are invalid.  Launches nothing. */

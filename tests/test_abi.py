@@ -34,6 +34,28 @@ def test_struct_layout_matches_header():
     # pointers 9*8, strides 5*24, sizes 5*8, ints 4*4
     assert ctypes.sizeof(ops.PrefillArgs) == 9 * 8 + 5 * 24 + 5 * 8 + 4 * 4 + 8 + 8
     assert ctypes.sizeof(ops.DecodeArgs) == 8 * 8 + 5 * 24 + 4 * 8 + 2 * 4
+    # pointers 22*8, int64 18*8, 4 int32 + 4 float
+    assert ctypes.sizeof(ops.PrologueArgs) == 22 * 8 + 18 * 8 + 4 * 4 + 4 * 4
+    assert ctypes.sizeof(ops.EpilogueArgs) == 4 * 8 + 24 + 8 * 8 + 3 * 4 + 4
+
+
+def test_layer_io_argument_checks():
+    lib = ops.load_library()
+    a = ops.PrologueArgs()
+    assert lib.gdn_layer_prologue(ctypes.byref(a), None) == -1
+    e = ops.EpilogueArgs()
+    assert lib.gdn_layer_epilogue(ctypes.byref(e), None) == -1
+    assert lib.gdn_layer_prologue(None, None) == -1 and lib.gdn_layer_epilogue(None, None) == -1
+    # all pointers set (never dereferenced), bad conv size and head size answer before any device use
+    ptrs = {n: 0x10000 * (i + 1) for i, n in enumerate(("xq", "xk", "xv", "xa", "xb", "A_log", "dt_bias", "q", "k", "v", "la", "beta"))}
+    a = ops.PrologueArgs(**ptrs, B=1, T=8, H=2, DK=128, DV=128, conv_size=9, in_dtype=1, out_dtype=1)
+    assert lib.gdn_layer_prologue(ctypes.byref(a), None) == -2
+    a.conv_size, a.DK = 4, 96
+    assert lib.gdn_layer_prologue(ctypes.byref(a), None) == -2
+    a.DK, a.in_dtype = 128, 7
+    assert lib.gdn_layer_prologue(ctypes.byref(a), None) == -3
+    e = ops.EpilogueArgs(y=0x10000, weight=0x20000, o=0x30000, B=1, T=1, H=1, DV=100, y_dtype=1, g_dtype=1, o_dtype=1)
+    assert lib.gdn_layer_epilogue(ctypes.byref(e), None) == -2
 
 
 def fake_args(**kw):
