@@ -1,6 +1,6 @@
 """Benchmark of the gated-DeltaNet hot path on B200 (one JSON line on rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--skip-extra]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--skip-extra] [--only decode]
     torchrun --nproc-per-node N bench.py --gpus N ...
 
 Headline (``value``): chunkwise prefill of configuration 1 -- B=8, T=4096, H=8, DK=DV=128,
@@ -354,6 +354,12 @@ def cpu_baseline(budget_s=12.0):
 
 def run_ours(args):
     rank, world, local = dist_init(args.gpus)
+    if args.only == "decode":  # one leg alone (profiling runs): its own object, not the bench line
+        res = bench_decode(args, rank, world)
+        if rank == 0:
+            print(json.dumps({"leg": "decode", **res}), flush=True)
+        finish(world)
+        return
     res = bench_prefill(args, rank, world)
     line = {
         "metric": METRIC, "value": res["value"], "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -427,6 +433,8 @@ def main():
     ap.add_argument("--prefill-impl", choices=["auto", "chunk", "chunk_cluster", "chunk_single", "recurrent", "segmented"], default="auto")
     ap.add_argument("--skip-extra", action="store_true", help="headline prefill only")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the cpu_baseline leg")
+    ap.add_argument("--only", choices=["decode"], default=None,
+                    help="run one extra leg alone and print its object (for profiling)")
     ap.add_argument("--no-graph", dest="graph", action="store_false",
                     help="time plain calls instead of CUDA-graph replays of one call")
     args = ap.parse_args()

@@ -130,3 +130,76 @@ def recurrence_c(q, k, v, la, beta=None, u=None, s0=None, nthreads=None):
     if rc != 0:
         raise RuntimeError(f"gdn_oracle_recurrence failed ({rc})")
     return y, S
+
+
+# ---------------------------------------------------------------------------------------------
+# Backward of the recurrence (float64 numpy), for checking the CUDA backward.
+# ---------------------------------------------------------------------------------------------
+
+
+def recurrence_bwd(q, k, v, la, dy, beta=None, u=None, s0=None, ds_T=None, chunk=64, dtype=np.float64):
+    """Gradients of the token-serial recurrence for incoming gradients ``dy`` (of y) and ``ds_T``
+    (of the final state).
+
+    Restates archbench's own backward of the recurrence (archbench/layers/nsgdn.py:112-155,
+    ``_nsgdn_bwd_kernel``): states are checkpointed at chunk starts in a forward sweep; each chunk,
+    last to first, recomputes its per-token states and then walks its tokens backwards with the
+    state gradient G (DV x DK per (b, h)):
+
+        G += dy_t q_t^T;  dr = G u_t (= dv_t);  du_t = G^T r_t;  G -= dr k_t^T;
+        dk_t = -Sp_t^T dr;  dla_t = <G, Sp_t>;  G = alpha_t G
+
+    with Sp_t = alpha_t S_{t-1} the decayed state and dq_t = S_t^T dy_t (nsgdn.py:130-134).
+    With ``beta`` (u = beta k) the write-vector gradient is folded in: dk += beta du and
+    dbeta = du . k.
+
+    Returns a dict with dq, dk, dv, dla, ds0 and du (``u`` given) or dbeta (``beta`` given).
+    """
+    q, k, v, la, dy = (np.asarray(a, dtype=dtype) for a in (q, k, v, la, dy))
+    if (beta is None) == (u is None):
+        raise ValueError("give exactly one of beta and u")
+    uu = np.asarray(beta, dtype=dtype)[..., None] * k if u is None else np.asarray(u, dtype=dtype)
+    B, T, H, DK = q.shape
+    DV = v.shape[-1]
+    S = np.zeros((B, H, DV, DK), dtype=dtype) if s0 is None else np.array(s0, dtype=dtype, copy=True)
+    starts = list(range(0, T, chunk))
+    ckpt = []
+    for c0 in starts:  # forward sweep: state at every chunk start
+        ckpt.append(S.copy())
+        for t in range(c0, min(T, c0 + chunk)):
+            S *= np.exp(la[:, t])[..., None, None]
+            r = v[:, t] - np.einsum("bhij,bhj->bhi", S, k[:, t])
+            S += r[..., :, None] * uu[:, t][..., None, :]
+    dq, dk, du = np.zeros_like(q), np.zeros_like(q), np.zeros_like(q)
+    dv, dla = np.zeros_like(v), np.zeros_like(la)
+    G = np.zeros((B, H, DV, DK), dtype=dtype) if ds_T is None else np.array(ds_T, dtype=dtype, copy=True)
+    for c0, S0 in zip(reversed(starts), reversed(ckpt)):
+        ts = list(range(c0, min(T, c0 + chunk)))
+        S = S0.copy()
+        Sp, R = [], []
+        for t in ts:  # recompute the chunk: decayed states and residuals
+            S *= np.exp(la[:, t])[..., None, None]
+            r = v[:, t] - np.einsum("bhij,bhj->bhi", S, k[:, t])
+            Sp.append(S.copy())
+            R.append(r)
+            S += r[..., :, None] * uu[:, t][..., None, :]
+            dq[:, t] = np.einsum("bhij,bhi->bhj", S, dy[:, t])
+        for i in reversed(range(len(ts))):
+            t = ts[i]
+            G += dy[:, t][..., :, None] * q[:, t][..., None, :]
+            dr = np.einsum("bhij,bhj->bhi", G, uu[:, t])
+            dv[:, t] = dr
+            du[:, t] = np.einsum("bhij,bhi->bhj", G, R[i])
+            G -= dr[..., :, None] * k[:, t][..., None, :]
+            dk[:, t] = -np.einsum("bhij,bhi->bhj", Sp[i], dr)
+            dla[:, t] = np.einsum("bhij,bhij->bh", G, Sp[i])
+            G *= np.exp(la[:, t])[..., None, None]
+    out = {"dq": dq, "dv": dv, "dla": dla, "ds0": G}
+    if u is None:
+        b = np.asarray(beta, dtype=dtype)
+        out["dk"] = dk + b[..., None] * du
+        out["dbeta"] = (du * k).sum(-1)
+    else:
+        out["dk"] = dk
+        out["du"] = du
+    return out

@@ -14,7 +14,14 @@ What it records (all float32 arithmetic, CPU):
         read y = S e_j = column j of the final state.
   * the write vectors of ``write_direction`` (nsgdn.py:61-75) for n_steps = 2, used as u;
   * fla 0.5.1's ``naive_recurrent_gated_delta_rule`` (fla/ops/gated_delta_rule/naive.py:13),
-    which takes an initial state and returns the final state directly (state layout [K, V]).
+    which takes an initial state and returns the final state directly (state layout [K, V]);
+  * gradients of ``nsgdn_ref`` (float64 torch autograd through the reference's own loop, with the
+    same prefix/suffix tokens for S0 and S_T) for given incoming gradients dy and dS_T: the
+    gradient of S0 is the gradient of the prefix tokens' v, and dS_T enters as the suffix
+    tokens' dy.  Once with u a leaf (du), once with u = beta k from ``write_direction``
+    (dbeta, and dk including the write-vector path).
+
+    python tests/golden/make_golden.py [/path/to/archbench-checkout] [--only NAME]
 """
 
 from __future__ import annotations
@@ -63,6 +70,30 @@ def digest(*arrays):
     for a in arrays:
         h.update(np.ascontiguousarray(a).tobytes())
     return h.hexdigest()
+
+
+def bwd_fixture(nsgdn_ref, write_direction):
+    """Gradients of archbench's nsgdn_ref (float64) with an initial state and a final-state readout."""
+    B, T, H, DK, DV = 1, 100, 2, 32, 32
+    x = {n: t.double() for n, t in make_inputs(B, T, H, DK, DV, seed=41, dtype=torch.float64).items()}
+    g = torch.Generator().manual_seed(42)
+    s0 = 0.5 * torch.randn(B, H, DV, DK, generator=g, dtype=torch.float64)
+    dy = torch.randn(B, T, H, DV, generator=g, dtype=torch.float64)
+    dsT = torch.randn(B, H, DV, DK, generator=g, dtype=torch.float64)
+    u_leaf = 0.7 * x["k"] + 0.1 * torch.randn(B, T, H, DK, generator=g, dtype=torch.float64)
+    d = dict(q=x["q"], k=x["k"], v=x["v"], beta=x["beta"], la=x["la"], s0=s0, dy=dy, dsT=dsT, u=u_leaf)
+    for mode in ("u", "beta"):
+        leaves = {n: d[n].clone().requires_grad_(True) for n in ("q", "k", "v", "la", "s0", "u" if mode == "u" else "beta")}
+        if mode == "u":
+            u = leaves["u"]
+        else:
+            u = write_direction(leaves["k"], torch.zeros_like(leaves["k"]), leaves["beta"], torch.ones(H, dtype=torch.float64), 1)
+        y, sT = run_with_state(nsgdn_ref, leaves["q"], leaves["k"], u, leaves["v"], leaves["la"], leaves["s0"])
+        loss = (y * dy).sum() + (sT * dsT).sum()
+        grads = torch.autograd.grad(loss, list(leaves.values()))
+        for n, gr in zip(leaves, grads):
+            d[f"{mode}_d{n}"] = gr.detach()
+    return d
 
 
 def main(ref_root):
@@ -114,11 +145,22 @@ def main(ref_root):
     o, hT = naive_recurrent_gated_delta_rule(x["q"], x["k"], x["v"], x["beta"], x["la"], scale=1.0, initial_state=h0, output_final_state=True)
     out["fla_naive"] = dict(q=x["q"], k=x["k"], v=x["v"], beta=x["beta"], la=x["la"], h0=h0, y=o, hT=hT)
 
+    out["bwd_small"] = bwd_fixture(nsgdn_ref, write_direction)
+
     for name, d in out.items():
+        if ONLY and name != ONLY:
+            continue
         arrs = {k: (v.numpy() if isinstance(v, torch.Tensor) else v) for k, v in d.items()}
         np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **arrs)
         print(name, {k: getattr(v, "shape", ()) for k, v in arrs.items()})
 
 
+ONLY = None
+
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    argv = sys.argv[1:]
+    if "--only" in argv:
+        i = argv.index("--only")
+        ONLY = argv[i + 1]
+        del argv[i : i + 2]
+    main(argv[0] if argv else "/root/reference")

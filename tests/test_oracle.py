@@ -90,3 +90,16 @@ def test_errors_helper():
     assert O.errors(np.ones(3), np.ones(3)) == (0.0, 0.0)
     mx, rel = O.errors(np.array([1.0, 2.0]), np.array([1.0, 1.0]))
     assert mx == 1.0 and abs(rel - 1 / np.sqrt(2)) < 1e-12
+
+
+@pytest.mark.parametrize("mode", ["u", "beta"])
+def test_backward_oracle_matches_reference_autograd(mode):
+    """The oracle's backward against float64 autograd through archbench's own nsgdn_ref."""
+    d = load("bwd_small")
+    kw = dict(u=d["u"]) if mode == "u" else dict(beta=d["beta"])
+    for chunk in (64, 16):
+        g = O.recurrence_bwd(d["q"], d["k"], d["v"], d["la"], d["dy"], s0=d["s0"], ds_T=d["dsT"], chunk=chunk, **kw)
+        names = ["dq", "dk", "dv", "dla", "ds0", "du" if mode == "u" else "dbeta"]
+        for n in names:
+            mx, rel = O.errors(g[n], d[f"{mode}_{n}"])
+            assert mx < 1e-10 and rel < 1e-12, (n, chunk, mx, rel)
