@@ -13,8 +13,10 @@ the updated state in it.  The projections are PyTorch GEMMs; the short convoluti
 norms and the gates run as one CUDA kernel (``ops.layer_prologue``), the token mixing is
 ``ops.gdn_prefill`` / ``ops.gdn_decode_step``, and the output norm and gate one more kernel
 (``ops.layer_epilogue``).  ``fused_io = False`` on a module (or a configuration the kernels do
-not serve: N-step write vectors, conv bias, odd head sizes) keeps those parts in PyTorch.  There
-is no CPU path.
+not serve: N-step write vectors, conv bias, odd head sizes) keeps those parts in PyTorch, and so
+does every call that builds an autograd graph (training): there the scan runs forward and
+backward on the CUDA kernels (DK = DV = 128) and the rest through PyTorch autograd.  There is no
+CPU path.
 """
 
 from __future__ import annotations
@@ -76,6 +78,13 @@ def _scan_impl(name: str) -> str:
 def _fused_ok(DK: int, DV: int) -> bool:
     """Head sizes the layer prologue/epilogue kernels serve."""
     return DK in (64, 128, 256) and DV in (64, 128, 256, 512) and DK <= DV <= 2 * DK
+
+
+def _training(x: torch.Tensor, m: nn.Module) -> bool:
+    """True when this call builds an autograd graph.  The fused prologue/epilogue kernels have no
+    backward, so such calls run those parts in PyTorch; the scan's backward is the CUDA one
+    (``ops.gdn_prefill`` is differentiable)."""
+    return torch.is_grad_enabled() and (x.requires_grad or any(p.requires_grad for p in m.parameters()))
 
 
 def _mix(q, k, v, la, beta, u, cache: Optional[GDNCache], impl: str):
@@ -159,7 +168,7 @@ class NStepGDN(nn.Module):
         n_qkv = 2 * self.qk_dim + self.v_dim
         proj = self.in_proj(x)
         if (self.fused_io and self.n_steps == 1 and _fused_ok(DK, DV) and proj.dtype in (torch.bfloat16, torch.float32)
-                and (self.conv is None or (self.conv.bias is None and self.conv.size <= 4))):
+                and (self.conv is None or (self.conv.bias is None and self.conv.size <= 4)) and not _training(x, self)):
             return self._forward_fused(x, proj, cache)
         qkv, g, ab = proj[..., :n_qkv], proj[..., n_qkv:n_qkv + self.n_gate], proj[..., n_qkv + self.n_gate:n_qkv + self.n_gate + 2 * H]
         if self.conv is not None:
@@ -285,7 +294,7 @@ class GatedDeltaNet(nn.Module):
         B, T, _ = x.shape
         want = cache is not None
         if (self.fused_io and _fused_ok(self.head_k_dim, self.head_v_dim) and not self.conv_bias and self.conv_size <= 4
-                and self.q_proj.weight.dtype in (torch.bfloat16, torch.float32)):
+                and self.q_proj.weight.dtype in (torch.bfloat16, torch.float32) and not _training(x, self)):
             return self._forward_fused(x, cache)
         if self.use_short_conv:
             q, sq = self.q_conv1d(self.q_proj(x), None if cache is None else cache.conv.get("q"), want)

@@ -94,6 +94,17 @@ class EpilogueArgs(ctypes.Structure):
                [(n, ctypes.c_int32) for n in ("y_dtype", "g_dtype", "o_dtype")] + [("eps", ctypes.c_float)]
 
 
+class BackwardArgs(ctypes.Structure):
+    """Mirror of gdn_backward_args (include/gdn_b200.h)."""
+
+    _fields_ = [(n, ctypes.c_void_p) for n in ("q", "k", "u", "v", "beta", "la", "s0", "dy", "ds_T",
+                                                 "dq", "dk", "du", "dv", "dbeta", "dla", "ds0")] + \
+               [(n, Strides) for n in ("sq", "sk", "su", "sv", "sdy")] + \
+               [(n, ctypes.c_int64) for n in ("B", "T", "H", "DK", "DV")] + \
+               [("in_dtype", ctypes.c_int32), ("dy_dtype", ctypes.c_int32), ("workspace", ctypes.c_void_p),
+                ("workspace_bytes", ctypes.c_uint64)]
+
+
 GDN_PROLOGUE_CLAMP_LA = 1
 
 # Every symbol include/gdn_b200.h declares, with its ctypes signature.
@@ -109,6 +120,8 @@ SYMBOLS = {
     "gdn_abi_version": ([], ctypes.c_int),
     "gdn_layer_prologue": ([ctypes.POINTER(PrologueArgs), ctypes.c_void_p], ctypes.c_int),
     "gdn_layer_epilogue": ([ctypes.POINTER(EpilogueArgs), ctypes.c_void_p], ctypes.c_int),
+    "gdn_prefill_bwd_workspace_bytes": ([ctypes.POINTER(BackwardArgs), ctypes.POINTER(ctypes.c_size_t)], ctypes.c_int),
+    "gdn_prefill_bwd": ([ctypes.POINTER(BackwardArgs), ctypes.c_void_p], ctypes.c_int),
 }
 
 _LIB = None
@@ -226,6 +239,49 @@ def _prefill_impl(q, k, u, v, la, beta, s0, output_final_state: bool, out_dtype:
     return y, s_out
 
 
+def _prefill_bwd_impl(q, k, u, v, la, beta, s0, dy, ds_T, want_ds0: bool):
+    """Gradients of a prefill (see gdn_prefill_bwd): (dq, dk, du_or_dbeta, dv, dla, ds0), fp32;
+    du_or_dbeta is du (B, T, H, DK) when u is given, else dbeta (B, T, H); ds0 is empty unless
+    ``want_ds0``."""
+    _check_cuda(q, k, u, v, la, beta, s0, dy, ds_T)
+    in_dtype = torch.bfloat16 if q.dtype == torch.bfloat16 else torch.float32
+    q, k, v = (_prep_token(t, n, in_dtype) for t, n in ((q, "q"), (k, "k"), (v, "v")))
+    u = None if u is None else _prep_token(u, "u", in_dtype)
+    dy = _prep_token(dy, "dy", torch.bfloat16 if dy.dtype == torch.bfloat16 else torch.float32)
+    B, T, H, DK = q.shape
+    DV = v.shape[-1]
+    if DK != 128 or DV != 128:
+        raise NotImplementedError(f"the prefill backward serves DK = DV = 128 (got DK={DK}, DV={DV})")
+    if dy.shape != (B, T, H, DV):
+        raise ValueError(f"dy must be {(B, T, H, DV)}, got {tuple(dy.shape)}")
+    la = la.float().contiguous()
+    beta = None if u is not None else beta.float().contiguous()
+    s0 = None if s0 is None else s0.float().contiguous()
+    ds_T = None if ds_T is None else ds_T.float().contiguous()
+    dev = q.device
+    dq = torch.empty(B, T, H, DK, device=dev, dtype=torch.float32)
+    dk = torch.empty_like(dq)
+    dv = torch.empty(B, T, H, DV, device=dev, dtype=torch.float32)
+    dla = torch.empty(B, T, H, device=dev, dtype=torch.float32)
+    du = torch.empty_like(dq) if u is not None else None
+    dbeta = torch.empty(B, T, H, device=dev, dtype=torch.float32) if u is None else None
+    ds0 = torch.empty(B, H, DV, DK, device=dev, dtype=torch.float32) if want_ds0 else None
+    a = BackwardArgs(
+        _ptr(q), _ptr(k), _ptr(u), _ptr(v), _ptr(beta), _ptr(la), _ptr(s0), _ptr(dy), _ptr(ds_T),
+        _ptr(dq), _ptr(dk), _ptr(du), _ptr(dv), _ptr(dbeta), _ptr(dla), _ptr(ds0),
+        _tok_strides(q), _tok_strides(k), _tok_strides(u) if u is not None else Strides(0, 0, 0), _tok_strides(v), _tok_strides(dy),
+        B, T, H, DK, DV, _DT[in_dtype], _DT[dy.dtype], None, 0)
+    lib = load_library()
+    with torch.cuda.device(dev):
+        need = ctypes.c_size_t(0)
+        _check(lib.gdn_prefill_bwd_workspace_bytes(ctypes.byref(a), ctypes.byref(need)))
+        ws = torch.empty(max(need.value, 1), dtype=torch.uint8, device=dev)  # through torch's caching allocator
+        a.workspace, a.workspace_bytes = ws.data_ptr(), need.value
+        _check(lib.gdn_prefill_bwd(ctypes.byref(a), ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)))
+    empty = q.new_empty(0, dtype=torch.float32)
+    return dq, dk, (du if u is not None else dbeta), dv, dla, (ds0 if ds0 is not None else empty)
+
+
 def _dec_strides(t: torch.Tensor) -> Strides:
     return Strides(t.stride(0), 0, t.stride(1))
 
@@ -283,6 +339,61 @@ def _(q, k, u, v, la, beta, s0, output_final_state, out_dtype_code, impl):
     y = q.new_empty(B, T, H, DV, dtype=_DTYPE_CODE[out_dtype_code])
     s = q.new_empty(B, H, DV, DK, dtype=torch.float32) if output_final_state else q.new_empty(0, dtype=torch.float32)
     return y, s
+
+
+@torch.library.custom_op("archbench_b200::prefill_bwd", mutates_args=())
+def _prefill_bwd_op(
+    q: torch.Tensor, k: torch.Tensor, u: Optional[torch.Tensor], v: torch.Tensor, la: torch.Tensor,
+    beta: Optional[torch.Tensor], s0: Optional[torch.Tensor], dy: torch.Tensor, ds_T: Optional[torch.Tensor], want_ds0: bool,
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    return _prefill_bwd_impl(q, k, u, v, la, beta, s0, dy, ds_T, want_ds0)
+
+
+@_prefill_bwd_op.register_fake
+def _(q, k, u, v, la, beta, s0, dy, ds_T, want_ds0):
+    B, T, H, DK = q.shape
+    DV = v.shape[-1]
+    f = lambda *shape: q.new_empty(*shape, dtype=torch.float32)
+    return (f(B, T, H, DK), f(B, T, H, DK), f(B, T, H, DK) if u is not None else f(B, T, H), f(B, T, H, DV), f(B, T, H),
+            f(B, H, DV, DK) if want_ds0 else f(0))
+
+
+def _prefill_setup(ctx, inputs, output):
+    q, k, u, v, la, beta, s0, output_final_state, out_dtype_code, impl = inputs
+    ctx.output_final_state = output_final_state
+    ctx.has = (u is not None, beta is not None, s0 is not None)
+    ctx.save_for_backward(q, k, u, v, la, beta, s0)
+
+
+def _prefill_backward(ctx, gy, gs):
+    """Autograd of archbench_b200::prefill: the chunked backward kernels (gdn_prefill_bwd).
+    Mirrors the autograd registration of archbench's scan ops (archbench/layers/nsgdn.py:206-216,
+    386-397)."""
+    q, k, u, v, la, beta, s0 = ctx.saved_tensors
+    if gy is None:
+        gy = torch.zeros(*q.shape[:3], v.shape[-1], device=q.device, dtype=torch.float32)
+    ds_T = gs if (ctx.output_final_state and gs is not None and gs.numel() > 0) else None
+    dq, dk, dub, dv, dla, ds0 = _prefill_bwd_op(q, k, u, v, la, beta, s0, gy, ds_T, s0 is not None)
+    cast = lambda g, ref: None if ref is None else g.to(ref.dtype)
+    return (cast(dq, q), cast(dk, k), cast(dub, u) if u is not None else None, cast(dv, v), cast(dla, la),
+            cast(dub, beta) if u is None and beta is not None else None, cast(ds0, s0) if s0 is not None else None,
+            None, None, None)
+
+
+_prefill_op.register_autograd(_prefill_backward, setup_context=_prefill_setup)
+
+
+def gdn_prefill_bwd(q, k, v, la, dy, beta=None, u=None, initial_state=None, ds_T=None, want_ds0=False):
+    """Gradients of ``gdn_prefill`` for incoming dy (B, T, H, DV) and ds_T (B, H, DV, DK) or None.
+    Returns a dict of fp32 tensors: dq, dk, dv, dla, du (u given) or dbeta, and ds0 if ``want_ds0``.
+    DK = DV = 128."""
+    if (u is None) == (beta is None):
+        raise ValueError("give exactly one of beta (u = beta * k) and u")
+    dq, dk, dub, dv, dla, ds0 = _prefill_bwd_op(q, k, u, v, la, beta, initial_state, dy, ds_T, bool(want_ds0))
+    out = {"dq": dq, "dk": dk, "dv": dv, "dla": dla, ("du" if u is not None else "dbeta"): dub}
+    if want_ds0:
+        out["ds0"] = ds0
+    return out
 
 
 @torch.library.custom_op("archbench_b200::decode_step", mutates_args=("state",))

@@ -78,3 +78,18 @@ def decode_bytes_per_token_head(DK=128, DV=128, in_bytes=2, out_bytes=2):
     """Algorithmic HBM bytes per decode step and head: fp32 state read and written once,
     plus q, k, v, beta, la in and y out."""
     return 2 * 4 * DK * DV + in_bytes * (2 * DK + DV) + out_bytes * DV + 8
+
+
+def backward_flops_per_chunk(C=64, D=128):
+    """Tensor FLOPs the chunked backward executes per (b, h, chunk) with DK = DV = D:
+    2 * (10 C D^2 + 17 C^2 D + 2 C^3) multiply-adds.  C D^2 products: the forward chain's R and state
+    update, the backward chain's dR and two dS terms, and in the local pass R, dR, dY S0, R dS1, dR S0;
+    C^2 D products: the prep pass's K U^T, Q U^T, T Gamma K, T V, the backward chain's A^T dY, and twelve
+    in the local pass; C^3: the two products of dL = -T^T dT T^T."""
+    return 2 * (10 * C * D * D + 17 * C * C * D + 2 * C**3)
+
+
+def backward_bytes_per_token_head(D=128, in_bytes=2, dy_bytes=2):
+    """Algorithmic HBM bytes of the backward per token and head: q, k, v, dy and the gates in; fp32 dq,
+    dk, dv, dla and dbeta out (the chunk workspace traffic is extra)."""
+    return in_bytes * 3 * D + dy_bytes * D + 8 + 4 * 3 * D + 8

@@ -1,6 +1,6 @@
 """Benchmark of the gated-DeltaNet hot path on B200 (one JSON line on rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--skip-extra] [--only decode]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--skip-extra] [--only decode|backward]
     torchrun --nproc-per-node N bench.py --gpus N ...
 
 Headline (``value``): chunkwise prefill of configuration 1 -- B=8, T=4096, H=8, DK=DV=128,
@@ -14,6 +14,8 @@ Extra objects on the same line:
                prefill; state streamed from HBM once per step (per rank: its own batch).
   long_context configuration 3: B=1, T=65536, H=32, heads sharded over the N ranks (strong
                scaling), outputs all-gathered over NCCL into (B, T, H, DV) on every rank.
+  backward     the configuration-1 prefill backward (gdn_prefill_bwd) and forward + backward as
+               one training step of the token mixing.
   e2e          the headline prefill through the public API with host buffers: pinned-host ->
                device copies of q/k/v/beta/la and the device -> host copy of y inside the timed
                region.
@@ -306,6 +308,40 @@ def bench_decode(args, rank, world):
             "gpu_launches": args.steps}
 
 
+def bench_backward(args, rank, world):
+    """Configuration-1 prefill backward (gdn_prefill_bwd: dq, dk, dv, dla, dbeta from dy), and the
+    forward + backward pair as one training step of the token mixing."""
+    from archbench_b200 import ops
+    from archbench_b200.workloads import backward_bytes_per_token_head, backward_flops_per_chunk
+
+    c = CONFIGS["cfg1"]
+    x = make_inputs(c.B, c.T, c.H, c.DK, c.DV, seed=6000 + rank, dtype=c.dtype, device="cuda")
+    g = torch.Generator(device="cuda").manual_seed(6100 + rank)
+    dy = torch.randn(c.B, c.T, c.H, c.DV, generator=g, device="cuda").to(torch.bfloat16)
+
+    def bwd():
+        ops.gdn_prefill_bwd(x["q"], x["k"], x["v"], x["la"], dy, beta=x["beta"])
+
+    def train():
+        ops.gdn_prefill(x["q"], x["k"], x["v"], x["la"], beta=x["beta"])
+        bwd()
+
+    steps = max(1, min(args.steps, 10))
+    t_b = timed(bwd, steps, min(args.warmup, 3), world) / steps
+    t_t = timed(train, steps, min(args.warmup, 3), world) / steps
+    th = c.B * c.T * c.H
+    flops = c.B * c.H * (c.T // 64) * backward_flops_per_chunk(64, c.DK)
+    hbm, tflops, src = peaks()
+    alg = th * backward_bytes_per_token_head(c.DK)
+    return {"value": world * c.B * c.T / t_b, "unit": "tok/s", "ms_per_step": t_b * 1e3, "train_step_ms": t_t * 1e3,
+            "train_step_tok_s": world * c.B * c.T / t_t, "config": "cfg1 B8 T4096 H8 d128, bf16 dy, fp32 gradients",
+            "roofline": {"bound": "tensor", "achieved": flops / t_b / 1e12, "peak": tflops, "unit": "TFLOP/s",
+                         "frac": flops / t_b / 1e12 / tflops, "peak_source": src,
+                         "executed_flops_per_launch": flops, "note": "mma.sync fp16 products; four launches (amax, prep, chains, local)",
+                         "hbm_achieved_gbs": alg / t_b / 1e9, "algorithmic_bytes_per_launch": alg},
+            "gpu_launches": 3 * steps + 4 * steps}
+
+
 def bench_long_context(args, rank, world):
     """cfg3 heads sharded over ranks; NCCL all-gather of y (strong scaling)."""
     from archbench_b200 import ops
@@ -354,10 +390,10 @@ def cpu_baseline(budget_s=12.0):
 
 def run_ours(args):
     rank, world, local = dist_init(args.gpus)
-    if args.only == "decode":  # one leg alone (profiling runs): its own object, not the bench line
-        res = bench_decode(args, rank, world)
+    if args.only:  # one leg alone (profiling runs): its own object, not the bench line
+        res = {"decode": bench_decode, "backward": bench_backward}[args.only](args, rank, world)
         if rank == 0:
-            print(json.dumps({"leg": "decode", **res}), flush=True)
+            print(json.dumps({"leg": args.only, **res}), flush=True)
         finish(world)
         return
     res = bench_prefill(args, rank, world)
@@ -377,7 +413,10 @@ def run_ours(args):
         line["decode"] = bench_decode(args, rank, world)
         torch.cuda.empty_cache()
         line["long_context"] = bench_long_context(args, rank, world)
-        line["gpu_launches"] += line["decode"]["gpu_launches"] + line["long_context"].get("gpu_launches", 0) * 2
+        torch.cuda.empty_cache()
+        line["backward"] = bench_backward(args, rank, world)
+        line["gpu_launches"] += (line["decode"]["gpu_launches"] + line["long_context"].get("gpu_launches", 0) * 2
+                                 + line["backward"]["gpu_launches"] + line["e2e"]["steps"])
     if rank == 0 and world == 1 and not args.skip_cpu:
         line["cpu_baseline"] = cpu_baseline()
     if rank == 0:
@@ -433,7 +472,7 @@ def main():
     ap.add_argument("--prefill-impl", choices=["auto", "chunk", "chunk_cluster", "chunk_single", "recurrent", "segmented"], default="auto")
     ap.add_argument("--skip-extra", action="store_true", help="headline prefill only")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the cpu_baseline leg")
-    ap.add_argument("--only", choices=["decode"], default=None,
+    ap.add_argument("--only", choices=["decode", "backward"], default=None,
                     help="run one extra leg alone and print its object (for profiling)")
     ap.add_argument("--no-graph", dest="graph", action="store_false",
                     help="time plain calls instead of CUDA-graph replays of one call")

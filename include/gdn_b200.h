@@ -227,6 +227,53 @@ typedef struct {
 
 int gdn_layer_epilogue(const gdn_epilogue_args* args, void* stream);
 
+/*
+ * Prefill backward: gradients of gdn_prefill_fwd's outputs (y and, optionally, the final state)
+ * with respect to q, k, u (or beta), v, la and the initial state, for DK = DV = 128.
+ *
+ * Replaces the backward of the custom ops archbench's scan runs under autograd:
+ * archbench::nsgdn_chunk_bwd (archbench/layers/nsgdn.py:369-384, registered as the autograd
+ * formula of nsgdn_chunk_fwd at nsgdn.py:386-397) and archbench::nsgdn_bwd (nsgdn.py:185-216,
+ * the recurrent scan's backward); and, for the `gdn` mixer, fla's chunk_gated_delta_rule
+ * backward.  Inputs are the forward's inputs (the forward saves nothing: every chunk product is
+ * recomputed) plus dy and, when the final state was an output, ds_T.
+ *
+ * Outputs are fp32 and contiguous: dq, dk (and du) (B, T, H, DK); dv (B, T, H, DV); dla and dbeta
+ * (B, T, H); ds0 (B, H, DV, DK) or NULL.  With u == NULL (u = beta k) dk includes the write
+ * vector's path and dbeta is written; with u given, du is written and beta/dbeta are ignored.
+ * Token tensors need 16-byte aligned rows.  The workspace (gdn_prefill_bwd_workspace_bytes,
+ * 256-byte aligned) holds per chunk T, A, W, T V, the fp16 operands of the two state chains, the
+ * state entering the chunk and the state gradient leaving it: about 176 KB per (b, h, 64-token
+ * chunk).  One memset and four launches on `stream`.
+ */
+typedef struct {
+  const void* q;       /* [B][T][H][DK], dtype in_dtype */
+  const void* k;
+  const void* u;       /* write vector or NULL (u = beta k) */
+  const void* v;       /* [B][T][H][DV] */
+  const float* beta;   /* (B, T, H) when u == NULL */
+  const float* la;     /* (B, T, H) */
+  const float* s0;     /* (B, H, DV, DK) initial state or NULL (zero) */
+  const void* dy;      /* [B][T][H][DV] gradient of y, dtype dy_dtype */
+  const float* ds_T;   /* (B, H, DV, DK) gradient of the final state, or NULL (zero) */
+  float* dq;
+  float* dk;
+  float* du;           /* when u is given */
+  float* dv;
+  float* dbeta;        /* when u == NULL */
+  float* dla;
+  float* ds0;          /* or NULL */
+  gdn_strides sq, sk, su, sv, sdy;
+  int64_t B, T, H, DK, DV;
+  int32_t in_dtype;    /* gdn_dtype of q, k, u, v */
+  int32_t dy_dtype;    /* gdn_dtype of dy */
+  void* workspace;
+  uint64_t workspace_bytes;
+} gdn_backward_args;
+
+int gdn_prefill_bwd_workspace_bytes(const gdn_backward_args* args, size_t* bytes);
+int gdn_prefill_bwd(const gdn_backward_args* args, void* stream);
+
 /* Which kernel a prefill with these arguments runs (GDN_IMPL_CHUNK_CLUSTER, _CHUNK_SINGLE,
  * _SEGMENTED or _RECURRENT; GDN_IMPL_CHUNK resolves to one of the two chunk variants), or a
  * negative gdn_status if the arguments are invalid.  Launches nothing. */
