@@ -17,8 +17,9 @@
 //
 // The state and its gradient cross chunks, so the work splits in four launches:
 //   amax_kernel   (one block per chunk): the largest |dY| (and |dS_T|) of every (b, h).
-//   prep_kernel   (one block per chunk, all chunks in parallel): g, T, W, Uw, A into the workspace, and the
-//                 fp16 operands the chains stream (U, d U, Gamma Q, dY times the gradient scale).
+//   prep_kernel   (one block per chunk, all chunks in parallel): g, T, W, Uw, A into the workspace, the
+//                 fp16 operands the chains stream (U, d U) and the backward chain's dS-independent terms
+//                 A^T dY and dY^T Gamma Q (dY times the gradient scale).
 //   chain_kernel  (two blocks per (b, h)): one walks the chunks forwards and records S0 of every chunk,
 //                 the other walks them backwards and records dS1 of every chunk; each warp owns 16
 //                 state rows as mma accumulators (rows of S are independent in both chains).
@@ -55,7 +56,8 @@ struct Params {
   int64_t sq_b, sq_t, sq_h, sk_b, sk_t, sk_h, su_b, su_t, su_h, sv_b, sv_t, sv_h, sd_b, sd_t, sd_h;
   int T, H, NC, BH;
   __half *wT, *wA, *wW, *wUw, *wS, *wdS;  // per chunk: T, A (C x C), W, Uw (C x D), S0, dS1 (D x D)
-  __half *wU, *wDU, *wGQ, *wdY;          // per chunk: U, d U, Gamma Q, scaled dY (C x D)
+  __half *wU, *wDU, *wdY, *wdR0;         // per chunk: U, d U, scaled dY, A^T dY (C x D)
+  __half* wPc;                            // per chunk: dY^T Gamma Q (D x D)
   float* wg;                              // per chunk: g (C)
   unsigned* amax;                         // per (b, h): max |dY| as float bits
   float* scale;                           // per (b, h): power-of-two gradient scale
@@ -86,30 +88,46 @@ __device__ __forceinline__ void ld8(const TI* p, float (&f)[8]) {
   }
 }
 
-// C x 128 token tile (row r = token t0 + r of `base`, rows `st` elements apart) -> fp16 shared tile with
-// LDT halves per row; rows >= nvalid are zero; row r is multiplied by mul * rs[r] (rs may be null).
-template <typename TI>
-__device__ __forceinline__ void tile_from_tokens(__half* dst, const TI* base, int64_t st, int nvalid, const float* rs,
-                                                 float mul) {
-  constexpr int PER = C * 16 / NTHR;  // 8-element segments per thread
-  float f[PER][8];
+// A C x 128 token tile held in registers as loaded (8-element segments, C * 16 / NTH per thread of an
+// NTH-thread block), so that several tiles' loads are in flight together before any is converted.
+template <typename TI, int NTH = NTHR>
+struct RawTile {
+  static constexpr int PER = C * 16 / NTH;
+  uint4 v[PER][sizeof(TI) / 2];
+};
+template <typename TI, int NTH>
+__device__ __forceinline__ void raw_load(RawTile<TI, NTH>& t, const TI* base, int64_t st, int nvalid) {
 #pragma unroll
-  for (int it = 0; it < PER; ++it) {  // every load of the thread in flight before the first use
-    const int i = threadIdx.x + it * NTHR, r = i >> 4, seg = i & 15;
-    if (r < nvalid) {
-      ld8(base + r * st + seg * 8, f[it]);
-    } else {
+  for (int it = 0; it < RawTile<TI, NTH>::PER; ++it) {
+    const int i = threadIdx.x + it * NTH, r = i >> 4, seg = i & 15;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) f[it][j] = 0.f;
-    }
+    for (int w = 0; w < (int)(sizeof(TI) / 2); ++w)
+      t.v[it][w] = r < nvalid ? __ldg(reinterpret_cast<const uint4*>(base + r * st + seg * 8) + w) : make_uint4(0, 0, 0, 0);
   }
+}
+// Raw tile -> fp16 shared tile (LDT pitch), row r times mul * rs[r] (rs may be null).
+template <typename TI, int NTH>
+__device__ __forceinline__ void raw_store(__half* dst, const RawTile<TI, NTH>& t, const float* rs, float mul) {
 #pragma unroll
-  for (int it = 0; it < PER; ++it) {
-    const int i = threadIdx.x + it * NTHR, r = i >> 4, seg = i & 15;
+  for (int it = 0; it < RawTile<TI, NTH>::PER; ++it) {
+    const int i = threadIdx.x + it * NTH, r = i >> 4, seg = i & 15;
+    float f[8];
+    if constexpr (sizeof(TI) == 2) {
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&t.v[it][0]);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 x = __bfloat1622float2(h[q]);
+        f[2 * q] = x.x;
+        f[2 * q + 1] = x.y;
+      }
+    } else {
+      const float* x = reinterpret_cast<const float*>(&t.v[it][0]);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) f[q] = x[q];
+    }
     const float m = rs ? mul * rs[r] : mul;
     *reinterpret_cast<uint4*>(dst + r * LDT + seg * 8) =
-        make_uint4(h2u(m * f[it][0], m * f[it][1]), h2u(m * f[it][2], m * f[it][3]), h2u(m * f[it][4], m * f[it][5]),
-                   h2u(m * f[it][6], m * f[it][7]));
+        make_uint4(h2u(m * f[0], m * f[1]), h2u(m * f[2], m * f[3]), h2u(m * f[4], m * f[5]), h2u(m * f[6], m * f[7]));
   }
 }
 
@@ -122,9 +140,10 @@ template <int N>
 __device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 // Dense fp16 rows x cols (global, row-major) -> shared tile with `ld` halves per row, asynchronously.
+template <int NTH = NTHR>
 __device__ __forceinline__ void tile_async(__half* dst, int ld, const __half* src, int rows, int cols) {
   const int segs = cols >> 3;
-  for (int i = threadIdx.x; i < rows * segs; i += NTHR) {
+  for (int i = threadIdx.x; i < rows * segs; i += NTH) {
     const int r = i / segs, sg = i - r * segs;
     cp16(dst + r * ld + sg * 8, src + (int64_t)r * cols + sg * 8);
   }
@@ -138,31 +157,19 @@ __device__ __forceinline__ void tile_store(__half* dst, const __half* src) {
   }
 }
 
-// Dense fp16 rows x cols (global, row-major) -> shared tile with `ld` halves per row.  neg: flip signs.
-__device__ __forceinline__ void tile_copy(__half* dst, int ld, const __half* src, int rows, int cols, bool neg) {
-  const int segs = cols >> 3;
-  const uint32_t flip = neg ? 0x80008000u : 0u;
-  for (int i = threadIdx.x; i < rows * segs; i += NTHR) {
-    const int r = i / segs, s = i - r * segs;
-    uint4 x = __ldg(reinterpret_cast<const uint4*>(src + (int64_t)r * cols + s * 8));
-    x.x ^= flip; x.y ^= flip; x.z ^= flip; x.w ^= flip;
-    *reinterpret_cast<uint4*>(dst + r * ld + s * 8) = x;
-  }
-}
-
 // acc[MT][NT][4] += opA (16 MT x K) * opB (K x 8 NT), fp16 shared-memory operands, fp32 accumulators.
 //   A_T = false: A(m, k) at a[m * lda + k];  A_T = true: A(m, k) at a[k * lda + m]
 //   B_T = false: B(k, n) at b[n * ldb + k];  B_T = true: B(k, n) at b[k * ldb + n]
 // Accumulator element e of tile (mt, nt): row m0 + 16 mt + lane/4 + 8 (e >> 1), column
 // n0 + 8 nt + 2 (lane % 4) + (e & 1).
-template <int MT, int NT, bool A_T, bool B_T>
+template <int MT, int NT, bool A_T, bool B_T, int K, bool FULL = false>
 __device__ __forceinline__ void mma_acc(float (&acc)[MT][NT][4], const __half* a, int lda, int m0, const __half* b,
-                                        int ldb, int n0, int K, int lane) {
+                                        int ldb, int n0, int lane) {
   static_assert(NT % 2 == 0, "B fragments are loaded for pairs of n tiles");
+  static_assert(K % 32 == 0, "K is a multiple of 32");
   const int j = lane >> 3, r = lane & 7;
   const uint32_t abase = sm(a), bbase = sm(b);
-#pragma unroll 1
-  for (int k0 = 0; k0 < K; k0 += 16) {
+  auto step = [&](int k0) {
     uint32_t af[MT][4];
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt) {
@@ -190,6 +197,14 @@ __device__ __forceinline__ void mma_acc(float (&acc)[MT][NT][4], const __half* a
         ptx::hmma16816(acc[mt][2 * np + 1], af[mt], bf[2], bf[3]);
       }
     }
+  };
+  // Unrolled (fully, or by two): the next step's fragments load while this step's products run.
+  if constexpr (FULL) {
+#pragma unroll
+    for (int k0 = 0; k0 < K; k0 += 16) step(k0);
+  } else {
+#pragma unroll 2
+    for (int k0 = 0; k0 < K; k0 += 16) step(k0);
   }
 }
 
@@ -223,7 +238,8 @@ __device__ __forceinline__ float quad_sum(float x) {
   return x;
 }
 
-// Block-wide reductions (all NTHR threads call; `red` holds 8 floats).
+// Block-wide reductions (all NTH threads call; `red` holds NTH / 32 floats).
+template <int NTH = NTHR>
 __device__ __forceinline__ float block_sum(float x, float* red) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
@@ -232,7 +248,7 @@ __device__ __forceinline__ float block_sum(float x, float* red) {
   __syncthreads();
   float s = 0.f;
 #pragma unroll
-  for (int i = 0; i < NTHR / 32; ++i) s += red[i];
+  for (int i = 0; i < NTH / 32; ++i) s += red[i];
   return s;
 }
 __device__ __forceinline__ float block_max(float x, float* red) {
@@ -371,13 +387,49 @@ __global__ void __launch_bounds__(NTHR) prep_kernel(Params p) {
   }
   __syncthreads();
 
-  const TI* kp = tok<TI>(p.k, p.sk_b, p.sk_t, p.sk_h, b, t0, h);
-  tile_from_tokens(sK, kp, p.sk_t, nvalid, nullptr, 1.f);
-  if (p.u) tile_from_tokens(sU, tok<TI>(p.u, p.su_b, p.su_t, p.su_h, b, t0, h), p.su_t, nvalid, nullptr, 1.f);
-  else tile_from_tokens(sU, kp, p.sk_t, nvalid, sbeta, 1.f);
-  tile_from_tokens(sQ, tok<TI>(p.q, p.sq_b, p.sq_t, p.sq_h, b, t0, h), p.sq_t, nvalid, nullptr, 1.f);
-  tile_from_tokens(sV, tok<TI>(p.v, p.sv_b, p.sv_t, p.sv_h, b, t0, h), p.sv_t, nvalid, nullptr, 1.f);
-  tile_from_tokens(sGK, kp, p.sk_t, nvalid, sgam, 1.f);
+  {
+    // k, q, v and dY loads all in flight at once; k feeds three tiles (K, beta K = U, Gamma K)
+    RawTile<TI> rk, rq, rv;
+    RawTile<TD> rd;
+    raw_load(rk, tok<TI>(p.k, p.sk_b, p.sk_t, p.sk_h, b, t0, h), p.sk_t, nvalid);
+    raw_load(rq, tok<TI>(p.q, p.sq_b, p.sq_t, p.sq_h, b, t0, h), p.sq_t, nvalid);
+    raw_load(rv, tok<TI>(p.v, p.sv_b, p.sv_t, p.sv_h, b, t0, h), p.sv_t, nvalid);
+    raw_load(rd, tok<TD>(p.dy, p.sd_b, p.sd_t, p.sd_h, b, t0, h), p.sd_t, nvalid);
+    raw_store(sK, rk, nullptr, 1.f);
+    raw_store(sGK, rk, sgam, 1.f);
+    if (p.u) {
+      RawTile<TI> ru;
+      raw_load(ru, tok<TI>(p.u, p.su_b, p.su_t, p.su_h, b, t0, h), p.su_t, nvalid);
+      raw_store(sU, ru, nullptr, 1.f);
+    } else {
+      raw_store(sU, rk, sbeta, 1.f);
+    }
+    raw_store(sQ, rq, nullptr, 1.f);
+    raw_store(sV, rv, nullptr, 1.f);
+    // dY times the gradient scale -> the workspace (dense rows), straight from registers
+    __half* wd = p.wdY + (int64_t)task * C * D;
+#pragma unroll
+    for (int it = 0; it < RawTile<TD>::PER; ++it) {
+      const int i = tid + it * NTHR, r = i >> 4, seg = i & 15;
+      float f[8];
+      if constexpr (sizeof(TD) == 2) {
+        const __nv_bfloat162* hh = reinterpret_cast<const __nv_bfloat162*>(&rd.v[it][0]);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 x = __bfloat1622float2(hh[q]);
+          f[2 * q] = x.x;
+          f[2 * q + 1] = x.y;
+        }
+      } else {
+        const float* x = reinterpret_cast<const float*>(&rd.v[it][0]);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) f[q] = x[q];
+      }
+      *reinterpret_cast<uint4*>(wd + r * D + seg * 8) =
+          make_uint4(h2u(scale * f[0], scale * f[1]), h2u(scale * f[2], scale * f[3]), h2u(scale * f[4], scale * f[5]),
+                     h2u(scale * f[6], scale * f[7]));
+    }
+  }
   __syncthreads();
 
   // M = K U^T -> L (fp32, strictly lower); P = Q U^T -> A (fp16, lower incl. diagonal, to the workspace)
@@ -386,8 +438,8 @@ __global__ void __launch_bounds__(NTHR) prep_kernel(Params p) {
     float accM[1][4][4], accP[1][4][4];
     zero(accM);
     zero(accP);
-    mma_acc<1, 4, false, false>(accM, sK, LDT, m0, sU, LDT, n0, D, lane);
-    mma_acc<1, 4, false, false>(accP, sQ, LDT, m0, sU, LDT, n0, D, lane);
+    mma_acc<1, 4, false, false, D>(accM, sK, LDT, m0, sU, LDT, n0, lane);
+    mma_acc<1, 4, false, false, D>(accP, sQ, LDT, m0, sU, LDT, n0, lane);
     __half* Aout = p.wA + (int64_t)task * C * C;
 #pragma unroll
     for (int nt = 0; nt < 4; ++nt)
@@ -464,7 +516,7 @@ __global__ void __launch_bounds__(NTHR) prep_kernel(Params p) {
 #pragma unroll 1
     for (int which = 0; which < 2; ++which) {
       zero(acc);
-      mma_acc<1, 8, false, true>(acc, sT, LDC, m0, which ? sV : sGK, LDT, n0, C, lane);
+      mma_acc<1, 8, false, true, C>(acc, sT, LDC, m0, which ? sV : sGK, LDT, n0, lane);
       __half* out = (which ? p.wUw : p.wW) + (int64_t)task * C * D;
 #pragma unroll
       for (int nt = 0; nt < 8; ++nt) {
@@ -474,8 +526,17 @@ __global__ void __launch_bounds__(NTHR) prep_kernel(Params p) {
       }
     }
   }
+  __syncthreads();  // Gamma K, T's fp32 copy and L are no longer read
 
-  // the chains' streamed operands: U, d U, Gamma Q (from the tiles above) and dY times the gradient scale
+  // The backward chain's dS-independent terms, once per chunk here instead of on the chain:
+  // dR0 = A^T dY (C x DV) and Pc = dY^T Gamma Q (DV x DK).  Gamma Q is built in K's space, dY (scaled, as
+  // written above) and A come back from the workspace into the spaces of Gamma K and L.
+  __half* sGQ = sK;
+  __half* sdY = sGK;
+  __half* sA = reinterpret_cast<__half*>(sL);
+  tile_async(sdY, LDT, p.wdY + (int64_t)task * C * D, C, D);
+  tile_async(sA, LDC, p.wA + (int64_t)task * C * C, C, C);
+  cp_commit();
   {
     const int64_t o = (int64_t)task * C * D;
     for (int i = tid; i < C * 16; i += NTHR) {
@@ -492,36 +553,46 @@ __global__ void __launch_bounds__(NTHR) prep_kernel(Params p) {
       }
       *reinterpret_cast<uint4*>(p.wU + o + r * D + sg8) = u;
       *reinterpret_cast<uint4*>(p.wDU + o + r * D + sg8) = make_uint4(du[0], du[1], du[2], du[3]);
-      *reinterpret_cast<uint4*>(p.wGQ + o + r * D + sg8) = make_uint4(gq[0], gq[1], gq[2], gq[3]);
+      *reinterpret_cast<uint4*>(sGQ + r * LDT + sg8) = make_uint4(gq[0], gq[1], gq[2], gq[3]);
     }
-    const TD* dyp = tok<TD>(p.dy, p.sd_b, p.sd_t, p.sd_h, b, t0, h);
-    constexpr int PER = C * 16 / NTHR;
-    float f[PER][8];
+  }
+  cp_wait<0>();
+  __syncthreads();
+  {
+    const int g = lane >> 2, t4 = lane & 3;
+    float acc[1][8][4];
+    // dR0: warp -> rows 16 (warp & 3).., columns 64 (warp >> 2)..
+    const int m0 = 16 * (warp & 3), n0 = 64 * (warp >> 2);
+    zero(acc);
+    mma_acc<1, 8, true, true, C>(acc, sA, LDC, m0, sdY, LDT, n0, lane);
+    __half* out = p.wdR0 + (int64_t)task * C * D;
 #pragma unroll
-    for (int it = 0; it < PER; ++it) {
-      const int i = tid + it * NTHR, r = i >> 4, seg = i & 15;
-      if (r < nvalid) {
-        ld8(dyp + r * p.sd_t + seg * 8, f[it]);
-      } else {
+    for (int nt = 0; nt < 8; ++nt) {
+      const int col = n0 + 8 * nt + 2 * t4;
+      *reinterpret_cast<uint32_t*>(out + (m0 + g) * D + col) = h2u(acc[0][nt][0], acc[0][nt][1]);
+      *reinterpret_cast<uint32_t*>(out + (m0 + g + 8) * D + col) = h2u(acc[0][nt][2], acc[0][nt][3]);
+    }
+    // Pc: warp -> rows 16 warp.., all 128 columns in two halves
+    __half* pc = p.wPc + (int64_t)task * D * D;
+#pragma unroll 1
+    for (int half = 0; half < 2; ++half) {
+      zero(acc);
+      mma_acc<1, 8, true, true, C>(acc, sdY, LDT, 16 * warp, sGQ, LDT, 64 * half, lane);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) f[it][j] = 0.f;
+      for (int nt = 0; nt < 8; ++nt) {
+        const int col = 64 * half + 8 * nt + 2 * t4;
+        *reinterpret_cast<uint32_t*>(pc + (16 * warp + g) * D + col) = h2u(acc[0][nt][0], acc[0][nt][1]);
+        *reinterpret_cast<uint32_t*>(pc + (16 * warp + g + 8) * D + col) = h2u(acc[0][nt][2], acc[0][nt][3]);
       }
-    }
-#pragma unroll
-    for (int it = 0; it < PER; ++it) {
-      const int i = tid + it * NTHR, r = i >> 4, seg = i & 15;
-      *reinterpret_cast<uint4*>(p.wdY + o + r * D + seg * 8) =
-          make_uint4(h2u(scale * f[it][0], scale * f[it][1]), h2u(scale * f[it][2], scale * f[it][3]),
-                     h2u(scale * f[it][4], scale * f[it][5]), h2u(scale * f[it][6], scale * f[it][7]));
     }
   }
 }
 
 // ---- chains: S0 of every chunk (forwards), dS1 of every chunk (backwards) ----------------------------
 // Per chunk the block streams its operands from the workspace with cp.async into one of two buffers,
-// the next chunk's while it works on this one.  Buffer: forward [W | Uw | U], backward [A | dY | d U |
-// Gamma Q | W], each followed by the chunk's g.
-constexpr int CHAIN_BUF = TILE_CC + 4 * TILE_CD;
+// the next chunk's while it works on this one.  Buffer: forward [W | Uw | U], backward [A^T dY | d U | W |
+// dY^T Gamma Q]; the chunk's g beside each.
+constexpr int CHAIN_BUF = 3 * TILE_CD + TILE_DD;
 constexpr int CHAIN_SMEM = (TILE_DD + TILE_CD + 2 * CHAIN_BUF) * 2 + 2 * C * 4 + 64;
 
 __global__ void __launch_bounds__(NTHR, 1) chain_kernel(Params p) {
@@ -544,11 +615,10 @@ __global__ void __launch_bounds__(NTHR, 1) chain_kernel(Params p) {
       tile_async(bb + TILE_CD, LDT, p.wUw + task * C * D, C, D);
       tile_async(bb + 2 * TILE_CD, LDT, p.wU + task * C * D, C, D);
     } else {
-      tile_async(bb, LDC, p.wA + task * C * C, C, C);
-      tile_async(bb + TILE_CC, LDT, p.wdY + task * C * D, C, D);
-      tile_async(bb + TILE_CC + TILE_CD, LDT, p.wDU + task * C * D, C, D);
-      tile_async(bb + TILE_CC + 2 * TILE_CD, LDT, p.wGQ + task * C * D, C, D);
-      tile_async(bb + TILE_CC + 3 * TILE_CD, LDT, p.wW + task * C * D, C, D);
+      tile_async(bb, LDT, p.wdR0 + task * C * D, C, D);
+      tile_async(bb + TILE_CD, LDT, p.wDU + task * C * D, C, D);
+      tile_async(bb + 2 * TILE_CD, LDT, p.wW + task * C * D, C, D);
+      tile_async(bb + 3 * TILE_CD, LDT, p.wPc + task * D * D, D, D);
     }
     if (tid < C / 4) cp16(sgb + bi * C + 4 * tid, p.wg + task * C + 4 * tid);
     cp_commit();
@@ -595,7 +665,7 @@ __global__ void __launch_bounds__(NTHR, 1) chain_kernel(Params p) {
     if (forward) {
       const __half *W = bb, *Uw = bb + TILE_CD, *U = bb + 2 * TILE_CD;
       // R = Uw - W S^T for this warp's 16 columns (= its state rows); d R -> sP
-      mma_acc<4, 2, false, false>(r, W, LDT, 0, sX, LDT, 16 * w, D, lane);
+      mma_acc<4, 2, false, false, D, true>(r, W, LDT, 0, sX, LDT, 16 * w, lane);
 #pragma unroll
       for (int mt = 0; mt < 4; ++mt)
 #pragma unroll
@@ -616,12 +686,22 @@ __global__ void __launch_bounds__(NTHR, 1) chain_kernel(Params p) {
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc[0][nt][e] *= gC;
       // S = gamma_C S + (d R)^T U
-      mma_acc<1, 16, true, true>(acc, sP, LDT, 16 * w, U, LDT, 0, C, lane);
+      mma_acc<1, 16, true, true, C, true>(acc, sP, LDT, 16 * w, U, LDT, 0, lane);
     } else {
-      const __half *A = bb, *dY = bb + TILE_CC, *DU = dY + TILE_CD, *GQ = DU + TILE_CD, *W = GQ + TILE_CD;
-      // dR = (d U) dS^T + A^T dY for this warp's 16 columns; -dR -> sP
-      mma_acc<4, 2, false, false>(r, DU, LDT, 0, sX, LDT, 16 * w, D, lane);
-      mma_acc<4, 2, true, true>(r, A, LDC, 0, dY, LDT, 16 * w, C, lane);
+      const __half *dR0 = bb, *DU = bb + TILE_CD, *W = DU + TILE_CD, *Pc = W + TILE_CD;
+      // dR = A^T dY + (d U) dS^T for this warp's 16 columns; -dR -> sP
+#pragma unroll
+      for (int mt = 0; mt < 4; ++mt)
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int hf = 0; hf < 2; ++hf) {
+            const int tr = 16 * mt + g + 8 * hf, dc = 16 * w + 8 * nt + 2 * t4;
+            const float2 x = u2f(*reinterpret_cast<const uint32_t*>(dR0 + tr * LDT + dc));
+            r[mt][nt][2 * hf] = x.x;
+            r[mt][nt][2 * hf + 1] = x.y;
+          }
+      mma_acc<4, 2, false, false, D, true>(r, DU, LDT, 0, sX, LDT, 16 * w, lane);
 #pragma unroll
       for (int mt = 0; mt < 4; ++mt)
 #pragma unroll
@@ -632,13 +712,18 @@ __global__ void __launch_bounds__(NTHR, 1) chain_kernel(Params p) {
             *reinterpret_cast<uint32_t*>(sP + tr * LDT + dc) = h2u(-r[mt][nt][2 * hf], -r[mt][nt][2 * hf + 1]);
           }
       __syncwarp();
-#pragma unroll
-      for (int nt = 0; nt < 16; ++nt)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[0][nt][e] *= gC;
       // dS = gamma_C dS + dY^T (Gamma Q) - dR^T W
-      mma_acc<1, 16, true, true>(acc, dY, LDT, 16 * w, GQ, LDT, 0, C, lane);
-      mma_acc<1, 16, true, true>(acc, sP, LDT, 16 * w, W, LDT, 0, C, lane);
+#pragma unroll
+      for (int nt = 0; nt < 16; ++nt) {
+        const int col = 8 * nt + 2 * t4;
+        const float2 x0 = u2f(*reinterpret_cast<const uint32_t*>(Pc + row0 * LDT + col));
+        const float2 x1 = u2f(*reinterpret_cast<const uint32_t*>(Pc + row1 * LDT + col));
+        acc[0][nt][0] = gC * acc[0][nt][0] + x0.x;
+        acc[0][nt][1] = gC * acc[0][nt][1] + x0.y;
+        acc[0][nt][2] = gC * acc[0][nt][2] + x1.x;
+        acc[0][nt][3] = gC * acc[0][nt][3] + x1.y;
+      }
+      mma_acc<1, 16, true, true, C, true>(acc, sP, LDT, 16 * w, W, LDT, 0, lane);
     }
     __syncthreads();  // every warp is done with buffer bi before the next iteration refills it
   }
@@ -718,9 +803,15 @@ __global__ void __launch_bounds__(NTHR, 1) local_kernel(Params p) {
     tile_async(sB1, LDT, p.wdS + (int64_t)task * D * D, D, D);
     cp_commit();
   }
-  tile_from_tokens(sQ, tok<TI>(p.q, p.sq_b, p.sq_t, p.sq_h, b, t0, h), p.sq_t, nvalid, nullptr, 1.f);
-  tile_from_tokens(sK, tok<TI>(p.k, p.sk_b, p.sk_t, p.sk_h, b, t0, h), p.sk_t, nvalid, nullptr, 1.f);
-  tile_from_tokens(sV, tok<TI>(p.v, p.sv_b, p.sv_t, p.sv_h, b, t0, h), p.sv_t, nvalid, nullptr, 1.f);
+  {
+    RawTile<TI> rq, rk, rv;
+    raw_load(rq, tok<TI>(p.q, p.sq_b, p.sq_t, p.sq_h, b, t0, h), p.sq_t, nvalid);
+    raw_load(rk, tok<TI>(p.k, p.sk_b, p.sk_t, p.sk_h, b, t0, h), p.sk_t, nvalid);
+    raw_load(rv, tok<TI>(p.v, p.sv_b, p.sv_t, p.sv_h, b, t0, h), p.sv_t, nvalid);
+    raw_store(sQ, rq, nullptr, 1.f);
+    raw_store(sK, rk, nullptr, 1.f);
+    raw_store(sV, rv, nullptr, 1.f);
+  }
   cp_wait<0>();
   __syncthreads();
 
@@ -731,29 +822,29 @@ __global__ void __launch_bounds__(NTHR, 1) local_kernel(Params p) {
 
   // R = T V - W S0^T
   zero(acc);
-  mma_acc<1, 8, false, false>(acc, sNW, LDT, m0, sB0, LDT, n0, D, lane);
+  mma_acc<1, 8, false, false, D>(acc, sNW, LDT, m0, sB0, LDT, n0, lane);
 #pragma unroll
   for (int nt = 0; nt < 8; ++nt)
 #pragma unroll
     for (int e = 0; e < 4; ++e) acc[0][nt][e] = -acc[0][nt][e];
-  mma_acc<1, 8, false, true>(acc, sT, LDC, m0, sV, LDT, n0, C, lane);
+  mma_acc<1, 8, false, true, C>(acc, sT, LDC, m0, sV, LDT, n0, lane);
   strip_to_smem(sR, LDT, m0, n0, acc, lane, 1.f);
   // dR = d (U dS1^T) + A^T dY
   zero(acc);
-  mma_acc<1, 8, false, false>(acc, sU, LDT, m0, sB1, LDT, n0, D, lane);
+  mma_acc<1, 8, false, false, D>(acc, sU, LDT, m0, sB1, LDT, n0, lane);
 #pragma unroll
   for (int nt = 0; nt < 8; ++nt) {
     acc[0][nt][0] *= sd[ra]; acc[0][nt][1] *= sd[ra];
     acc[0][nt][2] *= sd[rb]; acc[0][nt][3] *= sd[rb];
   }
-  mma_acc<1, 8, true, true>(acc, sA, LDC, m0, sdY, LDT, n0, C, lane);
+  mma_acc<1, 8, true, true, C>(acc, sA, LDC, m0, sdY, LDT, n0, lane);
   strip_to_smem(sdR, LDT, m0, n0, acc, lane, 1.f);
   __syncthreads();
 
   // X = dY S0: dg_t += gamma_t q_t . X_t;  dQ = Gamma X (+ dP U below)
   float aQ[1][8][4];
   zero(aQ);
-  mma_acc<1, 8, false, true>(aQ, sdY, LDT, m0, sB0, LDT, n0, D, lane);
+  mma_acc<1, 8, false, true, D>(aQ, sdY, LDT, m0, sB0, LDT, n0, lane);
   {
     float pa = 0.f, pb = 0.f;
 #pragma unroll
@@ -779,7 +870,7 @@ __global__ void __launch_bounds__(NTHR, 1) local_kernel(Params p) {
   // Z = R dS1: dd_t = Z_t . u_t;  dU = d Z (+ dP^T Q + dM^T K below)
   float aU[1][8][4];
   zero(aU);
-  mma_acc<1, 8, false, true>(aU, sR, LDT, m0, sB1, LDT, n0, D, lane);
+  mma_acc<1, 8, false, true, D>(aU, sR, LDT, m0, sB1, LDT, n0, lane);
   {
     float pa = 0.f, pb = 0.f;
 #pragma unroll
@@ -804,7 +895,7 @@ __global__ void __launch_bounds__(NTHR, 1) local_kernel(Params p) {
   }
   // dW = -dR S0 -> sNW (every warp has finished reading W)
   zero(acc);
-  mma_acc<1, 8, false, true>(acc, sdR, LDT, m0, sB0, LDT, n0, D, lane);
+  mma_acc<1, 8, false, true, D>(acc, sdR, LDT, m0, sB0, LDT, n0, lane);
   strip_to_smem(sNW, LDT, m0, n0, acc, lane, -1.f);
   // <dS1, S0>
   float dot = 0.f;
@@ -821,7 +912,7 @@ __global__ void __launch_bounds__(NTHR, 1) local_kernel(Params p) {
   float sq[1][4][4];
   // dA = tril(dY R^T): dg += rowsum(dA o A) - colsum(dA o A);  dP = dA o E
   zero(sq);
-  mma_acc<1, 4, false, false>(sq, sdY, LDT, m0, sR, LDT, c0, D, lane);
+  mma_acc<1, 4, false, false, D>(sq, sdY, LDT, m0, sR, LDT, c0, lane);
   {
     float rs[2] = {0.f, 0.f}, cs[4][2];
 #pragma unroll
@@ -847,19 +938,19 @@ __global__ void __launch_bounds__(NTHR, 1) local_kernel(Params p) {
   }
   // dT = (dW K^T) diag(gamma) + dR V^T
   zero(sq);
-  mma_acc<1, 4, false, false>(sq, sNW, LDT, m0, sK, LDT, c0, D, lane);
+  mma_acc<1, 4, false, false, D>(sq, sNW, LDT, m0, sK, LDT, c0, lane);
 #pragma unroll
   for (int nt = 0; nt < 4; ++nt) {
     const int col = c0 + 8 * nt + 2 * t4;
     sq[0][nt][0] *= sgam[col]; sq[0][nt][1] *= sgam[col + 1];
     sq[0][nt][2] *= sgam[col]; sq[0][nt][3] *= sgam[col + 1];
   }
-  mma_acc<1, 4, false, false>(sq, sdR, LDT, m0, sV, LDT, c0, D, lane);
+  mma_acc<1, 4, false, false, D>(sq, sdR, LDT, m0, sV, LDT, c0, lane);
   strip_to_smem(sdT, LDC, m0, c0, sq, lane, 1.f);
   __syncthreads();
   // Y1 = dT T^T
   zero(sq);
-  mma_acc<1, 4, false, false>(sq, sdT, LDC, m0, sT, LDC, c0, C, lane);
+  mma_acc<1, 4, false, false, C>(sq, sdT, LDC, m0, sT, LDC, c0, lane);
   strip_to_smem(sY1, LDC, m0, c0, sq, lane, 1.f);
   __syncthreads();
   // dL = strict_tril(-T^T Y1);  M = K U^T, L = M o E;  dg += rowsum(dL o L) - colsum(dL o L);  dM = dL o E
@@ -867,8 +958,8 @@ __global__ void __launch_bounds__(NTHR, 1) local_kernel(Params p) {
     float mm[1][4][4];
     zero(sq);
     zero(mm);
-    mma_acc<1, 4, true, true>(sq, sT, LDC, m0, sY1, LDC, c0, C, lane);
-    mma_acc<1, 4, false, false>(mm, sK, LDT, m0, sU, LDT, c0, D, lane);
+    mma_acc<1, 4, true, true, C>(sq, sT, LDC, m0, sY1, LDC, c0, lane);
+    mma_acc<1, 4, false, false, D>(mm, sK, LDT, m0, sU, LDT, c0, lane);
     float rs[2] = {0.f, 0.f}, cs[4][2];
 #pragma unroll
     for (int nt = 0; nt < 4; ++nt) {
@@ -897,7 +988,7 @@ __global__ void __launch_bounds__(NTHR, 1) local_kernel(Params p) {
   // dK = Gamma T^T dW + dM U;  dg_t += gamma_t (T^T dW)_t . k_t
   float aK[1][8][4];
   zero(aK);
-  mma_acc<1, 8, true, true>(aK, sT, LDC, m0, sNW, LDT, n0, C, lane);
+  mma_acc<1, 8, true, true, C>(aK, sT, LDC, m0, sNW, LDT, n0, lane);
   {
     float pa = 0.f, pb = 0.f;
 #pragma unroll
@@ -920,14 +1011,14 @@ __global__ void __launch_bounds__(NTHR, 1) local_kernel(Params p) {
       aK[0][nt][2] *= sgam[rb]; aK[0][nt][3] *= sgam[rb];
     }
   }
-  mma_acc<1, 8, false, true>(aK, sdM, LDC, m0, sU, LDT, n0, C, lane);
+  mma_acc<1, 8, false, true, C>(aK, sdM, LDC, m0, sU, LDT, n0, lane);
   // dQ += dP U;  dU += dP^T Q + dM^T K
-  mma_acc<1, 8, false, true>(aQ, sdP, LDC, m0, sU, LDT, n0, C, lane);
-  mma_acc<1, 8, true, true>(aU, sdP, LDC, m0, sQ, LDT, n0, C, lane);
-  mma_acc<1, 8, true, true>(aU, sdM, LDC, m0, sK, LDT, n0, C, lane);
+  mma_acc<1, 8, false, true, C>(aQ, sdP, LDC, m0, sU, LDT, n0, lane);
+  mma_acc<1, 8, true, true, C>(aU, sdP, LDC, m0, sQ, LDT, n0, lane);
+  mma_acc<1, 8, true, true, C>(aU, sdM, LDC, m0, sK, LDT, n0, lane);
   // dV = T^T dR
   zero(acc);
-  mma_acc<1, 8, true, true>(acc, sT, LDC, m0, sdR, LDT, n0, C, lane);
+  mma_acc<1, 8, true, true, C>(acc, sT, LDC, m0, sdR, LDT, n0, lane);
 
   // outputs (fp32, contiguous (B, T, H, 128)), divided by the gradient scale
   const bool has_u = p.u != nullptr;
@@ -1000,7 +1091,7 @@ __global__ void __launch_bounds__(NTHR, 1) local_kernel(Params p) {
 size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 struct Layout {
-  size_t T, A, W, Uw, U, DU, GQ, dY, S, dS, g, amax, scale, total;
+  size_t T, A, W, Uw, U, DU, dY, dR0, Pc, S, dS, g, amax, scale, total;
 };
 
 Layout layout(int64_t nch, int64_t bh) {
@@ -1013,8 +1104,9 @@ Layout layout(int64_t nch, int64_t bh) {
   l.Uw = take((size_t)nch * C * D * 2);
   l.U = take((size_t)nch * C * D * 2);
   l.DU = take((size_t)nch * C * D * 2);
-  l.GQ = take((size_t)nch * C * D * 2);
   l.dY = take((size_t)nch * C * D * 2);
+  l.dR0 = take((size_t)nch * C * D * 2);
+  l.Pc = take((size_t)nch * D * D * 2);
   l.S = take((size_t)nch * D * D * 2);
   l.dS = take((size_t)nch * D * D * 2);
   l.g = take((size_t)nch * C * 4);
@@ -1124,8 +1216,9 @@ int gdn_prefill_bwd(const gdn_backward_args* a, void* stream) {
   p.wdS = reinterpret_cast<__half*>(ws + l.dS);
   p.wU = reinterpret_cast<__half*>(ws + l.U);
   p.wDU = reinterpret_cast<__half*>(ws + l.DU);
-  p.wGQ = reinterpret_cast<__half*>(ws + l.GQ);
   p.wdY = reinterpret_cast<__half*>(ws + l.dY);
+  p.wdR0 = reinterpret_cast<__half*>(ws + l.dR0);
+  p.wPc = reinterpret_cast<__half*>(ws + l.Pc);
   p.wg = reinterpret_cast<float*>(ws + l.g);
   p.amax = reinterpret_cast<unsigned*>(ws + l.amax);
   p.scale = reinterpret_cast<float*>(ws + l.scale);

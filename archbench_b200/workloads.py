@@ -82,10 +82,10 @@ def decode_bytes_per_token_head(DK=128, DV=128, in_bytes=2, out_bytes=2):
 
 def backward_flops_per_chunk(C=64, D=128):
     """Tensor FLOPs the chunked backward executes per (b, h, chunk) with DK = DV = D:
-    2 * (10 C D^2 + 17 C^2 D + 2 C^3) multiply-adds.  C D^2 products: the forward chain's R and state
-    update, the backward chain's dR and two dS terms, and in the local pass R, dR, dY S0, R dS1, dR S0;
-    C^2 D products: the prep pass's K U^T, Q U^T, T Gamma K, T V, the backward chain's A^T dY, and twelve
-    in the local pass; C^3: the two products of dL = -T^T dT T^T."""
+    2 * (10 C D^2 + 17 C^2 D + 2 C^3) multiply-adds.  C D^2 products: the prep pass's dY^T Gamma Q, the
+    forward chain's R and state update, the backward chain's d U dS^T and dR^T W, and in the local pass
+    R, dR, dY S0, R dS1, dR S0; C^2 D products: the prep pass's K U^T, Q U^T, T Gamma K, T V, A^T dY and
+    twelve in the local pass; C^3: the two products of dL = -T^T dT T^T."""
     return 2 * (10 * C * D * D + 17 * C * C * D + 2 * C**3)
 
 

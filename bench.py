@@ -1,6 +1,6 @@
 """Benchmark of the gated-DeltaNet hot path on B200 (one JSON line on rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--skip-extra] [--only decode|backward]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--skip-extra] [--only decode|backward|layer]
     torchrun --nproc-per-node N bench.py --gpus N ...
 
 Headline (``value``): chunkwise prefill of configuration 1 -- B=8, T=4096, H=8, DK=DV=128,
@@ -16,6 +16,8 @@ Extra objects on the same line:
                scaling), outputs all-gathered over NCCL into (B, T, H, DV) on every rank.
   backward     the configuration-1 prefill backward (gdn_prefill_bwd) and forward + backward as
                one training step of the token mixing.
+  layer        the drop-in nsgdn mixer on configuration-1 tokens (d_model 1024): inference forward
+               with the fused prologue/epilogue kernels, and a training step through autograd.
   e2e          the headline prefill through the public API with host buffers: pinned-host ->
                device copies of q/k/v/beta/la and the device -> host copy of y inside the timed
                region.
@@ -342,6 +344,35 @@ def bench_backward(args, rank, world):
             "gpu_launches": 3 * steps + 4 * steps}
 
 
+def bench_layer(args, rank, world):
+    """The nsgdn mixer as a whole (projections, short conv, norms and gates, scan, output norm and gate,
+    output projection) on configuration-1 tokens: B=8, T=4096, d_model=1024, H=8, head_dim=128,
+    expand_v=1, n_steps=1, bf16 weights (random init).  Inference forward (fused prologue/epilogue
+    kernels) and one training step (forward + backward through autograd)."""
+    from archbench_b200.layers import NStepGDN
+
+    c = CONFIGS["cfg1"]
+    torch.manual_seed(7000 + rank)
+    m = NStepGDN(1024, num_heads=c.H, head_dim=c.DK, expand_v=1.0, n_steps=1).cuda().to(torch.bfloat16)
+    x = torch.randn(c.B, c.T, 1024, device="cuda", dtype=torch.bfloat16)
+
+    def infer():
+        with torch.no_grad():
+            m(x)
+
+    def train():
+        m.zero_grad(set_to_none=True)
+        m(x).float().square().mean().backward()
+
+    steps = max(1, min(args.steps, 10))
+    t_i = timed(infer, steps, min(args.warmup, 3), world) / steps
+    t_t = timed(train, steps, min(args.warmup, 3), world) / steps
+    tok = c.B * c.T
+    return {"config": "nsgdn layer, B8 T4096 d_model 1024 H8 head_dim 128, bf16", "infer_ms": t_i * 1e3,
+            "infer_tok_s": world * tok / t_i, "train_step_ms": t_t * 1e3, "train_tok_s": world * tok / t_t,
+            "gpu_launches": 8 * steps}
+
+
 def bench_long_context(args, rank, world):
     """cfg3 heads sharded over ranks; NCCL all-gather of y (strong scaling)."""
     from archbench_b200 import ops
@@ -391,7 +422,7 @@ def cpu_baseline(budget_s=12.0):
 def run_ours(args):
     rank, world, local = dist_init(args.gpus)
     if args.only:  # one leg alone (profiling runs): its own object, not the bench line
-        res = {"decode": bench_decode, "backward": bench_backward}[args.only](args, rank, world)
+        res = {"decode": bench_decode, "backward": bench_backward, "layer": bench_layer}[args.only](args, rank, world)
         if rank == 0:
             print(json.dumps({"leg": args.only, **res}), flush=True)
         finish(world)
@@ -415,8 +446,10 @@ def run_ours(args):
         line["long_context"] = bench_long_context(args, rank, world)
         torch.cuda.empty_cache()
         line["backward"] = bench_backward(args, rank, world)
+        torch.cuda.empty_cache()
+        line["layer"] = bench_layer(args, rank, world)
         line["gpu_launches"] += (line["decode"]["gpu_launches"] + line["long_context"].get("gpu_launches", 0) * 2
-                                 + line["backward"]["gpu_launches"] + line["e2e"]["steps"])
+                                 + line["backward"]["gpu_launches"] + line["e2e"]["steps"] + line["layer"]["gpu_launches"])
     if rank == 0 and world == 1 and not args.skip_cpu:
         line["cpu_baseline"] = cpu_baseline()
     if rank == 0:
@@ -472,7 +505,7 @@ def main():
     ap.add_argument("--prefill-impl", choices=["auto", "chunk", "chunk_cluster", "chunk_single", "recurrent", "segmented"], default="auto")
     ap.add_argument("--skip-extra", action="store_true", help="headline prefill only")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the cpu_baseline leg")
-    ap.add_argument("--only", choices=["decode", "backward"], default=None,
+    ap.add_argument("--only", choices=["decode", "backward", "layer"], default=None,
                     help="run one extra leg alone and print its object (for profiling)")
     ap.add_argument("--no-graph", dest="graph", action="store_false",
                     help="time plain calls instead of CUDA-graph replays of one call")

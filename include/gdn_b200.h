@@ -243,7 +243,7 @@ int gdn_layer_epilogue(const gdn_epilogue_args* args, void* stream);
  * vector's path and dbeta is written; with u given, du is written and beta/dbeta are ignored.
  * Token tensors need 16-byte aligned rows.  The workspace (gdn_prefill_bwd_workspace_bytes,
  * 256-byte aligned) holds per chunk T, A, W, T V, the fp16 operands of the two state chains, the
- * state entering the chunk and the state gradient leaving it: about 176 KB per (b, h, 64-token
+ * state entering the chunk and the state gradient leaving it: about 208 KB per (b, h, 64-token
  * chunk).  One memset and four launches on `stream`.
  */
 typedef struct {
