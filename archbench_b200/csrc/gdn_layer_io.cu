@@ -13,9 +13,10 @@
 // Epilogue: o = y / sqrt(mean(y^2) + eps) * weight * SiLU(g) over each head's DV values
 // (nsgdn.py:539-541; fla's FusedRMSNormGated), in fp32, rounded once to the output dtype.
 //
-// One warp per (b, t, h) in both kernels: a lane owns DK/32 channels of q and k and DV/32 of v.
-// The prologue reads the conv_size rows a token needs directly (the neighbouring tokens' warps
-// of the block find them in L1), so no warp waits on a chain of loads.
+// Prologue: one warp per (b, h) and run of up to 16 consecutive tokens, a lane owning DK/32 channels
+// of q and k and DV/32 of v; the run's projection rows are staged in shared memory with asynchronous
+// copies, so each projection row is read once and a warp's loads are all in flight together.
+// Epilogue: one warp per (b, t, h).
 #include <math.h>
 #include <string.h>
 
@@ -25,7 +26,7 @@ namespace gdn {
 namespace layer_io {
 
 constexpr int MAX_TAPS = 4;   // largest conv_size served (the reference uses 4)
-constexpr int TOKS = 4;       // tokens per prologue block (one warp each; neighbours share rows in L1)
+constexpr int TOKS = 4;       // warps per prologue block
 
 template <typename T>
 __device__ __forceinline__ float round_to(float x) {
@@ -102,6 +103,7 @@ struct PrologueParams {
   float* la;
   float* beta;
   int B, T, H, DK, DV, taps, clamp;
+  int run;  // tokens per warp (set at launch)
   float q_scale, eps, la_min, beta_scale;
 };
 
@@ -121,100 +123,139 @@ __device__ __forceinline__ void load_row(const Comp& cp, int b, int t, int taps,
   }
 }
 
-// SiLU(conv) of one component at token t for this lane's channels, in the projection dtype (the
-// weights rounded to it, as F.conv1d(x, weight.to(x.dtype)) uses them), accumulated tap by tap.
-template <typename TX, int NPL>
-__device__ __forceinline__ void conv_silu(const Comp& cp, int b, int t, int taps, int c0, float (&out)[NPL]) {
-  float acc[NPL];
+// One block per (b, h) and TOKS runs of p.run consecutive tokens, one run per warp.  The block stages the
+// head's conv weights (rounded to the projection dtype) in shared memory; each warp copies the projection
+// rows of its run (and the TAPS - 1 rows before it) into shared memory with asynchronous copies, all in
+// flight at once, then computes its tokens from there: every projection row is read from HBM once.
+__device__ __forceinline__ void cp16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+               : "memory");
+}
+
+// SiLU(conv) of one component at one token from staged rows (row j of the window at rows + j * ld),
+// taps accumulated in order 0 .. TAPS - 1, in the projection dtype as F.conv1d(x, weight.to(x.dtype)).
+template <typename TX, int TAPS, int NPL>
+__device__ __forceinline__ void conv_tok(const TX* rows, int ld, const float* w, int wld, bool has_w, float (&out)[NPL]) {
+  if (has_w) {
+    float acc[NPL];
 #pragma unroll
-  for (int n = 0; n < NPL; ++n) acc[n] = 0.f;
+    for (int n = 0; n < NPL; ++n) acc[n] = 0.f;
 #pragma unroll
-  for (int j = 0; j < MAX_TAPS; ++j) {
-    if (j >= taps) continue;
-    float row[NPL];
-    load_row<TX, NPL>(cp, b, t - (taps - 1) + j, taps, c0, row);
-    if (cp.w) {
-      float wt[NPL];
-      load_f32<NPL>(cp.w + (int64_t)j * cp.wch + c0, wt);  // coalesced: lanes own consecutive channels
+    for (int j = 0; j < TAPS; ++j) {
+      float wj[NPL], xj[NPL];
+      load_vec<NPL>(w + j * wld, wj);
+      load_vec<NPL>(rows + j * ld, xj);
 #pragma unroll
-      for (int n = 0; n < NPL; ++n) acc[n] = fmaf(round_to<TX>(wt[n]), row[n], acc[n]);
-    } else {
+      for (int n = 0; n < NPL; ++n) acc[n] = fmaf(wj[n], xj[n], acc[n]);
+    }
 #pragma unroll
-      for (int n = 0; n < NPL; ++n) acc[n] = row[n];
+    for (int n = 0; n < NPL; ++n) out[n] = round_to<TX>(silu(round_to<TX>(acc[n])));
+  } else {
+    float x[NPL];
+    load_vec<NPL>(rows + (TAPS - 1) * ld, x);
+#pragma unroll
+    for (int n = 0; n < NPL; ++n) out[n] = round_to<TX>(silu(x[n]));
+  }
+}
+
+template <typename TX, typename TO, int NK, int NV, int TAPS>
+__global__ void __launch_bounds__(32 * TOKS) prologue_kernel(const PrologueParams p) {
+  extern __shared__ __align__(16) float sw[];  // weights [q | k | v] x TAPS x (DK or DV), then the warps' rows
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int RUN = p.run, W = 2 * p.DK + p.DV;  // tokens per warp; elements per staged row
+  const int runs = (p.T + RUN - 1) / RUN, rgroups = (runs + TOKS - 1) / TOKS;
+  const int bh = blockIdx.x / rgroups, rg = blockIdx.x - bh * rgroups;
+  const int b = bh / p.H, h = bh - b * p.H;
+  const Comp* cs[3] = {&p.q, &p.k, &p.v};
+  const int off[3] = {0, p.DK, 2 * p.DK}, len[3] = {p.DK, p.DK, p.DV};
+  float* swc[3] = {sw, sw + TAPS * p.DK, sw + 2 * TAPS * p.DK};
+#pragma unroll
+  for (int c = 0; c < 3; ++c) {
+    if (!cs[c]->w) continue;
+    for (int i = threadIdx.x; i < TAPS * len[c]; i += blockDim.x) {
+      const int j = i / len[c], ch = i - j * len[c];
+      swc[c][i] = round_to<TX>(cs[c]->w[(int64_t)j * cs[c]->wch + (int64_t)h * len[c] + ch]);
     }
   }
+  TX* stage = reinterpret_cast<TX*>(sw + TAPS * W) + (size_t)wid * (RUN + TAPS - 1) * W;
+  __syncthreads();
+  const int run = rg * TOKS + wid;
+  if (run >= runs) return;
+  const int t0 = run * RUN, t1 = min(p.T, t0 + RUN), nrows = t1 - t0 + TAPS - 1;
+  // staged row r holds token t0 - (TAPS - 1) + r; tokens before 0 come from the incoming conv state
+  constexpr int EPC = 16 / sizeof(TX);
 #pragma unroll
-  for (int n = 0; n < NPL; ++n) out[n] = round_to<TX>(silu(cp.w ? round_to<TX>(acc[n]) : acc[n]));
-}
-
-// The next call's conv state of one component: rows T - (taps - 1) .. T - 1 of this lane's
-// channels (earlier rows from the incoming state when T is short).
-template <typename TX, int NPL>
-__device__ __forceinline__ void save_state(const Comp& cp, int b, int T, int taps, int c0) {
-  if (!cp.cout) return;
-  TX* pc = reinterpret_cast<TX*>(cp.cout) + (int64_t)b * cp.csb;
+  for (int c = 0; c < 3; ++c) {
+    const Comp& cp = *cs[c];
+    const int chunks = len[c] / EPC, hc = h * len[c];
+    for (int i = lane; i < nrows * chunks; i += 32) {
+      const int r = i / chunks, q = i - r * chunks, t = t0 - (TAPS - 1) + r;
+      TX* dst = stage + (size_t)r * W + off[c] + q * EPC;
+      if (t >= 0) {
+        cp16(dst, reinterpret_cast<const TX*>(cp.x) + (int64_t)b * cp.sb + (int64_t)t * cp.st + hc + q * EPC);
+      } else {
+        const TX* pc = cp.cin ? reinterpret_cast<const TX*>(cp.cin) + (int64_t)b * cp.csb : nullptr;
+#pragma unroll
+        for (int e = 0; e < EPC; ++e) {
+          const int ch = hc + q * EPC + e;
+          store_as(dst + e, pc ? to_f32(pc[(int64_t)ch * (TAPS - 1) + (TAPS - 1) + t]) : 0.f);
+        }
+      }
+    }
+  }
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+  __syncwarp();
+  const bool wq = p.q.w != nullptr, wk = p.k.w != nullptr, wv = p.v.w != nullptr;
+  const float dtb = p.dt_bias[h], Ae = expf(p.A_log[h]), bb_h = p.b_bias ? p.b_bias[h] : 0.f;
 #pragma unroll 1
-  for (int j = 1; j < taps; ++j) {
-    float row[NPL];
-    load_row<TX, NPL>(cp, b, T - taps + j, taps, c0, row);
+  for (int t = t0; t < t1; ++t) {
+    const TX* rows = stage + (size_t)(t - t0) * W;
+    float q[NK], k[NK], v[NV];
+    conv_tok<TX, TAPS, NK>(rows + lane * NK, W, swc[0] + lane * NK, p.DK, wq, q);
+    conv_tok<TX, TAPS, NK>(rows + p.DK + lane * NK, W, swc[1] + lane * NK, p.DK, wk, k);
+    conv_tok<TX, TAPS, NV>(rows + 2 * p.DK + lane * NV, W, swc[2] + lane * NV, p.DV, wv, v);
+    float sq = 0.f, sk = 0.f;
 #pragma unroll
-    for (int n = 0; n < NPL; ++n) store_as(pc + (int64_t)(c0 + n) * (taps - 1) + (j - 1), row[n]);
-  }
-}
-
-// One warp per (b, t, h): every load of the token is independent (conv rows re-read from L1 by
-// the neighbouring tokens' warps), so a launch keeps many loads in flight.
-template <typename TX, typename TO, int NK, int NV>
-__global__ void __launch_bounds__(32 * TOKS, NV >= 16 ? 4 : (NV >= 8 ? 6 : 8)) prologue_kernel(const PrologueParams p) {
-  const int lane = threadIdx.x & 31;
-  const int groups = (p.T + TOKS - 1) / TOKS;
-  const int blk = blockIdx.x;
-  const int tg = blk % groups, bh = blk / groups, h = bh % p.H, b = bh / p.H;
-  const int t = tg * TOKS + (threadIdx.x >> 5);
-  if (t >= p.T) return;
-  const int ck = h * p.DK + lane * NK, cv = h * p.DV + lane * NV;  // first channel of this lane
-  float q[NK], k[NK], v[NV];
-  conv_silu<TX, NK>(p.q, b, t, p.taps, ck, q);
-  conv_silu<TX, NK>(p.k, b, t, p.taps, ck, k);
-  conv_silu<TX, NV>(p.v, b, t, p.taps, cv, v);
-  float sq = 0.f, sk = 0.f;
+    for (int n = 0; n < NK; ++n) {
+      sq = fmaf(q[n], q[n], sq);
+      sk = fmaf(k[n], k[n], sk);
+    }
 #pragma unroll
-  for (int n = 0; n < NK; ++n) {
-    sq = fmaf(q[n], q[n], sq);
-    sk = fmaf(k[n], k[n], sk);
-  }
+    for (int o = 16; o > 0; o >>= 1) {
+      sq += __shfl_xor_sync(0xffffffffu, sq, o);
+      sk += __shfl_xor_sync(0xffffffffu, sk, o);
+    }
+    const float iq = p.q_scale / fmaxf(sqrtf(sq), p.eps), ik = 1.f / fmaxf(sqrtf(sk), p.eps);
+    const int64_t tok = ((int64_t)b * p.T + t) * p.H + h;
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    sq += __shfl_xor_sync(0xffffffffu, sq, o);
-    sk += __shfl_xor_sync(0xffffffffu, sk, o);
+    for (int n = 0; n < NK; ++n) {
+      q[n] *= iq;
+      k[n] *= ik;
+    }
+    store_vec<TO, NK>(reinterpret_cast<TO*>(p.q.out) + tok * p.DK + lane * NK, q);
+    store_vec<TO, NK>(reinterpret_cast<TO*>(p.k.out) + tok * p.DK + lane * NK, k);
+    store_vec<TO, NV>(reinterpret_cast<TO*>(p.v.out) + tok * p.DV + lane * NV, v);
+    if (lane == 0) {
+      const float a = to_f32(reinterpret_cast<const TX*>(p.xa)[(int64_t)b * p.sa_b + (int64_t)t * p.sa_t + h]);
+      const float bb = to_f32(reinterpret_cast<const TX*>(p.xb)[(int64_t)b * p.sb_b + (int64_t)t * p.sb_t + h]);
+      float la = -softplus(a + dtb) * Ae;
+      if (p.clamp) la = fmaxf(la, p.la_min);
+      p.la[tok] = la;
+      p.beta[tok] = p.beta_scale / (1.f + expf(-(bb + bb_h)));
+    }
   }
-  const float iq = p.q_scale / fmaxf(sqrtf(sq), p.eps), ik = 1.f / fmaxf(sqrtf(sk), p.eps);
-  const int64_t tok = ((int64_t)b * p.T + t) * p.H + h;
-  TO* oq = reinterpret_cast<TO*>(p.q.out) + tok * p.DK + lane * NK;
-  TO* ok = reinterpret_cast<TO*>(p.k.out) + tok * p.DK + lane * NK;
-  TO* ov = reinterpret_cast<TO*>(p.v.out) + tok * p.DV + lane * NV;
+  // the next call's conv state: tokens T - (TAPS - 1) .. T - 1, staged rows t1 - t0 .. t1 - t0 + TAPS - 2
+  if (t1 == p.T && TAPS > 1) {
 #pragma unroll
-  for (int n = 0; n < NK; ++n) {
-    q[n] *= iq;
-    k[n] *= ik;
-  }
-  store_vec<TO, NK>(oq, q);
-  store_vec<TO, NK>(ok, k);
-  store_vec<TO, NV>(ov, v);
-  if (lane == 0) {
-    const float a = to_f32(reinterpret_cast<const TX*>(p.xa)[(int64_t)b * p.sa_b + (int64_t)t * p.sa_t + h]);
-    const float bb = to_f32(reinterpret_cast<const TX*>(p.xb)[(int64_t)b * p.sb_b + (int64_t)t * p.sb_t + h]);
-    float la = -softplus(a + p.dt_bias[h]) * expf(p.A_log[h]);
-    if (p.clamp) la = fmaxf(la, p.la_min);
-    p.la[tok] = la;
-    p.beta[tok] = p.beta_scale / (1.f + expf(-(bb + (p.b_bias ? p.b_bias[h] : 0.f))));
-  }
-  // The next call's conv state: the last taps - 1 rows of every channel, from the sequence's last
-  // token (earlier rows come from the incoming state when T is short).
-  if (t == p.T - 1 && p.taps > 1) {
-    save_state<TX, NK>(p.q, b, p.T, p.taps, ck);
-    save_state<TX, NK>(p.k, b, p.T, p.taps, ck);
-    save_state<TX, NV>(p.v, b, p.T, p.taps, cv);
+    for (int c = 0; c < 3; ++c) {
+      const Comp& cp = *cs[c];
+      if (!cp.cout) continue;
+      TX* pc = reinterpret_cast<TX*>(cp.cout) + (int64_t)b * cp.csb;
+      for (int i = lane; i < (TAPS - 1) * len[c]; i += 32) {
+        const int j = i / len[c], ch = i - j * len[c];
+        pc[(int64_t)(h * len[c] + ch) * (TAPS - 1) + j] = stage[(size_t)(t1 - t0 + j) * W + off[c] + ch];
+      }
+    }
   }
 }
 
@@ -232,12 +273,14 @@ struct EpilogueParams {
 
 template <typename TY, typename TG, typename TO, int NPL>
 __global__ void __launch_bounds__(128) epilogue_kernel(const EpilogueParams p) {
-  const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  // 32-bit index arithmetic (B * T * H * 32 < 2^31 is checked on the host): 64-bit divisions would
+  // dominate this kernel's instruction count.
+  const unsigned row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  if (row >= (int64_t)p.B * p.T * p.H) return;
-  const int h = (int)(row % p.H);
-  const int64_t bt = row / p.H;
-  const int t = (int)(bt % p.T), b = (int)(bt / p.T);
+  if (row >= (unsigned)p.B * (unsigned)p.T * (unsigned)p.H) return;
+  const unsigned bt = row / (unsigned)p.H;
+  const int h = (int)(row - bt * (unsigned)p.H);
+  const int b = (int)(bt / (unsigned)p.T), t = (int)(bt - (unsigned)b * (unsigned)p.T);
   const int c0 = lane * NPL;
   float y[NPL];
   load_vec<NPL>(reinterpret_cast<const TY*>(p.y) + b * p.sy.b + t * p.sy.t + h * p.sy.h + c0, y);
@@ -269,16 +312,52 @@ bool device_ok() {
 
 bool a16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+constexpr int PROLOGUE_SMEM_MAX = 96 * 1024;
+
+// Shared memory of one prologue block: the weights and TOKS warps' staged rows.
+size_t prologue_smem(const PrologueParams& p, int run, int es) {
+  const size_t W = 2 * (size_t)p.DK + p.DV;
+  return (size_t)p.taps * W * 4 + (size_t)TOKS * (run + p.taps - 1) * W * es;
+}
+
+template <typename TX, typename TO, int NK, int NV, int TAPS>
+int launch_prologue_one(const PrologueParams& p, unsigned blocks, size_t sm, cudaStream_t s) {
+  static bool attr = false;  // per process: the attribute applies to every device's launches
+  if (!attr) {
+    if (cudaFuncSetAttribute(prologue_kernel<TX, TO, NK, NV, TAPS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             PROLOGUE_SMEM_MAX) != cudaSuccess)
+      return GDN_ERR_LAUNCH;
+    attr = true;
+  }
+  prologue_kernel<TX, TO, NK, NV, TAPS><<<blocks, 32 * TOKS, sm, s>>>(p);
+  return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+}
+
+template <typename TX, typename TO, int NK, int NV>
+int launch_prologue_taps(const PrologueParams& p, unsigned blocks, size_t sm, cudaStream_t s) {
+  switch (p.taps) {
+    case 1: return launch_prologue_one<TX, TO, NK, NV, 1>(p, blocks, sm, s);
+    case 2: return launch_prologue_one<TX, TO, NK, NV, 2>(p, blocks, sm, s);
+    case 3: return launch_prologue_one<TX, TO, NK, NV, 3>(p, blocks, sm, s);
+    case 4: return launch_prologue_one<TX, TO, NK, NV, 4>(p, blocks, sm, s);
+    default: return GDN_ERR_SHAPE;
+  }
+}
+
 template <typename TX, typename TO>
-int launch_prologue(const PrologueParams& p, cudaStream_t s) {
-  const int64_t blocks = (int64_t)p.B * p.H * ((p.T + TOKS - 1) / TOKS);
+int launch_prologue(PrologueParams p, cudaStream_t s) {
+  // the longest run (16, 8, .. 1 tokens per warp) whose staging fits the shared-memory budget
+  int run = 16;
+  while (run > 1 && prologue_smem(p, run, sizeof(TX)) > PROLOGUE_SMEM_MAX) run /= 2;
+  const size_t sm = prologue_smem(p, run, sizeof(TX));
+  if (sm > PROLOGUE_SMEM_MAX) return GDN_ERR_UNSUPPORTED;
+  p.run = run;
+  const int64_t runs = (p.T + run - 1) / run;
+  const int64_t blocks = (int64_t)p.B * p.H * ((runs + TOKS - 1) / TOKS);
   if (blocks > 0x7fffffff) return GDN_ERR_SHAPE;
   const int nk = p.DK / 32, nv = p.DV / 32;
-#define GDN_PRO(NK, NV)                                                                     \
-  if (nk == NK && nv == NV) {                                                               \
-    prologue_kernel<TX, TO, NK, NV><<<(unsigned)blocks, 32 * TOKS, 0, s>>>(p);              \
-    return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;                     \
-  }
+#define GDN_PRO(NK, NV) \
+  if (nk == NK && nv == NV) return launch_prologue_taps<TX, TO, NK, NV>(p, (unsigned)blocks, sm, s);
   GDN_PRO(2, 2) GDN_PRO(2, 4) GDN_PRO(4, 4) GDN_PRO(4, 8) GDN_PRO(8, 8) GDN_PRO(8, 16)
 #undef GDN_PRO
   return GDN_ERR_UNSUPPORTED;
@@ -349,6 +428,7 @@ int gdn_layer_epilogue(const gdn_epilogue_args* a, void* stream) {
   if (!a) return GDN_ERR_NULL;
   if (!a->y || !a->weight || !a->o) return GDN_ERR_NULL;
   if (a->B < 1 || a->T < 1 || a->H < 1 || (a->DV != 64 && a->DV != 128 && a->DV != 256 && a->DV != 512)) return GDN_ERR_SHAPE;
+  if (a->B * a->T * a->H * 32 > 0x7fffffffLL) return GDN_ERR_SHAPE;
   for (int32_t dt : {a->y_dtype, a->g_dtype, a->o_dtype})
     if (dt != GDN_DTYPE_BF16 && dt != GDN_DTYPE_F32) return GDN_ERR_DTYPE;
   if (!a16(a->y) || (a->g && !a16(a->g)) || !a16(a->o)) return GDN_ERR_ALIGN;

@@ -220,7 +220,7 @@ typedef struct {
   const float* weight;  /* (DV) fp32 */
   void* o;            /* [B][T][H*DV] */
   int64_t so_b, so_t;
-  int64_t B, T, H, DV;  /* DV in {64, 128, 256, 512} */
+  int64_t B, T, H, DV;  /* DV in {64, 128, 256, 512}; B * T * H < 2^26 */
   int32_t y_dtype, g_dtype, o_dtype;
   float eps;
 } gdn_epilogue_args;
