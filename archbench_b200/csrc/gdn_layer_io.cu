@@ -162,13 +162,15 @@ template <typename TX, typename TO, int NK, int NV, int TAPS>
 __global__ void __launch_bounds__(32 * TOKS) prologue_kernel(const PrologueParams p) {
   extern __shared__ __align__(16) float sw[];  // weights [q | k | v] x TAPS x (DK or DV), then the warps' rows
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  const int RUN = p.run, W = 2 * p.DK + p.DV;  // tokens per warp; elements per staged row
+  const int RUN = p.run;  // tokens per warp
+  constexpr int W = 2 * 32 * NK + 32 * NV;  // elements per staged row
   const int runs = (p.T + RUN - 1) / RUN, rgroups = (runs + TOKS - 1) / TOKS;
   const int bh = blockIdx.x / rgroups, rg = blockIdx.x - bh * rgroups;
   const int b = bh / p.H, h = bh - b * p.H;
+  constexpr int DK = 32 * NK, DV = 32 * NV;  // == p.DK, p.DV
   const Comp* cs[3] = {&p.q, &p.k, &p.v};
-  const int off[3] = {0, p.DK, 2 * p.DK}, len[3] = {p.DK, p.DK, p.DV};
-  float* swc[3] = {sw, sw + TAPS * p.DK, sw + 2 * TAPS * p.DK};
+  constexpr int off[3] = {0, DK, 2 * DK}, len[3] = {DK, DK, DV};
+  float* swc[3] = {sw, sw + TAPS * DK, sw + 2 * TAPS * DK};
 #pragma unroll
   for (int c = 0; c < 3; ++c) {
     if (!cs[c]->w) continue;
@@ -187,7 +189,8 @@ __global__ void __launch_bounds__(32 * TOKS) prologue_kernel(const PrologueParam
 #pragma unroll
   for (int c = 0; c < 3; ++c) {
     const Comp& cp = *cs[c];
-    const int chunks = len[c] / EPC, hc = h * len[c];
+    constexpr int chunks_[3] = {len[0] / EPC, len[1] / EPC, len[2] / EPC};
+    const int chunks = chunks_[c], hc = h * len[c];
     for (int i = lane; i < nrows * chunks; i += 32) {
       const int r = i / chunks, q = i - r * chunks, t = t0 - (TAPS - 1) + r;
       TX* dst = stage + (size_t)r * W + off[c] + q * EPC;
@@ -211,9 +214,9 @@ __global__ void __launch_bounds__(32 * TOKS) prologue_kernel(const PrologueParam
   for (int t = t0; t < t1; ++t) {
     const TX* rows = stage + (size_t)(t - t0) * W;
     float q[NK], k[NK], v[NV];
-    conv_tok<TX, TAPS, NK>(rows + lane * NK, W, swc[0] + lane * NK, p.DK, wq, q);
-    conv_tok<TX, TAPS, NK>(rows + p.DK + lane * NK, W, swc[1] + lane * NK, p.DK, wk, k);
-    conv_tok<TX, TAPS, NV>(rows + 2 * p.DK + lane * NV, W, swc[2] + lane * NV, p.DV, wv, v);
+    conv_tok<TX, TAPS, NK>(rows + lane * NK, W, swc[0] + lane * NK, DK, wq, q);
+    conv_tok<TX, TAPS, NK>(rows + DK + lane * NK, W, swc[1] + lane * NK, DK, wk, k);
+    conv_tok<TX, TAPS, NV>(rows + 2 * DK + lane * NV, W, swc[2] + lane * NV, DV, wv, v);
     float sq = 0.f, sk = 0.f;
 #pragma unroll
     for (int n = 0; n < NK; ++n) {
@@ -232,17 +235,19 @@ __global__ void __launch_bounds__(32 * TOKS) prologue_kernel(const PrologueParam
       q[n] *= iq;
       k[n] *= ik;
     }
-    store_vec<TO, NK>(reinterpret_cast<TO*>(p.q.out) + tok * p.DK + lane * NK, q);
-    store_vec<TO, NK>(reinterpret_cast<TO*>(p.k.out) + tok * p.DK + lane * NK, k);
-    store_vec<TO, NV>(reinterpret_cast<TO*>(p.v.out) + tok * p.DV + lane * NV, v);
-    if (lane == 0) {
-      const float a = to_f32(reinterpret_cast<const TX*>(p.xa)[(int64_t)b * p.sa_b + (int64_t)t * p.sa_t + h]);
-      const float bb = to_f32(reinterpret_cast<const TX*>(p.xb)[(int64_t)b * p.sb_b + (int64_t)t * p.sb_t + h]);
-      float la = -softplus(a + dtb) * Ae;
-      if (p.clamp) la = fmaxf(la, p.la_min);
-      p.la[tok] = la;
-      p.beta[tok] = p.beta_scale / (1.f + expf(-(bb + bb_h)));
-    }
+    store_vec<TO, NK>(reinterpret_cast<TO*>(p.q.out) + tok * DK + lane * NK, q);
+    store_vec<TO, NK>(reinterpret_cast<TO*>(p.k.out) + tok * DK + lane * NK, k);
+    store_vec<TO, NV>(reinterpret_cast<TO*>(p.v.out) + tok * DV + lane * NV, v);
+  }
+  // the gates, one token per lane
+  for (int t = t0 + lane; t < t1; t += 32) {
+    const int64_t tok = ((int64_t)b * p.T + t) * p.H + h;
+    const float a = to_f32(reinterpret_cast<const TX*>(p.xa)[(int64_t)b * p.sa_b + (int64_t)t * p.sa_t + h]);
+    const float bb = to_f32(reinterpret_cast<const TX*>(p.xb)[(int64_t)b * p.sb_b + (int64_t)t * p.sb_t + h]);
+    float la = -softplus(a + dtb) * Ae;
+    if (p.clamp) la = fmaxf(la, p.la_min);
+    p.la[tok] = la;
+    p.beta[tok] = p.beta_scale / (1.f + expf(-(bb + bb_h)));
   }
   // the next call's conv state: tokens T - (TAPS - 1) .. T - 1, staged rows t1 - t0 .. t1 - t0 + TAPS - 2
   if (t1 == p.T && TAPS > 1) {
@@ -346,9 +351,14 @@ int launch_prologue_taps(const PrologueParams& p, unsigned blocks, size_t sm, cu
 
 template <typename TX, typename TO>
 int launch_prologue(PrologueParams p, cudaStream_t s) {
-  // the longest run (16, 8, .. 1 tokens per warp) whose staging fits the shared-memory budget
+  // the longest run (16, 8, .. 1 tokens per warp) whose staging leaves room for 5 blocks per SM (44 KB),
+  // else the longest that fits the budget
   int run = 16;
-  while (run > 1 && prologue_smem(p, run, sizeof(TX)) > PROLOGUE_SMEM_MAX) run /= 2;
+  while (run > 1 && prologue_smem(p, run, sizeof(TX)) > 44 * 1024) run /= 2;
+  if (prologue_smem(p, run, sizeof(TX)) > 44 * 1024) {
+    run = 16;
+    while (run > 1 && prologue_smem(p, run, sizeof(TX)) > PROLOGUE_SMEM_MAX) run /= 2;
+  }
   const size_t sm = prologue_smem(p, run, sizeof(TX));
   if (sm > PROLOGUE_SMEM_MAX) return GDN_ERR_UNSUPPORTED;
   p.run = run;
