@@ -55,6 +55,7 @@ struct Params {
   float *dq, *dk, *du, *dv, *dbeta, *dla, *ds0;
   int64_t sq_b, sq_t, sq_h, sk_b, sk_t, sk_h, su_b, su_t, su_h, sv_b, sv_t, sv_h, sd_b, sd_t, sd_h;
   int T, H, NC, BH;
+  int DVt, vofs, accum;  // total DV; first state row of this 128-row slice; add dq/dk/du/dla/dbeta to the outputs
   __half *wT, *wA, *wW, *wUw, *wS, *wdS;  // per chunk: T, A (C x C), W, Uw (C x D), S0, dS1 (D x D)
   __half *wU, *wDU, *wdY, *wdR0;         // per chunk: U, d U, scaled dY, A^T dY (C x D)
   __half* wPc;                            // per chunk: dY^T Gamma Q (D x D)
@@ -329,7 +330,7 @@ __global__ void __launch_bounds__(NTHR) amax_kernel(Params p) {
 #pragma unroll
     for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(f[it][j]));
   if (c == 0 && p.dsT) {
-    const float4* s = reinterpret_cast<const float4*>(p.dsT + (int64_t)bh * D * D);
+    const float4* s = reinterpret_cast<const float4*>(p.dsT + ((int64_t)bh * p.DVt + p.vofs) * D);
     for (int i = threadIdx.x; i < D * D / 4; i += NTHR) {
       const float4 x = __ldg(s + i);
       m = fmaxf(m, fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w))));
@@ -632,8 +633,8 @@ __global__ void __launch_bounds__(NTHR, 1) chain_kernel(Params p) {
     const int col = 8 * nt + 2 * t4;
     float2 a = make_float2(0.f, 0.f), c2 = make_float2(0.f, 0.f);
     if (init) {
-      a = *reinterpret_cast<const float2*>(init + ((int64_t)bh * D + row0) * D + col);
-      c2 = *reinterpret_cast<const float2*>(init + ((int64_t)bh * D + row1) * D + col);
+      a = *reinterpret_cast<const float2*>(init + ((int64_t)bh * p.DVt + p.vofs + row0) * D + col);
+      c2 = *reinterpret_cast<const float2*>(init + ((int64_t)bh * p.DVt + p.vofs + row1) * D + col);
     }
     acc[0][nt][0] = scale * a.x; acc[0][nt][1] = scale * a.y; acc[0][nt][2] = scale * c2.x; acc[0][nt][3] = scale * c2.y;
   }
@@ -733,9 +734,9 @@ __global__ void __launch_bounds__(NTHR, 1) chain_kernel(Params p) {
 #pragma unroll
     for (int nt = 0; nt < 16; ++nt) {
       const int col = 8 * nt + 2 * t4;
-      *reinterpret_cast<float2*>(p.ds0 + ((int64_t)bh * D + row0) * D + col) =
+      *reinterpret_cast<float2*>(p.ds0 + ((int64_t)bh * p.DVt + p.vofs + row0) * D + col) =
           make_float2(inv * acc[0][nt][0], inv * acc[0][nt][1]);
-      *reinterpret_cast<float2*>(p.ds0 + ((int64_t)bh * D + row1) * D + col) =
+      *reinterpret_cast<float2*>(p.ds0 + ((int64_t)bh * p.DVt + p.vofs + row1) * D + col) =
           make_float2(inv * acc[0][nt][2], inv * acc[0][nt][3]);
     }
   }
@@ -1020,29 +1021,39 @@ __global__ void __launch_bounds__(NTHR, 1) local_kernel(Params p) {
   zero(acc);
   mma_acc<1, 8, true, true, C>(acc, sT, LDC, m0, sdR, LDT, n0, lane);
 
-  // outputs (fp32, contiguous (B, T, H, 128)), divided by the gradient scale
+  // outputs (fp32, contiguous (B, T, H, DK) and (B, T, H, DV)), divided by the gradient scale; dq, dk, du
+  // are added to the previous slice's when the state has more than 128 rows
   const bool has_u = p.u != nullptr;
   float pa = 0.f, pb = 0.f;  // dbeta partials: dU . k
+  auto put = [&](float* dst, float x, float y) {
+    float2* q2 = reinterpret_cast<float2*>(dst);
+    if (p.accum) {
+      const float2 o = *q2;
+      x += o.x;
+      y += o.y;
+    }
+    *q2 = make_float2(x, y);
+  };
 #pragma unroll
   for (int hf = 0; hf < 2; ++hf) {
     const int row = hf ? rb : ra;
     if (row >= nvalid) continue;
-    const int64_t o = (((int64_t)b * p.T + t0 + row) * p.H + h) * D;
+    const int64_t tokrow = ((int64_t)b * p.T + t0 + row) * p.H + h;
+    const int64_t o = tokrow * D, ov = tokrow * p.DVt + p.vofs;
     const float bt = sbeta[row];
 #pragma unroll
     for (int nt = 0; nt < 8; ++nt) {
       const int col = n0 + 8 * nt + 2 * t4;
       const int e0 = 2 * hf;
-      *reinterpret_cast<float2*>(p.dq + o + col) = make_float2(inv * aQ[0][nt][e0], inv * aQ[0][nt][e0 + 1]);
-      *reinterpret_cast<float2*>(p.dv + o + col) = make_float2(inv * acc[0][nt][e0], inv * acc[0][nt][e0 + 1]);
+      put(p.dq + o + col, inv * aQ[0][nt][e0], inv * aQ[0][nt][e0 + 1]);
+      *reinterpret_cast<float2*>(p.dv + ov + col) = make_float2(inv * acc[0][nt][e0], inv * acc[0][nt][e0 + 1]);
       if (has_u) {
-        *reinterpret_cast<float2*>(p.dk + o + col) = make_float2(inv * aK[0][nt][e0], inv * aK[0][nt][e0 + 1]);
-        *reinterpret_cast<float2*>(p.du + o + col) = make_float2(inv * aU[0][nt][e0], inv * aU[0][nt][e0 + 1]);
+        put(p.dk + o + col, inv * aK[0][nt][e0], inv * aK[0][nt][e0 + 1]);
+        put(p.du + o + col, inv * aU[0][nt][e0], inv * aU[0][nt][e0 + 1]);
       } else {
         // u = beta k: dk += beta dU, dbeta = dU . k
         const float2 kk = u2f(*reinterpret_cast<const uint32_t*>(sK + row * LDT + col));
-        *reinterpret_cast<float2*>(p.dk + o + col) =
-            make_float2(inv * (aK[0][nt][e0] + bt * aU[0][nt][e0]), inv * (aK[0][nt][e0 + 1] + bt * aU[0][nt][e0 + 1]));
+        put(p.dk + o + col, inv * (aK[0][nt][e0] + bt * aU[0][nt][e0]), inv * (aK[0][nt][e0 + 1] + bt * aU[0][nt][e0 + 1]));
         const float s = aU[0][nt][e0] * kk.x + aU[0][nt][e0 + 1] * kk.y;
         if (hf) pb += s; else pa += s;
       }
@@ -1078,11 +1089,12 @@ __global__ void __launch_bounds__(NTHR, 1) local_kernel(Params p) {
     }
     dg0 += __shfl_sync(0xffffffffu, dg1, 0);
     const int64_t gi = ((int64_t)b * p.T + t0) * p.H + h;
-    if (lane < nvalid) p.dla[gi + (int64_t)lane * p.H] = inv * dg0;
-    if (lane + 32 < nvalid) p.dla[gi + (int64_t)(lane + 32) * p.H] = inv * dg1;
+    auto put1 = [&](float* dst, float x) { *dst = p.accum ? *dst + x : x; };
+    if (lane < nvalid) put1(p.dla + gi + (int64_t)lane * p.H, inv * dg0);
+    if (lane + 32 < nvalid) put1(p.dla + gi + (int64_t)(lane + 32) * p.H, inv * dg1);
     if (!has_u) {
-      if (lane < nvalid) p.dbeta[gi + (int64_t)lane * p.H] = inv * (sdb[lane] + sdb[C + lane]);
-      if (lane + 32 < nvalid) p.dbeta[gi + (int64_t)(lane + 32) * p.H] = inv * (sdb[lane + 32] + sdb[C + lane + 32]);
+      if (lane < nvalid) put1(p.dbeta + gi + (int64_t)lane * p.H, inv * (sdb[lane] + sdb[C + lane]));
+      if (lane + 32 < nvalid) put1(p.dbeta + gi + (int64_t)(lane + 32) * p.H, inv * (sdb[lane + 32] + sdb[C + lane + 32]));
     }
   }
 }
@@ -1140,7 +1152,7 @@ int esize(int dt) { return dt == GDN_DTYPE_BF16 ? 2 : (dt == GDN_DTYPE_F32 ? 4 :
 int validate(const gdn_backward_args* a) {
   if (!a) return GDN_ERR_NULL;
   if (a->B <= 0 || a->H <= 0 || a->T < 0) return GDN_ERR_SHAPE;
-  if (a->DK != D || a->DV != D) return GDN_ERR_UNSUPPORTED;
+  if (a->DK != D || a->DV < D || a->DV % D != 0 || a->DV > 8 * D) return GDN_ERR_UNSUPPORTED;
   if (a->B * a->H > (1LL << 24) || a->T > (1LL << 30)) return GDN_ERR_SHAPE;
   const int es = esize(a->in_dtype), ed = esize(a->dy_dtype);
   if (!es || !ed) return GDN_ERR_DTYPE;
@@ -1188,7 +1200,7 @@ int gdn_prefill_bwd(const gdn_backward_args* a, void* stream) {
   const int64_t BH = a->B * a->H;
   if (a->T == 0) {  // no tokens: the initial-state gradient is the final-state gradient
     if (!a->ds0) return GDN_OK;
-    const size_t n = (size_t)BH * D * D * 4;
+    const size_t n = (size_t)BH * a->DV * D * 4;
     const cudaError_t e = a->ds_T ? cudaMemcpyAsync(a->ds0, a->ds_T, n, cudaMemcpyDeviceToDevice, s) : cudaMemsetAsync(a->ds0, 0, n, s);
     return e == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
   }
@@ -1223,10 +1235,23 @@ int gdn_prefill_bwd(const gdn_backward_args* a, void* stream) {
   p.amax = reinterpret_cast<unsigned*>(ws + l.amax);
   p.scale = reinterpret_cast<float*>(ws + l.scale);
   const bool in_bf = a->in_dtype == GDN_DTYPE_BF16, dy_bf = a->dy_dtype == GDN_DTYPE_BF16;
-  if (in_bf && dy_bf) return launch<__nv_bfloat16, __nv_bfloat16>(p, s);
-  if (in_bf) return launch<__nv_bfloat16, float>(p, s);
-  if (dy_bf) return launch<float, __nv_bfloat16>(p, s);
-  return launch<float, float>(p, s);
+  // The rows of the state are independent: a DV > 128 state is 128-row slices, each a full backward of
+  // its own v / dy columns (sharing q, k, u, la), whose dq, dk, du, dla, dbeta add up.
+  p.DVt = (int)a->DV;
+  const int es_in = in_bf ? 2 : 4, es_dy = dy_bf ? 2 : 4;
+  for (int sl = 0; sl < (int)(a->DV / D); ++sl) {
+    p.vofs = sl * D;
+    p.accum = sl > 0;
+    p.v = static_cast<const uint8_t*>(a->v) + (size_t)sl * D * es_in;
+    p.dy = static_cast<const uint8_t*>(a->dy) + (size_t)sl * D * es_dy;
+    int r;
+    if (in_bf && dy_bf) r = launch<__nv_bfloat16, __nv_bfloat16>(p, s);
+    else if (in_bf) r = launch<__nv_bfloat16, float>(p, s);
+    else if (dy_bf) r = launch<float, __nv_bfloat16>(p, s);
+    else r = launch<float, float>(p, s);
+    if (r != GDN_OK) return r;
+  }
+  return GDN_OK;
 }
 
 }  // extern "C"

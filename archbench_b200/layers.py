@@ -15,7 +15,7 @@ norms and the gates run as one CUDA kernel (``ops.layer_prologue``), the token m
 (``ops.layer_epilogue``).  ``fused_io = False`` on a module (or a configuration the kernels do
 not serve: N-step write vectors, conv bias, odd head sizes) keeps those parts in PyTorch, and so
 does every call that builds an autograd graph (training): there the scan runs forward and
-backward on the CUDA kernels (DK = DV = 128) and the rest through PyTorch autograd.  There is no
+backward on the CUDA kernels (DK = 128, DV a multiple of 128) and the rest through PyTorch autograd.  There is no
 CPU path.
 """
 

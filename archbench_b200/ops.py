@@ -250,8 +250,8 @@ def _prefill_bwd_impl(q, k, u, v, la, beta, s0, dy, ds_T, want_ds0: bool):
     dy = _prep_token(dy, "dy", torch.bfloat16 if dy.dtype == torch.bfloat16 else torch.float32)
     B, T, H, DK = q.shape
     DV = v.shape[-1]
-    if DK != 128 or DV != 128:
-        raise NotImplementedError(f"the prefill backward serves DK = DV = 128 (got DK={DK}, DV={DV})")
+    if DK != 128 or DV % 128 or DV > 1024:
+        raise NotImplementedError(f"the prefill backward serves DK = 128, DV a multiple of 128 up to 1024 (got DK={DK}, DV={DV})")
     if dy.shape != (B, T, H, DV):
         raise ValueError(f"dy must be {(B, T, H, DV)}, got {tuple(dy.shape)}")
     la = la.float().contiguous()
@@ -386,7 +386,7 @@ _prefill_op.register_autograd(_prefill_backward, setup_context=_prefill_setup)
 def gdn_prefill_bwd(q, k, v, la, dy, beta=None, u=None, initial_state=None, ds_T=None, want_ds0=False):
     """Gradients of ``gdn_prefill`` for incoming dy (B, T, H, DV) and ds_T (B, H, DV, DK) or None.
     Returns a dict of fp32 tensors: dq, dk, dv, dla, du (u given) or dbeta, and ds0 if ``want_ds0``.
-    DK = DV = 128."""
+    DK = 128, DV a multiple of 128."""
     if (u is None) == (beta is None):
         raise ValueError("give exactly one of beta (u = beta * k) and u")
     dq, dk, dub, dv, dla, ds0 = _prefill_bwd_op(q, k, u, v, la, beta, initial_state, dy, ds_T, bool(want_ds0))

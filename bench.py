@@ -341,7 +341,7 @@ def bench_backward(args, rank, world):
                          "frac": flops / t_b / 1e12 / tflops, "peak_source": src,
                          "executed_flops_per_launch": flops, "note": "mma.sync fp16 products; four launches (amax, prep, chains, local)",
                          "hbm_achieved_gbs": alg / t_b / 1e9, "algorithmic_bytes_per_launch": alg},
-            "gpu_launches": 3 * steps + 4 * steps}
+            "gpu_launches": 9 * steps}
 
 
 def bench_layer(args, rank, world):

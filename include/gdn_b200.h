@@ -229,7 +229,8 @@ int gdn_layer_epilogue(const gdn_epilogue_args* args, void* stream);
 
 /*
  * Prefill backward: gradients of gdn_prefill_fwd's outputs (y and, optionally, the final state)
- * with respect to q, k, u (or beta), v, la and the initial state, for DK = DV = 128.
+ * with respect to q, k, u (or beta), v, la and the initial state, for DK = 128 and DV a multiple of
+ * 128 up to 1024 (a state of more than 128 rows runs as 128-row slices, one after another).
  *
  * Replaces the backward of the custom ops archbench's scan runs under autograd:
  * archbench::nsgdn_chunk_bwd (archbench/layers/nsgdn.py:369-384, registered as the autograd

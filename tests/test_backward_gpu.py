@@ -34,12 +34,13 @@ def check(got, want, what):
     return rel
 
 
-def case(B, T, H, seed, s0=True, dsT=True, with_u=False, dy_scale=1.0, dy_dtype=torch.bfloat16, in_dtype=torch.bfloat16):
-    x = make_inputs(B, T, H, D, D, seed=seed, dtype=in_dtype)
+def case(B, T, H, seed, s0=True, dsT=True, with_u=False, dy_scale=1.0, dy_dtype=torch.bfloat16, in_dtype=torch.bfloat16,
+         DV=D):
+    x = make_inputs(B, T, H, D, DV, seed=seed, dtype=in_dtype)
     g = torch.Generator().manual_seed(seed + 7)
-    S0 = 0.3 * torch.randn(B, H, D, D, generator=g) if s0 else None
-    dS = torch.randn(B, H, D, D, generator=g) * dy_scale if dsT else None
-    dy = (torch.randn(B, T, H, D, generator=g) * dy_scale).to(dy_dtype)
+    S0 = 0.3 * torch.randn(B, H, DV, D, generator=g) if s0 else None
+    dS = torch.randn(B, H, DV, D, generator=g) * dy_scale if dsT else None
+    dy = (torch.randn(B, T, H, DV, generator=g) * dy_scale).to(dy_dtype)
     u = None
     if with_u:
         u = torch.nn.functional.normalize(0.7 * x["k"].float() + 0.1 * torch.randn(B, T, H, D, generator=g), dim=-1)
@@ -89,6 +90,14 @@ def test_backward_gradient_scale(dy_scale):
     scale (dy, dS_T) by a power of two per (b, h) before fp16 operands."""
     grads, want = run(*case(1, 128, 2, seed=11, dy_scale=dy_scale))
     check_all(grads, want, f"dy x {dy_scale:g}")
+
+
+@pytest.mark.parametrize("with_u", [False, True])
+def test_backward_wide_state(with_u):
+    """DV = 256 (head_dim 128, expand_v 2 as in archbench's gdn and nsgdn configs): two 128-row state
+    slices whose shared-input gradients add up."""
+    grads, want = run(*case(1, 130, 2, seed=29, with_u=with_u, DV=256))
+    check_all(grads, want, f"DV=256 u={with_u}")
 
 
 def test_backward_fp32_inputs_and_dy():
@@ -154,7 +163,7 @@ def _torch_recurrence(q, k, v, la, beta=None, u=None, initial_state=None, output
     return y, (S.float() if output_final_state else None)
 
 
-@pytest.mark.parametrize("layer", ["nsgdn1", "nsgdn2", "gdn"])
+@pytest.mark.parametrize("layer", ["nsgdn1", "nsgdn2", "gdn", "nsgdn_ref_config", "gdn_ref_config"])
 def test_layer_parameter_gradients(layer, monkeypatch):
     """A training step of the drop-in layers: parameter gradients through the CUDA backward against
     the same layer with its scan replaced by a float64 autograd recurrence."""
@@ -163,6 +172,10 @@ def test_layer_parameter_gradients(layer, monkeypatch):
     torch.manual_seed(0)
     if layer == "gdn":
         m = layers.GatedDeltaNet(hidden_size=256, expand_v=1, head_dim=128, num_heads=2).cuda()
+    elif layer == "gdn_ref_config":  # archbench configs/arch/gdn.yaml: head_dim 128, expand_v 2
+        m = layers.GatedDeltaNet(hidden_size=256, expand_v=2.0, head_dim=128, num_heads=2, use_gate=True, conv_size=4).cuda()
+    elif layer == "nsgdn_ref_config":  # archbench configs/arch/nsgdn.yaml: head_dim 128, expand_v 2, n_steps 2
+        m = layers.NStepGDN(256, num_heads=2, head_dim=128, expand_v=2.0, n_steps=2, lam=1.0, conv_size=4).cuda()
     else:
         m = layers.NStepGDN(256, num_heads=2, head_dim=128, expand_v=1.0, n_steps=1 if layer == "nsgdn1" else 2).cuda()
     x = torch.randn(2, 96, 256, device="cuda")
