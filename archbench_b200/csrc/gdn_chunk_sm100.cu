@@ -76,6 +76,7 @@ struct Params {
   void* y;
   gdn_strides sy;
   int B, T, H;
+  int srows;  // state rows per (b, h) of the full state (DV); this launch serves 128 of them
 };
 
 // Byte offset of 16-byte chunk `c` (0..7) of row `r` in a 128-byte-row, 128B-swizzled tile.
@@ -192,7 +193,7 @@ __global__ void __launch_bounds__(NT, 1)
 
   // Initial state -> TMEM (thread i owns state row i).
   {
-    const float* src = p.s0 ? p.s0 + ((int64_t)bh * D + tid) * D : nullptr;
+    const float* src = p.s0 ? p.s0 + ((int64_t)bh * p.srows + tid) * D : nullptr;
 #pragma unroll 1
     for (int c4 = 0; c4 < 4; ++c4) {
       float v[32];
@@ -476,7 +477,7 @@ __global__ void __launch_bounds__(NT, 1)
   }
 
   if (!abort && p.s_out != nullptr) {
-    float* dst = p.s_out + ((int64_t)bh * D + tid) * D;
+    float* dst = p.s_out + ((int64_t)bh * p.srows + tid) * D;
 #pragma unroll 1
     for (int c4 = 0; c4 < 4; ++c4) {
       float v[32];
@@ -545,10 +546,23 @@ int launch(const gdn_prefill_args* a, cudaStream_t stream) {
     attr_set = true;
   }
   Params p;
-  p.beta = a->beta; p.la = a->la; p.s0 = a->s0; p.s_out = a->s_out; p.y = a->y; p.sy = a->sy;
-  p.B = (int)a->B; p.T = (int)a->T; p.H = (int)a->H;
-  kern<<<(unsigned)(a->B * a->H), NT, LY::DYN, stream>>>(mq, mk, mv, mu, p);
-  return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+  p.beta = a->beta; p.la = a->la; p.B = (int)a->B; p.T = (int)a->T; p.H = (int)a->H; p.sy = a->sy;
+  p.srows = (int)a->DV;
+  // The state's rows are independent: a DV = 128 n state runs as n launches, each over 128 rows with its
+  // own v columns, y columns and state rows (q, k, u and the gates shared).
+  for (int sl = 0; sl < (int)(a->DV / D); ++sl) {
+    if (sl > 0) {
+      gdn_prefill_args b = *a;
+      b.v = static_cast<const __nv_bfloat16*>(a->v) + (size_t)sl * D;
+      if (!make_map(&mv, b.v, &b, a->sv)) return GDN_ERR_LAUNCH;
+    }
+    p.s0 = a->s0 ? a->s0 + (size_t)sl * D * D : nullptr;
+    p.s_out = a->s_out ? a->s_out + (size_t)sl * D * D : nullptr;
+    p.y = static_cast<TOut*>(a->y) + (size_t)sl * D;
+    kern<<<(unsigned)(a->B * a->H), NT, LY::DYN, stream>>>(mq, mk, mv, mu, p);
+    if (cudaGetLastError() != cudaSuccess) return GDN_ERR_LAUNCH;
+  }
+  return GDN_OK;
 }
 
 bool tma_ok(const void* ptr, const gdn_strides& s) {
@@ -561,14 +575,14 @@ bool tma_ok(const void* ptr, const gdn_strides& s) {
 
 // The chunked path: the warp-specialised kernel (gdn_chunk_ws_sm100.cu) for u = beta k with
 // DV any multiple of 128, and this single-warp-group kernel for an explicit write vector u
-// (nsgdn n_steps > 1) with DV = 128.  Both need 16-byte-aligned rows for TMA.
+// (nsgdn n_steps > 1) with DV a multiple of 128 (one launch per 128 state rows).  Both need 16-byte-aligned rows for TMA.
 bool gdn_chunk_supported(const gdn_prefill_args* a) {
   using namespace gdn::chunk;
   if (a->in_dtype != GDN_DTYPE_BF16 || a->DK != D || a->T < 1) return false;
   if (!tma_ok(a->q, a->sq) || !tma_ok(a->k, a->sk) || !tma_ok(a->v, a->sv)) return false;
   if (a->u && !tma_ok(a->u, a->su)) return false;
   if ((a->s0 && (uintptr_t)a->s0 % 16) || (a->s_out && (uintptr_t)a->s_out % 16)) return false;
-  if (a->u) return a->DV == D;
+  if (a->u) return a->DV % D == 0 && a->DV <= 8 * D;
   return gdn_chunk_ws_supported(a);
 }
 

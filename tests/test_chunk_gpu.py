@@ -178,3 +178,25 @@ def test_value_dim_multiple_of_128(DV):
     y, S = ops.gdn_prefill(g["q"], g["k"], g["v"], g["la"], beta=g["beta"], initial_state=S0.cuda(), output_final_state=True, out_dtype=torch.float32)
     check(y, y_o, f"y DV={DV}")
     check(S, S_o, f"S_T DV={DV}")
+
+
+@pytest.mark.parametrize("DV", [256, 384])
+def test_write_vectors_with_wide_state(DV):
+    """n_steps = 2 write vectors with DV = 2 DK (configs/arch/nsgdn.yaml: head_dim 128, expand_v 2,
+    n_steps 2): the explicit-u kernel runs once per 128-row state slice; bf16 output, initial state
+    updated in place."""
+    B, T, H = 2, 130, 2
+    x = make_inputs(B, T, H, 128, DV, seed=31 + DV, dtype=torch.bfloat16)
+    k = np32(x["k"]).astype(np.float64)
+    p = np.pad(k[:, :-1], ((0, 0), (1, 0), (0, 0), (0, 0)))
+    u = O.write_direction(k, p, np32(x["beta"]).astype(np.float64), np.array([1.0, 0.7]), 2)
+    u_bf = torch.from_numpy(u.astype(np.float32)).to(torch.bfloat16)
+    S0 = torch.randn(B, H, DV, 128, generator=torch.Generator().manual_seed(4)) * 0.2
+    y_o, S_o = O.recurrence_c(*(np32(x[n]) for n in ("q", "k", "v", "la")), u=np32(u_bf), s0=S0.numpy())
+    g = {k_: v.cuda() for k_, v in x.items()}
+    assert ops.selected_impl(g["q"], g["k"], g["v"], g["la"], u=u_bf.cuda()) == "chunk_single"
+    s = S0.cuda()
+    y, S = ops.gdn_prefill(g["q"], g["k"], g["v"], g["la"], u=u_bf.cuda(), initial_state=s, output_final_state=True,
+                           out_dtype=torch.float32)
+    check(y, y_o, f"y DV={DV} (u given)")
+    check(S, S_o, f"S_T DV={DV} (u given)")
