@@ -1,0 +1,553 @@
+// Backward of the layer prologue and epilogue (gdn_layer_io.cu), so that training runs the fused
+// kernels too.  Everything the forward computed is recomputed from its inputs.
+//
+// Prologue, per (b, t, h) and component (conv weights w, taps TAPS):
+//   c_t = sum_j w_j x_{t-(TAPS-1)+j},  s_t = SiLU(c_t);  q = q_scale s / max(|s|, eps), k likewise, v = s.
+//   ds = scale / m (dq - [|s| > eps] s^ (s^ . dq)) with m = max(|s|, eps), s^ = s / m (v: ds = dv);
+//   dc = ds SiLU'(c);  dx_t = sum_j w_j dc_{t+(TAPS-1)-j};  dw_j = sum_t dc_t x_{t-(TAPS-1)+j};
+//   la = -softplus(a + dt_bias) exp(A_log) (zero gradient where clamped at la_min):
+//     da = dla (-sigmoid(a + dt_bias) exp(A_log)), ddt_bias = sum da, dA_log = sum dla la;
+//   beta = beta_scale sigmoid(b + b_bias): db = dbeta beta_scale sigmoid (1 - sigmoid), db_bias = sum db.
+// One warp per (b, h) and run of RUN tokens as in the forward; the run's projection rows (and the conv
+// halo on both sides) are staged in shared memory by cp.async; dc of the last TAPS tokens is kept in
+// registers, so dx of a token is finished as soon as dc of the TAPS - 1 tokens after it is known.
+// Parameter gradients are reduced over the block's warps in shared memory and added to the outputs
+// with one atomic add per element and block (fp32; the summation order across blocks is not fixed).
+//
+// Epilogue, per (b, t, h) over DV: o = y r w SiLU(g), r = (mean(y^2) + eps)^-1/2:
+//   z = w SiLU(g) do;  dy = r z - y r^3 mean(y z);  dg = do y r w SiLU'(g);  dw = sum do y r SiLU(g).
+#include <math.h>
+#include <string.h>
+
+#include "gdn_common.cuh"
+
+namespace gdn {
+namespace layer_io_bwd {
+
+constexpr int MAX_TAPS = 4;
+constexpr int WARPS = 4;  // warps per prologue block
+constexpr int RUN = 16;   // tokens per warp
+
+__device__ __forceinline__ float sigm(float x) { return 1.f / (1.f + __expf(-x)); }
+__device__ __forceinline__ float softplus(float x) { return x > 20.f ? x : log1pf(expf(x)); }
+__device__ __forceinline__ float dsilu(float c) {
+  const float s = sigm(c);
+  return s * (1.f + c * (1.f - s));
+}
+
+template <typename TO, int N>
+__device__ __forceinline__ void stv(TO* p, const float (&v)[N]) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) store_as(p + i, v[i]);
+}
+
+__device__ __forceinline__ void cp16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+               : "memory");
+}
+
+struct CompB {             // one of q, k, v
+  const void* x;           // projection [B][T][channels] with strides
+  int64_t sb, st;
+  const float* w;          // (taps, channels) fp32 or NULL
+  int64_t wch;
+  const void* g;           // incoming gradient [B][T][H][D] contiguous (grad dtype)
+  void* dx;                // projection gradient, strides dsb, dst (projection dtype)
+  int64_t dsb, dst;
+  float* dw;               // (taps, channels) fp32 accumulated, or NULL
+};
+
+struct ProBwdParams {
+  CompB q, k, v;
+  const void* xa;
+  const void* xb;
+  int64_t sa_b, sa_t, sb_b, sb_t;
+  void* dxa;
+  void* dxb;
+  int64_t dsa_b, dsa_t, dsb_b, dsb_t;
+  const float* dla;
+  const float* dbeta;
+  const float* A_log;
+  const float* dt_bias;
+  const float* b_bias;
+  float* dA_log;
+  float* ddt_bias;
+  float* db_bias;
+  int B, T, H, DK, DV, clamp;
+  float q_scale, eps, la_min, beta_scale;
+};
+
+// One component of one lane: dc window (last TAPS tokens), conv-weight gradient accumulators.
+template <int TAPS, int NPL>
+struct Lane {
+  float win[TAPS][NPL];  // win[j] = dc of token t - (TAPS - 1) + j after the latest push
+  float dw[TAPS][NPL];
+  __device__ __forceinline__ void clear() {
+#pragma unroll
+    for (int j = 0; j < TAPS; ++j)
+#pragma unroll
+      for (int n = 0; n < NPL; ++n) win[j][n] = dw[j][n] = 0.f;
+  }
+  __device__ __forceinline__ void push(const float (&dc)[NPL]) {
+#pragma unroll
+    for (int j = 0; j + 1 < TAPS; ++j)
+#pragma unroll
+      for (int n = 0; n < NPL; ++n) win[j][n] = win[j + 1][n];
+#pragma unroll
+    for (int n = 0; n < NPL; ++n) win[TAPS - 1][n] = dc[n];
+  }
+};
+
+// dx of the token TAPS - 1 before the latest push: sum_j w_j dc_{tau + (TAPS-1) - j} = sum_j w_j win[TAPS-1-j].
+template <int TAPS, int NPL>
+__device__ __forceinline__ void dx_of(const Lane<TAPS, NPL>& L, const float* w, int wld, bool has_w, float (&o)[NPL]) {
+  if (has_w) {
+#pragma unroll
+    for (int n = 0; n < NPL; ++n) o[n] = 0.f;
+#pragma unroll
+    for (int j = 0; j < TAPS; ++j) {
+      float wj[NPL];
+      load_vec<NPL>(w + j * wld, wj);
+#pragma unroll
+      for (int n = 0; n < NPL; ++n) o[n] = fmaf(wj[n], L.win[TAPS - 1 - j][n], o[n]);
+    }
+  } else {
+#pragma unroll
+    for (int n = 0; n < NPL; ++n) o[n] = L.win[0][n];
+  }
+}
+
+// dc of one component at token t from the staged rows (row j of the conv window at rows + j * ld).
+template <typename TX, typename TG, int TAPS, int NPL, bool NORM>
+__device__ __forceinline__ void comp_dc(const TX* rows, int ld, const float* w, int wld, bool has_w, const TG* gp,
+                                        float scale, float eps, float (&dc)[NPL]) {
+  float c[NPL], xj[NPL];
+  if (has_w) {
+#pragma unroll
+    for (int n = 0; n < NPL; ++n) c[n] = 0.f;
+#pragma unroll
+    for (int j = 0; j < TAPS; ++j) {
+      float wj[NPL];
+      load_vec<NPL>(w + j * wld, wj);
+      load_vec<NPL>(rows + j * ld, xj);
+#pragma unroll
+      for (int n = 0; n < NPL; ++n) c[n] = fmaf(wj[n], xj[n], c[n]);
+    }
+  } else {
+    load_vec<NPL>(rows + (TAPS - 1) * ld, c);
+  }
+  float g[NPL], s[NPL];
+  load_vec<NPL>(gp, g);
+#pragma unroll
+  for (int n = 0; n < NPL; ++n) s[n] = c[n] * sigm(c[n]);
+  if (NORM) {
+    float ss = 0.f, sg = 0.f;
+#pragma unroll
+    for (int n = 0; n < NPL; ++n) {
+      ss = fmaf(s[n], s[n], ss);
+      sg = fmaf(s[n], g[n], sg);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      sg += __shfl_xor_sync(0xffffffffu, sg, o);
+    }
+    const float nrm = sqrtf(ss), m = fmaxf(nrm, eps), inv = 1.f / m;
+    const float proj = nrm > eps ? sg * inv * inv : 0.f;  // s^ . dq / m with s^ = s / m
+#pragma unroll
+    for (int n = 0; n < NPL; ++n) g[n] = scale * inv * (g[n] - s[n] * proj);
+  }
+#pragma unroll
+  for (int n = 0; n < NPL; ++n) dc[n] = g[n] * dsilu(c[n]);
+}
+
+template <typename TX, typename TG, int NK, int NV, int TAPS>
+__global__ void __launch_bounds__(32 * WARPS) prologue_bwd_kernel(const ProBwdParams p) {
+  extern __shared__ __align__(16) float sw[];  // weights [q | k | v] x TAPS x D, then staged rows per warp
+  constexpr int DK = 32 * NK, DV = 32 * NV, W = 2 * DK + DV;
+  constexpr int NROWS = RUN + 2 * (TAPS - 1);  // staged tokens t0 - (TAPS - 1) .. t1 + TAPS - 2
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int runs = (p.T + RUN - 1) / RUN, rgroups = (runs + WARPS - 1) / WARPS;
+  const int bh = blockIdx.x / rgroups, rg = blockIdx.x - bh * rgroups;
+  const int b = bh / p.H, h = bh - b * p.H;
+  const CompB* cs[3] = {&p.q, &p.k, &p.v};
+  constexpr int off[3] = {0, DK, 2 * DK}, len[3] = {DK, DK, DV};
+  float* swc[3] = {sw, sw + TAPS * DK, sw + 2 * TAPS * DK};
+#pragma unroll
+  for (int c = 0; c < 3; ++c) {
+    if (!cs[c]->w) continue;
+    for (int i = threadIdx.x; i < TAPS * len[c]; i += blockDim.x) {
+      const int j = i / len[c], ch = i - j * len[c];
+      swc[c][i] = cs[c]->w[(int64_t)j * cs[c]->wch + (int64_t)h * len[c] + ch];
+    }
+  }
+  TX* stage = reinterpret_cast<TX*>(sw + TAPS * W) + (size_t)wid * NROWS * W;
+  __syncthreads();
+  const int run = rg * WARPS + wid;
+  const bool active = run < runs;
+  const int t0 = run * RUN, t1 = active ? min(p.T, t0 + RUN) : t0;
+  const int tend = min(p.T, t1 + TAPS - 1);  // dc is needed for tokens t0 .. tend - 1
+  constexpr int EPC = 16 / sizeof(TX);
+  if (active) {
+    const int nrows = tend - t0 + TAPS - 1;
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+      const CompB& cp = *cs[c];
+      constexpr int chunks_[3] = {len[0] / EPC, len[1] / EPC, len[2] / EPC};
+      const int chunks = chunks_[c], hc = h * len[c];
+      for (int i = lane; i < nrows * chunks; i += 32) {
+        const int r = i / chunks, q = i - r * chunks, t = t0 - (TAPS - 1) + r;
+        TX* dst = stage + (size_t)r * W + off[c] + q * EPC;
+        if (t >= 0) {
+          cp16(dst, reinterpret_cast<const TX*>(cp.x) + (int64_t)b * cp.sb + (int64_t)t * cp.st + hc + q * EPC);
+        } else {
+#pragma unroll
+          for (int e = 0; e < EPC; ++e) store_as(dst + e, 0.f);  // training calls start from zero history
+        }
+      }
+    }
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+    __syncwarp();
+  }
+  const bool wq = p.q.w != nullptr, wk = p.k.w != nullptr, wv = p.v.w != nullptr;
+  Lane<TAPS, NK> lq, lk;
+  Lane<TAPS, NV> lv;
+  lq.clear();
+  lk.clear();
+  lv.clear();
+  const int64_t tokb = ((int64_t)b * p.T) * p.H + h;  // token (b, 0, h)
+  if (active) {
+#pragma unroll 1
+    for (int t = t0; t <= t1 + TAPS - 2; ++t) {
+      float dq[NK], dk[NK], dv[NV];
+      if (t < tend) {
+        const TX* rows = stage + (size_t)(t - t0) * W;
+        const int64_t tok = tokb + (int64_t)t * p.H;
+        comp_dc<TX, TG, TAPS, NK, true>(rows + lane * NK, W, swc[0] + lane * NK, DK, wq,
+                                       reinterpret_cast<const TG*>(p.q.g) + tok * DK + lane * NK, p.q_scale, p.eps, dq);
+        comp_dc<TX, TG, TAPS, NK, true>(rows + DK + lane * NK, W, swc[1] + lane * NK, DK, wk,
+                                       reinterpret_cast<const TG*>(p.k.g) + tok * DK + lane * NK, 1.f, p.eps, dk);
+        comp_dc<TX, TG, TAPS, NV, false>(rows + 2 * DK + lane * NV, W, swc[2] + lane * NV, DV, wv,
+                                        reinterpret_cast<const TG*>(p.v.g) + tok * DV + lane * NV, 1.f, p.eps, dv);
+        if (t < t1) {  // conv-weight gradients of this run's tokens
+#pragma unroll
+          for (int j = 0; j < TAPS; ++j) {
+            float xq[NK], xk[NK], xv[NV];
+            load_vec<NK>(rows + j * W + lane * NK, xq);
+            load_vec<NK>(rows + j * W + DK + lane * NK, xk);
+            load_vec<NV>(rows + j * W + 2 * DK + lane * NV, xv);
+#pragma unroll
+            for (int n = 0; n < NK; ++n) {
+              lq.dw[j][n] = fmaf(dq[n], xq[n], lq.dw[j][n]);
+              lk.dw[j][n] = fmaf(dk[n], xk[n], lk.dw[j][n]);
+            }
+#pragma unroll
+            for (int n = 0; n < NV; ++n) lv.dw[j][n] = fmaf(dv[n], xv[n], lv.dw[j][n]);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int n = 0; n < NK; ++n) dq[n] = dk[n] = 0.f;
+#pragma unroll
+        for (int n = 0; n < NV; ++n) dv[n] = 0.f;
+      }
+      lq.push(dq);
+      lk.push(dk);
+      lv.push(dv);
+      const int tau = t - (TAPS - 1);
+      if (tau >= t0) {
+        float oq[NK], ok[NK], ov[NV];
+        dx_of<TAPS, NK>(lq, swc[0] + lane * NK, DK, wq, oq);
+        dx_of<TAPS, NK>(lk, swc[1] + lane * NK, DK, wk, ok);
+        dx_of<TAPS, NV>(lv, swc[2] + lane * NV, DV, wv, ov);
+        stv<TX, NK>(reinterpret_cast<TX*>(p.q.dx) + (int64_t)b * p.q.dsb + (int64_t)tau * p.q.dst + h * DK + lane * NK, oq);
+        stv<TX, NK>(reinterpret_cast<TX*>(p.k.dx) + (int64_t)b * p.k.dsb + (int64_t)tau * p.k.dst + h * DK + lane * NK, ok);
+        stv<TX, NV>(reinterpret_cast<TX*>(p.v.dx) + (int64_t)b * p.v.dsb + (int64_t)tau * p.v.dst + h * DV + lane * NV, ov);
+      }
+    }
+  }
+  // gates, one token per lane; their parameter gradients summed over the warp
+  float s_dt = 0.f, s_al = 0.f, s_bb = 0.f;
+  if (active) {
+    const float dtb = p.dt_bias[h], Ae = expf(p.A_log[h]), bb_h = p.b_bias ? p.b_bias[h] : 0.f;
+    for (int t = t0 + lane; t < t1; t += 32) {
+      const int64_t tok = tokb + (int64_t)t * p.H;
+      const float a = to_f32(reinterpret_cast<const TX*>(p.xa)[(int64_t)b * p.sa_b + (int64_t)t * p.sa_t + h]);
+      const float bb = to_f32(reinterpret_cast<const TX*>(p.xb)[(int64_t)b * p.sb_b + (int64_t)t * p.sb_t + h]);
+      const float z = a + dtb, la = -softplus(z) * Ae, gl = p.dla[tok];
+      const bool live = !(p.clamp && la < p.la_min);
+      const float dz = live ? gl * (-sigm(z) * Ae) : 0.f;
+      s_dt += dz;
+      s_al += live ? gl * la : 0.f;
+      const float sb = sigm(bb + bb_h), dzb = p.dbeta[tok] * p.beta_scale * sb * (1.f - sb);
+      s_bb += dzb;
+      store_as(reinterpret_cast<TX*>(p.dxa) + (int64_t)b * p.dsa_b + (int64_t)t * p.dsa_t + h, dz);
+      store_as(reinterpret_cast<TX*>(p.dxb) + (int64_t)b * p.dsb_b + (int64_t)t * p.dsb_t + h, dzb);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    s_dt += __shfl_xor_sync(0xffffffffu, s_dt, o);
+    s_al += __shfl_xor_sync(0xffffffffu, s_al, o);
+    s_bb += __shfl_xor_sync(0xffffffffu, s_bb, o);
+  }
+  if (lane == 0 && active) {
+    atomicAdd(p.ddt_bias + h, s_dt);
+    atomicAdd(p.dA_log + h, s_al);
+    if (p.db_bias) atomicAdd(p.db_bias + h, s_bb);
+  }
+  // conv-weight gradients: the block's warps (same head) summed in shared memory, one atomic per element
+  if (!(wq || wk || wv)) return;
+  __syncthreads();  // every warp is done with its staged rows
+  float* red = sw + TAPS * W;  // WARPS x TAPS x W floats fit in the staging area
+#pragma unroll
+  for (int j = 0; j < TAPS; ++j) {
+#pragma unroll
+    for (int n = 0; n < NK; ++n) {
+      red[((size_t)wid * TAPS + j) * W + lane * NK + n] = lq.dw[j][n];
+      red[((size_t)wid * TAPS + j) * W + DK + lane * NK + n] = lk.dw[j][n];
+    }
+#pragma unroll
+    for (int n = 0; n < NV; ++n) red[((size_t)wid * TAPS + j) * W + 2 * DK + lane * NV + n] = lv.dw[j][n];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < TAPS * W; i += blockDim.x) {
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < WARPS; ++w) s += red[(size_t)w * TAPS * W + i];
+    const int j = i / W, e = i - j * W;
+    const int c = e < DK ? 0 : (e < 2 * DK ? 1 : 2);
+    const int ch = e - off[c];
+    if (cs[c]->dw) atomicAdd(cs[c]->dw + (int64_t)j * cs[c]->wch + (int64_t)h * len[c] + ch, s);
+  }
+}
+
+// ---- epilogue backward ------------------------------------------------------------------------------
+struct EpiBwdParams {
+  const void* y;
+  gdn_strides sy;
+  const void* g;
+  int64_t sg_b, sg_t;
+  const float* weight;
+  const void* dout;
+  int64_t sdo_b, sdo_t;
+  void* dy;   // [B][T][H][DV] contiguous
+  void* dg;   // [B][T][H*DV] contiguous
+  float* dweight;
+  int B, T, H, DV;
+  float eps;
+};
+
+template <typename TY, typename TG, typename TD, int NPL>
+__global__ void __launch_bounds__(128) epilogue_bwd_kernel(const EpiBwdParams p) {
+  const int lane = threadIdx.x & 31;
+  const unsigned rows = (unsigned)p.B * (unsigned)p.T * (unsigned)p.H;
+  const int c0 = lane * NPL;
+  float w[NPL], dw[NPL];
+  load_vec<NPL>(p.weight + c0, w);
+#pragma unroll
+  for (int n = 0; n < NPL; ++n) dw[n] = 0.f;
+  const unsigned warps = gridDim.x * (blockDim.x >> 5);
+  for (unsigned row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < rows; row += warps) {
+    const unsigned bt = row / (unsigned)p.H;
+    const int h = (int)(row - bt * (unsigned)p.H);
+    const int b = (int)(bt / (unsigned)p.T), t = (int)(bt - (unsigned)b * (unsigned)p.T);
+    float y[NPL], d[NPL], g[NPL], s[NPL];
+    load_vec<NPL>(reinterpret_cast<const TY*>(p.y) + b * p.sy.b + t * p.sy.t + h * p.sy.h + c0, y);
+    load_vec<NPL>(reinterpret_cast<const TD*>(p.dout) + b * p.sdo_b + t * p.sdo_t + (int64_t)h * p.DV + c0, d);
+    if (p.g) {
+      load_vec<NPL>(reinterpret_cast<const TG*>(p.g) + b * p.sg_b + t * p.sg_t + (int64_t)h * p.DV + c0, g);
+#pragma unroll
+      for (int n = 0; n < NPL; ++n) s[n] = g[n] * sigm(g[n]);
+    } else {
+#pragma unroll
+      for (int n = 0; n < NPL; ++n) s[n] = 1.f;
+    }
+    float ss = 0.f, yz = 0.f, z[NPL];
+#pragma unroll
+    for (int n = 0; n < NPL; ++n) {
+      z[n] = w[n] * s[n] * d[n];
+      ss = fmaf(y[n], y[n], ss);
+      yz = fmaf(y[n], z[n], yz);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      yz += __shfl_xor_sync(0xffffffffu, yz, o);
+    }
+    const float r = rsqrtf(ss / (float)p.DV + p.eps), k3 = r * r * r * yz / (float)p.DV;
+    float oy[NPL], og[NPL];
+#pragma unroll
+    for (int n = 0; n < NPL; ++n) {
+      oy[n] = r * z[n] - y[n] * k3;
+      dw[n] = fmaf(d[n] * y[n] * r, s[n], dw[n]);
+      og[n] = p.g ? d[n] * y[n] * r * w[n] * dsilu(g[n]) : 0.f;
+    }
+    const int64_t tok = ((int64_t)b * p.T + t) * p.H + h;
+    stv<TY, NPL>(reinterpret_cast<TY*>(p.dy) + tok * p.DV + c0, oy);
+    if (p.g) stv<TG, NPL>(reinterpret_cast<TG*>(p.dg) + tok * p.DV + c0, og);
+  }
+  __shared__ float red[4][512];
+  const int wid = threadIdx.x >> 5;
+#pragma unroll
+  for (int n = 0; n < NPL; ++n) red[wid][c0 + n] = dw[n];
+  __syncthreads();
+  for (int i = threadIdx.x; i < p.DV; i += blockDim.x)
+    atomicAdd(p.dweight + i, (red[0][i] + red[1][i]) + (red[2][i] + red[3][i]));
+}
+
+bool a16(const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; }
+
+bool device_ok() {
+  int dev = 0, major = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return false;
+  return major == 10;
+}
+
+template <typename TX, typename TG, int NK, int NV, int TAPS>
+int launch_pro(const ProBwdParams& p, cudaStream_t s) {
+  constexpr int W = 2 * 32 * NK + 32 * NV;
+  const size_t stage = (size_t)WARPS * (RUN + 2 * (TAPS - 1)) * W * sizeof(TX);
+  const size_t red = (size_t)WARPS * TAPS * W * sizeof(float);
+  const size_t sm = (size_t)TAPS * W * 4 + (stage > red ? stage : red);
+  if (sm > 200 * 1024) return GDN_ERR_UNSUPPORTED;
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(prologue_bwd_kernel<TX, TG, NK, NV, TAPS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             200 * 1024) != cudaSuccess)
+      return GDN_ERR_LAUNCH;
+    attr = true;
+  }
+  const int64_t runs = (p.T + RUN - 1) / RUN;
+  const int64_t blocks = (int64_t)p.B * p.H * ((runs + WARPS - 1) / WARPS);
+  if (blocks > 0x7fffffff) return GDN_ERR_SHAPE;
+  prologue_bwd_kernel<TX, TG, NK, NV, TAPS><<<(unsigned)blocks, 32 * WARPS, sm, s>>>(p);
+  return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+}
+
+template <typename TX, typename TG, int NK, int NV>
+int launch_pro_taps(const ProBwdParams& p, int taps, cudaStream_t s) {
+  switch (taps) {
+    case 1: return launch_pro<TX, TG, NK, NV, 1>(p, s);
+    case 2: return launch_pro<TX, TG, NK, NV, 2>(p, s);
+    case 3: return launch_pro<TX, TG, NK, NV, 3>(p, s);
+    case 4: return launch_pro<TX, TG, NK, NV, 4>(p, s);
+    default: return GDN_ERR_SHAPE;
+  }
+}
+
+template <typename TX, typename TG>
+int launch_pro_dims(const ProBwdParams& p, int taps, cudaStream_t s) {
+  const int nk = p.DK / 32, nv = p.DV / 32;
+  if (nk == 4 && nv == 4) return launch_pro_taps<TX, TG, 4, 4>(p, taps, s);
+  if (nk == 4 && nv == 8) return launch_pro_taps<TX, TG, 4, 8>(p, taps, s);
+  if (nk == 2 && nv == 2) return launch_pro_taps<TX, TG, 2, 2>(p, taps, s);
+  if (nk == 2 && nv == 4) return launch_pro_taps<TX, TG, 2, 4>(p, taps, s);
+  return GDN_ERR_UNSUPPORTED;
+}
+
+template <typename TY, typename TG, typename TD>
+int launch_epi(const EpiBwdParams& p, cudaStream_t s) {
+  int sms = 148, dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t rows = (int64_t)p.B * p.T * p.H;
+  int64_t blocks = (rows + 3) / 4;
+  if (blocks > (int64_t)sms * 16) blocks = (int64_t)sms * 16;
+  switch (p.DV / 32) {
+    case 2: epilogue_bwd_kernel<TY, TG, TD, 2><<<(unsigned)blocks, 128, 0, s>>>(p); break;
+    case 4: epilogue_bwd_kernel<TY, TG, TD, 4><<<(unsigned)blocks, 128, 0, s>>>(p); break;
+    case 8: epilogue_bwd_kernel<TY, TG, TD, 8><<<(unsigned)blocks, 128, 0, s>>>(p); break;
+    case 16: epilogue_bwd_kernel<TY, TG, TD, 16><<<(unsigned)blocks, 128, 0, s>>>(p); break;
+    default: return GDN_ERR_UNSUPPORTED;
+  }
+  return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+}
+
+}  // namespace layer_io_bwd
+}  // namespace gdn
+
+using namespace gdn::layer_io_bwd;
+
+extern "C" {
+
+int gdn_layer_prologue_bwd(const gdn_prologue_bwd_args* a, void* stream) {
+  if (!a) return GDN_ERR_NULL;
+  if (!a->xq || !a->xk || !a->xv || !a->xa || !a->xb || !a->A_log || !a->dt_bias || !a->dq || !a->dk || !a->dv ||
+      !a->dla || !a->dbeta || !a->dxq || !a->dxk || !a->dxv || !a->dxa || !a->dxb || !a->dA_log || !a->ddt_bias)
+    return GDN_ERR_NULL;
+  if (a->B < 1 || a->T < 1 || a->H < 1 || a->B * a->T * a->H > (int64_t)1 << 31) return GDN_ERR_SHAPE;
+  if (a->conv_size < 1 || a->conv_size > MAX_TAPS) return GDN_ERR_SHAPE;
+  if ((a->wq != nullptr) != (a->dwq != nullptr) || (a->wk != nullptr) != (a->dwk != nullptr) ||
+      (a->wv != nullptr) != (a->dwv != nullptr))
+    return GDN_ERR_NULL;
+  if (a->in_dtype != GDN_DTYPE_BF16 && a->in_dtype != GDN_DTYPE_F32) return GDN_ERR_DTYPE;
+  if (a->grad_dtype != GDN_DTYPE_BF16 && a->grad_dtype != GDN_DTYPE_F32) return GDN_ERR_DTYPE;
+  const int64_t es = a->in_dtype == GDN_DTYPE_BF16 ? 2 : 4;
+  const int64_t sts[] = {a->sxq_b, a->sxq_t, a->sxk_b, a->sxk_t, a->sxv_b, a->sxv_t};
+  for (int64_t st : sts)
+    if ((st * es) % 16) return GDN_ERR_ALIGN;
+  if (!a16(a->xq) || !a16(a->xk) || !a16(a->xv) || !a16(a->dq) || !a16(a->dk) || !a16(a->dv)) return GDN_ERR_ALIGN;
+  if (!device_ok()) return GDN_ERR_DEVICE;
+  ProBwdParams p;
+  memset(&p, 0, sizeof(p));
+  p.q = {a->xq, a->sxq_b, a->sxq_t, a->wq, a->H * a->DK, a->dq, a->dxq, a->sdxq_b, a->sdxq_t, a->dwq};
+  p.k = {a->xk, a->sxk_b, a->sxk_t, a->wk, a->H * a->DK, a->dk, a->dxk, a->sdxk_b, a->sdxk_t, a->dwk};
+  p.v = {a->xv, a->sxv_b, a->sxv_t, a->wv, a->H * a->DV, a->dv, a->dxv, a->sdxv_b, a->sdxv_t, a->dwv};
+  p.xa = a->xa; p.xb = a->xb;
+  p.sa_b = a->sxa_b; p.sa_t = a->sxa_t; p.sb_b = a->sxb_b; p.sb_t = a->sxb_t;
+  p.dxa = a->dxa; p.dxb = a->dxb;
+  p.dsa_b = a->sdxa_b; p.dsa_t = a->sdxa_t; p.dsb_b = a->sdxb_b; p.dsb_t = a->sdxb_t;
+  p.dla = a->dla; p.dbeta = a->dbeta;
+  p.A_log = a->A_log; p.dt_bias = a->dt_bias; p.b_bias = a->b_bias;
+  p.dA_log = a->dA_log; p.ddt_bias = a->ddt_bias; p.db_bias = a->db_bias;
+  p.B = (int)a->B; p.T = (int)a->T; p.H = (int)a->H; p.DK = (int)a->DK; p.DV = (int)a->DV;
+  p.clamp = (a->flags & GDN_PROLOGUE_CLAMP_LA) != 0;
+  p.q_scale = a->q_scale; p.eps = a->l2_eps; p.la_min = a->la_min; p.beta_scale = a->beta_scale;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // parameter gradients accumulate atomically: start from zero
+  const size_t tb = (size_t)a->conv_size * 4;
+  if ((a->dwq && cudaMemsetAsync(a->dwq, 0, tb * a->H * a->DK, s) != cudaSuccess) ||
+      (a->dwk && cudaMemsetAsync(a->dwk, 0, tb * a->H * a->DK, s) != cudaSuccess) ||
+      (a->dwv && cudaMemsetAsync(a->dwv, 0, tb * a->H * a->DV, s) != cudaSuccess) ||
+      cudaMemsetAsync(a->dA_log, 0, a->H * 4, s) != cudaSuccess || cudaMemsetAsync(a->ddt_bias, 0, a->H * 4, s) != cudaSuccess ||
+      (a->db_bias && cudaMemsetAsync(a->db_bias, 0, a->H * 4, s) != cudaSuccess))
+    return GDN_ERR_LAUNCH;
+  using bf = __nv_bfloat16;
+  const bool xb = a->in_dtype == GDN_DTYPE_BF16, gb = a->grad_dtype == GDN_DTYPE_BF16;
+  if (xb && gb) return launch_pro_dims<bf, bf>(p, a->conv_size, s);
+  if (xb) return launch_pro_dims<bf, float>(p, a->conv_size, s);
+  if (gb) return launch_pro_dims<float, bf>(p, a->conv_size, s);
+  return launch_pro_dims<float, float>(p, a->conv_size, s);
+}
+
+int gdn_layer_epilogue_bwd(const gdn_epilogue_bwd_args* a, void* stream) {
+  if (!a) return GDN_ERR_NULL;
+  if (!a->y || !a->weight || !a->dout || !a->dy || !a->dweight || (a->g && !a->dg)) return GDN_ERR_NULL;
+  if (a->B < 1 || a->T < 1 || a->H < 1 || (a->DV != 64 && a->DV != 128 && a->DV != 256 && a->DV != 512)) return GDN_ERR_SHAPE;
+  if (a->B * a->T * a->H * 32 > 0x7fffffffLL) return GDN_ERR_SHAPE;
+  for (int32_t dt : {a->y_dtype, a->g_dtype, a->do_dtype})
+    if (dt != GDN_DTYPE_BF16 && dt != GDN_DTYPE_F32) return GDN_ERR_DTYPE;
+  if (!a16(a->y) || (a->g && !a16(a->g)) || !a16(a->dout)) return GDN_ERR_ALIGN;
+  if (!device_ok()) return GDN_ERR_DEVICE;
+  EpiBwdParams p;
+  p.y = a->y; p.sy = a->sy; p.g = a->g; p.sg_b = a->sg_b; p.sg_t = a->sg_t; p.weight = a->weight;
+  p.dout = a->dout; p.sdo_b = a->sdo_b; p.sdo_t = a->sdo_t; p.dy = a->dy; p.dg = a->dg; p.dweight = a->dweight;
+  p.B = (int)a->B; p.T = (int)a->T; p.H = (int)a->H; p.DV = (int)a->DV; p.eps = a->eps;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(a->dweight, 0, a->DV * 4, s) != cudaSuccess) return GDN_ERR_LAUNCH;
+  using bf = __nv_bfloat16;
+  const int key = a->y_dtype * 4 + a->g_dtype * 2 + a->do_dtype;  // F32 = 0, BF16 = 1
+  switch (key) {
+    case 7: return launch_epi<bf, bf, bf>(p, s);
+    case 6: return launch_epi<bf, bf, float>(p, s);
+    case 3: return launch_epi<float, bf, bf>(p, s);
+    case 2: return launch_epi<float, bf, float>(p, s);
+    case 5: return launch_epi<bf, float, bf>(p, s);
+    case 4: return launch_epi<bf, float, float>(p, s);
+    case 1: return launch_epi<float, float, bf>(p, s);
+    default: return launch_epi<float, float, float>(p, s);
+  }
+}
+
+}  // extern "C"

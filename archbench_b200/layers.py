@@ -13,9 +13,10 @@ the updated state in it.  The projections are PyTorch GEMMs; the short convoluti
 norms and the gates run as one CUDA kernel (``ops.layer_prologue``), the token mixing is
 ``ops.gdn_prefill`` / ``ops.gdn_decode_step``, and the output norm and gate one more kernel
 (``ops.layer_epilogue``).  ``fused_io = False`` on a module (or a configuration the kernels do
-not serve: N-step write vectors, conv bias, odd head sizes) keeps those parts in PyTorch, and so
-does every call that builds an autograd graph (training): there the scan runs forward and
-backward on the CUDA kernels (DK = 128, DV a multiple of 128) and the rest through PyTorch autograd.  There is no
+not serve: N-step write vectors, conv bias, odd head sizes) keeps those parts in PyTorch.  Calls that
+build an autograd graph (training) run the prologue, scan and epilogue forward and backward on the
+CUDA kernels (DK = 128; DV = DK or 2 DK for the fused prologue/epilogue, a multiple of 128 for the
+scan); without a backward kernel for a configuration, those parts run in PyTorch.  There is no
 CPU path.
 """
 
@@ -81,10 +82,17 @@ def _fused_ok(DK: int, DV: int) -> bool:
 
 
 def _training(x: torch.Tensor, m: nn.Module) -> bool:
-    """True when this call builds an autograd graph.  The fused prologue/epilogue kernels have no
-    backward, so such calls run those parts in PyTorch; the scan's backward is the CUDA one
-    (``ops.gdn_prefill`` is differentiable)."""
+    """True when this call builds an autograd graph (the scan, ``ops.gdn_prefill``, is always
+    differentiable; the fused prologue/epilogue use their differentiable variants)."""
     return torch.is_grad_enabled() and (x.requires_grad or any(p.requires_grad for p in m.parameters()))
+
+
+def _fused_allowed(x: torch.Tensor, m: nn.Module, cache, DK: int, DV: int, conv_size: int) -> bool:
+    """The fused prologue/epilogue serve this call: always without autograd; with autograd (training)
+    when their backward kernels serve the head sizes and no decode cache is carried."""
+    if not _training(x, m):
+        return True
+    return cache is None and ops.layer_io_trainable(DK, DV, conv_size)
 
 
 def _mix(q, k, v, la, beta, u, cache: Optional[GDNCache], impl: str):
@@ -149,17 +157,24 @@ class NStepGDN(nn.Module):
             if st is not None:
                 state = (st[:, :qd], st[:, qd:2 * qd], st[:, 2 * qd:])
         dt = torch.bfloat16 if (DK == 128 and self._impl != "recurrent") else torch.float32
-        q, k, v, la, beta, new_state = ops.layer_prologue(
-            proj[..., :qd], proj[..., qd:2 * qd], proj[..., 2 * qd:n_qkv], proj[..., ab0:ab0 + H], proj[..., ab0 + H:ab0 + 2 * H],
-            self.A_log, self.dt_bias, H=H, DK=DK, DV=DV, b_bias=self.b_bias, conv=conv, conv_state=state,
-            want_state=cache is not None, q_scale=DK**-0.5, la_min=self.la_min, out_dtype=dt)
+        parts = (proj[..., :qd], proj[..., qd:2 * qd], proj[..., 2 * qd:n_qkv], proj[..., ab0:ab0 + H], proj[..., ab0 + H:ab0 + 2 * H])
+        train = _training(x, self)
+        if train:
+            q, k, v, la, beta = ops.layer_prologue_train(*parts, self.A_log, self.dt_bias, H=H, DK=DK, DV=DV, b_bias=self.b_bias,
+                                                         conv=conv, q_scale=DK**-0.5, la_min=self.la_min, out_dtype=dt)
+            new_state = None
+        else:
+            q, k, v, la, beta, new_state = ops.layer_prologue(
+                *parts, self.A_log, self.dt_bias, H=H, DK=DK, DV=DV, b_bias=self.b_bias, conv=conv, conv_state=state,
+                want_state=cache is not None, q_scale=DK**-0.5, la_min=self.la_min, out_dtype=dt)
         if cache is not None and new_state is not None:
             cache.conv["qkv"] = torch.cat(new_state, 1)
         y = _mix(q, k, v, la, beta, None, cache, self._impl)
         if cache is not None:
             cache.seen += T
         g = proj[..., n_qkv:n_qkv + self.n_gate] if self.use_gate else None
-        o = ops.layer_epilogue(y, self.norm.weight, g, eps=self.norm.eps, out_dtype=x.dtype)
+        epi = ops.layer_epilogue_train if train else ops.layer_epilogue
+        o = epi(y, self.norm.weight, g, eps=self.norm.eps, out_dtype=x.dtype)
         return self.o_proj(o)
 
     def forward(self, x: torch.Tensor, cache: Optional[GDNCache] = None) -> torch.Tensor:
@@ -168,7 +183,8 @@ class NStepGDN(nn.Module):
         n_qkv = 2 * self.qk_dim + self.v_dim
         proj = self.in_proj(x)
         if (self.fused_io and self.n_steps == 1 and _fused_ok(DK, DV) and proj.dtype in (torch.bfloat16, torch.float32)
-                and (self.conv is None or (self.conv.bias is None and self.conv.size <= 4)) and not _training(x, self)):
+                and (self.conv is None or (self.conv.bias is None and self.conv.size <= 4))
+                and _fused_allowed(x, self, cache, DK, DV, self.conv.size if self.conv is not None else 1)):
             return self._forward_fused(x, proj, cache)
         qkv, g, ab = proj[..., :n_qkv], proj[..., n_qkv:n_qkv + self.n_gate], proj[..., n_qkv + self.n_gate:n_qkv + self.n_gate + 2 * H]
         if self.conv is not None:
@@ -276,17 +292,25 @@ class GatedDeltaNet(nn.Module):
                 state = (cache.conv["q"], cache.conv["k"], cache.conv["v"])
         xq, xk, xv, xa, xb = self.q_proj(x), self.k_proj(x), self.v_proj(x), self.a_proj(x), self.b_proj(x)
         dt = torch.bfloat16 if DK == 128 else torch.float32
-        q, k, v, la, beta, new_state = ops.layer_prologue(
-            xq, xk, xv, xa.to(xq.dtype), xb.to(xq.dtype), self.A_log, self.dt_bias, H=H, DK=DK, DV=DV, conv=conv,
-            conv_state=state, want_state=cache is not None, q_scale=DK**-0.5, l2_eps=1e-6,
-            beta_scale=2.0 if self.allow_neg_eigval else 1.0, out_dtype=dt)
+        train = _training(x, self)
+        if train:
+            q, k, v, la, beta = ops.layer_prologue_train(
+                xq, xk, xv, xa.to(xq.dtype), xb.to(xq.dtype), self.A_log, self.dt_bias, H=H, DK=DK, DV=DV, conv=conv,
+                q_scale=DK**-0.5, l2_eps=1e-6, beta_scale=2.0 if self.allow_neg_eigval else 1.0, out_dtype=dt)
+            new_state = None
+        else:
+            q, k, v, la, beta, new_state = ops.layer_prologue(
+                xq, xk, xv, xa.to(xq.dtype), xb.to(xq.dtype), self.A_log, self.dt_bias, H=H, DK=DK, DV=DV, conv=conv,
+                conv_state=state, want_state=cache is not None, q_scale=DK**-0.5, l2_eps=1e-6,
+                beta_scale=2.0 if self.allow_neg_eigval else 1.0, out_dtype=dt)
         if cache is not None and new_state is not None:
             cache.conv.update(q=new_state[0], k=new_state[1], v=new_state[2])
         o = _mix(q, k, v, la, beta, None, cache, "auto")
         if cache is not None:
             cache.seen += T
         g = self.g_proj(x) if self.use_gate else None
-        o = ops.layer_epilogue(o, self.o_norm.weight, g, eps=self.o_norm.eps, out_dtype=x.dtype)
+        epi = ops.layer_epilogue_train if train else ops.layer_epilogue
+        o = epi(o, self.o_norm.weight, g, eps=self.o_norm.eps, out_dtype=x.dtype)
         return self.o_proj(o)
 
     def forward(self, hidden_states: torch.Tensor, cache: Optional[GDNCache] = None, **kwargs) -> torch.Tensor:
@@ -294,7 +318,8 @@ class GatedDeltaNet(nn.Module):
         B, T, _ = x.shape
         want = cache is not None
         if (self.fused_io and _fused_ok(self.head_k_dim, self.head_v_dim) and not self.conv_bias and self.conv_size <= 4
-                and self.q_proj.weight.dtype in (torch.bfloat16, torch.float32) and not _training(x, self)):
+                and self.q_proj.weight.dtype in (torch.bfloat16, torch.float32)
+                and _fused_allowed(x, self, cache, self.head_k_dim, self.head_v_dim, self.conv_size if self.use_short_conv else 1)):
             return self._forward_fused(x, cache)
         if self.use_short_conv:
             q, sq = self.q_conv1d(self.q_proj(x), None if cache is None else cache.conv.get("q"), want)

@@ -105,6 +105,34 @@ class BackwardArgs(ctypes.Structure):
                 ("workspace_bytes", ctypes.c_uint64)]
 
 
+class PrologueBwdArgs(ctypes.Structure):
+    """Mirror of gdn_prologue_bwd_args (include/gdn_b200.h)."""
+
+    _fields_ = [(n, ctypes.c_void_p) for n in ("xq", "xk", "xv")] + \
+               [(n, ctypes.c_int64) for n in ("sxq_b", "sxq_t", "sxk_b", "sxk_t", "sxv_b", "sxv_t")] + \
+               [(n, ctypes.c_void_p) for n in ("xa", "xb")] + \
+               [(n, ctypes.c_int64) for n in ("sxa_b", "sxa_t", "sxb_b", "sxb_t")] + \
+               [(n, ctypes.c_void_p) for n in ("wq", "wk", "wv", "A_log", "dt_bias", "b_bias", "dq", "dk", "dv", "dla", "dbeta",
+                                                 "dxq", "dxk", "dxv")] + \
+               [(n, ctypes.c_int64) for n in ("sdxq_b", "sdxq_t", "sdxk_b", "sdxk_t", "sdxv_b", "sdxv_t")] + \
+               [(n, ctypes.c_void_p) for n in ("dxa", "dxb")] + \
+               [(n, ctypes.c_int64) for n in ("sdxa_b", "sdxa_t", "sdxb_b", "sdxb_t")] + \
+               [(n, ctypes.c_void_p) for n in ("dwq", "dwk", "dwv", "dA_log", "ddt_bias", "db_bias")] + \
+               [(n, ctypes.c_int64) for n in ("B", "T", "H", "DK", "DV")] + \
+               [(n, ctypes.c_int32) for n in ("conv_size", "flags", "in_dtype", "grad_dtype")] + \
+               [(n, ctypes.c_float) for n in ("q_scale", "l2_eps", "la_min", "beta_scale")]
+
+
+class EpilogueBwdArgs(ctypes.Structure):
+    """Mirror of gdn_epilogue_bwd_args (include/gdn_b200.h)."""
+
+    _fields_ = [("y", ctypes.c_void_p), ("sy", Strides), ("g", ctypes.c_void_p), ("sg_b", ctypes.c_int64),
+                ("sg_t", ctypes.c_int64), ("weight", ctypes.c_void_p), ("dout", ctypes.c_void_p), ("sdo_b", ctypes.c_int64),
+                ("sdo_t", ctypes.c_int64), ("dy", ctypes.c_void_p), ("dg", ctypes.c_void_p), ("dweight", ctypes.c_void_p)] + \
+               [(n, ctypes.c_int64) for n in ("B", "T", "H", "DV")] + \
+               [(n, ctypes.c_int32) for n in ("y_dtype", "g_dtype", "do_dtype")] + [("eps", ctypes.c_float)]
+
+
 GDN_PROLOGUE_CLAMP_LA = 1
 
 # Every symbol include/gdn_b200.h declares, with its ctypes signature.
@@ -122,6 +150,8 @@ SYMBOLS = {
     "gdn_layer_epilogue": ([ctypes.POINTER(EpilogueArgs), ctypes.c_void_p], ctypes.c_int),
     "gdn_prefill_bwd_workspace_bytes": ([ctypes.POINTER(BackwardArgs), ctypes.POINTER(ctypes.c_size_t)], ctypes.c_int),
     "gdn_prefill_bwd": ([ctypes.POINTER(BackwardArgs), ctypes.c_void_p], ctypes.c_int),
+    "gdn_layer_prologue_bwd": ([ctypes.POINTER(PrologueBwdArgs), ctypes.c_void_p], ctypes.c_int),
+    "gdn_layer_epilogue_bwd": ([ctypes.POINTER(EpilogueBwdArgs), ctypes.c_void_p], ctypes.c_int),
 }
 
 _LIB = None
@@ -571,3 +601,138 @@ def layer_epilogue(y, weight, g=None, eps=1e-5, out_dtype=torch.bfloat16):
                      _DTC[g.dtype] if g is not None else GDN_DTYPE_F32, _DTC[out_dtype], float(eps))
     _check(load_library().gdn_layer_epilogue(ctypes.byref(a), ctypes.c_void_p(torch.cuda.current_stream(y.device).cuda_stream)))
     return o
+
+
+# ------------------------------------------------------------------------------------------------
+# Differentiable prologue / epilogue (training through the fused kernels)
+# ------------------------------------------------------------------------------------------------
+
+
+def layer_io_trainable(DK: int, DV: int, conv_size: int) -> bool:
+    """Head sizes and conv widths the prologue/epilogue backward kernels serve."""
+    return DK in (64, 128) and DV in (DK, 2 * DK) and 1 <= conv_size <= 4
+
+
+@torch.library.custom_op("archbench_b200::layer_prologue_train", mutates_args=())
+def _prologue_train_op(
+    xq: torch.Tensor, xk: torch.Tensor, xv: torch.Tensor, xa: torch.Tensor, xb: torch.Tensor,
+    wq: Optional[torch.Tensor], wk: Optional[torch.Tensor], wv: Optional[torch.Tensor],
+    A_log: torch.Tensor, dt_bias: torch.Tensor, b_bias: Optional[torch.Tensor], H: int, DK: int, DV: int,
+    q_scale: float, l2_eps: float, la_min: Optional[float], beta_scale: float, out_dtype_code: int,
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    conv = None if wq is None else tuple(w.t() for w in (wq, wk, wv))  # tap-major -> (channels, taps)
+    q, k, v, la, beta, _ = layer_prologue(xq, xk, xv, xa, xb, A_log, dt_bias, H=H, DK=DK, DV=DV, b_bias=b_bias, conv=conv,
+                                          q_scale=q_scale, l2_eps=l2_eps, la_min=la_min, beta_scale=beta_scale,
+                                          out_dtype=_DTYPE_CODE[out_dtype_code])
+    return q, k, v, la, beta
+
+
+@_prologue_train_op.register_fake
+def _(xq, xk, xv, xa, xb, wq, wk, wv, A_log, dt_bias, b_bias, H, DK, DV, q_scale, l2_eps, la_min, beta_scale, out_dtype_code):
+    B, T = xq.shape[:2]
+    od = _DTYPE_CODE[out_dtype_code]
+    e = lambda *sh, dt=od: xq.new_empty(*sh, dtype=dt)
+    return e(B, T, H, DK), e(B, T, H, DK), e(B, T, H, DV), e(B, T, H, dt=torch.float32), e(B, T, H, dt=torch.float32)
+
+
+def _prologue_train_setup(ctx, inputs, output):
+    xq, xk, xv, xa, xb, wq, wk, wv, A_log, dt_bias, b_bias, H, DK, DV, q_scale, l2_eps, la_min, beta_scale, _ = inputs
+    ctx.save_for_backward(xq, xk, xv, xa, xb, wq, wk, wv, A_log, dt_bias, b_bias)
+    ctx.cfg = (H, DK, DV, q_scale, l2_eps, la_min, beta_scale)
+
+
+def _prologue_train_backward(ctx, dq, dk, dv, dla, dbeta):
+    """The prologue's backward kernel (gdn_layer_prologue_bwd): projection, gate, conv-weight and
+    A_log / dt_bias / b_bias gradients in one pass."""
+    xq, xk, xv, xa, xb, wq, wk, wv, A_log, dt_bias, b_bias = ctx.saved_tensors
+    H, DK, DV, q_scale, l2_eps, la_min, beta_scale = ctx.cfg
+    B, T, _ = xq.shape
+    dev, dt = xq.device, xq.dtype
+    gd = dq.dtype if dq is not None else torch.float32
+    dq = torch.zeros(B, T, H, DK, device=dev, dtype=gd) if dq is None else dq.contiguous()
+    dk = torch.zeros(B, T, H, DK, device=dev, dtype=gd) if dk is None else dk.to(gd).contiguous()
+    dv = torch.zeros(B, T, H, DV, device=dev, dtype=gd) if dv is None else dv.to(gd).contiguous()
+    dla = torch.zeros(B, T, H, device=dev) if dla is None else dla.float().contiguous()
+    dbeta = torch.zeros(B, T, H, device=dev) if dbeta is None else dbeta.float().contiguous()
+    xq, xk, xv = _rows16(xq), _rows16(xk), _rows16(xv)
+    dxq, dxk = torch.empty(B, T, H * DK, device=dev, dtype=dt), torch.empty(B, T, H * DK, device=dev, dtype=dt)
+    dxv = torch.empty(B, T, H * DV, device=dev, dtype=dt)
+    dxa, dxb = torch.empty(B, T, H, device=dev, dtype=dt), torch.empty(B, T, H, device=dev, dtype=dt)
+    taps = 1 if wq is None else wq.shape[0]
+    dws = [None, None, None] if wq is None else [torch.empty_like(w) for w in (wq, wk, wv)]
+    dA, ddt = torch.empty(H, device=dev), torch.empty(H, device=dev)
+    dbb = None if b_bias is None else torch.empty(H, device=dev)
+    A32, dt32 = A_log.float().contiguous(), dt_bias.float().contiguous()
+    bb32 = None if b_bias is None else b_bias.float().contiguous()
+    ws = [None, None, None] if wq is None else [w.contiguous() for w in (wq, wk, wv)]
+    a = PrologueBwdArgs(
+        _ptr(xq), _ptr(xk), _ptr(xv), xq.stride(0), xq.stride(1), xk.stride(0), xk.stride(1), xv.stride(0), xv.stride(1),
+        _ptr(xa), _ptr(xb), xa.stride(0), xa.stride(1), xb.stride(0), xb.stride(1),
+        *[_ptr(w) for w in ws], _ptr(A32), _ptr(dt32), _ptr(bb32), _ptr(dq), _ptr(dk), _ptr(dv), _ptr(dla), _ptr(dbeta),
+        _ptr(dxq), _ptr(dxk), _ptr(dxv), dxq.stride(0), dxq.stride(1), dxk.stride(0), dxk.stride(1), dxv.stride(0), dxv.stride(1),
+        _ptr(dxa), _ptr(dxb), dxa.stride(0), dxa.stride(1), dxb.stride(0), dxb.stride(1),
+        *[_ptr(w) for w in dws], _ptr(dA), _ptr(ddt), _ptr(dbb),
+        B, T, H, DK, DV, taps, GDN_PROLOGUE_CLAMP_LA if la_min is not None else 0, _DTC[dt], _DTC[gd],
+        float(q_scale), float(l2_eps), float(la_min if la_min is not None else 0.0), float(beta_scale))
+    _check(load_library().gdn_layer_prologue_bwd(ctypes.byref(a), ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)))
+    return (dxq, dxk, dxv, dxa, dxb, dws[0], dws[1], dws[2], dA.to(A_log.dtype), ddt.to(dt_bias.dtype),
+            None if dbb is None else dbb.to(b_bias.dtype), None, None, None, None, None, None, None, None)
+
+
+_prologue_train_op.register_autograd(_prologue_train_backward, setup_context=_prologue_train_setup)
+
+
+@torch.library.custom_op("archbench_b200::layer_epilogue_train", mutates_args=())
+def _epilogue_train_op(y: torch.Tensor, weight: torch.Tensor, g: Optional[torch.Tensor], eps: float, out_dtype_code: int) -> torch.Tensor:
+    return layer_epilogue(y, weight, g, eps=eps, out_dtype=_DTYPE_CODE[out_dtype_code])
+
+
+@_epilogue_train_op.register_fake
+def _(y, weight, g, eps, out_dtype_code):
+    B, T, H, DV = y.shape
+    return y.new_empty(B, T, H * DV, dtype=_DTYPE_CODE[out_dtype_code])
+
+
+def _epilogue_train_setup(ctx, inputs, output):
+    y, weight, g, eps, _ = inputs
+    ctx.save_for_backward(y, weight, g)
+    ctx.eps = eps
+
+
+def _epilogue_train_backward(ctx, do):
+    """The epilogue's backward kernel (gdn_layer_epilogue_bwd): dy, dg and the norm weight's gradient."""
+    y, weight, g = ctx.saved_tensors
+    B, T, H, DV = y.shape
+    yv = _prep_token(y, "y", y.dtype)
+    gv = None if g is None else _rows16(g.reshape(B, T, H * DV))
+    do = _rows16(do.reshape(B, T, H * DV))
+    if do.dtype not in _DTC:
+        do = do.float()
+    dy = torch.empty(B, T, H, DV, device=y.device, dtype=y.dtype)
+    dg = None if g is None else torch.empty(B, T, H * DV, device=y.device, dtype=gv.dtype)
+    dw = torch.empty(DV, device=y.device)
+    w = weight.float().contiguous()
+    a = EpilogueBwdArgs(_ptr(yv), _tok_strides(yv), _ptr(gv), 0 if gv is None else gv.stride(0), 0 if gv is None else gv.stride(1),
+                        _ptr(w), _ptr(do), do.stride(0), do.stride(1), _ptr(dy), _ptr(dg), _ptr(dw), B, T, H, DV,
+                        _DTC[y.dtype], _DTC[gv.dtype] if gv is not None else GDN_DTYPE_F32, _DTC[do.dtype], float(ctx.eps))
+    _check(load_library().gdn_layer_epilogue_bwd(ctypes.byref(a), ctypes.c_void_p(torch.cuda.current_stream(y.device).cuda_stream)))
+    return dy, dw.to(weight.dtype), (None if g is None else dg.reshape(g.shape)), None, None
+
+
+_epilogue_train_op.register_autograd(_epilogue_train_backward, setup_context=_epilogue_train_setup)
+
+
+def layer_prologue_train(xq, xk, xv, xa, xb, A_log, dt_bias, *, H, DK, DV, b_bias=None, conv=None, q_scale=1.0,
+                         l2_eps=1e-12, la_min=None, beta_scale=1.0, out_dtype=torch.bfloat16):
+    """``layer_prologue`` without conv state, differentiable: its backward is one CUDA kernel.  ``conv`` =
+    (wq, wk, wv) of shape (channels, conv_size) (or the layer's (channels, 1, conv_size)), or None."""
+    ws = (None, None, None)
+    if conv is not None:
+        ws = tuple(w.reshape(w.shape[0], w.shape[-1]).float().t().contiguous() for w in conv)  # tap-major fp32
+    return _prologue_train_op(xq, xk, xv, xa, xb, *ws, A_log, dt_bias, b_bias, H, DK, DV, float(q_scale), float(l2_eps),
+                              None if la_min is None else float(la_min), float(beta_scale), _DTC[out_dtype])
+
+
+def layer_epilogue_train(y, weight, g=None, eps=1e-5, out_dtype=torch.bfloat16):
+    """``layer_epilogue``, differentiable: its backward is one CUDA kernel."""
+    return _epilogue_train_op(y, weight, g, float(eps), _DTC[out_dtype])

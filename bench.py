@@ -370,7 +370,7 @@ def bench_layer(args, rank, world):
     tok = c.B * c.T
     return {"config": "nsgdn layer, B8 T4096 d_model 1024 H8 head_dim 128, bf16", "infer_ms": t_i * 1e3,
             "infer_tok_s": world * tok / t_i, "train_step_ms": t_t * 1e3, "train_tok_s": world * tok / t_t,
-            "gpu_launches": 8 * steps}
+            "gpu_launches": 12 * steps}
 
 
 def bench_long_context(args, rank, world):

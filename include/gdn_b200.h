@@ -275,6 +275,77 @@ typedef struct {
 int gdn_prefill_bwd_workspace_bytes(const gdn_backward_args* args, size_t* bytes);
 int gdn_prefill_bwd(const gdn_backward_args* args, void* stream);
 
+/*
+ * Backward of the layer prologue for training (no incoming conv state): gradients of the q, k, v
+ * projections, the gate pre-activations, the conv weights and A_log / dt_bias / b_bias, given the
+ * gradients of q, k, v (dtype grad_dtype, contiguous [B][T][H][D]) and of la, beta.  Replaces the
+ * autograd of the torch ops it fuses (archbench/layers/nsgdn.py:457-470, 520-536; the ShortConv backward
+ * at nsgdn.py:426-454).  Parameter gradients are fp32, zeroed and then accumulated with atomic adds
+ * (their summation order is not fixed).  DK = 64 or 128, DV in {DK, 2 DK}.
+ */
+typedef struct {
+  const void* xq;     /* forward inputs, as in gdn_prologue_args */
+  const void* xk;
+  const void* xv;
+  int64_t sxq_b, sxq_t, sxk_b, sxk_t, sxv_b, sxv_t;
+  const void* xa;
+  const void* xb;
+  int64_t sxa_b, sxa_t, sxb_b, sxb_t;
+  const float* wq;    /* (conv_size, H*DK) fp32 tap-major, or NULL */
+  const float* wk;
+  const float* wv;
+  const float* A_log;
+  const float* dt_bias;
+  const float* b_bias;
+  const void* dq;     /* [B][T][H][DK] contiguous, dtype grad_dtype */
+  const void* dk;
+  const void* dv;     /* [B][T][H][DV] */
+  const float* dla;   /* (B, T, H) */
+  const float* dbeta;
+  void* dxq;          /* projection gradients, dtype in_dtype, element strides of b and t below */
+  void* dxk;
+  void* dxv;
+  int64_t sdxq_b, sdxq_t, sdxk_b, sdxk_t, sdxv_b, sdxv_t;
+  void* dxa;
+  void* dxb;
+  int64_t sdxa_b, sdxa_t, sdxb_b, sdxb_t;
+  float* dwq;         /* (conv_size, H*DK) fp32; NULL exactly when wq is NULL */
+  float* dwk;
+  float* dwv;
+  float* dA_log;      /* (H) fp32 */
+  float* ddt_bias;
+  float* db_bias;     /* or NULL */
+  int64_t B, T, H, DK, DV;
+  int32_t conv_size, flags, in_dtype, grad_dtype;
+  float q_scale, l2_eps, la_min, beta_scale;
+} gdn_prologue_bwd_args;
+
+int gdn_layer_prologue_bwd(const gdn_prologue_bwd_args* args, void* stream);
+
+/*
+ * Backward of the layer epilogue: dy ([B][T][H][DV] contiguous, dtype y_dtype), dg ([B][T][H*DV]
+ * contiguous, dtype g_dtype; when g is given) and dweight ((DV) fp32, zeroed then accumulated with
+ * atomic adds) for the gradient `dout` of o.  Replaces the autograd of RMSNorm x SiLU(g)
+ * (archbench/layers/nsgdn.py:539-541; fla's FusedRMSNormGated).
+ */
+typedef struct {
+  const void* y;
+  gdn_strides sy;
+  const void* g;      /* or NULL */
+  int64_t sg_b, sg_t;
+  const float* weight;
+  const void* dout;   /* [B][T][H*DV], element strides of b and t below, dtype do_dtype */
+  int64_t sdo_b, sdo_t;
+  void* dy;
+  void* dg;
+  float* dweight;
+  int64_t B, T, H, DV;  /* B * T * H < 2^26 */
+  int32_t y_dtype, g_dtype, do_dtype;
+  float eps;
+} gdn_epilogue_bwd_args;
+
+int gdn_layer_epilogue_bwd(const gdn_epilogue_bwd_args* args, void* stream);
+
 /* Which kernel a prefill with these arguments runs (GDN_IMPL_CHUNK_CLUSTER, _CHUNK_SINGLE,
  * _SEGMENTED or _RECURRENT; GDN_IMPL_CHUNK resolves to one of the two chunk variants), or a
  * negative gdn_status if the arguments are invalid.  Launches nothing. */
