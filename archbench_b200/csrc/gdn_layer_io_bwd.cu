@@ -332,7 +332,8 @@ struct EpiBwdParams {
   const void* dout;
   int64_t sdo_b, sdo_t;
   void* dy;   // [B][T][H][DV] contiguous
-  void* dg;   // [B][T][H*DV] contiguous
+  void* dg;   // [B][T][H*DV], strides sdg_b, sdg_t
+  int64_t sdg_b, sdg_t;
   float* dweight;
   int B, T, H, DV;
   float eps;
@@ -385,7 +386,7 @@ __global__ void __launch_bounds__(128) epilogue_bwd_kernel(const EpiBwdParams p)
     }
     const int64_t tok = ((int64_t)b * p.T + t) * p.H + h;
     stv<TY, NPL>(reinterpret_cast<TY*>(p.dy) + tok * p.DV + c0, oy);
-    if (p.g) stv<TG, NPL>(reinterpret_cast<TG*>(p.dg) + tok * p.DV + c0, og);
+    if (p.g) stv<TG, NPL>(reinterpret_cast<TG*>(p.dg) + b * p.sdg_b + t * p.sdg_t + (int64_t)h * p.DV + c0, og);
   }
   __shared__ float red[4][512];
   const int wid = threadIdx.x >> 5;
@@ -533,6 +534,7 @@ int gdn_layer_epilogue_bwd(const gdn_epilogue_bwd_args* a, void* stream) {
   EpiBwdParams p;
   p.y = a->y; p.sy = a->sy; p.g = a->g; p.sg_b = a->sg_b; p.sg_t = a->sg_t; p.weight = a->weight;
   p.dout = a->dout; p.sdo_b = a->sdo_b; p.sdo_t = a->sdo_t; p.dy = a->dy; p.dg = a->dg; p.dweight = a->dweight;
+  p.sdg_b = a->sdg_b; p.sdg_t = a->sdg_t;
   p.B = (int)a->B; p.T = (int)a->T; p.H = (int)a->H; p.DV = (int)a->DV; p.eps = a->eps;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (cudaMemsetAsync(a->dweight, 0, a->DV * 4, s) != cudaSuccess) return GDN_ERR_LAUNCH;

@@ -159,6 +159,12 @@ class NStepGDN(nn.Module):
         dt = torch.bfloat16 if (DK == 128 and self._impl != "recurrent") else torch.float32
         parts = (proj[..., :qd], proj[..., qd:2 * qd], proj[..., 2 * qd:n_qkv], proj[..., ab0:ab0 + H], proj[..., ab0 + H:ab0 + 2 * H])
         train = _training(x, self)
+        if train and dt == torch.bfloat16:
+            # the whole mixer as one autograd node: the projection's gradient is written once
+            cw = None if self.conv is None else self.conv.weight.reshape(n_qkv, -1).float()
+            o = ops.NsgdnMixerTrain.apply(proj, cw, self.A_log, self.dt_bias, self.b_bias, self.norm.weight,
+                                          (H, DK, DV, self.n_gate, DK**-0.5, self.la_min, self.norm.eps, self._impl))
+            return self.o_proj(o)
         if train:
             q, k, v, la, beta = ops.layer_prologue_train(*parts, self.A_log, self.dt_bias, H=H, DK=DK, DV=DV, b_bias=self.b_bias,
                                                          conv=conv, q_scale=DK**-0.5, la_min=self.la_min, out_dtype=dt)

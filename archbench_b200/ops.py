@@ -128,7 +128,8 @@ class EpilogueBwdArgs(ctypes.Structure):
 
     _fields_ = [("y", ctypes.c_void_p), ("sy", Strides), ("g", ctypes.c_void_p), ("sg_b", ctypes.c_int64),
                 ("sg_t", ctypes.c_int64), ("weight", ctypes.c_void_p), ("dout", ctypes.c_void_p), ("sdo_b", ctypes.c_int64),
-                ("sdo_t", ctypes.c_int64), ("dy", ctypes.c_void_p), ("dg", ctypes.c_void_p), ("dweight", ctypes.c_void_p)] + \
+                ("sdo_t", ctypes.c_int64), ("dy", ctypes.c_void_p), ("dg", ctypes.c_void_p), ("sdg_b", ctypes.c_int64),
+                ("sdg_t", ctypes.c_int64), ("dweight", ctypes.c_void_p)] + \
                [(n, ctypes.c_int64) for n in ("B", "T", "H", "DV")] + \
                [(n, ctypes.c_int32) for n in ("y_dtype", "g_dtype", "do_dtype")] + [("eps", ctypes.c_float)]
 
@@ -641,13 +642,14 @@ def _prologue_train_setup(ctx, inputs, output):
     ctx.cfg = (H, DK, DV, q_scale, l2_eps, la_min, beta_scale)
 
 
-def _prologue_train_backward(ctx, dq, dk, dv, dla, dbeta):
-    """The prologue's backward kernel (gdn_layer_prologue_bwd): projection, gate, conv-weight and
-    A_log / dt_bias / b_bias gradients in one pass."""
-    xq, xk, xv, xa, xb, wq, wk, wv, A_log, dt_bias, b_bias = ctx.saved_tensors
-    H, DK, DV, q_scale, l2_eps, la_min, beta_scale = ctx.cfg
+def _run_prologue_bwd(xs, ws, A_log, dt_bias, b_bias, grads, outs, H, DK, DV, q_scale, l2_eps, la_min, beta_scale):
+    """gdn_layer_prologue_bwd: xs = (xq, xk, xv, xa, xb) forward inputs; ws = tap-major fp32 conv weights
+    or Nones; grads = (dq, dk, dv, dla, dbeta); outs = (dxq, dxk, dxv, dxa, dxb) to write (any b/t strides).
+    Returns (dws, dA_log, ddt_bias, db_bias) in fp32."""
+    xq, xk, xv, xa, xb = xs
     B, T, _ = xq.shape
     dev, dt = xq.device, xq.dtype
+    dq, dk, dv, dla, dbeta = grads
     gd = dq.dtype if dq is not None else torch.float32
     dq = torch.zeros(B, T, H, DK, device=dev, dtype=gd) if dq is None else dq.contiguous()
     dk = torch.zeros(B, T, H, DK, device=dev, dtype=gd) if dk is None else dk.to(gd).contiguous()
@@ -655,16 +657,14 @@ def _prologue_train_backward(ctx, dq, dk, dv, dla, dbeta):
     dla = torch.zeros(B, T, H, device=dev) if dla is None else dla.float().contiguous()
     dbeta = torch.zeros(B, T, H, device=dev) if dbeta is None else dbeta.float().contiguous()
     xq, xk, xv = _rows16(xq), _rows16(xk), _rows16(xv)
-    dxq, dxk = torch.empty(B, T, H * DK, device=dev, dtype=dt), torch.empty(B, T, H * DK, device=dev, dtype=dt)
-    dxv = torch.empty(B, T, H * DV, device=dev, dtype=dt)
-    dxa, dxb = torch.empty(B, T, H, device=dev, dtype=dt), torch.empty(B, T, H, device=dev, dtype=dt)
-    taps = 1 if wq is None else wq.shape[0]
-    dws = [None, None, None] if wq is None else [torch.empty_like(w) for w in (wq, wk, wv)]
+    dxq, dxk, dxv, dxa, dxb = outs
+    taps = 1 if ws[0] is None else ws[0].shape[0]
+    dws = [None, None, None] if ws[0] is None else [torch.empty_like(w) for w in ws]
     dA, ddt = torch.empty(H, device=dev), torch.empty(H, device=dev)
     dbb = None if b_bias is None else torch.empty(H, device=dev)
     A32, dt32 = A_log.float().contiguous(), dt_bias.float().contiguous()
     bb32 = None if b_bias is None else b_bias.float().contiguous()
-    ws = [None, None, None] if wq is None else [w.contiguous() for w in (wq, wk, wv)]
+    ws = [None if w is None else w.contiguous() for w in ws]
     a = PrologueBwdArgs(
         _ptr(xq), _ptr(xk), _ptr(xv), xq.stride(0), xq.stride(1), xk.stride(0), xk.stride(1), xv.stride(0), xv.stride(1),
         _ptr(xa), _ptr(xb), xa.stride(0), xa.stride(1), xb.stride(0), xb.stride(1),
@@ -675,7 +675,22 @@ def _prologue_train_backward(ctx, dq, dk, dv, dla, dbeta):
         B, T, H, DK, DV, taps, GDN_PROLOGUE_CLAMP_LA if la_min is not None else 0, _DTC[dt], _DTC[gd],
         float(q_scale), float(l2_eps), float(la_min if la_min is not None else 0.0), float(beta_scale))
     _check(load_library().gdn_layer_prologue_bwd(ctypes.byref(a), ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)))
-    return (dxq, dxk, dxv, dxa, dxb, dws[0], dws[1], dws[2], dA.to(A_log.dtype), ddt.to(dt_bias.dtype),
+    return dws, dA, ddt, dbb
+
+
+def _prologue_train_backward(ctx, dq, dk, dv, dla, dbeta):
+    """The prologue's backward kernel (gdn_layer_prologue_bwd): projection, gate, conv-weight and
+    A_log / dt_bias / b_bias gradients in one pass."""
+    xq, xk, xv, xa, xb, wq, wk, wv, A_log, dt_bias, b_bias = ctx.saved_tensors
+    H, DK, DV, q_scale, l2_eps, la_min, beta_scale = ctx.cfg
+    B, T, _ = xq.shape
+    dev, dt = xq.device, xq.dtype
+    outs = (torch.empty(B, T, H * DK, device=dev, dtype=dt), torch.empty(B, T, H * DK, device=dev, dtype=dt),
+            torch.empty(B, T, H * DV, device=dev, dtype=dt), torch.empty(B, T, H, device=dev, dtype=dt),
+            torch.empty(B, T, H, device=dev, dtype=dt))
+    dws, dA, ddt, dbb = _run_prologue_bwd((xq, xk, xv, xa, xb), (wq, wk, wv), A_log, dt_bias, b_bias,
+                                          (dq, dk, dv, dla, dbeta), outs, H, DK, DV, q_scale, l2_eps, la_min, beta_scale)
+    return (*outs, dws[0], dws[1], dws[2], dA.to(A_log.dtype), ddt.to(dt_bias.dtype),
             None if dbb is None else dbb.to(b_bias.dtype), None, None, None, None, None, None, None, None)
 
 
@@ -699,23 +714,32 @@ def _epilogue_train_setup(ctx, inputs, output):
     ctx.eps = eps
 
 
-def _epilogue_train_backward(ctx, do):
-    """The epilogue's backward kernel (gdn_layer_epilogue_bwd): dy, dg and the norm weight's gradient."""
-    y, weight, g = ctx.saved_tensors
+def _run_epilogue_bwd(y, weight, g, do, dy, dg, eps):
+    """gdn_layer_epilogue_bwd: writes dy (contiguous (B, T, H, DV)) and dg (any b/t strides) and returns
+    the fp32 gradient of the norm weight."""
     B, T, H, DV = y.shape
     yv = _prep_token(y, "y", y.dtype)
     gv = None if g is None else _rows16(g.reshape(B, T, H * DV))
     do = _rows16(do.reshape(B, T, H * DV))
     if do.dtype not in _DTC:
         do = do.float()
-    dy = torch.empty(B, T, H, DV, device=y.device, dtype=y.dtype)
-    dg = None if g is None else torch.empty(B, T, H * DV, device=y.device, dtype=gv.dtype)
     dw = torch.empty(DV, device=y.device)
     w = weight.float().contiguous()
     a = EpilogueBwdArgs(_ptr(yv), _tok_strides(yv), _ptr(gv), 0 if gv is None else gv.stride(0), 0 if gv is None else gv.stride(1),
-                        _ptr(w), _ptr(do), do.stride(0), do.stride(1), _ptr(dy), _ptr(dg), _ptr(dw), B, T, H, DV,
-                        _DTC[y.dtype], _DTC[gv.dtype] if gv is not None else GDN_DTYPE_F32, _DTC[do.dtype], float(ctx.eps))
+                        _ptr(w), _ptr(do), do.stride(0), do.stride(1), _ptr(dy), _ptr(dg), 0 if dg is None else dg.stride(0),
+                        0 if dg is None else dg.stride(1), _ptr(dw), B, T, H, DV,
+                        _DTC[y.dtype], _DTC[gv.dtype] if gv is not None else GDN_DTYPE_F32, _DTC[do.dtype], float(eps))
     _check(load_library().gdn_layer_epilogue_bwd(ctypes.byref(a), ctypes.c_void_p(torch.cuda.current_stream(y.device).cuda_stream)))
+    return dw
+
+
+def _epilogue_train_backward(ctx, do):
+    """The epilogue's backward kernel (gdn_layer_epilogue_bwd): dy, dg and the norm weight's gradient."""
+    y, weight, g = ctx.saved_tensors
+    B, T, H, DV = y.shape
+    dy = torch.empty(B, T, H, DV, device=y.device, dtype=y.dtype)
+    dg = None if g is None else torch.empty(B, T, H * DV, device=y.device, dtype=g.dtype)
+    dw = _run_epilogue_bwd(y, weight, g, do, dy, dg, ctx.eps)
     return dy, dw.to(weight.dtype), (None if g is None else dg.reshape(g.shape)), None, None
 
 
@@ -736,3 +760,53 @@ def layer_prologue_train(xq, xk, xv, xa, xb, A_log, dt_bias, *, H, DK, DV, b_bia
 def layer_epilogue_train(y, weight, g=None, eps=1e-5, out_dtype=torch.bfloat16):
     """``layer_epilogue``, differentiable: its backward is one CUDA kernel."""
     return _epilogue_train_op(y, weight, g, float(eps), _DTC[out_dtype])
+
+
+class NsgdnMixerTrain(torch.autograd.Function):
+    """The nsgdn mixer between its fused input projection and its output projection (n_steps = 1):
+    prologue, scan and epilogue forward and backward on the CUDA kernels.  The gradient of the
+    projection is written once, column block by column block, by the three backward kernels (no
+    per-slice accumulation).  Inputs: proj (B, T, width) with columns [q | k | v | g | a | b | pad],
+    conv weight (3 H DK.., taps) fp32 or None, A_log, dt_bias, b_bias, norm weight; output o
+    (B, T, H DV) in proj's dtype."""
+
+    @staticmethod
+    def forward(ctx, proj, conv_w, A_log, dt_bias, b_bias, norm_w, cfg):
+        H, DK, DV, n_gate, q_scale, la_min, eps, impl = cfg
+        qd = H * DK
+        n_qkv = 2 * qd + H * DV
+        ab0 = n_qkv + n_gate
+        xs = (proj[..., :qd], proj[..., qd:2 * qd], proj[..., 2 * qd:n_qkv], proj[..., ab0:ab0 + H], proj[..., ab0 + H:ab0 + 2 * H])
+        conv = None if conv_w is None else (conv_w[:qd], conv_w[qd:2 * qd], conv_w[2 * qd:])
+        q, k, v, la, beta, _ = layer_prologue(*xs, A_log, dt_bias, H=H, DK=DK, DV=DV, b_bias=b_bias, conv=conv, q_scale=q_scale,
+                                              la_min=la_min, out_dtype=torch.bfloat16)
+        y, _ = _prefill_impl(q, k, None, v, la, beta, None, False, torch.bfloat16, impl)
+        g = proj[..., n_qkv:n_qkv + n_gate] if n_gate else None
+        o = layer_epilogue(y, norm_w, g, eps=eps, out_dtype=proj.dtype)
+        ctx.save_for_backward(proj, conv_w, A_log, dt_bias, b_bias, norm_w, q, k, v, la, beta, y)
+        ctx.cfg = cfg
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        proj, conv_w, A_log, dt_bias, b_bias, norm_w, q, k, v, la, beta, y = ctx.saved_tensors
+        H, DK, DV, n_gate, q_scale, la_min, eps, impl = ctx.cfg
+        B, T, width = proj.shape
+        qd = H * DK
+        n_qkv = 2 * qd + H * DV
+        ab0 = n_qkv + n_gate
+        dproj = torch.empty_like(proj)
+        if width > ab0 + 2 * H:
+            dproj[..., ab0 + 2 * H:].zero_()
+        g = proj[..., n_qkv:n_qkv + n_gate] if n_gate else None
+        dy = torch.empty_like(y)
+        dnorm = _run_epilogue_bwd(y, norm_w, g, do, dy, dproj[..., n_qkv:n_qkv + n_gate] if n_gate else None, eps)
+        dq, dk, dbeta, dv, dla, _ = _prefill_bwd_impl(q, k, None, v, la, beta, None, dy, None, False)
+        xs = (proj[..., :qd], proj[..., qd:2 * qd], proj[..., 2 * qd:n_qkv], proj[..., ab0:ab0 + H], proj[..., ab0 + H:ab0 + 2 * H])
+        outs = (dproj[..., :qd], dproj[..., qd:2 * qd], dproj[..., 2 * qd:n_qkv], dproj[..., ab0:ab0 + H], dproj[..., ab0 + H:ab0 + 2 * H])
+        ws = (None, None, None) if conv_w is None else tuple(w.t().contiguous() for w in (conv_w[:qd], conv_w[qd:2 * qd], conv_w[2 * qd:]))
+        dws, dA, ddt, dbb = _run_prologue_bwd(xs, ws, A_log, dt_bias, b_bias, (dq, dk, dv, dla, dbeta), outs, H, DK, DV,
+                                              q_scale, 1e-12, la_min, 1.0)
+        dconv = None if conv_w is None else torch.cat([w.t() for w in dws], 0).to(conv_w.dtype)
+        return (dproj, dconv, dA.to(A_log.dtype), ddt.to(dt_bias.dtype), None if dbb is None else dbb.to(b_bias.dtype),
+                dnorm.to(norm_w.dtype), None)

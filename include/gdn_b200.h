@@ -324,7 +324,7 @@ int gdn_layer_prologue_bwd(const gdn_prologue_bwd_args* args, void* stream);
 
 /*
  * Backward of the layer epilogue: dy ([B][T][H][DV] contiguous, dtype y_dtype), dg ([B][T][H*DV]
- * contiguous, dtype g_dtype; when g is given) and dweight ((DV) fp32, zeroed then accumulated with
+ * with the strides given, dtype g_dtype; when g is given) and dweight ((DV) fp32, zeroed then accumulated with
  * atomic adds) for the gradient `dout` of o.  Replaces the autograd of RMSNorm x SiLU(g)
  * (archbench/layers/nsgdn.py:539-541; fla's FusedRMSNormGated).
  */
@@ -338,6 +338,7 @@ typedef struct {
   int64_t sdo_b, sdo_t;
   void* dy;
   void* dg;
+  int64_t sdg_b, sdg_t;  /* element strides of b and t of dg (unit channel stride) */
   float* dweight;
   int64_t B, T, H, DV;  /* B * T * H < 2^26 */
   int32_t y_dtype, g_dtype, do_dtype;

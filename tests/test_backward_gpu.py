@@ -179,6 +179,7 @@ def test_layer_parameter_gradients(layer, monkeypatch):
     else:
         m = layers.NStepGDN(256, num_heads=2, head_dim=128, expand_v=1.0, n_steps=1 if layer == "nsgdn1" else 2).cuda()
     x = torch.randn(2, 96, 256, device="cuda")
+    m.fused_io = False  # the scan is the part under test: keep the rest on the PyTorch path
 
     def grads():
         m.zero_grad()
