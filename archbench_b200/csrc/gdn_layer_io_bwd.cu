@@ -8,9 +8,10 @@
 //   la = -softplus(a + dt_bias) exp(A_log) (zero gradient where clamped at la_min):
 //     da = dla (-sigmoid(a + dt_bias) exp(A_log)), ddt_bias = sum da, dA_log = sum dla la;
 //   beta = beta_scale sigmoid(b + b_bias): db = dbeta beta_scale sigmoid (1 - sigmoid), db_bias = sum db.
-// One warp per (b, h) and run of RUN tokens as in the forward; the run's projection rows (and the conv
-// halo on both sides) are staged in shared memory by cp.async; dc of the last TAPS tokens is kept in
-// registers, so dx of a token is finished as soon as dc of the TAPS - 1 tokens after it is known.
+// One block per component (q, k or v), (b, h) and 4 runs of RUN tokens, one warp per run; the run's rows
+// of the component (and the conv halo on both sides) are staged in shared memory by cp.async, the next
+// token's incoming gradient is loaded while the current one is used; dc of the last TAPS tokens is kept
+// in registers, so dx of a token is finished as soon as dc of the TAPS - 1 tokens after it is known.
 // Parameter gradients are reduced over the block's warps in shared memory and added to the outputs
 // with one atomic add per element and block (fp32; the summation order across blocks is not fixed).
 //
@@ -117,208 +118,180 @@ __device__ __forceinline__ void dx_of(const Lane<TAPS, NPL>& L, const float* w, 
   }
 }
 
-// dc of one component at token t from the staged rows (row j of the conv window at rows + j * ld).
-template <typename TX, typename TG, int TAPS, int NPL, bool NORM>
-__device__ __forceinline__ void comp_dc(const TX* rows, int ld, const float* w, int wld, bool has_w, const TG* gp,
-                                        float scale, float eps, float (&dc)[NPL]) {
-  float c[NPL], xj[NPL];
-  if (has_w) {
-#pragma unroll
-    for (int n = 0; n < NPL; ++n) c[n] = 0.f;
-#pragma unroll
-    for (int j = 0; j < TAPS; ++j) {
-      float wj[NPL];
-      load_vec<NPL>(w + j * wld, wj);
-      load_vec<NPL>(rows + j * ld, xj);
-#pragma unroll
-      for (int n = 0; n < NPL; ++n) c[n] = fmaf(wj[n], xj[n], c[n]);
-    }
-  } else {
-    load_vec<NPL>(rows + (TAPS - 1) * ld, c);
-  }
-  float g[NPL], s[NPL];
-  load_vec<NPL>(gp, g);
-#pragma unroll
-  for (int n = 0; n < NPL; ++n) s[n] = c[n] * sigm(c[n]);
-  if (NORM) {
-    float ss = 0.f, sg = 0.f;
-#pragma unroll
-    for (int n = 0; n < NPL; ++n) {
-      ss = fmaf(s[n], s[n], ss);
-      sg = fmaf(s[n], g[n], sg);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      ss += __shfl_xor_sync(0xffffffffu, ss, o);
-      sg += __shfl_xor_sync(0xffffffffu, sg, o);
-    }
-    const float nrm = sqrtf(ss), m = fmaxf(nrm, eps), inv = 1.f / m;
-    const float proj = nrm > eps ? sg * inv * inv : 0.f;  // s^ . dq / m with s^ = s / m
-#pragma unroll
-    for (int n = 0; n < NPL; ++n) g[n] = scale * inv * (g[n] - s[n] * proj);
-  }
-#pragma unroll
-  for (int n = 0; n < NPL; ++n) dc[n] = g[n] * dsilu(c[n]);
-}
-
-template <typename TX, typename TG, int NK, int NV, int TAPS>
-__global__ void __launch_bounds__(32 * WARPS) prologue_bwd_kernel(const ProBwdParams p) {
-  extern __shared__ __align__(16) float sw[];  // weights [q | k | v] x TAPS x D, then staged rows per warp
-  constexpr int DK = 32 * NK, DV = 32 * NV, W = 2 * DK + DV;
+// One component (q, k or v: blockIdx.y) of one (b, h) and WARPS runs of RUN tokens per block, one run per
+// warp; the v blocks also do the gates.
+template <typename TX, typename TG, int NPL, bool NORM, int TAPS>
+__device__ __forceinline__ void prologue_bwd_comp(const ProBwdParams& p, const CompB& cp, float scale, bool gates,
+                                                  float* sw) {
+  constexpr int D = 32 * NPL;
   constexpr int NROWS = RUN + 2 * (TAPS - 1);  // staged tokens t0 - (TAPS - 1) .. t1 + TAPS - 2
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int runs = (p.T + RUN - 1) / RUN, rgroups = (runs + WARPS - 1) / WARPS;
   const int bh = blockIdx.x / rgroups, rg = blockIdx.x - bh * rgroups;
   const int b = bh / p.H, h = bh - b * p.H;
-  const CompB* cs[3] = {&p.q, &p.k, &p.v};
-  constexpr int off[3] = {0, DK, 2 * DK}, len[3] = {DK, DK, DV};
-  float* swc[3] = {sw, sw + TAPS * DK, sw + 2 * TAPS * DK};
-#pragma unroll
-  for (int c = 0; c < 3; ++c) {
-    if (!cs[c]->w) continue;
-    for (int i = threadIdx.x; i < TAPS * len[c]; i += blockDim.x) {
-      const int j = i / len[c], ch = i - j * len[c];
-      swc[c][i] = cs[c]->w[(int64_t)j * cs[c]->wch + (int64_t)h * len[c] + ch];
+  const bool has_w = cp.w != nullptr;
+  if (has_w)
+    for (int i = threadIdx.x; i < TAPS * D; i += blockDim.x) {
+      const int j = i / D, ch = i - j * D;
+      sw[i] = cp.w[(int64_t)j * cp.wch + (int64_t)h * D + ch];
     }
-  }
-  TX* stage = reinterpret_cast<TX*>(sw + TAPS * W) + (size_t)wid * NROWS * W;
+  TX* stage = reinterpret_cast<TX*>(sw + TAPS * D) + (size_t)wid * NROWS * D;
   __syncthreads();
   const int run = rg * WARPS + wid;
   const bool active = run < runs;
   const int t0 = run * RUN, t1 = active ? min(p.T, t0 + RUN) : t0;
   const int tend = min(p.T, t1 + TAPS - 1);  // dc is needed for tokens t0 .. tend - 1
-  constexpr int EPC = 16 / sizeof(TX);
+  constexpr int EPC = 16 / sizeof(TX), CHUNKS = D / EPC;
   if (active) {
-    const int nrows = tend - t0 + TAPS - 1;
+    const int nrows = tend - t0 + TAPS - 1, hc = h * D;
+    for (int i = lane; i < nrows * CHUNKS; i += 32) {
+      const int r = i / CHUNKS, q = i - r * CHUNKS, t = t0 - (TAPS - 1) + r;
+      TX* dst = stage + (size_t)r * D + q * EPC;
+      if (t >= 0) {
+        cp16(dst, reinterpret_cast<const TX*>(cp.x) + (int64_t)b * cp.sb + (int64_t)t * cp.st + hc + q * EPC);
+      } else {
 #pragma unroll
-    for (int c = 0; c < 3; ++c) {
-      const CompB& cp = *cs[c];
-      constexpr int chunks_[3] = {len[0] / EPC, len[1] / EPC, len[2] / EPC};
-      const int chunks = chunks_[c], hc = h * len[c];
-      for (int i = lane; i < nrows * chunks; i += 32) {
-        const int r = i / chunks, q = i - r * chunks, t = t0 - (TAPS - 1) + r;
-        TX* dst = stage + (size_t)r * W + off[c] + q * EPC;
-        if (t >= 0) {
-          cp16(dst, reinterpret_cast<const TX*>(cp.x) + (int64_t)b * cp.sb + (int64_t)t * cp.st + hc + q * EPC);
-        } else {
-#pragma unroll
-          for (int e = 0; e < EPC; ++e) store_as(dst + e, 0.f);  // training calls start from zero history
-        }
+        for (int e = 0; e < EPC; ++e) store_as(dst + e, 0.f);  // training calls start from zero history
       }
     }
     asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
     __syncwarp();
   }
-  const bool wq = p.q.w != nullptr, wk = p.k.w != nullptr, wv = p.v.w != nullptr;
-  Lane<TAPS, NK> lq, lk;
-  Lane<TAPS, NV> lv;
-  lq.clear();
-  lk.clear();
-  lv.clear();
+  Lane<TAPS, NPL> L;
+  L.clear();
   const int64_t tokb = ((int64_t)b * p.T) * p.H + h;  // token (b, 0, h)
+  const float* wl = sw + lane * NPL;
   if (active) {
+    // the next token's incoming gradient is loaded while this token's is used
+    float gnext[NPL];
+    load_vec<NPL>(reinterpret_cast<const TG*>(cp.g) + (tokb + (int64_t)t0 * p.H) * D + lane * NPL, gnext);
 #pragma unroll 1
     for (int t = t0; t <= t1 + TAPS - 2; ++t) {
-      float dq[NK], dk[NK], dv[NV];
+      float dc[NPL];
       if (t < tend) {
-        const TX* rows = stage + (size_t)(t - t0) * W;
-        const int64_t tok = tokb + (int64_t)t * p.H;
-        comp_dc<TX, TG, TAPS, NK, true>(rows + lane * NK, W, swc[0] + lane * NK, DK, wq,
-                                       reinterpret_cast<const TG*>(p.q.g) + tok * DK + lane * NK, p.q_scale, p.eps, dq);
-        comp_dc<TX, TG, TAPS, NK, true>(rows + DK + lane * NK, W, swc[1] + lane * NK, DK, wk,
-                                       reinterpret_cast<const TG*>(p.k.g) + tok * DK + lane * NK, 1.f, p.eps, dk);
-        comp_dc<TX, TG, TAPS, NV, false>(rows + 2 * DK + lane * NV, W, swc[2] + lane * NV, DV, wv,
-                                        reinterpret_cast<const TG*>(p.v.g) + tok * DV + lane * NV, 1.f, p.eps, dv);
-        if (t < t1) {  // conv-weight gradients of this run's tokens
+        float g[NPL];
+#pragma unroll
+        for (int n = 0; n < NPL; ++n) g[n] = gnext[n];
+        if (t + 1 < tend)
+          load_vec<NPL>(reinterpret_cast<const TG*>(cp.g) + (tokb + (int64_t)(t + 1) * p.H) * D + lane * NPL, gnext);
+        const TX* rows = stage + (size_t)(t - t0) * D + lane * NPL;
+        float c[NPL], xs[TAPS][NPL];
+#pragma unroll
+        for (int j = 0; j < TAPS; ++j) load_vec<NPL>(rows + j * D, xs[j]);
+        if (has_w) {
+#pragma unroll
+          for (int n = 0; n < NPL; ++n) c[n] = 0.f;
 #pragma unroll
           for (int j = 0; j < TAPS; ++j) {
-            float xq[NK], xk[NK], xv[NV];
-            load_vec<NK>(rows + j * W + lane * NK, xq);
-            load_vec<NK>(rows + j * W + DK + lane * NK, xk);
-            load_vec<NV>(rows + j * W + 2 * DK + lane * NV, xv);
+            float wj[NPL];
+            load_vec<NPL>(wl + j * D, wj);
 #pragma unroll
-            for (int n = 0; n < NK; ++n) {
-              lq.dw[j][n] = fmaf(dq[n], xq[n], lq.dw[j][n]);
-              lk.dw[j][n] = fmaf(dk[n], xk[n], lk.dw[j][n]);
-            }
-#pragma unroll
-            for (int n = 0; n < NV; ++n) lv.dw[j][n] = fmaf(dv[n], xv[n], lv.dw[j][n]);
+            for (int n = 0; n < NPL; ++n) c[n] = fmaf(wj[n], xs[j][n], c[n]);
           }
+        } else {
+#pragma unroll
+          for (int n = 0; n < NPL; ++n) c[n] = xs[TAPS - 1][n];
+        }
+        float sg_[NPL], s[NPL];
+#pragma unroll
+        for (int n = 0; n < NPL; ++n) {
+          sg_[n] = sigm(c[n]);
+          s[n] = c[n] * sg_[n];
+        }
+        if (NORM) {
+          float ss = 0.f, sgd = 0.f;
+#pragma unroll
+          for (int n = 0; n < NPL; ++n) {
+            ss = fmaf(s[n], s[n], ss);
+            sgd = fmaf(s[n], g[n], sgd);
+          }
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) {
+            ss += __shfl_xor_sync(0xffffffffu, ss, o);
+            sgd += __shfl_xor_sync(0xffffffffu, sgd, o);
+          }
+          const float nrm = sqrtf(ss), m = fmaxf(nrm, p.eps), inv = 1.f / m;
+          const float proj = nrm > p.eps ? sgd * inv * inv : 0.f;
+#pragma unroll
+          for (int n = 0; n < NPL; ++n) g[n] = scale * inv * (g[n] - s[n] * proj);
+        }
+#pragma unroll
+        for (int n = 0; n < NPL; ++n) dc[n] = g[n] * (sg_[n] * (1.f + c[n] * (1.f - sg_[n])));
+        if (t < t1) {  // conv-weight gradient of this run's tokens
+#pragma unroll
+          for (int j = 0; j < TAPS; ++j)
+#pragma unroll
+            for (int n = 0; n < NPL; ++n) L.dw[j][n] = fmaf(dc[n], xs[j][n], L.dw[j][n]);
         }
       } else {
 #pragma unroll
-        for (int n = 0; n < NK; ++n) dq[n] = dk[n] = 0.f;
-#pragma unroll
-        for (int n = 0; n < NV; ++n) dv[n] = 0.f;
+        for (int n = 0; n < NPL; ++n) dc[n] = 0.f;
       }
-      lq.push(dq);
-      lk.push(dk);
-      lv.push(dv);
+      L.push(dc);
       const int tau = t - (TAPS - 1);
       if (tau >= t0) {
-        float oq[NK], ok[NK], ov[NV];
-        dx_of<TAPS, NK>(lq, swc[0] + lane * NK, DK, wq, oq);
-        dx_of<TAPS, NK>(lk, swc[1] + lane * NK, DK, wk, ok);
-        dx_of<TAPS, NV>(lv, swc[2] + lane * NV, DV, wv, ov);
-        stv<TX, NK>(reinterpret_cast<TX*>(p.q.dx) + (int64_t)b * p.q.dsb + (int64_t)tau * p.q.dst + h * DK + lane * NK, oq);
-        stv<TX, NK>(reinterpret_cast<TX*>(p.k.dx) + (int64_t)b * p.k.dsb + (int64_t)tau * p.k.dst + h * DK + lane * NK, ok);
-        stv<TX, NV>(reinterpret_cast<TX*>(p.v.dx) + (int64_t)b * p.v.dsb + (int64_t)tau * p.v.dst + h * DV + lane * NV, ov);
+        float o[NPL];
+        dx_of<TAPS, NPL>(L, wl, D, has_w, o);
+        stv<TX, NPL>(reinterpret_cast<TX*>(cp.dx) + (int64_t)b * cp.dsb + (int64_t)tau * cp.dst + h * D + lane * NPL, o);
       }
     }
   }
-  // gates, one token per lane; their parameter gradients summed over the warp
-  float s_dt = 0.f, s_al = 0.f, s_bb = 0.f;
-  if (active) {
-    const float dtb = p.dt_bias[h], Ae = expf(p.A_log[h]), bb_h = p.b_bias ? p.b_bias[h] : 0.f;
-    for (int t = t0 + lane; t < t1; t += 32) {
-      const int64_t tok = tokb + (int64_t)t * p.H;
-      const float a = to_f32(reinterpret_cast<const TX*>(p.xa)[(int64_t)b * p.sa_b + (int64_t)t * p.sa_t + h]);
-      const float bb = to_f32(reinterpret_cast<const TX*>(p.xb)[(int64_t)b * p.sb_b + (int64_t)t * p.sb_t + h]);
-      const float z = a + dtb, la = -softplus(z) * Ae, gl = p.dla[tok];
-      const bool live = !(p.clamp && la < p.la_min);
-      const float dz = live ? gl * (-sigm(z) * Ae) : 0.f;
-      s_dt += dz;
-      s_al += live ? gl * la : 0.f;
-      const float sb = sigm(bb + bb_h), dzb = p.dbeta[tok] * p.beta_scale * sb * (1.f - sb);
-      s_bb += dzb;
-      store_as(reinterpret_cast<TX*>(p.dxa) + (int64_t)b * p.dsa_b + (int64_t)t * p.dsa_t + h, dz);
-      store_as(reinterpret_cast<TX*>(p.dxb) + (int64_t)b * p.dsb_b + (int64_t)t * p.dsb_t + h, dzb);
+  if (gates) {  // one token per lane; parameter gradients summed over the warp
+    float s_dt = 0.f, s_al = 0.f, s_bb = 0.f;
+    if (active) {
+      const float dtb = p.dt_bias[h], Ae = expf(p.A_log[h]), bb_h = p.b_bias ? p.b_bias[h] : 0.f;
+      for (int t = t0 + lane; t < t1; t += 32) {
+        const int64_t tok = tokb + (int64_t)t * p.H;
+        const float a = to_f32(reinterpret_cast<const TX*>(p.xa)[(int64_t)b * p.sa_b + (int64_t)t * p.sa_t + h]);
+        const float bb = to_f32(reinterpret_cast<const TX*>(p.xb)[(int64_t)b * p.sb_b + (int64_t)t * p.sb_t + h]);
+        const float z = a + dtb, la = -softplus(z) * Ae, gl = p.dla[tok];
+        const bool live = !(p.clamp && la < p.la_min);
+        const float dz = live ? gl * (-sigm(z) * Ae) : 0.f;
+        s_dt += dz;
+        s_al += live ? gl * la : 0.f;
+        const float sb = sigm(bb + bb_h), dzb = p.dbeta[tok] * p.beta_scale * sb * (1.f - sb);
+        s_bb += dzb;
+        store_as(reinterpret_cast<TX*>(p.dxa) + (int64_t)b * p.dsa_b + (int64_t)t * p.dsa_t + h, dz);
+        store_as(reinterpret_cast<TX*>(p.dxb) + (int64_t)b * p.dsb_b + (int64_t)t * p.dsb_t + h, dzb);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      s_dt += __shfl_xor_sync(0xffffffffu, s_dt, o);
+      s_al += __shfl_xor_sync(0xffffffffu, s_al, o);
+      s_bb += __shfl_xor_sync(0xffffffffu, s_bb, o);
+    }
+    if (lane == 0 && active) {
+      atomicAdd(p.ddt_bias + h, s_dt);
+      atomicAdd(p.dA_log + h, s_al);
+      if (p.db_bias) atomicAdd(p.db_bias + h, s_bb);
     }
   }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    s_dt += __shfl_xor_sync(0xffffffffu, s_dt, o);
-    s_al += __shfl_xor_sync(0xffffffffu, s_al, o);
-    s_bb += __shfl_xor_sync(0xffffffffu, s_bb, o);
-  }
-  if (lane == 0 && active) {
-    atomicAdd(p.ddt_bias + h, s_dt);
-    atomicAdd(p.dA_log + h, s_al);
-    if (p.db_bias) atomicAdd(p.db_bias + h, s_bb);
-  }
-  // conv-weight gradients: the block's warps (same head) summed in shared memory, one atomic per element
-  if (!(wq || wk || wv)) return;
+  // conv-weight gradient: the block's warps summed in shared memory, one atomic per element
+  if (!has_w) return;
   __syncthreads();  // every warp is done with its staged rows
-  float* red = sw + TAPS * W;  // WARPS x TAPS x W floats fit in the staging area
+  float* red = sw + TAPS * D;  // WARPS x TAPS x D floats fit in the staging area
 #pragma unroll
-  for (int j = 0; j < TAPS; ++j) {
+  for (int j = 0; j < TAPS; ++j)
 #pragma unroll
-    for (int n = 0; n < NK; ++n) {
-      red[((size_t)wid * TAPS + j) * W + lane * NK + n] = lq.dw[j][n];
-      red[((size_t)wid * TAPS + j) * W + DK + lane * NK + n] = lk.dw[j][n];
-    }
-#pragma unroll
-    for (int n = 0; n < NV; ++n) red[((size_t)wid * TAPS + j) * W + 2 * DK + lane * NV + n] = lv.dw[j][n];
-  }
+    for (int n = 0; n < NPL; ++n) red[((size_t)wid * TAPS + j) * D + lane * NPL + n] = L.dw[j][n];
   __syncthreads();
-  for (int i = threadIdx.x; i < TAPS * W; i += blockDim.x) {
-    float s = 0.f;
+  for (int i = threadIdx.x; i < TAPS * D; i += blockDim.x) {
+    float v = 0.f;
 #pragma unroll
-    for (int w = 0; w < WARPS; ++w) s += red[(size_t)w * TAPS * W + i];
-    const int j = i / W, e = i - j * W;
-    const int c = e < DK ? 0 : (e < 2 * DK ? 1 : 2);
-    const int ch = e - off[c];
-    if (cs[c]->dw) atomicAdd(cs[c]->dw + (int64_t)j * cs[c]->wch + (int64_t)h * len[c] + ch, s);
+    for (int w = 0; w < WARPS; ++w) v += red[(size_t)w * TAPS * D + i];
+    const int j = i / D, ch = i - j * D;
+    atomicAdd(cp.dw + (int64_t)j * cp.wch + (int64_t)h * D + ch, v);
+  }
+}
+
+template <typename TX, typename TG, int NK, int NV, int TAPS>
+__global__ void __launch_bounds__(32 * WARPS) prologue_bwd_kernel(const ProBwdParams p) {
+  extern __shared__ __align__(16) float sw[];  // this component's weights (TAPS x D), then staged rows per warp
+  switch (blockIdx.y) {
+    case 0: prologue_bwd_comp<TX, TG, NK, true, TAPS>(p, p.q, p.q_scale, false, sw); break;
+    case 1: prologue_bwd_comp<TX, TG, NK, true, TAPS>(p, p.k, 1.f, false, sw); break;
+    default: prologue_bwd_comp<TX, TG, NV, false, TAPS>(p, p.v, 1.f, true, sw); break;
   }
 }
 
@@ -408,22 +381,22 @@ bool device_ok() {
 
 template <typename TX, typename TG, int NK, int NV, int TAPS>
 int launch_pro(const ProBwdParams& p, cudaStream_t s) {
-  constexpr int W = 2 * 32 * NK + 32 * NV;
-  const size_t stage = (size_t)WARPS * (RUN + 2 * (TAPS - 1)) * W * sizeof(TX);
-  const size_t red = (size_t)WARPS * TAPS * W * sizeof(float);
-  const size_t sm = (size_t)TAPS * W * 4 + (stage > red ? stage : red);
-  if (sm > 200 * 1024) return GDN_ERR_UNSUPPORTED;
+  constexpr int D = 32 * (NK > NV ? NK : NV);
+  const size_t stage = (size_t)WARPS * (RUN + 2 * (TAPS - 1)) * D * sizeof(TX);
+  const size_t red = (size_t)WARPS * TAPS * D * sizeof(float);
+  const size_t sm = (size_t)TAPS * D * 4 + (stage > red ? stage : red);
+  if (sm > 100 * 1024) return GDN_ERR_UNSUPPORTED;
   static bool attr = false;
   if (!attr) {
     if (cudaFuncSetAttribute(prologue_bwd_kernel<TX, TG, NK, NV, TAPS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             200 * 1024) != cudaSuccess)
+                             100 * 1024) != cudaSuccess)
       return GDN_ERR_LAUNCH;
     attr = true;
   }
   const int64_t runs = (p.T + RUN - 1) / RUN;
   const int64_t blocks = (int64_t)p.B * p.H * ((runs + WARPS - 1) / WARPS);
   if (blocks > 0x7fffffff) return GDN_ERR_SHAPE;
-  prologue_bwd_kernel<TX, TG, NK, NV, TAPS><<<(unsigned)blocks, 32 * WARPS, sm, s>>>(p);
+  prologue_bwd_kernel<TX, TG, NK, NV, TAPS><<<dim3((unsigned)blocks, 3), 32 * WARPS, sm, s>>>(p);
   return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
 }
 
