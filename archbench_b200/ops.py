@@ -463,6 +463,49 @@ def gdn_prefill(q, k, v, la, beta=None, u=None, initial_state=None, output_final
     return y, (s if output_final_state else None)
 
 
+_COPY_STREAMS = {}
+
+
+def _copy_streams(dev: torch.device):
+    if dev.index not in _COPY_STREAMS:
+        _COPY_STREAMS[dev.index] = (torch.cuda.Stream(dev), torch.cuda.Stream(dev))
+    return _COPY_STREAMS[dev.index]
+
+
+def gdn_prefill_from_host(q, k, v, la, beta, y_out, pieces=8, impl="auto", device=None):
+    """Prefill of host tensors (pinned, for asynchronous copies) into the host tensor ``y_out``.
+
+    The batch is cut into ``pieces`` along B: each piece's inputs are copied to the GPU on one copy
+    stream, its prefill runs on the current stream and its output is copied back on another, so the
+    host-to-device copies of later pieces overlap the prefill and the device-to-host copies of earlier
+    ones (PCIe carries both directions at once).  Returns after enqueueing; the current stream waits
+    for the last copy back, so synchronising it (or an event recorded on it) covers the whole call.
+    Same arguments and result as ``gdn_prefill(q, k, v, la, beta=beta)`` with y in ``y_out``'s dtype."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    cur = torch.cuda.current_stream(dev)
+    h2d, d2h = _copy_streams(dev)
+    B = q.shape[0]
+    pieces = max(1, min(int(pieces), B))
+    cuts = [B * i // pieces for i in range(pieces + 1)]
+    h2d.wait_stream(cur)
+    d2h.wait_stream(cur)
+    for b0, b1 in zip(cuts[:-1], cuts[1:]):
+        if b1 == b0:
+            continue
+        with torch.cuda.stream(h2d):
+            g = [t[b0:b1].to(dev, non_blocking=True) for t in (q, k, v, la, beta)]
+        cur.wait_stream(h2d)
+        for t in g:
+            t.record_stream(cur)
+        y, _ = gdn_prefill(*g[:4], beta=g[4], out_dtype=y_out.dtype, impl=impl)
+        d2h.wait_stream(cur)
+        y.record_stream(d2h)
+        with torch.cuda.stream(d2h):
+            y_out[b0:b1].copy_(y, non_blocking=True)
+    cur.wait_stream(d2h)
+    return y_out
+
+
 def gdn_decode_step(q, k, v, la, state, beta=None, u=None, out_dtype=None):
     """One token per sequence: q, k, u (B, H, DK), v (B, H, DV), la/beta (B, H); ``state``
     (B, H, DV, DK) fp32 is updated in place.  Returns y (B, H, DV)."""

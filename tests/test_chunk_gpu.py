@@ -200,3 +200,19 @@ def test_write_vectors_with_wide_state(DV):
                            out_dtype=torch.float32)
     check(y, y_o, f"y DV={DV} (u given)")
     check(S, S_o, f"S_T DV={DV} (u given)")
+
+
+@pytest.mark.parametrize("pieces", [1, 3, 8])
+def test_prefill_from_host_buffers(pieces):
+    """ops.gdn_prefill_from_host (pinned host in, host out, copies pipelined with the prefill) returns
+    exactly what gdn_prefill returns for each piece of the batch."""
+    B, T, H = 8, 200, 2
+    x = {n: t.pin_memory() for n, t in make_inputs(B, T, H, 128, 128, seed=41, dtype=torch.bfloat16).items()}
+    y_host = torch.empty(B, T, H, 128, dtype=torch.bfloat16).pin_memory()
+    ops.gdn_prefill_from_host(x["q"], x["k"], x["v"], x["la"], x["beta"], y_host, pieces=pieces)
+    torch.cuda.synchronize()
+    cuts = [B * i // pieces for i in range(pieces + 1)]
+    for b0, b1 in zip(cuts[:-1], cuts[1:]):
+        g = {n: t[b0:b1].cuda() for n, t in x.items()}
+        y, _ = ops.gdn_prefill(g["q"], g["k"], g["v"], g["la"], beta=g["beta"])
+        assert torch.equal(y.cpu(), y_host[b0:b1]), (b0, b1)
