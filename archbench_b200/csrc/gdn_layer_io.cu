@@ -105,6 +105,11 @@ struct PrologueParams {
   int B, T, H, DK, DV, taps, clamp;
   int run;  // tokens per warp (set at launch)
   float q_scale, eps, la_min, beta_scale;
+  int n_steps;            // write-vector steps (nsgdn.py:61-75); > 1: u below
+  void* u;                // [B][T][H][DK] contiguous, out dtype
+  const float* lam;       // (H) step sizes (the layer's softplus(lam))
+  const float* kprev_in;  // (B, H, DK) fp32 normalised k before t = 0, or NULL (zero)
+  float* kprev_out;       // (B, H, DK) fp32 normalised k of token T - 1, or NULL
 };
 
 // Row `t` (t < 0: the incoming conv state, or zeros) of channels [c0, c0 + NPL) of a component.
@@ -179,12 +184,14 @@ __global__ void __launch_bounds__(32 * TOKS) prologue_kernel(const PrologueParam
       swc[c][i] = round_to<TX>(cs[c]->w[(int64_t)j * cs[c]->wch + (int64_t)h * len[c] + ch]);
     }
   }
-  TX* stage = reinterpret_cast<TX*>(sw + TAPS * W) + (size_t)wid * (RUN + TAPS - 1) * W;
+  TX* stage = reinterpret_cast<TX*>(sw + TAPS * W) + (size_t)wid * (RUN + TAPS) * W;
+  const bool nstep = p.n_steps > 1;
+  const int lead = nstep ? 1 : 0;  // n-step write vectors need k of the token before the run
   __syncthreads();
   const int run = rg * TOKS + wid;
   if (run >= runs) return;
-  const int t0 = run * RUN, t1 = min(p.T, t0 + RUN), nrows = t1 - t0 + TAPS - 1;
-  // staged row r holds token t0 - (TAPS - 1) + r; tokens before 0 come from the incoming conv state
+  const int t0 = run * RUN, t1 = min(p.T, t0 + RUN), nrows = t1 - t0 + TAPS - 1 + lead;
+  // staged row r holds token t0 - (TAPS - 1) - lead + r; tokens before 0 come from the incoming conv state
   constexpr int EPC = 16 / sizeof(TX);
 #pragma unroll
   for (int c = 0; c < 3; ++c) {
@@ -192,10 +199,13 @@ __global__ void __launch_bounds__(32 * TOKS) prologue_kernel(const PrologueParam
     constexpr int chunks_[3] = {len[0] / EPC, len[1] / EPC, len[2] / EPC};
     const int chunks = chunks_[c], hc = h * len[c];
     for (int i = lane; i < nrows * chunks; i += 32) {
-      const int r = i / chunks, q = i - r * chunks, t = t0 - (TAPS - 1) + r;
+      const int r = i / chunks, q = i - r * chunks, t = t0 - (TAPS - 1) - lead + r;
       TX* dst = stage + (size_t)r * W + off[c] + q * EPC;
       if (t >= 0) {
         cp16(dst, reinterpret_cast<const TX*>(cp.x) + (int64_t)b * cp.sb + (int64_t)t * cp.st + hc + q * EPC);
+      } else if (t < -(TAPS - 1)) {  // before the conv state: only reached for k of token -1, which is unused
+#pragma unroll
+        for (int e = 0; e < EPC; ++e) store_as(dst + e, 0.f);
       } else {
         const TX* pc = cp.cin ? reinterpret_cast<const TX*>(cp.cin) + (int64_t)b * cp.csb : nullptr;
 #pragma unroll
@@ -210,9 +220,30 @@ __global__ void __launch_bounds__(32 * TOKS) prologue_kernel(const PrologueParam
   __syncwarp();
   const bool wq = p.q.w != nullptr, wk = p.k.w != nullptr, wv = p.v.w != nullptr;
   const float dtb = p.dt_bias[h], Ae = expf(p.A_log[h]), bb_h = p.b_bias ? p.b_bias[h] : 0.f;
+  // n-step write vectors: p = k of the previous token (normalised), from the run's lead row, the
+  // incoming k_prev at t = 0, or zero
+  float kp[NK];
+#pragma unroll
+  for (int n = 0; n < NK; ++n) kp[n] = 0.f;
+  const float lam_h = nstep ? p.lam[h] : 0.f;
+  if (nstep) {
+    if (t0 > 0) {
+      conv_tok<TX, TAPS, NK>(stage + DK + lane * NK, W, swc[1] + lane * NK, DK, wk, kp);
+      float s2 = 0.f;
+#pragma unroll
+      for (int n = 0; n < NK; ++n) s2 = fmaf(kp[n], kp[n], s2);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+      const float ik = 1.f / fmaxf(sqrtf(s2), p.eps);
+#pragma unroll
+      for (int n = 0; n < NK; ++n) kp[n] *= ik;
+    } else if (p.kprev_in) {
+      load_f32<NK>(p.kprev_in + ((int64_t)b * p.H + h) * DK + lane * NK, kp);
+    }
+  }
 #pragma unroll 1
   for (int t = t0; t < t1; ++t) {
-    const TX* rows = stage + (size_t)(t - t0) * W;
+    const TX* rows = stage + (size_t)(t - t0 + lead) * W;
     float q[NK], k[NK], v[NV];
     conv_tok<TX, TAPS, NK>(rows + lane * NK, W, swc[0] + lane * NK, DK, wq, q);
     conv_tok<TX, TAPS, NK>(rows + DK + lane * NK, W, swc[1] + lane * NK, DK, wk, k);
@@ -238,6 +269,39 @@ __global__ void __launch_bounds__(32 * TOKS) prologue_kernel(const PrologueParam
     store_vec<TO, NK>(reinterpret_cast<TO*>(p.q.out) + tok * DK + lane * NK, q);
     store_vec<TO, NK>(reinterpret_cast<TO*>(p.k.out) + tok * DK + lane * NK, k);
     store_vec<TO, NV>(reinterpret_cast<TO*>(p.v.out) + tok * DV + lane * NV, v);
+    if (nstep) {  // u = beta k, then n - 1 steps u -= lam beta (p . u) (p - (p . k) k)   (nsgdn.py:61-75)
+      const float xbt = to_f32(reinterpret_cast<const TX*>(p.xb)[(int64_t)b * p.sb_b + (int64_t)t * p.sb_t + h]);
+      const float bt = p.beta_scale / (1.f + expf(-(xbt + bb_h)));
+      float pk = 0.f;
+#pragma unroll
+      for (int n = 0; n < NK; ++n) pk = fmaf(kp[n], k[n], pk);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) pk += __shfl_xor_sync(0xffffffffu, pk, o);
+      float u[NK], pp[NK];
+#pragma unroll
+      for (int n = 0; n < NK; ++n) {
+        pp[n] = kp[n] - pk * k[n];
+        u[n] = bt * k[n];
+      }
+      const float lb = lam_h * bt;
+#pragma unroll 1
+      for (int st = 1; st < p.n_steps; ++st) {
+        float pu = 0.f;
+#pragma unroll
+        for (int n = 0; n < NK; ++n) pu = fmaf(kp[n], u[n], pu);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) pu += __shfl_xor_sync(0xffffffffu, pu, o);
+#pragma unroll
+        for (int n = 0; n < NK; ++n) u[n] -= lb * pu * pp[n];
+      }
+      store_vec<TO, NK>(reinterpret_cast<TO*>(p.u) + tok * DK + lane * NK, u);
+#pragma unroll
+      for (int n = 0; n < NK; ++n) kp[n] = k[n];
+    }
+  }
+  if (nstep && t1 == p.T && p.kprev_out) {
+#pragma unroll
+    for (int n = 0; n < NK; ++n) p.kprev_out[((int64_t)b * p.H + h) * DK + lane * NK + n] = kp[n];
   }
   // the gates, one token per lane
   for (int t = t0 + lane; t < t1; t += 32) {
@@ -258,7 +322,7 @@ __global__ void __launch_bounds__(32 * TOKS) prologue_kernel(const PrologueParam
       TX* pc = reinterpret_cast<TX*>(cp.cout) + (int64_t)b * cp.csb;
       for (int i = lane; i < (TAPS - 1) * len[c]; i += 32) {
         const int j = i / len[c], ch = i - j * len[c];
-        pc[(int64_t)(h * len[c] + ch) * (TAPS - 1) + j] = stage[(size_t)(t1 - t0 + j) * W + off[c] + ch];
+        pc[(int64_t)(h * len[c] + ch) * (TAPS - 1) + j] = stage[(size_t)(t1 - t0 + lead + j) * W + off[c] + ch];
       }
     }
   }
@@ -322,7 +386,7 @@ constexpr int PROLOGUE_SMEM_MAX = 96 * 1024;
 // Shared memory of one prologue block: the weights and TOKS warps' staged rows.
 size_t prologue_smem(const PrologueParams& p, int run, int es) {
   const size_t W = 2 * (size_t)p.DK + p.DV;
-  return (size_t)p.taps * W * 4 + (size_t)TOKS * (run + p.taps - 1) * W * es;
+  return (size_t)p.taps * W * 4 + (size_t)TOKS * (run + p.taps) * W * es;
 }
 
 template <typename TX, typename TO, int NK, int NV, int TAPS>
@@ -427,6 +491,13 @@ int gdn_layer_prologue(const gdn_prologue_args* a, void* stream) {
   p.B = (int)a->B; p.T = (int)a->T; p.H = (int)a->H; p.DK = (int)a->DK; p.DV = (int)a->DV;
   p.taps = a->conv_size; p.clamp = (a->flags & GDN_PROLOGUE_CLAMP_LA) != 0;
   p.q_scale = a->q_scale; p.eps = a->l2_eps; p.la_min = a->la_min; p.beta_scale = a->beta_scale;
+  p.n_steps = a->n_steps < 1 ? 1 : a->n_steps;
+  if (p.n_steps > 8) return GDN_ERR_SHAPE;
+  if (p.n_steps > 1) {
+    if (!a->u || !a->lam) return GDN_ERR_NULL;
+    if (!a16(a->u) || (a->k_prev_in && !a16(a->k_prev_in))) return GDN_ERR_ALIGN;
+  }
+  p.u = a->u; p.lam = a->lam; p.kprev_in = a->k_prev_in; p.kprev_out = a->k_prev_out;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (a->in_dtype == GDN_DTYPE_BF16)
     return a->out_dtype == GDN_DTYPE_BF16 ? launch_prologue<__nv_bfloat16, __nv_bfloat16>(p, s)

@@ -12,8 +12,9 @@ a call with a cache continues from it (prefill of any length, or one-token decod
 the updated state in it.  The projections are PyTorch GEMMs; the short convolution, the q/k
 norms and the gates run as one CUDA kernel (``ops.layer_prologue``), the token mixing is
 ``ops.gdn_prefill`` / ``ops.gdn_decode_step``, and the output norm and gate one more kernel
-(``ops.layer_epilogue``).  ``fused_io = False`` on a module (or a configuration the kernels do
-not serve: N-step write vectors, conv bias, odd head sizes) keeps those parts in PyTorch.  Calls that
+(``ops.layer_epilogue``); the prologue kernel also computes nsgdn's n-step write vectors (inference
+and decode).  ``fused_io = False`` on a module (or a configuration the kernels do not serve: conv bias,
+odd head sizes, training with n-step write vectors) keeps those parts in PyTorch.  Calls that
 build an autograd graph (training) run the prologue, scan and epilogue forward and backward on the
 CUDA kernels (DK = 128; DV = DK or 2 DK for the fused prologue/epilogue, a multiple of 128 for the
 scan); without a backward kernel for a configuration, those parts run in PyTorch.  There is no
@@ -169,13 +170,22 @@ class NStepGDN(nn.Module):
             q, k, v, la, beta = ops.layer_prologue_train(*parts, self.A_log, self.dt_bias, H=H, DK=DK, DV=DV, b_bias=self.b_bias,
                                                          conv=conv, q_scale=DK**-0.5, la_min=self.la_min, out_dtype=dt)
             new_state = None
-        else:
+        u = None
+        if not train and self.n_steps > 1:  # n-step write vectors computed by the prologue kernel
+            kp = cache.conv.get("k_prev") if cache is not None else None
+            q, k, v, la, beta, new_state, u, k_last = ops.layer_prologue(
+                *parts, self.A_log, self.dt_bias, H=H, DK=DK, DV=DV, b_bias=self.b_bias, conv=conv, conv_state=state,
+                want_state=cache is not None, q_scale=DK**-0.5, la_min=self.la_min, out_dtype=dt, n_steps=self.n_steps,
+                lam=F.softplus(self.lam.float()), k_prev=None if kp is None else kp.reshape(B, H, DK))
+            if cache is not None:
+                cache.conv["k_prev"] = k_last.reshape(B, 1, H, DK)
+        elif not train:
             q, k, v, la, beta, new_state = ops.layer_prologue(
                 *parts, self.A_log, self.dt_bias, H=H, DK=DK, DV=DV, b_bias=self.b_bias, conv=conv, conv_state=state,
                 want_state=cache is not None, q_scale=DK**-0.5, la_min=self.la_min, out_dtype=dt)
         if cache is not None and new_state is not None:
             cache.conv["qkv"] = torch.cat(new_state, 1)
-        y = _mix(q, k, v, la, beta, None, cache, self._impl)
+        y = _mix(q, k, v, la, None if u is not None else beta, u, cache, self._impl)
         if cache is not None:
             cache.seen += T
         g = proj[..., n_qkv:n_qkv + self.n_gate] if self.use_gate else None
@@ -188,8 +198,9 @@ class NStepGDN(nn.Module):
         H, DK, DV = self.H, self.DK, self.DV
         n_qkv = 2 * self.qk_dim + self.v_dim
         proj = self.in_proj(x)
-        if (self.fused_io and self.n_steps == 1 and _fused_ok(DK, DV) and proj.dtype in (torch.bfloat16, torch.float32)
+        if (self.fused_io and _fused_ok(DK, DV) and proj.dtype in (torch.bfloat16, torch.float32)
                 and (self.conv is None or (self.conv.bias is None and self.conv.size <= 4))
+                and (self.n_steps == 1 or (self.n_steps <= 8 and not _training(x, self)))
                 and _fused_allowed(x, self, cache, DK, DV, self.conv.size if self.conv is not None else 1)):
             return self._forward_fused(x, proj, cache)
         qkv, g, ab = proj[..., :n_qkv], proj[..., n_qkv:n_qkv + self.n_gate], proj[..., n_qkv + self.n_gate:n_qkv + self.n_gate + 2 * H]

@@ -81,7 +81,9 @@ class PrologueArgs(ctypes.Structure):
                [(n, ctypes.c_void_p) for n in ("A_log", "dt_bias", "b_bias", "q", "k", "v", "la", "beta")] + \
                [(n, ctypes.c_int64) for n in ("B", "T", "H", "DK", "DV")] + \
                [(n, ctypes.c_int32) for n in ("conv_size", "flags", "in_dtype", "out_dtype")] + \
-               [(n, ctypes.c_float) for n in ("q_scale", "l2_eps", "la_min", "beta_scale")]
+               [(n, ctypes.c_float) for n in ("q_scale", "l2_eps", "la_min", "beta_scale")] + \
+               [(n, ctypes.c_void_p) for n in ("u", "lam", "k_prev_in", "k_prev_out")] + \
+               [("n_steps", ctypes.c_int32), ("reserved", ctypes.c_int32)]
 
 
 class EpilogueArgs(ctypes.Structure):
@@ -583,14 +585,17 @@ def _rows16(t: torch.Tensor) -> torch.Tensor:
 
 
 def layer_prologue(xq, xk, xv, xa, xb, A_log, dt_bias, *, H, DK, DV, b_bias=None, conv=None, conv_state=None,
-                   want_state=False, q_scale=1.0, l2_eps=1e-12, la_min=None, beta_scale=1.0, out_dtype=torch.bfloat16):
+                   want_state=False, q_scale=1.0, l2_eps=1e-12, la_min=None, beta_scale=1.0, out_dtype=torch.bfloat16,
+                   n_steps=1, lam=None, k_prev=None):
     """q, k, v (B, T, H, D) in ``out_dtype`` and la, beta (B, T, H) fp32 from the layer's
     projections, in one CUDA kernel: SiLU(short causal conv) of each projection, l2-normalised q
     (times ``q_scale``) and k, la = -softplus(a + dt_bias) exp(A_log) (clamped at ``la_min``),
     beta = sigmoid(b + b_bias) * beta_scale.  ``conv`` = (wq, wk, wv) weights of shape
     (channels, conv_size) (or the layer's (channels, 1, conv_size)) or None (SiLU only); ``conv_state`` = (cq, ck, cv) of shape
     (B, channels, conv_size - 1) continues a previous call.  Returns (q, k, v, la, beta, new_state)
-    with new_state None unless ``want_state``."""
+    with new_state None unless ``want_state``.  With ``n_steps`` > 1 (nsgdn write vectors, ``lam`` the
+    per-head step sizes, ``k_prev`` (B, H, DK) the previous call's last normalised k or None) it returns
+    (q, k, v, la, beta, new_state, u, k_last) with k_last (B, H, DK) fp32 when ``want_state``."""
     _check_cuda(xq, xk, xv, xa, xb)
     dt = xq.dtype
     if dt not in _DTC or any(t.dtype != dt for t in (xk, xv, xa, xb)):
@@ -612,6 +617,11 @@ def layer_prologue(xq, xk, xv, xa, xb, A_log, dt_bias, *, H, DK, DV, b_bias=None
     A_log, dt_bias = A_log.float().contiguous(), dt_bias.float().contiguous()
     b_bias = None if b_bias is None else b_bias.float().contiguous()
     st = lambda c: 0 if c is None else c.stride(0)
+    nstep = int(n_steps) > 1
+    u = torch.empty(B, T, H, DK, device=dev, dtype=out_dtype) if nstep else None
+    lam32 = lam.float().contiguous() if nstep else None
+    kp_in = k_prev.reshape(B, H, DK).float().contiguous() if (nstep and k_prev is not None) else None
+    kp_out = torch.empty(B, H, DK, device=dev, dtype=torch.float32) if (nstep and want_state) else None
     a = PrologueArgs(
         _ptr(xq), _ptr(xk), _ptr(xv), xq.stride(0), xq.stride(1), xk.stride(0), xk.stride(1), xv.stride(0), xv.stride(1),
         _ptr(xa), _ptr(xb), xa.stride(0), xa.stride(1), xb.stride(0), xb.stride(1),
@@ -620,12 +630,16 @@ def layer_prologue(xq, xk, xv, xa, xb, A_log, dt_bias, *, H, DK, DV, b_bias=None
         st(cout[2] if cout[2] is not None else cin[2]),
         _ptr(A_log), _ptr(dt_bias), _ptr(b_bias), _ptr(q), _ptr(k), _ptr(v), _ptr(la), _ptr(beta),
         B, T, H, DK, DV, taps, GDN_PROLOGUE_CLAMP_LA if la_min is not None else 0, _DTC[dt], _DTC[out_dtype],
-        float(q_scale), float(l2_eps), float(la_min if la_min is not None else 0.0), float(beta_scale))
+        float(q_scale), float(l2_eps), float(la_min if la_min is not None else 0.0), float(beta_scale),
+        _ptr(u), _ptr(lam32), _ptr(kp_in), _ptr(kp_out), int(n_steps) if nstep else 1, 0)
     for t in (xa, xb):
         if t.stride(-1) != 1:
             raise ValueError("gate projections need a unit last stride")
     _check(load_library().gdn_layer_prologue(ctypes.byref(a), ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)))
-    return q, k, v, la, beta, (tuple(cout) if want_state and taps > 1 else None)
+    st = tuple(cout) if want_state and taps > 1 else None
+    if nstep:
+        return q, k, v, la, beta, st, u, kp_out
+    return q, k, v, la, beta, st
 
 
 def layer_epilogue(y, weight, g=None, eps=1e-5, out_dtype=torch.bfloat16):

@@ -164,7 +164,7 @@ int gdn_prefill_fwd_static_workspace(const gdn_prefill_args* args, void* stream)
  *
  * Replaces the torch ops between the projections and the scan in archbench's NStepGDN.forward
  * (archbench/layers/nsgdn.py:520-536: ShortConv nsgdn.py:457-470, F.normalize, the gate and
- * beta; n_steps = 1) and in fla's GatedDeltaNet.forward (fla/layers/gated_deltanet.py:240-279:
+ * beta; the n-step write vector of nsgdn.py:61-75) and in fla's GatedDeltaNet.forward (fla/layers/gated_deltanet.py:240-279:
  * q/k/v_conv1d, the kernel-side l2norm with eps 1e-6, the gate and beta).
  */
 #define GDN_PROLOGUE_CLAMP_LA 1
@@ -202,6 +202,15 @@ typedef struct {
   int32_t in_dtype;   /* gdn_dtype of the projections and conv states */
   int32_t out_dtype;  /* gdn_dtype of q, k, v */
   float q_scale, l2_eps, la_min, beta_scale;
+  /* n-step write vectors (archbench/layers/nsgdn.py:61-75, NStepGDN n_steps > 1): with n_steps > 1 the
+   * kernel also writes u = beta k, then n_steps - 1 times u -= lam beta (p . u) (p - (p . k) k) with
+   * p the previous token's normalised k (k_prev_in before t = 0, zero when NULL). */
+  void* u;            /* [B][T][H][DK] contiguous, dtype out_dtype; required when n_steps > 1 */
+  const float* lam;   /* (H) fp32 step sizes (the layer's softplus(lam)); required when n_steps > 1 */
+  const float* k_prev_in;  /* (B, H, DK) fp32, or NULL */
+  float* k_prev_out;  /* (B, H, DK) fp32 normalised k of token T - 1, or NULL */
+  int32_t n_steps;    /* 0 or 1: no write vectors; 2 .. 8 */
+  int32_t reserved;
 } gdn_prologue_args;
 
 int gdn_layer_prologue(const gdn_prologue_args* args, void* stream);

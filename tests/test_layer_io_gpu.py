@@ -159,3 +159,63 @@ def test_fused_cache_decode_equals_prefill(cls):
     cache = GDNCache()
     parts = [m(x[:, :64], cache=cache)] + [m(x[:, t:t + 1], cache=cache) for t in range(64, 72)]
     assert rel(torch.cat(parts, 1), full) < 5e-3
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("T,conv_size", [(1, 4), (37, 4), (100, 4), (64, 1)])
+@pytest.mark.parametrize("n_steps,with_prev", [(2, False), (2, True), (3, True)])
+def test_prologue_nstep_write_vectors(dtype, T, conv_size, n_steps, with_prev):
+    """nsgdn write vectors u (archbench/layers/nsgdn.py:472-487): u = beta k, then n-1 corrections
+    u -= lam beta (p.u) (p - (p.k) k) with p the previous token's normalised k (the previous call's
+    last k for the first token, zero at the start of a sequence)."""
+    from archbench_b200.nstep import write_direction
+    B, H, DK, DV = 2, 3, 128, 256
+    xq, xk, xv, xa, xb, conv, A_log, dt_bias, b_bias = make(B, T, H, DK, DV, dtype, conv_size=conv_size, seed=T + n_steps)
+    if conv_size == 1:
+        conv = None
+    g_ = torch.Generator(device="cuda").manual_seed(17)
+    lam = torch.rand(H, device="cuda", generator=g_) + 0.5
+    kp = F.normalize(torch.randn(B, H, DK, device="cuda", generator=g_), dim=-1) if with_prev else None
+    kw = dict(q_scale=DK**-0.5, b_bias=b_bias, la_min=-3.0)
+    got = ops.layer_prologue(xq, xk, xv, xa, xb, A_log, dt_bias, H=H, DK=DK, DV=DV, conv=conv, want_state=True,
+                             out_dtype=torch.float32, n_steps=n_steps, lam=lam, k_prev=kp, **kw)
+    assert len(got) == 8
+    want = torch_prologue(xq, xk, xv, xa, xb, A_log, dt_bias, H, DK, DV, conv=conv, **kw)
+    k = want[1]
+    p = torch.cat([(kp if kp is not None else torch.zeros_like(k[:, 0]))[:, None], k[:, :-1]], 1)
+    u = write_direction(k, p, want[4], lam, n_steps)
+    if dtype == torch.float32:
+        assert (got[6] - u).abs().max().item() <= 1e-5, (got[6] - u).abs().max().item()
+        assert (got[7] - k[:, -1]).abs().max().item() <= 1e-5
+    else:  # k itself may differ by one bf16 rounding of the conv output
+        assert rel(got[6], u) < 2e-2 and rel(got[7], k[:, -1]) < 2e-2
+
+
+@pytest.mark.parametrize("expand_v", [1.0, 2.0])
+@pytest.mark.parametrize("n_steps", [2, 3])
+def test_nstep_layer_fused_matches_torch_path(expand_v, n_steps):
+    torch.manual_seed(13)
+    m = NStepGDN(256, num_heads=2, head_dim=128, expand_v=expand_v, n_steps=n_steps, la_min=-4.0).cuda()
+    x = torch.randn(2, 100, 256, device="cuda")
+    m.fused_io = True
+    a = m(x)
+    m.fused_io = False
+    b = m(x)
+    assert rel(a, b) < 2e-3, rel(a, b)
+
+
+@pytest.mark.parametrize("fused_prefill,fused_decode", [(True, True), (True, False), (False, True)])
+def test_nstep_cache_decode_equals_prefill(fused_prefill, fused_decode):
+    """A prefill then token-by-token decode through the cache (conv state and the last k carried between
+    calls) gives the one-call output; the fused and PyTorch paths share the cache layout."""
+    torch.manual_seed(14)
+    m = NStepGDN(256, num_heads=2, head_dim=128, expand_v=2.0, n_steps=2).cuda()
+    x = torch.randn(2, 72, 256, device="cuda")
+    m.fused_io = True
+    full = m(x)
+    cache = GDNCache()
+    m.fused_io = fused_prefill
+    parts = [m(x[:, :64], cache=cache)]
+    m.fused_io = fused_decode
+    parts += [m(x[:, t:t + 1], cache=cache) for t in range(64, 72)]
+    assert rel(torch.cat(parts, 1), full) < 5e-3
