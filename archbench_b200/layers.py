@@ -193,7 +193,11 @@ class NStepGDN(nn.Module):
         o = epi(y, self.norm.weight, g, eps=self.norm.eps, out_dtype=x.dtype)
         return self.o_proj(o)
 
+    bound_cache: Optional[GDNCache] = None  # used when called without a cache (decode.bind_caches)
+
     def forward(self, x: torch.Tensor, cache: Optional[GDNCache] = None) -> torch.Tensor:
+        if cache is None:
+            cache = self.bound_cache
         B, T, _ = x.shape
         H, DK, DV = self.H, self.DK, self.DV
         n_qkv = 2 * self.qk_dim + self.v_dim
@@ -330,7 +334,11 @@ class GatedDeltaNet(nn.Module):
         o = epi(o, self.o_norm.weight, g, eps=self.o_norm.eps, out_dtype=x.dtype)
         return self.o_proj(o)
 
+    bound_cache: Optional[GDNCache] = None  # used when called without a cache (decode.bind_caches)
+
     def forward(self, hidden_states: torch.Tensor, cache: Optional[GDNCache] = None, **kwargs) -> torch.Tensor:
+        if cache is None:
+            cache = self.bound_cache
         x = hidden_states
         B, T, _ = x.shape
         want = cache is not None

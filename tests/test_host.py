@@ -113,3 +113,37 @@ def test_config_table_matches_baseline():
     assert (c["cfg1"].B, c["cfg1"].T, c["cfg1"].H, c["cfg1"].DK) == (8, 4096, 8, 128)
     assert (c["cfg2"].B, c["cfg2"].H) == (256, 16)
     assert (c["cfg3"].B, c["cfg3"].T, c["cfg3"].H) == (1, 65536, 32)
+
+
+def test_bind_caches_host_checks():
+    """Cache binding is host logic: every mixer must carry state; smear must be off."""
+    import torch.nn as nn
+
+    from archbench_b200.decode import bind_caches
+    from archbench_b200.registry import build_mixer
+
+    class Blk(nn.Module):
+        def __init__(self, mixer):
+            super().__init__()
+            self.mixer = mixer
+
+    m = nn.Module()
+    m.blocks = nn.ModuleList([Blk(build_mixer("nsgdn", 256, 0, 2, num_heads=2, head_dim=128)),
+                              Blk(build_mixer("gdn", 256, 1, 2, num_heads=2, head_dim=128))])
+    m.smear_gate = None
+    with bind_caches(m) as caches:
+        assert len(caches) == 2
+        assert m.blocks[0].mixer.bound_cache is caches[0] and m.blocks[1].mixer.layer.bound_cache is caches[1]
+        with pytest.raises(RuntimeError):
+            with bind_caches(m):
+                pass
+    assert m.blocks[0].mixer.bound_cache is None and m.blocks[1].mixer.layer.bound_cache is None
+    m.smear_gate = nn.Linear(24, 1)
+    with pytest.raises(ValueError, match="smear"):
+        with bind_caches(m):
+            pass
+    m.smear_gate = None
+    m.blocks.append(Blk(nn.Linear(256, 256)))
+    with pytest.raises(ValueError, match="no recurrent state"):
+        with bind_caches(m):
+            pass
