@@ -260,6 +260,8 @@ def _prepare(q, k, u, v, la, beta, s0, output_final_state: bool, out_dtype: torc
 def _prefill_impl(q, k, u, v, la, beta, s0, output_final_state: bool, out_dtype: torch.dtype, impl: str):
     a, y, s_out, _keep = _prepare(q, k, u, v, la, beta, s0, output_final_state, out_dtype, impl)
     lib = load_library()
+    if a.B == 0 or a.H == 0:  # an empty batch: empty outputs, nothing to launch
+        return y, s_out
     ws = None
     with torch.cuda.device(q.device):
         if impl in ("auto", "segmented"):

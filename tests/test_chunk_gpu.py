@@ -216,3 +216,19 @@ def test_prefill_from_host_buffers(pieces):
         g = {n: t[b0:b1].cuda() for n, t in x.items()}
         y, _ = ops.gdn_prefill(g["q"], g["k"], g["v"], g["la"], beta=g["beta"])
         assert torch.equal(y.cpu(), y_host[b0:b1]), (b0, b1)
+
+
+@pytest.mark.parametrize("impl", ["auto"] + VARIANTS)
+def test_empty_inputs(impl):
+    """T = 0: no token is read or written and S_T = S_0; B = 0: empty outputs."""
+    B, H = 2, 2
+    x = make_inputs(B, 64, H, 128, 128, seed=5, dtype=torch.bfloat16, device="cuda")
+    S0 = torch.randn(B, H, 128, 128, device="cuda")
+    e = {n: t[:, :0] for n, t in x.items()}
+    y, S = ops.gdn_prefill(e["q"], e["k"], e["v"], e["la"], beta=e["beta"], initial_state=S0, output_final_state=True,
+                           impl=impl)
+    assert y.shape == (B, 0, H, 128) and torch.equal(S, S0)
+    e = {n: t[:0] for n, t in x.items()}
+    y, S = ops.gdn_prefill(e["q"], e["k"], e["v"], e["la"], beta=e["beta"], output_final_state=True, impl=impl)
+    assert y.shape == (0, 64, H, 128) and S.shape == (0, H, 128, 128)
+    assert ops.device_status() == 0
