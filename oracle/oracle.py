@@ -7,7 +7,7 @@ vector of nsgdn.py:61-75 (``write_direction``).  It exists to check the CUDA ker
 of ``bench.py`` may import it.  The product path (``archbench_b200``) never calls it.
 
 Pinning: ``tests/golden/make_golden.py`` ran archbench's own ``nsgdn_ref`` (and fla 0.5.1's
-``naive_recurrent_gated_delta_rule``, the second naive recurrence the survey found) on seeded
+``naive_recurrent_gated_delta_rule``, a second, independent naive recurrence) on seeded
 inputs and stored the outputs under ``tests/golden/``; ``tests/test_oracle.py`` checks this
 module against them.
 
