@@ -76,7 +76,8 @@ struct Params {
   void* y;
   gdn_strides sy;
   int B, T, H;
-  int srows;  // state rows per (b, h) of the full state (DV); this launch serves 128 of them
+  int srows;  // state rows per (b, h) of the full state (DV)
+  int nsl;    // 128-row state slices per (b, h): CTA (bh, sl) serves rows [128 sl, 128 sl + 128)
 };
 
 // Byte offset of 16-byte chunk `c` (0..7) of row `r` in a 128-byte-row, 128B-swizzled tile.
@@ -155,7 +156,8 @@ __global__ void __launch_bounds__(NT, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int bh = blockIdx.x, b = bh / p.H, h = bh % p.H;
+  const int bh = blockIdx.x / p.nsl, sl = blockIdx.x % p.nsl, b = bh / p.H, h = bh % p.H;
+  const int dv0 = sl * D;  // first state row (v / y column) of this CTA's slice
   const int nchunks = (p.T + C - 1) / C;
 
   float* la_s = reinterpret_cast<float*>(sm + LY::SMALL);
@@ -193,7 +195,7 @@ __global__ void __launch_bounds__(NT, 1)
 
   // Initial state -> TMEM (thread i owns state row i).
   {
-    const float* src = p.s0 ? p.s0 + ((int64_t)bh * p.srows + tid) * D : nullptr;
+    const float* src = p.s0 ? p.s0 + ((int64_t)bh * p.srows + dv0 + tid) * D : nullptr;
 #pragma unroll 1
     for (int c4 = 0; c4 < 4; ++c4) {
       float v[32];
@@ -216,8 +218,8 @@ __global__ void __launch_bounds__(NT, 1)
     ptx::tma_load_4d(st + LY::KQ + 1 * TILE, &tm_q, bar, 0, h, t0, b);
     ptx::tma_load_4d(st + LY::KQ + 2 * TILE, &tm_k, bar, 64, h, t0, b);
     ptx::tma_load_4d(st + LY::KQ + 3 * TILE, &tm_q, bar, 64, h, t0, b);
-    ptx::tma_load_4d(st + LY::V + 0 * TILE, &tm_v, bar, 0, h, t0, b);
-    ptx::tma_load_4d(st + LY::V + 1 * TILE, &tm_v, bar, 64, h, t0, b);
+    ptx::tma_load_4d(st + LY::V + 0 * TILE, &tm_v, bar, dv0, h, t0, b);
+    ptx::tma_load_4d(st + LY::V + 1 * TILE, &tm_v, bar, dv0 + 64, h, t0, b);
     if (HAS_U) {
       ptx::tma_load_4d(st + LY::U + 0 * TILE, &tm_u, bar, 0, h, t0, b);
       ptx::tma_load_4d(st + LY::U + 1 * TILE, &tm_u, bar, 64, h, t0, b);
@@ -457,7 +459,7 @@ __global__ void __launch_bounds__(NT, 1)
 
     // ---- y_t = gamma_t Z + Yi (thread i writes feature i of every token) ----
     {
-      TOut* yb = static_cast<TOut*>(p.y) + (int64_t)b * p.sy.b + (int64_t)h * p.sy.h + tid;
+      TOut* yb = static_cast<TOut*>(p.y) + (int64_t)b * p.sy.b + (int64_t)h * p.sy.h + dv0 + tid;
       const int nvalid = min(C, p.T - t0);
 #pragma unroll 1
       for (int half = 0; half < 2; ++half) {
@@ -477,7 +479,7 @@ __global__ void __launch_bounds__(NT, 1)
   }
 
   if (!abort && p.s_out != nullptr) {
-    float* dst = p.s_out + ((int64_t)bh * p.srows + tid) * D;
+    float* dst = p.s_out + ((int64_t)bh * p.srows + dv0 + tid) * D;
 #pragma unroll 1
     for (int c4 = 0; c4 < 4; ++c4) {
       float v[32];
@@ -514,10 +516,10 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 // [B][T][H][D] bf16 view -> 4-D tensor map (d, h, t, b), box 64 x 1 x 64 x 1, 128B swizzle.
-bool make_map(CUtensorMap* m, const void* base, const gdn_prefill_args* a, const gdn_strides& s) {
+bool make_map(CUtensorMap* m, const void* base, const gdn_prefill_args* a, const gdn_strides& s, int64_t width = D) {
   auto fn = encode_fn();
   if (!fn) return false;
-  cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)a->H, (cuuint64_t)a->T, (cuuint64_t)a->B};
+  cuuint64_t dims[4] = {(cuuint64_t)width, (cuuint64_t)a->H, (cuuint64_t)a->T, (cuuint64_t)a->B};
   cuuint64_t strides[3] = {(cuuint64_t)s.h * 2, (cuuint64_t)s.t * 2, (cuuint64_t)s.b * 2};
   cuuint32_t box[4] = {64, 1, (cuuint32_t)C, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
@@ -531,7 +533,7 @@ template <bool HAS_U, int STAGES, typename TOut>
 int launch(const gdn_prefill_args* a, cudaStream_t stream) {
   using LY = Layout<HAS_U, STAGES>;
   CUtensorMap mq, mk, mv, mu;
-  if (!make_map(&mq, a->q, a, a->sq) || !make_map(&mk, a->k, a, a->sk) || !make_map(&mv, a->v, a, a->sv))
+  if (!make_map(&mq, a->q, a, a->sq) || !make_map(&mk, a->k, a, a->sk) || !make_map(&mv, a->v, a, a->sv, a->DV))
     return GDN_ERR_LAUNCH;
   if (HAS_U) {
     if (!make_map(&mu, a->u, a, a->su)) return GDN_ERR_LAUNCH;
@@ -548,20 +550,15 @@ int launch(const gdn_prefill_args* a, cudaStream_t stream) {
   Params p;
   p.beta = a->beta; p.la = a->la; p.B = (int)a->B; p.T = (int)a->T; p.H = (int)a->H; p.sy = a->sy;
   p.srows = (int)a->DV;
-  // The state's rows are independent: a DV = 128 n state runs as n launches, each over 128 rows with its
-  // own v columns, y columns and state rows (q, k, u and the gates shared).
-  for (int sl = 0; sl < (int)(a->DV / D); ++sl) {
-    if (sl > 0) {
-      gdn_prefill_args b = *a;
-      b.v = static_cast<const __nv_bfloat16*>(a->v) + (size_t)sl * D;
-      if (!make_map(&mv, b.v, &b, a->sv)) return GDN_ERR_LAUNCH;
-    }
-    p.s0 = a->s0 ? a->s0 + (size_t)sl * D * D : nullptr;
-    p.s_out = a->s_out ? a->s_out + (size_t)sl * D * D : nullptr;
-    p.y = static_cast<TOut*>(a->y) + (size_t)sl * D;
-    kern<<<(unsigned)(a->B * a->H), NT, LY::DYN, stream>>>(mq, mk, mv, mu, p);
-    if (cudaGetLastError() != cudaSuccess) return GDN_ERR_LAUNCH;
-  }
+  // The state's rows are independent: a DV = 128 n state runs as n CTAs per (b, h), each over 128 rows
+  // with its own v columns, y columns and state rows (q, k, u and the gates shared, read through L2 by
+  // the n neighbouring CTAs), all in one launch.
+  p.nsl = (int)(a->DV / D);
+  p.s0 = a->s0;
+  p.s_out = a->s_out;
+  p.y = a->y;
+  kern<<<(unsigned)(a->B * a->H * p.nsl), NT, LY::DYN, stream>>>(mq, mk, mv, mu, p);
+  if (cudaGetLastError() != cudaSuccess) return GDN_ERR_LAUNCH;
   return GDN_OK;
 }
 
@@ -575,7 +572,7 @@ bool tma_ok(const void* ptr, const gdn_strides& s) {
 
 // The chunked path: the warp-specialised kernel (gdn_chunk_ws_sm100.cu) for u = beta k with
 // DV any multiple of 128, and this single-warp-group kernel for an explicit write vector u
-// (nsgdn n_steps > 1) with DV a multiple of 128 (one launch per 128 state rows).  Both need 16-byte-aligned rows for TMA.
+// (nsgdn n_steps > 1) with DV a multiple of 128 (one CTA per 128 state rows, all in one launch).  Both need 16-byte-aligned rows for TMA.
 bool gdn_chunk_supported(const gdn_prefill_args* a) {
   using namespace gdn::chunk;
   if (a->in_dtype != GDN_DTYPE_BF16 || a->DK != D || a->T < 1) return false;

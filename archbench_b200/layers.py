@@ -13,8 +13,9 @@ the updated state in it.  The projections are PyTorch GEMMs; the short convoluti
 norms and the gates run as one CUDA kernel (``ops.layer_prologue``), the token mixing is
 ``ops.gdn_prefill`` / ``ops.gdn_decode_step``, and the output norm and gate one more kernel
 (``ops.layer_epilogue``); the prologue kernel also computes nsgdn's n-step write vectors (inference
-and decode).  ``fused_io = False`` on a module (or a configuration the kernels do not serve: conv bias,
-odd head sizes, training with n-step write vectors) keeps those parts in PyTorch.  Calls that
+and decode; in training they are computed by PyTorch ops between the fused prologue and the scan).
+``fused_io = False`` on a module (or a configuration the kernels do not serve: conv bias, odd head
+sizes) keeps those parts in PyTorch.  Calls that
 build an autograd graph (training) run the prologue, scan and epilogue forward and backward on the
 CUDA kernels (DK = 128; DV = DK or 2 DK for the fused prologue/epilogue, a multiple of 128 for the
 scan); without a backward kernel for a configuration, those parts run in PyTorch.  There is no
@@ -160,18 +161,24 @@ class NStepGDN(nn.Module):
         dt = torch.bfloat16 if (DK == 128 and self._impl != "recurrent") else torch.float32
         parts = (proj[..., :qd], proj[..., qd:2 * qd], proj[..., 2 * qd:n_qkv], proj[..., ab0:ab0 + H], proj[..., ab0 + H:ab0 + 2 * H])
         train = _training(x, self)
-        if train and dt == torch.bfloat16:
+        if train and dt == torch.bfloat16 and self.n_steps == 1:
             # the whole mixer as one autograd node: the projection's gradient is written once
             cw = None if self.conv is None else self.conv.weight.reshape(n_qkv, -1).float()
             o = ops.NsgdnMixerTrain.apply(proj, cw, self.A_log, self.dt_bias, self.b_bias, self.norm.weight,
                                           (H, DK, DV, self.n_gate, DK**-0.5, self.la_min, self.norm.eps, self._impl))
             return self.o_proj(o)
+        u = None
         if train:
             q, k, v, la, beta = ops.layer_prologue_train(*parts, self.A_log, self.dt_bias, H=H, DK=DK, DV=DV, b_bias=self.b_bias,
                                                          conv=conv, q_scale=DK**-0.5, la_min=self.la_min, out_dtype=dt)
             new_state = None
-        u = None
-        if not train and self.n_steps > 1:  # n-step write vectors computed by the prologue kernel
+            if self.n_steps > 1:  # write vectors through autograd (no cache in training: zero before token 0)
+                from .nstep import write_direction
+
+                kf = k.float()
+                p = F.pad(kf[:, :-1], (0, 0, 0, 0, 1, 0))
+                u = write_direction(kf, p, beta, F.softplus(self.lam.float()), self.n_steps).to(dt)
+        elif self.n_steps > 1:  # n-step write vectors computed by the prologue kernel
             kp = cache.conv.get("k_prev") if cache is not None else None
             q, k, v, la, beta, new_state, u, k_last = ops.layer_prologue(
                 *parts, self.A_log, self.dt_bias, H=H, DK=DK, DV=DV, b_bias=self.b_bias, conv=conv, conv_state=state,
@@ -179,7 +186,7 @@ class NStepGDN(nn.Module):
                 lam=F.softplus(self.lam.float()), k_prev=None if kp is None else kp.reshape(B, H, DK))
             if cache is not None:
                 cache.conv["k_prev"] = k_last.reshape(B, 1, H, DK)
-        elif not train:
+        else:
             q, k, v, la, beta, new_state = ops.layer_prologue(
                 *parts, self.A_log, self.dt_bias, H=H, DK=DK, DV=DV, b_bias=self.b_bias, conv=conv, conv_state=state,
                 want_state=cache is not None, q_scale=DK**-0.5, la_min=self.la_min, out_dtype=dt)
@@ -204,7 +211,7 @@ class NStepGDN(nn.Module):
         proj = self.in_proj(x)
         if (self.fused_io and _fused_ok(DK, DV) and proj.dtype in (torch.bfloat16, torch.float32)
                 and (self.conv is None or (self.conv.bias is None and self.conv.size <= 4))
-                and (self.n_steps == 1 or (self.n_steps <= 8 and not _training(x, self)))
+                and self.n_steps <= 8
                 and _fused_allowed(x, self, cache, DK, DV, self.conv.size if self.conv is not None else 1)):
             return self._forward_fused(x, proj, cache)
         qkv, g, ab = proj[..., :n_qkv], proj[..., n_qkv:n_qkv + self.n_gate], proj[..., n_qkv + self.n_gate:n_qkv + self.n_gate + 2 * H]

@@ -369,9 +369,17 @@ def bench_layer(args, rank, world):
     t_i = timed(infer, steps, min(args.warmup, 3), world) / steps
     t_t = timed(train, steps, min(args.warmup, 3), world) / steps
     tok = c.B * c.T
-    return {"config": "nsgdn layer, B8 T4096 d_model 1024 H8 head_dim 128, bf16", "infer_ms": t_i * 1e3,
+    # archbench's default nsgdn layer keys (configs/arch/nsgdn.yaml: expand_v 2, n_steps 2)
+    del m
+    m = NStepGDN(1024, num_heads=c.H, head_dim=c.DK, expand_v=2.0, n_steps=2).cuda().to(torch.bfloat16)
+    t_i2 = timed(infer, steps, min(args.warmup, 3), world) / steps
+    t_t2 = timed(train, steps, min(args.warmup, 3), world) / steps
+    return {"config": "nsgdn layer, B8 T4096 d_model 1024 H8 head_dim 128 expand_v 1 n_steps 1, bf16", "infer_ms": t_i * 1e3,
             "infer_tok_s": world * tok / t_i, "train_step_ms": t_t * 1e3, "train_tok_s": world * tok / t_t,
-            "gpu_launches": 12 * steps}
+            "default_keys": {"config": "the same with expand_v 2, n_steps 2 (archbench's nsgdn defaults)",
+                             "infer_ms": t_i2 * 1e3, "infer_tok_s": world * tok / t_i2, "train_step_ms": t_t2 * 1e3,
+                             "train_tok_s": world * tok / t_t2},
+            "gpu_launches": 24 * steps}
 
 
 def bench_long_context(args, rank, world):

@@ -81,13 +81,15 @@ def test_epilogue_backward_matches_torch(ydt, gate):
         assert r <= tol, f"{n}: rel-L2 {r:.3e}"
 
 
-@pytest.mark.parametrize("cls,expand_v", [("nsgdn", 1.0), ("nsgdn", 2.0), ("gdn", 1.0), ("gdn", 2.0)])
-def test_layer_training_fused_matches_torch_path(cls, expand_v):
+@pytest.mark.parametrize("cls,expand_v,n_steps", [("nsgdn", 1.0, 1), ("nsgdn", 2.0, 1), ("nsgdn", 2.0, 2), ("nsgdn", 1.0, 3),
+                                                   ("gdn", 1.0, 1), ("gdn", 2.0, 1)])
+def test_layer_training_fused_matches_torch_path(cls, expand_v, n_steps):
     """Parameter gradients of a training step on the fused kernels (prologue, scan, epilogue forward and
-    backward) against the same layer with its prologue/epilogue in PyTorch."""
+    backward; nsgdn's n-step write vectors through autograd between prologue and scan) against the
+    same layer with its prologue/epilogue in PyTorch."""
     torch.manual_seed(3)
     if cls == "nsgdn":
-        m = NStepGDN(256, num_heads=2, head_dim=128, expand_v=expand_v, n_steps=1).cuda()
+        m = NStepGDN(256, num_heads=2, head_dim=128, expand_v=expand_v, n_steps=n_steps).cuda()
     else:
         m = GatedDeltaNet(hidden_size=256, expand_v=expand_v, head_dim=128, num_heads=2).cuda()
     x = torch.randn(2, 100, 256, device="cuda")
@@ -102,4 +104,4 @@ def test_layer_training_fused_matches_torch_path(cls, expand_v):
     assert set(got) == set(want) and len(got) >= 6
     for n in want:
         r = rel(got[n], want[n])
-        assert r <= 2e-2, f"{cls} expand_v={expand_v} {n}: rel-L2 {r:.3e}"
+        assert r <= 2e-2, f"{cls} expand_v={expand_v} n_steps={n_steps} {n}: rel-L2 {r:.3e}"
