@@ -570,9 +570,10 @@ bool tma_ok(const void* ptr, const gdn_strides& s) {
 }  // namespace chunk
 }  // namespace gdn
 
-// The chunked path: the warp-specialised kernel (gdn_chunk_ws_sm100.cu) for u = beta k with
-// DV any multiple of 128, and this single-warp-group kernel for an explicit write vector u
-// (nsgdn n_steps > 1) with DV a multiple of 128 (one CTA per 128 state rows, all in one launch).  Both need 16-byte-aligned rows for TMA.
+// The chunked path: the warp-specialised kernel (gdn_chunk_ws_sm100.cu) for DV any multiple of
+// 128, with u = beta k or an explicit write vector u (nsgdn n_steps > 1), where y's rows are 16-byte
+// aligned (it stores y by TMA); this single-warp-group kernel for an explicit u with any y strides
+// (one CTA per 128 state rows, all in one launch).  Both need 16-byte-aligned q/k/u/v rows for TMA.
 bool gdn_chunk_supported(const gdn_prefill_args* a) {
   using namespace gdn::chunk;
   if (a->in_dtype != GDN_DTYPE_BF16 || a->DK != D || a->T < 1) return false;
@@ -585,7 +586,7 @@ bool gdn_chunk_supported(const gdn_prefill_args* a) {
 
 int gdn_launch_chunk_sm100(const gdn_prefill_args* a, cudaStream_t stream) {
   using namespace gdn::chunk;
-  if (a->u == nullptr) return gdn_launch_chunk_ws(a, stream);
+  if (gdn_chunk_ws_supported(a)) return gdn_launch_chunk_ws(a, stream);
   return a->out_dtype == GDN_DTYPE_BF16 ? launch<true, 1, __nv_bfloat16>(a, stream) : launch<true, 1, float>(a, stream);
 }
 

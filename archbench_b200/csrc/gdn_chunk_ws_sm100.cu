@@ -78,10 +78,18 @@ struct Params {
 
 __device__ int g_status = 0;
 
-template <typename TOut>
+// HAS_U: an explicit write vector u (nsgdn n_steps > 1) replaces beta k where the state is written
+// (G = [K;Q] U^T for L and A, S += (R diag w)^T U with w free of beta); its tiles ride in the q/k
+// ring, which is then two entries of [K0][Q0][K1][Q1][U0][U1] instead of three of [K0][Q0][K1][Q1].
+template <bool HAS_U, typename TOut>
 __global__ void __launch_bounds__(NT, 1)
     ws_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-              const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_y, const Params p) {
+              const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_y,
+              const __grid_constant__ CUtensorMap tm_u, const Params p) {
+  constexpr int NR = HAS_U ? 2 : 3;                       // ring entries
+  constexpr uint32_t KQB = HAS_U ? 6 * TILE : KQ_BYTES;   // bytes per ring entry
+  constexpr int NCONV = HAS_U ? 6 : 4;                    // tiles converted to fp16 in place
+  static_assert(NR * KQB == 3 * KQ_BYTES, "the ring keeps its footprint");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sb = ptx::smem_u32(sm);
@@ -125,6 +133,7 @@ __global__ void __launch_bounds__(NT, 1)
     ptx::prefetch_tensormap(&tm_k);
     ptx::prefetch_tensormap(&tm_v);
     ptx::prefetch_tensormap(&tm_y);
+    if (HAS_U) ptx::prefetch_tensormap(&tm_u);
   }
   ptx::tc_fence_before();
   __syncthreads();
@@ -141,14 +150,18 @@ __global__ void __launch_bounds__(NT, 1)
     return !ptx::named_bar_or(group, n, fail);
   };
   auto issue_kq = [&](int c) {
-    uint8_t* dst = sm + KQ + (c % 3) * KQ_BYTES;
-    uint64_t* bar = &bars[B_KQ + c % 3];
-    ptx::mbar_arrive_expect_tx(bar, KQ_BYTES);
+    uint8_t* dst = sm + KQ + (c % NR) * KQB;
+    uint64_t* bar = &bars[B_KQ + c % NR];
+    ptx::mbar_arrive_expect_tx(bar, KQB);
     const int t0 = (cb + c) * C;
     ptx::tma_load_4d(dst + 0 * TILE, &tm_k, bar, 0, h, t0, b);
     ptx::tma_load_4d(dst + 1 * TILE, &tm_q, bar, 0, h, t0, b);
     ptx::tma_load_4d(dst + 2 * TILE, &tm_k, bar, 64, h, t0, b);
     ptx::tma_load_4d(dst + 3 * TILE, &tm_q, bar, 64, h, t0, b);
+    if (HAS_U) {
+      ptx::tma_load_4d(dst + 4 * TILE, &tm_u, bar, 0, h, t0, b);
+      ptx::tma_load_4d(dst + 5 * TILE, &tm_u, bar, 64, h, t0, b);
+    }
   };
   auto issue_v = [&](int c) {
     uint8_t* dst = sm + VB + (c & 1) * V_BYTES;
@@ -183,8 +196,11 @@ __global__ void __launch_bounds__(NT, 1)
       ga0 = ga1 = gb0 = gb1 = 0.f;
       const int t0 = (cb + c) * C;
       const int64_t gi = ((int64_t)b * p.T + t0) * p.H + h;
-      if (t0 + lane < p.T) { ga0 = p.la[gi + (int64_t)lane * p.H]; gb0 = p.beta[gi + (int64_t)lane * p.H]; }
-      if (t0 + lane + 32 < p.T) { ga1 = p.la[gi + (int64_t)(lane + 32) * p.H]; gb1 = p.beta[gi + (int64_t)(lane + 32) * p.H]; }
+      if (t0 + lane < p.T) { ga0 = p.la[gi + (int64_t)lane * p.H]; gb0 = HAS_U ? 1.f : p.beta[gi + (int64_t)lane * p.H]; }
+      if (t0 + lane + 32 < p.T) {
+        ga1 = p.la[gi + (int64_t)(lane + 32) * p.H];
+        gb1 = HAS_U ? 1.f : p.beta[gi + (int64_t)(lane + 32) * p.H];
+      }
     };
     if (ww == 1) load_gates(0);
     if (leader && !virt && nch > 0) {
@@ -232,7 +248,7 @@ __global__ void __launch_bounds__(NT, 1)
 #pragma unroll 1
     for (; c < nch; ++c) {
       const int pb = c & 1;
-      const uint32_t kq_o = KQ + (c % 3) * KQ_BYTES;
+      const uint32_t kq_o = KQ + (c % NR) * KQB;
       uint8_t* kq = sm + kq_o;
       const uint32_t v_o = VB + pb * V_BYTES;
       float* la_s = small + (c % 3) * SLOT;
@@ -242,13 +258,14 @@ __global__ void __launch_bounds__(NT, 1)
       float* w_s = gam_s + C;
       float* misc_s = w_s + C;
 
-      if (!gwait(B_KQ + c % 3, (uint32_t)(c / 3) & 1u, leader, 1, NWORK)) break;
-      if (leader) {  // G = [K;Q] K^T from the bf16 tiles as loaded
+      if (!gwait(B_KQ + c % NR, (uint32_t)(c / NR) & 1u, leader, 1, NWORK)) break;
+      if (leader) {  // G = [K;Q] K^T (or [K;Q] U^T) from the bf16 tiles as loaded
         ptx::tc_fence_after();
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           const uint64_t a = at(D_K, kq_o + (k >> 2) * 2 * TILE + (k & 3) * 32);
-          ptx::mma_f16_ss(tmem + COL_G, a, a, ID_G, k > 0);
+          const uint64_t bu = HAS_U ? at(D_K, kq_o + (4 + (k >> 2)) * TILE + (k & 3) * 32) : a;
+          ptx::mma_f16_ss(tmem + COL_G, a, bu, ID_G, k > 0);
         }
         ptx::mma_commit(&bars[B_G]);
         issued = true;
@@ -297,9 +314,10 @@ __global__ void __launch_bounds__(NT, 1)
       if (leader) issued = false;
       ptx::tc_fence_after();
 
-      // bf16 -> fp16 in place: K (tiles 0, 2) and gamma-scaled Q (tiles 1, 3).  V stays bf16.
+      // bf16 -> fp16 in place: K (tiles 0, 2), gamma-scaled Q (tiles 1, 3) and U (tiles 4, 5).  V
+      // stays bf16.
 #pragma unroll 4
-      for (int i = wt; i < 4 * 512; i += NWORK) {
+      for (int i = wt; i < NCONV * 512; i += NWORK) {
         const int tile = i >> 9;
         uint8_t* base = kq + tile * TILE;
         const int off = (i & 511) * 16;
@@ -505,17 +523,32 @@ __global__ void __launch_bounds__(NT, 1)
 #pragma unroll 1
     for (int c = 0; c < nch; ++c) {
       const int pb = c & 1;
-      const uint32_t kq_o = KQ + (c % 3) * KQ_BYTES;
+      const uint32_t kq_o = KQ + (c % NR) * KQB;
       const float* slot = small + (c % 3) * SLOT;
       const float* w_s = slot + 4 * C;
+      // The next tile load goes into the ring entry of chunk c-1, freed by S(c-1).  With two entries
+      // (HAS_U) it is chunk c+1's, which prep(c+1) waits for, so it is issued before waiting for prep(c).
+      if (HAS_U) {
+        if (c > 0) {
+          if (!gwait(B_S, (uint32_t)(c - 1) & 1u, leader, 2, 128)) break;
+          if (leader) issued = false;
+        }
+        ptx::tc_fence_after();
+        const int nxt = c + NR - 1;
+        if (leader && nxt < nch && nxt >= kq_issued) { issue_kq(nxt); kq_issued = nxt + 1; }
+      }
       if (!gwait(B_PREP, (uint32_t)c & 1u, leader, 2, 128)) break;
       const float gC = slot[5 * C];  // written by prep(c): read only after its ready barrier
-      if (c > 0) {
-        if (!gwait(B_S, (uint32_t)(c - 1) & 1u, leader, 2, 128)) break;
-        if (leader) issued = false;
+      if (!HAS_U) {
+        if (c > 0) {
+          if (!gwait(B_S, (uint32_t)(c - 1) & 1u, leader, 2, 128)) break;
+          if (leader) issued = false;
+        }
+        ptx::tc_fence_after();
+        const int nxt = c + NR - 1;
+        if (leader && nxt < nch && nxt >= kq_issued) { issue_kq(nxt); kq_issued = nxt + 1; }
       }
       ptx::tc_fence_after();
-      if (leader && c + 2 < nch) { issue_kq(c + 2); kq_issued = c + 3; }  // buffer of chunk c-1, freed by S(c-1)
       // S16 <- fp16(S): four loads, one wait.
       float sv[128];
 #pragma unroll
@@ -583,7 +616,8 @@ __global__ void __launch_bounds__(NT, 1)
         ptx::tc_fence_after();
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          ptx::mma_f16_ss(tmem + COL_S, at(D_K, SR + 2 * TILE + k * 32), at(D_MN16K, kq_o + k * 2048), ID_N128_BMN, 1);
+          ptx::mma_f16_ss(tmem + COL_S, at(D_K, SR + 2 * TILE + k * 32),
+                          HAS_U ? at(D_MN8K, kq_o + 4 * TILE + k * 2048) : at(D_MN16K, kq_o + k * 2048), ID_N128_BMN, 1);
         if (want_y) {
 #pragma unroll
           for (int k = 0; k < 4; ++k)
@@ -617,8 +651,8 @@ __global__ void __launch_bounds__(NT, 1)
         ptx::mma_commit(&bars[B_DRAIN + 1]);
         ptx::mbar_wait_bounded(&bars[B_DRAIN + 1], 0, WAIT_LIMIT);
       }
-      for (int c = kq_issued - 3 < 0 ? 0 : kq_issued - 3; c < kq_issued; ++c)
-        ptx::mbar_wait_bounded(&bars[B_KQ + c % 3], (uint32_t)(c / 3) & 1u, WAIT_LIMIT);
+      for (int c = kq_issued - NR < 0 ? 0 : kq_issued - NR; c < kq_issued; ++c)
+        ptx::mbar_wait_bounded(&bars[B_KQ + c % NR], (uint32_t)(c / NR) & 1u, WAIT_LIMIT);
     }
   }
 
@@ -635,13 +669,19 @@ struct Segmentation {
   float* seg_out = nullptr;
 };
 
-template <typename TOut>
+template <bool HAS_U, typename TOut>
 int launch(const gdn_prefill_args* a, const Segmentation& sg, cudaStream_t stream) {
-  CUtensorMap mq, mk, mv, my;
+  CUtensorMap mq, mk, mv, my, mu;
   if (!make_map(&mq, a->q, a->DK, a, a->sq) || !make_map(&mk, a->k, a->DK, a, a->sk) ||
       !make_map(&mv, a->v, a->DV, a, a->sv) || !make_store_map<TOut>(&my, a->y, a->DV, a, a->sy))
     return GDN_ERR_LAUNCH;
-  auto kern = ws_kernel<TOut>;
+  if (HAS_U != (a->u != nullptr) || (HAS_U && sg.mode != 0) || (HAS_U && sg.nseg != 1)) return GDN_ERR_UNSUPPORTED;
+  if (HAS_U) {
+    if (!make_map(&mu, a->u, a->DK, a, a->su)) return GDN_ERR_LAUNCH;
+  } else {
+    mu = mk;
+  }
+  auto kern = ws_kernel<HAS_U, TOut>;
   static bool attr_set = false;
   if (!attr_set) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, DYN) != cudaSuccess)
@@ -662,21 +702,21 @@ int launch(const gdn_prefill_args* a, const Segmentation& sg, cudaStream_t strea
   p.ws_stride = sg.ws_stride;
   const int64_t grid = a->B * a->H * (int64_t)p.nseg * p.ntiles;
   if (grid <= 0 || grid > 0x7fffffff) return GDN_ERR_SHAPE;
-  kern<<<(unsigned)grid, NT, DYN, stream>>>(mq, mk, mv, my, p);
+  kern<<<(unsigned)grid, NT, DYN, stream>>>(mq, mk, mv, my, mu, p);
   return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
 }
 
 template <typename TOut>
 int launch(const gdn_prefill_args* a, cudaStream_t stream) {
-  return launch<TOut>(a, Segmentation(), stream);
+  return a->u ? launch<true, TOut>(a, Segmentation(), stream) : launch<false, TOut>(a, Segmentation(), stream);
 }
 
 }  // namespace ws
 }  // namespace gdn
 
-// DK = 128, DV a multiple of 128, u = beta k (no explicit write vector).
+// DK = 128, DV a multiple of 128; u = beta k or an explicit write vector u.
 bool gdn_chunk_ws_supported(const gdn_prefill_args* a) {
-  if (a->u != nullptr || a->DK != 128 || a->DV % 128 != 0 || a->DV < 128) return false;
+  if (a->DK != 128 || a->DV % 128 != 0 || a->DV < 128) return false;
   const int64_t es = a->out_dtype == GDN_DTYPE_BF16 ? 2 : 4;
   auto ok = [&](int64_t x) { return x > 0 && (x * es) % 16 == 0; };
   return a->y && (uintptr_t)a->y % 16 == 0 && ok(a->sy.h) && ok(a->sy.t) && ok(a->sy.b);
@@ -698,8 +738,9 @@ int gdn_launch_chunk_ws_segments(const gdn_prefill_args* a, int mode, int nseg, 
   sg.ws_stride = ws_stride;
   sg.seg_s0 = ws;
   sg.seg_out = ws;
-  return a->out_dtype == GDN_DTYPE_BF16 ? gdn::ws::launch<__nv_bfloat16>(a, sg, stream)
-                                        : gdn::ws::launch<float>(a, sg, stream);
+  if (a->u != nullptr) return GDN_ERR_UNSUPPORTED;  // segments are planned for u = beta k only
+  return a->out_dtype == GDN_DTYPE_BF16 ? gdn::ws::launch<false, __nv_bfloat16>(a, sg, stream)
+                                        : gdn::ws::launch<false, float>(a, sg, stream);
 }
 
 namespace gdn {

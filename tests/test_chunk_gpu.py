@@ -232,3 +232,24 @@ def test_empty_inputs(impl):
     y, S = ops.gdn_prefill(e["q"], e["k"], e["v"], e["la"], beta=e["beta"], output_final_state=True, impl=impl)
     assert y.shape == (0, 64, H, 128) and S.shape == (0, H, 128, 128)
     assert ops.device_status() == 0
+
+
+@pytest.mark.parametrize("T", [100, 192])
+def test_write_vectors_unaligned_y_rows(T):
+    """An explicit u with y rows that are not 16-byte aligned (fp32 y with a row stride of 129
+    elements) cannot take the TMA-storing kernel; the single-warp-group kernel serves it."""
+    import ctypes
+
+    B, H = 2, 2
+    x = make_inputs(B, T, H, 128, 128, seed=31 + T, dtype=torch.bfloat16)
+    u = (x["beta"][..., None] * x["k"].float()).to(torch.bfloat16)
+    y_o, S_o = O.recurrence_c(*(np32(x[n]) for n in ("q", "k", "v", "la")), u=np32(u))
+    g = {k: v.cuda() for k, v in x.items()}
+    a, _, s_out, keep = ops._prepare(g["q"], g["k"], u.cuda(), g["v"], g["la"], None, None, True, torch.float32, "chunk_single")
+    ybuf = torch.full((B, T, H, 129), float("nan"), device="cuda")
+    a.y, a.sy = ybuf.data_ptr(), ops.Strides(T * H * 129, H * 129, 129)
+    ops._check(ops.load_library().gdn_prefill_fwd(ctypes.byref(a), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
+    torch.cuda.synchronize()
+    check(ybuf[..., :128], y_o, "y (u given, unaligned y rows)")
+    check(s_out, S_o, "S_T (u given, unaligned y rows)")
+    assert torch.isnan(ybuf[..., 128]).all()
