@@ -438,6 +438,148 @@ int launch_epi(const EpiBwdParams& p, cudaStream_t s) {
   return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
 }
 
+// ---------------------------------------------------------------------------------------------
+// Backward of nsgdn's n-step write vectors (archbench/layers/nsgdn.py:61-75), per (b, t, h) with
+// p = k_{t-1} (zero at t = 0):
+//   c = p.k,  pp = p - c k,  u_0 = beta k,  s_i = p.u_{i-1},  u_i = u_{i-1} - lam beta s_i pp  (0 < i < n).
+// From g = du_{n-1}, for i = n-1 .. 1 with e = pp.g:
+//   dpp -= lam beta s_i g;  dp -= lam beta e u_{i-1};  dlam -= beta s_i e;  dbeta -= lam s_i e;
+//   g <- g - lam beta e p   (= du_{i-1});
+// then dbeta += k.g, dc = -k.dpp, dk_t += beta g - c dpp + dc p and dp += dpp + dc k, which is token
+// t-1's share of dk.  One warp per (b, h) and run of WV_RUN tokens, walking the run backwards so that
+// each token's dp is in registers when the token before it is finished; the token after the run is
+// recomputed for its dp.  Each lane holds DK/32 consecutive channels; the forward is recomputed in
+// registers (n <= 8).  dlam: one fp32 atomic per run (summation order across runs not fixed).
+constexpr int WV_RUN = 16;
+constexpr int WV_MAXN = 8;
+
+struct WvParams {
+  const void* k;
+  const float* beta;
+  const float* lam;
+  const float* du;
+  float* dk;
+  float* dbeta;
+  float* dlam;
+  int B, T, H, n_steps;
+};
+
+__device__ __forceinline__ float wv_sum(float x) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+  return x;
+}
+
+template <typename TK, int NK>
+__device__ __forceinline__ void wv_token(const WvParams& p, int b, int t, int h, int lane, float lam, float (&dks)[NK],
+                                         float (&dp)[NK], float& dbeta, float& dlam) {
+  const int64_t row = ((int64_t)b * p.T + t) * p.H + h;
+  const TK* kb = static_cast<const TK*>(p.k);
+  float k[NK], pv[NK], g[NK], pp[NK], dpp[NK];
+  load_vec<NK>(kb + row * (NK * 32) + lane * NK, k);
+  if (t > 0) {
+    load_vec<NK>(kb + (row - p.H) * (NK * 32) + lane * NK, pv);
+  } else {
+#pragma unroll
+    for (int i = 0; i < NK; ++i) pv[i] = 0.f;
+  }
+  load_vec<NK>(p.du + row * (NK * 32) + lane * NK, g);
+  const float beta = p.beta[row], lb = lam * beta;
+  float c = 0.f;
+#pragma unroll
+  for (int i = 0; i < NK; ++i) c = fmaf(pv[i], k[i], c);
+  c = wv_sum(c);
+  float u[WV_MAXN][NK], s[WV_MAXN];
+#pragma unroll
+  for (int i = 0; i < NK; ++i) {
+    pp[i] = pv[i] - c * k[i];
+    u[0][i] = beta * k[i];
+    dpp[i] = 0.f;
+    dp[i] = 0.f;
+  }
+  s[0] = 0.f;
+#pragma unroll
+  for (int j = 1; j < WV_MAXN; ++j) {
+    s[j] = 0.f;
+    if (j < p.n_steps) {
+      float sj = 0.f;
+#pragma unroll
+      for (int i = 0; i < NK; ++i) sj = fmaf(pv[i], u[j - 1][i], sj);
+      sj = wv_sum(sj);
+      s[j] = sj;
+#pragma unroll
+      for (int i = 0; i < NK; ++i) u[j][i] = u[j - 1][i] - lb * sj * pp[i];
+    }
+  }
+  dbeta = 0.f;
+  dlam = 0.f;
+#pragma unroll
+  for (int j = WV_MAXN - 1; j >= 1; --j) {
+    if (j < p.n_steps) {
+      float e = 0.f;
+#pragma unroll
+      for (int i = 0; i < NK; ++i) e = fmaf(pp[i], g[i], e);
+      e = wv_sum(e);
+      const float sj = s[j];
+#pragma unroll
+      for (int i = 0; i < NK; ++i) {
+        dpp[i] -= lb * sj * g[i];
+        dp[i] -= lb * e * u[j - 1][i];
+        g[i] -= lb * e * pv[i];
+      }
+      dlam -= beta * sj * e;
+      dbeta -= lam * sj * e;
+    }
+  }
+  float kg = 0.f, kd = 0.f;
+#pragma unroll
+  for (int i = 0; i < NK; ++i) {
+    kg = fmaf(k[i], g[i], kg);
+    kd = fmaf(k[i], dpp[i], kd);
+  }
+  kg = wv_sum(kg);
+  const float dc = -wv_sum(kd);
+  dbeta += kg;
+#pragma unroll
+  for (int i = 0; i < NK; ++i) {
+    dks[i] = beta * g[i] - c * dpp[i] + dc * pv[i];
+    dp[i] += dpp[i] + dc * k[i];
+  }
+}
+
+template <typename TK, int NK>
+__global__ void __launch_bounds__(128) write_vectors_bwd_kernel(const WvParams p) {
+  const int lane = threadIdx.x & 31;
+  const int nrun = (p.T + WV_RUN - 1) / WV_RUN;
+  const int64_t w = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5);
+  if (w >= (int64_t)p.B * p.H * nrun) return;  // whole warps leave together
+  const int r = (int)(w % nrun);
+  const int64_t bh = w / nrun;
+  const int h = (int)(bh % p.H), b = (int)(bh / p.H);
+  const float lam = p.lam[h];
+  const int t0 = r * WV_RUN, t1 = min(p.T, t0 + WV_RUN);
+  float dks[NK], dp[NK], dp_next[NK], db, dl, dl_run = 0.f;
+#pragma unroll
+  for (int i = 0; i < NK; ++i) dp_next[i] = 0.f;
+  if (t1 < p.T) wv_token<TK, NK>(p, b, t1, h, lane, lam, dks, dp_next, db, dl);  // only its dp is used
+#pragma unroll 1
+  for (int t = t1 - 1; t >= t0; --t) {
+    wv_token<TK, NK>(p, b, t, h, lane, lam, dks, dp, db, dl);
+    const int64_t row = ((int64_t)b * p.T + t) * p.H + h;
+    float* dkr = p.dk + row * (NK * 32) + lane * NK;
+    float cur[NK];
+    load_vec<NK>(dkr, cur);
+#pragma unroll
+    for (int i = 0; i < NK; ++i) {
+      dkr[i] = cur[i] + dks[i] + dp_next[i];
+      dp_next[i] = dp[i];
+    }
+    if (lane == 0) p.dbeta[row] = db;
+    dl_run += dl;
+  }
+  if (lane == 0) atomicAdd(p.dlam + h, dl_run);
+}
+
 }  // namespace layer_io_bwd
 }  // namespace gdn
 
@@ -523,6 +665,34 @@ int gdn_layer_epilogue_bwd(const gdn_epilogue_bwd_args* a, void* stream) {
     case 1: return launch_epi<float, float, bf>(p, s);
     default: return launch_epi<float, float, float>(p, s);
   }
+}
+
+int gdn_write_vectors_bwd(const gdn_write_vectors_bwd_args* a, void* stream) {
+  if (!a) return GDN_ERR_NULL;
+  if (!a->k || !a->beta || !a->lam || !a->du || !a->dk || !a->dbeta || !a->dlam) return GDN_ERR_NULL;
+  if (a->B < 1 || a->T < 1 || a->H < 1 || (a->DK != 64 && a->DK != 128) || a->n_steps < 2 || a->n_steps > WV_MAXN)
+    return GDN_ERR_SHAPE;
+  if (a->B * a->T * a->H > 0x3fffffffLL) return GDN_ERR_SHAPE;
+  if (a->k_dtype != GDN_DTYPE_BF16 && a->k_dtype != GDN_DTYPE_F32) return GDN_ERR_DTYPE;
+  if (!a16(a->k) || !a16(a->du) || !a16(a->dk)) return GDN_ERR_ALIGN;
+  if (!device_ok()) return GDN_ERR_DEVICE;
+  WvParams p;
+  p.k = a->k; p.beta = a->beta; p.lam = a->lam; p.du = a->du; p.dk = a->dk; p.dbeta = a->dbeta; p.dlam = a->dlam;
+  p.B = (int)a->B; p.T = (int)a->T; p.H = (int)a->H; p.n_steps = a->n_steps;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(a->dlam, 0, a->H * 4, s) != cudaSuccess) return GDN_ERR_LAUNCH;
+  const int64_t warps = a->B * a->H * ((a->T + WV_RUN - 1) / WV_RUN);
+  const unsigned blocks = (unsigned)((warps + 3) / 4);
+  using bf = __nv_bfloat16;
+  const bool kb = a->k_dtype == GDN_DTYPE_BF16;
+  if (a->DK == 128) {
+    if (kb) write_vectors_bwd_kernel<bf, 4><<<blocks, 128, 0, s>>>(p);
+    else write_vectors_bwd_kernel<float, 4><<<blocks, 128, 0, s>>>(p);
+  } else {
+    if (kb) write_vectors_bwd_kernel<bf, 2><<<blocks, 128, 0, s>>>(p);
+    else write_vectors_bwd_kernel<float, 2><<<blocks, 128, 0, s>>>(p);
+  }
+  return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
 }
 
 }  // extern "C"

@@ -12,10 +12,10 @@ a call with a cache continues from it (prefill of any length, or one-token decod
 the updated state in it.  The projections are PyTorch GEMMs; the short convolution, the q/k
 norms and the gates run as one CUDA kernel (``ops.layer_prologue``), the token mixing is
 ``ops.gdn_prefill`` / ``ops.gdn_decode_step``, and the output norm and gate one more kernel
-(``ops.layer_epilogue``); the prologue kernel also computes nsgdn's n-step write vectors (inference
-and decode; in training they are computed by PyTorch ops between the fused prologue and the scan).
-``fused_io = False`` on a module (or a configuration the kernels do not serve: conv bias, odd head
-sizes) keeps those parts in PyTorch.  Calls that
+(``ops.layer_epilogue``); the prologue kernel also computes nsgdn's n-step write vectors, and in
+training ``gdn_write_vectors_bwd`` differentiates them (fp32 fallbacks for other head sizes use
+PyTorch ops there).  ``fused_io = False`` on a module (or a configuration the kernels do not serve:
+conv bias, odd head sizes) keeps those parts in PyTorch.  Calls that
 build an autograd graph (training) run the prologue, scan and epilogue forward and backward on the
 CUDA kernels (DK = 128; DV = DK or 2 DK for the fused prologue/epilogue, a multiple of 128 for the
 scan); without a backward kernel for a configuration, those parts run in PyTorch.  There is no
@@ -161,11 +161,12 @@ class NStepGDN(nn.Module):
         dt = torch.bfloat16 if (DK == 128 and self._impl != "recurrent") else torch.float32
         parts = (proj[..., :qd], proj[..., qd:2 * qd], proj[..., 2 * qd:n_qkv], proj[..., ab0:ab0 + H], proj[..., ab0 + H:ab0 + 2 * H])
         train = _training(x, self)
-        if train and dt == torch.bfloat16 and self.n_steps == 1:
+        if train and dt == torch.bfloat16:
             # the whole mixer as one autograd node: the projection's gradient is written once
             cw = None if self.conv is None else self.conv.weight.reshape(n_qkv, -1).float()
             o = ops.NsgdnMixerTrain.apply(proj, cw, self.A_log, self.dt_bias, self.b_bias, self.norm.weight,
-                                          (H, DK, DV, self.n_gate, DK**-0.5, self.la_min, self.norm.eps, self._impl))
+                                          F.softplus(self.lam.float()),
+                                          (H, DK, DV, self.n_gate, DK**-0.5, self.la_min, self.norm.eps, self._impl, self.n_steps))
             return self.o_proj(o)
         u = None
         if train:

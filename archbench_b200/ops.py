@@ -125,6 +125,13 @@ class PrologueBwdArgs(ctypes.Structure):
                [(n, ctypes.c_float) for n in ("q_scale", "l2_eps", "la_min", "beta_scale")]
 
 
+class WriteVectorsBwdArgs(ctypes.Structure):
+    """Mirror of gdn_write_vectors_bwd_args (include/gdn_b200.h)."""
+
+    _fields_ = [(n, ctypes.c_void_p) for n in ("k", "beta", "lam", "du", "dk", "dbeta", "dlam")] + \
+               [(n, ctypes.c_int64) for n in ("B", "T", "H", "DK")] + [("k_dtype", ctypes.c_int32), ("n_steps", ctypes.c_int32)]
+
+
 class EpilogueBwdArgs(ctypes.Structure):
     """Mirror of gdn_epilogue_bwd_args (include/gdn_b200.h)."""
 
@@ -148,6 +155,7 @@ SYMBOLS = {
     "gdn_selftest_bounded_wait": ([ctypes.c_longlong, ctypes.c_void_p], ctypes.c_int),
     "gdn_prefill_fwd_static_workspace": ([ctypes.POINTER(PrefillArgs), ctypes.c_void_p], ctypes.c_int),
     "gdn_status_string": ([ctypes.c_int], ctypes.c_char_p),
+    "gdn_write_vectors_bwd": ([ctypes.POINTER(WriteVectorsBwdArgs), ctypes.c_void_p], ctypes.c_int),
     "gdn_abi_version": ([], ctypes.c_int),
     "gdn_layer_prologue": ([ctypes.POINTER(PrologueArgs), ctypes.c_void_p], ctypes.c_int),
     "gdn_layer_epilogue": ([ctypes.POINTER(EpilogueArgs), ctypes.c_void_p], ctypes.c_int),
@@ -792,6 +800,25 @@ def _run_epilogue_bwd(y, weight, g, do, dy, dg, eps):
     return dw
 
 
+def write_vectors_bwd(k, beta, lam, du, dk, n_steps):
+    """Backward of the n-step write vectors u(k, beta, lam) (archbench/layers/nsgdn.py:61-75, p = the
+    previous token's k, zero before the first) in one CUDA kernel (gdn_write_vectors_bwd): adds
+    their share of dk into ``dk`` ((B, T, H, DK) fp32 contiguous, in place) and returns
+    (dbeta (B, T, H), dlam (H,)) in fp32."""
+    _check_cuda(k, beta, lam, du, dk)
+    B, T, H, DK = k.shape
+    k = k.contiguous() if k.dtype in (torch.bfloat16, torch.float32) else k.float().contiguous()
+    beta, lam, du = beta.float().contiguous(), lam.float().contiguous(), du.float().contiguous()
+    if dk.dtype != torch.float32 or not dk.is_contiguous() or dk.shape != (B, T, H, DK):
+        raise ValueError("dk must be a contiguous fp32 (B, T, H, DK) tensor")
+    dbeta = torch.empty(B, T, H, device=k.device)
+    dlam = torch.empty(H, device=k.device)
+    a = WriteVectorsBwdArgs(_ptr(k), _ptr(beta), _ptr(lam), _ptr(du), _ptr(dk), _ptr(dbeta), _ptr(dlam), B, T, H, DK,
+                            _DTC[k.dtype], int(n_steps))
+    _check(load_library().gdn_write_vectors_bwd(ctypes.byref(a), ctypes.c_void_p(torch.cuda.current_stream(k.device).cuda_stream)))
+    return dbeta, dlam
+
+
 def _epilogue_train_backward(ctx, do):
     """The epilogue's backward kernel (gdn_layer_epilogue_bwd): dy, dg and the norm weight's gradient."""
     y, weight, g = ctx.saved_tensors
@@ -822,34 +849,42 @@ def layer_epilogue_train(y, weight, g=None, eps=1e-5, out_dtype=torch.bfloat16):
 
 
 class NsgdnMixerTrain(torch.autograd.Function):
-    """The nsgdn mixer between its fused input projection and its output projection (n_steps = 1):
-    prologue, scan and epilogue forward and backward on the CUDA kernels.  The gradient of the
-    projection is written once, column block by column block, by the three backward kernels (no
-    per-slice accumulation).  Inputs: proj (B, T, width) with columns [q | k | v | g | a | b | pad],
-    conv weight (3 H DK.., taps) fp32 or None, A_log, dt_bias, b_bias, norm weight; output o
-    (B, T, H DV) in proj's dtype."""
+    """The nsgdn mixer between its fused input projection and its output projection: prologue,
+    scan and epilogue forward and backward on the CUDA kernels.  The gradient of the projection is
+    written once, column block by column block, by the three backward kernels (no per-slice
+    accumulation).  Inputs: proj (B, T, width) with columns [q | k | v | g | a | b | pad], conv
+    weight (3 H DK.., taps) fp32 or None, A_log, dt_bias, b_bias, norm weight, softplus(lam) (H,)
+    fp32; output o (B, T, H DV) in proj's dtype.  With n_steps > 1 the prologue kernel also forms the
+    write vectors (archbench/layers/nsgdn.py:61-75, previous token's k, zero before the first) and
+    ``write_vectors_bwd`` differentiates them."""
 
     @staticmethod
-    def forward(ctx, proj, conv_w, A_log, dt_bias, b_bias, norm_w, cfg):
-        H, DK, DV, n_gate, q_scale, la_min, eps, impl = cfg
+    def forward(ctx, proj, conv_w, A_log, dt_bias, b_bias, norm_w, lam_sp, cfg):
+        H, DK, DV, n_gate, q_scale, la_min, eps, impl, n_steps = cfg
         qd = H * DK
         n_qkv = 2 * qd + H * DV
         ab0 = n_qkv + n_gate
         xs = (proj[..., :qd], proj[..., qd:2 * qd], proj[..., 2 * qd:n_qkv], proj[..., ab0:ab0 + H], proj[..., ab0 + H:ab0 + 2 * H])
         conv = None if conv_w is None else (conv_w[:qd], conv_w[qd:2 * qd], conv_w[2 * qd:])
-        q, k, v, la, beta, _ = layer_prologue(*xs, A_log, dt_bias, H=H, DK=DK, DV=DV, b_bias=b_bias, conv=conv, q_scale=q_scale,
-                                              la_min=la_min, out_dtype=torch.bfloat16)
-        y, _ = _prefill_impl(q, k, None, v, la, beta, None, False, torch.bfloat16, impl)
+        u = None
+        if n_steps > 1:  # the prologue kernel also forms the write vectors
+            q, k, v, la, beta, _, u, _ = layer_prologue(*xs, A_log, dt_bias, H=H, DK=DK, DV=DV, b_bias=b_bias, conv=conv,
+                                                        q_scale=q_scale, la_min=la_min, out_dtype=torch.bfloat16,
+                                                        n_steps=n_steps, lam=lam_sp)
+        else:
+            q, k, v, la, beta, _ = layer_prologue(*xs, A_log, dt_bias, H=H, DK=DK, DV=DV, b_bias=b_bias, conv=conv,
+                                                  q_scale=q_scale, la_min=la_min, out_dtype=torch.bfloat16)
+        y, _ = _prefill_impl(q, k, u, v, la, None if u is not None else beta, None, False, torch.bfloat16, impl)
         g = proj[..., n_qkv:n_qkv + n_gate] if n_gate else None
         o = layer_epilogue(y, norm_w, g, eps=eps, out_dtype=proj.dtype)
-        ctx.save_for_backward(proj, conv_w, A_log, dt_bias, b_bias, norm_w, q, k, v, la, beta, y)
+        ctx.save_for_backward(proj, conv_w, A_log, dt_bias, b_bias, norm_w, q, k, v, la, beta, y, u, lam_sp)
         ctx.cfg = cfg
         return o
 
     @staticmethod
     def backward(ctx, do):
-        proj, conv_w, A_log, dt_bias, b_bias, norm_w, q, k, v, la, beta, y = ctx.saved_tensors
-        H, DK, DV, n_gate, q_scale, la_min, eps, impl = ctx.cfg
+        proj, conv_w, A_log, dt_bias, b_bias, norm_w, q, k, v, la, beta, y, u, lam_sp = ctx.saved_tensors
+        H, DK, DV, n_gate, q_scale, la_min, eps, impl, n_steps = ctx.cfg
         B, T, width = proj.shape
         qd = H * DK
         n_qkv = 2 * qd + H * DV
@@ -860,7 +895,12 @@ class NsgdnMixerTrain(torch.autograd.Function):
         g = proj[..., n_qkv:n_qkv + n_gate] if n_gate else None
         dy = torch.empty_like(y)
         dnorm = _run_epilogue_bwd(y, norm_w, g, do, dy, dproj[..., n_qkv:n_qkv + n_gate] if n_gate else None, eps)
-        dq, dk, dbeta, dv, dla, _ = _prefill_bwd_impl(q, k, None, v, la, beta, None, dy, None, False)
+        dlam = None
+        if u is None:
+            dq, dk, dbeta, dv, dla, _ = _prefill_bwd_impl(q, k, None, v, la, beta, None, dy, None, False)
+        else:
+            dq, dk, du, dv, dla, _ = _prefill_bwd_impl(q, k, u, v, la, None, None, dy, None, False)
+            dbeta, dlam = write_vectors_bwd(k, beta, lam_sp, du, dk, n_steps)
         xs = (proj[..., :qd], proj[..., qd:2 * qd], proj[..., 2 * qd:n_qkv], proj[..., ab0:ab0 + H], proj[..., ab0 + H:ab0 + 2 * H])
         outs = (dproj[..., :qd], dproj[..., qd:2 * qd], dproj[..., 2 * qd:n_qkv], dproj[..., ab0:ab0 + H], dproj[..., ab0 + H:ab0 + 2 * H])
         ws = (None, None, None) if conv_w is None else tuple(w.t().contiguous() for w in (conv_w[:qd], conv_w[qd:2 * qd], conv_w[2 * qd:]))
@@ -868,4 +908,4 @@ class NsgdnMixerTrain(torch.autograd.Function):
                                               q_scale, 1e-12, la_min, 1.0)
         dconv = None if conv_w is None else torch.cat([w.t() for w in dws], 0).to(conv_w.dtype)
         return (dproj, dconv, dA.to(A_log.dtype), ddt.to(dt_bias.dtype), None if dbb is None else dbb.to(b_bias.dtype),
-                dnorm.to(norm_w.dtype), None)
+                dnorm.to(norm_w.dtype), dlam, None)

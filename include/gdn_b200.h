@@ -356,6 +356,29 @@ typedef struct {
 
 int gdn_layer_epilogue_bwd(const gdn_epilogue_bwd_args* args, void* stream);
 
+/*
+ * Backward of nsgdn's n-step write vectors (replaces autograd through `write_direction`,
+ * archbench/layers/nsgdn.py:61-75, as NStepGDN.forward calls it at nsgdn.py:529-533): u is built
+ * from the normalised k of token t, p = k of token t - 1 (zero at t = 0, no cache in training),
+ * beta and the head's step size lam.  Given du, adds the write vectors' share to dk (both the
+ * token's own and its successor's, through p) and writes dbeta and dlam.  All tensors contiguous;
+ * k, du and dk 16-byte aligned.  dlam is summed with fp32 atomics (order not fixed).
+ */
+typedef struct gdn_write_vectors_bwd_args {
+  const void* k;       /* (B, T, H, DK), k_dtype: the normalised keys */
+  const float* beta;   /* (B, T, H) */
+  const float* lam;    /* (H): softplus of the layer's lam */
+  const float* du;     /* (B, T, H, DK): gradient of the write vectors */
+  float* dk;           /* (B, T, H, DK), in/out: the write vectors' share is added */
+  float* dbeta;        /* (B, T, H), out */
+  float* dlam;         /* (H), out */
+  int64_t B, T, H, DK; /* DK 64 or 128; B * T * H < 2^30 */
+  int32_t k_dtype;     /* GDN_DTYPE_BF16 or GDN_DTYPE_F32 */
+  int32_t n_steps;     /* 2 .. 8 */
+} gdn_write_vectors_bwd_args;
+
+int gdn_write_vectors_bwd(const gdn_write_vectors_bwd_args* args, void* stream);
+
 /* Which kernel a prefill with these arguments runs (GDN_IMPL_CHUNK_CLUSTER, _CHUNK_SINGLE,
  * _SEGMENTED or _RECURRENT; GDN_IMPL_CHUNK resolves to one of the two chunk variants), or a
  * negative gdn_status if the arguments are invalid.  Launches nothing. */

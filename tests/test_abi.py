@@ -36,6 +36,7 @@ def test_struct_layout_matches_header():
     assert ctypes.sizeof(ops.DecodeArgs) == 8 * 8 + 5 * 24 + 4 * 8 + 2 * 4
     # pointers 22*8, int64 18*8, 4 int32 + 4 float
     assert ctypes.sizeof(ops.PrologueArgs) == 22 * 8 + 18 * 8 + 4 * 4 + 4 * 4 + 4 * 8 + 2 * 4
+    assert ctypes.sizeof(ops.WriteVectorsBwdArgs) == 7 * 8 + 4 * 8 + 2 * 4
     assert ctypes.sizeof(ops.EpilogueArgs) == 4 * 8 + 24 + 8 * 8 + 3 * 4 + 4
 
 

@@ -81,7 +81,7 @@ def test_epilogue_backward_matches_torch(ydt, gate):
         assert r <= tol, f"{n}: rel-L2 {r:.3e}"
 
 
-@pytest.mark.parametrize("cls,expand_v,n_steps", [("nsgdn", 1.0, 1), ("nsgdn", 2.0, 1), ("nsgdn", 2.0, 2), ("nsgdn", 1.0, 3),
+@pytest.mark.parametrize("cls,expand_v,n_steps", [("nsgdn", 1.0, 1), ("nsgdn", 2.0, 1), ("nsgdn", 2.0, 2), ("nsgdn", 1.0, 3), ("nsgdn", 2.0, 8),
                                                    ("gdn", 1.0, 1), ("gdn", 2.0, 1)])
 def test_layer_training_fused_matches_torch_path(cls, expand_v, n_steps):
     """Parameter gradients of a training step on the fused kernels (prologue, scan, epilogue forward and
@@ -105,3 +105,31 @@ def test_layer_training_fused_matches_torch_path(cls, expand_v, n_steps):
     for n in want:
         r = rel(got[n], want[n])
         assert r <= 2e-2, f"{cls} expand_v={expand_v} n_steps={n_steps} {n}: rel-L2 {r:.3e}"
+
+
+@pytest.mark.parametrize("kdt", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("T,n_steps,DK", [(37, 2, 128), (100, 3, 128), (16, 5, 128), (64, 2, 64), (1, 2, 128)])
+def test_write_vectors_backward_matches_autograd(kdt, T, n_steps, DK):
+    """gdn_write_vectors_bwd against autograd through write_direction (archbench/layers/nsgdn.py:61-75)
+    on the same (possibly bf16-rounded) keys: dk (own and successor's share), dbeta, dlam to fp32
+    rounding (rel-L2 <= 1e-5)."""
+    from archbench_b200.nstep import write_direction
+
+    B, H = 2, 3
+    g_ = torch.Generator(device="cuda").manual_seed(T * 7 + n_steps)
+    k = F.normalize(torch.randn(B, T, H, DK, device="cuda", generator=g_), dim=-1).to(kdt)
+    beta = torch.rand(B, T, H, device="cuda", generator=g_)
+    lam = torch.rand(H, device="cuda", generator=g_) + 0.5
+    du = torch.randn(B, T, H, DK, device="cuda", generator=g_)
+    dk0 = torch.randn(B, T, H, DK, device="cuda", generator=g_)
+    kr, br, lr = (t.float().clone().requires_grad_(True) for t in (k, beta, lam))
+    p = F.pad(kr[:, :-1], (0, 0, 0, 0, 1, 0))
+    dk_w, db_w, dl_w = torch.autograd.grad(write_direction(kr, p, br, lr, n_steps), (kr, br, lr), du)
+    dk = dk0.clone()
+    dbeta, dlam = ops.write_vectors_bwd(k, beta, lam, du, dk, n_steps)
+    for n, got, want in (("dk", dk, dk0 + dk_w), ("dbeta", dbeta, db_w), ("dlam", dlam, dl_w)):
+        if want.abs().max().item() == 0.0:  # T = 1: no previous key, so lam has no effect
+            assert got.abs().max().item() == 0.0, n
+            continue
+        r = rel(got, want)
+        assert r <= 1e-5, f"{n}: rel-L2 {r:.3e}"
