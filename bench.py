@@ -379,7 +379,7 @@ def bench_layer(args, rank, world):
             "default_keys": {"config": "the same with expand_v 2, n_steps 2 (archbench's nsgdn defaults)",
                              "infer_ms": t_i2 * 1e3, "infer_tok_s": world * tok / t_i2, "train_step_ms": t_t2 * 1e3,
                              "train_tok_s": world * tok / t_t2},
-            "gpu_launches": 24 * steps}
+            "gpu_launches": 29 * steps}
 
 
 def bench_long_context(args, rank, world):
