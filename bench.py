@@ -18,6 +18,8 @@ Extra objects on the same line:
                one training step of the token mixing.
   layer        the drop-in nsgdn mixer on configuration-1 tokens (d_model 1024): inference forward
                with the fused prologue/epilogue kernels, and a training step through autograd.
+  nstep        nsgdn's n-step write vectors with its default keys (DV=256, n_steps=2) on
+               configuration-1 tokens: the prefill with u given and the write vectors' backward.
   e2e          the headline prefill through the public API with host buffers: pinned-host ->
                device copies of q/k/v/beta/la and the device -> host copy of y inside the timed
                region.
@@ -345,6 +347,46 @@ def bench_backward(args, rank, world):
             "gpu_launches": 9 * steps}
 
 
+def bench_nstep(args, rank, world):
+    """nsgdn's n-step write vectors at configuration-1 tokens with archbench's default nsgdn keys
+    (B=8, T=4096, H=8, DK=128, DV=256, n_steps=2): the prefill with u given (single-CTA kernel,
+    u tiles in its q/k ring) and the write vectors' backward (gdn_write_vectors_bwd)."""
+    import torch.nn.functional as F
+
+    from archbench_b200 import ops
+    from archbench_b200.nstep import write_direction
+
+    c = CONFIGS["cfg1"]
+    DV = 2 * c.DV
+    x = make_inputs(c.B, c.T, c.H, c.DK, DV, seed=8000 + rank, dtype=c.dtype, device="cuda")
+    g = torch.Generator(device="cuda").manual_seed(8100 + rank)
+    lam = torch.rand(c.H, generator=g, device="cuda") + 0.5
+    kf = x["k"].float()
+    u = write_direction(kf, F.pad(kf[:, :-1], (0, 0, 0, 0, 1, 0)), x["beta"], lam, 2).to(torch.bfloat16)
+    du = torch.randn(c.B, c.T, c.H, c.DK, generator=g, device="cuda")
+    dk = torch.zeros_like(du)
+
+    def fwd():
+        ops.gdn_prefill(x["q"], x["k"], x["v"], x["la"], u=u)
+
+    def wv_bwd():
+        ops.write_vectors_bwd(x["k"], x["beta"], lam, du, dk, 2)
+
+    steps = max(1, min(args.steps, 10))
+    t_f = timed(fwd, steps, min(args.warmup, 3), world) / steps
+    t_w = timed(wv_bwd, steps, min(args.warmup, 3), world) / steps
+    th = c.B * c.T * c.H
+    hbm, _, src = peaks()
+    alg_f = th * (3 * 2 * c.DK + 2 * 2 * DV + 4)   # q, k, u, v in; y out (bf16); la (fp32)
+    alg_w = th * (2 * c.DK + 4 + 3 * 4 * c.DK + 4)  # k (bf16), beta, du, dk in/out (fp32), dbeta
+    return {"config": "cfg1 tokens B8 T4096 H8 DK128 DV256, u = 2-step write vectors", "prefill_ms": t_f * 1e3,
+            "prefill_tok_s": world * c.B * c.T / t_f, "write_vectors_bwd_ms": t_w * 1e3,
+            "roofline": {"bound": "hbm", "prefill_achieved_gbs": alg_f / t_f / 1e9, "prefill_frac": alg_f / t_f / 1e9 / hbm,
+                         "write_vectors_bwd_achieved_gbs": alg_w / t_w / 1e9, "write_vectors_bwd_frac": alg_w / t_w / 1e9 / hbm,
+                         "peak": hbm, "unit": "GB/s", "peak_source": src},
+            "gpu_launches": 2 * steps}
+
+
 def bench_layer(args, rank, world):
     """The nsgdn mixer as a whole (projections, short conv, norms and gates, scan, output norm and gate,
     output projection) on configuration-1 tokens: B=8, T=4096, d_model=1024, H=8, head_dim=128,
@@ -435,7 +477,8 @@ def cpu_baseline(budget_s=10.0):
 def run_ours(args):
     rank, world, local = dist_init(args.gpus)
     if args.only:  # one leg alone (profiling runs): its own object, not the bench line
-        res = {"decode": bench_decode, "backward": bench_backward, "layer": bench_layer}[args.only](args, rank, world)
+        res = {"decode": bench_decode, "backward": bench_backward, "layer": bench_layer,
+               "nstep": bench_nstep}[args.only](args, rank, world)
         if rank == 0:
             print(json.dumps({"leg": args.only, **res}), flush=True)
         finish(world)
@@ -461,8 +504,11 @@ def run_ours(args):
         line["backward"] = bench_backward(args, rank, world)
         torch.cuda.empty_cache()
         line["layer"] = bench_layer(args, rank, world)
+        torch.cuda.empty_cache()
+        line["nstep"] = bench_nstep(args, rank, world)
         line["gpu_launches"] += (line["decode"]["gpu_launches"] + line["long_context"].get("gpu_launches", 0) * 2
-                                 + line["backward"]["gpu_launches"] + line["e2e"]["gpu_launches"] + line["layer"]["gpu_launches"])
+                                 + line["backward"]["gpu_launches"] + line["e2e"]["gpu_launches"] + line["layer"]["gpu_launches"]
+                                 + line["nstep"]["gpu_launches"])
     if rank == 0 and world == 1 and not args.skip_cpu:
         line["cpu_baseline"] = cpu_baseline()
     if rank == 0:
@@ -520,7 +566,7 @@ def main():
     ap.add_argument("--prefill-impl", choices=["auto", "chunk", "chunk_cluster", "chunk_single", "recurrent", "segmented"], default="auto")
     ap.add_argument("--skip-extra", action="store_true", help="headline prefill only")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the cpu_baseline leg")
-    ap.add_argument("--only", choices=["decode", "backward", "layer"], default=None,
+    ap.add_argument("--only", choices=["decode", "backward", "layer", "nstep"], default=None,
                     help="run one extra leg alone and print its object (for profiling)")
     ap.add_argument("--no-graph", dest="graph", action="store_false",
                     help="time plain calls instead of CUDA-graph replays of one call")
