@@ -675,7 +675,7 @@ int launch(const gdn_prefill_args* a, const Segmentation& sg, cudaStream_t strea
   if (!make_map(&mq, a->q, a->DK, a, a->sq) || !make_map(&mk, a->k, a->DK, a, a->sk) ||
       !make_map(&mv, a->v, a->DV, a, a->sv) || !make_store_map<TOut>(&my, a->y, a->DV, a, a->sy))
     return GDN_ERR_LAUNCH;
-  if (HAS_U != (a->u != nullptr) || (HAS_U && sg.mode != 0) || (HAS_U && sg.nseg != 1)) return GDN_ERR_UNSUPPORTED;
+  if (HAS_U != (a->u != nullptr)) return GDN_ERR_UNSUPPORTED;
   if (HAS_U) {
     if (!make_map(&mu, a->u, a->DK, a, a->su)) return GDN_ERR_LAUNCH;
   } else {
@@ -738,7 +738,9 @@ int gdn_launch_chunk_ws_segments(const gdn_prefill_args* a, int mode, int nseg, 
   sg.ws_stride = ws_stride;
   sg.seg_s0 = ws;
   sg.seg_out = ws;
-  if (a->u != nullptr) return GDN_ERR_UNSUPPORTED;  // segments are planned for u = beta k only
+  if (a->u != nullptr)
+    return a->out_dtype == GDN_DTYPE_BF16 ? gdn::ws::launch<true, __nv_bfloat16>(a, sg, stream)
+                                          : gdn::ws::launch<true, float>(a, sg, stream);
   return a->out_dtype == GDN_DTYPE_BF16 ? gdn::ws::launch<false, __nv_bfloat16>(a, sg, stream)
                                         : gdn::ws::launch<false, float>(a, sg, stream);
 }

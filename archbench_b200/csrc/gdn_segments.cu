@@ -102,7 +102,7 @@ int sm_count() {
 // Segment plan for these arguments; false when the single-pass kernel is the better choice.
 // `max_bytes` (0 = no limit) caps the workspace by using fewer, longer segments.
 static bool plan(const gdn_prefill_args* a, int sms, size_t max_bytes, int* nseg, int* seg_len, size_t* bytes) {
-  if (!gdn_chunk_supported(a) || a->u != nullptr) return false;
+  if (!gdn_chunk_supported(a)) return false;
   const int64_t nch = (a->T + 63) / 64;
   const int64_t units = a->B * a->H * (a->DV / 128);
   if (sms <= 0 || units * 4 > sms || nch < 8) return false;

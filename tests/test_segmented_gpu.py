@@ -2,6 +2,7 @@
 recurrent kernel.  Same tolerance as the single-pass chunk kernel: max-abs <= 2e-3 and
 rel-L2 <= 1e-3 on y and S_T (fp32 outputs)."""
 
+import numpy as np
 import pytest
 import torch
 
@@ -55,3 +56,25 @@ def test_segmented_equals_single_pass_bf16_output():
     y2, _ = ops.gdn_prefill(g["q"], g["k"], g["v"], g["la"], beta=g["beta"], impl="segmented")
     d = (y1.float() - y2.float())
     assert (d.norm() / y1.float().norm()).item() < 3e-3
+
+
+@pytest.mark.parametrize("T,DV", [(40 * 64 + 37, 128), (24 * 64, 256)])
+def test_segmented_write_vectors_against_oracle(T, DV):
+    """Explicit n-step write vectors (nsgdn n_steps = 2, archbench/layers/nsgdn.py:61-75) on the
+    segmented path: both passes run the single-CTA kernel with u tiles."""
+    B, H = 1, 2
+    x = make_inputs(B, T, H, 128, DV, seed=T + 3 * DV, dtype=torch.bfloat16)
+    k = np32(x["k"]).astype(np.float64)
+    p = np.pad(k[:, :-1], ((0, 0), (1, 0), (0, 0), (0, 0)))
+    u = O.write_direction(k, p, np32(x["beta"]).astype(np.float64), np.array([1.0, 0.7]), 2)
+    u_bf = torch.from_numpy(u.astype(np.float32)).to(torch.bfloat16)
+    S0 = torch.randn(B, H, DV, 128, generator=torch.Generator().manual_seed(9)) * 0.3
+    y_o, S_o = O.recurrence_c(*(np32(x[n]) for n in ("q", "k", "v", "la")), u=np32(u_bf), s0=S0.numpy())
+    g = {k_: v.cuda() for k_, v in x.items()}
+    assert ops.selected_impl(g["q"], g["k"], g["v"], g["la"], u=u_bf.cuda()) == "segmented"
+    y, S = ops.gdn_prefill(g["q"], g["k"], g["v"], g["la"], u=u_bf.cuda(), initial_state=S0.cuda(), output_final_state=True,
+                           out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    check(y, y_o, "y")
+    check(S, S_o, "S_T")
+    assert ops.device_status() == 0
