@@ -147,3 +147,17 @@ def test_bind_caches_host_checks():
     with pytest.raises(ValueError, match="no recurrent state"):
         with bind_caches(m):
             pass
+
+
+def test_nstep_write_direction_matches_golden():
+    """The torch restatement of the write vectors (the autograd reference of the write-vector
+    backward kernel's parity test) against the reference's own output in tests/golden."""
+    import numpy as np
+
+    from archbench_b200.nstep import write_direction
+
+    d = np.load(os.path.join(os.path.dirname(__file__), "golden", "nstep_small.npz"))
+    k = torch.from_numpy(d["k"]).double()
+    p = torch.nn.functional.pad(k[:, :-1], (0, 0, 0, 0, 1, 0))
+    u = write_direction(k, p, torch.from_numpy(d["beta"]).double(), torch.from_numpy(d["lam"]).double(), 2)
+    assert torch.allclose(u, torch.from_numpy(d["u"]).double(), rtol=0, atol=1e-6)
