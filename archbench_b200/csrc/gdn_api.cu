@@ -196,12 +196,15 @@ int gdn_prefill_fwd(const gdn_prefill_args* a, void* stream) {
 }
 
 int gdn_prefill_fwd_static_workspace(const gdn_prefill_args* a, void* stream) {
-  int st = validate(a);
+  if (!a) return GDN_ERR_NULL;
+  gdn_prefill_args checked = *a;  // impl is ignored by this entry point, so it is not validated
+  checked.impl = GDN_IMPL_AUTO;
+  int st = validate(&checked);
   if (st != GDN_OK) return st;
   st = check_device();
   if (st != GDN_OK) return st;
   if (a->T == 0) return GDN_ERR_UNSUPPORTED;
-  return gdn_launch_segmented_static(a, plan_sms(), static_cast<cudaStream_t>(stream));
+  return gdn_launch_segmented_static(&checked, plan_sms(), static_cast<cudaStream_t>(stream));
 }
 
 int gdn_decode_step(const gdn_decode_args* d, void* stream) {

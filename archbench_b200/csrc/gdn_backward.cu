@@ -1130,14 +1130,11 @@ Layout layout(int64_t nch, int64_t bh) {
 
 template <typename TI, typename TD>
 int launch(const Params& p, cudaStream_t s) {
-  static bool attr_set = false;  // per process; the attribute applies to every device's launches
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(prep_kernel<TI, TD>, cudaFuncAttributeMaxDynamicSharedMemorySize, PREP_SMEM) != cudaSuccess ||
-        cudaFuncSetAttribute(chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, CHAIN_SMEM) != cudaSuccess ||
-        cudaFuncSetAttribute(local_kernel<TI, TD>, cudaFuncAttributeMaxDynamicSharedMemorySize, LOCAL_SMEM) != cudaSuccess)
-      return GDN_ERR_LAUNCH;
-    attr_set = true;
-  }
+  static std::atomic<unsigned long long> opted{0};  // per device (see opt_in_smem)
+  if (!opt_in_smem(opted, {{(const void*)prep_kernel<TI, TD>, (int)PREP_SMEM},
+                           {(const void*)chain_kernel, (int)CHAIN_SMEM},
+                           {(const void*)local_kernel<TI, TD>, (int)LOCAL_SMEM}}))
+    return GDN_ERR_LAUNCH;
   const int64_t nch = (int64_t)p.NC * p.BH;
   if (cudaMemsetAsync(p.amax, 0, (size_t)p.BH * 4, s) != cudaSuccess) return GDN_ERR_LAUNCH;
   amax_kernel<TD><<<(unsigned)nch, NTHR, 0, s>>>(p);

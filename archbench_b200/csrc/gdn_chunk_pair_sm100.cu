@@ -840,12 +840,8 @@ int launch(const gdn_prefill_args* a, int nseg, int seg_len, const float* seg_s0
       !make_map(&mv, a->v, a->DV, a, a->sv) || !make_store_map<TOut>(&my, a->y, a->DV, a, a->sy, YS_BYTES))
     return GDN_ERR_LAUNCH;
   auto kern = pair_kernel<TOut>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, DYN) != cudaSuccess)
-      return GDN_ERR_LAUNCH;
-    attr_set = true;
-  }
+  static std::atomic<unsigned long long> opted{0};  // per device (see opt_in_smem)
+  if (!opt_in_smem(opted, {{(const void*)kern, (int)(DYN)}})) return GDN_ERR_LAUNCH;
   const int nch = (int)((a->T + C - 1) / C);
   Params p;
   p.beta = a->beta; p.la = a->la; p.s0 = a->s0; p.s_out = a->s_out;

@@ -541,12 +541,8 @@ int launch(const gdn_prefill_args* a, cudaStream_t stream) {
     mu = mk;
   }
   auto kern = chunk_kernel<HAS_U, STAGES, TOut>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, LY::DYN) != cudaSuccess)
-      return GDN_ERR_LAUNCH;
-    attr_set = true;
-  }
+  static std::atomic<unsigned long long> opted{0};  // per device (see opt_in_smem)
+  if (!opt_in_smem(opted, {{(const void*)kern, (int)(LY::DYN)}})) return GDN_ERR_LAUNCH;
   Params p;
   p.beta = a->beta; p.la = a->la; p.B = (int)a->B; p.T = (int)a->T; p.H = (int)a->H; p.sy = a->sy;
   p.srows = (int)a->DV;

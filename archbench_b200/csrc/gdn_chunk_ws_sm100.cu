@@ -682,12 +682,8 @@ int launch(const gdn_prefill_args* a, const Segmentation& sg, cudaStream_t strea
     mu = mk;
   }
   auto kern = ws_kernel<HAS_U, TOut>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, DYN) != cudaSuccess)
-      return GDN_ERR_LAUNCH;
-    attr_set = true;
-  }
+  static std::atomic<unsigned long long> opted{0};  // per device (see opt_in_smem)
+  if (!opt_in_smem(opted, {{(const void*)kern, (int)(DYN)}})) return GDN_ERR_LAUNCH;
   const int nch = (int)((a->T + C - 1) / C);
   Params p;
   p.beta = a->beta; p.la = a->la; p.s0 = a->s0; p.s_out = a->s_out; p.y = a->y; p.sy = a->sy;

@@ -6,6 +6,9 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+#include <initializer_list>
+
 #include "gdn_b200.h"
 
 namespace gdn {
@@ -50,6 +53,27 @@ template <>
 struct DtypeOf<__nv_bfloat16> {
   static constexpr int value = GDN_DTYPE_BF16;
 };
+
+// Opt kernels into more than 48 KB of dynamic shared memory on the current device.  A function
+// attribute belongs to the function as loaded in one device's context, so it is set once per
+// device: bit `dev` of `done` records that the current device's context has it.  Setting it twice
+// from two host threads is harmless (the call is idempotent); `done` is atomic, so any thread may
+// call.  Devices past 63 set the attribute on every call.
+struct SmemOptIn {
+  const void* kernel;
+  int bytes;
+};
+
+inline bool opt_in_smem(std::atomic<unsigned long long>& done, std::initializer_list<SmemOptIn> kernels) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  const unsigned long long bit = (dev >= 0 && dev < 64) ? (1ull << dev) : 0ull;
+  if (bit && (done.load(std::memory_order_acquire) & bit)) return true;
+  for (const SmemOptIn& k : kernels)
+    if (cudaFuncSetAttribute(k.kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, k.bytes) != cudaSuccess) return false;
+  if (bit) done.fetch_or(bit, std::memory_order_acq_rel);
+  return true;
+}
 
 }  // namespace gdn
 

@@ -391,13 +391,9 @@ size_t prologue_smem(const PrologueParams& p, int run, int es) {
 
 template <typename TX, typename TO, int NK, int NV, int TAPS>
 int launch_prologue_one(const PrologueParams& p, unsigned blocks, size_t sm, cudaStream_t s) {
-  static bool attr = false;  // per process: the attribute applies to every device's launches
-  if (!attr) {
-    if (cudaFuncSetAttribute(prologue_kernel<TX, TO, NK, NV, TAPS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             PROLOGUE_SMEM_MAX) != cudaSuccess)
-      return GDN_ERR_LAUNCH;
-    attr = true;
-  }
+  static std::atomic<unsigned long long> opted{0};  // per device (see opt_in_smem)
+  if (!opt_in_smem(opted, {{(const void*)prologue_kernel<TX, TO, NK, NV, TAPS>, (int)PROLOGUE_SMEM_MAX}}))
+    return GDN_ERR_LAUNCH;
   prologue_kernel<TX, TO, NK, NV, TAPS><<<blocks, 32 * TOKS, sm, s>>>(p);
   return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
 }

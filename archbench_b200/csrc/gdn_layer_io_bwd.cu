@@ -386,13 +386,9 @@ int launch_pro(const ProBwdParams& p, cudaStream_t s) {
   const size_t red = (size_t)WARPS * TAPS * D * sizeof(float);
   const size_t sm = (size_t)TAPS * D * 4 + (stage > red ? stage : red);
   if (sm > 100 * 1024) return GDN_ERR_UNSUPPORTED;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(prologue_bwd_kernel<TX, TG, NK, NV, TAPS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             100 * 1024) != cudaSuccess)
-      return GDN_ERR_LAUNCH;
-    attr = true;
-  }
+  static std::atomic<unsigned long long> opted{0};  // per device (see opt_in_smem)
+  if (!opt_in_smem(opted, {{(const void*)prologue_bwd_kernel<TX, TG, NK, NV, TAPS>, 100 * 1024}}))
+    return GDN_ERR_LAUNCH;
   const int64_t runs = (p.T + RUN - 1) / RUN;
   const int64_t blocks = (int64_t)p.B * p.H * ((runs + WARPS - 1) / WARPS);
   if (blocks > 0x7fffffff) return GDN_ERR_SHAPE;

@@ -134,13 +134,9 @@ static int launch_plan(const gdn_prefill_args* a, float* ws, size_t ws_bytes, in
   if (st != GDN_OK) return st;
   const int rblocks = (int)(a->DV / gdn::seg::RB);
   const int64_t grid = a->B * a->H * rblocks;
-  static bool attr_set = false;
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(gdn::seg::combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)gdn::seg::COMB_SMEM) != cudaSuccess)
-      return GDN_ERR_LAUNCH;
-    attr_set = true;
-  }
+  static std::atomic<unsigned long long> opted{0};  // per device (see gdn::opt_in_smem)
+  if (!gdn::opt_in_smem(opted, {{(const void*)gdn::seg::combine_kernel, (int)gdn::seg::COMB_SMEM}}))
+    return GDN_ERR_LAUNCH;
   gdn::seg::combine_kernel<<<(unsigned)grid, gdn::seg::D, gdn::seg::COMB_SMEM, stream>>>(ws, a->s0, (int)a->DV, P - 1,
                                                                                           rblocks);
   if (cudaGetLastError() != cudaSuccess) return GDN_ERR_LAUNCH;

@@ -95,8 +95,6 @@ def dist_init(n_gpus):
         import torch.distributed as dist
 
         torch.cuda.set_device(local)
-        # Keep rank 0's stdout to the one JSON line: NCCL's version banner goes only where asked for.
-        os.environ.setdefault("NCCL_DEBUG", "WARN")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
     elif torch.cuda.is_available():
         torch.cuda.set_device(0)
@@ -277,8 +275,8 @@ def bench_prefill_e2e(args, rank, world):
         # the public host-buffer entry: pieces of the batch pipelined through H2D copy, prefill, D2H copy
         ops.gdn_prefill_from_host(xh["q"], xh["k"], xh["v"], xh["la"], xh["beta"], y_host, impl=args.prefill_impl)
 
-    steps = max(1, min(args.steps, 5))
-    secs = timed(step, steps, min(args.warmup, 2), world)
+    steps = args.steps
+    secs = timed(step, steps, args.warmup, world)
     return {"value": world * c.B * c.T * steps / secs, "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "steps": steps, "ms_per_step": secs / steps * 1e3, "api": "ops.gdn_prefill_from_host (8 pieces)",
             "gpu_launches": 8 * steps}
@@ -452,33 +450,165 @@ def bench_long_context(args, rank, world):
             "gpu_launches": steps}
 
 
-def cpu_baseline(budget_s=10.0):
-    """archbench's recurrence (torch restatement) on the host cores, configuration-1 shapes: the
-    whole 4096-token workload in 64-token slices (state carried), repeated until ~budget_s have
-    passed; tok/s at B=8, H=8, d=128."""
+CPU_SAMPLE = ("cfg1 B8 T4096 H8 d128 fp32: each step one pass over the whole configuration-1 batch (8 sequences of "
+              "4096 tokens, fed in 64-token slices with the state carried)")
+
+
+def bench_lm(args, rank, world):
+    """Configuration 4: the 380M-class decoder (24 gdn blocks, d_model 1024, 8 heads of 128, SwiGLU 2816,
+    vocabulary 50304, bf16 weights ~ N(0, 0.02), random init; archbench_b200.lm) -- a prefill of 16 prompts
+    of 2048 uniform-random token ids, then 256 greedy decode steps through the per-layer recurrent caches
+    (archbench_b200.decode.bind_caches).  The batch is sharded over the ranks (16 / N prompts each, model
+    replicas, no collective)."""
+    from archbench_b200.decode import bind_caches
+    from archbench_b200.lm import CONFIG4, config4_lm
+
+    B_all, T, steps = 16, 2048, 256
+    if B_all % world:
+        return {"skipped": f"batch {B_all} not divisible by {world} ranks"}
+    B = B_all // world
+    torch.manual_seed(9000)  # the same weights on every rank
+    m = config4_lm()
+    g = torch.Generator(device="cuda").manual_seed(9100 + rank)
+    idx = torch.randint(0, CONFIG4["vocab_size"], (B, T), device="cuda", generator=g)
+
+    def run(n_steps, e=None):
+        with torch.no_grad(), bind_caches(m):
+            if e:
+                e[0].record()
+            logits = m(idx)[0][:, -1]
+            if e:
+                e[1].record()
+            for _ in range(n_steps):
+                logits = m(logits.argmax(-1)[:, None])[0][:, -1]
+            if e:
+                e[2].record()
+            return logits
+
+    run(4)  # warm-up: one prefill and a few steps
+    torch.cuda.synchronize()
+    barrier(world)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    run(steps, ev)
+    torch.cuda.synchronize()
+    barrier(world)
+    t_pre = max_over_ranks(ev[0].elapsed_time(ev[1]) / 1e3, world)
+    t_dec = max_over_ranks(ev[1].elapsed_time(ev[2]) / 1e3, world)
+    del m
+    return {"config": "cfg4: 24 gdn blocks d_model 1024 H8 head_dim 128 expand_v 1, SwiGLU 2816, vocab 50304, bf16; "
+                      "prefill 16 x 2048 then 256 greedy steps, batch sharded",
+            "prefill_ms": t_pre * 1e3, "prefill_tok_s": world * B * T / t_pre,
+            "decode_ms_per_step": t_dec / steps * 1e3, "decode_tok_s": world * B * steps / t_dec,
+            "prompts_per_rank": B, "gpu_launches": 3 * CONFIG4["n_layer"] * (1 + steps),  # prologue, scan, epilogue per layer and call
+            "note": "eager PyTorch host loop around this package's kernels (projections and MLP are cuBLAS GEMMs)"}
+
+
+def bench_fla(args, rank, world, ours_prefill_ms, ours_decode_ms):
+    """The reference's own GPU kernels on this box: fla 0.5.1's Triton ``chunk_gated_delta_rule`` on the
+    configuration-1 inputs (what archbench's ``gdn`` arch runs in prefill, fla/layers/gated_deltanet.py:266-279,
+    and the state pass archbench's nsgdn chunk path shares, nsgdn.py:352-363) and
+    ``fused_recurrent_gated_delta_rule`` on the configuration-2 decode step (gated_deltanet.py:281-294).  Same
+    q/k/v/beta/la as our legs (q already scaled, so scale=1; no in-kernel l2norm); fla's state layout is
+    [B, H, K, V].  Timed like ours (CUDA events, warm-up first; the first call JIT-compiles)."""
+    try:
+        import fla
+        from fla.ops.gated_delta_rule import chunk_gated_delta_rule, fused_recurrent_gated_delta_rule
+    except Exception as e:
+        return {"unavailable": f"fla does not import on this host: {e!r}"[:300]}
+    from archbench_b200 import ops
+    from archbench_b200.workloads import DECODE_PREFILL_T
+
+    c = CONFIGS["cfg1"]
+    x = make_inputs(c.B, c.T, c.H, c.DK, c.DV, seed=1000 + rank, dtype=c.dtype, device="cuda")
+
+    def f_chunk():
+        return chunk_gated_delta_rule(x["q"], x["k"], x["v"], x["la"], x["beta"], scale=1.0)
+
+    t0 = time.perf_counter()
+    o, _ = f_chunk()
+    torch.cuda.synchronize()
+    jit_s = time.perf_counter() - t0
+    y, _ = ops.gdn_prefill(x["q"], x["k"], x["v"], x["la"], beta=x["beta"])
+    rel = float((o.float() - y.float()).norm() / y.float().norm())
+    del o, y
+    steps = max(1, min(args.steps, 20))
+    t_chunk = timed(f_chunk, steps, args.warmup, world) / steps
+    del x
+    c2 = CONFIGS["cfg2"]
+    B, H, D = c2.B, c2.H, c2.DK
+    pre = make_inputs(B, DECODE_PREFILL_T, H, D, D, seed=3000 + rank, dtype=torch.bfloat16, device="cuda")
+    _, state = ops.gdn_prefill(pre["q"], pre["k"], pre["v"], pre["la"], beta=pre["beta"], output_final_state=True)
+    del pre
+    h0 = state.transpose(-1, -2).contiguous()
+    tok = make_inputs(B, 1, H, D, D, seed=4000 + rank, dtype=torch.bfloat16, device="cuda")
+
+    def f_dec():
+        return fused_recurrent_gated_delta_rule(tok["q"], tok["k"], tok["v"], tok["la"], beta=tok["beta"], scale=1.0,
+                                                initial_state=h0, output_final_state=True)
+
+    t_dec = timed(f_dec, steps, args.warmup, world) / steps
+    return {"impl": f"fla {fla.__version__} (Triton)", "prefill_ms": t_chunk * 1e3, "prefill_tok_s": world * c.B * c.T / t_chunk,
+            "prefill_speedup_ours_vs_fla": t_chunk * 1e3 / ours_prefill_ms, "prefill_fla_vs_ours_rel_l2": rel,
+            "decode_ms": t_dec * 1e3, "decode_tok_s": world * B / t_dec, "decode_speedup_ours_vs_fla": t_dec * 1e3 / ours_decode_ms,
+            "first_call_s": jit_s, "gpu_launches": 0,
+            "note": "fla's kernels are the checker here, not ours: not counted in gpu_launches"}
+
+
+def cpu_reference_setup():
+    """Inputs of the CPU legs: the whole configuration-1 batch in fp32 (seed 7), u = beta k."""
+    torch.set_num_threads(os.cpu_count() or 1)  # every host core (torchrun sets OMP_NUM_THREADS=1 for its ranks)
+    c = CONFIGS["cfg1"]
+    x = make_inputs(c.B, c.T, c.H, c.DK, c.DV, seed=7, dtype=torch.float32, device="cpu")
+    x["u"] = x["beta"][..., None] * x["k"]
+    return x
+
+
+def cpu_reference_pass(x, slice_t=64):
+    """One pass of archbench's recurrence (torch restatement, oracle/cpu_reference.py) over the whole
+    batch; returns the tokens processed (B * T)."""
     from oracle.cpu_reference import nsgdn_ref_torch
 
-    torch.set_num_threads(os.cpu_count() or 1)  # every host core
-    c = CONFIGS["cfg1"]
-    x = make_inputs(c.B, 64, c.H, c.DK, c.DV, seed=7, dtype=torch.float32, device="cpu")
-    u = x["beta"][..., None] * x["k"]
-    nsgdn_ref_torch(x["q"][:, :4], x["k"][:, :4], u[:, :4], x["v"][:, :4], x["la"][:, :4])  # warm-up
-    tokens, t0, S, passes = 0, time.perf_counter(), None, 0
-    while time.perf_counter() - t0 < budget_s or tokens % (c.B * c.T):
-        _, S = nsgdn_ref_torch(x["q"], x["k"], u, x["v"], x["la"], s0=S)
-        tokens += c.B * 64
-        if tokens % (c.B * c.T) == 0:  # a whole sequence done: start the next pass from S = 0
-            S, passes = None, passes + 1
+    B, T = x["q"].shape[:2]
+    S = None
+    for t0 in range(0, T, slice_t):
+        sl = slice(t0, t0 + slice_t)
+        _, S = nsgdn_ref_torch(x["q"][:, sl], x["k"][:, sl], x["u"][:, sl], x["v"][:, sl], x["la"][:, sl], s0=S)
+    return B * T
+
+
+def cpu_reference_rate(x, steps, warmup):
+    """tok/s of ``steps`` timed passes after ``warmup`` untimed ones: the one measurement both CPU legs
+    report (``cpu_baseline`` on our line, and the ``--impl reference`` arm)."""
+    for _ in range(warmup):
+        cpu_reference_pass(x)
+    t0 = time.perf_counter()
+    tokens = sum(cpu_reference_pass(x) for _ in range(steps))
     dt = time.perf_counter() - t0
-    return {"value": tokens / dt, "unit": "tok/s", "cores": torch.get_num_threads(), "kind": "port",
-            "sample": f"cfg1 shapes B8 H8 d128 fp32, the whole 4096-token sequences in 64-token slices, {passes} passes ({dt:.1f} s)"}
+    return tokens / dt, dt
+
+
+def cpu_threads_note():
+    aff = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else None
+    return f"{torch.get_num_threads()} torch threads; os.cpu_count() {os.cpu_count()}, affinity {aff}"
+
+
+def cpu_baseline(budget_s=10.0):
+    """The reference arm's measurement on our line: the same passes and warm-up, as many whole passes
+    as fit in about ``budget_s``."""
+    x = cpu_reference_setup()
+    rate0, dt0 = cpu_reference_rate(x, 1, 3)
+    steps = max(1, int(budget_s / dt0))
+    rate, dt = cpu_reference_rate(x, steps, 0)
+    total = (rate0 * dt0 + rate * dt) / (dt0 + dt)
+    return {"value": total, "unit": "tok/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{CPU_SAMPLE}; 3 warm-up passes, {steps + 1} timed passes ({dt + dt0:.1f} s); {cpu_threads_note()}"}
 
 
 def run_ours(args):
     rank, world, local = dist_init(args.gpus)
     if args.only:  # one leg alone (profiling runs): its own object, not the bench line
         res = {"decode": bench_decode, "backward": bench_backward, "layer": bench_layer,
-               "nstep": bench_nstep}[args.only](args, rank, world)
+               "nstep": bench_nstep, "lm": bench_lm}[args.only](args, rank, world)
         if rank == 0:
             print(json.dumps({"leg": args.only, **res}), flush=True)
         finish(world)
@@ -506,9 +636,14 @@ def run_ours(args):
         line["layer"] = bench_layer(args, rank, world)
         torch.cuda.empty_cache()
         line["nstep"] = bench_nstep(args, rank, world)
+        torch.cuda.empty_cache()
+        line["lm"] = bench_lm(args, rank, world)
+        if world == 1:
+            torch.cuda.empty_cache()
+            line["reference_gpu"] = bench_fla(args, rank, world, res["ms_per_step"], line["decode"]["ms_per_step"])
         line["gpu_launches"] += (line["decode"]["gpu_launches"] + line["long_context"].get("gpu_launches", 0) * 2
                                  + line["backward"]["gpu_launches"] + line["e2e"]["gpu_launches"] + line["layer"]["gpu_launches"]
-                                 + line["nstep"]["gpu_launches"])
+                                 + line["nstep"]["gpu_launches"] + line["lm"].get("gpu_launches", 0))
     if rank == 0 and world == 1 and not args.skip_cpu:
         line["cpu_baseline"] = cpu_baseline()
     if rank == 0:
@@ -517,28 +652,15 @@ def run_ours(args):
 
 
 def run_reference(args):
-    """The reference's CPU implementation of this path on the host cores (rank 0 only)."""
+    """The reference's CPU implementation of this path on the host cores (rank 0 only): each step is one
+    pass over the whole configuration-1 batch, the sample ``cpu_baseline`` times too."""
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
-    from oracle.cpu_reference import nsgdn_ref_torch
-
-    # every host core (torchrun sets OMP_NUM_THREADS=1 for its ranks; rank 0 runs alone here)
-    torch.set_num_threads(os.cpu_count() or 1)
-    c = CONFIGS["cfg1"]
-    T_slice = 128
-    x = make_inputs(c.B, T_slice, c.H, c.DK, c.DV, seed=7, dtype=torch.float32, device="cpu")
-    u = x["beta"][..., None] * x["k"]
-    S = None
-    for _ in range(args.warmup):
-        _, S = nsgdn_ref_torch(x["q"], x["k"], u, x["v"], x["la"], s0=S)
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        _, S = nsgdn_ref_torch(x["q"], x["k"], u, x["v"], x["la"], s0=S)
-    dt = time.perf_counter() - t0
-    v = c.B * T_slice * args.steps / dt
-    sample = f"cfg1 shapes B8 H8 d128 fp32, {T_slice}-token slice per step (state carried)"
+    x = cpu_reference_setup()
+    v, dt = cpu_reference_rate(x, args.steps, args.warmup)
+    sample = f"{CPU_SAMPLE}; {args.warmup} warm-up passes, {args.steps} timed ({dt:.1f} s); {cpu_threads_note()}"
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
@@ -566,7 +688,7 @@ def main():
     ap.add_argument("--prefill-impl", choices=["auto", "chunk", "chunk_cluster", "chunk_single", "recurrent", "segmented"], default="auto")
     ap.add_argument("--skip-extra", action="store_true", help="headline prefill only")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the cpu_baseline leg")
-    ap.add_argument("--only", choices=["decode", "backward", "layer", "nstep"], default=None,
+    ap.add_argument("--only", choices=["decode", "backward", "layer", "nstep", "lm"], default=None,
                     help="run one extra leg alone and print its object (for profiling)")
     ap.add_argument("--no-graph", dest="graph", action="store_false",
                     help="time plain calls instead of CUDA-graph replays of one call")

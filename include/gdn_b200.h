@@ -142,9 +142,12 @@ int gdn_prefill_workspace_bytes(const gdn_prefill_args* args, size_t* bytes);
  * Same computation as gdn_prefill_fwd's segmented path (few, long sequences), with the segment
  * workspace taken from an array of GDN_STATIC_WORKSPACE_BYTES that the library reserves on every
  * GPU that loads it and holds until the process exits; args->impl, args->workspace and
- * args->workspace_bytes are ignored.  When the usual segmentation would need more, fewer and
- * longer segments are used; if none fits, the call fails with GDN_ERR_WORKSPACE.  Arguments the
- * segmented path does not serve (many sequences, short T, u given) fail with GDN_ERR_UNSUPPORTED.
+ * args->workspace_bytes are ignored (any impl value is accepted).  Explicit write vectors
+ * (args->u, nsgdn's n_steps > 1) are served as in gdn_prefill_fwd.  When the usual segmentation
+ * would need more, fewer and longer segments are used; if none fits, the call fails with
+ * GDN_ERR_WORKSPACE (on a 148-SM B200 every shape the segmented path takes fits: its largest
+ * segment-state slot is under 5 MB).  Arguments the segmented path does not serve (many
+ * sequences, short T, T = 0) fail with GDN_ERR_UNSUPPORTED.
  * Calls no cudaMalloc, cudaFree or allocating routine.  The first call on a device looks up the
  * array's device address (cudaGetSymbolAddress); make that first call before any stream capture.
  * Every call shares the one array and leaves its contents behind: calls that overlap on the GPU

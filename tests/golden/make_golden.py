@@ -21,7 +21,13 @@ What it records (all float32 arithmetic, CPU):
     tokens' dy.  Once with u a leaf (du), once with u = beta k from ``write_direction``
     (dbeta, and dk including the write-vector path).
 
+  * archbench's own ``NStepGDN`` layer (nsgdn.py:473-542) forward on CPU in float32 (where
+    ``pick_scan`` takes ``nsgdn_ref``), parameters from ``layer_params.fill`` and seeded inputs,
+    for n_steps 1 and 2, expand_v 1 and 2 and a ragged T: ``nsgdn_layer.npz``.
+
     python tests/golden/make_golden.py [/path/to/archbench-checkout] [--only NAME]
+
+The checkout defaults to the environment variable ARCHBENCH_REFERENCE.
 """
 
 from __future__ import annotations
@@ -96,6 +102,36 @@ def bwd_fixture(nsgdn_ref, write_direction):
     return d
 
 
+# Layer cases: (name, B, T, d_model, keywords).  head_dim 128 puts the scan on the tensor-core kernels.
+LAYER_CASES = [
+    ("e1_n1", 2, 128, 64, dict(num_heads=2, head_dim=128, expand_v=1.0, n_steps=1)),
+    ("e1_n2_ragged", 2, 100, 64, dict(num_heads=2, head_dim=128, expand_v=1.0, n_steps=2)),
+    ("e2_n2", 1, 128, 64, dict(num_heads=2, head_dim=128, expand_v=2.0, n_steps=2)),
+    ("e2_n1_ragged", 1, 100, 64, dict(num_heads=1, head_dim=128, expand_v=2.0, n_steps=1, use_gate=False)),
+]
+
+
+def layer_fixture(ref_root):
+    """archbench's NStepGDN.forward (CPU, float32) on seeded parameters and inputs."""
+    sys.path.insert(0, HERE)
+    import layer_params  # noqa: E402
+
+    sys.path.insert(0, ref_root)
+    from archbench.layers.nsgdn import NStepGDN as RefNStepGDN  # noqa: E402
+
+    d = {}
+    for i, (name, B, T, D, kw) in enumerate(LAYER_CASES):
+        m = RefNStepGDN(D, **kw)
+        digest_w = layer_params.fill(m, 500 + i)
+        x = layer_params.layer_input(B, T, D, 600 + i)
+        with torch.no_grad():
+            y = m(x)
+        d[f"{name}_y"] = y
+        d[f"{name}_x_sum"] = np.float64(x.double().sum())
+        d[f"{name}_params_sha256"] = np.bytes_(digest_w)
+    return d
+
+
 def main(ref_root):
     torch.manual_seed(0)
     nsgdn_ref, write_direction = _ref_modules(ref_root)
@@ -147,6 +183,9 @@ def main(ref_root):
 
     out["bwd_small"] = bwd_fixture(nsgdn_ref, write_direction)
 
+    if ONLY in (None, "nsgdn_layer"):
+        out["nsgdn_layer"] = layer_fixture(ref_root)
+
     for name, d in out.items():
         if ONLY and name != ONLY:
             continue
@@ -163,4 +202,7 @@ if __name__ == "__main__":
         i = argv.index("--only")
         ONLY = argv[i + 1]
         del argv[i : i + 2]
-    main(argv[0] if argv else "/root/reference")
+    root = argv[0] if argv else os.environ.get("ARCHBENCH_REFERENCE")
+    if not root:
+        sys.exit("give the archbench checkout as an argument or in ARCHBENCH_REFERENCE")
+    main(root)
