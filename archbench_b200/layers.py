@@ -43,6 +43,19 @@ class GDNCache:
     state: Optional[torch.Tensor] = None
     conv: dict = field(default_factory=dict)
     seen: int = 0
+    # A static cache keeps its tensors: decode steps overwrite the recurrent state and the conv
+    # states in place, so a decode step captured in a CUDA graph reads and writes the same buffers
+    # on every replay (decode.GraphDecoder).
+    static: bool = False
+
+
+def _put(cache: GDNCache, key: str, value: torch.Tensor) -> None:
+    """Store a conv-state entry; a static cache overwrites the tensor it already holds."""
+    old = cache.conv.get(key)
+    if cache.static and old is not None and old.shape == value.shape:
+        old.copy_(value)
+    else:
+        cache.conv[key] = value
 
 
 class ShortConv(nn.Module):
@@ -186,13 +199,13 @@ class NStepGDN(nn.Module):
                 want_state=cache is not None, q_scale=DK**-0.5, la_min=self.la_min, out_dtype=dt, n_steps=self.n_steps,
                 lam=F.softplus(self.lam.float()), k_prev=None if kp is None else kp.reshape(B, H, DK))
             if cache is not None:
-                cache.conv["k_prev"] = k_last.reshape(B, 1, H, DK)
+                _put(cache, "k_prev", k_last.reshape(B, 1, H, DK))
         else:
             q, k, v, la, beta, new_state = ops.layer_prologue(
                 *parts, self.A_log, self.dt_bias, H=H, DK=DK, DV=DV, b_bias=self.b_bias, conv=conv, conv_state=state,
                 want_state=cache is not None, q_scale=DK**-0.5, la_min=self.la_min, out_dtype=dt)
         if cache is not None and new_state is not None:
-            cache.conv["qkv"] = torch.cat(new_state, 1)
+            _put(cache, "qkv", torch.cat(new_state, 1))
         y = _mix(q, k, v, la, None if u is not None else beta, u, cache, self._impl)
         if cache is not None:
             cache.seen += T
@@ -219,7 +232,7 @@ class NStepGDN(nn.Module):
         if self.conv is not None:
             qkv, st = self.conv(qkv, None if cache is None else cache.conv.get("qkv"), want_state=cache is not None)
             if cache is not None:
-                cache.conv["qkv"] = st
+                _put(cache, "qkv", st)
         with torch.autocast(x.device.type, enabled=False):
             qkv = qkv.float()
             q = F.normalize(qkv[..., :self.qk_dim].view(B, T, H, DK), dim=-1) * DK**-0.5
@@ -238,7 +251,7 @@ class NStepGDN(nn.Module):
                 p = torch.cat([prev if prev is not None else torch.zeros_like(k[:, :1]), k[:, :-1]], 1)
                 u = write_direction(k, p, beta, F.softplus(self.lam.float()), self.n_steps)
                 if cache is not None:
-                    cache.conv["k_prev"] = k[:, -1:].detach()
+                    _put(cache, "k_prev", k[:, -1:].detach())
             dt = torch.bfloat16 if (DK == 128 and self._impl != "recurrent") else torch.float32
             y = _mix(q.to(dt), k.to(dt), v.to(dt), la, None if u is not None else beta, None if u is None else u.to(dt), cache, self._impl)
         if cache is not None:
@@ -333,7 +346,8 @@ class GatedDeltaNet(nn.Module):
                 conv_state=state, want_state=cache is not None, q_scale=DK**-0.5, l2_eps=1e-6,
                 beta_scale=2.0 if self.allow_neg_eigval else 1.0, out_dtype=dt)
         if cache is not None and new_state is not None:
-            cache.conv.update(q=new_state[0], k=new_state[1], v=new_state[2])
+            for key, st in zip("qkv", new_state):
+                _put(cache, key, st)
         o = _mix(q, k, v, la, beta, None, cache, "auto")
         if cache is not None:
             cache.seen += T
@@ -359,7 +373,8 @@ class GatedDeltaNet(nn.Module):
             k, sk = self.k_conv1d(self.k_proj(x), None if cache is None else cache.conv.get("k"), want)
             v, sv = self.v_conv1d(self.v_proj(x), None if cache is None else cache.conv.get("v"), want)
             if want:
-                cache.conv.update(q=sq, k=sk, v=sv)
+                for key, st in zip("qkv", (sq, sk, sv)):
+                    _put(cache, key, st)
         else:
             q, k, v = F.silu(self.q_proj(x)), F.silu(self.k_proj(x)), F.silu(self.v_proj(x))
         H, DK, DV = self.num_heads, self.head_k_dim, self.head_v_dim

@@ -451,7 +451,7 @@ def bench_long_context(args, rank, world):
 
 
 CPU_SAMPLE = ("cfg1 B8 T4096 H8 d128 fp32: each step one pass over the whole configuration-1 batch (8 sequences of "
-              "4096 tokens, fed in 64-token slices with the state carried)")
+              "4096 tokens, fed in 64-token slices with the state carried); glibc heap trimming off (mallopt)")
 
 
 def bench_lm(args, rank, world):
@@ -460,7 +460,7 @@ def bench_lm(args, rank, world):
     of 2048 uniform-random token ids, then 256 greedy decode steps through the per-layer recurrent caches
     (archbench_b200.decode.bind_caches).  The batch is sharded over the ranks (16 / N prompts each, model
     replicas, no collective)."""
-    from archbench_b200.decode import bind_caches
+    from archbench_b200.decode import GraphDecoder, bind_caches
     from archbench_b200.lm import CONFIG4, config4_lm
 
     B_all, T, steps = 16, 2048, 256
@@ -472,35 +472,40 @@ def bench_lm(args, rank, world):
     g = torch.Generator(device="cuda").manual_seed(9100 + rank)
     idx = torch.randint(0, CONFIG4["vocab_size"], (B, T), device="cuda", generator=g)
 
-    def run(n_steps, e=None):
-        with torch.no_grad(), bind_caches(m):
-            if e:
-                e[0].record()
+    def run(n_steps, timing):
+        """Prefill, then n_steps greedy steps replayed from one captured CUDA graph; with ``timing`` the
+        prefill and the replays are timed with CUDA events (the capture itself is outside both)."""
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        with torch.no_grad(), bind_caches(m) as caches:
+            ev[0].record()
             logits = m(idx)[0][:, -1]
-            if e:
-                e[1].record()
+            ev[1].record()
+            dec = GraphDecoder(m, caches, logits.argmax(-1))
+            torch.cuda.synchronize()
+            barrier(world)
+            ev[2].record()
             for _ in range(n_steps):
-                logits = m(logits.argmax(-1)[:, None])[0][:, -1]
-            if e:
-                e[2].record()
-            return logits
+                dec.step()
+            ev[3].record()
+            torch.cuda.synchronize()
+        if not timing:
+            return None
+        return ev[0].elapsed_time(ev[1]) / 1e3, ev[2].elapsed_time(ev[3]) / 1e3
 
-    run(4)  # warm-up: one prefill and a few steps
+    run(8, False)  # warm-up: one prefill, a capture and a few replays
     torch.cuda.synchronize()
     barrier(world)
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
-    run(steps, ev)
-    torch.cuda.synchronize()
-    barrier(world)
-    t_pre = max_over_ranks(ev[0].elapsed_time(ev[1]) / 1e3, world)
-    t_dec = max_over_ranks(ev[1].elapsed_time(ev[2]) / 1e3, world)
+    t_pre, t_dec = run(steps, True)
+    t_pre = max_over_ranks(t_pre, world)
+    t_dec = max_over_ranks(t_dec, world)
     del m
     return {"config": "cfg4: 24 gdn blocks d_model 1024 H8 head_dim 128 expand_v 1, SwiGLU 2816, vocab 50304, bf16; "
                       "prefill 16 x 2048 then 256 greedy steps, batch sharded",
             "prefill_ms": t_pre * 1e3, "prefill_tok_s": world * B * T / t_pre,
             "decode_ms_per_step": t_dec / steps * 1e3, "decode_tok_s": world * B * steps / t_dec,
             "prompts_per_rank": B, "gpu_launches": 3 * CONFIG4["n_layer"] * (1 + steps),  # prologue, scan, epilogue per layer and call
-            "note": "eager PyTorch host loop around this package's kernels (projections and MLP are cuBLAS GEMMs)"}
+            "note": "prefill: one eager model call; decode: one captured CUDA graph per step (projections and MLP are "
+                    "cuBLAS GEMMs, the token mixing and the layer prologue/epilogue this package's kernels)"}
 
 
 def bench_fla(args, rank, world, ours_prefill_ms, ours_decode_ms):
@@ -554,8 +559,28 @@ def bench_fla(args, rank, world, ours_prefill_ms, ours_decode_ms):
             "note": "fla's kernels are the checker here, not ours: not counted in gpu_launches"}
 
 
+def keep_freed_heap():
+    """Stop glibc from handing freed heap memory back to the OS between the CPU path's per-token 4 MB
+    temporaries.  Without it a fresh process trims the heap after every free, so each new state tensor
+    is faulted in again page by page: the same code measured 21.6-26.3 K tok/s in a fresh process and
+    57-61 K tok/s with trimming off or in a process whose heap had grown (16 cores).  Returns whether
+    glibc accepted the settings."""
+    try:
+        import ctypes
+
+        libc = ctypes.CDLL("libc.so.6")
+        M_TRIM_THRESHOLD, M_TOP_PAD, M_MMAP_THRESHOLD = -1, -2, -3
+        ok = libc.mallopt(M_MMAP_THRESHOLD, 32 << 20) == 1      # 4 MB tensors come from the heap
+        ok &= libc.mallopt(M_TRIM_THRESHOLD, 1 << 30) == 1      # freed memory stays in the heap
+        ok &= libc.mallopt(M_TOP_PAD, 64 << 20) == 1
+        return bool(ok)
+    except Exception:
+        return False
+
+
 def cpu_reference_setup():
     """Inputs of the CPU legs: the whole configuration-1 batch in fp32 (seed 7), u = beta k."""
+    keep_freed_heap()
     torch.set_num_threads(os.cpu_count() or 1)  # every host core (torchrun sets OMP_NUM_THREADS=1 for its ranks)
     c = CONFIGS["cfg1"]
     x = make_inputs(c.B, c.T, c.H, c.DK, c.DV, seed=7, dtype=torch.float32, device="cpu")
