@@ -230,8 +230,8 @@ def prefill_args(q, k, v, la, beta=None, u=None, initial_state=None, output_fina
     return _prepare(q, k, u, v, la, beta, initial_state, bool(output_final_state), out_dtype, impl)
 
 
-def _prepare(q, k, u, v, la, beta, s0, output_final_state: bool, out_dtype: torch.dtype, impl: str):
-    _check_cuda(q, k, u, v, la, beta, s0)
+def _prepare(q, k, u, v, la, beta, s0, output_final_state: bool, out_dtype: torch.dtype, impl: str, y_out=None):
+    _check_cuda(q, k, u, v, la, beta, s0, y_out)
     in_dtype = torch.bfloat16 if q.dtype == torch.bfloat16 else torch.float32
     q, k, v = (_prep_token(t, n, in_dtype) for t, n in ((q, "q"), (k, "k"), (v, "v")))
     if u is not None:
@@ -255,7 +255,14 @@ def _prepare(q, k, u, v, la, beta, s0, output_final_state: bool, out_dtype: torc
         s0 = s0.float().contiguous()
         if s0.shape != (B, H, DV, DK):
             raise ValueError(f"initial_state must be (B, H, DV, DK) = {(B, H, DV, DK)}")
-    y = torch.empty(B, T, H, DV, device=q.device, dtype=out_dtype)
+    if y_out is None:
+        y = torch.empty(B, T, H, DV, device=q.device, dtype=out_dtype)
+    else:
+        if tuple(y_out.shape) != (B, T, H, DV) or y_out.dtype not in _DT or y_out.device != q.device:
+            raise ValueError(f"y must be a float32 or bfloat16 (B, T, H, DV) = {(B, T, H, DV)} tensor on {q.device}")
+        if y_out.stride(-1) != 1:
+            raise ValueError("y must have a unit last stride")
+        y, out_dtype = y_out, y_out.dtype
     s_out = torch.empty(B, H, DV, DK, device=q.device, dtype=torch.float32) if output_final_state else None
     a = PrefillArgs(
         _ptr(q), _ptr(k), _ptr(u), _ptr(v), _ptr(beta), _ptr(la), _ptr(s0), _ptr(y), _ptr(s_out),
@@ -265,8 +272,8 @@ def _prepare(q, k, u, v, la, beta, s0, output_final_state: bool, out_dtype: torc
     return a, y, s_out, (q, k, u, v, la, beta, s0)
 
 
-def _prefill_impl(q, k, u, v, la, beta, s0, output_final_state: bool, out_dtype: torch.dtype, impl: str):
-    a, y, s_out, _keep = _prepare(q, k, u, v, la, beta, s0, output_final_state, out_dtype, impl)
+def _prefill_impl(q, k, u, v, la, beta, s0, output_final_state: bool, out_dtype: torch.dtype, impl: str, y_out=None):
+    a, y, s_out, _keep = _prepare(q, k, u, v, la, beta, s0, output_final_state, out_dtype, impl, y_out)
     lib = load_library()
     if a.B == 0 or a.H == 0:  # an empty batch: empty outputs, nothing to launch
         return y, s_out
@@ -473,6 +480,16 @@ def gdn_prefill(q, k, v, la, beta=None, u=None, initial_state=None, output_final
     # (workspace for the segmented path is sized and allocated per call by _prefill_impl)
     y, s = _prefill_op(q, k, u, v, la, beta, initial_state, bool(output_final_state), _code(out_dtype, q.dtype if q.dtype in _DT else torch.float32), impl)
     return y, (s if output_final_state else None)
+
+
+def gdn_prefill_into(y, q, k, v, la, beta=None, u=None, initial_state=None, output_final_state=False, impl="auto"):
+    """``gdn_prefill`` writing its output into ``y``, a (B, T, H, DV) tensor or view with any element
+    strides and a unit last stride (e.g. this rank's slice of a head-major all-gather buffer, seen
+    through a permute).  No autograd.  Returns S_T or None."""
+    if impl not in IMPLS:
+        raise ValueError(f"impl must be one of {sorted(IMPLS)}")
+    _, s = _prefill_impl(q, k, u, v, la, beta, initial_state, bool(output_final_state), y.dtype, impl, y_out=y)
+    return s
 
 
 _COPY_STREAMS = {}

@@ -423,7 +423,12 @@ def bench_layer(args, rank, world):
 
 
 def bench_long_context(args, rank, world):
-    """cfg3 heads sharded over ranks; NCCL all-gather of y (strong scaling)."""
+    """cfg3 heads sharded over ranks (strong scaling).  Three timings of the same prefill: compute only;
+    with the NCCL all-gather into a head-major (H, B, T, DV) buffer that the kernel writes its heads into
+    directly (in-place gather, no copy -- the reported ``value``); and with the gather into the
+    (B, T, H, DV) layout (gather then one permute-copy)."""
+    import torch.distributed as dist
+
     from archbench_b200 import ops
     from archbench_b200.sharded import gather_heads
 
@@ -432,26 +437,35 @@ def bench_long_context(args, rank, world):
         return {"skipped": f"H={c.H} not divisible by {world} ranks"}
     h_loc = c.H // world
     x = make_inputs(c.B, c.T, h_loc, c.DK, c.DV, seed=5000 + rank, dtype=c.dtype, device="cuda")
+    full = torch.empty((c.H, c.B, c.T, c.DV), dtype=c.dtype, device="cuda")
+    mine = full[rank * h_loc:(rank + 1) * h_loc]
     out = {}
 
     def step_compute():
         out["y"], _ = ops.gdn_prefill(x["q"], x["k"], x["v"], x["la"], beta=x["beta"])
 
-    def step_gather():
+    def step_gather_head_major():
+        ops.gdn_prefill_into(mine.permute(1, 2, 0, 3), x["q"], x["k"], x["v"], x["la"], beta=x["beta"])
+        if world > 1:
+            dist.all_gather_into_tensor(full, mine)
+
+    def step_gather_bthd():
         step_compute()
         out["full"] = gather_heads(out["y"], world)
 
     steps = max(1, min(args.steps, 10))
     t_c = timed(step_compute, steps, min(args.warmup, 3), world)
-    t_g = timed(step_gather, steps, min(args.warmup, 3), world)
+    t_h = timed(step_gather_head_major, steps, min(args.warmup, 3), world)
+    t_g = timed(step_gather_bthd, steps, min(args.warmup, 3), world)
     tokens = c.B * c.T
-    return {"value": tokens * steps / t_g, "unit": "tok/s", "value_without_gather": tokens * steps / t_c,
-            "ms_per_step": t_g / steps * 1e3, "ms_compute": t_c / steps * 1e3, "heads_per_rank": h_loc, "scaling": "strong",
-            "gpu_launches": steps}
-
-
-CPU_SAMPLE = ("cfg1 B8 T4096 H8 d128 fp32: each step one pass over the whole configuration-1 batch (8 sequences of "
-              "4096 tokens, fed in 64-token slices with the state carried); glibc heap trimming off (mallopt)")
+    sel = ops.selected_impl(x["q"], x["k"], x["v"], x["la"], beta=x["beta"])
+    return {"value": tokens * steps / t_h, "unit": "tok/s", "value_without_gather": tokens * steps / t_c,
+            "value_gather_bthd": tokens * steps / t_g,
+            "ms_per_step": t_h / steps * 1e3, "ms_compute": t_c / steps * 1e3, "ms_gather_head_major": (t_h - t_c) / steps * 1e3,
+            "ms_gather_bthd": (t_g - t_c) / steps * 1e3, "heads_per_rank": h_loc, "kernel": sel, "scaling": "strong",
+            "gather": "NCCL all_gather_into_tensor, in place into a head-major (H, B, T, DV) buffer; value_gather_bthd: "
+                      "gather then permute-copy into (B, T, H, DV)",
+            "gpu_launches": 3 * steps}
 
 
 def bench_lm(args, rank, world):
@@ -633,7 +647,7 @@ def run_ours(args):
     rank, world, local = dist_init(args.gpus)
     if args.only:  # one leg alone (profiling runs): its own object, not the bench line
         res = {"decode": bench_decode, "backward": bench_backward, "layer": bench_layer,
-               "nstep": bench_nstep, "lm": bench_lm}[args.only](args, rank, world)
+               "nstep": bench_nstep, "lm": bench_lm, "long_context": bench_long_context}[args.only](args, rank, world)
         if rank == 0:
             print(json.dumps({"leg": args.only, **res}), flush=True)
         finish(world)
@@ -666,7 +680,7 @@ def run_ours(args):
         if world == 1:
             torch.cuda.empty_cache()
             line["reference_gpu"] = bench_fla(args, rank, world, res["ms_per_step"], line["decode"]["ms_per_step"])
-        line["gpu_launches"] += (line["decode"]["gpu_launches"] + line["long_context"].get("gpu_launches", 0) * 2
+        line["gpu_launches"] += (line["decode"]["gpu_launches"] + line["long_context"].get("gpu_launches", 0)
                                  + line["backward"]["gpu_launches"] + line["e2e"]["gpu_launches"] + line["layer"]["gpu_launches"]
                                  + line["nstep"]["gpu_launches"] + line["lm"].get("gpu_launches", 0))
     if rank == 0 and world == 1 and not args.skip_cpu:
@@ -713,7 +727,7 @@ def main():
     ap.add_argument("--prefill-impl", choices=["auto", "chunk", "chunk_cluster", "chunk_single", "recurrent", "segmented"], default="auto")
     ap.add_argument("--skip-extra", action="store_true", help="headline prefill only")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the cpu_baseline leg")
-    ap.add_argument("--only", choices=["decode", "backward", "layer", "nstep", "lm"], default=None,
+    ap.add_argument("--only", choices=["decode", "backward", "layer", "nstep", "lm", "long_context"], default=None,
                     help="run one extra leg alone and print its object (for profiling)")
     ap.add_argument("--no-graph", dest="graph", action="store_false",
                     help="time plain calls instead of CUDA-graph replays of one call")

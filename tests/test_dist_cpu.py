@@ -2,7 +2,9 @@
 
 * head sharding + all-gather reassemble the full (B, T, H, DV) output on every rank;
 * sharded_prefill runs each rank's heads only (the kernel call is replaced by the CPU oracle
-  here, since this host has no GPU) and the gathered result equals the unsharded oracle;
+  here, since this host has no GPU) and the gathered result equals the unsharded oracle, in the
+  (B, T, H, DV) layout and in the head-major layout whose gather runs in place (the kernel's output
+  view is this rank's slice of the gather buffer);
 * failure detection: when one rank raises before the collective, the other rank's collective
   ends with an error within the process group's short timeout instead of hanging.
 """
@@ -70,6 +72,33 @@ def _worker_sharded(rank, world, port, q):
         q.put((rank, False, repr(e)))
 
 
+def _worker_sharded_head_major(rank, world, port, q):
+    try:
+        _init(rank, world, port)
+        from archbench_b200 import ops, sharded
+        from archbench_b200.workloads import make_inputs
+        from oracle import oracle as O
+
+        seen = []
+
+        def fake_prefill_into(y, q_, k, v, la, beta=None, u=None, initial_state=None, output_final_state=False, impl="auto"):
+            seen.append((tuple(y.shape), y.stride()))
+            out, S = O.recurrence(q_.numpy(), k.numpy(), v.numpy(), la.numpy(), beta=beta.numpy())
+            y.copy_(torch.from_numpy(out).float())  # through the strided view: into the gather buffer
+            return torch.from_numpy(S).float() if output_final_state else None
+
+        ops.gdn_prefill_into = fake_prefill_into
+        x = make_inputs(2, 24, 4, 16, 8, seed=6, dtype=torch.float32)
+        full, _ = sharded.sharded_prefill(x["q"], x["k"], x["v"], x["la"], beta=x["beta"], layout="hbtd")
+        y_ref, _ = O.recurrence(x["q"].numpy(), x["k"].numpy(), x["v"].numpy(), x["la"].numpy(), beta=x["beta"].numpy())
+        ok = (tuple(full.shape) == (4, 2, 24, 8) and seen == [((2, 24, 2, 8), (24 * 8, 8, 2 * 24 * 8, 1))]
+              and np.allclose(full.permute(1, 2, 0, 3).numpy(), y_ref, atol=1e-6))
+        q.put((rank, bool(ok), None))
+        dist.destroy_process_group()
+    except Exception as e:  # pragma: no cover
+        q.put((rank, False, repr(e)))
+
+
 def _worker_failure(rank, world, port, q):
     _init(rank, world, port, timeout_s=4)
     if rank == 1:
@@ -106,6 +135,11 @@ def test_gather_heads_two_ranks():
 
 def test_sharded_prefill_matches_unsharded():
     res = _run(_worker_sharded)
+    assert all(ok for _, ok, _ in res), res
+
+
+def test_sharded_prefill_head_major_gathers_in_place():
+    res = _run(_worker_sharded_head_major)
     assert all(ok for _, ok, _ in res), res
 
 
