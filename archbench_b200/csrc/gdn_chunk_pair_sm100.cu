@@ -899,9 +899,9 @@ int max_active_clusters() {
 }  // namespace pair
 }  // namespace gdn
 
-// DK = DV = 128, u = beta k; the rest as the single-CTA kernel (bf16 inputs, TMA-aligned y).
+// DK = DV = 128, u = beta k; the rest as the single-CTA kernel, and y stored by TMA.
 bool gdn_chunk_pair_supported(const gdn_prefill_args* a) {
-  return a->DV == 128 && a->in_dtype == GDN_DTYPE_BF16 && gdn_chunk_ws_supported(a);
+  return a->DV == 128 && a->in_dtype == GDN_DTYPE_BF16 && gdn_chunk_ws_supported(a) && gdn_y_tma_ok(a);
 }
 
 int gdn_chunk_pair_max_clusters() { return gdn::pair::max_active_clusters(); }

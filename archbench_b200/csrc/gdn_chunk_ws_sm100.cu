@@ -1,8 +1,8 @@
 // Warp-specialised chunkwise gated delta rule (u = beta k) on tcgen05 / TMEM, sm_100a.
 //
-// Same mathematics as gdn_chunk_sm100.cu (the WY form of archbench/layers/nsgdn.py:408-417,
-// derivation as in nsgdn.py:240-249); this version overlaps the state-independent work of
-// chunk c+1 with the state recurrence of chunk c.  One CTA of 384 threads per (b, h, 128-row
+// The WY form of archbench/layers/nsgdn.py:408-417 (derivation as in nsgdn.py:240-249), with the
+// state-independent work of chunk c+1 overlapped with the state recurrence of chunk c.  y goes out
+// by TMA tile stores, or, where y's rows are not 16-byte aligned, by each thread's own stores.  One CTA of 384 threads per (b, h, 128-row
 // slice of the state), three warp groups, each thread bound to the TMEM lane of its warp's
 // quarter:
 //
@@ -22,6 +22,8 @@
 // 16 KB with T16/(T Gamma)16, ordered by the MMA completion barriers.  Every mbarrier wait is
 // bounded and abortable: a timeout raises a shared flag that makes every other wait return,
 // the issuing threads drain their MMAs (bounded) and the CTA releases TMEM and exits.
+#include <string.h>
+
 #include "gdn_tiles.cuh"
 
 namespace gdn {
@@ -74,6 +76,7 @@ struct Params {
   const float* seg_s0;  // mode 0: initial state of segment s >= 1 at slot (bh, s - 1)
   float* seg_out;       // mode 1: [N_s; M_s] of each segment at slot (bh, s)
   int ws_stride;        // slots per (b, h) in the segment workspace
+  int y_direct;         // y rows not 16-byte aligned (no TMA store): each thread writes its feature directly
 };
 
 __device__ int g_status = 0;
@@ -132,7 +135,7 @@ __global__ void __launch_bounds__(NT, 1)
     ptx::prefetch_tensormap(&tm_q);
     ptx::prefetch_tensormap(&tm_k);
     ptx::prefetch_tensormap(&tm_v);
-    ptx::prefetch_tensormap(&tm_y);
+    if (!p.y_direct) ptx::prefetch_tensormap(&tm_y);
     if (HAS_U) ptx::prefetch_tensormap(&tm_u);
   }
   ptx::tc_fence_before();
@@ -224,6 +227,16 @@ __global__ void __launch_bounds__(NT, 1)
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(&bars[B_YE + pp]);
+      if (p.y_direct) {
+        // y rows not 16-byte aligned: every thread stores its feature of the chunk's tokens itself
+        // (a warp writes 32 consecutive features of one token per store), tokens past T skipped.
+        const int t0 = (cb + c) * C;
+        TOut* yrow = static_cast<TOut*>(p.y) + (int64_t)b * p.sy.b + (int64_t)h * p.sy.h + dv0 + row;
+#pragma unroll 8
+        for (int j = 0; j < C; ++j)
+          if (t0 + j < p.T) store_as(yrow + (int64_t)(t0 + j) * p.sy.t, yv[j]);
+        return true;
+      }
       constexpr int ROWS = (int)(TILE / (D * sizeof(TOut)));  // tokens per 8 KB staging piece
       TOut* stage = reinterpret_cast<TOut*>(sm + AB + pp * TILE);
 #pragma unroll
@@ -672,8 +685,10 @@ struct Segmentation {
 template <bool HAS_U, typename TOut>
 int launch(const gdn_prefill_args* a, const Segmentation& sg, cudaStream_t stream) {
   CUtensorMap mq, mk, mv, my, mu;
+  const bool y_tma = gdn_y_tma_ok(a);  // else y is written by direct stores (no tensor map)
+  memset(&my, 0, sizeof(my));
   if (!make_map(&mq, a->q, a->DK, a, a->sq) || !make_map(&mk, a->k, a->DK, a, a->sk) ||
-      !make_map(&mv, a->v, a->DV, a, a->sv) || !make_store_map<TOut>(&my, a->y, a->DV, a, a->sy))
+      !make_map(&mv, a->v, a->DV, a, a->sv) || (y_tma && !make_store_map<TOut>(&my, a->y, a->DV, a, a->sy)))
     return GDN_ERR_LAUNCH;
   if (HAS_U != (a->u != nullptr)) return GDN_ERR_UNSUPPORTED;
   if (HAS_U) {
@@ -696,6 +711,7 @@ int launch(const gdn_prefill_args* a, const Segmentation& sg, cudaStream_t strea
   p.seg_s0 = sg.seg_s0;
   p.seg_out = sg.seg_out;
   p.ws_stride = sg.ws_stride;
+  p.y_direct = y_tma ? 0 : 1;
   const int64_t grid = a->B * a->H * (int64_t)p.nseg * p.ntiles;
   if (grid <= 0 || grid > 0x7fffffff) return GDN_ERR_SHAPE;
   kern<<<(unsigned)grid, NT, DYN, stream>>>(mq, mk, mv, my, mu, p);
@@ -711,12 +727,41 @@ int launch(const gdn_prefill_args* a, cudaStream_t stream) {
 }  // namespace gdn
 
 // DK = 128, DV a multiple of 128; u = beta k or an explicit write vector u.
-bool gdn_chunk_ws_supported(const gdn_prefill_args* a) {
-  if (a->DK != 128 || a->DV % 128 != 0 || a->DV < 128) return false;
+// y can be stored by TMA: 16-byte-aligned base and row strides.
+bool gdn_y_tma_ok(const gdn_prefill_args* a) {
   const int64_t es = a->out_dtype == GDN_DTYPE_BF16 ? 2 : 4;
   auto ok = [&](int64_t x) { return x > 0 && (x * es) % 16 == 0; };
   return a->y && (uintptr_t)a->y % 16 == 0 && ok(a->sy.h) && ok(a->sy.t) && ok(a->sy.b);
 }
+
+// DK = 128 and DV a multiple of 128; y of any strides (TMA stores where y allows them, direct
+// stores otherwise).
+bool gdn_chunk_ws_supported(const gdn_prefill_args* a) {
+  return a->DK == 128 && a->DV % 128 == 0 && a->DV >= 128 && a->DV <= 8 * 128;
+}
+
+namespace {
+// A row of a [B][T][H][D] bf16 tensor can be TMA-loaded: 16-byte-aligned base and strides.
+bool tma_ok(const void* ptr, const gdn_strides& s) {
+  auto a16 = [](int64_t x) { return x > 0 && (x * 2) % 16 == 0 && x * 2 < (1LL << 40); };
+  return ptr && ((uintptr_t)ptr % 16 == 0) && a16(s.h) && a16(s.t) && a16(s.b);
+}
+}  // namespace
+
+// The chunked path (the single-CTA kernel, or the cluster kernel where it applies): bf16 inputs,
+// DK = 128, DV a multiple of 128 up to 1024, u = beta k or an explicit write vector u (nsgdn
+// n_steps > 1), 16-byte-aligned q/k/u/v rows for the TMA loads and states for the vector accesses.
+bool gdn_chunk_supported(const gdn_prefill_args* a) {
+  if (a->in_dtype != GDN_DTYPE_BF16 || a->DK != 128 || a->T < 1) return false;
+  if (!tma_ok(a->q, a->sq) || !tma_ok(a->k, a->sk) || !tma_ok(a->v, a->sv)) return false;
+  if (a->u && !tma_ok(a->u, a->su)) return false;
+  if ((a->s0 && (uintptr_t)a->s0 % 16) || (a->s_out && (uintptr_t)a->s_out % 16)) return false;
+  return gdn_chunk_ws_supported(a);
+}
+
+int gdn_launch_chunk_sm100(const gdn_prefill_args* a, cudaStream_t stream) { return gdn_launch_chunk_ws(a, stream); }
+
+int gdn_chunk_read_status(int* out, int reset) { return gdn_chunk_ws_read_status(out, reset); }
 
 int gdn_launch_chunk_ws(const gdn_prefill_args* a, cudaStream_t stream) {
   return a->out_dtype == GDN_DTYPE_BF16 ? gdn::ws::launch<__nv_bfloat16>(a, stream) : gdn::ws::launch<float>(a, stream);

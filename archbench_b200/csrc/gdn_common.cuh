@@ -85,6 +85,7 @@ int gdn_launch_chunk_sm100(const gdn_prefill_args* a, cudaStream_t stream);
 bool gdn_chunk_supported(const gdn_prefill_args* a);
 int gdn_chunk_read_status(int* out, int reset);
 bool gdn_chunk_ws_supported(const gdn_prefill_args* a);
+bool gdn_y_tma_ok(const gdn_prefill_args* a);
 int gdn_launch_chunk_ws(const gdn_prefill_args* a, cudaStream_t stream);
 int gdn_chunk_ws_read_status(int* out, int reset);
 int gdn_launch_selftest_wait(long long max_cycles, cudaStream_t stream);

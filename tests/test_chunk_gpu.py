@@ -235,21 +235,29 @@ def test_empty_inputs(impl):
 
 
 @pytest.mark.parametrize("T", [100, 192])
-def test_write_vectors_unaligned_y_rows(T):
-    """An explicit u with y rows that are not 16-byte aligned (fp32 y with a row stride of 129
-    elements) cannot take the TMA-storing kernel; the single-warp-group kernel serves it."""
+@pytest.mark.parametrize("with_u", [True, False])
+def test_unaligned_y_rows(T, with_u):
+    """y rows that are not 16-byte aligned (fp32 y with a row stride of 129 elements) cannot be TMA
+    stores: the single-CTA kernel writes them with its own stores (auto selection), for an explicit u
+    and for u = beta k."""
     import ctypes
 
     B, H = 2, 2
     x = make_inputs(B, T, H, 128, 128, seed=31 + T, dtype=torch.bfloat16)
-    u = (x["beta"][..., None] * x["k"].float()).to(torch.bfloat16)
-    y_o, S_o = O.recurrence_c(*(np32(x[n]) for n in ("q", "k", "v", "la")), u=np32(u))
+    u = (x["beta"][..., None] * x["k"].float()).to(torch.bfloat16) if with_u else None
+    y_o, S_o = O.recurrence_c(*(np32(x[n]) for n in ("q", "k", "v", "la")), u=None if u is None else np32(u),
+                              beta=None if with_u else np32(x["beta"]))
     g = {k: v.cuda() for k, v in x.items()}
-    a, _, s_out, keep = ops._prepare(g["q"], g["k"], u.cuda(), g["v"], g["la"], None, None, True, torch.float32, "chunk_single")
+    a, _, s_out, keep = ops._prepare(g["q"], g["k"], None if u is None else u.cuda(), g["v"], g["la"],
+                                     None if with_u else g["beta"], None, True, torch.float32, "auto")
     ybuf = torch.full((B, T, H, 129), float("nan"), device="cuda")
     a.y, a.sy = ybuf.data_ptr(), ops.Strides(T * H * 129, H * 129, 129)
-    ops._check(ops.load_library().gdn_prefill_fwd(ctypes.byref(a), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
+    lib = ops.load_library()
+    assert lib.gdn_prefill_select_impl(ctypes.byref(a)) == 5  # GDN_IMPL_CHUNK_SINGLE
+    ops._check(lib.gdn_prefill_fwd(ctypes.byref(a), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
     torch.cuda.synchronize()
-    check(ybuf[..., :128], y_o, "y (u given, unaligned y rows)")
-    check(s_out, S_o, "S_T (u given, unaligned y rows)")
+    what = "u given" if with_u else "u = beta k"
+    check(ybuf[..., :128], y_o, f"y ({what}, unaligned y rows)")
+    check(s_out, S_o, f"S_T ({what}, unaligned y rows)")
     assert torch.isnan(ybuf[..., 128]).all()
+    assert ops.device_status() == 0
