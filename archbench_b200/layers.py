@@ -52,6 +52,8 @@ class GDNCache:
 def _put(cache: GDNCache, key: str, value: torch.Tensor) -> None:
     """Store a conv-state entry; a static cache overwrites the tensor it already holds."""
     old = cache.conv.get(key)
+    if old is not None and old.shape == value.shape and old.data_ptr() == value.data_ptr():
+        return  # written in place by the kernel
     if cache.static and old is not None and old.shape == value.shape:
         old.copy_(value)
     else:
@@ -197,14 +199,16 @@ class NStepGDN(nn.Module):
             q, k, v, la, beta, new_state, u, k_last = ops.layer_prologue(
                 *parts, self.A_log, self.dt_bias, H=H, DK=DK, DV=DV, b_bias=self.b_bias, conv=conv, conv_state=state,
                 want_state=cache is not None, q_scale=DK**-0.5, la_min=self.la_min, out_dtype=dt, n_steps=self.n_steps,
-                lam=F.softplus(self.lam.float()), k_prev=None if kp is None else kp.reshape(B, H, DK))
+                lam=ops._cached(self.lam, "softplus", lambda t: F.softplus(t.float())),
+                k_prev=None if kp is None else kp.reshape(B, H, DK), in_place=cache is not None and cache.static)
             if cache is not None:
                 _put(cache, "k_prev", k_last.reshape(B, 1, H, DK))
         else:
             q, k, v, la, beta, new_state = ops.layer_prologue(
                 *parts, self.A_log, self.dt_bias, H=H, DK=DK, DV=DV, b_bias=self.b_bias, conv=conv, conv_state=state,
-                want_state=cache is not None, q_scale=DK**-0.5, la_min=self.la_min, out_dtype=dt)
-        if cache is not None and new_state is not None:
+                want_state=cache is not None, q_scale=DK**-0.5, la_min=self.la_min, out_dtype=dt,
+                in_place=cache is not None and cache.static)
+        if cache is not None and new_state is not None and not (state is not None and new_state[0] is state[0]):
             _put(cache, "qkv", torch.cat(new_state, 1))
         y = _mix(q, k, v, la, None if u is not None else beta, u, cache, self._impl)
         if cache is not None:
@@ -332,9 +336,19 @@ class GatedDeltaNet(nn.Module):
             conv = (self.q_conv1d.weight, self.k_conv1d.weight, self.v_conv1d.weight)
             if cache is not None and cache.conv.get("q") is not None:
                 state = (cache.conv["q"], cache.conv["k"], cache.conv["v"])
-        xq, xk, xv, xa, xb = self.q_proj(x), self.k_proj(x), self.v_proj(x), self.a_proj(x), self.b_proj(x)
         dt = torch.bfloat16 if DK == 128 else torch.float32
         train = _training(x, self)
+        g = None
+        if train:
+            xq, xk, xv, xa, xb = self.q_proj(x), self.k_proj(x), self.v_proj(x), self.a_proj(x), self.b_proj(x)
+        else:  # one GEMM for all six projections (their weights concatenated once, kept while unchanged)
+            proj = F.linear(x, self._projection_weight())
+            kd, vd, nh = self.key_dim, self.value_dim, self.num_v_heads
+            xq, xk, xv = proj[..., :kd], proj[..., kd:2 * kd], proj[..., 2 * kd:2 * kd + vd]
+            o0 = 2 * kd + vd
+            if self.use_gate:
+                g, o0 = proj[..., o0:o0 + vd], o0 + vd
+            xa, xb = proj[..., o0:o0 + nh], proj[..., o0 + nh:o0 + 2 * nh]
         if train:
             q, k, v, la, beta = ops.layer_prologue_train(
                 xq, xk, xv, xa.to(xq.dtype), xb.to(xq.dtype), self.A_log, self.dt_bias, H=H, DK=DK, DV=DV, conv=conv,
@@ -344,19 +358,33 @@ class GatedDeltaNet(nn.Module):
             q, k, v, la, beta, new_state = ops.layer_prologue(
                 xq, xk, xv, xa.to(xq.dtype), xb.to(xq.dtype), self.A_log, self.dt_bias, H=H, DK=DK, DV=DV, conv=conv,
                 conv_state=state, want_state=cache is not None, q_scale=DK**-0.5, l2_eps=1e-6,
-                beta_scale=2.0 if self.allow_neg_eigval else 1.0, out_dtype=dt)
+                beta_scale=2.0 if self.allow_neg_eigval else 1.0, out_dtype=dt, in_place=cache is not None and cache.static)
         if cache is not None and new_state is not None:
             for key, st in zip("qkv", new_state):
                 _put(cache, key, st)
         o = _mix(q, k, v, la, beta, None, cache, "auto")
         if cache is not None:
             cache.seen += T
-        g = self.g_proj(x) if self.use_gate else None
+        if train and self.use_gate:
+            g = self.g_proj(x)
         epi = ops.layer_epilogue_train if train else ops.layer_epilogue
         o = epi(o, self.o_norm.weight, g, eps=self.o_norm.eps, out_dtype=x.dtype)
         return self.o_proj(o)
 
     bound_cache: Optional[GDNCache] = None  # used when called without a cache (decode.bind_caches)
+
+    def _projection_weight(self) -> torch.Tensor:
+        """[q; k; v; g; a; b] projection weights in one matrix, rebuilt when any of them changes."""
+        ws = [self.q_proj.weight, self.k_proj.weight, self.v_proj.weight]
+        ws += [self.g_proj.weight] if self.use_gate else []
+        ws += [self.a_proj.weight, self.b_proj.weight]
+        key = tuple((w.data_ptr(), w._version, w.dtype, w.device) for w in ws)
+        hit = getattr(self, "_proj_cat", None)
+        if hit is None or hit[0] != key:
+            with torch.no_grad():
+                hit = (key, torch.cat(ws, 0))
+            self._proj_cat = hit
+        return hit[1]
 
     def forward(self, hidden_states: torch.Tensor, cache: Optional[GDNCache] = None, **kwargs) -> torch.Tensor:
         if cache is None:

@@ -603,6 +603,33 @@ def selftest_bounded_wait(max_cycles: int = 2_000_000) -> int:
 _DTC = {torch.bfloat16: GDN_DTYPE_BF16, torch.float32: GDN_DTYPE_F32}
 
 
+def _cached(t: torch.Tensor, kind: str, make):
+    """``make(t)`` (a derived copy of a parameter: fp32, transposed, ...), kept on the tensor object and
+    reused while the tensor is unchanged (same storage and version counter).  Calls that record
+    autograd history on ``t`` compute afresh.  Inference and CUDA-graph decode steps then launch no
+    conversion kernels for the layer's constants."""
+    if torch.is_grad_enabled() and t.requires_grad:
+        return make(t)
+    key = (t.data_ptr(), t._version, tuple(t.shape), t.dtype, t.device)
+    store = getattr(t, "_gdn_derived", None)
+    if store is None:
+        store = {}
+        try:
+            t._gdn_derived = store
+        except (AttributeError, RuntimeError):
+            return make(t)
+    hit = store.get(kind)
+    if hit is not None and hit[0] == key:
+        return hit[1]
+    val = make(t)
+    store[kind] = (key, val)
+    return val
+
+
+def _f32(t: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
+    return None if t is None else _cached(t, "f32", lambda x: x.float().contiguous())
+
+
 def _rows16(t: torch.Tensor) -> torch.Tensor:
     """A (B, T, C) view with unit channel stride and 16-byte aligned (b, t) strides, else a copy."""
     es = t.element_size()
@@ -613,7 +640,7 @@ def _rows16(t: torch.Tensor) -> torch.Tensor:
 
 def layer_prologue(xq, xk, xv, xa, xb, A_log, dt_bias, *, H, DK, DV, b_bias=None, conv=None, conv_state=None,
                    want_state=False, q_scale=1.0, l2_eps=1e-12, la_min=None, beta_scale=1.0, out_dtype=torch.bfloat16,
-                   n_steps=1, lam=None, k_prev=None):
+                   n_steps=1, lam=None, k_prev=None, in_place=False):
     """q, k, v (B, T, H, D) in ``out_dtype`` and la, beta (B, T, H) fp32 from the layer's
     projections, in one CUDA kernel: SiLU(short causal conv) of each projection, l2-normalised q
     (times ``q_scale``) and k, la = -softplus(a + dt_bias) exp(A_log) (clamped at ``la_min``),
@@ -622,7 +649,10 @@ def layer_prologue(xq, xk, xv, xa, xb, A_log, dt_bias, *, H, DK, DV, b_bias=None
     (B, channels, conv_size - 1) continues a previous call.  Returns (q, k, v, la, beta, new_state)
     with new_state None unless ``want_state``.  With ``n_steps`` > 1 (nsgdn write vectors, ``lam`` the
     per-head step sizes, ``k_prev`` (B, H, DK) the previous call's last normalised k or None) it returns
-    (q, k, v, la, beta, new_state, u, k_last) with k_last (B, H, DK) fp32 when ``want_state``."""
+    (q, k, v, la, beta, new_state, u, k_last) with k_last (B, H, DK) fp32 when ``want_state``.
+    ``in_place`` (one token, ``want_state``, a conv state given): the new conv state (and k_last) are
+    written over ``conv_state`` (and ``k_prev``) and those tensors are returned; a one-token call is
+    one run of one warp per (b, h), which reads the old state before it writes the new one."""
     _check_cuda(xq, xk, xv, xa, xb)
     dt = xq.dtype
     if dt not in _DTC or any(t.dtype != dt for t in (xk, xv, xa, xb)):
@@ -636,19 +666,32 @@ def layer_prologue(xq, xk, xv, xa, xb, A_log, dt_bias, *, H, DK, DV, b_bias=None
     la = torch.empty(B, T, H, device=dev, dtype=torch.float32)
     beta = torch.empty(B, T, H, device=dev, dtype=torch.float32)
     taps = 1 if conv is None else conv[0].shape[-1]
-    ws = [None, None, None] if conv is None else [w.reshape(w.shape[0], taps).float().t().contiguous() for w in conv]
-    cin = [None, None, None] if conv_state is None else [c.to(dt).contiguous() for c in conv_state]
-    cout = [None, None, None]
-    if want_state and taps > 1:
-        cout = [torch.empty(B, ch, taps - 1, device=dev, dtype=dt) for ch in (H * DK, H * DK, H * DV)]
-    A_log, dt_bias = A_log.float().contiguous(), dt_bias.float().contiguous()
-    b_bias = None if b_bias is None else b_bias.float().contiguous()
-    st = lambda c: 0 if c is None else c.stride(0)
+    ws = [None, None, None] if conv is None else [
+        _cached(w, f"convT{taps}", lambda x: x.reshape(x.shape[0], taps).float().t().contiguous()) for w in conv]
     nstep = int(n_steps) > 1
+    in_place = bool(in_place) and T == 1 and want_state and taps > 1 and conv_state is not None
+    if in_place:  # the state tensors are read and rewritten by the kernel: channel stride taps - 1, unit last
+        for c, ch in zip(conv_state, (H * DK, H * DK, H * DV)):
+            if c.dtype != dt or tuple(c.shape) != (B, ch, taps - 1) or c.stride(2) != 1 or c.stride(1) != taps - 1:
+                in_place = False
+        if nstep and k_prev is not None and (k_prev.dtype != torch.float32 or not k_prev.is_contiguous()):
+            in_place = False
+    if in_place:
+        cin = list(conv_state)
+        cout = list(conv_state)
+    else:
+        cin = [None, None, None] if conv_state is None else [c.to(dt).contiguous() for c in conv_state]
+        cout = [None, None, None]
+        if want_state and taps > 1:
+            cout = [torch.empty(B, ch, taps - 1, device=dev, dtype=dt) for ch in (H * DK, H * DK, H * DV)]
+    A_log, dt_bias, b_bias = _f32(A_log), _f32(dt_bias), _f32(b_bias)
+    st = lambda c: 0 if c is None else c.stride(0)
     u = torch.empty(B, T, H, DK, device=dev, dtype=out_dtype) if nstep else None
     lam32 = lam.float().contiguous() if nstep else None
     kp_in = k_prev.reshape(B, H, DK).float().contiguous() if (nstep and k_prev is not None) else None
-    kp_out = torch.empty(B, H, DK, device=dev, dtype=torch.float32) if (nstep and want_state) else None
+    kp_out = None
+    if nstep and want_state:
+        kp_out = kp_in if (in_place and kp_in is not None) else torch.empty(B, H, DK, device=dev, dtype=torch.float32)
     a = PrologueArgs(
         _ptr(xq), _ptr(xk), _ptr(xv), xq.stride(0), xq.stride(1), xk.stride(0), xk.stride(1), xv.stride(0), xv.stride(1),
         _ptr(xa), _ptr(xb), xa.stride(0), xa.stride(1), xb.stride(0), xb.stride(1),
@@ -680,7 +723,7 @@ def layer_epilogue(y, weight, g=None, eps=1e-5, out_dtype=torch.bfloat16):
     if g is not None:
         g = _rows16(g.reshape(B, T, H * DV))
     o = torch.empty(B, T, H * DV, device=y.device, dtype=out_dtype)
-    w = weight.float().contiguous()
+    w = _f32(weight)
     a = EpilogueArgs(_ptr(y), _tok_strides(y), _ptr(g), 0 if g is None else g.stride(0), 0 if g is None else g.stride(1),
                      _ptr(w), _ptr(o), o.stride(0), o.stride(1), B, T, H, DV, _DTC[y.dtype],
                      _DTC[g.dtype] if g is not None else GDN_DTYPE_F32, _DTC[out_dtype], float(eps))
