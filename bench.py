@@ -477,7 +477,7 @@ def bench_lm(args, rank, world):
     from archbench_b200.decode import GraphDecoder, bind_caches
     from archbench_b200.lm import CONFIG4, config4_lm
 
-    B_all, T, steps = 16, 2048, 256
+    B_all, T, steps = 16, 2048, args.lm_steps
     if B_all % world:
         return {"skipped": f"batch {B_all} not divisible by {world} ranks"}
     B = B_all // world
@@ -729,6 +729,8 @@ def main():
     ap.add_argument("--skip-cpu", action="store_true", help="omit the cpu_baseline leg")
     ap.add_argument("--only", choices=["decode", "backward", "layer", "nstep", "lm", "long_context"], default=None,
                     help="run one extra leg alone and print its object (for profiling)")
+    ap.add_argument("--lm-steps", type=int, default=256,
+                    help="greedy decode steps of the configuration-4 leg (256 in the benchmark configuration)")
     ap.add_argument("--no-graph", dest="graph", action="store_false",
                     help="time plain calls instead of CUDA-graph replays of one call")
     args = ap.parse_args()
