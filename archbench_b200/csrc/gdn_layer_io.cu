@@ -328,6 +328,140 @@ __global__ void __launch_bounds__(32 * TOKS) prologue_kernel(const PrologueParam
   }
 }
 
+// One-token calls (decode steps): one warp per (b, h) and nothing staged.  The same arithmetic as
+// prologue_kernel at T = 1, in the same order: the window is the incoming conv state and the token's
+// projection row, the conv weights are rounded to the projection dtype as read from the fp32 copy.
+// The new conv state of a channel is written by the lane that read the old one, after reading it,
+// so it may overwrite the incoming state in place.
+template <typename TX, int TAPS, int NPL>
+__device__ __forceinline__ void conv_window(const Comp& cp, int b, int c0, float (&r)[TAPS][NPL], float (&out)[NPL]) {
+#pragma unroll
+  for (int j = 0; j < TAPS; ++j) load_row<TX, NPL>(cp, b, j - (TAPS - 1), TAPS, c0, r[j]);
+  if (cp.w) {
+    float acc[NPL];
+#pragma unroll
+    for (int n = 0; n < NPL; ++n) acc[n] = 0.f;
+#pragma unroll
+    for (int j = 0; j < TAPS; ++j) {
+      float wj[NPL];
+      load_f32<NPL>(cp.w + (int64_t)j * cp.wch + c0, wj);
+#pragma unroll
+      for (int n = 0; n < NPL; ++n) acc[n] = fmaf(round_to<TX>(wj[n]), r[j][n], acc[n]);
+    }
+#pragma unroll
+    for (int n = 0; n < NPL; ++n) out[n] = round_to<TX>(silu(round_to<TX>(acc[n])));
+  } else {
+#pragma unroll
+    for (int n = 0; n < NPL; ++n) out[n] = round_to<TX>(silu(r[TAPS - 1][n]));
+  }
+}
+
+template <typename TX, int TAPS, int NPL>
+__device__ __forceinline__ void conv_state_out(const Comp& cp, int b, int c0, const float (&r)[TAPS][NPL]) {
+  if (TAPS < 2 || !cp.cout) return;
+  TX* pc = reinterpret_cast<TX*>(cp.cout) + (int64_t)b * cp.csb;
+#pragma unroll
+  for (int n = 0; n < NPL; ++n)
+#pragma unroll
+    for (int j = 0; j + 1 < TAPS; ++j) store_as(pc + (int64_t)(c0 + n) * (TAPS - 1) + j, r[j + 1][n]);
+}
+
+template <typename TX, typename TO, int NK, int NV, int TAPS>
+__global__ void __launch_bounds__(128) prologue_decode_kernel(const PrologueParams p) {
+  const int lane = threadIdx.x & 31;
+  const int bh = blockIdx.x * 4 + (threadIdx.x >> 5);
+  if (bh >= p.B * p.H) return;
+  const int b = bh / p.H, h = bh - b * p.H;
+  constexpr int DK = 32 * NK, DV = 32 * NV;
+  float rq[TAPS][NK], rk[TAPS][NK], rv[TAPS][NV];
+  float q[NK], k[NK], v[NV];
+  conv_window<TX, TAPS, NK>(p.q, b, h * DK + lane * NK, rq, q);
+  conv_window<TX, TAPS, NK>(p.k, b, h * DK + lane * NK, rk, k);
+  conv_window<TX, TAPS, NV>(p.v, b, h * DV + lane * NV, rv, v);
+  const bool nstep = p.n_steps > 1;
+  float kp[NK];
+#pragma unroll
+  for (int n = 0; n < NK; ++n) kp[n] = 0.f;
+  if (nstep && p.kprev_in) load_f32<NK>(p.kprev_in + ((int64_t)b * p.H + h) * DK + lane * NK, kp);
+  conv_state_out<TX, TAPS, NK>(p.q, b, h * DK + lane * NK, rq);
+  conv_state_out<TX, TAPS, NK>(p.k, b, h * DK + lane * NK, rk);
+  conv_state_out<TX, TAPS, NV>(p.v, b, h * DV + lane * NV, rv);
+  float sq = 0.f, sk = 0.f;
+#pragma unroll
+  for (int n = 0; n < NK; ++n) {
+    sq = fmaf(q[n], q[n], sq);
+    sk = fmaf(k[n], k[n], sk);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    sq += __shfl_xor_sync(0xffffffffu, sq, o);
+    sk += __shfl_xor_sync(0xffffffffu, sk, o);
+  }
+  const float iq = p.q_scale / fmaxf(sqrtf(sq), p.eps), ik = 1.f / fmaxf(sqrtf(sk), p.eps);
+  const int64_t tok = (int64_t)b * p.H + h;  // T = 1
+#pragma unroll
+  for (int n = 0; n < NK; ++n) {
+    q[n] *= iq;
+    k[n] *= ik;
+  }
+  store_vec<TO, NK>(reinterpret_cast<TO*>(p.q.out) + tok * DK + lane * NK, q);
+  store_vec<TO, NK>(reinterpret_cast<TO*>(p.k.out) + tok * DK + lane * NK, k);
+  store_vec<TO, NV>(reinterpret_cast<TO*>(p.v.out) + tok * DV + lane * NV, v);
+  const float dtb = p.dt_bias[h], Ae = expf(p.A_log[h]), bb_h = p.b_bias ? p.b_bias[h] : 0.f;
+  const float xbt = to_f32(reinterpret_cast<const TX*>(p.xb)[(int64_t)b * p.sb_b + h]);
+  if (nstep) {  // u = beta k, then n - 1 steps u -= lam beta (p . u) (p - (p . k) k)   (nsgdn.py:61-75)
+    const float bt = p.beta_scale / (1.f + expf(-(xbt + bb_h)));
+    const float lam_h = p.lam[h];
+    float pk = 0.f;
+#pragma unroll
+    for (int n = 0; n < NK; ++n) pk = fmaf(kp[n], k[n], pk);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) pk += __shfl_xor_sync(0xffffffffu, pk, o);
+    float u[NK], pp[NK];
+#pragma unroll
+    for (int n = 0; n < NK; ++n) {
+      pp[n] = kp[n] - pk * k[n];
+      u[n] = bt * k[n];
+    }
+    const float lb = lam_h * bt;
+#pragma unroll 1
+    for (int st = 1; st < p.n_steps; ++st) {
+      float pu = 0.f;
+#pragma unroll
+      for (int n = 0; n < NK; ++n) pu = fmaf(kp[n], u[n], pu);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) pu += __shfl_xor_sync(0xffffffffu, pu, o);
+#pragma unroll
+      for (int n = 0; n < NK; ++n) u[n] -= lb * pu * pp[n];
+    }
+    store_vec<TO, NK>(reinterpret_cast<TO*>(p.u) + tok * DK + lane * NK, u);
+    if (p.kprev_out) {
+#pragma unroll
+      for (int n = 0; n < NK; ++n) p.kprev_out[((int64_t)b * p.H + h) * DK + lane * NK + n] = k[n];
+    }
+  }
+  if (lane == 0) {  // the gates of the token
+    const float a = to_f32(reinterpret_cast<const TX*>(p.xa)[(int64_t)b * p.sa_b + h]);
+    float la = -softplus(a + dtb) * Ae;
+    if (p.clamp) la = fmaxf(la, p.la_min);
+    p.la[tok] = la;
+    p.beta[tok] = p.beta_scale / (1.f + expf(-(xbt + bb_h)));
+  }
+}
+
+template <typename TX, typename TO, int NK, int NV>
+int launch_prologue_decode(const PrologueParams& p, cudaStream_t s) {
+  const unsigned blocks = (unsigned)(((int64_t)p.B * p.H + 3) / 4);
+  switch (p.taps) {
+    case 1: prologue_decode_kernel<TX, TO, NK, NV, 1><<<blocks, 128, 0, s>>>(p); break;
+    case 2: prologue_decode_kernel<TX, TO, NK, NV, 2><<<blocks, 128, 0, s>>>(p); break;
+    case 3: prologue_decode_kernel<TX, TO, NK, NV, 3><<<blocks, 128, 0, s>>>(p); break;
+    case 4: prologue_decode_kernel<TX, TO, NK, NV, 4><<<blocks, 128, 0, s>>>(p); break;
+    default: return GDN_ERR_SHAPE;
+  }
+  return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+}
+
 struct EpilogueParams {
   const void* y;
   gdn_strides sy;
@@ -411,6 +545,15 @@ int launch_prologue_taps(const PrologueParams& p, unsigned blocks, size_t sm, cu
 
 template <typename TX, typename TO>
 int launch_prologue(PrologueParams p, cudaStream_t s) {
+  if (p.T == 1) {  // decode steps: one warp per (b, h), no staging
+    p.run = 1;
+    const int nk = p.DK / 32, nv = p.DV / 32;
+#define GDN_PRO1(NK, NV) \
+    if (nk == NK && nv == NV) return launch_prologue_decode<TX, TO, NK, NV>(p, s);
+    GDN_PRO1(2, 2) GDN_PRO1(2, 4) GDN_PRO1(4, 4) GDN_PRO1(4, 8) GDN_PRO1(8, 8) GDN_PRO1(8, 16)
+#undef GDN_PRO1
+    return GDN_ERR_UNSUPPORTED;
+  }
   // the longest run (16, 8, .. 1 tokens per warp) whose staging leaves room for 5 blocks per SM (44 KB),
   // else the longest that fits the budget
   int run = 16;
