@@ -161,6 +161,7 @@ class NStepGDN(nn.Module):
         self.layer_idx = layer_idx
         self.fused_io = True
 
+    @torch.compiler.disable  # ctypes kernel calls run eagerly; the compiled graph breaks around them
     def _forward_fused(self, x: torch.Tensor, proj: torch.Tensor, cache: Optional[GDNCache]) -> torch.Tensor:
         B, T, _ = x.shape
         H, DK, DV = self.H, self.DK, self.DV
@@ -328,6 +329,7 @@ class GatedDeltaNet(nn.Module):
         self.o_proj = nn.Linear(self.value_dim, hidden_size, bias=False)
         self.fused_io = True
 
+    @torch.compiler.disable  # ctypes kernel calls run eagerly; the compiled graph breaks around them
     def _forward_fused(self, x: torch.Tensor, cache: Optional[GDNCache]) -> torch.Tensor:
         B, T, _ = x.shape
         H, DK, DV = self.num_heads, self.head_k_dim, self.head_v_dim

@@ -2,7 +2,9 @@
 ``include/gdn_b200.h`` (``libgdn_b200.so``) plus ``torch.library`` custom ops.
 
 There is no CPU path and no other backend: every function here requires CUDA tensors and the
-native library, and raises if either is missing.
+native library, and raises if either is missing.  Under ``torch.compile`` the kernels are opaque:
+custom ops with fake implementations, or host functions the compiler does not trace
+(``torch.compiler.disable``: the ctypes calls run eagerly between compiled regions).
 
 Public functions
   gdn_prefill(q, k, v, la, beta=None, u=None, initial_state=None, output_final_state=False,
@@ -482,6 +484,7 @@ def gdn_prefill(q, k, v, la, beta=None, u=None, initial_state=None, output_final
     return y, (s if output_final_state else None)
 
 
+@torch.compiler.disable
 def gdn_prefill_into(y, q, k, v, la, beta=None, u=None, initial_state=None, output_final_state=False, impl="auto"):
     """``gdn_prefill`` writing its output into ``y``, a (B, T, H, DV) tensor or view with any element
     strides and a unit last stride (e.g. this rank's slice of a head-major all-gather buffer, seen
@@ -501,6 +504,7 @@ def _copy_streams(dev: torch.device):
     return _COPY_STREAMS[dev.index]
 
 
+@torch.compiler.disable
 def gdn_prefill_from_host(q, k, v, la, beta, y_out, pieces=8, impl="auto", device=None):
     """Prefill of host tensors (pinned, for asynchronous copies) into the host tensor ``y_out``.
 
@@ -553,6 +557,7 @@ def nsgdn_scan(q, k, u, v, la) -> torch.Tensor:
     return gdn_prefill(q, k, v, la, u=u)[0]
 
 
+@torch.compiler.disable
 def selected_impl(q, k, v, la, beta=None, u=None, impl="auto") -> str:
     """Name of the kernel ``gdn_prefill`` runs for these arguments ("chunk_cluster", "chunk_single",
     "segmented" or "recurrent")."""
@@ -579,6 +584,7 @@ def selected_impl(q, k, v, la, beta=None, u=None, impl="auto") -> str:
     return IMPL_NAMES[r]
 
 
+@torch.compiler.disable
 def device_status(reset: bool = False) -> int:
     """The sticky device-side status word (0 = no kernel reported a bounded-wait timeout)."""
     out = ctypes.c_int(0)
@@ -586,6 +592,7 @@ def device_status(reset: bool = False) -> int:
     return out.value
 
 
+@torch.compiler.disable
 def selftest_bounded_wait(max_cycles: int = 2_000_000) -> int:
     """Run the device-side bounded-wait self test and return the status word it leaves
     (GDN_ERR_TIMEOUT = -8 when the wait gave up as designed).  Clears the word first."""
@@ -638,6 +645,7 @@ def _rows16(t: torch.Tensor) -> torch.Tensor:
     return t
 
 
+@torch.compiler.disable
 def layer_prologue(xq, xk, xv, xa, xb, A_log, dt_bias, *, H, DK, DV, b_bias=None, conv=None, conv_state=None,
                    want_state=False, q_scale=1.0, l2_eps=1e-12, la_min=None, beta_scale=1.0, out_dtype=torch.bfloat16,
                    n_steps=1, lam=None, k_prev=None, in_place=False):
@@ -712,6 +720,7 @@ def layer_prologue(xq, xk, xv, xa, xb, A_log, dt_bias, *, H, DK, DV, b_bias=None
     return q, k, v, la, beta, st
 
 
+@torch.compiler.disable
 def layer_epilogue(y, weight, g=None, eps=1e-5, out_dtype=torch.bfloat16):
     """o (B, T, H*DV) = RMSNorm over each head's DV values of y (B, T, H, DV) times ``weight``,
     times SiLU(g) when g (B, T, H*DV) is given; fp32 arithmetic, one rounding to ``out_dtype``."""
@@ -860,6 +869,7 @@ def _run_epilogue_bwd(y, weight, g, do, dy, dg, eps):
     return dw
 
 
+@torch.compiler.disable
 def write_vectors_bwd(k, beta, lam, du, dk, n_steps):
     """Backward of the n-step write vectors u(k, beta, lam) (archbench/layers/nsgdn.py:61-75, p = the
     previous token's k, zero before the first) in one CUDA kernel (gdn_write_vectors_bwd): adds
