@@ -1,6 +1,7 @@
 """Benchmark of the gated-DeltaNet hot path on B200 (one JSON line on rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--skip-extra] [--only decode|backward|layer]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--skip-extra]
+                    [--only decode|backward|layer|nstep|lm|long_context|fla] [--lm-steps S]
     torchrun --nproc-per-node N bench.py --gpus N ...
 
 Headline (``value``): chunkwise prefill of configuration 1 -- B=8, T=4096, H=8, DK=DV=128,
@@ -522,6 +523,13 @@ def bench_lm(args, rank, world):
                     "cuBLAS GEMMs, the token mixing and the layer prologue/epilogue this package's kernels)"}
 
 
+# fla's backward is not run here: on this pool's B200 its chunk_gated_delta_rule backward (fla 0.5.1, which
+# dispatched chunk_bwd_dqkwg to its TileLang backend) stopped with "CUDA error: misaligned address" on the
+# configuration-1 inputs below (contiguous bf16 q/k/v/dy, fp32 gates) after the forward had run cleanly.
+FLA_BACKWARD_NOT_RUN = ("not run: fla 0.5.1's backward (chunk_bwd_dqkwg, TileLang backend) raised CUDA "
+                        "'misaligned address' on this box's B200 with the configuration-1 inputs")
+
+
 def bench_fla(args, rank, world, ours_prefill_ms, ours_decode_ms):
     """The reference's own GPU kernels on this box: fla 0.5.1's Triton ``chunk_gated_delta_rule`` on the
     configuration-1 inputs (what archbench's ``gdn`` arch runs in prefill, fla/layers/gated_deltanet.py:266-279,
@@ -552,6 +560,7 @@ def bench_fla(args, rank, world, ours_prefill_ms, ours_decode_ms):
     del o, y
     steps = max(1, min(args.steps, 20))
     t_chunk = timed(f_chunk, steps, args.warmup, world) / steps
+
     del x
     c2 = CONFIGS["cfg2"]
     B, H, D = c2.B, c2.H, c2.DK
@@ -567,8 +576,9 @@ def bench_fla(args, rank, world, ours_prefill_ms, ours_decode_ms):
 
     t_dec = timed(f_dec, steps, args.warmup, world) / steps
     return {"impl": f"fla {fla.__version__} (Triton)", "prefill_ms": t_chunk * 1e3, "prefill_tok_s": world * c.B * c.T / t_chunk,
-            "prefill_speedup_ours_vs_fla": t_chunk * 1e3 / ours_prefill_ms, "prefill_fla_vs_ours_rel_l2": rel,
-            "decode_ms": t_dec * 1e3, "decode_tok_s": world * B / t_dec, "decode_speedup_ours_vs_fla": t_dec * 1e3 / ours_decode_ms,
+            "prefill_speedup_ours_vs_fla": t_chunk * 1e3 / ours_prefill_ms if ours_prefill_ms else None, "prefill_fla_vs_ours_rel_l2": rel,
+            "backward": FLA_BACKWARD_NOT_RUN,
+            "decode_ms": t_dec * 1e3, "decode_tok_s": world * B / t_dec, "decode_speedup_ours_vs_fla": t_dec * 1e3 / ours_decode_ms if ours_decode_ms else None,
             "first_call_s": jit_s, "gpu_launches": 0,
             "note": "fla's kernels are the checker here, not ours: not counted in gpu_launches"}
 
@@ -647,7 +657,8 @@ def run_ours(args):
     rank, world, local = dist_init(args.gpus)
     if args.only:  # one leg alone (profiling runs): its own object, not the bench line
         res = {"decode": bench_decode, "backward": bench_backward, "layer": bench_layer,
-               "nstep": bench_nstep, "lm": bench_lm, "long_context": bench_long_context}[args.only](args, rank, world)
+               "nstep": bench_nstep, "lm": bench_lm, "long_context": bench_long_context,
+               "fla": lambda a, r, w: bench_fla(a, r, w, None, None)}[args.only](args, rank, world)
         if rank == 0:
             print(json.dumps({"leg": args.only, **res}), flush=True)
         finish(world)
@@ -727,7 +738,7 @@ def main():
     ap.add_argument("--prefill-impl", choices=["auto", "chunk", "chunk_cluster", "chunk_single", "recurrent", "segmented"], default="auto")
     ap.add_argument("--skip-extra", action="store_true", help="headline prefill only")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the cpu_baseline leg")
-    ap.add_argument("--only", choices=["decode", "backward", "layer", "nstep", "lm", "long_context"], default=None,
+    ap.add_argument("--only", choices=["decode", "backward", "layer", "nstep", "lm", "long_context", "fla"], default=None,
                     help="run one extra leg alone and print its object (for profiling)")
     ap.add_argument("--lm-steps", type=int, default=256,
                     help="greedy decode steps of the configuration-4 leg (256 in the benchmark configuration)")
