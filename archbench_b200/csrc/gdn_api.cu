@@ -51,7 +51,7 @@ int validate(const gdn_prefill_args* a) {
   if (a->B * a->H * a->DV > (1LL << 31)) return GDN_ERR_SHAPE;
   const int es = dtype_size(a->in_dtype);
   if (!es || !dtype_size(a->out_dtype)) return GDN_ERR_DTYPE;
-  if (a->impl < GDN_IMPL_AUTO || a->impl > GDN_IMPL_CHUNK_SINGLE) return GDN_ERR_UNSUPPORTED;
+  if (a->impl < GDN_IMPL_AUTO || a->impl > GDN_IMPL_CHUNK_SPLIT) return GDN_ERR_UNSUPPORTED;
   // The recurrent kernel reads DK/32 consecutive elements per lane as one vector.
   const int vec = (int)(a->DK / 32) * es;
   const int vb = vec >= 16 ? 16 : vec;
@@ -87,6 +87,13 @@ bool segmented_preferred(const gdn_prefill_args* a, int sms) {
   return a->B * a->H * 8 <= (int64_t)sms;
 }
 
+// The split path (prep pass over every chunk, then the state-only chunk kernel) where the cluster
+// kernel does not apply: state rows beyond 128 or explicit write vectors.  Its workspace holds every
+// chunk's products.
+bool split_preferred(const gdn_prefill_args* a) {
+  return gdn_chunk_supported(a) && gdn_chunk_split_supported(a) && chunk_variant(a) != GDN_IMPL_CHUNK_CLUSTER;
+}
+
 int select_impl(const gdn_prefill_args* a) {
   const bool chunk_ok = gdn_chunk_supported(a);
   int P = 0, L = 0;
@@ -94,6 +101,8 @@ int select_impl(const gdn_prefill_args* a) {
   const bool seg_ok = chunk_ok && gdn_segmented_plan(a, plan_sms(), &P, &L, &need);
   const bool seg_auto = seg_ok && segmented_preferred(a, plan_sms());
   const bool ws_ok = seg_ok && a->workspace != nullptr && a->workspace_bytes >= need;
+  const bool split_ok = chunk_ok && gdn_chunk_split_supported(a);
+  const bool split_ws = split_ok && a->workspace != nullptr && a->workspace_bytes >= gdn_chunk_prep_bytes(a);
   switch (a->impl) {
     case GDN_IMPL_CHUNK: return chunk_ok ? chunk_variant(a) : (int)GDN_ERR_UNSUPPORTED;
     case GDN_IMPL_CHUNK_CLUSTER:
@@ -104,8 +113,12 @@ int select_impl(const gdn_prefill_args* a) {
     case GDN_IMPL_SEGMENTED:
       if (!seg_ok) return (int)GDN_ERR_UNSUPPORTED;
       return ws_ok ? (int)GDN_IMPL_SEGMENTED : (int)GDN_ERR_SHAPE;
+    case GDN_IMPL_CHUNK_SPLIT:
+      if (!split_ok) return (int)GDN_ERR_UNSUPPORTED;
+      return split_ws ? (int)GDN_IMPL_CHUNK_SPLIT : (int)GDN_ERR_SHAPE;
     default:
       if (ws_ok && seg_auto) return (int)GDN_IMPL_SEGMENTED;
+      if (split_ws && split_preferred(a)) return (int)GDN_IMPL_CHUNK_SPLIT;
       return chunk_ok ? chunk_variant(a) : (int)GDN_IMPL_RECURRENT;
   }
 }
@@ -136,12 +149,14 @@ int gdn_device_status(int* status, int reset) {
   if (!status) return GDN_ERR_NULL;
   int st = check_device();
   if (st != GDN_OK) return st;
-  int single = 0, pair = 0;
+  int single = 0, pair = 0, prep = 0;
   st = gdn_chunk_read_status(&single, reset);
   if (st != GDN_OK) return st;
   st = gdn_chunk_pair_read_status(&pair, reset);
   if (st != GDN_OK) return st;
-  *status = single != 0 ? single : pair;
+  st = gdn_chunk_prep_read_status(&prep, reset);
+  if (st != GDN_OK) return st;
+  *status = single != 0 ? single : (pair != 0 ? pair : prep);
   return GDN_OK;
 }
 
@@ -162,6 +177,9 @@ int gdn_prefill_workspace_bytes(const gdn_prefill_args* a, size_t* bytes) {
                                            segmented_preferred(a, plan_sms()))) &&
       a->T > 0 && gdn_segmented_plan(a, plan_sms(), &P, &L, &need))
     *bytes = need;
+  else if (a->T > 0 && ((a->impl == GDN_IMPL_CHUNK_SPLIT && gdn_chunk_supported(a) && gdn_chunk_split_supported(a)) ||
+                        (a->impl == GDN_IMPL_AUTO && split_preferred(a))))
+    *bytes = gdn_chunk_prep_bytes(a);
   return GDN_OK;
 }
 
@@ -191,6 +209,11 @@ int gdn_prefill_fwd(const gdn_prefill_args* a, void* stream) {
   if (impl == GDN_IMPL_SEGMENTED)
     return gdn_launch_segmented(a, static_cast<float*>(a->workspace), (size_t)a->workspace_bytes, plan_sms(), s);
   if (impl == GDN_IMPL_CHUNK_CLUSTER) return gdn_launch_chunk_pair(a, 1, 0, nullptr, 0, s);
+  if (impl == GDN_IMPL_CHUNK_SPLIT) {
+    st = gdn_launch_chunk_prep(a, a->workspace, s);
+    if (st != GDN_OK) return st;
+    return gdn_launch_chunk_split(a, a->workspace, 0, 1, 0, nullptr, 0, s);
+  }
   if (impl == GDN_IMPL_CHUNK_SINGLE) return gdn_launch_chunk_sm100(a, s);
   return gdn_launch_recurrent(a, a->s0, a->s_out, s);
 }

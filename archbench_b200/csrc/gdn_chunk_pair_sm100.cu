@@ -35,6 +35,16 @@
 // Every mbarrier wait is bounded and abortable.  An abort raised in either CTA is copied into the
 // other; both drain their own MMAs and tile loads, and the two CTAs leave through one cluster
 // barrier, so neither exits while the other may still write into its shared memory.
+//
+// State-only mode (SPLIT): the state CTA alone, one per (b, h, segment, 128-row state tile), no
+// cluster.  The products of every chunk were written beforehand by the prep kernel
+// (gdn_chunk_prep_sm100.cu, the same arithmetic as the prep CTA here), and the output warps bulk-load
+// chunk c + 2's into the product slot chunk c has released.  This serves what one prep CTA per
+// state tile cannot: state rows beyond 128 (DV = 256: two state CTAs share one chunk's products
+// instead of each preparing them), explicit write vectors (HAS_U: the u tiles ride in a two-entry
+// k/q ring and replace k where the state is written, S += (R diag w)^T U, w free of beta) and the
+// passes of the segmented prefill (mode 1: no y; the transition block, S_0 = I and v = 0, as an extra
+// tile; the segment's end state written to the segment workspace).
 #include "gdn_tiles.cuh"
 
 namespace gdn {
@@ -50,10 +60,12 @@ constexpr uint32_t V_BYTES = 2 * TILE;   // [V0][V1]
 constexpr uint32_t PS_BYTES = 3 * TILE;  // product slot: [A16][T16][TG16]
 constexpr int NB = 3;                    // k/q tile buffers of the state CTA: chunk c uses buffer c % NB
 constexpr int NBV = 2;                   // v tile buffers: chunk c uses buffer c % NBV
+constexpr uint32_t RING_BYTES = NB * KQ_BYTES;  // the k/q ring: three [K0][Q0][K1][Q1] entries, or
+                                                // two [K0][Q0][K1][Q1][U0][U1] with write vectors
 
 // State CTA shared-memory map (bytes from a 1024-aligned base).
-constexpr uint32_t S_KQ = 0;                       // NB x KQ: bf16 as loaded -> fp16 K in place (q stays bf16)
-constexpr uint32_t S_V = S_KQ + NB * KQ_BYTES;     // NBV x V: bf16 -> fp16 in place
+constexpr uint32_t S_KQ = 0;                       // NB x KQ: bf16 as loaded -> fp16 K (and U) in place (q stays bf16)
+constexpr uint32_t S_V = S_KQ + RING_BYTES;        // NBV x V: bf16 -> fp16 in place
 constexpr uint32_t S_WQ = S_V + NBV * V_BYTES;     // [W16 | QT16]: DK rows x 64 tokens each, 16 KB apart
 constexpr uint32_t S_PS = S_WQ + 4 * TILE;         // 2 product slots, written by the prep CTA
 constexpr uint32_t S_YS = S_PS + 2 * PS_BYTES;     // y staging: one bf16 chunk (or half an fp32 one)
@@ -98,16 +110,22 @@ enum SBar {
 enum PBar { PB_KQF = 0, PB_G = 2, PB_PE = 4, PB_DRAIN = 6 };
 
 struct Params {
-  const float* beta;
+  const float* beta;  // NULL with explicit write vectors
   const float* la;
   const float* s0;
   float* s_out;
-  int B, T, H;
+  int B, T, H, DV;
   // Segments: cluster (b, h, seg) runs chunks [seg * seg_len, (seg + 1) * seg_len); segment s >= 1
   // starts from the state at slot (bh, s - 1) of seg_s0 ((DV + 128) x 128 floats per slot).
   int nseg, seg_len;
   const float* seg_s0;
   int ws_stride;
+  // State-only mode: chunk products [B * H][NCt] x PS_BYTES from the prep kernel; state tiles per
+  // (b, h, seg) (nv real ones of 128 rows, plus the transition block in mode 1); mode 1 writes
+  // [N_s; M_s] of segment s to slot (bh, s) of seg_out instead of y.
+  const uint8_t* prod;
+  int NCt, nv, ntiles, mode;
+  float* seg_out;
 };
 
 __device__ int g_status = 0;
@@ -158,20 +176,29 @@ __device__ __noinline__ void convert_pair(uint8_t* t0, uint8_t* t1, int ht) {
   ptx::fence_proxy_async_smem();
 }
 
-template <typename TOut>
+template <bool SPLIT, bool HAS_U, typename TOut>
 __global__ void __launch_bounds__(NT, 1)
     pair_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_y, const Params p) {
+                const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_y,
+                const __grid_constant__ CUtensorMap tm_u, const Params p) {
+  static_assert(SPLIT || !HAS_U, "explicit write vectors take the state-only mode");
+  constexpr int NBK = HAS_U ? 2 : NB;                           // k/q ring entries
+  constexpr uint32_t KQB = HAS_U ? 6 * TILE : KQ_BYTES;         // bytes per ring entry
+  static_assert(NBK * KQB == RING_BYTES, "the ring keeps its footprint");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sb = ptx::smem_u32(sm);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const uint32_t rank = ptx::cluster_ctarank();
-  const int rest = blockIdx.x >> 1;
+  const uint32_t rank = SPLIT ? 0u : ptx::cluster_ctarank();
+  const int tile = SPLIT ? (int)(blockIdx.x % (unsigned)p.ntiles) : 0;
+  const int rest = SPLIT ? (int)(blockIdx.x / (unsigned)p.ntiles) : (int)(blockIdx.x >> 1);
   const int seg = rest % p.nseg, bh = rest / p.nseg;
   const int b = bh / p.H, h = bh % p.H;
   const int cb = seg * p.seg_len;  // first chunk of this cluster's segment
   const int nch = max(0, min((p.T + C - 1) / C - cb, p.seg_len));
+  const bool virt = SPLIT && tile >= p.nv;   // mode 1's transition block: S_0 = I, v = 0
+  const bool want_y = !SPLIT || p.mode == 0;
+  const int dv0 = virt ? 0 : D * tile;       // first state row (and v / y feature) of this tile
 
   uint64_t* sbar = reinterpret_cast<uint64_t*>(sm + S_BARS);
   uint64_t* pbar = reinterpret_cast<uint64_t*>(sm + P_BARS);
@@ -179,11 +206,11 @@ __global__ void __launch_bounds__(NT, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + CTRL + 4);
   volatile int* loads_issued = reinterpret_cast<volatile int*>(sm + CTRL + 8);
   volatile int* v_loads_issued = reinterpret_cast<volatile int*>(sm + CTRL + 12);
-  const uint32_t peer_abort = ptx::mapa_shared(sb + CTRL + 4, rank ^ 1u);
+  const uint32_t peer_abort = SPLIT ? 0u : ptx::mapa_shared(sb + CTRL + 4, rank ^ 1u);
   // Abort here and in the other CTA of the cluster (idempotent).
   auto raise_abort = [&]() {
     *abort_flag = 1;
-    ptx::st_cluster_u32(peer_abort, 1u);
+    if (!SPLIT) ptx::st_cluster_u32(peer_abort, 1u);
   };
 
   const uint32_t tmem_cols = rank == 0 ? 512u : 128u;
@@ -202,6 +229,7 @@ __global__ void __launch_bounds__(NT, 1)
     ptx::prefetch_tensormap(&tm_q);
     ptx::prefetch_tensormap(&tm_k);
     ptx::prefetch_tensormap(&tm_v);
+    if (HAS_U) ptx::prefetch_tensormap(&tm_u);
     *abort_flag = 0;
     *loads_issued = 0;
     *v_loads_issued = 0;
@@ -210,7 +238,7 @@ __global__ void __launch_bounds__(NT, 1)
   }
   ptx::tc_fence_before();
   __syncthreads();
-  ptx::cluster_sync();  // both CTAs' barriers exist before any remote arrive
+  if (!SPLIT) ptx::cluster_sync();  // both CTAs' barriers exist before any remote arrive
   ptx::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t my = tmem + ((uint32_t)((warp & 3) * 32) << 16);  // this warp's TMEM lane quarter
@@ -224,15 +252,23 @@ __global__ void __launch_bounds__(NT, 1)
   constexpr uint32_t ID_N64 = ptx::idesc_f16_f32(128, 64, false, false, false);
   constexpr uint32_t ID_N64_AMN = ptx::idesc_f16_f32(128, 64, true, false, false);
   constexpr uint32_t ID_N128_BMN_NEG = ptx::idesc_f16_f32(128, 128, false, true, true);
+  constexpr uint32_t ID_N64_BMN_NEG = ptx::idesc_f16_f32(128, 64, false, true, true);
   constexpr uint32_t ID_N128_BMN = ptx::idesc_f16_f32(128, 128, false, true, false);
 
-  // la and beta of 64 tokens, two per lane (zero past the end of the sequence).
+  // la and beta of 64 tokens, two per lane (zero past the end of the sequence; beta = 1 with
+  // explicit write vectors, which carry it).
   auto load_gates = [&](int c, float& la0, float& la1, float& be0, float& be1) {
     la0 = la1 = be0 = be1 = 0.f;
     const int t0 = (cb + c) * C;
     const int64_t gi = ((int64_t)b * p.T + t0) * p.H + h;
-    if (t0 + lane < p.T) { la0 = p.la[gi + (int64_t)lane * p.H]; be0 = p.beta[gi + (int64_t)lane * p.H]; }
-    if (t0 + lane + 32 < p.T) { la1 = p.la[gi + (int64_t)(lane + 32) * p.H]; be1 = p.beta[gi + (int64_t)(lane + 32) * p.H]; }
+    if (t0 + lane < p.T) {
+      la0 = p.la[gi + (int64_t)lane * p.H];
+      be0 = HAS_U ? 1.f : p.beta[gi + (int64_t)lane * p.H];
+    }
+    if (t0 + lane + 32 < p.T) {
+      la1 = p.la[gi + (int64_t)(lane + 32) * p.H];
+      be1 = HAS_U ? 1.f : p.beta[gi + (int64_t)(lane + 32) * p.H];
+    }
   };
   auto issue_kq = [&](uint8_t* dst, uint64_t* bar, int c) {  // the caller has set the barrier's byte count
     const int t0 = (cb + c) * C;
@@ -240,6 +276,10 @@ __global__ void __launch_bounds__(NT, 1)
     ptx::tma_load_4d(dst + 1 * TILE, &tm_q, bar, 0, h, t0, b);
     ptx::tma_load_4d(dst + 2 * TILE, &tm_k, bar, 64, h, t0, b);
     ptx::tma_load_4d(dst + 3 * TILE, &tm_q, bar, 64, h, t0, b);
+    if (HAS_U) {
+      ptx::tma_load_4d(dst + 4 * TILE, &tm_u, bar, 0, h, t0, b);
+      ptx::tma_load_4d(dst + 5 * TILE, &tm_u, bar, 64, h, t0, b);
+    }
   };
 
   if (rank == 0) {
@@ -264,23 +304,48 @@ __global__ void __launch_bounds__(NT, 1)
       if (leader && fail) raise_abort();
       return !ptx::named_bar_or(group, 128, leader && fail);
     };
-    // k and q tiles of chunk c into buffer c % NB (one thread of the output warps; every MMA of the
-    // buffer's previous chunk, c - NB, has completed).
+    // k and q (and u) tiles of chunk c into buffer c % NBK (one thread of the output warps; every
+    // MMA of the buffer's previous chunk, c - NBK, has completed).  The state-only kernel has no prep
+    // CTA pulling its tiles into L2 a chunk ahead: it prefetches the next chunk's tiles itself.
     auto issue_loads = [&](int c) {
-      uint64_t* bar = &sbar[SB_KQF + c % NB];
-      ptx::mbar_arrive_expect_tx(bar, KQ_BYTES);
-      issue_kq(sm + S_KQ + (c % NB) * KQ_BYTES, bar, c);
+      uint64_t* bar = &sbar[SB_KQF + c % NBK];
+      ptx::mbar_arrive_expect_tx(bar, KQB);
+      issue_kq(sm + S_KQ + (c % NBK) * KQB, bar, c);
       *loads_issued = c + 1;
+      if (SPLIT && c + 1 < nch) {
+        const int t1 = (cb + c + 1) * C;
+        ptx::tma_prefetch_4d(&tm_k, 0, h, t1, b);
+        ptx::tma_prefetch_4d(&tm_k, 64, h, t1, b);
+        ptx::tma_prefetch_4d(&tm_q, 0, h, t1, b);
+        ptx::tma_prefetch_4d(&tm_q, 64, h, t1, b);
+        if (HAS_U) {
+          ptx::tma_prefetch_4d(&tm_u, 0, h, t1, b);
+          ptx::tma_prefetch_4d(&tm_u, 64, h, t1, b);
+        }
+        if (!virt) {
+          ptx::tma_prefetch_4d(&tm_v, dv0, h, t1, b);
+          ptx::tma_prefetch_4d(&tm_v, dv0 + 64, h, t1, b);
+        }
+      }
     };
     // v tiles of chunk c into buffer c % NBV (convert warps; the buffer's previous chunk's U MMA,
-    // covered by that chunk's R commit, has completed).
+    // covered by that chunk's R commit, has completed).  The transition block has none (v = 0).
     auto issue_v_loads = [&](int c) {
       uint64_t* bar = &sbar[SB_VF + c % NBV];
       uint8_t* dst = sm + S_V + (c % NBV) * V_BYTES;
       ptx::mbar_arrive_expect_tx(bar, V_BYTES);
-      ptx::tma_load_4d(dst, &tm_v, bar, 0, h, (cb + c) * C, b);
-      ptx::tma_load_4d(dst + TILE, &tm_v, bar, 64, h, (cb + c) * C, b);
+      ptx::tma_load_4d(dst, &tm_v, bar, dv0, h, (cb + c) * C, b);
+      ptx::tma_load_4d(dst + TILE, &tm_v, bar, dv0 + 64, h, (cb + c) * C, b);
       *v_loads_issued = c + 1;
+    };
+    // State-only mode: the products of chunk c into slot c & 1 (the slot's previous chunk, c - 2,
+    // has completed every MMA), counted per slot for the abort drain.
+    auto issue_products = [&](int c) {
+      const int s = c & 1;
+      ptx::mbar_arrive_expect_tx(&sbar[SB_PF + s], PS_BYTES);
+      ptx::bulk_load(sm + S_PS + s * PS_BYTES, p.prod + ((int64_t)bh * p.NCt + cb + c) * PS_BYTES, PS_BYTES,
+                     &sbar[SB_PF + s]);
+      reinterpret_cast<volatile int*>(sm + CTRL + 24)[s] = (c >> 1) + 1;
     };
     float* gslots = reinterpret_cast<float*>(sm + S_GS);
 
@@ -289,12 +354,15 @@ __global__ void __launch_bounds__(NT, 1)
       const bool leader = tid == 0;
       bool issued = false;
       {
-        // Initial state: the caller's S_0 (first segment) or the combined state of the segments before.
+        // Initial state: the caller's S_0 (first segment) or the combined state of the segments
+        // before; in mode 1, zero (a real tile) or the identity (the transition block).
         const float* src = nullptr;
-        if (seg == 0) {
-          if (p.s0) src = p.s0 + ((int64_t)bh * D + row) * D;
-        } else {
-          src = p.seg_s0 + ((int64_t)(bh * p.ws_stride + seg - 1) * (2 * D) + row) * D;
+        if (want_y) {
+          if (seg == 0) {
+            if (p.s0) src = p.s0 + ((int64_t)bh * p.DV + dv0 + row) * D;
+          } else {
+            src = p.seg_s0 + ((int64_t)(bh * p.ws_stride + seg - 1) * (p.DV + D) + dv0 + row) * D;
+          }
         }
 #pragma unroll 1
         for (int c4 = 0; c4 < 4; ++c4) {
@@ -303,6 +371,10 @@ __global__ void __launch_bounds__(NT, 1)
           for (int i = 0; i < 32; i += 4) {
             const float4 t4 = src ? *reinterpret_cast<const float4*>(src + c4 * 32 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
             v[i] = t4.x; v[i + 1] = t4.y; v[i + 2] = t4.z; v[i + 3] = t4.w;
+          }
+          if (virt) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = (c4 * 32 + i == row) ? 1.f : 0.f;
           }
           ptx::tmem_st32(my + COL_S + c4 * 32, v);
         }
@@ -315,9 +387,9 @@ __global__ void __launch_bounds__(NT, 1)
       }
 #pragma unroll 1
       for (int c = 0; c < nch; ++c) {
-        const int s = c & 1, tb = c % NB;  // product slot; k/q tile buffer
-        const uint32_t ph = (uint32_t)(c >> 1) & 1u, tph = (uint32_t)(c / NB) & 1u;
-        const uint32_t kq_o = S_KQ + tb * KQ_BYTES, v_o = S_V + (c % NBV) * V_BYTES, ps_o = S_PS + s * PS_BYTES;
+        const int s = c & 1, tb = c % NBK;  // product slot; k/q tile buffer
+        const uint32_t ph = (uint32_t)(c >> 1) & 1u, tph = (uint32_t)(c / NBK) & 1u;
+        const uint32_t kq_o = S_KQ + tb * KQB, v_o = S_V + (c % NBV) * V_BYTES, ps_o = S_PS + s * PS_BYTES;
         const float* gs = gslots + tb * GSLOT;
         {
           // S(c-1) done; fp16 K and V and the gates of chunk c; A, T, T Gamma of chunk c from the
@@ -333,7 +405,7 @@ __global__ void __launch_bounds__(NT, 1)
         if (leader) *reinterpret_cast<volatile int*>(sm + CTRL + 16 + 4 * s) = (c >> 1) + 1;
         const float gC = gs[2 * C];
         ptx::tc_fence_after();
-        if (warp == 0) {  // U^T = V^T T^T while the state is converted (issued from the converged warp)
+        if (warp == 0 && !virt) {  // U^T = V^T T^T while the state is converted (issued from the converged warp)
 #pragma unroll 1
           for (int k = 0; k < 4; ++k)
             ptx::mma_f16_ss_elect(tmem + COL_U, at(D_MN8K, v_o + k * 2048), at(D_K, ps_o + TILE + k * 32), ID_N64_AMN,
@@ -371,10 +443,14 @@ __global__ void __launch_bounds__(NT, 1)
             fail = __shfl_sync(0xffffffffu, fail, 0);
             ptx::tc_fence_after();
             if (!fail) {
+              // Without y (mode 1) only the R half, N = 64; the transition block has U = 0, so its
+              // first K step overwrites the accumulator.
+              const uint32_t idf = want_y ? ID_N128_BMN_NEG : ID_N64_BMN_NEG;
 #pragma unroll 1
               for (int k = 0; k < 8; ++k)
-                ptx::mma_f16_ts_elect(tmem + COL_U, tmem + COL_S16 + 8 * k, at(D_MN16K, S_WQ + k * 2048), ID_N128_BMN_NEG,
-                                      1);
+                ptx::mma_f16_ts_elect(tmem + COL_U, tmem + COL_S16 + 8 * k, at(D_MN16K, S_WQ + k * 2048), idf,
+                                      (k > 0 || !virt) ? 1u : 0u);
+              issued = true;
               ptx::mma_commit_elect(&sbar[SB_R]);
               if (leader) lwait(fail, SB_R, (uint32_t)c & 1u);
             }
@@ -403,15 +479,19 @@ __global__ void __launch_bounds__(NT, 1)
         }
         ptx::tc_fence_before();
         ptx::named_bar(1, 128);
-        if (warp == 0) {  // S += (R diag w)^T K (committed alone), then Y += R^T A^T
+        if (warp == 0) {  // S += (R diag w)^T K (or U; committed alone), then Y += R^T A^T
           ptx::tc_fence_after();
+          // The write side of the state: K tiles 16 KB apart, or the U tiles 8 KB apart.
+          const uint64_t bw = HAS_U ? at(D_MN8K, kq_o + 4 * TILE) : at(D_MN16K, kq_o);
 #pragma unroll 1
           for (int k = 0; k < 4; ++k)
-            ptx::mma_f16_ts_elect(tmem + COL_S, tmem + COL_RW16 + 8 * k, at(D_MN16K, kq_o + k * 2048), ID_N128_BMN, 1);
+            ptx::mma_f16_ts_elect(tmem + COL_S, tmem + COL_RW16 + 8 * k, bw + (uint64_t)(k * 2048 >> 4), ID_N128_BMN, 1);
           ptx::mma_commit_elect(&sbar[SB_S]);
+          if (want_y) {
 #pragma unroll 1
-          for (int k = 0; k < 4; ++k)
-            ptx::mma_f16_ts_elect(tmem + COL_Y, tmem + COL_R16 + 8 * k, at(D_K, ps_o + k * 32), ID_N64, 1);
+            for (int k = 0; k < 4; ++k)
+              ptx::mma_f16_ts_elect(tmem + COL_Y, tmem + COL_R16 + 8 * k, at(D_K, ps_o + k * 32), ID_N64, 1);
+          }
           ptx::mma_commit_elect(&sbar[SB_YF]);
           issued = true;
         }
@@ -419,8 +499,12 @@ __global__ void __launch_bounds__(NT, 1)
       // The last Y MMA may still run after this wait: `issued` stays set for the abort drain.
       if (!*abort_flag && nch > 0 && gwait(SB_S, (uint32_t)(nch - 1) & 1u, leader, 1, false)) {
         ptx::tc_fence_after();
-        if (seg == p.nseg - 1 && p.s_out != nullptr) {
-          float* dst = p.s_out + ((int64_t)bh * D + row) * D;
+        float* dst = nullptr;
+        if (!want_y)  // mode 1: N_s (a real tile) or M_s (the transition block) of this segment
+          dst = p.seg_out + ((int64_t)(bh * p.ws_stride + seg) * (p.DV + D) + (virt ? p.DV : dv0) + row) * D;
+        else if (seg == p.nseg - 1 && p.s_out != nullptr)
+          dst = p.s_out + ((int64_t)bh * p.DV + dv0 + row) * D;
+        if (dst != nullptr) {
 #pragma unroll 1
           for (int c4 = 0; c4 < 4; ++c4) {
             float v[32];
@@ -444,13 +528,13 @@ __global__ void __launch_bounds__(NT, 1)
       bool issued = false;
       float la0 = 0.f, la1 = 0.f, be0 = 0.f, be1 = 0.f;
       if (ww == 1 && nch > 0) load_gates(0, la0, la1, be0, be1);
-      if (leader)
+      if (leader && !virt)
         for (int c = 0; c < NBV && c < nch; ++c) issue_v_loads(c);
 #pragma unroll 1
       for (int c = 0; c < nch; ++c) {
-        const int s = c & 1, tb = c % NB;  // product slot; k/q tile buffer
-        const uint32_t ph = (uint32_t)(c >> 1) & 1u, tph = (uint32_t)(c / NB) & 1u;
-        const uint32_t kq_o = S_KQ + tb * KQ_BYTES, ps_o = S_PS + s * PS_BYTES;
+        const int s = c & 1, tb = c % NBK;  // product slot; k/q tile buffer
+        const uint32_t ph = (uint32_t)(c >> 1) & 1u, tph = (uint32_t)(c / NBK) & 1u;
+        const uint32_t kq_o = S_KQ + tb * KQB, ps_o = S_PS + s * PS_BYTES;
         float* gs = gslots + tb * GSLOT;
         float g0 = 0.f, g1 = 0.f, gC = 0.f;
         if (ww == 1) cumsum_gates(la0, la1, g0, g1, gC);
@@ -468,6 +552,7 @@ __global__ void __launch_bounds__(NT, 1)
           if (c + 1 < nch) load_gates(c + 1, la0, la1, be0, be1);
         }
         convert_pair(sm + kq_o, sm + kq_o + 2 * TILE, wt);  // K -> fp16 (the output warps take V)
+        if (HAS_U) convert_pair(sm + kq_o + 4 * TILE, sm + kq_o + 5 * TILE, wt);  // and U
         ptx::named_bar(2, 128);                              // gate slot and fp16 K written
         if (leader) ptx::mbar_arrive(&sbar[SB_KQR + tb]);
         // W^T = K^T (T Gamma)^T once T Gamma has arrived (the W columns were read out by this group
@@ -488,7 +573,7 @@ __global__ void __launch_bounds__(NT, 1)
           if (leader) {
             if (c > 0) {
               lwait(fail, SB_R, (uint32_t)(c - 1) & 1u);
-              if (!fail && c + 1 < nch) issue_v_loads(c + 1);
+              if (!fail && c + 1 < nch && !virt) issue_v_loads(c + 1);
             }
             lwait(fail, SB_WM, (uint32_t)c & 1u);
           }
@@ -524,24 +609,31 @@ __global__ void __launch_bounds__(NT, 1)
       // MMA.  Iteration -1 only prepares chunk 0.
       const bool leader = tid == 256;
       const int ow = (tid - 256) >> 5;
-      const uint32_t peer_pe0 = ptx::mapa_shared(ptx::smem_u32(&pbar[PB_PE]), 1u);
+      const uint32_t peer_pe0 = SPLIT ? 0u : ptx::mapa_shared(ptx::smem_u32(&pbar[PB_PE]), 1u);
       constexpr int ROWS = (int)(YS_BYTES / (D * sizeof(TOut)));  // tokens per staging piece
       TOut* stage = reinterpret_cast<TOut*>(sm + S_YS);
+      if (SPLIT && leader)
+        for (int c = 0; c < 2 && c < nch; ++c) issue_products(c);
 #pragma unroll 1
       for (int c = -1; c < nch; ++c) {
         const int cn = c + 1;
-        if (leader) {
+        if (leader && !SPLIT) {
           // Every MMA of chunk c-1 has completed (its Y was read out last iteration): its tile
-          // buffer takes the loads of chunk c + 2.  Iteration -1 issues those of chunks 0 and 1.
-          // One call site.
-          for (int l = c < 0 ? 0 : c + 2; l <= c + 2 && l < nch; ++l) issue_loads(l);
+          // buffer takes the loads of chunk c + NBK - 1.  Iteration -1 issues those of chunks
+          // 0 .. NBK - 2.  One call site.
+          for (int l = c < 0 ? 0 : c + NBK - 1; l <= c + NBK - 1 && l < nch; ++l) issue_loads(l);
         }
-        if (cn < nch) {  // V of chunk c + 1 -> fp16 (the convert warps take K and the gates)
+        if (leader && SPLIT && c < 0) {  // state-only: every buffer at once, then one per chunk done
+          for (int l = 0; l < NBK && l < nch; ++l) issue_loads(l);
+        }
+        if (cn < nch && !virt) {  // V of chunk c + 1 -> fp16 (the convert warps take K and the gates)
           if (!gwait(SB_VF + cn % NBV, (uint32_t)(cn / NBV) & 1u, leader, 3, false)) break;
           const uint32_t v_o = S_V + (cn % NBV) * V_BYTES;
           convert_pair(sm + v_o, sm + v_o + TILE, tid - 256);
           ptx::named_bar(3, 128);
-          if (leader) ptx::mbar_arrive(&sbar[SB_KQR + cn % NB]);
+          if (leader) ptx::mbar_arrive(&sbar[SB_KQR + cn % NBK]);
+        } else if (cn < nch && leader) {  // the transition block has no v tile
+          ptx::mbar_arrive(&sbar[SB_KQR + cn % NBK]);
         }
         if (cn < nch) {
           // QT16 = (-Gamma Q)^T of chunk c + 1, DK rows x 64 tokens (the Y half of the fused MMA's B
@@ -552,17 +644,17 @@ __global__ void __launch_bounds__(NT, 1)
           bool fail = false;  // the fused MMA of chunk c; q tiles and gates of chunk c + 1
           if (leader) {
             if (c >= 0) lwait(fail, SB_R, (uint32_t)c & 1u);
-            lwait(fail, SB_KQR + cn % NB, (uint32_t)(cn / NB) & 1u);
+            lwait(fail, SB_KQR + cn % NBK, (uint32_t)(cn / NBK) & 1u);
           }
           if (!agree(fail, leader, 3)) break;
-          const float* gs = gslots + (cn % NB) * GSLOT;
+          const float* gs = gslots + (cn % NBK) * GSLOT;
           float ng[8];  // -gamma of the 8 tokens this lane scales: 8 j + lane / 4
 #pragma unroll
           for (int j = 0; j < 8; ++j) ng[j] = -gs[8 * j + (lane >> 2)];
-          const uint32_t qs = sb + S_KQ + (cn % NB) * KQ_BYTES + TILE, qd = sb + S_WQ + 2 * TILE;
+          const uint32_t qs = sb + S_KQ + (cn % NBK) * KQB + TILE, qd = sb + S_WQ + 2 * TILE;
           const int m = lane >> 3, r8 = lane & 7;
 #pragma unroll 1
-          for (int fq = 0; fq < 4; ++fq) {
+          for (int fq = 0; fq < (want_y ? 4 : 0); ++fq) {  // mode 1 has no y: the fused MMA leaves out QT16
             const int fb = 4 * ow + fq;  // feature block
             const uint32_t src = qs + (uint32_t)(fb >> 3) * 2 * TILE;
             uint32_t x[2][4];
@@ -585,13 +677,23 @@ __global__ void __launch_bounds__(NT, 1)
         }
         if (c >= 0) {
           if (!gwait(SB_YF, (uint32_t)c & 1u, leader, 3, false)) break;  // every MMA of chunk c
-          // Chunk c's product slot goes back to the prep CTA at once (its copy of chunk c + 2 waits).
-          if (leader) ptx::mbar_arrive_remote_relaxed(peer_pe0 + 8u * (uint32_t)(c & 1));
+          // Chunk c's product slot goes back to the prep CTA at once (its copy of chunk c + 2 waits),
+          // or, state-only, takes chunk c + 2's products from the workspace.
+          if (leader) {
+            if (SPLIT) {
+              // Without a prep CTA to pull the tiles into L2 ahead, the loads go out as early as
+              // possible: chunk c's buffer is free now, before its y is read out.
+              if (c + NBK < nch) issue_loads(c + NBK);
+              if (c + 2 < nch) issue_products(c + 2);
+            } else {
+              ptx::mbar_arrive_remote_relaxed(peer_pe0 + 8u * (uint32_t)(c & 1));
+            }
+          }
           ptx::tc_fence_after();
           // y of chunk c straight from tensor memory, 16 tokens at a time (a short loop body), through
           // the staging tile: one TMA store per piece.
 #pragma unroll 1
-          for (int piece = 0; piece < C / ROWS; ++piece) {
+          for (int piece = 0; piece < (want_y ? C / ROWS : 0); ++piece) {
             // The staging tile's previous store (the last chunk's, or the previous piece) must have
             // been read out first.
             if (leader) ptx::bulk_wait_read0();
@@ -607,17 +709,19 @@ __global__ void __launch_bounds__(NT, 1)
             ptx::fence_proxy_async_smem();
             ptx::named_bar(3, 128);
             if (leader) {
-              ptx::tma_store_4d(&tm_y, stage, 0, h, (cb + c) * C + piece * ROWS, b);
+              ptx::tma_store_4d(&tm_y, stage, dv0, h, (cb + c) * C + piece * ROWS, b);
               ptx::bulk_commit();
             }
           }
           // Y is accumulated afresh by the fused MMA of chunk c + 1: zero it, then hand it back.
-          float z[32];
+          if (want_y) {
+            float z[32];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) z[j] = 0.f;
-          ptx::tmem_st32(my + COL_Y, z);
-          ptx::tmem_st32(my + COL_Y + 32, z);
-          ptx::tc_wait_st();
+            for (int j = 0; j < 32; ++j) z[j] = 0.f;
+            ptx::tmem_st32(my + COL_Y, z);
+            ptx::tmem_st32(my + COL_Y + 32, z);
+            ptx::tc_wait_st();
+          }
           ptx::tc_fence_before();
           __syncwarp();
           if (lane == 0) ptx::mbar_arrive(&sbar[SB_YE]);
@@ -812,13 +916,16 @@ __global__ void __launch_bounds__(NT, 1)
   __syncthreads();
   if (rank == 0 && tid == 0 && *abort_flag) {  // tile loads still in flight: the last one per buffer
     const int n = *loads_issued, nv = *v_loads_issued;
-    for (int c = n - NB < 0 ? 0 : n - NB; c < n; ++c)
-      ptx::mbar_wait_bounded(&sbar[SB_KQF + c % NB], (uint32_t)(c / NB) & 1u, WAIT_LIMIT);
+    for (int c = n - NBK < 0 ? 0 : n - NBK; c < n; ++c)
+      ptx::mbar_wait_bounded(&sbar[SB_KQF + c % NBK], (uint32_t)(c / NBK) & 1u, WAIT_LIMIT);
     for (int c = nv - NBV < 0 ? 0 : nv - NBV; c < nv; ++c)
       ptx::mbar_wait_bounded(&sbar[SB_VF + c % NBV], (uint32_t)(c / NBV) & 1u, WAIT_LIMIT);
   }
   __syncwarp();
-  ptx::cluster_sync();  // every remote store, arrive and copy of both CTAs has been issued
+  if (SPLIT)
+    __syncthreads();
+  else
+    ptx::cluster_sync();  // every remote store, arrive and copy of both CTAs has been issued
   if (rank == 0 && tid == 0 && *abort_flag) {  // product copies still in flight into this CTA
     for (int sl = 0; sl < 2; ++sl) {
       const int issued_n = *reinterpret_cast<volatile int*>(sm + CTRL + 24 + 4 * sl);
@@ -827,30 +934,44 @@ __global__ void __launch_bounds__(NT, 1)
     }
   }
   __syncwarp();
-  ptx::cluster_sync();  // neither CTA leaves while the other may still read from or write into it
+  if (SPLIT)
+    __syncthreads();
+  else
+    ptx::cluster_sync();  // neither CTA leaves while the other may still read from or write into it
   ptx::tc_fence_after();
   if (tid == 0 && *abort_flag) atomicExch(&g_status, GDN_ERR_TIMEOUT);
   if (warp == 0) ptx::tmem_dealloc(tmem, tmem_cols);
 }
 
-template <typename TOut>
-int launch(const gdn_prefill_args* a, int nseg, int seg_len, const float* seg_s0, int ws_stride, cudaStream_t stream) {
-  CUtensorMap mq, mk, mv, my;
+// Parameters shared by both modes; the caller fills the segment and state-only fields.
+inline Params base_params(const gdn_prefill_args* a) {
+  Params p = {};
+  p.beta = a->beta; p.la = a->la; p.s0 = a->s0; p.s_out = a->s_out;
+  p.B = (int)a->B; p.T = (int)a->T; p.H = (int)a->H; p.DV = (int)a->DV;
+  p.NCt = (int)((a->T + C - 1) / C);
+  p.nseg = 1;
+  p.seg_len = p.NCt;
+  p.nv = (int)(a->DV / D);
+  p.ntiles = p.nv;
+  return p;
+}
+
+// SPLIT: one CTA per (b, h, segment, state tile), no cluster; otherwise two-CTA clusters.
+template <bool SPLIT, bool HAS_U, typename TOut>
+int launch(const gdn_prefill_args* a, const Params& p, cudaStream_t stream) {
+  CUtensorMap mq, mk, mv, my, mu;
   if (!make_map(&mq, a->q, a->DK, a, a->sq) || !make_map(&mk, a->k, a->DK, a, a->sk) ||
       !make_map(&mv, a->v, a->DV, a, a->sv) || !make_store_map<TOut>(&my, a->y, a->DV, a, a->sy, YS_BYTES))
     return GDN_ERR_LAUNCH;
-  auto kern = pair_kernel<TOut>;
+  if (HAS_U) {
+    if (!make_map(&mu, a->u, a->DK, a, a->su)) return GDN_ERR_LAUNCH;
+  } else {
+    mu = mk;
+  }
+  auto kern = pair_kernel<SPLIT, HAS_U, TOut>;
   static std::atomic<unsigned long long> opted{0};  // per device (see opt_in_smem)
   if (!opt_in_smem(opted, {{(const void*)kern, (int)(DYN)}})) return GDN_ERR_LAUNCH;
-  const int nch = (int)((a->T + C - 1) / C);
-  Params p;
-  p.beta = a->beta; p.la = a->la; p.s0 = a->s0; p.s_out = a->s_out;
-  p.B = (int)a->B; p.T = (int)a->T; p.H = (int)a->H;
-  p.nseg = nseg;
-  p.seg_len = seg_len > 0 ? seg_len : nch;
-  p.seg_s0 = seg_s0;
-  p.ws_stride = ws_stride;
-  const int64_t grid = 2 * a->B * a->H * (int64_t)nseg;
+  const int64_t grid = (SPLIT ? (int64_t)p.ntiles : 2) * a->B * a->H * (int64_t)p.nseg;
   if (grid <= 0 || grid > 0x7fffffff) return GDN_ERR_SHAPE;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid, 1, 1);
@@ -863,9 +984,15 @@ int launch(const gdn_prefill_args* a, int nseg, int seg_len, const float* seg_s0
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, kern, mq, mk, mv, my, p) != cudaSuccess) return GDN_ERR_LAUNCH;
+  cfg.numAttrs = SPLIT ? 0 : 1;
+  if (cudaLaunchKernelEx(&cfg, kern, mq, mk, mv, my, mu, p) != cudaSuccess) return GDN_ERR_LAUNCH;
   return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+}
+
+template <bool SPLIT, bool HAS_U>
+int launch_dt(const gdn_prefill_args* a, const Params& p, cudaStream_t stream) {
+  return a->out_dtype == GDN_DTYPE_BF16 ? launch<SPLIT, HAS_U, __nv_bfloat16>(a, p, stream)
+                                        : launch<SPLIT, HAS_U, float>(a, p, stream);
 }
 
 // Clusters of this kernel that fit on the device at once (0 if the query fails).
@@ -874,7 +1001,7 @@ int max_active_clusters() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
   if (cached[dev] > 0) return cached[dev];
-  auto kern = pair_kernel<__nv_bfloat16>;
+  auto kern = pair_kernel<false, false, __nv_bfloat16>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, DYN) != cudaSuccess) return 0;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2, 1, 1);
@@ -908,8 +1035,35 @@ int gdn_chunk_pair_max_clusters() { return gdn::pair::max_active_clusters(); }
 
 int gdn_launch_chunk_pair(const gdn_prefill_args* a, int nseg, int seg_len, const float* seg_s0, int ws_stride,
                           cudaStream_t stream) {
-  return a->out_dtype == GDN_DTYPE_BF16 ? gdn::pair::launch<__nv_bfloat16>(a, nseg, seg_len, seg_s0, ws_stride, stream)
-                                        : gdn::pair::launch<float>(a, nseg, seg_len, seg_s0, ws_stride, stream);
+  gdn::pair::Params p = gdn::pair::base_params(a);
+  p.nseg = nseg;
+  if (seg_len > 0) p.seg_len = seg_len;
+  p.seg_s0 = seg_s0;
+  p.ws_stride = ws_stride;
+  return gdn::pair::launch_dt<false, false>(a, p, stream);
+}
+
+// The state-only chunk kernel: any DV multiple of 128, u = beta k or explicit write vectors, y
+// stored by TMA.
+bool gdn_chunk_split_supported(const gdn_prefill_args* a) { return gdn_chunk_supported(a) && gdn_y_tma_ok(a); }
+
+int gdn_launch_chunk_split(const gdn_prefill_args* a, const void* prod, int mode, int nseg, int seg_len, float* ws,
+                           int ws_stride, cudaStream_t stream) {
+  if (prod == nullptr || (uintptr_t)prod % 16) return GDN_ERR_ALIGN;
+  gdn::pair::Params p = gdn::pair::base_params(a);
+  p.prod = static_cast<const uint8_t*>(prod);
+  p.mode = mode;
+  p.nseg = nseg;
+  if (seg_len > 0) p.seg_len = seg_len;
+  p.ws_stride = ws_stride;
+  if (mode == 1) {
+    p.seg_out = ws;
+    p.ntiles = p.nv + 1;
+  } else {
+    p.seg_s0 = ws;
+  }
+  return a->u != nullptr ? gdn::pair::launch_dt<true, true>(a, p, stream)
+                         : gdn::pair::launch_dt<true, false>(a, p, stream);
 }
 
 int gdn_chunk_pair_read_status(int* out, int reset) {

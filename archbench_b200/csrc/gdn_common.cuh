@@ -100,3 +100,12 @@ int gdn_chunk_pair_max_clusters();
 int gdn_launch_chunk_pair(const gdn_prefill_args* a, int nseg, int seg_len, const float* seg_s0, int ws_stride,
                           cudaStream_t stream);
 int gdn_chunk_pair_read_status(int* out, int reset);
+// Split chunk path: the prep kernel writes every chunk's products (A, T, T Gamma; 24 KB per chunk) to
+// `prod`, then the state-only chunk kernel streams them back.  mode 0 writes y (segment s >= 1 starts
+// from slot s - 1 of `ws`); mode 1 writes [N_s; M_s] of each segment to slot s of `ws`.
+size_t gdn_chunk_prep_bytes(const gdn_prefill_args* a);
+int gdn_launch_chunk_prep(const gdn_prefill_args* a, void* prod, cudaStream_t stream);
+int gdn_chunk_prep_read_status(int* out, int reset);
+bool gdn_chunk_split_supported(const gdn_prefill_args* a);
+int gdn_launch_chunk_split(const gdn_prefill_args* a, const void* prod, int mode, int nseg, int seg_len, float* ws,
+                           int ws_stride, cudaStream_t stream);

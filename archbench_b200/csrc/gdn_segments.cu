@@ -3,13 +3,18 @@
 // A sequence with too few (b, h) units to fill the GPU is cut into P segments of L chunks; the
 // per-chunk transition S -> gamma_C S + (U - W S^T)^T diag(w) K is affine in S, so a segment
 // maps its entry state to S_out = S_in M_s + N_s.  Three passes, all on the stream:
-//   A. gdn_chunk_ws_sm100.cu in state mode over segments 0..P-2: N_s from S = 0 with the real
-//      v, M_s from S = I with v = 0 (one extra 128-row tile per (b, h, segment)); no y.
+//   A. a chunk kernel in state mode over segments 0..P-2: N_s from S = 0 with the real v, M_s from
+//      S = I with v = 0 (one extra 128-row tile per (b, h, segment)); no y.
 //   B. combine_kernel: S_{s+1} = S_s M_s + N_s, s = 0..P-2, fp32 on CUDA cores, the state rows
 //      split over CTAs (rows evolve independently), M_s double-buffered in shared memory, result
 //      written over N_s.
 //   C. the chunk kernel in output mode over all P segments, segment s starting from S_s.
-// Workspace (caller-allocated): B*H*(P-1) slots of (DV + 128) x 128 fp32.
+// The chunk kernel is the state-only one of gdn_chunk_pair_sm100.cu after one prep pass over every
+// chunk (gdn_chunk_prep_sm100.cu), whose products both passes read; where y cannot be stored by TMA,
+// and for the entry point without allocation, the single-CTA kernel of gdn_chunk_ws_sm100.cu, which
+// prepares the products in every tile itself.
+// Workspace (caller-allocated): B*H*(P-1) slots of (DV + 128) x 128 fp32, then (split kernels) the
+// chunk products, 24 KB per (b, h, chunk).
 // The reference computes the same recurrence sequentially (archbench/layers/nsgdn.py:408-417,
 // fla's chunk_gated_delta_rule_fwd_h walks chunks in order); this split is this build's own.
 #include <mutex>
@@ -120,18 +125,19 @@ static bool plan(const gdn_prefill_args* a, int sms, size_t max_bytes, int* nseg
   return true;
 }
 
+// The split chunk kernels (prep pass, then the state-only kernel for both passes) where they apply:
+// the workspace then holds the segment slots, then every chunk's products.
+static size_t slots_rounded(size_t slot_bytes) { return (slot_bytes + 255) / 256 * 256; }
+
 bool gdn_segmented_plan(const gdn_prefill_args* a, int sms, int* nseg, int* seg_len, size_t* bytes) {
-  return plan(a, sms, 0, nseg, seg_len, bytes);
+  if (!plan(a, sms, 0, nseg, seg_len, bytes)) return false;
+  if (gdn_chunk_split_supported(a)) *bytes = slots_rounded(*bytes) + gdn_chunk_prep_bytes(a);
+  return true;
 }
 
 int gdn_segmented_sms() { return gdn::seg::sm_count(); }
 
-static int launch_plan(const gdn_prefill_args* a, float* ws, size_t ws_bytes, int P, int L, size_t need,
-                       cudaStream_t stream) {
-  if (ws == nullptr || ws_bytes < need) return GDN_ERR_SHAPE;
-  if ((uintptr_t)ws % 16) return GDN_ERR_ALIGN;
-  int st = gdn_launch_chunk_ws_segments(a, 1, P - 1, L, ws, P - 1, stream);
-  if (st != GDN_OK) return st;
+static int launch_combine(const gdn_prefill_args* a, float* ws, int P, cudaStream_t stream) {
   const int rblocks = (int)(a->DV / gdn::seg::RB);
   const int64_t grid = a->B * a->H * rblocks;
   static std::atomic<unsigned long long> opted{0};  // per device (see gdn::opt_in_smem)
@@ -139,14 +145,43 @@ static int launch_plan(const gdn_prefill_args* a, float* ws, size_t ws_bytes, in
     return GDN_ERR_LAUNCH;
   gdn::seg::combine_kernel<<<(unsigned)grid, gdn::seg::D, gdn::seg::COMB_SMEM, stream>>>(ws, a->s0, (int)a->DV, P - 1,
                                                                                           rblocks);
-  if (cudaGetLastError() != cudaSuccess) return GDN_ERR_LAUNCH;
+  return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+}
+
+// The three passes on the single-CTA kernel (each state tile prepares its own chunk products).
+static int launch_plan(const gdn_prefill_args* a, float* ws, size_t ws_bytes, int P, int L, size_t need,
+                       cudaStream_t stream) {
+  if (ws == nullptr || ws_bytes < need) return GDN_ERR_SHAPE;
+  if ((uintptr_t)ws % 16) return GDN_ERR_ALIGN;
+  int st = gdn_launch_chunk_ws_segments(a, 1, P - 1, L, ws, P - 1, stream);
+  if (st != GDN_OK) return st;
+  st = launch_combine(a, ws, P, stream);
+  if (st != GDN_OK) return st;
   return gdn_launch_chunk_ws_segments(a, 0, P, L, ws, P - 1, stream);
+}
+
+// The same passes on the split kernels: every chunk's products once, then the state-only kernel
+// in state mode (segments 0..P-2), the combine, and the state-only kernel in output mode.
+static int launch_plan_split(const gdn_prefill_args* a, float* ws, size_t ws_bytes, int P, int L, size_t slot_bytes,
+                             cudaStream_t stream) {
+  const size_t off = slots_rounded(slot_bytes);
+  if (ws == nullptr || ws_bytes < off + gdn_chunk_prep_bytes(a)) return GDN_ERR_SHAPE;
+  if ((uintptr_t)ws % 16) return GDN_ERR_ALIGN;
+  void* prod = reinterpret_cast<uint8_t*>(ws) + off;
+  int st = gdn_launch_chunk_prep(a, prod, stream);
+  if (st != GDN_OK) return st;
+  st = gdn_launch_chunk_split(a, prod, 1, P - 1, L, ws, P - 1, stream);
+  if (st != GDN_OK) return st;
+  st = launch_combine(a, ws, P, stream);
+  if (st != GDN_OK) return st;
+  return gdn_launch_chunk_split(a, prod, 0, P, L, ws, P - 1, stream);
 }
 
 int gdn_launch_segmented(const gdn_prefill_args* a, float* ws, size_t ws_bytes, int sms, cudaStream_t stream) {
   int P = 0, L = 0;
   size_t need = 0;
   if (!plan(a, sms, 0, &P, &L, &need)) return GDN_ERR_UNSUPPORTED;
+  if (gdn_chunk_split_supported(a)) return launch_plan_split(a, ws, ws_bytes, P, L, need, stream);
   return launch_plan(a, ws, ws_bytes, P, L, need, stream);
 }
 

@@ -424,5 +424,20 @@ __device__ __forceinline__ void bulk_copy_to_cluster(uint32_t dst_cluster, const
       "r"(smem_u32(src)), "r"(bytes), "r"(mbar_cluster)
       : "memory");
 }
+// Bulk copy (no tensor map, no multicast) global -> this CTA's shared memory, completing `bytes`
+// on `bar`.  Addresses 16-byte aligned, size a multiple of 16.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+// Bulk copy shared -> global, bulk-group completion (bulk_commit / bulk_wait0).  Addresses 16-byte
+// aligned, size a multiple of 16.
+__device__ __forceinline__ void bulk_store(void* dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(reinterpret_cast<uint64_t>(dst)),
+               "r"(smem_u32(src)), "r"(bytes)
+               : "memory");
+}
 }  // namespace ptx
 }  // namespace gdn

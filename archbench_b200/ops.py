@@ -28,8 +28,10 @@ _PKG = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_PKG, "libgdn_b200.so")
 
 GDN_DTYPE_F32, GDN_DTYPE_BF16 = 0, 1
-IMPLS = {"auto": 0, "chunk": 1, "recurrent": 2, "segmented": 3, "chunk_cluster": 4, "chunk_single": 5}
-IMPL_NAMES = {1: "chunk", 2: "recurrent", 3: "segmented", 4: "chunk_cluster", 5: "chunk_single"}
+IMPLS = {"auto": 0, "chunk": 1, "recurrent": 2, "segmented": 3, "chunk_cluster": 4, "chunk_single": 5, "chunk_split": 6}
+IMPL_NAMES = {1: "chunk", 2: "recurrent", 3: "segmented", 4: "chunk_cluster", 5: "chunk_single", 6: "chunk_split"}
+# impl values whose calls may need a workspace (gdn_prefill_workspace_bytes), allocated per call
+_WORKSPACE_IMPLS = ("auto", "segmented", "chunk_split")
 _DT = {torch.float32: GDN_DTYPE_F32, torch.bfloat16: GDN_DTYPE_BF16}
 
 
@@ -281,7 +283,7 @@ def _prefill_impl(q, k, u, v, la, beta, s0, output_final_state: bool, out_dtype:
         return y, s_out
     ws = None
     with torch.cuda.device(q.device):
-        if impl in ("auto", "segmented"):
+        if impl in _WORKSPACE_IMPLS:
             need = ctypes.c_size_t(0)
             _check(lib.gdn_prefill_workspace_bytes(ctypes.byref(a), ctypes.byref(need)))
             if need.value > 0:  # scratch through torch's caching allocator; the library allocates nothing
@@ -560,7 +562,7 @@ def nsgdn_scan(q, k, u, v, la) -> torch.Tensor:
 @torch.compiler.disable
 def selected_impl(q, k, v, la, beta=None, u=None, impl="auto") -> str:
     """Name of the kernel ``gdn_prefill`` runs for these arguments ("chunk_cluster", "chunk_single",
-    "segmented" or "recurrent")."""
+    "chunk_split", "segmented" or "recurrent")."""
     _check_cuda(q, k, u, v, la, beta)
     in_dtype = torch.bfloat16 if q.dtype == torch.bfloat16 else torch.float32
     q, k, v = (_prep_token(t, n, in_dtype) for t, n in ((q, "q"), (k, "k"), (v, "v")))
@@ -573,7 +575,7 @@ def selected_impl(q, k, v, la, beta=None, u=None, impl="auto") -> str:
         Strides(T * H * DV, H * DV, DV), B, T, H, DK, DV, _DT[in_dtype], _DT[in_dtype], IMPLS[impl], 0,
     )
     lib = load_library()
-    if impl in ("auto", "segmented"):
+    if impl in _WORKSPACE_IMPLS:
         need = ctypes.c_size_t(0)
         _check(lib.gdn_prefill_workspace_bytes(ctypes.byref(a), ctypes.byref(need)))
         if need.value > 0:  # the caller of gdn_prefill always supplies it

@@ -735,7 +735,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--prefill-impl", choices=["auto", "chunk", "chunk_cluster", "chunk_single", "recurrent", "segmented"], default="auto")
+    ap.add_argument("--prefill-impl", choices=["auto", "chunk", "chunk_cluster", "chunk_single", "chunk_split", "recurrent", "segmented"], default="auto")
     ap.add_argument("--skip-extra", action="store_true", help="headline prefill only")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the cpu_baseline leg")
     ap.add_argument("--only", choices=["decode", "backward", "layer", "nstep", "lm", "long_context", "fla"], default=None,

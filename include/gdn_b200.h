@@ -58,7 +58,11 @@ typedef enum {
   GDN_IMPL_SEGMENTED = 3,  /* chunk kernel split into sequence segments for few long sequences;
                               needs the workspace gdn_prefill_workspace_bytes reports */
   GDN_IMPL_CHUNK_CLUSTER = 4, /* chunk kernel on a two-CTA cluster per sequence (DV = 128, u = NULL) */
-  GDN_IMPL_CHUNK_SINGLE = 5   /* chunk kernel on one CTA per sequence and 128-row state tile */
+  GDN_IMPL_CHUNK_SINGLE = 5,  /* chunk kernel on one CTA per sequence and 128-row state tile */
+  GDN_IMPL_CHUNK_SPLIT = 6    /* every chunk's state-independent products in one parallel pass, then
+                                 one state-only CTA per sequence and 128-row state tile reading them
+                                 (any DV multiple of 128, u given or not); needs the workspace
+                                 gdn_prefill_workspace_bytes reports (24 KB per (b, h, chunk)) */
 } gdn_impl;
 
 /* Strides of one token tensor, in elements.  The last (feature) dimension has stride 1. */
@@ -92,7 +96,8 @@ typedef struct {
   int32_t out_dtype;  /* gdn_dtype of y */
   int32_t impl;       /* gdn_impl */
   int32_t reserved;
-  void* workspace;    /* device scratch for GDN_IMPL_SEGMENTED (16-byte aligned), or NULL */
+  void* workspace;    /* device scratch for GDN_IMPL_SEGMENTED / GDN_IMPL_CHUNK_SPLIT (16-byte
+                         aligned), or NULL */
   uint64_t workspace_bytes;
 } gdn_prefill_args;
 
@@ -125,11 +130,14 @@ typedef struct {
 int gdn_decode_step(const gdn_decode_args* args, void* stream);
 
 /*
- * Bytes of device workspace the segmented path needs for these arguments (0 when it does not
- * apply).  The segmented path is chosen for few (b, h) sequences with long T: phase A writes a
- * (DV + 128) x 128 fp32 pair of segment states per (b, h, segment), phase B combines them, phase
- * C reads them back.  Under GDN_IMPL_AUTO a call without enough workspace runs the single-pass
- * chunk kernel instead; GDN_IMPL_SEGMENTED without it fails with GDN_ERR_SHAPE.
+ * Bytes of device workspace the call needs for these arguments (0 when none).  The segmented path
+ * is chosen for few (b, h) sequences with long T: phase A writes a (DV + 128) x 128 fp32 pair of
+ * segment states per (b, h, segment), phase B combines them, phase C reads them back; where the
+ * split chunk kernels serve it, every chunk's products (24 KB per (b, h, chunk)) follow the segment
+ * states.  The split path (GDN_IMPL_CHUNK_SPLIT; under GDN_IMPL_AUTO for DV > 128 or explicit write
+ * vectors) needs the products alone.  Under GDN_IMPL_AUTO a call without enough workspace runs a
+ * single-pass chunk kernel instead; GDN_IMPL_SEGMENTED or GDN_IMPL_CHUNK_SPLIT without it fails with
+ * GDN_ERR_SHAPE.
  */
 int gdn_prefill_workspace_bytes(const gdn_prefill_args* args, size_t* bytes);
 
@@ -383,8 +391,8 @@ typedef struct gdn_write_vectors_bwd_args {
 int gdn_write_vectors_bwd(const gdn_write_vectors_bwd_args* args, void* stream);
 
 /* Which kernel a prefill with these arguments runs (GDN_IMPL_CHUNK_CLUSTER, _CHUNK_SINGLE,
- * _SEGMENTED or _RECURRENT; GDN_IMPL_CHUNK resolves to one of the two chunk variants), or a
- * negative gdn_status if the arguments are invalid.  Launches nothing. */
+ * _CHUNK_SPLIT, _SEGMENTED or _RECURRENT; GDN_IMPL_CHUNK resolves to one of the two single-launch
+ * chunk variants), or a negative gdn_status if the arguments are invalid.  Launches nothing. */
 int gdn_prefill_select_impl(const gdn_prefill_args* args);
 
 /*

@@ -87,7 +87,8 @@ def test_validation_codes():
     assert status(fake_args(DV=0)) == -5
     assert status(fake_args(in_dtype=7)) == -3
     assert status(fake_args(impl=9)) == -5
-    assert status(fake_args(impl=6)) == -5
+    assert status(fake_args(impl=7)) == -5
+    assert status(fake_args(impl=6)) == -2  # the split path without its workspace
     assert status(fake_args(q=0x10002)) == -4  # misaligned vector loads
 
 
@@ -163,3 +164,29 @@ def test_ops_refuse_cpu_tensors():
     x = torch.zeros(1, 4, 1, 32)
     with pytest.raises(ValueError, match="CUDA"):
         ops.gdn_prefill(x, x, x, torch.zeros(1, 4, 1), beta=torch.zeros(1, 4, 1))
+
+
+def test_split_path_workspace_and_selection():
+    """DV > 128 (or explicit write vectors) under auto: the split path when the caller supplies the
+    workspace gdn_prefill_workspace_bytes reports (24 KB per (b, h, chunk)), else the single-CTA kernel."""
+    lib = ops.load_library()
+    B, T, H, DV = 2, 130, 4, 256
+    a = fake_args(shape=(B, T, H, 128, DV))
+    need = ctypes.c_size_t(0)
+    assert lib.gdn_prefill_workspace_bytes(ctypes.byref(a), ctypes.byref(need)) == 0
+    assert need.value == B * H * 3 * 24576
+    assert status(a) == 5  # no workspace: the single-CTA kernel
+    a.workspace, a.workspace_bytes = 0x100000, need.value
+    assert status(a) == 6
+    a.workspace_bytes = need.value - 16
+    assert status(a) == 5
+    # DV = 128, u = beta k: the cluster kernel, no workspace
+    b = fake_args(shape=(B, T, H, 128, 128))
+    assert lib.gdn_prefill_workspace_bytes(ctypes.byref(b), ctypes.byref(need)) == 0 and need.value == 0
+    assert status(b) == 4
+    # the same with the split path requested
+    b.impl = 6
+    assert lib.gdn_prefill_workspace_bytes(ctypes.byref(b), ctypes.byref(need)) == 0
+    assert need.value == B * H * 3 * 24576
+    b.workspace, b.workspace_bytes = 0x100000, need.value
+    assert status(b) == 6

@@ -16,9 +16,10 @@ from oracle import oracle as O
 pytestmark = pytest.mark.gpu
 TOL_MAX, TOL_REL = 2e-3, 1e-3
 TOL_REL_BF16_OUT = 3e-3
-# The two chunk kernels: a two-CTA cluster per sequence (DV = 128, u = beta k) and one CTA per
-# sequence and 128-row state slice.
-VARIANTS = ["chunk_cluster", "chunk_single"]
+# The chunk kernels: a two-CTA cluster per sequence (DV = 128, u = beta k), one CTA per sequence
+# and 128-row state slice, and the split path (every chunk's products in one parallel pass, then
+# one state-only CTA per sequence and state slice).
+VARIANTS = ["chunk_cluster", "chunk_single", "chunk_split"]
 
 
 def np32(t):
@@ -69,13 +70,15 @@ def test_initial_state(impl):
     check(S, S_o, "S_T")
 
 
-def test_write_vector_given():
-    y, S, y_o, S_o = run_case(2, 160, 2, seed=6, with_u=True)
+@pytest.mark.parametrize("impl", ["chunk", "chunk_split"])
+def test_write_vector_given(impl):
+    y, S, y_o, S_o = run_case(2, 160, 2, seed=6, with_u=True, impl=impl)
     check(y, y_o, "y (u given)")
     check(S, S_o, "S_T (u given)")
 
 
-def test_nstep_write_vectors():
+@pytest.mark.parametrize("impl", ["chunk", "chunk_split"])
+def test_nstep_write_vectors(impl):
     """n_steps = 2 write vectors (archbench/layers/nsgdn.py:61-75): u is not parallel to k."""
     B, T, H = 1, 128, 2
     x = make_inputs(B, T, H, 128, 128, seed=17, dtype=torch.bfloat16)
@@ -85,7 +88,7 @@ def test_nstep_write_vectors():
     u_bf = torch.from_numpy(u.astype(np.float32)).to(torch.bfloat16)
     y_o, S_o = O.recurrence_c(*(np32(x[n]) for n in ("q", "k", "v", "la")), u=np32(u_bf))
     g = {k_: v.cuda() for k_, v in x.items()}
-    y, S = ops.gdn_prefill(g["q"], g["k"], g["v"], g["la"], u=u_bf.cuda(), output_final_state=True, out_dtype=torch.float32, impl="chunk")
+    y, S = ops.gdn_prefill(g["q"], g["k"], g["v"], g["la"], u=u_bf.cuda(), output_final_state=True, out_dtype=torch.float32, impl=impl)
     check(y, y_o, "y")
     check(S, S_o, "S_T")
 
@@ -167,21 +170,26 @@ def test_bounded_wait_times_out_and_context_survives():
     check(y, y_o, "y after timeout self test")
 
 
+@pytest.mark.parametrize("impl", ["auto", "chunk_single"])
 @pytest.mark.parametrize("DV", [256, 384])
-def test_value_dim_multiple_of_128(DV):
-    """expand_v > 1 (configs/arch/nsgdn.yaml uses DV = 2 DK): one CTA per 128-row state slice."""
+def test_value_dim_multiple_of_128(DV, impl):
+    """expand_v > 1 (configs/arch/nsgdn.yaml uses DV = 2 DK): one CTA per 128-row state slice (the
+    split path under auto, the single-CTA kernel on request)."""
     x = make_inputs(2, 130, 2, 128, DV, seed=DV, dtype=torch.bfloat16)
     S0 = torch.randn(2, 2, DV, 128, generator=torch.Generator().manual_seed(3)) * 0.2
     y_o, S_o = O.recurrence_c(*(np32(x[n]) for n in ("q", "k", "v", "la")), beta=np32(x["beta"]), s0=S0.numpy())
     g = {k: v.cuda() for k, v in x.items()}
-    assert ops.selected_impl(g["q"], g["k"], g["v"], g["la"], beta=g["beta"]) == "chunk_single"
-    y, S = ops.gdn_prefill(g["q"], g["k"], g["v"], g["la"], beta=g["beta"], initial_state=S0.cuda(), output_final_state=True, out_dtype=torch.float32)
+    want = "chunk_split" if impl == "auto" else impl
+    assert ops.selected_impl(g["q"], g["k"], g["v"], g["la"], beta=g["beta"], impl=impl) == want
+    y, S = ops.gdn_prefill(g["q"], g["k"], g["v"], g["la"], beta=g["beta"], initial_state=S0.cuda(), output_final_state=True,
+                           out_dtype=torch.float32, impl=impl)
     check(y, y_o, f"y DV={DV}")
     check(S, S_o, f"S_T DV={DV}")
 
 
+@pytest.mark.parametrize("impl", ["auto", "chunk_single"])
 @pytest.mark.parametrize("DV", [256, 384])
-def test_write_vectors_with_wide_state(DV):
+def test_write_vectors_with_wide_state(DV, impl):
     """n_steps = 2 write vectors with DV = 2 DK (configs/arch/nsgdn.yaml: head_dim 128, expand_v 2,
     n_steps 2): the explicit-u kernel runs once per 128-row state slice; bf16 output, initial state
     updated in place."""
@@ -194,10 +202,11 @@ def test_write_vectors_with_wide_state(DV):
     S0 = torch.randn(B, H, DV, 128, generator=torch.Generator().manual_seed(4)) * 0.2
     y_o, S_o = O.recurrence_c(*(np32(x[n]) for n in ("q", "k", "v", "la")), u=np32(u_bf), s0=S0.numpy())
     g = {k_: v.cuda() for k_, v in x.items()}
-    assert ops.selected_impl(g["q"], g["k"], g["v"], g["la"], u=u_bf.cuda()) == "chunk_single"
+    want = "chunk_split" if impl == "auto" else impl
+    assert ops.selected_impl(g["q"], g["k"], g["v"], g["la"], u=u_bf.cuda(), impl=impl) == want
     s = S0.cuda()
     y, S = ops.gdn_prefill(g["q"], g["k"], g["v"], g["la"], u=u_bf.cuda(), initial_state=s, output_final_state=True,
-                           out_dtype=torch.float32)
+                           out_dtype=torch.float32, impl=impl)
     check(y, y_o, f"y DV={DV} (u given)")
     check(S, S_o, f"S_T DV={DV} (u given)")
 
@@ -260,4 +269,22 @@ def test_unaligned_y_rows(T, with_u):
     check(ybuf[..., :128], y_o, f"y ({what}, unaligned y rows)")
     check(s_out, S_o, f"S_T ({what}, unaligned y rows)")
     assert torch.isnan(ybuf[..., 128]).all()
+    assert ops.device_status() == 0
+
+
+@pytest.mark.parametrize("T,s0", [(1, False), (63, True), (64, False), (130, True), (4096, False)])
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16])
+def test_split_equals_cluster_bitwise(T, s0, out_dtype):
+    """The prep kernel restates the cluster kernel's prep CTA operation for operation and the state-only
+    kernel is that kernel's state CTA: for DV = 128 and u = beta k both paths give the same bits."""
+    B, H = 2, 3
+    g = make_inputs(B, T, H, 128, 128, seed=50 + T, dtype=torch.bfloat16, device="cuda")
+    S0 = torch.randn(B, H, 128, 128, device="cuda", generator=torch.Generator(device="cuda").manual_seed(T)) * 0.3 if s0 else None
+    out = {}
+    for impl in ("chunk_cluster", "chunk_split"):
+        out[impl] = ops.gdn_prefill(g["q"], g["k"], g["v"], g["la"], beta=g["beta"], initial_state=S0, output_final_state=True,
+                                    out_dtype=out_dtype, impl=impl)
+    torch.cuda.synchronize()
+    assert torch.equal(out["chunk_cluster"][0], out["chunk_split"][0])
+    assert torch.equal(out["chunk_cluster"][1], out["chunk_split"][1])
     assert ops.device_status() == 0
