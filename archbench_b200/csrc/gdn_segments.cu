@@ -6,8 +6,8 @@
 //   A. a chunk kernel in state mode over segments 0..P-2: N_s from S = 0 with the real v, M_s from
 //      S = I with v = 0 (one extra 128-row tile per (b, h, segment)); no y.
 //   B. combine_kernel: S_{s+1} = S_s M_s + N_s, s = 0..P-2, fp32 on CUDA cores, the state rows
-//      split over CTAs (rows evolve independently), M_s double-buffered in shared memory, result
-//      written over N_s.
+//      split over CTAs (rows evolve independently), the contraction over four threads per column,
+//      M_s double-buffered in shared memory, result written over N_s.
 //   C. the chunk kernel in output mode over all P segments, segment s starting from S_s.
 // The chunk kernel is the state-only one of gdn_chunk_pair_sm100.cu after one prep pass over every
 // chunk (gdn_chunk_prep_sm100.cu), whose products both passes read; where y cannot be stored by TMA,
@@ -26,6 +26,7 @@ namespace seg {
 
 constexpr int D = 128;
 constexpr int RB = 4;                                 // state rows per combine CTA
+constexpr int KS = 4;                                 // threads per state column (contraction quarters)
 constexpr uint32_t COMB_SMEM = 2u * D * D * 4u;       // two transition matrices M_s (64 KB each)
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
@@ -37,56 +38,72 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-// S_{s+1} = S_s M_s + N_s for s = 0..nslots-1, RB state rows per CTA (rows evolve independently),
-// one thread per state column.  M_s is staged in shared memory by cp.async, the next step's copy
-// in flight while the current step computes: the chain of steps is bound by the step's own
-// arithmetic instead of by L2 latency.
-__global__ void __launch_bounds__(D) combine_kernel(float* __restrict__ ws, const float* __restrict__ s0, int DV,
-                                                    int nslots, int rblocks) {
+// S_{s+1} = S_s M_s + N_s for s = 0..nslots-1, RB state rows per CTA (rows evolve independently).
+// Thread (j, ks) of the KS x D threads takes state column j and the ks-th quarter of the
+// contraction; the quarters meet in shared memory in a fixed order.  M_s is staged in shared memory
+// by cp.async, the next step's copy in flight while the current step computes: the chain of steps
+// is bound by the step's own latency instead of by L2 latency.
+__global__ void __launch_bounds__(KS * D) combine_kernel(float* __restrict__ ws, const float* __restrict__ s0, int DV,
+                                                         int nslots, int rblocks) {
   extern __shared__ __align__(16) float msm[];  // [2][D][D]
   __shared__ float srow[RB][D];
+  __shared__ float part[KS][RB][D];
   const int bh = blockIdx.x / rblocks, r0 = (blockIdx.x % rblocks) * RB;
-  const int j = threadIdx.x;
+  const int j = threadIdx.x % D, ks = threadIdx.x / D;
+  constexpr int KQ = D / KS;  // contraction indices per thread
   float s[RB];
 #pragma unroll
-  for (int r = 0; r < RB; ++r) s[r] = s0 ? s0[((int64_t)bh * DV + r0 + r) * D + j] : 0.f;
+  for (int r = 0; r < RB; ++r) s[r] = (ks == 0 && s0) ? s0[((int64_t)bh * DV + r0 + r) * D + j] : 0.f;
   auto slot = [&](int t) { return ws + (int64_t)(bh * nslots + t) * (DV + D) * D; };
   auto prefetch = [&](int t) {
     const float* M = slot(t) + (int64_t)DV * D;
     float* dst = msm + (t & 1) * D * D;
-#pragma unroll 4
-    for (int i = j; i < D * D / 4; i += D) cp_async16(dst + 4 * i, M + 4 * i);
+#pragma unroll 2
+    for (int i = threadIdx.x; i < D * D / 4; i += KS * D) cp_async16(dst + 4 * i, M + 4 * i);
     cp_async_commit();
   };
   if (nslots > 0) prefetch(0);
 #pragma unroll 1
   for (int t = 0; t < nslots; ++t) {
     float* mat = slot(t);
-#pragma unroll
-    for (int r = 0; r < RB; ++r) srow[r][j] = s[r];
     float acc[RB];
+    if (ks == 0) {
 #pragma unroll
-    for (int r = 0; r < RB; ++r) acc[r] = mat[(int64_t)(r0 + r) * D + j];
-    if (t + 1 < nslots) {  // the buffer it fills was last read at step t - 1 (barrier below)
+      for (int r = 0; r < RB; ++r) {
+        srow[r][j] = s[r];
+        acc[r] = mat[(int64_t)(r0 + r) * D + j];
+      }
+    }
+    if (t + 1 < nslots) {  // the buffer it fills was last read at step t - 1 (barriers below)
       prefetch(t + 1);
       cp_async_wait<1>();
     } else {
       cp_async_wait<0>();
     }
     __syncthreads();  // srow written; M_t copied by every thread
-    const float* M = msm + (t & 1) * D * D;
+    const float* M = msm + (t & 1) * D * D + ks * KQ * D;
+    float pr[RB];
+#pragma unroll
+    for (int r = 0; r < RB; ++r) pr[r] = 0.f;
 #pragma unroll 8
-    for (int k = 0; k < D; ++k) {
+    for (int k = 0; k < KQ; ++k) {
       const float m = M[k * D + j];
 #pragma unroll
-      for (int r = 0; r < RB; ++r) acc[r] = fmaf(srow[r][k], m, acc[r]);
+      for (int r = 0; r < RB; ++r) pr[r] = fmaf(srow[r][ks * KQ + k], m, pr[r]);
     }
 #pragma unroll
-    for (int r = 0; r < RB; ++r) {
-      s[r] = acc[r];
-      mat[(int64_t)(r0 + r) * D + j] = acc[r];
+    for (int r = 0; r < RB; ++r) part[ks][r][j] = pr[r];
+    __syncthreads();  // every quarter written; M_t and srow read
+    if (ks == 0) {
+#pragma unroll
+      for (int r = 0; r < RB; ++r) {
+        float v = acc[r];
+#pragma unroll
+        for (int q = 0; q < KS; ++q) v += part[q][r][j];
+        s[r] = v;
+        mat[(int64_t)(r0 + r) * D + j] = v;
+      }
     }
-    __syncthreads();
   }
 }
 
@@ -143,7 +160,7 @@ static int launch_combine(const gdn_prefill_args* a, float* ws, int P, cudaStrea
   static std::atomic<unsigned long long> opted{0};  // per device (see gdn::opt_in_smem)
   if (!gdn::opt_in_smem(opted, {{(const void*)gdn::seg::combine_kernel, (int)gdn::seg::COMB_SMEM}}))
     return GDN_ERR_LAUNCH;
-  gdn::seg::combine_kernel<<<(unsigned)grid, gdn::seg::D, gdn::seg::COMB_SMEM, stream>>>(ws, a->s0, (int)a->DV, P - 1,
+  gdn::seg::combine_kernel<<<(unsigned)grid, gdn::seg::KS * gdn::seg::D, gdn::seg::COMB_SMEM, stream>>>(ws, a->s0, (int)a->DV, P - 1,
                                                                                           rblocks);
   return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
 }
