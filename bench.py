@@ -178,6 +178,11 @@ class ClockSampler:
                 "samples": len(rows), "power_w_max": max(r[2] for r in rows)}
 
 
+# Kernel launches of one gdn_prefill per selected path (the segmented path: prep, state pass, combine,
+# output pass; the split path: prep and the state-only kernel).
+LAUNCHES_PER_PREFILL = {"chunk_cluster": 1, "chunk_single": 1, "chunk_split": 2, "segmented": 4, "recurrent": 1}
+
+
 def timed(fn, steps, warmup, world, stream=None):
     """Warm up, then time exactly ``steps`` calls with CUDA events on the launching stream,
     bracketed by a barrier and a device synchronize; returns max-over-ranks seconds."""
@@ -348,8 +353,9 @@ def bench_backward(args, rank, world):
 
 def bench_nstep(args, rank, world):
     """nsgdn's n-step write vectors at configuration-1 tokens with archbench's default nsgdn keys
-    (B=8, T=4096, H=8, DK=128, DV=256, n_steps=2): the prefill with u given (single-CTA kernel,
-    u tiles in its q/k ring) and the write vectors' backward (gdn_write_vectors_bwd)."""
+    (B=8, T=4096, H=8, DK=128, DV=256, n_steps=2): the prefill with u given (the split path: prep
+    kernel, then the state-only chunk kernel with u tiles in its k/q ring) and the write vectors'
+    backward (gdn_write_vectors_bwd)."""
     import torch.nn.functional as F
 
     from archbench_b200 import ops
@@ -383,7 +389,8 @@ def bench_nstep(args, rank, world):
             "roofline": {"bound": "hbm", "prefill_achieved_gbs": alg_f / t_f / 1e9, "prefill_frac": alg_f / t_f / 1e9 / hbm,
                          "write_vectors_bwd_achieved_gbs": alg_w / t_w / 1e9, "write_vectors_bwd_frac": alg_w / t_w / 1e9 / hbm,
                          "peak": hbm, "unit": "GB/s", "peak_source": src},
-            "gpu_launches": 2 * steps}
+            "kernel": ops.selected_impl(x["q"], x["k"], x["v"], x["la"], u=u),
+            "gpu_launches": (LAUNCHES_PER_PREFILL[ops.selected_impl(x["q"], x["k"], x["v"], x["la"], u=u)] + 1) * steps}
 
 
 def bench_layer(args, rank, world):
@@ -420,7 +427,10 @@ def bench_layer(args, rank, world):
             "default_keys": {"config": "the same with expand_v 2, n_steps 2 (archbench's nsgdn defaults)",
                              "infer_ms": t_i2 * 1e3, "infer_tok_s": world * tok / t_i2, "train_step_ms": t_t2 * 1e3,
                              "train_tok_s": world * tok / t_t2},
-            "gpu_launches": 29 * steps}
+            # expand_v 1: inference 3, training step 9 (prologue, scan, epilogue; their backwards with the
+            # scan's four); default keys: inference 4 (split scan: 2), training step 15 (DV = 256: two slices
+            # of the scan's backward, the write vectors' backward)
+            "gpu_launches": 31 * steps}
 
 
 def bench_long_context(args, rank, world):
@@ -466,7 +476,7 @@ def bench_long_context(args, rank, world):
             "ms_gather_bthd": (t_g - t_c) / steps * 1e3, "heads_per_rank": h_loc, "kernel": sel, "scaling": "strong",
             "gather": "NCCL all_gather_into_tensor, in place into a head-major (H, B, T, DV) buffer; value_gather_bthd: "
                       "gather then permute-copy into (B, T, H, DV)",
-            "gpu_launches": 3 * steps}
+            "gpu_launches": 3 * LAUNCHES_PER_PREFILL[sel] * steps}
 
 
 def bench_lm(args, rank, world):
