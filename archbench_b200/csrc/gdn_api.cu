@@ -87,11 +87,20 @@ bool segmented_preferred(const gdn_prefill_args* a, int sms) {
   return a->B * a->H * 8 <= (int64_t)sms;
 }
 
-// The split path (prep pass over every chunk, then the state-only chunk kernel) where the cluster
-// kernel does not apply: state rows beyond 128 or explicit write vectors.  Its workspace holds every
-// chunk's products.
+// Waves of CTAs a launch of `ctas` CTAs takes at `per_wave` resident at once.
+int64_t waves(int64_t ctas, int64_t per_wave) { return per_wave > 0 ? (ctas + per_wave - 1) / per_wave : ctas; }
+
+// The split path (prep pass over every chunk, then the state-only chunk kernel: one CTA per sequence
+// and 128-row state slice) where the cluster kernel does not apply -- state rows beyond 128 or
+// explicit write vectors -- or where the cluster kernel, two SMs per sequence, would need more waves
+// than the state-only kernel (more sequences than clusters fit on the GPU).  Its workspace holds
+// every chunk's products.
 bool split_preferred(const gdn_prefill_args* a) {
-  return gdn_chunk_supported(a) && gdn_chunk_split_supported(a) && chunk_variant(a) != GDN_IMPL_CHUNK_CLUSTER;
+  if (!gdn_chunk_supported(a) || !gdn_chunk_split_supported(a)) return false;
+  if (chunk_variant(a) != GDN_IMPL_CHUNK_CLUSTER) return true;
+  const int clusters = gdn_chunk_pair_max_clusters();
+  const int64_t seqs = a->B * a->H;
+  return clusters > 0 && waves(seqs, clusters) > waves(seqs, plan_sms());
 }
 
 int select_impl(const gdn_prefill_args* a) {

@@ -612,6 +612,10 @@ def keep_freed_heap():
         return False
 
 
+CPU_SAMPLE = ("cfg1 B8 T4096 H8 d128 fp32: each step one pass over the whole configuration-1 batch (8 sequences of "
+              "4096 tokens, fed in 64-token slices with the state carried); glibc heap trimming off (mallopt)")
+
+
 def cpu_reference_setup():
     """Inputs of the CPU legs: the whole configuration-1 batch in fp32 (seed 7), u = beta k."""
     keep_freed_heap()

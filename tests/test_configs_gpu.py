@@ -41,7 +41,7 @@ def test_cfg2_decode_after_prefill_against_oracle():
     sub = lambda x: x[bs][:, :, hs]
     ref_in = {n: torch.cat([sub(pre[n]), sub(tok[n])], 1) for n in pre}
     _, state = ops.gdn_prefill(pre["q"], pre["k"], pre["v"], pre["la"], beta=pre["beta"], output_final_state=True)
-    assert ops.selected_impl(pre["q"], pre["k"], pre["v"], pre["la"], beta=pre["beta"]) in ("chunk_cluster", "chunk_single")
+    assert ops.selected_impl(pre["q"], pre["k"], pre["v"], pre["la"], beta=pre["beta"]) in ("chunk_cluster", "chunk_single", "chunk_split")
     del pre
     ys = []
     for t in range(steps):

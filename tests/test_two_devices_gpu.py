@@ -3,8 +3,9 @@ opts in per device (a function attribute belongs to the function as loaded in on
 context), so launches on the second device must work after the first device has set up its own.
 
 The same calls run on cuda:0 and then on cuda:1 -- the cluster and single-CTA chunk kernels, the
-segmented path, the allocation-free entry point, the backward and the fused layer prologue and
-epilogue -- and must give bitwise the same results on both devices (the kernels are deterministic);
+split path (prep kernel and state-only chunk kernel), the segmented path, the allocation-free entry
+point, the backward and the fused layer prologue and epilogue -- and must give bitwise the same
+results on both devices (the kernels are deterministic);
 the prefill is also checked against the float64 oracle.  No peer memory is touched.  Skipped with
 fewer than two GPUs."""
 
@@ -27,7 +28,7 @@ def _run_all(dev):
     out = {}
     with torch.cuda.device(dev):
         x = make_inputs(2, 320, 3, 128, 128, seed=41, dtype=torch.bfloat16, device=dev)
-        for impl in ("chunk_cluster", "chunk_single"):
+        for impl in ("chunk_cluster", "chunk_single", "chunk_split"):
             y, S = ops.gdn_prefill(x["q"], x["k"], x["v"], x["la"], beta=x["beta"], output_final_state=True,
                                    out_dtype=torch.float32, impl=impl)
             out[f"y_{impl}"], out[f"S_{impl}"] = y, S
@@ -61,7 +62,7 @@ def test_every_kernel_runs_on_both_devices_with_equal_results():
     for k in r0:
         assert torch.equal(r0[k], r1[k]), f"{k} differs between cuda:0 and cuda:1"
     y_o, S_o = O.recurrence_c(*(x0[n].numpy() for n in ("q", "k", "v", "la")), beta=x0["beta"].numpy())
-    for impl in ("chunk_cluster", "chunk_single"):
+    for impl in ("chunk_cluster", "chunk_single", "chunk_split"):
         for got, want, what in ((r0[f"y_{impl}"], y_o, "y"), (r0[f"S_{impl}"], S_o, "S")):
             mx, rel = O.errors(got.numpy(), want)
             assert mx <= 2e-3 and rel <= 1e-3, f"{impl} {what}: max-abs {mx:.3e} rel-L2 {rel:.3e}"
