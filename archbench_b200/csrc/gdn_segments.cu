@@ -27,7 +27,8 @@ namespace seg {
 constexpr int D = 128;
 constexpr int RB = 4;                                 // state rows per combine CTA
 constexpr int KS = 4;                                 // threads per state column (contraction quarters)
-constexpr uint32_t COMB_SMEM = 2u * D * D * 4u;       // two transition matrices M_s (64 KB each)
+constexpr int NMB = 2;                                // transition matrices in flight per combine CTA
+constexpr uint32_t COMB_SMEM = NMB * D * D * 4u;     // NMB transition matrices M_s (64 KB each)
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(smem))),
@@ -41,11 +42,11 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 // S_{s+1} = S_s M_s + N_s for s = 0..nslots-1, RB state rows per CTA (rows evolve independently).
 // Thread (j, ks) of the KS x D threads takes state column j and the ks-th quarter of the
 // contraction; the quarters meet in shared memory in a fixed order.  M_s is staged in shared memory
-// by cp.async, the next step's copy in flight while the current step computes: the chain of steps
-// is bound by the step's own latency instead of by L2 latency.
+// by cp.async, the copies of the next NMB - 1 steps in flight while the current step computes: the
+// chain of steps is bound by the step's own latency instead of by L2 latency.
 __global__ void __launch_bounds__(KS * D) combine_kernel(float* __restrict__ ws, const float* __restrict__ s0, int DV,
                                                          int nslots, int rblocks) {
-  extern __shared__ __align__(16) float msm[];  // [2][D][D]
+  extern __shared__ __align__(16) float msm[];  // [NMB][D][D]
   __shared__ float srow[RB][D];
   __shared__ float part[KS][RB][D];
   const int bh = blockIdx.x / rblocks, r0 = (blockIdx.x % rblocks) * RB;
@@ -57,12 +58,16 @@ __global__ void __launch_bounds__(KS * D) combine_kernel(float* __restrict__ ws,
   auto slot = [&](int t) { return ws + (int64_t)(bh * nslots + t) * (DV + D) * D; };
   auto prefetch = [&](int t) {
     const float* M = slot(t) + (int64_t)DV * D;
-    float* dst = msm + (t & 1) * D * D;
+    float* dst = msm + (t % NMB) * D * D;
 #pragma unroll 2
     for (int i = threadIdx.x; i < D * D / 4; i += KS * D) cp_async16(dst + 4 * i, M + 4 * i);
     cp_async_commit();
   };
-  if (nslots > 0) prefetch(0);
+  for (int t = 0; t < NMB - 1 && t < nslots; ++t) prefetch(t);
+  // N_t's rows (written over by S_{t+1} at the end of step t) are loaded a step ahead, into registers.
+  float accn[RB];
+#pragma unroll
+  for (int r = 0; r < RB; ++r) accn[r] = (ks == 0 && nslots > 0) ? slot(0)[(int64_t)(r0 + r) * D + j] : 0.f;
 #pragma unroll 1
   for (int t = 0; t < nslots; ++t) {
     float* mat = slot(t);
@@ -71,17 +76,26 @@ __global__ void __launch_bounds__(KS * D) combine_kernel(float* __restrict__ ws,
 #pragma unroll
       for (int r = 0; r < RB; ++r) {
         srow[r][j] = s[r];
-        acc[r] = mat[(int64_t)(r0 + r) * D + j];
+        acc[r] = accn[r];
+      }
+      if (t + 1 < nslots) {
+        const float* nxt = slot(t + 1);
+#pragma unroll
+        for (int r = 0; r < RB; ++r) accn[r] = nxt[(int64_t)(r0 + r) * D + j];
       }
     }
-    if (t + 1 < nslots) {  // the buffer it fills was last read at step t - 1 (barriers below)
-      prefetch(t + 1);
+    // The copy of step t + NMB - 1 goes into the buffer step t - 1 read (barriers below); then every
+    // copy but the newest NMB - 2 has landed, step t's among them.
+    if (t + NMB - 1 < nslots) {
+      prefetch(t + NMB - 1);
+      cp_async_wait<NMB - 1>();
+    } else if (t + 1 < nslots) {
       cp_async_wait<1>();
     } else {
       cp_async_wait<0>();
     }
     __syncthreads();  // srow written; M_t copied by every thread
-    const float* M = msm + (t & 1) * D * D + ks * KQ * D;
+    const float* M = msm + (t % NMB) * D * D + ks * KQ * D;
     float pr[RB];
 #pragma unroll
     for (int r = 0; r < RB; ++r) pr[r] = 0.f;
