@@ -207,6 +207,23 @@ def timed(fn, steps, warmup, world, stream=None):
 # ------------------------------------------------------------------------------------------
 
 
+def graphed(fn):
+    """``fn`` (device work only, no collective) captured once in a CUDA graph after two warm-up calls
+    (the second on a side stream, as capture requires); returns the graph's replay.  Allocations ``fn``
+    makes come from the graph's private pool and stay valid for every replay."""
+    fn()
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        fn()
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        fn()
+    return graph.replay
+
+
 def bench_prefill(args, rank, world):
     from archbench_b200 import ops
 
@@ -219,21 +236,9 @@ def bench_prefill(args, rank, world):
         out["y"], _ = ops.gdn_prefill(x["q"], x["k"], x["v"], x["la"], beta=x["beta"], impl=impl)
 
     sel = ops.selected_impl(x["q"], x["k"], x["v"], x["la"], beta=x["beta"], impl=impl)
-    run = step
-    if args.graph:
-        # One gdn_prefill call (one kernel launch) captured in a CUDA graph and replayed per step:
-        # the timed loop then carries no host work (Python, argument checks, tensor-map encoding).
-        step()
-        torch.cuda.synchronize()
-        side = torch.cuda.Stream()
-        side.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(side):
-            step()
-        torch.cuda.current_stream().wait_stream(side)
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            step()
-        run = graph.replay
+    # One gdn_prefill call (one kernel launch) captured in a CUDA graph and replayed per step: the timed
+    # loop then carries no host work (Python, argument checks, tensor-map encoding).
+    run = graphed(step) if args.graph else step
     with ClockSampler(torch.cuda.current_device()) as clk:
         secs = timed(run, args.steps, args.warmup, world)
     fastest = min_over_ranks(secs, world)
@@ -452,11 +457,20 @@ def bench_long_context(args, rank, world):
     mine = full[rank * h_loc:(rank + 1) * h_loc]
     out = {}
 
-    def step_compute():
+    def prefill():
         out["y"], _ = ops.gdn_prefill(x["q"], x["k"], x["v"], x["la"], beta=x["beta"])
 
-    def step_gather_head_major():
+    def prefill_into_slice():
         ops.gdn_prefill_into(mine.permute(1, 2, 0, 3), x["q"], x["k"], x["v"], x["la"], beta=x["beta"])
+
+    # Each rank's prefill (up to four launches: prep, segment states, combine, output pass) is replayed
+    # from a CUDA graph, as the headline's step is, so host launch jitter on a busy host does not leak into
+    # the max over ranks; the NCCL gathers run eagerly between replays.
+    step_compute = graphed(prefill) if args.graph else prefill
+    fill_slice = graphed(prefill_into_slice) if args.graph else prefill_into_slice
+
+    def step_gather_head_major():
+        fill_slice()
         if world > 1:
             dist.all_gather_into_tensor(full, mine)
 
@@ -476,6 +490,8 @@ def bench_long_context(args, rank, world):
             "ms_gather_bthd": (t_g - t_c) / steps * 1e3, "heads_per_rank": h_loc, "kernel": sel, "scaling": "strong",
             "gather": "NCCL all_gather_into_tensor, in place into a head-major (H, B, T, DV) buffer; value_gather_bthd: "
                       "gather then permute-copy into (B, T, H, DV)",
+            "timing": ("each rank's prefill a CUDA graph replay, the gathers eager" if args.graph else
+                       "eager calls"),
             "gpu_launches": 3 * LAUNCHES_PER_PREFILL[sel] * steps}
 
 
