@@ -18,14 +18,17 @@ int dtype_size(int dt) {
 int check_device() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return GDN_ERR_DEVICE;
-  static int cached[64] = {0};  // 0 unknown, 1 ok, -1 bad
-  if (dev >= 0 && dev < 64 && cached[dev] != 0) return cached[dev] > 0 ? GDN_OK : GDN_ERR_DEVICE;
+  static std::atomic<int> cached[64] = {};  // 0 unknown, 1 ok, -1 bad (any host thread may call)
+  if (dev >= 0 && dev < 64) {
+    const int c = cached[dev].load(std::memory_order_relaxed);
+    if (c != 0) return c > 0 ? GDN_OK : GDN_ERR_DEVICE;
+  }
   int major = 0, minor = 0;
   if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess)
     return GDN_ERR_DEVICE;
   const bool ok = (major == 10 && minor == 0);
-  if (dev >= 0 && dev < 64) cached[dev] = ok ? 1 : -1;
+  if (dev >= 0 && dev < 64) cached[dev].store(ok ? 1 : -1, std::memory_order_relaxed);
   return ok ? GDN_OK : GDN_ERR_DEVICE;
 }
 

@@ -997,10 +997,11 @@ int launch_dt(const gdn_prefill_args* a, const Params& p, cudaStream_t stream) {
 
 // Clusters of this kernel that fit on the device at once (0 if the query fails).
 int max_active_clusters() {
-  static int cached[64] = {0};
+  static std::atomic<int> cached[64] = {};  // per device; any host thread may call
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
-  if (cached[dev] > 0) return cached[dev];
+  const int known = cached[dev].load(std::memory_order_relaxed);
+  if (known > 0) return known;
   auto kern = pair_kernel<false, false, __nv_bfloat16>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, DYN) != cudaSuccess) return 0;
   cudaLaunchConfig_t cfg = {};
@@ -1019,7 +1020,7 @@ int max_active_clusters() {
     cudaGetLastError();
     return 0;
   }
-  cached[dev] = n;
+  cached[dev].store(n, std::memory_order_relaxed);
   return n;
 }
 

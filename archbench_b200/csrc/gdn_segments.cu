@@ -122,13 +122,16 @@ __global__ void __launch_bounds__(KS * D) combine_kernel(float* __restrict__ ws,
 }
 
 int sm_count() {
-  static int cached[64] = {0};
+  static std::atomic<int> cached[64] = {};  // per device; any host thread may call
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 0;
-  if (dev >= 0 && dev < 64 && cached[dev] > 0) return cached[dev];
+  if (dev >= 0 && dev < 64) {
+    const int known = cached[dev].load(std::memory_order_relaxed);
+    if (known > 0) return known;
+  }
   int n = 0;
   if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
-  if (dev >= 0 && dev < 64) cached[dev] = n;
+  if (dev >= 0 && dev < 64) cached[dev].store(n, std::memory_order_relaxed);
   return n;
 }
 
