@@ -507,7 +507,7 @@ def _copy_streams(dev: torch.device):
 
 
 @torch.compiler.disable
-def gdn_prefill_from_host(q, k, v, la, beta, y_out, pieces=8, impl="auto", device=None):
+def gdn_prefill_from_host(q, k, v, la, beta, y_out, pieces=8, impl="auto", device=None, wait_current=False):
     """Prefill of host tensors (pinned, for asynchronous copies) into the host tensor ``y_out``.
 
     The batch is cut into ``pieces`` along B: each piece's inputs are copied to the GPU on one copy
@@ -515,14 +515,21 @@ def gdn_prefill_from_host(q, k, v, la, beta, y_out, pieces=8, impl="auto", devic
     host-to-device copies of later pieces overlap the prefill and the device-to-host copies of earlier
     ones (PCIe carries both directions at once).  Returns after enqueueing; the current stream waits
     for the last copy back, so synchronising it (or an event recorded on it) covers the whole call.
-    Same arguments and result as ``gdn_prefill(q, k, v, la, beta=beta)`` with y in ``y_out``'s dtype."""
+    Same arguments and result as ``gdn_prefill(q, k, v, la, beta=beta)`` with y in ``y_out``'s dtype.
+
+    The copies in start at once: the host inputs must hold their values when the call is made, as they
+    do when the host wrote them, so consecutive calls overlap one call's copies in with the previous
+    call's last prefill and copy back.  ``wait_current=True`` starts them only after the work already
+    queued on the current stream -- for inputs that a device-to-host copy ordered on that stream is
+    still writing.  The copies back always follow the current stream's earlier work."""
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
     cur = torch.cuda.current_stream(dev)
     h2d, d2h = _copy_streams(dev)
     B = q.shape[0]
     pieces = max(1, min(int(pieces), B))
     cuts = [B * i // pieces for i in range(pieces + 1)]
-    h2d.wait_stream(cur)
+    if wait_current:
+        h2d.wait_stream(cur)
     d2h.wait_stream(cur)
     for b0, b1 in zip(cuts[:-1], cuts[1:]):
         if b1 == b0:

@@ -227,6 +227,33 @@ def test_prefill_from_host_buffers(pieces):
         assert torch.equal(y.cpu(), y_host[b0:b1]), (b0, b1)
 
 
+def test_prefill_from_host_back_to_back_and_after_device_work():
+    """Consecutive host-buffer calls overlap one call's copies in with the previous call's tail: two calls
+    enqueued without a synchronisation in between each return what gdn_prefill returns; with
+    wait_current=True a call reads inputs that a device-to-host copy on the current stream is still
+    writing only after that copy."""
+    B, T, H = 4, 200, 2
+    xs = [{n: t.pin_memory() for n, t in make_inputs(B, T, H, 128, 128, seed=51 + i, dtype=torch.bfloat16).items()}
+          for i in range(2)]
+    ys = [torch.empty(B, T, H, 128, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    for x, y in zip(xs, ys):
+        ops.gdn_prefill_from_host(x["q"], x["k"], x["v"], x["la"], x["beta"], y, pieces=2)
+    torch.cuda.synchronize()
+    for x, y in zip(xs, ys):
+        g = {n: t.cuda() for n, t in x.items()}
+        want, _ = ops.gdn_prefill(g["q"], g["k"], g["v"], g["la"], beta=g["beta"])
+        assert torch.equal(want.cpu(), y)
+    # q produced on the device and copied to pinned host memory on the current stream, not yet complete
+    gq = make_inputs(B, T, H, 128, 128, seed=60, dtype=torch.bfloat16, device="cuda")["q"]
+    xs[0]["q"].copy_(gq, non_blocking=True)
+    ops.gdn_prefill_from_host(xs[0]["q"], xs[0]["k"], xs[0]["v"], xs[0]["la"], xs[0]["beta"], ys[0], pieces=2,
+                              wait_current=True)
+    torch.cuda.synchronize()
+    g = {n: t.cuda() for n, t in xs[0].items()}
+    want, _ = ops.gdn_prefill(gq, g["k"], g["v"], g["la"], beta=g["beta"])
+    assert torch.equal(want.cpu(), ys[0])
+
+
 @pytest.mark.parametrize("impl", ["auto"] + VARIANTS)
 def test_empty_inputs(impl):
     """T = 0: no token is read or written and S_T = S_0; B = 0: empty outputs."""
