@@ -315,3 +315,17 @@ def test_split_equals_cluster_bitwise(T, s0, out_dtype):
     assert torch.equal(out["chunk_cluster"][0], out["chunk_split"][0])
     assert torch.equal(out["chunk_cluster"][1], out["chunk_split"][1])
     assert ops.device_status() == 0
+
+
+def test_split_selected_for_more_sequences_than_clusters():
+    """More sequences than two-CTA clusters fit at once (configuration 4's prefill: B=16, H=8): AUTO runs
+    the split path, one state-only CTA per sequence in one wave, with the cluster kernel's bits."""
+    B, T, H = 16, 200, 8
+    g = make_inputs(B, T, H, 128, 128, seed=77, dtype=torch.bfloat16, device="cuda")
+    assert ops.selected_impl(g["q"], g["k"], g["v"], g["la"], beta=g["beta"]) == "chunk_split"
+    y_a, S_a = ops.gdn_prefill(g["q"], g["k"], g["v"], g["la"], beta=g["beta"], output_final_state=True)
+    y_c, S_c = ops.gdn_prefill(g["q"], g["k"], g["v"], g["la"], beta=g["beta"], output_final_state=True,
+                               impl="chunk_cluster")
+    torch.cuda.synchronize()
+    assert torch.equal(y_a, y_c) and torch.equal(S_a, S_c)
+    assert ops.device_status() == 0
