@@ -31,20 +31,25 @@ constexpr long long WAIT_LIMIT = 4000000000LL;  // ~2 s of SM clocks
 constexpr uint32_t PS_BYTES = 3 * TILE;         // [A16][T16][TG16]
 
 // Shared-memory map (bytes from a 1024-aligned base).  The staged products reuse the tile
-// buffer once the G MMA, its only reader, has completed.
+// buffer once the G MMA, its only reader, has completed.  With u tiles (OVERLAY) the buffer is
+// 48 KB: the fp16 L matrix, the diagonal blocks and the decay tables then take its last 24 KB too
+// (the tables computed after the MMA), which keeps a CTA at ~50 KB and four of them on an SM.
 template <bool HAS_U>
 struct Map {
+  static constexpr bool OVERLAY = HAS_U;
   static constexpr uint32_t KQ = 0;                                  // [K0][Q0][K1][Q1] (+ [U0][U1])
   static constexpr uint32_t KQ_BYTES = (HAS_U ? 6 : 4) * TILE;
   static constexpr uint32_t ST = 0;                                  // staged [A16][T16][TG16]
-  static constexpr uint32_t L16 = KQ + KQ_BYTES;                     // 64 rows x LD16 bytes
+  static constexpr uint32_t L16 = OVERLAY ? ST + PS_BYTES : KQ + KQ_BYTES;  // 64 rows x LD16 bytes
   static constexpr uint32_t LDIAG = L16 + 64 * LD16;                 // 4 x 16 x LDG floats
   static constexpr uint32_t EXPT = LDIAG + 4 * 16 * LDG * 4;         // 64 + 4x64 + 4x16x20 floats
-  static constexpr uint32_t GS = EXPT + (64 + 4 * 64 + 4 * 16 * 20) * 4;  // beta[64], g[64], gamma[64]
+  static constexpr uint32_t EXPT_END = EXPT + (64 + 4 * 64 + 4 * 16 * 20) * 4;
+  static constexpr uint32_t GS = OVERLAY ? KQ + KQ_BYTES : EXPT_END;  // beta[64], g[64], gamma[64]
   static constexpr uint32_t BARS = GS + 3 * C * 4;                   // 2 mbarriers, TMEM slot, abort flag
   static constexpr uint32_t TOTAL = BARS + 32;
   static constexpr uint32_t DYN = TOTAL + 1024;
   static_assert(KQ_BYTES >= PS_BYTES, "staging fits in the tile buffer");
+  static_assert(!OVERLAY || EXPT_END <= KQ + KQ_BYTES, "the overlaid tables fit in the tile buffer");
   static_assert(L16 % 16 == 0 && BARS % 8 == 0, "alignment");
 };
 
@@ -192,22 +197,26 @@ __global__ void __launch_bounds__(NT)
       break;
     }
     // Decay tables: 1,344 exponentials per chunk instead of one per (t, j) pair; every factor is exp
-    // of a non-positive number, so none overflows whatever the decay.
+    // of a non-positive number, so none overflows whatever the decay.  Computed while the G MMA
+    // runs, or after it where they overlay the tile buffer it reads.
+    auto tables = [&]() {
 #pragma unroll 1
-    for (int e = tid; e < 5 * C; e += NT) {
-      if (e < C) {
-        eT[e] = __expf(g_s[e] - g_s[e & ~15]);
-      } else {
-        const int bb = (e - C) >> 6, j = (e - C) & 63;
-        eJ[bb * C + j] = (bb > 0 && j < 16 * bb) ? beta_s[j] * __expf(g_s[16 * bb] - g_s[j]) : 0.f;
+      for (int e = tid; e < 5 * C; e += NT) {
+        if (e < C) {
+          eT[e] = __expf(g_s[e] - g_s[e & ~15]);
+        } else {
+          const int bb = (e - C) >> 6, j = (e - C) & 63;
+          eJ[bb * C + j] = (bb > 0 && j < 16 * bb) ? beta_s[j] * __expf(g_s[16 * bb] - g_s[j]) : 0.f;
+        }
       }
-    }
 #pragma unroll 1
-    for (int n = 0; n < 8; ++n) {
-      const int e = tid + NT * n;  // 1024 diagonal-block entries
-      const int bb = e >> 8, r = (e >> 4) & 15, cc = e & 15;
-      Ed[(bb * 16 + r) * 20 + cc] = cc <= r ? beta_s[16 * bb + cc] * __expf(g_s[16 * bb + r] - g_s[16 * bb + cc]) : 0.f;
-    }
+      for (int n = 0; n < 8; ++n) {
+        const int e = tid + NT * n;  // 1024 diagonal-block entries
+        const int bb = e >> 8, r = (e >> 4) & 15, cc = e & 15;
+        Ed[(bb * 16 + r) * 20 + cc] = cc <= r ? beta_s[16 * bb + cc] * __expf(g_s[16 * bb + r] - g_s[16 * bb + cc]) : 0.f;
+      }
+    };
+    if (!M::OVERLAY) tables();
     if (tid == 0) fail = !ptx::mbar_wait_abortable(&bars[1], ph, WAIT_LIMIT, abort_flag);
     if (ptx::named_bar_or(1, NT, fail)) {  // the MMA did not complete: drain it before TMEM is freed
       if (tid == 0) {
@@ -215,6 +224,10 @@ __global__ void __launch_bounds__(NT)
         atomicExch(&g_status, GDN_ERR_TIMEOUT);
       }
       break;
+    }
+    if (M::OVERLAY) {
+      tables();
+      __syncthreads();
     }
     ptx::tc_fence_after();
     // Row tid of G: rows 0-63 give L (strictly lower), rows 64-127 give A (lower with diagonal), one
