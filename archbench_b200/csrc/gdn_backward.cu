@@ -35,6 +35,7 @@
 #include <math.h>
 
 #include "gdn_common.cuh"
+#include "gdn_tiles.cuh"
 #include "sm100_ptx.cuh"
 
 namespace gdn {
@@ -56,6 +57,7 @@ struct Params {
   int64_t sq_b, sq_t, sq_h, sk_b, sk_t, sk_h, su_b, su_t, su_h, sv_b, sv_t, sv_h, sd_b, sd_t, sd_h;
   int T, H, NC, BH;
   int DVt, vofs, accum;  // total DV; first state row of this 128-row slice; add dq/dk/du/dla/dbeta to the outputs
+  int pf;                 // prep: chunks between a block and the one whose tiles it prefetches into L2 (0: none)
   __half *wT, *wA, *wW, *wUw, *wS, *wdS;  // per chunk: T, A (C x C), W, Uw (C x D), S0, dS1 (D x D)
   __half *wU, *wDU, *wdY, *wdR0;         // per chunk: U, d U, scaled dY, A^T dY (C x D)
   __half* wPc;                            // per chunk: dY^T Gamma Q (D x D)
@@ -352,18 +354,51 @@ __global__ void __launch_bounds__(NTHR) prep_kernel(Params p) {
   __half* sV = sQ + TILE_CD;
   __half* sGK = sV + TILE_CD;
   __half* sT = sGK + TILE_CD;
-  float* sL = reinterpret_cast<float*>(sT + TILE_CC);  // C x (C + 1): L below the diagonal, block scratch above
+  float* sL = reinterpret_cast<float*>(sT + TILE_CC);  // C x (C + 1) floats: L in fp16 and its diagonal blocks in fp32
   float* sg = sL + C * (C + 1);
   float* sgam = sg + C;
   float* sd = sgam + C;
   float* sbeta = sd + C;
-  float* sTf = reinterpret_cast<float*>(sK);
-  constexpr int LL = C + 1;
+  __half* sL16 = reinterpret_cast<__half*>(sL);                                           // C rows of LD16 bytes
+  float* sLd = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(sL) + C * tiles::LD16);  // 4 x 16 x LDG
+  static_assert(C * tiles::LD16 + 4 * 16 * tiles::LDG * 4 <= C * (C + 1) * 4, "L16 and its diagonal blocks fit");
+  static_assert(LDC * 2 == tiles::LD16, "T rows as the block merges address them");
 
   const int task = blockIdx.x, bh = task / p.NC, c = task - bh * p.NC;
   const int b = bh / p.H, h = bh - b * p.H;
   const int t0 = c * C, nvalid = min(C, p.T - t0);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  // This chunk's q, k, (u,) v and dY tiles in flight first, under the gate scan below.
+  RawTile<TI> rk, rq, rv, ru;
+  RawTile<TD> rd;
+  raw_load(rk, tok<TI>(p.k, p.sk_b, p.sk_t, p.sk_h, b, t0, h), p.sk_t, nvalid);
+  raw_load(rq, tok<TI>(p.q, p.sq_b, p.sq_t, p.sq_h, b, t0, h), p.sq_t, nvalid);
+  raw_load(rv, tok<TI>(p.v, p.sv_b, p.sv_t, p.sv_h, b, t0, h), p.sv_t, nvalid);
+  raw_load(rd, tok<TD>(p.dy, p.sd_b, p.sd_t, p.sd_h, b, t0, h), p.sd_t, nvalid);
+  if (p.u) raw_load(ru, tok<TI>(p.u, p.su_b, p.su_t, p.su_h, b, t0, h), p.su_t, nvalid);
+  // The tiles of the chunk p.pf blocks on (one resident wave: its block starts about when this one
+  // ends) into L2, so that its loads do not wait on HBM.
+  if (p.pf > 0 && (int64_t)task + p.pf < (int64_t)p.NC * p.BH) {
+    const int nt = task + p.pf, nbh = nt / p.NC, nc = nt - nbh * p.NC;
+    const int nb = nbh / p.H, nh = nbh - nb * p.H, n0 = nc * C, nv = min(C, p.T - n0);
+    for (int e = tid; e < (p.u ? 5 : 4) * C; e += NTHR) {
+      const int which = e / C, r = e - which * C;
+      if (r >= nv) continue;
+      const char* row;
+      int bytes = D * (int)sizeof(TI);
+      switch (which) {
+        case 0: row = reinterpret_cast<const char*>(tok<TI>(p.k, p.sk_b, p.sk_t, p.sk_h, nb, n0 + r, nh)); break;
+        case 1: row = reinterpret_cast<const char*>(tok<TI>(p.q, p.sq_b, p.sq_t, p.sq_h, nb, n0 + r, nh)); break;
+        case 2: row = reinterpret_cast<const char*>(tok<TI>(p.v, p.sv_b, p.sv_t, p.sv_h, nb, n0 + r, nh)); break;
+        case 3:
+          row = reinterpret_cast<const char*>(tok<TD>(p.dy, p.sd_b, p.sd_t, p.sd_h, nb, n0 + r, nh));
+          bytes = D * (int)sizeof(TD);
+          break;
+        default: row = reinterpret_cast<const char*>(tok<TI>(p.u, p.su_b, p.su_t, p.su_h, nb, n0 + r, nh)); break;
+      }
+      for (int o = 0; o < bytes; o += 128) ptx::prefetch_l2(row + o);
+    }
+  }
   const float scale = grad_scale(p.amax[bh]);
   if (c == 0 && tid == 0) p.scale[bh] = scale;
 
@@ -389,18 +424,10 @@ __global__ void __launch_bounds__(NTHR) prep_kernel(Params p) {
   __syncthreads();
 
   {
-    // k, q, v and dY loads all in flight at once; k feeds three tiles (K, beta K = U, Gamma K)
-    RawTile<TI> rk, rq, rv;
-    RawTile<TD> rd;
-    raw_load(rk, tok<TI>(p.k, p.sk_b, p.sk_t, p.sk_h, b, t0, h), p.sk_t, nvalid);
-    raw_load(rq, tok<TI>(p.q, p.sq_b, p.sq_t, p.sq_h, b, t0, h), p.sq_t, nvalid);
-    raw_load(rv, tok<TI>(p.v, p.sv_b, p.sv_t, p.sv_h, b, t0, h), p.sv_t, nvalid);
-    raw_load(rd, tok<TD>(p.dy, p.sd_b, p.sd_t, p.sd_h, b, t0, h), p.sd_t, nvalid);
+    // k feeds three tiles (K, beta K = U, Gamma K)
     raw_store(sK, rk, nullptr, 1.f);
     raw_store(sGK, rk, sgam, 1.f);
     if (p.u) {
-      RawTile<TI> ru;
-      raw_load(ru, tok<TI>(p.u, p.su_b, p.su_t, p.su_h, b, t0, h), p.su_t, nvalid);
       raw_store(sU, ru, nullptr, 1.f);
     } else {
       raw_store(sU, rk, sbeta, 1.f);
@@ -447,68 +474,61 @@ __global__ void __launch_bounds__(NTHR) prep_kernel(Params p) {
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
         const int row = m0 + g + 8 * hf, col = n0 + 8 * nt + 2 * t4;
-        float e[2], a[2];
+        float e[2], a[2], l[2];
 #pragma unroll
         for (int x = 0; x < 2; ++x) {
           const int cc = col + x;
           e[x] = cc <= row ? __expf(sg[row] - sg[cc]) : 0.f;
-          sL[row * LL + cc] = cc < row ? accM[0][nt][2 * hf + x] * e[x] : 0.f;
+          l[x] = cc < row ? accM[0][nt][2 * hf + x] * e[x] : 0.f;
           a[x] = accP[0][nt][2 * hf + x] * e[x];
         }
+        *reinterpret_cast<uint32_t*>(sL16 + row * (tiles::LD16 / 2) + col) = h2u(l[0], l[1]);
+        if ((row >> 4) == (col >> 4))  // the diagonal blocks also in fp32, for the substitution
+          *reinterpret_cast<float2*>(sLd + row * tiles::LDG + (col & 15)) = make_float2(l[0], l[1]);
         *reinterpret_cast<uint32_t*>(Aout + row * C + col) = h2u(a[0], a[1]);
       }
   }
-  __syncthreads();  // L complete; K no longer needed (its space holds T from here on)
+  __syncthreads();  // L complete
 
-  // T = (I + L)^-1 in 16 x 16 blocks, fp32.  Diagonal blocks by forward substitution (one column of one
-  // block per thread); then for block distance d = 1..3: X_ij = sum_{k=j}^{i-1} L_ik T_kj (kept in the
-  // unused upper block (j, i) of sL) and T_ij = -T_ii X_ij.
+  // T = (I + L)^-1: the diagonal blocks D_b = (I + L_bb)^-1 by fp32 forward substitution (one column
+  // per thread) into L16's diagonal blocks, then block column J of T on warp J by mma.sync merges of
+  // the fp16 blocks, T_iJ = -D_i sum_{k=J}^{i-1} L_ik T_kJ (tiles::merge_column_core).
   if (tid < C) {
-    const int blk = tid >> 4, col = tid & 15, o = 16 * blk;
-    float x[16];
+    const int bb = tid >> 4, j = tid & 15;
+    const float* Lb = sLd + bb * 16 * tiles::LDG;
+    float x[16], acc[16];
 #pragma unroll
-    for (int r = 0; r < 16; ++r) {
-      float acc = (r == col) ? 1.f : 0.f;
+    for (int r = 0; r < 16; ++r) acc[r] = 0.f;
 #pragma unroll
-      for (int q = 0; q < r; ++q) acc -= sL[(o + r) * LL + o + q] * x[q];
-      x[r] = r < col ? 0.f : acc;
-      sTf[(o + r) * LL + o + col] = x[r];
+    for (int m = 0; m < 16; ++m) {
+      x[m] = (m == j) ? 1.f : (m > j ? -acc[m] : 0.f);
+#pragma unroll
+      for (int r = m + 1; r < 16; ++r) acc[r] = fmaf(Lb[r * tiles::LDG + m], x[m], acc[r]);
     }
-  }
-  for (int e = tid; e < 6 * 256; e += NTHR) {  // blocks above the diagonal are zero
-    const int pr = e >> 8, r = (e >> 4) & 15, cc = e & 15;
-    const int bi = pr < 3 ? 0 : (pr < 5 ? 1 : 2), bj = pr < 3 ? pr + 1 : (pr < 5 ? pr - 1 : 3);
-    sTf[(16 * bi + r) * LL + 16 * bj + cc] = 0.f;
+#pragma unroll
+    for (int r = 0; r < 16; ++r) sL16[(bb * 16 + r) * (tiles::LD16 / 2) + bb * 16 + j] = __float2half_rn(x[r]);
   }
   __syncthreads();
-#pragma unroll 1
-  for (int d = 1; d < 4; ++d) {
-    for (int e = tid; e < (4 - d) * 256; e += NTHR) {
-      const int j = e >> 8, i = j + d, r = (e >> 4) & 15, cc = e & 15;
-      float acc = 0.f;
-      for (int k = 16 * j; k < 16 * i; ++k) acc += sL[(16 * i + r) * LL + k] * sTf[k * LL + 16 * j + cc];
-      sL[(16 * j + r) * LL + 16 * i + cc] = acc;
-    }
-    __syncthreads();
-    for (int e = tid; e < (4 - d) * 256; e += NTHR) {
-      const int j = e >> 8, i = j + d, r = (e >> 4) & 15, cc = e & 15;
-      float acc = 0.f;
-#pragma unroll
-      for (int q = 0; q < 16; ++q) acc -= sTf[(16 * i + r) * LL + 16 * i + q] * sL[(16 * j + q) * LL + 16 * i + cc];
-      sTf[(16 * i + r) * LL + 16 * j + cc] = acc;
-    }
-    __syncthreads();
+  if (warp < 4) {
+    const uint32_t tT = ptx::smem_u32(sT);
+    auto emit = [&](int i, const float (&f)[8]) {
+      const uint32_t v[4] = {h2u(f[0], f[1]), h2u(f[2], f[3]), h2u(f[4], f[5]), h2u(f[6], f[7])};
+      ptx::stsm_x4_t(tiles::frag_addr_plain(tT, LDC * 2, 16 * i, 16 * warp, lane), v);
+    };
+    auto zero = [&](int i) {
+      const uint32_t z[4] = {0u, 0u, 0u, 0u};
+      ptx::stsm_x4_t(tiles::frag_addr_plain(tT, LDC * 2, 16 * i, 16 * warp, lane), z);
+    };
+    tiles::merge_column_core(warp, ptx::smem_u32(sL16), lane, emit, zero);
   }
+  __syncthreads();
   {
     __half* Tout = p.wT + (int64_t)task * C * C;
-    for (int i = tid; i < C * C / 2; i += NTHR) {
-      const int row = i / (C / 2), col = 2 * (i - row * (C / 2));
-      const uint32_t x = h2u(sTf[row * LL + col], sTf[row * LL + col + 1]);
-      *reinterpret_cast<uint32_t*>(sT + row * LDC + col) = x;
-      *reinterpret_cast<uint32_t*>(Tout + row * C + col) = x;
+    for (int i = tid; i < C * C / 8; i += NTHR) {
+      const int row = i >> 3, seg = i & 7;
+      *reinterpret_cast<uint4*>(Tout + row * C + seg * 8) = *reinterpret_cast<const uint4*>(sT + row * LDC + seg * 8);
     }
   }
-  __syncthreads();
 
   // W = T (Gamma K), Uw = T V -> workspace (fp16)
   {
@@ -527,7 +547,7 @@ __global__ void __launch_bounds__(NTHR) prep_kernel(Params p) {
       }
     }
   }
-  __syncthreads();  // Gamma K, T's fp32 copy and L are no longer read
+  __syncthreads();  // Gamma K, T and L are no longer read
 
   // The backward chain's dS-independent terms, once per chunk here instead of on the chain:
   // dR0 = A^T dY (C x DV) and Pc = dY^T Gamma Q (DV x DK).  Gamma Q is built in K's space, dY (scaled, as
@@ -1136,9 +1156,16 @@ int launch(const Params& p, cudaStream_t s) {
                            {(const void*)local_kernel<TI, TD>, (int)LOCAL_SMEM}}))
     return GDN_ERR_LAUNCH;
   const int64_t nch = (int64_t)p.NC * p.BH;
+  Params pp = p;  // the prep blocks prefetch one resident wave ahead
+  int dev = 0, sms = 0, per_sm = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess &&
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, prep_kernel<TI, TD>, NTHR, PREP_SMEM) == cudaSuccess)
+    pp.pf = sms * per_sm;
+  else
+    pp.pf = 0;
   if (cudaMemsetAsync(p.amax, 0, (size_t)p.BH * 4, s) != cudaSuccess) return GDN_ERR_LAUNCH;
   amax_kernel<TD><<<(unsigned)nch, NTHR, 0, s>>>(p);
-  prep_kernel<TI, TD><<<(unsigned)nch, NTHR, PREP_SMEM, s>>>(p);
+  prep_kernel<TI, TD><<<(unsigned)nch, NTHR, PREP_SMEM, s>>>(pp);
   chain_kernel<<<(unsigned)(2 * p.BH), NTHR, CHAIN_SMEM, s>>>(p);
   local_kernel<TI, TD><<<(unsigned)nch, NTHR, LOCAL_SMEM, s>>>(p);
   return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
@@ -1207,7 +1234,7 @@ int gdn_prefill_bwd(const gdn_backward_args* a, void* stream) {
   if (((uintptr_t)a->workspace & 255u) != 0) return GDN_ERR_ALIGN;
   if (NC * BH > 0x7fffffffLL) return GDN_ERR_SHAPE;
   uint8_t* ws = reinterpret_cast<uint8_t*>(a->workspace);
-  Params p;
+  Params p{};
   p.q = a->q; p.k = a->k; p.u = a->u; p.v = a->v; p.dy = a->dy;
   p.beta = a->u ? nullptr : a->beta; p.la = a->la; p.s0 = a->s0; p.dsT = a->ds_T;
   p.dq = a->dq; p.dk = a->dk; p.du = a->du; p.dv = a->dv; p.dbeta = a->dbeta; p.dla = a->dla; p.ds0 = a->ds0;

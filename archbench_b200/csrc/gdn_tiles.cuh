@@ -146,35 +146,14 @@ __device__ __forceinline__ void merge_column_of(int J, uint32_t l16, uint32_t th
   }
 }
 
-// merge_column for a block column J known only at run time (warp-uniform): one code path for all
-// four columns, so that the warps merging different columns share their instructions (a smaller
-// instruction working set than four specialised copies).  Same results as merge_column<J>.
-template <bool SPLIT>
-__device__ __forceinline__ void merge_column_any(int J, uint32_t l16, uint32_t thi, uint32_t tlo, uint32_t tg16,
-                                                 const float* gam, int lane) {
-  const int g = lane >> 2;
-  const float g0 = gam[16 * J + g], g8 = gam[16 * J + g + 8];
+// Block column J of T = (I + L)^-1 for a J known only at run time (warp-uniform): one code path for
+// all four columns, so that the warps merging different columns share their instructions (a smaller
+// instruction working set than four specialised copies).  Same arithmetic as merge_column<J>; the
+// output is left to the caller: emit(i, f) receives block (i, J) of T as an fp32 fragment of T^T in
+// A-fragment order (for stmatrix .trans), zero(i) is called for the blocks i < J above the diagonal.
+template <typename Emit, typename Zero>
+__device__ __forceinline__ void merge_column_core(int J, uint32_t l16, int lane, Emit&& emit, Zero&& zero) {
   uint32_t X[4][4];
-  auto emit = [&](int i, const float (&f)[8]) {
-    uint32_t hi[4], lo[4], gs[4];
-#pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      const float a = f[2 * r], b = f[2 * r + 1];
-      if constexpr (SPLIT) {
-        const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-        const float2 hf = __bfloat1622float2(h);
-        hi[r] = *reinterpret_cast<const uint32_t*>(&h);
-        lo[r] = pack_bf2(a - hf.x, b - hf.y);
-      } else {
-        hi[r] = pack_h2(a, b);
-      }
-      const float sc = (r & 1) ? g8 : g0;
-      gs[r] = pack_h2(a * sc, b * sc);
-    }
-    ptx::stsm_x4_t(frag_addr_sw(thi, 16 * i, 16 * J, lane), hi);
-    if constexpr (SPLIT) ptx::stsm_x4_t(frag_addr_sw(tlo, 16 * i, 16 * J, lane), lo);
-    ptx::stsm_x4_t(frag_addr_sw(tg16, 16 * i, 16 * J, lane), gs);
-  };
   // Diagonal block D_J (held transposed in the fragments).
   uint32_t xd[4];
   ptx::ldsm_x4_t(frag_addr_plain(l16, LD16, 16 * J, 16 * J, lane), xd);
@@ -192,13 +171,8 @@ __device__ __forceinline__ void merge_column_any(int J, uint32_t l16, uint32_t t
     }
     emit(J, f);
   }
-  const uint32_t z[4] = {0u, 0u, 0u, 0u};
 #pragma unroll 1
-  for (int i = 0; i < J; ++i) {  // blocks above the diagonal
-    ptx::stsm_x4_t(frag_addr_sw(thi, 16 * i, 16 * J, lane), z);
-    if constexpr (SPLIT) ptx::stsm_x4_t(frag_addr_sw(tlo, 16 * i, 16 * J, lane), z);
-    ptx::stsm_x4_t(frag_addr_sw(tg16, 16 * i, 16 * J, lane), z);
-  }
+  for (int i = 0; i < J; ++i) zero(i);  // blocks above the diagonal
 #pragma unroll
   for (int i = 1; i < 4; ++i) {
     if (i <= J) continue;
@@ -223,6 +197,42 @@ __device__ __forceinline__ void merge_column_any(int J, uint32_t l16, uint32_t t
     X[i][3] = pack_h2(Tt[6], Tt[7]);
     emit(i, Tt);
   }
+}
+
+// merge_column<J, SPLIT> for a run-time J, through merge_column_core: block column J of T (and T_lo)
+// and of T Gamma into swizzled 64x64 tiles.
+template <bool SPLIT>
+__device__ __forceinline__ void merge_column_any(int J, uint32_t l16, uint32_t thi, uint32_t tlo, uint32_t tg16,
+                                                 const float* gam, int lane) {
+  const int g = lane >> 2;
+  const float g0 = gam[16 * J + g], g8 = gam[16 * J + g + 8];
+  auto emit = [&](int i, const float (&f)[8]) {
+    uint32_t hi[4], lo[4], gs[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const float a = f[2 * r], b = f[2 * r + 1];
+      if constexpr (SPLIT) {
+        const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+        const float2 hf = __bfloat1622float2(h);
+        hi[r] = *reinterpret_cast<const uint32_t*>(&h);
+        lo[r] = pack_bf2(a - hf.x, b - hf.y);
+      } else {
+        hi[r] = pack_h2(a, b);
+      }
+      const float sc = (r & 1) ? g8 : g0;
+      gs[r] = pack_h2(a * sc, b * sc);
+    }
+    ptx::stsm_x4_t(frag_addr_sw(thi, 16 * i, 16 * J, lane), hi);
+    if constexpr (SPLIT) ptx::stsm_x4_t(frag_addr_sw(tlo, 16 * i, 16 * J, lane), lo);
+    ptx::stsm_x4_t(frag_addr_sw(tg16, 16 * i, 16 * J, lane), gs);
+  };
+  auto zero = [&](int i) {
+    const uint32_t z[4] = {0u, 0u, 0u, 0u};
+    ptx::stsm_x4_t(frag_addr_sw(thi, 16 * i, 16 * J, lane), z);
+    if constexpr (SPLIT) ptx::stsm_x4_t(frag_addr_sw(tlo, 16 * i, 16 * J, lane), z);
+    ptx::stsm_x4_t(frag_addr_sw(tg16, 16 * i, 16 * J, lane), z);
+  };
+  merge_column_core(J, l16, lane, emit, zero);
 }
 
 // ---- host: tensor maps ---------------------------------------------------------------------
