@@ -298,6 +298,39 @@ __device__ __forceinline__ const TI* tok(const void* base, int64_t sb, int64_t s
   return reinterpret_cast<const TI*>(base) + (int64_t)b * sb + (int64_t)t * st + (int64_t)h * sh;
 }
 
+// Every 128-byte line of [ptr, ptr + bytes) into L2, spread over the block's threads.
+__device__ __forceinline__ void prefetch_span(const void* ptr, int64_t bytes) {
+  const char* c = reinterpret_cast<const char*>(ptr);
+  for (int64_t o = (int64_t)threadIdx.x * 128; o < bytes; o += (int64_t)NTHR * 128) ptx::prefetch_l2(c + o);
+}
+
+// The k, q and v rows of chunk `task` (and dY's, and u's when asked) into L2, one row per thread.
+template <typename TI, typename TD>
+__device__ __forceinline__ void prefetch_rows(const Params& p, int task, bool with_dy, bool with_u) {
+  const int bh = task / p.NC, c = task - bh * p.NC;
+  const int b = bh / p.H, h = bh - b * p.H, t0 = c * C, nv = min(C, p.T - t0);
+  const int ntens = 3 + (int)with_dy + (int)with_u;
+  for (int e = threadIdx.x; e < ntens * C; e += NTHR) {
+    int which = e / C;
+    const int r = e - which * C;
+    if (r >= nv) continue;
+    if (which == 3 && !with_dy) which = 4;
+    const char* row;
+    int bytes = D * (int)sizeof(TI);
+    switch (which) {
+      case 0: row = reinterpret_cast<const char*>(tok<TI>(p.k, p.sk_b, p.sk_t, p.sk_h, b, t0 + r, h)); break;
+      case 1: row = reinterpret_cast<const char*>(tok<TI>(p.q, p.sq_b, p.sq_t, p.sq_h, b, t0 + r, h)); break;
+      case 2: row = reinterpret_cast<const char*>(tok<TI>(p.v, p.sv_b, p.sv_t, p.sv_h, b, t0 + r, h)); break;
+      case 3:
+        row = reinterpret_cast<const char*>(tok<TD>(p.dy, p.sd_b, p.sd_t, p.sd_h, b, t0 + r, h));
+        bytes = D * (int)sizeof(TD);
+        break;
+      default: row = reinterpret_cast<const char*>(tok<TI>(p.u, p.su_b, p.su_t, p.su_h, b, t0 + r, h)); break;
+    }
+    for (int o = 0; o < bytes; o += 128) ptx::prefetch_l2(row + o);
+  }
+}
+
 // Power of two that brings max |dY|, max |dS_T| of one (b, h) into [0.5, 1) (1 when they are 0).
 __device__ __forceinline__ float grad_scale(unsigned bits) {
   const float a = __uint_as_float(bits);
@@ -378,27 +411,7 @@ __global__ void __launch_bounds__(NTHR) prep_kernel(Params p) {
   if (p.u) raw_load(ru, tok<TI>(p.u, p.su_b, p.su_t, p.su_h, b, t0, h), p.su_t, nvalid);
   // The tiles of the chunk p.pf blocks on (one resident wave: its block starts about when this one
   // ends) into L2, so that its loads do not wait on HBM.
-  if (p.pf > 0 && (int64_t)task + p.pf < (int64_t)p.NC * p.BH) {
-    const int nt = task + p.pf, nbh = nt / p.NC, nc = nt - nbh * p.NC;
-    const int nb = nbh / p.H, nh = nbh - nb * p.H, n0 = nc * C, nv = min(C, p.T - n0);
-    for (int e = tid; e < (p.u ? 5 : 4) * C; e += NTHR) {
-      const int which = e / C, r = e - which * C;
-      if (r >= nv) continue;
-      const char* row;
-      int bytes = D * (int)sizeof(TI);
-      switch (which) {
-        case 0: row = reinterpret_cast<const char*>(tok<TI>(p.k, p.sk_b, p.sk_t, p.sk_h, nb, n0 + r, nh)); break;
-        case 1: row = reinterpret_cast<const char*>(tok<TI>(p.q, p.sq_b, p.sq_t, p.sq_h, nb, n0 + r, nh)); break;
-        case 2: row = reinterpret_cast<const char*>(tok<TI>(p.v, p.sv_b, p.sv_t, p.sv_h, nb, n0 + r, nh)); break;
-        case 3:
-          row = reinterpret_cast<const char*>(tok<TD>(p.dy, p.sd_b, p.sd_t, p.sd_h, nb, n0 + r, nh));
-          bytes = D * (int)sizeof(TD);
-          break;
-        default: row = reinterpret_cast<const char*>(tok<TI>(p.u, p.su_b, p.su_t, p.su_h, nb, n0 + r, nh)); break;
-      }
-      for (int o = 0; o < bytes; o += 128) ptx::prefetch_l2(row + o);
-    }
-  }
+  if (p.pf > 0 && (int64_t)task + p.pf < (int64_t)p.NC * p.BH) prefetch_rows<TI, TD>(p, task + p.pf, true, p.u != nullptr);
   const float scale = grad_scale(p.amax[bh]);
   if (c == 0 && tid == 0) p.scale[bh] = scale;
 
@@ -829,6 +842,19 @@ __global__ void __launch_bounds__(NTHR, 1) local_kernel(Params p) {
     raw_load(rq, tok<TI>(p.q, p.sq_b, p.sq_t, p.sq_h, b, t0, h), p.sq_t, nvalid);
     raw_load(rk, tok<TI>(p.k, p.sk_b, p.sk_t, p.sk_h, b, t0, h), p.sk_t, nvalid);
     raw_load(rv, tok<TI>(p.v, p.sv_b, p.sv_t, p.sv_h, b, t0, h), p.sv_t, nvalid);
+    // One block per SM loads its chunk and then computes with the SM's loads idle: the chunk one
+    // resident wave on (its block starts about when this one ends) goes into L2 meanwhile.
+    if (p.pf > 0 && (int64_t)task + p.pf < (int64_t)p.NC * p.BH) {
+      const int64_t nt = task + p.pf, oc = nt * C * D;
+      prefetch_span(p.wU + oc, C * D * 2);
+      prefetch_span(p.wdY + oc, C * D * 2);
+      prefetch_span(p.wW + oc, C * D * 2);
+      prefetch_span(p.wT + nt * C * C, C * C * 2);
+      prefetch_span(p.wA + nt * C * C, C * C * 2);
+      prefetch_span(p.wS + nt * D * D, D * D * 2);
+      prefetch_span(p.wdS + nt * D * D, D * D * 2);
+      prefetch_rows<TI, TD>(p, (int)nt, false, false);
+    }
     raw_store(sQ, rq, nullptr, 1.f);
     raw_store(sK, rk, nullptr, 1.f);
     raw_store(sV, rv, nullptr, 1.f);
@@ -1156,18 +1182,20 @@ int launch(const Params& p, cudaStream_t s) {
                            {(const void*)local_kernel<TI, TD>, (int)LOCAL_SMEM}}))
     return GDN_ERR_LAUNCH;
   const int64_t nch = (int64_t)p.NC * p.BH;
-  Params pp = p;  // the prep blocks prefetch one resident wave ahead
+  // The prep and local blocks prefetch the chunk one resident wave ahead (0: no prefetch).
+  Params pp = p, pl = p;
   int dev = 0, sms = 0, per_sm = 0;
-  if (cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess &&
-      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, prep_kernel<TI, TD>, NTHR, PREP_SMEM) == cudaSuccess)
-    pp.pf = sms * per_sm;
-  else
-    pp.pf = 0;
+  const bool have_sms =
+      cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess;
+  pp.pf = have_sms && cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, prep_kernel<TI, TD>, NTHR, PREP_SMEM) == cudaSuccess
+              ? sms * per_sm : 0;
+  pl.pf = have_sms && cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, local_kernel<TI, TD>, NTHR, LOCAL_SMEM) == cudaSuccess
+              ? sms * per_sm : 0;
   if (cudaMemsetAsync(p.amax, 0, (size_t)p.BH * 4, s) != cudaSuccess) return GDN_ERR_LAUNCH;
   amax_kernel<TD><<<(unsigned)nch, NTHR, 0, s>>>(p);
   prep_kernel<TI, TD><<<(unsigned)nch, NTHR, PREP_SMEM, s>>>(pp);
   chain_kernel<<<(unsigned)(2 * p.BH), NTHR, CHAIN_SMEM, s>>>(p);
-  local_kernel<TI, TD><<<(unsigned)nch, NTHR, LOCAL_SMEM, s>>>(p);
+  local_kernel<TI, TD><<<(unsigned)nch, NTHR, LOCAL_SMEM, s>>>(pl);
   return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
 }
 
