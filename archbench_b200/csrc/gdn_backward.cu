@@ -1071,14 +1071,14 @@ __global__ void __launch_bounds__(NTHR, 1) local_kernel(Params p) {
   // are added to the previous slice's when the state has more than 128 rows
   const bool has_u = p.u != nullptr;
   float pa = 0.f, pb = 0.f;  // dbeta partials: dU . k
+  // A later slice adds its part with reduction stores (no load to wait on: a load of one output may
+  // not pass a store to another that could alias it, so read-add-write serialised on every load);
+  // one add per element per launch, after the first slice's store in stream order, so the sums are
+  // the same bits in the same order as a read-add-write.
   auto put = [&](float* dst, float x, float y) {
     float2* q2 = reinterpret_cast<float2*>(dst);
-    if (p.accum) {
-      const float2 o = *q2;
-      x += o.x;
-      y += o.y;
-    }
-    *q2 = make_float2(x, y);
+    if (p.accum) atomicAdd(q2, make_float2(x, y));
+    else *q2 = make_float2(x, y);
   };
 #pragma unroll
   for (int hf = 0; hf < 2; ++hf) {
@@ -1135,7 +1135,10 @@ __global__ void __launch_bounds__(NTHR, 1) local_kernel(Params p) {
     }
     dg0 += __shfl_sync(0xffffffffu, dg1, 0);
     const int64_t gi = ((int64_t)b * p.T + t0) * p.H + h;
-    auto put1 = [&](float* dst, float x) { *dst = p.accum ? *dst + x : x; };
+    auto put1 = [&](float* dst, float x) {
+      if (p.accum) atomicAdd(dst, x);
+      else *dst = x;
+    };
     if (lane < nvalid) put1(p.dla + gi + (int64_t)lane * p.H, inv * dg0);
     if (lane + 32 < nvalid) put1(p.dla + gi + (int64_t)(lane + 32) * p.H, inv * dg1);
     if (!has_u) {

@@ -105,8 +105,11 @@ def test_backward_fp32_inputs_and_dy():
     check_all(grads, want, "fp32 I/O")
 
 
-def test_backward_deterministic():
-    x, S0, dS, dy, u = case(1, 192, 2, seed=17)
+@pytest.mark.parametrize("DV,with_u", [(D, False), (2 * D, False), (2 * D, True)])
+def test_backward_deterministic(DV, with_u):
+    """Bitwise the same gradients on a second call, also when a later 128-row state slice adds its part
+    of dq, dk, du, dla and dbeta to the earlier slice's outputs."""
+    x, S0, dS, dy, u = case(1, 192, 2, seed=17, DV=DV, with_u=with_u)
     a, _ = run(x, S0, dS, dy, u)
     b, _ = run(x, S0, dS, dy, u)
     for n in a:
