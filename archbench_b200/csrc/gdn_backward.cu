@@ -304,17 +304,14 @@ __device__ __forceinline__ void prefetch_span(const void* ptr, int64_t bytes) {
   for (int64_t o = (int64_t)threadIdx.x * 128; o < bytes; o += (int64_t)NTHR * 128) ptx::prefetch_l2(c + o);
 }
 
-// The k, q and v rows of chunk `task` (and dY's, and u's when asked) into L2, one row per thread.
+// The q and v rows of chunk `task` (and k's, dY's and u's when asked) into L2, one row per thread.
 template <typename TI, typename TD>
-__device__ __forceinline__ void prefetch_rows(const Params& p, int task, bool with_dy, bool with_u) {
+__device__ __forceinline__ void prefetch_rows(const Params& p, int task, bool with_k, bool with_dy, bool with_u) {
   const int bh = task / p.NC, c = task - bh * p.NC;
   const int b = bh / p.H, h = bh - b * p.H, t0 = c * C, nv = min(C, p.T - t0);
-  const int ntens = 3 + (int)with_dy + (int)with_u;
-  for (int e = threadIdx.x; e < ntens * C; e += NTHR) {
-    int which = e / C;
-    const int r = e - which * C;
-    if (r >= nv) continue;
-    if (which == 3 && !with_dy) which = 4;
+  for (int e = threadIdx.x; e < 5 * C; e += NTHR) {
+    const int which = e / C, r = e - which * C;
+    if (r >= nv || (which == 0 && !with_k) || (which == 3 && !with_dy) || (which == 4 && !with_u)) continue;
     const char* row;
     int bytes = D * (int)sizeof(TI);
     switch (which) {
@@ -376,9 +373,12 @@ __global__ void __launch_bounds__(NTHR) amax_kernel(Params p) {
 }
 
 // ---- prep: per chunk g, T, A, W, Uw and the chains' fp16 operands U, d U, Gamma Q, scaled dY ---------------
+// REUSE (the state slices after the first of DV > 128): g, T, A, W, U and d U do not depend on the slice
+// and are in the workspace from the first slice's prep; only T V, the scaled dY, A^T dY and dY^T Gamma Q
+// are formed, from T and A read back.
 constexpr int PREP_SMEM = 5 * TILE_CD * 2 + TILE_CC * 2 + C * (C + 1) * 4 + 5 * C * 4 + 64;
 
-template <typename TI, typename TD>
+template <typename TI, typename TD, bool REUSE>
 __global__ void __launch_bounds__(NTHR) prep_kernel(Params p) {
   extern __shared__ __align__(128) uint8_t smem[];
   __half* sK = reinterpret_cast<__half*>(smem);  // later T in fp32 (C x (C + 1))
@@ -404,14 +404,15 @@ __global__ void __launch_bounds__(NTHR) prep_kernel(Params p) {
   // This chunk's q, k, (u,) v and dY tiles in flight first, under the gate scan below.
   RawTile<TI> rk, rq, rv, ru;
   RawTile<TD> rd;
-  raw_load(rk, tok<TI>(p.k, p.sk_b, p.sk_t, p.sk_h, b, t0, h), p.sk_t, nvalid);
+  if constexpr (!REUSE) raw_load(rk, tok<TI>(p.k, p.sk_b, p.sk_t, p.sk_h, b, t0, h), p.sk_t, nvalid);
   raw_load(rq, tok<TI>(p.q, p.sq_b, p.sq_t, p.sq_h, b, t0, h), p.sq_t, nvalid);
   raw_load(rv, tok<TI>(p.v, p.sv_b, p.sv_t, p.sv_h, b, t0, h), p.sv_t, nvalid);
   raw_load(rd, tok<TD>(p.dy, p.sd_b, p.sd_t, p.sd_h, b, t0, h), p.sd_t, nvalid);
-  if (p.u) raw_load(ru, tok<TI>(p.u, p.su_b, p.su_t, p.su_h, b, t0, h), p.su_t, nvalid);
+  if (!REUSE && p.u) raw_load(ru, tok<TI>(p.u, p.su_b, p.su_t, p.su_h, b, t0, h), p.su_t, nvalid);
   // The tiles of the chunk p.pf blocks on (one resident wave: its block starts about when this one
   // ends) into L2, so that its loads do not wait on HBM.
-  if (p.pf > 0 && (int64_t)task + p.pf < (int64_t)p.NC * p.BH) prefetch_rows<TI, TD>(p, task + p.pf, true, p.u != nullptr);
+  if (p.pf > 0 && (int64_t)task + p.pf < (int64_t)p.NC * p.BH)
+    prefetch_rows<TI, TD>(p, task + p.pf, !REUSE, true, !REUSE && p.u != nullptr);
   const float scale = grad_scale(p.amax[bh]);
   if (c == 0 && tid == 0) p.scale[bh] = scale;
 
@@ -432,18 +433,23 @@ __global__ void __launch_bounds__(NTHR) prep_kernel(Params p) {
   if (tid < C) {
     sgam[tid] = expf(sg[tid]);
     sd[tid] = expf(sg[C - 1] - sg[tid]);
-    p.wg[(int64_t)task * C + tid] = sg[tid];
+    if (!REUSE) p.wg[(int64_t)task * C + tid] = sg[tid];
   }
   __syncthreads();
 
   {
-    // k feeds three tiles (K, beta K = U, Gamma K)
-    raw_store(sK, rk, nullptr, 1.f);
-    raw_store(sGK, rk, sgam, 1.f);
-    if (p.u) {
-      raw_store(sU, ru, nullptr, 1.f);
+    if constexpr (REUSE) {
+      tile_async(sT, LDC, p.wT + (int64_t)task * C * C, C, C);
+      cp_commit();
     } else {
-      raw_store(sU, rk, sbeta, 1.f);
+      // k feeds three tiles (K, beta K = U, Gamma K)
+      raw_store(sK, rk, nullptr, 1.f);
+      raw_store(sGK, rk, sgam, 1.f);
+      if (p.u) {
+        raw_store(sU, ru, nullptr, 1.f);
+      } else {
+        raw_store(sU, rk, sbeta, 1.f);
+      }
     }
     raw_store(sQ, rq, nullptr, 1.f);
     raw_store(sV, rv, nullptr, 1.f);
@@ -473,73 +479,78 @@ __global__ void __launch_bounds__(NTHR) prep_kernel(Params p) {
   }
   __syncthreads();
 
-  // M = K U^T -> L (fp32, strictly lower); P = Q U^T -> A (fp16, lower incl. diagonal, to the workspace)
-  {
-    const int m0 = 16 * (warp & 3), n0 = 32 * (warp >> 2), g = lane >> 2, t4 = lane & 3;
-    float accM[1][4][4], accP[1][4][4];
-    zero(accM);
-    zero(accP);
-    mma_acc<1, 4, false, false, D>(accM, sK, LDT, m0, sU, LDT, n0, lane);
-    mma_acc<1, 4, false, false, D>(accP, sQ, LDT, m0, sU, LDT, n0, lane);
-    __half* Aout = p.wA + (int64_t)task * C * C;
-#pragma unroll
-    for (int nt = 0; nt < 4; ++nt)
-#pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        const int row = m0 + g + 8 * hf, col = n0 + 8 * nt + 2 * t4;
-        float e[2], a[2], l[2];
-#pragma unroll
-        for (int x = 0; x < 2; ++x) {
-          const int cc = col + x;
-          e[x] = cc <= row ? __expf(sg[row] - sg[cc]) : 0.f;
-          l[x] = cc < row ? accM[0][nt][2 * hf + x] * e[x] : 0.f;
-          a[x] = accP[0][nt][2 * hf + x] * e[x];
+  if constexpr (REUSE) {
+    cp_wait<0>();
+    __syncthreads();
+  } else {
+    // M = K U^T -> L (fp32, strictly lower); P = Q U^T -> A (fp16, lower incl. diagonal, to the workspace)
+    {
+      const int m0 = 16 * (warp & 3), n0 = 32 * (warp >> 2), g = lane >> 2, t4 = lane & 3;
+      float accM[1][4][4], accP[1][4][4];
+      zero(accM);
+      zero(accP);
+      mma_acc<1, 4, false, false, D>(accM, sK, LDT, m0, sU, LDT, n0, lane);
+      mma_acc<1, 4, false, false, D>(accP, sQ, LDT, m0, sU, LDT, n0, lane);
+      __half* Aout = p.wA + (int64_t)task * C * C;
+  #pragma unroll
+      for (int nt = 0; nt < 4; ++nt)
+  #pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          const int row = m0 + g + 8 * hf, col = n0 + 8 * nt + 2 * t4;
+          float e[2], a[2], l[2];
+  #pragma unroll
+          for (int x = 0; x < 2; ++x) {
+            const int cc = col + x;
+            e[x] = cc <= row ? __expf(sg[row] - sg[cc]) : 0.f;
+            l[x] = cc < row ? accM[0][nt][2 * hf + x] * e[x] : 0.f;
+            a[x] = accP[0][nt][2 * hf + x] * e[x];
+          }
+          *reinterpret_cast<uint32_t*>(sL16 + row * (tiles::LD16 / 2) + col) = h2u(l[0], l[1]);
+          if ((row >> 4) == (col >> 4))  // the diagonal blocks also in fp32, for the substitution
+            *reinterpret_cast<float2*>(sLd + row * tiles::LDG + (col & 15)) = make_float2(l[0], l[1]);
+          *reinterpret_cast<uint32_t*>(Aout + row * C + col) = h2u(a[0], a[1]);
         }
-        *reinterpret_cast<uint32_t*>(sL16 + row * (tiles::LD16 / 2) + col) = h2u(l[0], l[1]);
-        if ((row >> 4) == (col >> 4))  // the diagonal blocks also in fp32, for the substitution
-          *reinterpret_cast<float2*>(sLd + row * tiles::LDG + (col & 15)) = make_float2(l[0], l[1]);
-        *reinterpret_cast<uint32_t*>(Aout + row * C + col) = h2u(a[0], a[1]);
-      }
-  }
-  __syncthreads();  // L complete
-
-  // T = (I + L)^-1: the diagonal blocks D_b = (I + L_bb)^-1 by fp32 forward substitution (one column
-  // per thread) into L16's diagonal blocks, then block column J of T on warp J by mma.sync merges of
-  // the fp16 blocks, T_iJ = -D_i sum_{k=J}^{i-1} L_ik T_kJ (tiles::merge_column_core).
-  if (tid < C) {
-    const int bb = tid >> 4, j = tid & 15;
-    const float* Lb = sLd + bb * 16 * tiles::LDG;
-    float x[16], acc[16];
-#pragma unroll
-    for (int r = 0; r < 16; ++r) acc[r] = 0.f;
-#pragma unroll
-    for (int m = 0; m < 16; ++m) {
-      x[m] = (m == j) ? 1.f : (m > j ? -acc[m] : 0.f);
-#pragma unroll
-      for (int r = m + 1; r < 16; ++r) acc[r] = fmaf(Lb[r * tiles::LDG + m], x[m], acc[r]);
     }
-#pragma unroll
-    for (int r = 0; r < 16; ++r) sL16[(bb * 16 + r) * (tiles::LD16 / 2) + bb * 16 + j] = __float2half_rn(x[r]);
-  }
-  __syncthreads();
-  if (warp < 4) {
-    const uint32_t tT = ptx::smem_u32(sT);
-    auto emit = [&](int i, const float (&f)[8]) {
-      const uint32_t v[4] = {h2u(f[0], f[1]), h2u(f[2], f[3]), h2u(f[4], f[5]), h2u(f[6], f[7])};
-      ptx::stsm_x4_t(tiles::frag_addr_plain(tT, LDC * 2, 16 * i, 16 * warp, lane), v);
-    };
-    auto zero = [&](int i) {
-      const uint32_t z[4] = {0u, 0u, 0u, 0u};
-      ptx::stsm_x4_t(tiles::frag_addr_plain(tT, LDC * 2, 16 * i, 16 * warp, lane), z);
-    };
-    tiles::merge_column_core(warp, ptx::smem_u32(sL16), lane, emit, zero);
-  }
-  __syncthreads();
-  {
-    __half* Tout = p.wT + (int64_t)task * C * C;
-    for (int i = tid; i < C * C / 8; i += NTHR) {
-      const int row = i >> 3, seg = i & 7;
-      *reinterpret_cast<uint4*>(Tout + row * C + seg * 8) = *reinterpret_cast<const uint4*>(sT + row * LDC + seg * 8);
+    __syncthreads();  // L complete
+
+    // T = (I + L)^-1: the diagonal blocks D_b = (I + L_bb)^-1 by fp32 forward substitution (one column
+    // per thread) into L16's diagonal blocks, then block column J of T on warp J by mma.sync merges of
+    // the fp16 blocks, T_iJ = -D_i sum_{k=J}^{i-1} L_ik T_kJ (tiles::merge_column_core).
+    if (tid < C) {
+      const int bb = tid >> 4, j = tid & 15;
+      const float* Lb = sLd + bb * 16 * tiles::LDG;
+      float x[16], acc[16];
+  #pragma unroll
+      for (int r = 0; r < 16; ++r) acc[r] = 0.f;
+  #pragma unroll
+      for (int m = 0; m < 16; ++m) {
+        x[m] = (m == j) ? 1.f : (m > j ? -acc[m] : 0.f);
+  #pragma unroll
+        for (int r = m + 1; r < 16; ++r) acc[r] = fmaf(Lb[r * tiles::LDG + m], x[m], acc[r]);
+      }
+  #pragma unroll
+      for (int r = 0; r < 16; ++r) sL16[(bb * 16 + r) * (tiles::LD16 / 2) + bb * 16 + j] = __float2half_rn(x[r]);
+    }
+    __syncthreads();
+    if (warp < 4) {
+      const uint32_t tT = ptx::smem_u32(sT);
+      auto emit = [&](int i, const float (&f)[8]) {
+        const uint32_t v[4] = {h2u(f[0], f[1]), h2u(f[2], f[3]), h2u(f[4], f[5]), h2u(f[6], f[7])};
+        ptx::stsm_x4_t(tiles::frag_addr_plain(tT, LDC * 2, 16 * i, 16 * warp, lane), v);
+      };
+      auto zero = [&](int i) {
+        const uint32_t z[4] = {0u, 0u, 0u, 0u};
+        ptx::stsm_x4_t(tiles::frag_addr_plain(tT, LDC * 2, 16 * i, 16 * warp, lane), z);
+      };
+      tiles::merge_column_core(warp, ptx::smem_u32(sL16), lane, emit, zero);
+    }
+    __syncthreads();
+    {
+      __half* Tout = p.wT + (int64_t)task * C * C;
+      for (int i = tid; i < C * C / 8; i += NTHR) {
+        const int row = i >> 3, seg = i & 7;
+        *reinterpret_cast<uint4*>(Tout + row * C + seg * 8) = *reinterpret_cast<const uint4*>(sT + row * LDC + seg * 8);
+      }
     }
   }
 
@@ -548,7 +559,7 @@ __global__ void __launch_bounds__(NTHR) prep_kernel(Params p) {
     const int m0 = 16 * (warp & 3), n0 = 64 * (warp >> 2), g = lane >> 2, t4 = lane & 3;
     float acc[1][8][4];
 #pragma unroll 1
-    for (int which = 0; which < 2; ++which) {
+    for (int which = REUSE ? 1 : 0; which < 2; ++which) {
       zero(acc);
       mma_acc<1, 8, false, true, C>(acc, sT, LDC, m0, which ? sV : sGK, LDT, n0, lane);
       __half* out = (which ? p.wUw : p.wW) + (int64_t)task * C * D;
@@ -575,19 +586,27 @@ __global__ void __launch_bounds__(NTHR) prep_kernel(Params p) {
     const int64_t o = (int64_t)task * C * D;
     for (int i = tid; i < C * 16; i += NTHR) {
       const int r = i >> 4, sg8 = (i & 15) * 8;
-      const uint4 u = *reinterpret_cast<const uint4*>(sU + r * LDT + sg8);
       const uint4 q = *reinterpret_cast<const uint4*>(sQ + r * LDT + sg8);
-      const uint32_t uw[4] = {u.x, u.y, u.z, u.w}, qw[4] = {q.x, q.y, q.z, q.w};
-      uint32_t du[4], gq[4];
+      const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+      uint32_t gq[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const float2 a = u2f(uw[j]), bq = u2f(qw[j]);
-        du[j] = h2u(sd[r] * a.x, sd[r] * a.y);
+        const float2 bq = u2f(qw[j]);
         gq[j] = h2u(sgam[r] * bq.x, sgam[r] * bq.y);
       }
-      *reinterpret_cast<uint4*>(p.wU + o + r * D + sg8) = u;
-      *reinterpret_cast<uint4*>(p.wDU + o + r * D + sg8) = make_uint4(du[0], du[1], du[2], du[3]);
       *reinterpret_cast<uint4*>(sGQ + r * LDT + sg8) = make_uint4(gq[0], gq[1], gq[2], gq[3]);
+      if constexpr (!REUSE) {
+        const uint4 u = *reinterpret_cast<const uint4*>(sU + r * LDT + sg8);
+        const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
+        uint32_t du[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 a = u2f(uw[j]);
+          du[j] = h2u(sd[r] * a.x, sd[r] * a.y);
+        }
+        *reinterpret_cast<uint4*>(p.wU + o + r * D + sg8) = u;
+        *reinterpret_cast<uint4*>(p.wDU + o + r * D + sg8) = make_uint4(du[0], du[1], du[2], du[3]);
+      }
     }
   }
   cp_wait<0>();
@@ -853,7 +872,7 @@ __global__ void __launch_bounds__(NTHR, 1) local_kernel(Params p) {
       prefetch_span(p.wA + nt * C * C, C * C * 2);
       prefetch_span(p.wS + nt * D * D, D * D * 2);
       prefetch_span(p.wdS + nt * D * D, D * D * 2);
-      prefetch_rows<TI, TD>(p, (int)nt, false, false);
+      prefetch_rows<TI, TD>(p, (int)nt, true, false, false);
     }
     raw_store(sQ, rq, nullptr, 1.f);
     raw_store(sK, rk, nullptr, 1.f);
@@ -1180,7 +1199,8 @@ Layout layout(int64_t nch, int64_t bh) {
 template <typename TI, typename TD>
 int launch(const Params& p, cudaStream_t s) {
   static std::atomic<unsigned long long> opted{0};  // per device (see opt_in_smem)
-  if (!opt_in_smem(opted, {{(const void*)prep_kernel<TI, TD>, (int)PREP_SMEM},
+  if (!opt_in_smem(opted, {{(const void*)prep_kernel<TI, TD, false>, (int)PREP_SMEM},
+                           {(const void*)prep_kernel<TI, TD, true>, (int)PREP_SMEM},
                            {(const void*)chain_kernel, (int)CHAIN_SMEM},
                            {(const void*)local_kernel<TI, TD>, (int)LOCAL_SMEM}}))
     return GDN_ERR_LAUNCH;
@@ -1190,13 +1210,16 @@ int launch(const Params& p, cudaStream_t s) {
   int dev = 0, sms = 0, per_sm = 0;
   const bool have_sms =
       cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess;
-  pp.pf = have_sms && cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, prep_kernel<TI, TD>, NTHR, PREP_SMEM) == cudaSuccess
+  pp.pf = have_sms && cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, prep_kernel<TI, TD, false>, NTHR, PREP_SMEM) == cudaSuccess
               ? sms * per_sm : 0;
   pl.pf = have_sms && cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, local_kernel<TI, TD>, NTHR, LOCAL_SMEM) == cudaSuccess
               ? sms * per_sm : 0;
   if (cudaMemsetAsync(p.amax, 0, (size_t)p.BH * 4, s) != cudaSuccess) return GDN_ERR_LAUNCH;
   amax_kernel<TD><<<(unsigned)nch, NTHR, 0, s>>>(p);
-  prep_kernel<TI, TD><<<(unsigned)nch, NTHR, PREP_SMEM, s>>>(pp);
+  if (p.accum)  // a later state slice of the same call: the first slice's slice-independent products are in the workspace
+    prep_kernel<TI, TD, true><<<(unsigned)nch, NTHR, PREP_SMEM, s>>>(pp);
+  else
+    prep_kernel<TI, TD, false><<<(unsigned)nch, NTHR, PREP_SMEM, s>>>(pp);
   chain_kernel<<<(unsigned)(2 * p.BH), NTHR, CHAIN_SMEM, s>>>(p);
   local_kernel<TI, TD><<<(unsigned)nch, NTHR, LOCAL_SMEM, s>>>(pl);
   return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
