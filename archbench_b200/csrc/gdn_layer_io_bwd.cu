@@ -29,7 +29,10 @@ constexpr int MAX_TAPS = 4;
 constexpr int WARPS = 4;  // warps per prologue block
 constexpr int RUN = 16;   // tokens per warp
 
-__device__ __forceinline__ float sigm(float x) { return 1.f / (1.f + __expf(-x)); }
+// Logistic sigmoid with the fast exponential and division, as the forward kernels' SiLU (a few ulps of
+// fp32; 0 once 1 + exp(-x) exceeds 2^126, where the exact value is below fp32's normal range): the backward passes
+// are bound by their per-element instruction count.
+__device__ __forceinline__ float sigm(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
 __device__ __forceinline__ float softplus(float x) { return x > 20.f ? x : log1pf(expf(x)); }
 __device__ __forceinline__ float dsilu(float c) {
   const float s = sigm(c);
