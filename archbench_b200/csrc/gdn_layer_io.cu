@@ -226,6 +226,13 @@ __global__ void __launch_bounds__(32 * TOKS) prologue_kernel(const PrologueParam
 #pragma unroll
   for (int n = 0; n < NK; ++n) kp[n] = 0.f;
   const float lam_h = nstep ? p.lam[h] : 0.f;
+  // beta of token t0 + lane (a run has at most 16 tokens), loaded and formed before the token loop, which
+  // takes it by shuffle: a load per token there would put its latency on the loop's critical path
+  float bt_lane = 0.f;
+  if (nstep && t0 + lane < t1) {
+    const float xbt = to_f32(reinterpret_cast<const TX*>(p.xb)[(int64_t)b * p.sb_b + (int64_t)(t0 + lane) * p.sb_t + h]);
+    bt_lane = p.beta_scale / (1.f + expf(-(xbt + bb_h)));
+  }
   if (nstep) {
     if (t0 > 0) {
       conv_tok<TX, TAPS, NK>(stage + DK + lane * NK, W, swc[1] + lane * NK, DK, wk, kp);
@@ -270,8 +277,7 @@ __global__ void __launch_bounds__(32 * TOKS) prologue_kernel(const PrologueParam
     store_vec<TO, NK>(reinterpret_cast<TO*>(p.k.out) + tok * DK + lane * NK, k);
     store_vec<TO, NV>(reinterpret_cast<TO*>(p.v.out) + tok * DV + lane * NV, v);
     if (nstep) {  // u = beta k, then n - 1 steps u -= lam beta (p . u) (p - (p . k) k)   (nsgdn.py:61-75)
-      const float xbt = to_f32(reinterpret_cast<const TX*>(p.xb)[(int64_t)b * p.sb_b + (int64_t)t * p.sb_t + h]);
-      const float bt = p.beta_scale / (1.f + expf(-(xbt + bb_h)));
+      const float bt = __shfl_sync(0xffffffffu, bt_lane, t - t0);
       float pk = 0.f;
 #pragma unroll
       for (int n = 0; n < NK; ++n) pk = fmaf(kp[n], k[n], pk);
