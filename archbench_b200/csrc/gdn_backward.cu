@@ -483,7 +483,8 @@ __global__ void __launch_bounds__(NTHR) prep_kernel(Params p) {
     cp_wait<0>();
     __syncthreads();
   } else {
-    // M = K U^T -> L (fp32, strictly lower); P = Q U^T -> A (fp16, lower incl. diagonal, to the workspace)
+    // M = K U^T -> L (strictly lower, fp16; its diagonal blocks also fp32); P = Q U^T -> A (fp16, lower incl.
+    // diagonal, to the workspace)
     {
       const int m0 = 16 * (warp & 3), n0 = 32 * (warp >> 2), g = lane >> 2, t4 = lane & 3;
       float accM[1][4][4], accP[1][4][4];
@@ -492,13 +493,13 @@ __global__ void __launch_bounds__(NTHR) prep_kernel(Params p) {
       mma_acc<1, 4, false, false, D>(accM, sK, LDT, m0, sU, LDT, n0, lane);
       mma_acc<1, 4, false, false, D>(accP, sQ, LDT, m0, sU, LDT, n0, lane);
       __half* Aout = p.wA + (int64_t)task * C * C;
-  #pragma unroll
+#pragma unroll
       for (int nt = 0; nt < 4; ++nt)
-  #pragma unroll
+#pragma unroll
         for (int hf = 0; hf < 2; ++hf) {
           const int row = m0 + g + 8 * hf, col = n0 + 8 * nt + 2 * t4;
           float e[2], a[2], l[2];
-  #pragma unroll
+#pragma unroll
           for (int x = 0; x < 2; ++x) {
             const int cc = col + x;
             e[x] = cc <= row ? __expf(sg[row] - sg[cc]) : 0.f;
@@ -520,15 +521,15 @@ __global__ void __launch_bounds__(NTHR) prep_kernel(Params p) {
       const int bb = tid >> 4, j = tid & 15;
       const float* Lb = sLd + bb * 16 * tiles::LDG;
       float x[16], acc[16];
-  #pragma unroll
+#pragma unroll
       for (int r = 0; r < 16; ++r) acc[r] = 0.f;
-  #pragma unroll
+#pragma unroll
       for (int m = 0; m < 16; ++m) {
         x[m] = (m == j) ? 1.f : (m > j ? -acc[m] : 0.f);
-  #pragma unroll
+#pragma unroll
         for (int r = m + 1; r < 16; ++r) acc[r] = fmaf(Lb[r * tiles::LDG + m], x[m], acc[r]);
       }
-  #pragma unroll
+#pragma unroll
       for (int r = 0; r < 16; ++r) sL16[(bb * 16 + r) * (tiles::LD16 / 2) + bb * 16 + j] = __float2half_rn(x[r]);
     }
     __syncthreads();
